@@ -1,0 +1,273 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes bindings to the CPU checkers.
+
+* ``Port``  -> oracle/_ref/libmoe_port.so, this repository's plain-C
+  restatement of the reference hot path (oracle/moe_oracle.c);
+* ``Ref``   -> oracle/_ref/libmoe_ref.so, the reference's own C++ hot path
+  compiled from its sources (oracle/ref_harness.cpp + oracle/Makefile).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline and
+reference arms may use this module, and only as the checker or the timed
+CPU baseline.  The CUDA product never calls it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REF_DIR = HERE / "_ref"
+PORT_SO = REF_DIR / "libmoe_port.so"
+REF_SO = REF_DIR / "libmoe_ref.so"
+REFERENCE_ROOT = Path(os.environ.get("MOE_REFERENCE_ROOT", "/root/reference"))
+
+_u8p = C.POINTER(C.c_uint8)
+_u16p = C.POINTER(C.c_uint16)
+_i32p = C.POINTER(C.c_int32)
+_u32p = C.POINTER(C.c_uint32)
+_f32p = C.POINTER(C.c_float)
+
+
+def build(ref: bool = True) -> None:
+    """Builds the port always, and the reference library when its sources
+    are present (they are not on the GPU box, which uses the prebuilt .so)."""
+    targets = ["port"]
+    if ref and REFERENCE_ROOT.is_dir():
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-j8", "-C", str(HERE), f"REF={REFERENCE_ROOT}"] + targets,
+                   check=True)
+
+
+def _p(a: np.ndarray, t):
+    return a.ctypes.data_as(t) if a is not None else None
+
+
+class MoLayer(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("experts", C.c_uint32),
+                ("top_k", C.c_uint32), ("score_sigmoid", C.c_int32), ("norm_topk", C.c_int32),
+                ("routed_scale", C.c_float), ("router_bf16", _u16p), ("gate", _u8p), ("up", _u8p),
+                ("down", _u8p), ("shared_gate", _u8p), ("shared_up", _u8p), ("shared_down", _u8p)]
+
+
+class RefLayer(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("experts", C.c_uint32),
+                ("top_k", C.c_uint32), ("router_bf16", _u16p), ("gate", _u8p), ("up", _u8p),
+                ("down", _u8p), ("shared_gate", _u8p), ("shared_up", _u8p), ("shared_down", _u8p)]
+
+
+class Assignment(C.Structure):
+    _fields_ = [("token_index", C.c_uint32), ("layer", C.c_uint32), ("expert", C.c_uint32),
+                ("router_score", C.c_float)]
+
+
+class Batch(C.Structure):
+    _fields_ = [("layer", C.c_uint32), ("expert", C.c_uint32), ("first_sorted_index", C.c_uint32),
+                ("token_count", C.c_uint32)]
+
+
+def _c(a, dtype):
+    return None if a is None else np.ascontiguousarray(a, dtype=dtype)
+
+
+class Port:
+    """The C restatement (always available once built)."""
+
+    def __init__(self, path: Path = PORT_SO):
+        self.lib = C.CDLL(str(path))
+        L = self.lib
+        L.mo_e8m0_to_f32.restype = C.c_float
+        L.mo_e8m0_to_f32.argtypes = [C.c_uint8]
+        L.mo_mxfp4_value.restype = C.c_float
+        L.mo_mxfp4_value.argtypes = [C.c_uint8]
+        L.mo_mxfp4_dot_row.restype = C.c_float
+        L.mo_mxfp4_dot_row.argtypes = [_u8p, _f32p, C.c_uint32]
+        L.mo_bf16_dot_row.restype = C.c_float
+        L.mo_bf16_dot_row.argtypes = [_u16p, _f32p, C.c_uint32]
+        L.mo_silu.restype = C.c_float
+        L.mo_silu.argtypes = [C.c_float]
+        L.mo_router_scores.argtypes = [C.POINTER(MoLayer), _f32p, _f32p]
+        L.mo_router_topk.restype = C.c_int
+        L.mo_router_topk.argtypes = [C.POINTER(MoLayer), _f32p, _i32p, _f32p, _u32p]
+        L.mo_group_tokens_by_expert.restype = C.c_int
+        L.mo_group_tokens_by_expert.argtypes = [C.POINTER(Assignment), C.c_uint32, C.POINTER(Assignment),
+                                                C.POINTER(Batch), C.c_uint32, _u32p]
+        L.mo_expert_triplet.restype = C.c_int
+        L.mo_expert_triplet.argtypes = [_u8p, _u8p, _u8p, _f32p, C.c_uint32, C.c_uint32, _f32p, _f32p, _f32p]
+        L.mo_moe_layer.restype = C.c_int
+        L.mo_moe_layer.argtypes = [C.POINTER(MoLayer), _u16p, C.c_uint32, _f32p, _i32p, _f32p,
+                                   C.c_uint32, _u32p]
+
+    def _layer(self, li, score_sigmoid=0, norm_topk=None, routed_scale=1.0):
+        s = li.shape
+        keep = dict(router=_c(li.router, np.uint16), gate=_c(li.gate, np.uint8), up=_c(li.up, np.uint8),
+                    down=_c(li.down, np.uint8), sg=_c(li.shared_gate, np.uint8),
+                    su=_c(li.shared_up, np.uint8), sd=_c(li.shared_down, np.uint8))
+        nt = s.norm_topk if norm_topk is None else norm_topk
+        L = MoLayer(s.hidden, s.intermediate, s.experts, s.top_k, int(score_sigmoid), int(nt),
+                    float(routed_scale), _p(keep["router"], _u16p), _p(keep["gate"], _u8p),
+                    _p(keep["up"], _u8p), _p(keep["down"], _u8p), _p(keep["sg"], _u8p),
+                    _p(keep["su"], _u8p), _p(keep["sd"], _u8p))
+        return L, keep
+
+    def moe_layer(self, li, x=None, threads: int = 0, **kw):
+        x = _c(li.x if x is None else x, np.uint16)
+        T = x.shape[0]
+        L, keep = self._layer(li, **kw)
+        H, K = li.shape.hidden, li.shape.top_k
+        y = np.zeros((T, H), np.float32)
+        ids = np.zeros((T, K), np.int32)
+        w = np.zeros((T, K), np.float32)
+        ties = C.c_uint32(0)
+        ok = self.lib.mo_moe_layer(C.byref(L), _p(x, _u16p), T, _p(y, _f32p), _p(ids, _i32p), _p(w, _f32p),
+                                   threads or (os.cpu_count() or 1), C.byref(ties))
+        if not ok:
+            raise RuntimeError("oracle layer failed")
+        return y, ids, w, ties.value
+
+    def router_topk(self, li, x=None, **kw):
+        x = _c(li.x if x is None else x, np.uint16)
+        L, keep = self._layer(li, **kw)
+        T, K, E = x.shape[0], li.shape.top_k, li.shape.experts
+        ids = np.zeros((T, K), np.int32)
+        w = np.zeros((T, K), np.float32)
+        scores = np.zeros((T, E), np.float32)
+        ties = C.c_uint32(0)
+        xf = bf16_to_f32(x)
+        for t in range(T):
+            row = np.ascontiguousarray(xf[t])
+            self.lib.mo_router_scores(C.byref(L), _p(row, _f32p), _p(scores[t], _f32p))
+            self.lib.mo_router_topk(C.byref(L), _p(row, _f32p), _p(ids[t], _i32p), _p(w[t], _f32p),
+                                    C.byref(ties))
+        return ids, w, scores, ties.value
+
+    def mxfp4_dot_rows(self, packed: np.ndarray, x: np.ndarray) -> np.ndarray:
+        packed = _c(packed, np.uint8)
+        x = _c(x, np.float32)
+        rows = packed.shape[0]
+        out = np.empty(rows, np.float32)
+        for r in range(rows):
+            out[r] = self.lib.mo_mxfp4_dot_row(_p(packed[r], _u8p), _p(x, _f32p), x.shape[0])
+        return out
+
+    def group_tokens(self, token, expert, score=None, layer=None):
+        n = len(token)
+        a = (Assignment * n)()
+        for i in range(n):
+            a[i] = Assignment(int(token[i]), 0 if layer is None else int(layer[i]), int(expert[i]),
+                              0.0 if score is None else float(score[i]))
+        out = (Assignment * n)()
+        batches = (Batch * max(n, 1))()
+        cnt = C.c_uint32(0)
+        ok = self.lib.mo_group_tokens_by_expert(a, n, out, batches, max(n, 1), C.byref(cnt))
+        return ok, out, batches, cnt.value
+
+
+class Ref:
+    """The reference's own compiled hot path."""
+
+    def __init__(self, metadata_json: str, path: Path = REF_SO):
+        self.lib = C.CDLL(str(path))
+        L = self.lib
+        L.ref_engine_create.restype = C.c_void_p
+        L.ref_engine_create.argtypes = [C.c_char_p]
+        L.ref_engine_destroy.argtypes = [C.c_void_p]
+        L.ref_row_threads.restype = C.c_uint32
+        L.ref_e8m0_to_f32.restype = C.c_float
+        L.ref_e8m0_to_f32.argtypes = [C.c_uint8]
+        L.ref_mxfp4_value.restype = C.c_float
+        L.ref_mxfp4_value.argtypes = [C.c_uint8]
+        L.ref_silu.restype = C.c_float
+        L.ref_silu.argtypes = [C.c_float]
+        L.ref_mxfp4_dot_rows.argtypes = [_u8p, C.c_uint32, C.c_uint32, _f32p, _f32p]
+        L.ref_bf16_dot_rows.argtypes = [_u16p, C.c_uint32, C.c_uint32, _f32p, _f32p]
+        L.ref_router_topk.restype = C.c_int
+        L.ref_router_topk.argtypes = [C.c_void_p, _u16p, C.c_uint32, C.c_uint32, _u16p, C.c_uint32,
+                                      C.c_uint32, _i32p, _f32p, _f32p]
+        L.ref_moe_layer.restype = C.c_int
+        L.ref_moe_layer.argtypes = [C.c_void_p, C.POINTER(RefLayer), _u16p, C.c_uint32, _f32p, _i32p, _f32p]
+        L.ref_group_tokens_by_expert.restype = C.c_int
+        L.ref_group_tokens_by_expert.argtypes = [C.POINTER(Assignment), C.c_uint32, C.POINTER(Assignment),
+                                                 C.POINTER(Batch), C.c_uint32, _u32p]
+        self.engine = L.ref_engine_create(metadata_json.encode())
+        if not self.engine:
+            raise RuntimeError("reference engine create failed")
+
+    def close(self):
+        if self.engine:
+            self.lib.ref_engine_destroy(self.engine)
+            self.engine = None
+
+    def moe_layer(self, li, x=None):
+        s = li.shape
+        x = _c(li.x if x is None else x, np.uint16)
+        T = x.shape[0]
+        keep = [_c(li.router, np.uint16), _c(li.gate, np.uint8), _c(li.up, np.uint8), _c(li.down, np.uint8),
+                _c(li.shared_gate, np.uint8), _c(li.shared_up, np.uint8), _c(li.shared_down, np.uint8)]
+        d = RefLayer(s.hidden, s.intermediate, s.experts, s.top_k, _p(keep[0], _u16p), _p(keep[1], _u8p),
+                     _p(keep[2], _u8p), _p(keep[3], _u8p), _p(keep[4], _u8p), _p(keep[5], _u8p),
+                     _p(keep[6], _u8p))
+        y = np.zeros((T, s.hidden), np.float32)
+        ids = np.zeros((T, s.top_k), np.int32)
+        w = np.zeros((T, s.top_k), np.float32)
+        if not self.lib.ref_moe_layer(self.engine, C.byref(d), _p(x, _u16p), T, _p(y, _f32p), _p(ids, _i32p),
+                                      _p(w, _f32p)):
+            raise RuntimeError("reference layer failed")
+        return y, ids, w
+
+    def router_topk(self, li, x=None):
+        s = li.shape
+        x = _c(li.x if x is None else x, np.uint16)
+        router = _c(li.router, np.uint16)
+        T = x.shape[0]
+        ids = np.zeros((T, s.top_k), np.int32)
+        w = np.zeros((T, s.top_k), np.float32)
+        scores = np.zeros((T, s.experts), np.float32)
+        if not self.lib.ref_router_topk(self.engine, _p(router, _u16p), s.experts, s.hidden, _p(x, _u16p), T,
+                                        s.top_k, _p(ids, _i32p), _p(w, _f32p), _p(scores, _f32p)):
+            raise RuntimeError("reference router failed")
+        return ids, w, scores
+
+    def mxfp4_dot_rows(self, packed, x):
+        packed = _c(packed, np.uint8)
+        x = _c(x, np.float32)
+        out = np.empty(packed.shape[0], np.float32)
+        self.lib.ref_mxfp4_dot_rows(_p(packed, _u8p), packed.shape[0], x.shape[0], _p(x, _f32p), _p(out, _f32p))
+        return out
+
+    def bf16_dot_rows(self, w, x):
+        w = _c(w, np.uint16)
+        x = _c(x, np.float32)
+        out = np.empty(w.shape[0], np.float32)
+        self.lib.ref_bf16_dot_rows(_p(w, _u16p), w.shape[0], w.shape[1], _p(x, _f32p), _p(out, _f32p))
+        return out
+
+    def group_tokens(self, token, expert, score=None, layer=None):
+        n = len(token)
+        a = (Assignment * n)()
+        for i in range(n):
+            a[i] = Assignment(int(token[i]), 0 if layer is None else int(layer[i]), int(expert[i]),
+                              0.0 if score is None else float(score[i]))
+        out = (Assignment * n)()
+        batches = (Batch * max(n, 1))()
+        cnt = C.c_uint32(0)
+        ok = self.lib.ref_group_tokens_by_expert(a, n, out, batches, max(n, 1), C.byref(cnt))
+        return ok, out, batches, cnt.value
+
+
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def metadata_json(top_k: int, norm_topk: bool = False, sigmoid: bool = False,
+                  routed_scale: float = 1.0) -> str:
+    """GGUF metadata keys the reference router reads
+    (generation_router.cpp.inc:361-482)."""
+    parts = [f'"num_experts_per_tok":{int(top_k)}', f'"norm_topk_prob":{"true" if norm_topk else "false"}']
+    if sigmoid:
+        parts.append('"scoring_func":"sigmoid"')
+        if routed_scale != 1.0:
+            parts.append(f'"routed_scaling_factor":{routed_scale!r}')
+    return "{" + ",".join(parts) + "}"

@@ -1,0 +1,258 @@
+// TEST INFRASTRUCTURE ONLY -- never part of the shipped product path.
+//
+// Compiles the reference's own CPU MoE hot path (jujumelona/storage.llm,
+// moe_engine) into oracle/_ref/libmoe_ref.so so the tests and the bench's
+// reference arm can call it.  This file contains no reference source: it
+// textually includes the reference's single translation unit
+// (moe_engine/src/moe_pc_engine.cpp, which itself includes every
+// src/parts/*.cpp.inc) from the read-only reference checkout, and adds thin
+// extern "C" entry points around the reference's `static` hot-path functions.
+//
+// The layer entry point composes the reference leaves in exactly the order
+// of moe_layer_moe_mlp_f32 (generation_mlp.cpp.inc:776-1442) for one token at
+// a time, which is how the engine runs a layer (generation_forward.cpp.inc:
+// 212-215 / generation_api_main.cpp.inc:261-283):
+//   router     moe_router_topk_f32            generation_router.cpp.inc:560-682
+//   shared     dense MLP (gate/up/act, down)  generation_mlp.cpp.inc:596-727, 839-860
+//   gate/up    moe_parallel_rows(k*I) -> moe_dot_gguf_mxfp4_row x2 -> act
+//                                             generation_mlp.cpp.inc:1335-1376
+//   down       moe_parallel_rows(k*H) -> moe_dot_gguf_mxfp4_row
+//                                             generation_mlp.cpp.inc:1378-1413
+//   combine    moe_axpy_f32 in router order   generation_mlp.cpp.inc:1415-1431
+// Weights are passed in the reference's GGUF MXFP4 byte layout (17-byte
+// blocks per 32 K-elements, tensor_layout.cpp.inc:174-176).
+#include "moe_engine/src/moe_pc_engine.cpp"
+
+#include <xmmintrin.h>
+#include <pmmintrin.h>
+
+namespace {
+
+// Restores the caller thread's MXCSR: the reference's row pool switches the
+// calling thread to FTZ/DAZ (parallel_rows.cpp.inc:39-46, 215) and the
+// Python test process must not inherit that.
+struct mxcsr_guard {
+    unsigned int saved;
+    mxcsr_guard() : saved(_mm_getcsr()) {}
+    ~mxcsr_guard() { _mm_setcsr(saved); }
+};
+
+uint64_t router_cache_key(int32_t layer) {
+    // Same key the reference builds in moe_map_router_tensor
+    // (generation_router.cpp.inc:159-160).
+    const uint32_t suffix_hash = moe_router_fnv1a_hash_string("ffn_gate_inp.weight");
+    return ((uint64_t)(uint32_t)layer << 32) | suffix_hash | 0x80000000ull;
+}
+
+float bf16_to_f32(uint16_t v) {
+    uint32_t bits = (uint32_t)v << 16;
+    float out;
+    std::memcpy(&out, &bits, sizeof(out));
+    return out;
+}
+
+}  // namespace
+
+extern "C" {
+
+typedef struct {
+    uint32_t hidden;        // H
+    uint32_t intermediate;  // I
+    uint32_t experts;       // E
+    uint32_t top_k;         // k (also written to the engine metadata)
+    const uint16_t* router_bf16;  // [E x H] row-major bf16 (ffn_gate_inp.weight)
+    const uint8_t* gate;    // [E][I rows][ceil(H/32)*17 B]
+    const uint8_t* up;      // [E][I rows][ceil(H/32)*17 B]
+    const uint8_t* down;    // [E][H rows][ceil(I/32)*17 B]
+    const uint8_t* shared_gate;  // [I][ceil(H/32)*17] or null
+    const uint8_t* shared_up;
+    const uint8_t* shared_down;  // [H][ceil(I/32)*17]
+} ref_layer_desc;
+
+// Creates a reference engine whose GGUF metadata JSON is `metadata_json`
+// (e.g. {"num_experts_per_tok":4,"norm_topk_prob":false}).  Routing semantics
+// come from those keys exactly as in the engine (generation_router.cpp.inc:
+// 361-482).
+void* ref_engine_create(const char* metadata_json) {
+    mxcsr_guard guard;
+    moe_pc_engine_config_t cfg = moe_pc_default_config();
+    cfg.prefer_gpu = 0;
+    cfg.vram_budget_bytes = 0;
+    moe_pc_engine_t* engine = moe_pc_engine_create(&cfg);
+    if (!engine) return nullptr;
+    engine->offload_gguf_metadata_json = metadata_json ? metadata_json : "";
+    return engine;
+}
+
+void ref_engine_destroy(void* engine) {
+    mxcsr_guard guard;
+    moe_pc_engine_destroy(static_cast<moe_pc_engine_t*>(engine));
+}
+
+uint32_t ref_row_threads(void) { return row_hw_threads(); }
+
+float ref_e8m0_to_f32(uint8_t v) { return moe_e8m0_to_f32_half(v); }
+
+float ref_mxfp4_value(uint8_t code) { return moe_mxfp4_value_from_code(code); }
+
+// One reference MXFP4 row dot per row (tensor_dot_cpu_kernels.cpp.inc:601-667).
+void ref_mxfp4_dot_rows(const uint8_t* packed, uint32_t rows, uint32_t cols,
+                        const float* x, float* out) {
+    mxcsr_guard guard;
+    const uint64_t row_bytes = (uint64_t)((cols + 31u) / 32u) * 17u;
+    for (uint32_t r = 0; r < rows; ++r) {
+        out[r] = moe_dot_gguf_mxfp4_row(packed + (uint64_t)r * row_bytes, x, cols);
+    }
+}
+
+// Reference bf16 router row dot (raw_forward_utils.cpp.inc:174-216).
+void ref_bf16_dot_rows(const uint16_t* w, uint32_t rows, uint32_t cols,
+                       const float* x, float* out) {
+    mxcsr_guard guard;
+    for (uint32_t r = 0; r < rows; ++r) {
+        out[r] = moe_dot_bf16_row(reinterpret_cast<const uint8_t*>(w + (uint64_t)r * cols), x, cols);
+    }
+}
+
+float ref_silu(float x) { return moe_generation_silu(x); }
+
+// Router top-k for T tokens through moe_router_topk_f32 itself.  `logits`
+// (optional, [T x E]) receives the router's post-softmax scores.
+int ref_router_topk(void* eng, const uint16_t* router_bf16, uint32_t experts,
+                    uint32_t hidden, const uint16_t* x_bf16, uint32_t tokens,
+                    uint32_t top_k, int32_t* out_ids, float* out_w, float* out_scores) {
+    mxcsr_guard guard;
+    moe_pc_engine* engine = static_cast<moe_pc_engine*>(eng);
+    if (!engine || !router_bf16 || !x_bf16) return 0;
+    const int32_t layer = 0;
+    moe_raw_tensor_cache_entry entry{};
+    entry.base = reinterpret_cast<const uint8_t*>(router_bf16);
+    entry.bytes = (uint64_t)experts * hidden * 2ull;
+    entry.rows = experts;
+    entry.cols = hidden;
+    entry.scalar_encoding = moe_RAW_SCALAR_BF16;
+    entry.weight_format = moe_WEIGHT_ENCODING_RAW_BF16;
+    {
+        std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
+        engine->raw_tensor_cache[router_cache_key(layer)] = entry;
+    }
+    std::vector<float> x(hidden);
+    std::vector<int> ids;
+    std::vector<float> w, logits;
+    std::vector<uint32_t> order;
+    for (uint32_t t = 0; t < tokens; ++t) {
+        for (uint32_t h = 0; h < hidden; ++h) x[h] = bf16_to_f32(x_bf16[(uint64_t)t * hidden + h]);
+        if (!moe_router_topk_f32(engine, layer, x.data(), hidden, experts, top_k,
+                                 &ids, &w, &logits, &order)) {
+            return 0;
+        }
+        if (ids.size() != top_k) return 0;
+        for (uint32_t j = 0; j < top_k; ++j) {
+            out_ids[(uint64_t)t * top_k + j] = ids[j];
+            out_w[(uint64_t)t * top_k + j] = w[j];
+        }
+        if (out_scores) {
+            for (uint32_t e = 0; e < experts; ++e) out_scores[(uint64_t)t * experts + e] = logits[e];
+        }
+    }
+    return 1;
+}
+
+// Whole MoE FFN layer for T tokens, one token at a time, in the order of
+// moe_layer_moe_mlp_f32.  y_f32 receives the MoE block output `mlp`
+// (shared + sum_e w_e * y_e) before the residual add of
+// moe_add_mlp_residual_f32 (generation_mlp.cpp.inc:572-594).
+int ref_moe_layer(void* eng, const ref_layer_desc* d, const uint16_t* x_bf16,
+                  uint32_t tokens, float* y_f32, int32_t* out_ids, float* out_w) {
+    mxcsr_guard guard;
+    moe_pc_engine* engine = static_cast<moe_pc_engine*>(eng);
+    if (!engine || !d || !x_bf16 || !y_f32) return 0;
+    const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, K = d->top_k;
+    const int32_t layer = 0;
+    const uint64_t row_h = (uint64_t)((H + 31u) / 32u) * 17u;
+    const uint64_t row_i = (uint64_t)((I + 31u) / 32u) * 17u;
+    const uint64_t expert_gu_bytes = (uint64_t)I * row_h;
+    const uint64_t expert_d_bytes = (uint64_t)H * row_i;
+
+    moe_raw_tensor_cache_entry entry{};
+    entry.base = reinterpret_cast<const uint8_t*>(d->router_bf16);
+    entry.bytes = (uint64_t)E * H * 2ull;
+    entry.rows = E;
+    entry.cols = H;
+    entry.scalar_encoding = moe_RAW_SCALAR_BF16;
+    entry.weight_format = moe_WEIGHT_ENCODING_RAW_BF16;
+    {
+        std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
+        engine->raw_tensor_cache[router_cache_key(layer)] = entry;
+    }
+    const int activation_mode = moe_engine_gelu_activation_mode(engine);
+
+    std::vector<float> x(H), mlp(H), shared_gate(I), shared_out(H);
+    std::vector<float> gate_pool((uint64_t)K * I), up_pool((uint64_t)K * I), out_pool((uint64_t)K * H);
+    std::vector<int> ids;
+    std::vector<float> w, logits;
+    std::vector<uint32_t> order;
+    for (uint32_t t = 0; t < tokens; ++t) {
+        for (uint32_t h = 0; h < H; ++h) x[h] = bf16_to_f32(x_bf16[(uint64_t)t * H + h]);
+        std::fill(mlp.begin(), mlp.end(), 0.0f);
+        // Shared expert first (generation_mlp.cpp.inc:839-860, dense MLP :707-727).
+        if (d->shared_gate && d->shared_up && d->shared_down) {
+            if (!moe_parallel_rows(engine, I, 0, [&](uint32_t row) {
+                    const float g = moe_dot_gguf_mxfp4_row(d->shared_gate + row * row_h, x.data(), H);
+                    const float u = moe_dot_gguf_mxfp4_row(d->shared_up + row * row_h, x.data(), H);
+                    shared_gate[row] = moe_generation_gated_activation_cached(activation_mode, g, u);
+                    return 1;
+                })) return 0;
+            if (!moe_parallel_rows(engine, H, 0, [&](uint32_t row) {
+                    shared_out[row] = moe_dot_gguf_mxfp4_row(d->shared_down + row * row_i, shared_gate.data(), I);
+                    return 1;
+                })) return 0;
+            const float gate_scalar = 1.0f;  // no shared gate tensor (:478-512)
+            for (uint32_t i = 0; i < H; ++i) mlp[i] += shared_out[i] * gate_scalar;
+        }
+        if (!moe_router_topk_f32(engine, layer, x.data(), H, E, K, &ids, &w, &logits, &order)) {
+            return 0;
+        }
+        const size_t sel = ids.size();
+        if (sel != K) return 0;
+        // Phase 2a: gate + up + activation over k*I flat rows (:1346-1370).
+        if (!moe_parallel_rows(engine, (uint32_t)(sel * I), 0, [&](uint32_t flat_row) {
+                const uint32_t e = flat_row / I;
+                const uint32_t r = flat_row % I;
+                const uint64_t ex = (uint64_t)ids[e];
+                const float g = moe_dot_gguf_mxfp4_row(d->gate + ex * expert_gu_bytes + r * row_h, x.data(), H);
+                const float u = moe_dot_gguf_mxfp4_row(d->up + ex * expert_gu_bytes + r * row_h, x.data(), H);
+                gate_pool[(uint64_t)e * I + r] = moe_generation_gated_activation_cached(activation_mode, g, u);
+                return 1;
+            })) return 0;
+        // Phase 2b: down over k*H flat rows (:1385-1404).
+        if (!moe_parallel_rows(engine, (uint32_t)(sel * H), 0, [&](uint32_t flat_row) {
+                const uint32_t e = flat_row / H;
+                const uint32_t r = flat_row % H;
+                const uint64_t ex = (uint64_t)ids[e];
+                out_pool[(uint64_t)e * H + r] = moe_dot_gguf_mxfp4_row(
+                    d->down + ex * expert_d_bytes + r * row_i, gate_pool.data() + (uint64_t)e * I, I);
+                return 1;
+            })) return 0;
+        // Phase 3: weighted combine in router order (:1417-1431).
+        for (size_t e = 0; e < sel; ++e) {
+            moe_axpy_f32(mlp.data(), out_pool.data() + e * H, w[e], H);
+        }
+        std::memcpy(y_f32 + (uint64_t)t * H, mlp.data(), (size_t)H * sizeof(float));
+        if (out_ids) for (uint32_t j = 0; j < K; ++j) out_ids[(uint64_t)t * K + j] = ids[j];
+        if (out_w) for (uint32_t j = 0; j < K; ++j) out_w[(uint64_t)t * K + j] = w[j];
+    }
+    return 1;
+}
+
+// The reference's public grouping utility (token_grouping.cpp.inc:1-83) is
+// already extern "C" (moe_pc_group_tokens_by_expert); this alias keeps the
+// oracle's symbols in one namespace.
+int ref_group_tokens_by_expert(const moe_token_expert_assignment_t* a, uint32_t n,
+                               moe_token_expert_assignment_t* sorted,
+                               moe_expert_batch_t* batches, uint32_t max_batches,
+                               uint32_t* batch_count) {
+    return moe_pc_group_tokens_by_expert(a, n, sorted, batches, max_batches, batch_count);
+}
+
+}  // extern "C"

@@ -1,0 +1,129 @@
+"""Writes the golden fixtures under tests/golden/ from the reference itself.
+
+The reference ships no tests, golden vectors or fixtures, so parity is pinned
+by running the reference's own CPU hot path (compiled from its sources into
+oracle/_ref/libmoe_ref.so by oracle/Makefile) on seeded synthetic inputs and
+recording its outputs here.  Run it in a checkout that has the reference
+sources (MOE_REFERENCE_ROOT, default /root/reference):
+
+    python tests/golden/make_golden.py
+
+Small cases store every input; full-size cases store the seed and a sha256 of
+the regenerated inputs, so a test can prove it regenerated the same bytes.
+"""
+from __future__ import annotations
+
+import importlib.util
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT / "oracle"))
+import oracle  # noqa: E402
+
+
+def _load_synth():
+    spec = importlib.util.spec_from_file_location("moe_b200_synth", ROOT / "storage.llm_b200" / "synth.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+synth = _load_synth()
+OUT = Path(__file__).resolve().parent
+
+# name -> (shape, seed, tokens or None, store_inputs)
+LAYER_CASES = {
+    "mini": (synth.small_shape(tokens=16), 1, None, True),
+    "tail": (synth.small_shape(name="tail", hidden=80, intermediate=100, tokens=20), 3, None, True),
+    "shared": (synth.small_shape(name="shared", shared=True, tokens=20), 4, None, True),
+    "norm_topk": (synth.small_shape(name="norm_topk", top_k=4, norm_topk=True, tokens=20), 5, None, True),
+    "c0": (synth.CONFIGS[0], 0, None, False),
+    "c1_t8": (synth.CONFIGS[1], 0, 8, False),
+    "c3_t16": (synth.CONFIGS[3], 0, 16, False),
+}
+
+
+def layer_case(name, shape, seed, tokens, store_inputs):
+    li = synth.make_layer(shape, seed=seed, tokens=tokens)
+    ref = oracle.Ref(oracle.metadata_json(shape.top_k, norm_topk=shape.norm_topk))
+    try:
+        y, ids, w = ref.moe_layer(li)
+        _, _, scores = ref.router_topk(li)
+    finally:
+        ref.close()
+    rec = dict(hidden=shape.hidden, intermediate=shape.intermediate, experts=shape.experts,
+               top_k=shape.top_k, tokens=li.x.shape[0], shared=int(shape.shared),
+               norm_topk=int(shape.norm_topk), skew=shape.skew or "", seed=seed,
+               digest=li.digest(), ids=ids, w=w, y=y, scores=scores)
+    if store_inputs:
+        rec.update(router=li.router, gate=li.gate, up=li.up, down=li.down, x=li.x)
+        if shape.shared:
+            rec.update(shared_gate=li.shared_gate, shared_up=li.shared_up, shared_down=li.shared_down)
+    np.savez_compressed(OUT / f"layer_{name}.npz", **rec)
+    print(f"layer_{name}: T={li.x.shape[0]} digest={rec['digest'][:16]}")
+
+
+def sigmoid_case():
+    shape = synth.small_shape(name="sigmoid", top_k=3, experts=16, tokens=24)
+    li = synth.make_layer(shape, seed=7)
+    ref = oracle.Ref(oracle.metadata_json(3, norm_topk=True, sigmoid=True, routed_scale=2.5))
+    try:
+        ids, w, scores = ref.router_topk(li)
+    finally:
+        ref.close()
+    np.savez_compressed(OUT / "router_sigmoid.npz", router=li.router, x=li.x, ids=ids, w=w, scores=scores,
+                        hidden=shape.hidden, experts=shape.experts, top_k=3, norm_topk=1, routed_scale=2.5)
+    print("router_sigmoid")
+
+
+def grouping_case():
+    rng = np.random.default_rng(11)
+    n = 300
+    token = rng.integers(0, 60, n).astype(np.uint32)
+    expert = rng.integers(0, 12, n).astype(np.uint32)
+    layer = rng.integers(0, 2, n).astype(np.uint32)
+    score = rng.random(n).astype(np.float32)
+    ref = oracle.Ref("{}")
+    try:
+        ok, out, batches, cnt = ref.group_tokens(token, expert, score, layer)
+    finally:
+        ref.close()
+    sorted_ = np.array([(a.token_index, a.layer, a.expert) for a in out], np.uint32)
+    sorted_score = np.array([a.router_score for a in out], np.float32)
+    b = np.array([(x.layer, x.expert, x.first_sorted_index, x.token_count) for x in batches[:cnt]], np.uint32)
+    np.savez_compressed(OUT / "grouping.npz", token=token, expert=expert, layer=layer, score=score,
+                        ok=ok, sorted=sorted_, sorted_score=sorted_score, batches=b)
+    print("grouping", cnt, "batches")
+
+
+def decode_tables():
+    ref = oracle.Ref("{}")
+    try:
+        e8m0 = np.array([ref.lib.ref_e8m0_to_f32(v) for v in range(256)], np.float32)
+        e2m1 = np.array([ref.lib.ref_mxfp4_value(c) for c in range(16)], np.float32)
+        rng = np.random.default_rng(12)
+        silu_x = np.concatenate([rng.standard_normal(200).astype(np.float32) * 6,
+                                 np.array([0.0, -0.0, 88.0, -88.0, 1e-30, -100.0], np.float32)])
+        silu_y = np.array([ref.lib.ref_silu(float(v)) for v in silu_x], np.float32)
+    finally:
+        ref.close()
+    np.savez_compressed(OUT / "decode_tables.npz", e8m0=e8m0, e2m1=e2m1, silu_x=silu_x, silu_y=silu_y)
+    print("decode_tables")
+
+
+def main():
+    if not oracle.REF_SO.exists():
+        oracle.build(ref=True)
+    decode_tables()
+    grouping_case()
+    sigmoid_case()
+    for name, (shape, seed, tokens, store) in LAYER_CASES.items():
+        layer_case(name, shape, seed, tokens, store)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,122 @@
+"""Pins the CPU oracle (oracle/moe_oracle.c) to the reference.
+
+Against the golden fixtures written by tests/golden/make_golden.py from the
+reference's own compiled hot path, and -- where the reference library was
+built in this checkout -- against that library on fresh seeds.  Everything
+here is bit-exact: ids, weights, scores and layer outputs compare as bit
+patterns.
+"""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, golden, layer_from_golden
+
+LAYER_FIXTURES = sorted(p.name for p in GOLDEN.glob("layer_*.npz"))
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def test_decode_tables(port):
+    g = golden("decode_tables.npz")
+    e8m0 = np.array([port.lib.mo_e8m0_to_f32(v) for v in range(256)], np.float32)
+    e2m1 = np.array([port.lib.mo_mxfp4_value(c) for c in range(16)], np.float32)
+    assert np.array_equal(bits(e8m0), bits(g["e8m0"]))
+    assert np.array_equal(bits(e2m1), bits(g["e2m1"]))
+    # known answers from the reference source itself
+    assert e8m0[127] == 1.0 and e8m0[0] == 2.0 ** -127 and np.isinf(e8m0[255])
+    assert list(e2m1[:8]) == [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+    silu = np.array([port.lib.mo_silu(float(v)) for v in g["silu_x"]], np.float32)
+    assert np.array_equal(bits(silu), bits(g["silu_y"]))
+
+
+@pytest.mark.parametrize("name", LAYER_FIXTURES)
+def test_layer_matches_reference_fixture(name, port, synth):
+    g = golden(name)
+    li = layer_from_golden(synth, g)
+    y, ids, w, ties = port.moe_layer(li)
+    assert ties == 0
+    assert np.array_equal(ids, g["ids"])
+    assert np.array_equal(bits(w), bits(g["w"]))
+    assert np.array_equal(bits(y), bits(g["y"]))
+    _, _, scores, _ = port.router_topk(li)
+    assert np.array_equal(bits(scores), bits(g["scores"]))
+
+
+def test_sigmoid_router_fixture(port, synth):
+    g = golden("router_sigmoid.npz")
+    shape = synth.small_shape(top_k=int(g["top_k"]), experts=int(g["experts"]), hidden=int(g["hidden"]),
+                              tokens=g["x"].shape[0])
+    li = synth.LayerInputs(shape, g["router"], None, None, None, g["x"])
+    ids, w, scores, ties = port.router_topk(li, score_sigmoid=1, norm_topk=int(g["norm_topk"]),
+                                            routed_scale=float(g["routed_scale"]))
+    assert ties == 0
+    assert np.array_equal(ids, g["ids"])
+    assert np.array_equal(bits(w), bits(g["w"]))
+    assert np.array_equal(bits(scores), bits(g["scores"]))
+
+
+def test_grouping_fixture(port):
+    g = golden("grouping.npz")
+    ok, out, batches, cnt = port.group_tokens(g["token"], g["expert"], g["score"], g["layer"])
+    assert ok == int(g["ok"])
+    sorted_ = np.array([(a.token_index, a.layer, a.expert) for a in out], np.uint32)
+    assert np.array_equal(sorted_, g["sorted"])
+    b = np.array([(x.layer, x.expert, x.first_sorted_index, x.token_count) for x in batches[:cnt]], np.uint32)
+    assert np.array_equal(b, g["batches"])
+
+
+def test_grouping_edge_cases(port):
+    # empty input fails with zero batches; one assignment is one batch
+    # (token_grouping.cpp.inc:9-28)
+    ok, _, _, cnt = port.group_tokens([], [])
+    assert ok == 0 and cnt == 0
+    ok, out, batches, cnt = port.group_tokens([5], [3])
+    assert ok == 1 and cnt == 1 and batches[0].token_count == 1 and batches[0].expert == 3
+
+
+def test_tail_block_dot(port, synth):
+    rng = np.random.default_rng(5)
+    for cols in (1, 17, 31, 33, 80, 100):
+        pk = synth.gen_mxfp4(rng, (), 4, cols)
+        x = rng.standard_normal(cols).astype(np.float32)
+        out = port.mxfp4_dot_rows(pk, x)
+        # exact rational value, independent of the summation order
+        vals = np.zeros((4, cols), np.float64)
+        nblk = (cols + 31) // 32
+        for r in range(4):
+            for b in range(nblk):
+                blk = pk[r, b * 17:(b + 1) * 17]
+                s = 2.0 ** (int(blk[0]) - 127)
+                for i in range(min(32, cols - b * 32)):
+                    code = (blk[1 + i] & 15) if i < 16 else (blk[1 + i - 16] >> 4)
+                    vals[r, b * 32 + i] = port.lib.mo_mxfp4_value(int(code)) * s
+        want = vals @ x.astype(np.float64)
+        assert np.allclose(out, want, rtol=1e-5, atol=1e-6)
+
+
+@pytest.fixture(scope="module")
+def ref_lib(oracle_mod):
+    if not oracle_mod.REF_SO.exists():
+        if not oracle_mod.REFERENCE_ROOT.is_dir():
+            pytest.skip("reference sources absent; fixtures pin the oracle instead")
+        oracle_mod.build(ref=True)
+    return oracle_mod
+
+
+@pytest.mark.parametrize("seed", [21, 22])
+def test_port_matches_reference_fresh_seeds(seed, ref_lib, port, synth):
+    for shape in (synth.small_shape(tokens=12, experts=12, top_k=3),
+                  synth.small_shape(name="s2", hidden=96, intermediate=64, tokens=9, shared=True)):
+        li = synth.make_layer(shape, seed=seed)
+        ref = ref_lib.Ref(ref_lib.metadata_json(shape.top_k, norm_topk=shape.norm_topk))
+        try:
+            y2, i2, w2 = ref.moe_layer(li)
+        finally:
+            ref.close()
+        y1, i1, w1, ties = port.moe_layer(li)
+        assert ties == 0
+        assert np.array_equal(i1, i2)
+        assert np.array_equal(bits(w1), bits(w2))
+        assert np.array_equal(bits(y1), bits(y2))
