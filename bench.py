@@ -1,0 +1,361 @@
+"""Benchmark of the B200 MoE expert-FFN layer (the BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 1] [--tokens 256]
+
+Prints ONE JSON line on rank 0.
+
+Workload (N=1 headline): configuration 1 of the benchmark -- H=2880, 32
+experts, top-4, I=2880, SwiGLU, MXFP4 weights, Zipf(1.1)-skewed routing --
+at its largest decode batch, 256 tokens per step.  Synthetic, seeded inputs
+(there is no dataset for this path).  A step is one layer forward over one
+batch: router top-k, permutation, gather, gate/up grouped GEMM + SwiGLU, down
+grouped GEMM, weighted combine.
+
+* value     tokens/s over the timed steps with inputs resident in HBM, timed
+            with CUDA events on the launching stream (max over ranks);
+* e2e       the same metric through the host-buffer C-ABI call
+            (moe_b200_layer_forward_host): pinned-host x in, y/ids/weights out,
+            copies inside the timed region;
+* roofline  the dominant kernel (gate/up grouped GEMM): algorithmic bytes per
+            launch (MXFP4 bytes of the distinct experts routed to + activation
+            rows in + intermediate out) / its CUDA-event duration, against the
+            measured HBM copy bandwidth;
+* cpu_baseline  the reference's own CPU path (oracle/_ref/libmoe_ref.so, the
+            reference sources compiled by oracle/Makefile) timed on this host's
+            cores over one 256-token batch (kind "reference"), or the C
+            restatement when that library is absent (kind "port").
+
+L2: the 423 MB of expert weights a step streams exceed the 126 MB L2, so no
+flush is needed between steps ("l2": "inputs_exceed_l2").
+
+Multi-GPU (torchrun, N ranks): expert-parallel sharding is not built yet;
+every rank runs its own replica of the layer on its own token batch (weak
+scaling, no collective on the data path) and value sums the ranks' tokens
+over the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "storage.llm_b200"
+
+
+def load_pkg():
+    if "moe_b200" in sys.modules:
+        return sys.modules["moe_b200"]
+    spec = importlib.util.spec_from_file_location("moe_b200", PKG / "__init__.py",
+                                                  submodule_search_locations=[str(PKG)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["moe_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        load = sorted(sm)[len(sm) // 2:]  # upper half ~ under load
+        return {"sm_mhz": float(np.median(load)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(li, seconds: float = 8.0):
+    """The reference's CPU layer (or the C restatement) on this host's cores."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle  # test infrastructure: the timed CPU baseline only
+    s = li.shape
+    if oracle.REF_SO.exists():
+        ref = oracle.Ref(oracle.metadata_json(s.top_k, norm_topk=s.norm_topk))
+        run = lambda: ref.moe_layer(li)
+        kind, cores = "reference", int(ref.lib.ref_row_threads())
+    else:
+        if not oracle.PORT_SO.exists():
+            oracle.build(ref=False)
+        port = oracle.Port()
+        cores = os.cpu_count() or 1
+        run = lambda: port.moe_layer(li, threads=cores)
+        kind = "port"
+    run()  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        run()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= 20:
+            break
+    T = li.x.shape[0]
+    try:
+        cpu = subprocess.run(["bash", "-c", "lscpu | grep 'Model name' | head -1 | cut -d: -f2"],
+                             capture_output=True, text=True).stdout.strip()
+    except OSError:
+        cpu = ""
+    return {"value": T * reps / el, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"{reps} x {T}-token batches of the same workload ({el:.1f} s), per-token reference "
+                      f"layer order, -march=x86-64-v3, host CPU {cpu}"}
+
+
+def run_reference(args, shape, metric):
+    """--impl reference: the reference's CPU path on the host cores."""
+    import moe_b200.synth as synth
+    li = synth.make_layer(shape, seed=0, tokens=args.tokens)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    if oracle.REF_SO.exists():
+        ref = oracle.Ref(oracle.metadata_json(shape.top_k, norm_topk=shape.norm_topk))
+        step = lambda: ref.moe_layer(li)
+        kind, cores = "reference", int(ref.lib.ref_row_threads())
+    else:
+        if not oracle.PORT_SO.exists():
+            oracle.build(ref=False)
+        port = oracle.Port()
+        cores = os.cpu_count() or 1
+        step = lambda: port.moe_layer(li, threads=cores)
+        kind = "port"
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = args.tokens * args.steps / el
+    return {"metric": metric, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded)", "config": config_dict(shape, args),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
+                             "sample": f"{args.steps} x {args.tokens}-token batches"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def config_dict(shape, args):
+    return {"workload": f"config{args.config}: H{shape.hidden} E{shape.experts} top{shape.top_k} "
+                        f"I{shape.intermediate} SwiGLU MXFP4, {args.tokens} tokens/step"
+                        + (f", skew {shape.skew}" if shape.skew else ""),
+            "hidden": shape.hidden, "experts": shape.experts, "top_k": shape.top_k,
+            "intermediate": shape.intermediate, "tokens_per_step": args.tokens, "shared_expert": shape.shared,
+            "parallelism": f"replica{args.gpus}" if args.gpus > 1 else "single",
+            "l2": "inputs_exceed_l2"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--tokens", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    load_pkg()
+    import moe_b200.synth as synth
+
+    shape = synth.CONFIGS[args.config]
+    if args.tokens <= 0:
+        args.tokens = 256 if args.config == 1 else (shape.tokens or sum(synth.prefill_lengths()))
+    metric = "MoE-layer tokens/sec"
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args, shape, metric)), flush=True)
+        return
+
+    import torch
+    import moe_b200.lib as L
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+
+    li = synth.make_layer(shape, seed=0, tokens=args.tokens)
+    if world > 1:  # each rank its own token batch (weak scaling)
+        li.x = synth.gen_tokens(shape, args.tokens, seed=100 + rank, mu=li.mu)
+    eng = L.Engine(local)
+    eng.upload_layer(li)
+    cfg = L.Engine.cfg(shape)
+    T, H, K = args.tokens, shape.hidden, shape.top_k
+    x = torch.from_numpy(li.x.view(np.int16)).cuda()
+    y = torch.empty((T, H), dtype=torch.int16, device="cuda")
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        eng.forward(cfg, x, T, y_bf16=y, ids=ids, w=w, stream=sp)
+
+    for _ in range(args.warmup):
+        step()
+    eng.sync(sp)
+    launches_per_step = eng.launches()
+
+    # ---- device-timed region: inputs resident in HBM ----
+    eng.profile_enable(args.steps)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    eng.sync(sp)
+    ms = start.elapsed_time(end)
+    stage_ms, prof_calls = eng.profile_read()
+    eng.profile_enable(0)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    value = T * args.steps * world / (ms / 1000.0)
+
+    # ---- end to end through the host-buffer C-ABI call ----
+    xh = torch.from_numpy(li.x.view(np.int16)).pin_memory()
+    yh = torch.empty((T, H), dtype=torch.int16).pin_memory()
+    idsh = torch.empty((T, K), dtype=torch.int32).pin_memory()
+    wh = torch.empty((T, K), dtype=torch.float32).pin_memory()
+    lib = L.load()
+    import ctypes as C
+
+    def step_host():
+        ok = lib.moe_b200_layer_forward_host(eng.h, C.byref(cfg), xh.data_ptr(), T, yh.data_ptr(), None,
+                                             idsh.data_ptr(), wh.data_ptr(), None, eng.err)
+        if not ok:
+            raise L.MoEError(eng.err.value.decode())
+
+    for _ in range(3):
+        step_host()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e2e_steps = max(10, args.steps // 2)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        step_host()
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = T * e2e_steps * world / e2e_s
+
+    # ---- roofline of the dominant kernel (gate/up grouped GEMM) ----
+    counts = eng.read(L.BUF_GROUP_COUNT, (shape.experts,), np.uint32)
+    distinct = int((counts > 0).sum())
+    P = T * K
+    Kp = (H + 63) // 64 * 64
+    Ip = (shape.intermediate + 63) // 64 * 64
+    gu_weight_bytes = distinct * 2 * shape.intermediate * H * 17 / 32
+    gu_bytes = gu_weight_bytes + P * Kp * 2 + P * Ip * 2
+    gu_ms = stage_ms["gate_up"] / max(prof_calls, 1)
+    hbm, bf16, peak_kind = measured_peaks()
+    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
+    dn_ms = stage_ms["down"] / max(prof_calls, 1)
+    dn_bytes = distinct * shape.intermediate * H * 17 / 32 + P * Ip * 2 + P * H * 4
+
+    result = {
+        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": config_dict(shape, args),
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2 + T * K * 8},
+        "roofline": {"kernel": "gemm_tc_kernel<gate_up>", "bound": "hbm", "achieved": achieved, "peak": hbm,
+                     "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_kind,
+                     "traffic": None, "algorithmic_bytes_per_launch": gu_bytes,
+                     "launch_ms": gu_ms, "distinct_experts": distinct},
+        "stages_ms_per_step": {k: v / max(prof_calls, 1) for k, v in stage_ms.items()},
+        "down_gemm": {"achieved_gbs": dn_bytes / (dn_ms / 1000.0) / 1e9, "launch_ms": dn_ms},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        li_cpu = synth.make_layer(shape, seed=0, tokens=args.tokens)
+        result["cpu_baseline"] = cpu_baseline(li_cpu)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

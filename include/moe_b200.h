@@ -1,0 +1,193 @@
+/*
+ * moe_b200.h -- C ABI of the B200 (sm_100a) MoE expert-FFN hot path.
+ *
+ * Drop-in for the CPU expert dispatch of jujumelona/storage.llm's moe_engine:
+ * router top-k, token permutation into ragged per-expert groups, MXFP4
+ * gate/up grouped GEMM with fused SwiGLU, down grouped GEMM and the weighted
+ * combine.  Conventions follow the reference C API
+ * (moe_engine/include/moe_pc_engine.h and include/parts/*.h.inc):
+ *   - functions return int 1 on success and 0 on failure, never throw;
+ *   - a caller-owned `err` buffer of MOE_B200_ERR_LEN bytes (may be NULL)
+ *     receives a human-readable message, like moe_generation_stats_t.error
+ *     (moe_forward_api.h.inc:63-69);
+ *   - buffers are caller-owned with explicit element counts that are checked
+ *     against the layer shape (expert_triplet_cpu.cpp.inc:34-43);
+ *   - weights are given in the reference's GGUF MXFP4 byte layout (17-byte
+ *     blocks per 32 K-elements, rows of ceil(K/32)*17 bytes,
+ *     tensor_layout.cpp.inc:174-176) and router weights as bf16 [E x H];
+ *   - one engine per CUDA device; calls on one engine are not reentrant.
+ * No torch types cross this boundary.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ERR_LEN 160
+
+#if defined(__GNUC__)
+#define MOE_B200_API __attribute__((visibility("default")))
+#else
+#define MOE_B200_API
+#endif
+
+typedef struct moe_b200_engine moe_b200_engine_t;
+
+typedef struct {
+    int32_t device;      /* CUDA device ordinal */
+    uint32_t max_layers; /* number of layer weight slots (0 -> 1) */
+} moe_b200_init_t;
+
+enum {
+    MOE_B200_SCORE_SOFTMAX = 0, /* generation_router.cpp.inc:606-622 (default) */
+    MOE_B200_SCORE_SIGMOID = 1  /* generation_router.cpp.inc:600-605 */
+};
+
+enum {
+    MOE_B200_GEMM_TCGEN05 = 0, /* tensor-core grouped GEMMs (the product path) */
+    MOE_B200_GEMM_SIMT = 1     /* CUDA-core grouped GEMMs, a cross-check for tests */
+};
+
+/* Explicit form of the routing metadata the reference reads from GGUF JSON
+ * keys (num_experts_per_tok, scoring_func, norm_topk_prob,
+ * routed_scaling_factor: generation_router.cpp.inc:361-482). */
+typedef struct {
+    uint32_t hidden;       /* H, multiple of 8 */
+    uint32_t intermediate; /* I */
+    uint32_t experts;      /* E routed experts, <= 1024 */
+    uint32_t top_k;        /* k, 1..32 and <= E */
+    int32_t layer;         /* weight slot */
+    int32_t score_func;    /* MOE_B200_SCORE_* */
+    int32_t norm_topk;     /* renormalise the k weights (:659-668) */
+    float routed_scale;    /* applied for sigmoid routers only (:669-674); 0 -> 1 */
+    int32_t use_shared;    /* add the layer's always-on shared expert (generation_mlp.cpp.inc:833-860) */
+    int32_t gemm_path;     /* MOE_B200_GEMM_* */
+} moe_b200_layer_cfg_t;
+
+/* Same layout as moe_token_expert_assignment_t / moe_expert_batch_t
+ * (include/parts/moe_tensor_types.h.inc:62-74). */
+typedef struct {
+    uint32_t token_index;
+    uint32_t layer;
+    uint32_t expert;
+    float router_score;
+} moe_b200_assignment_t;
+
+typedef struct {
+    uint32_t layer;
+    uint32_t expert;
+    uint32_t first_sorted_index;
+    uint32_t token_count;
+} moe_b200_batch_t;
+
+/* Engine lifetime.  Replaces moe_pc_engine_create/destroy
+ * (include/parts/moe_lifecycle_api.h.inc:6-7) for the GPU hot path. */
+MOE_B200_API moe_b200_engine_t* moe_b200_create(const moe_b200_init_t* init, char* err);
+MOE_B200_API void moe_b200_destroy(moe_b200_engine_t* engine);
+
+/* Router weight ffn_gate_inp.weight, bf16 [experts x hidden] row-major
+ * (the tensor moe_map_router_tensor resolves, generation_router.cpp.inc:
+ * 140-186).  `src_on_device` = 1 when `w_bf16` is device memory. */
+MOE_B200_API int moe_b200_upload_router(moe_b200_engine_t* engine, int32_t layer, const uint16_t* w_bf16, uint32_t experts,
+                           uint32_t hidden, int32_t src_on_device, char* err);
+
+/* One expert's gate [I x H], up [I x H] and down [H x I] projections in the
+ * reference's GGUF MXFP4 bytes (per-expert records of codec_table.cpp.inc:
+ * 1586-1646).  expert = -1 uploads the layer's shared expert.  The bytes are
+ * repacked once into the device tile layout; the caller keeps ownership.
+ * Replaces the residency upload of device_copy_tensor_from_host
+ * (device_tensor_copy_ops.cpp.inc:73) for expert triplets.  The router of
+ * the layer must be uploaded first. */
+MOE_B200_API int moe_b200_upload_expert(moe_b200_engine_t* engine, int32_t layer, int32_t expert, const uint8_t* gate,
+                           uint64_t gate_bytes, const uint8_t* up, uint64_t up_bytes, const uint8_t* down,
+                           uint64_t down_bytes, uint32_t hidden, uint32_t intermediate, int32_t src_on_device,
+                           char* err);
+
+/* The MoE FFN for `tokens` tokens, all pointers device memory, enqueued on
+ * `stream` (a cudaStream_t; NULL = legacy default stream).  Replaces the
+ * per-token moe_layer_moe_mlp_f32 expert phase (generation_mlp.cpp.inc:
+ * 874-1431) and fills the batched slot moe_layer_moe_mlp_batched_f32
+ * (generation_api_batch.cpp.inc:68-78).
+ *   x_bf16    [tokens x H] expert input (the router input)
+ *   y_bf16    [tokens x H] output mlp = shared + sum_j w_j * expert_j(x) (may be NULL)
+ *   y_f32     [tokens x H] the same in fp32 (may be NULL)
+ *   topk_ids  [tokens x k] selected experts, descending score (may be NULL)
+ *   topk_w    [tokens x k] their weights (may be NULL)
+ *   perm      [tokens x k] assignment index t*k+j at each sorted position,
+ *             the order of moe_pc_group_tokens_by_expert (may be NULL)
+ * The residual add (generation_mlp.cpp.inc:572-594) stays with the caller.
+ * Errors found on the device are reported by moe_b200_sync. */
+MOE_B200_API int moe_b200_layer_forward(moe_b200_engine_t* engine, const moe_b200_layer_cfg_t* cfg, const uint16_t* x_bf16,
+                           uint32_t tokens, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w,
+                           uint32_t* perm, void* stream, char* err);
+
+/* Same with host buffers: copies in, runs, copies out and synchronises. */
+MOE_B200_API int moe_b200_layer_forward_host(moe_b200_engine_t* engine, const moe_b200_layer_cfg_t* cfg,
+                                const uint16_t* x_bf16, uint32_t tokens, uint16_t* y_bf16, float* y_f32,
+                                int32_t* topk_ids, float* topk_w, uint32_t* perm, char* err);
+
+/* Waits for the engine's work and reports any error a kernel recorded
+ * (bounded waits that timed out, out-of-range expert ids). */
+MOE_B200_API int moe_b200_sync(moe_b200_engine_t* engine, void* stream, char* err);
+
+/* Drop-in for moe_pc_engine_run_expert_triplet_f32
+ * (include/parts/moe_forward_api.h.inc:85-96, expert_triplet_cpu.cpp.inc:
+ * 22-106): one expert on one fp32 hidden vector, host buffers; scratch_gate
+ * receives SiLU(gate)*up, scratch_up receives up.  Synchronous. */
+MOE_B200_API int moe_b200_run_expert_triplet_f32(moe_b200_engine_t* engine, int layer, int expert, const float* hidden,
+                                    uint32_t hidden_count, float* scratch_gate, float* scratch_up,
+                                    uint32_t intermediate_count, float* out_hidden, uint32_t out_count);
+
+/* Drop-in for moe_pc_group_tokens_by_expert (include/parts/moe_names_api.h.inc:
+ * 1-8, token_grouping.cpp.inc:1-83), same signature, host buffers: sorts by
+ * (layer, expert, token_index) on the current CUDA device and emits the
+ * contiguous batches.  Assignments with equal keys keep their input order. */
+MOE_B200_API int moe_b200_group_tokens_by_expert(const moe_b200_assignment_t* assignments, uint32_t assignment_count,
+                                    moe_b200_assignment_t* out_sorted_assignments, moe_b200_batch_t* out_batches,
+                                    uint32_t max_batches, uint32_t* out_batch_count);
+
+/* Test and diagnostics hooks (no reference counterpart). */
+enum {
+    MOE_B200_PROJ_GATE = 0,
+    MOE_B200_PROJ_UP = 1,
+    MOE_B200_PROJ_DOWN = 2
+};
+/* Decodes an uploaded projection from the device tile layout back to bf16
+ * [rows x cols] in host memory, with the kernels' own decode arithmetic. */
+MOE_B200_API int moe_b200_debug_dequant(moe_b200_engine_t* engine, int32_t layer, int32_t expert, int32_t proj,
+                           uint16_t* out_bf16, uint64_t out_elems, char* err);
+
+enum {
+    MOE_B200_BUF_LOGITS = 0,     /* float  [T x E] */
+    MOE_B200_BUF_SCORES = 1,     /* float  [T x E] router scores after softmax/sigmoid */
+    MOE_B200_BUF_GROUP_COUNT = 2,/* uint32 [G] */
+    MOE_B200_BUF_GROUP_OFFSET = 3,/* uint32 [G+1] */
+    MOE_B200_BUF_ROW_TOKEN = 4,  /* uint32 [P] source token of each permuted row */
+    MOE_B200_BUF_XPERM = 5,      /* bf16   [P x Kp] */
+    MOE_B200_BUF_HPERM = 6,      /* bf16   [P x Ip] */
+    MOE_B200_BUF_YPERM = 7       /* float  [P x H] */
+};
+/* Copies an internal buffer of the last forward call to host memory. */
+MOE_B200_API int moe_b200_debug_read(moe_b200_engine_t* engine, int32_t which, void* dst, uint64_t bytes, char* err);
+
+/* Stage timing with CUDA events recorded on the forward's own stream.
+ * Stages: 0 router (logits + top-k), 1 permutation (count/scan/scatter),
+ * 2 gather of permuted rows, 3 gate/up GEMM, 4 down GEMM, 5 combine.
+ * enable(max_calls > 0) starts recording for up to max_calls forwards
+ * (0 stops); read() synchronises and returns the summed milliseconds per
+ * stage and the number of forwards recorded. */
+#define MOE_B200_STAGES 6
+MOE_B200_API int moe_b200_profile_enable(moe_b200_engine_t* engine, uint32_t max_calls, char* err);
+MOE_B200_API int moe_b200_profile_read(moe_b200_engine_t* engine, float* stage_ms, uint32_t* calls, char* err);
+
+/* Number of kernel launches issued by the last moe_b200_layer_forward. */
+MOE_B200_API uint32_t moe_b200_last_launch_count(const moe_b200_engine_t* engine);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H */

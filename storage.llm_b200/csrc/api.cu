@@ -1,0 +1,740 @@
+// C ABI of the B200 MoE expert-FFN hot path (include/moe_b200.h): engine,
+// device weight cache, workspace and the per-layer launch sequence
+//   router -> permute (count/scan/scatter) -> gather -> gate/up GEMM ->
+//   down GEMM -> combine
+// all enqueued on the caller's stream with no host synchronisation, so the
+// sequence can be captured in a CUDA graph.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace moe_b200;
+
+namespace {
+
+void set_err(char* err, const char* fmt, ...) {
+    if (!err) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, MOE_B200_ERR_LEN, fmt, ap);
+    va_end(ap);
+}
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) {                                                                   \
+            set_err(err, "%s failed: %s", #call, cudaGetErrorString(e_));                          \
+            return 0;                                                                              \
+        }                                                                                          \
+    } while (0)
+
+// Device buffer that only grows.
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    cudaError_t reserve(size_t want) {
+        if (want <= bytes) return cudaSuccess;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMalloc(&ptr, want);
+        if (e == cudaSuccess) bytes = want;
+        return e;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(ptr);
+    }
+};
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct LayerWeights {
+    uint32_t E = 0, H = 0, I = 0;
+    DevBuf router;          // bf16 [E x H]
+    DevBuf gu;              // [E+1] groups of interleaved gate/up tiles
+    DevBuf dn;              // [E+1] groups of down tiles
+    uint64_t gu_stride = 0, dn_stride = 0;
+    std::vector<uint8_t> present;  // [E+1]; slot E = shared expert
+};
+
+uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+
+}  // namespace
+
+struct moe_b200_engine {
+    int device = 0;
+    int num_sms = 148;
+    std::vector<LayerWeights> layers;
+    DevBuf staging;  // GGUF bytes copied from the host before the repack
+    // workspace
+    DevBuf logits, scores, ids, wts, tile_counts, rank, pos_of, row_token, row_assign;
+    DevBuf g_count, g_offset, g_gu_off, g_dn_off;
+    DevBuf xperm, hperm, yperm;
+    DevBuf err_word;
+    // host-call staging
+    DevBuf hx, hy, hyf, hids, hw, hperm_out, tri;
+    CUtensorMap tmap_x{}, tmap_h{};
+    void* tmap_x_base = nullptr;
+    void* tmap_h_base = nullptr;
+    uint64_t tmap_x_dims[2] = {0, 0}, tmap_h_dims[2] = {0, 0};
+    EncodeTiledFn encode = nullptr;
+    // last-forward geometry (debug reads)
+    uint32_t last_T = 0, last_E = 0, last_G = 0, last_P = 0, last_Kp = 0, last_Ip = 0, last_H = 0;
+    uint32_t last_launches = 0;
+    // stage profiling
+    std::vector<cudaEvent_t> prof_events;  // [max_calls][MOE_B200_STAGES + 1]
+    uint32_t prof_max = 0, prof_calls = 0;
+};
+
+namespace {
+
+int check_dims(const moe_b200_layer_cfg_t* c, char* err) {
+    if (!c) {
+        set_err(err, "null layer config");
+        return 0;
+    }
+    if (c->hidden == 0 || c->hidden % 8 != 0 || c->hidden > 65536) {
+        set_err(err, "hidden=%u must be a positive multiple of 8 (<= 65536)", c->hidden);
+        return 0;
+    }
+    if (c->intermediate == 0 || c->intermediate > 100000) {
+        set_err(err, "invalid intermediate size %u", c->intermediate);
+        return 0;
+    }
+    if (c->experts == 0 || c->experts > 1024) {
+        set_err(err, "experts=%u outside 1..1024", c->experts);
+        return 0;
+    }
+    if (c->top_k == 0 || c->top_k > 32 || c->top_k > c->experts) {
+        set_err(err, "top_k=%u outside 1..min(32, experts)", c->top_k);
+        return 0;
+    }
+    return 1;
+}
+
+int make_tmap(moe_b200_engine* eng, CUtensorMap* map, void* base, uint64_t cols, uint64_t rows, char* err) {
+    if (!eng->encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (!fn || q != cudaDriverEntryPointSuccess) {
+            set_err(err, "cuTensorMapEncodeTiled unavailable");
+            return 0;
+        }
+        eng->encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {64, kBlockN};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = eng->encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_err(err, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return 0;
+    }
+    return 1;
+}
+
+LayerWeights* get_layer(moe_b200_engine* eng, int32_t layer, char* err) {
+    if (!eng) {
+        set_err(err, "null engine");
+        return nullptr;
+    }
+    if (layer < 0 || (size_t)layer >= eng->layers.size()) {
+        set_err(err, "layer %d outside 0..%zu", layer, eng->layers.size() - 1);
+        return nullptr;
+    }
+    return &eng->layers[layer];
+}
+
+}  // namespace
+
+extern "C" {
+
+moe_b200_engine_t* moe_b200_create(const moe_b200_init_t* init, char* err) {
+    const int device = init ? init->device : 0;
+    const uint32_t layers = (init && init->max_layers) ? init->max_layers : 1;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+        set_err(err, "CUDA device %d not available (%d devices)", device, count);
+        return nullptr;
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+        set_err(err, "cudaGetDeviceProperties failed");
+        return nullptr;
+    }
+    if (prop.major != 10) {
+        set_err(err, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device, prop.major,
+                prop.minor);
+        return nullptr;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        set_err(err, "cudaSetDevice(%d) failed", device);
+        return nullptr;
+    }
+    auto* eng = new (std::nothrow) moe_b200_engine();
+    if (!eng) {
+        set_err(err, "out of host memory");
+        return nullptr;
+    }
+    eng->device = device;
+    eng->num_sms = prop.multiProcessorCount;
+    eng->layers.resize(layers);
+    if (eng->err_word.reserve(sizeof(uint32_t)) != cudaSuccess ||
+        cudaMemset(eng->err_word.ptr, 0, sizeof(uint32_t)) != cudaSuccess) {
+        set_err(err, "device allocation failed");
+        delete eng;
+        return nullptr;
+    }
+    return eng;
+}
+
+void moe_b200_destroy(moe_b200_engine_t* eng) {
+    if (!eng) return;
+    cudaSetDevice(eng->device);
+    cudaDeviceSynchronize();
+    for (auto& l : eng->layers) {
+        l.router.release();
+        l.gu.release();
+        l.dn.release();
+    }
+    DevBuf* bufs[] = {&eng->staging, &eng->logits, &eng->scores, &eng->ids, &eng->wts, &eng->tile_counts,
+                      &eng->rank, &eng->pos_of, &eng->row_token, &eng->row_assign, &eng->g_count,
+                      &eng->g_offset, &eng->g_gu_off, &eng->g_dn_off, &eng->xperm, &eng->hperm,
+                      &eng->yperm, &eng->err_word, &eng->hx, &eng->hy, &eng->hyf, &eng->hids,
+                      &eng->hw, &eng->hperm_out, &eng->tri};
+    for (DevBuf* b : bufs) b->release();
+    for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
+    delete eng;
+}
+
+int moe_b200_upload_router(moe_b200_engine_t* eng, int32_t layer, const uint16_t* w, uint32_t experts,
+                           uint32_t hidden, int32_t src_on_device, char* err) {
+    LayerWeights* L = get_layer(eng, layer, err);
+    if (!L) return 0;
+    if (!w || experts == 0 || experts > 1024 || hidden == 0 || hidden % 8) {
+        set_err(err, "invalid router upload (experts=%u hidden=%u)", experts, hidden);
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    if (L->E && (L->E != experts || L->H != hidden)) {
+        // a new shape invalidates the layer's experts
+        L->gu.release();
+        L->dn.release();
+        L->present.clear();
+        L->I = 0;
+    }
+    const size_t bytes = (size_t)experts * hidden * 2;
+    CK(L->router.reserve(bytes));
+    CK(cudaMemcpy(L->router.ptr, w, bytes, src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+    L->E = experts;
+    L->H = hidden;
+    return 1;
+}
+
+int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert, const uint8_t* gate,
+                           uint64_t gate_bytes, const uint8_t* up, uint64_t up_bytes, const uint8_t* down,
+                           uint64_t down_bytes, uint32_t hidden, uint32_t intermediate, int32_t src_on_device,
+                           char* err) {
+    LayerWeights* L = get_layer(eng, layer, err);
+    if (!L) return 0;
+    if (!L->E) {
+        set_err(err, "upload the router of layer %d before its experts", layer);
+        return 0;
+    }
+    if (hidden != L->H || intermediate == 0 || intermediate > 100000) {
+        set_err(err, "expert shape H=%u I=%u does not match layer H=%u", hidden, intermediate, L->H);
+        return 0;
+    }
+    if (expert < -1 || expert >= (int32_t)L->E) {
+        set_err(err, "expert %d outside -1..%u", expert, L->E - 1);
+        return 0;
+    }
+    const uint64_t gu_need = (uint64_t)intermediate * ceil_div(hidden, 32) * 17;
+    const uint64_t dn_need = (uint64_t)hidden * ceil_div(intermediate, 32) * 17;
+    if (!gate || !up || !down || gate_bytes < gu_need || up_bytes < gu_need || down_bytes < dn_need) {
+        set_err(err, "expert %d: MXFP4 byte counts %llu/%llu/%llu below %llu/%llu/%llu", expert,
+                (unsigned long long)gate_bytes, (unsigned long long)up_bytes, (unsigned long long)down_bytes,
+                (unsigned long long)gu_need, (unsigned long long)gu_need, (unsigned long long)dn_need);
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    if (L->I != intermediate || !L->gu.ptr) {
+        L->I = intermediate;
+        L->gu_stride = (uint64_t)ceil_div(intermediate, kTileRows) * ceil_div(hidden, kTileK) * 2 * kTileBytes;
+        L->dn_stride = (uint64_t)ceil_div(hidden, kTileRows) * ceil_div(intermediate, kTileK) * kTileBytes;
+        L->gu.release();
+        L->dn.release();
+        CK(L->gu.reserve(L->gu_stride * (L->E + 1)));
+        CK(L->dn.reserve(L->dn_stride * (L->E + 1)));
+        L->present.assign(L->E + 1, 0);
+    }
+    const uint32_t slot = expert < 0 ? L->E : (uint32_t)expert;
+    const uint8_t* src[3] = {gate, up, down};
+    const uint64_t need[3] = {gu_need, gu_need, dn_need};
+    const uint8_t* dsrc[3] = {gate, up, down};
+    if (!src_on_device) {
+        CK(eng->staging.reserve(2 * gu_need + dn_need));
+        uint8_t* st = eng->staging.as<uint8_t>();
+        uint64_t off = 0;
+        for (int i = 0; i < 3; ++i) {
+            CK(cudaMemcpy(st + off, src[i], need[i], cudaMemcpyHostToDevice));
+            dsrc[i] = st + off;
+            off += need[i];
+        }
+    }
+    uint8_t* gu_dst = L->gu.as<uint8_t>() + L->gu_stride * slot;
+    uint8_t* dn_dst = L->dn.as<uint8_t>() + L->dn_stride * slot;
+    CK(launch_repack_mxfp4(dsrc[0], intermediate, hidden, gu_dst, 2 * kTileBytes, 0));
+    CK(launch_repack_mxfp4(dsrc[1], intermediate, hidden, gu_dst + kTileBytes, 2 * kTileBytes, 0));
+    CK(launch_repack_mxfp4(dsrc[2], hidden, intermediate, dn_dst, kTileBytes, 0));
+    CK(cudaDeviceSynchronize());
+    L->present[slot] = 1;
+    return 1;
+}
+
+int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const uint16_t* x,
+                           uint32_t T, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w,
+                           uint32_t* perm, void* stream, char* err) {
+    if (!check_dims(cfg, err)) return 0;
+    LayerWeights* L = get_layer(eng, cfg->layer, err);
+    if (!L) return 0;
+    const uint32_t H = cfg->hidden, I = cfg->intermediate, E = cfg->experts, K = cfg->top_k;
+    if (L->E != E || L->H != H || L->I != I) {
+        set_err(err, "layer %d holds E=%u H=%u I=%u, config asks E=%u H=%u I=%u", cfg->layer, L->E, L->H, L->I, E,
+                H, I);
+        return 0;
+    }
+    for (uint32_t e = 0; e < E; ++e) {
+        if (!L->present[e]) {
+            set_err(err, "expert %u of layer %d was never uploaded", e, cfg->layer);
+            return 0;
+        }
+    }
+    const bool shared = cfg->use_shared != 0;
+    if (shared && !L->present[E]) {
+        set_err(err, "layer %d has no shared expert uploaded", cfg->layer);
+        return 0;
+    }
+    if (T == 0) return 1;
+    if (!x) {
+        set_err(err, "null input");
+        return 0;
+    }
+    if ((uint64_t)T * K > 0x7fffffffull) {
+        set_err(err, "tokens x top_k too large");
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const uint32_t n = T * K;
+    const uint32_t shared_rows = shared ? T : 0;
+    const uint32_t P = n + shared_rows;
+    const uint32_t G = E + (shared ? 1 : 0);
+    const uint32_t Kp = round_up(H, kTileK), Ip = round_up(I, kTileK);
+    const uint32_t rows_cap = std::max(P, kBlockN);
+    const uint32_t ntiles = sort_tiles(n);
+
+    CK(eng->logits.reserve((size_t)T * E * 4));
+    CK(eng->scores.reserve((size_t)T * E * 4));
+    CK(eng->ids.reserve((size_t)n * 4));
+    CK(eng->wts.reserve((size_t)n * 4));
+    CK(eng->tile_counts.reserve((size_t)std::max(ntiles, 1u) * E * 4));
+    CK(eng->rank.reserve((size_t)n * 4));
+    CK(eng->pos_of.reserve((size_t)n * 4));
+    CK(eng->row_token.reserve((size_t)P * 4));
+    CK(eng->row_assign.reserve((size_t)P * 4));
+    CK(eng->g_count.reserve((size_t)(G + 1) * 4));
+    CK(eng->g_offset.reserve((size_t)(G + 1) * 4));
+    CK(eng->g_gu_off.reserve((size_t)(G + 1) * 4));
+    CK(eng->g_dn_off.reserve((size_t)(G + 1) * 4));
+    CK(eng->xperm.reserve((size_t)rows_cap * Kp * 2));
+    CK(eng->hperm.reserve((size_t)rows_cap * Ip * 2));
+    CK(eng->yperm.reserve((size_t)P * H * 4));
+
+    // tensor maps over the permuted activations and the intermediate
+    const uint64_t xrows = eng->xperm.bytes / ((uint64_t)Kp * 2), hrows = eng->hperm.bytes / ((uint64_t)Ip * 2);
+    if (eng->tmap_x_base != eng->xperm.ptr || eng->tmap_x_dims[0] != Kp || eng->tmap_x_dims[1] != xrows) {
+        if (!make_tmap(eng, &eng->tmap_x, eng->xperm.ptr, Kp, xrows, err)) return 0;
+        eng->tmap_x_base = eng->xperm.ptr;
+        eng->tmap_x_dims[0] = Kp;
+        eng->tmap_x_dims[1] = xrows;
+    }
+    if (eng->tmap_h_base != eng->hperm.ptr || eng->tmap_h_dims[0] != Ip || eng->tmap_h_dims[1] != hrows) {
+        if (!make_tmap(eng, &eng->tmap_h, eng->hperm.ptr, Ip, hrows, err)) return 0;
+        eng->tmap_h_base = eng->hperm.ptr;
+        eng->tmap_h_dims[0] = Ip;
+        eng->tmap_h_dims[1] = hrows;
+    }
+
+    cudaEvent_t* ev = nullptr;
+    if (eng->prof_max && eng->prof_calls < eng->prof_max) {
+        ev = &eng->prof_events[(size_t)eng->prof_calls * (MOE_B200_STAGES + 1)];
+        ++eng->prof_calls;
+    }
+    auto mark = [&](int i) {
+        if (ev) cudaEventRecord(ev[i], st);
+    };
+    mark(0);
+    int32_t* ids = topk_ids ? topk_ids : eng->ids.as<int32_t>();
+    float* w = topk_w ? topk_w : eng->wts.as<float>();
+    uint32_t* errw = eng->err_word.as<uint32_t>();
+    uint32_t launches = 0;
+
+    const int sigmoid = cfg->score_func == MOE_B200_SCORE_SIGMOID;
+    const float rscale = cfg->routed_scale > 0.f ? cfg->routed_scale : 1.0f;
+    CK(launch_router(x, L->router.as<uint16_t>(), T, E, H, K, sigmoid, cfg->norm_topk, rscale,
+                     eng->logits.as<float>(), ids, w, eng->scores.as<float>(), st));
+    launches += 2;
+    mark(1);
+
+    GroupInfo gi;
+    gi.count = eng->g_count.as<uint32_t>();
+    gi.offset = eng->g_offset.as<uint32_t>();
+    gi.gu_tile_off = eng->g_gu_off.as<uint32_t>();
+    gi.dn_tile_off = eng->g_dn_off.as<uint32_t>();
+    gi.block_n = kBlockN;
+    gi.gu_row_tiles = ceil_div(I, kTileRows);
+    gi.dn_row_tiles = ceil_div(H, kTileRows);
+    CK(launch_permute(ids, T, K, E, shared_rows, eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi,
+                      eng->pos_of.as<uint32_t>(), eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(),
+                      errw, st));
+    launches += 3;
+    mark(2);
+    CK(launch_gather(x, H, Kp, eng->row_token.as<uint32_t>(), P, eng->xperm.as<uint16_t>(), st));
+    launches += 1;
+    mark(3);
+
+    GemmParams gp{};
+    gp.groups = G;
+    gp.count = gi.count;
+    gp.offset = gi.offset;
+    gp.err = errw;
+    // gate/up: K = H, output columns = Ip
+    gp.wt = L->gu.as<uint8_t>();
+    gp.group_stride = L->gu_stride;
+    gp.k_tiles = Kp / kTileK;
+    gp.m_valid = Ip;
+    gp.tile_off = gi.gu_tile_off;
+    gp.h_out = eng->hperm.as<uint16_t>();
+    gp.h_stride = Ip;
+    if (cfg->gemm_path == MOE_B200_GEMM_SIMT) {
+        CK(launch_gemm_simt(kGateUp, eng->xperm.as<uint16_t>(), Kp, P, gp, Ip, st));
+    } else {
+        CK(launch_gemm_tc(kGateUp, eng->tmap_x, gp, eng->num_sms, st));
+    }
+    launches += 1;
+    mark(4);
+    // down: K = Ip, output columns = H
+    gp.wt = L->dn.as<uint8_t>();
+    gp.group_stride = L->dn_stride;
+    gp.k_tiles = Ip / kTileK;
+    gp.m_valid = H;
+    gp.tile_off = gi.dn_tile_off;
+    gp.y_out = eng->yperm.as<float>();
+    gp.y_stride = H;
+    if (cfg->gemm_path == MOE_B200_GEMM_SIMT) {
+        CK(launch_gemm_simt(kDown, eng->hperm.as<uint16_t>(), Ip, P, gp, H, st));
+    } else {
+        CK(launch_gemm_tc(kDown, eng->tmap_h, gp, eng->num_sms, st));
+    }
+    launches += 1;
+    mark(5);
+
+    CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), w, T, K, shared ? 1 : 0, n, y_bf16,
+                      y_f32, st));
+    launches += 1;
+    mark(6);
+    if (perm) {
+        CK(cudaMemcpyAsync(perm, eng->row_assign.ptr, (size_t)n * 4, cudaMemcpyDeviceToDevice, st));
+    }
+    eng->last_T = T;
+    eng->last_E = E;
+    eng->last_G = G;
+    eng->last_P = P;
+    eng->last_Kp = Kp;
+    eng->last_Ip = Ip;
+    eng->last_H = H;
+    eng->last_launches = launches;
+    return 1;
+}
+
+int moe_b200_sync(moe_b200_engine_t* eng, void* stream, char* err) {
+    if (!eng) {
+        set_err(err, "null engine");
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    CK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    uint32_t code = 0;
+    CK(cudaMemcpy(&code, eng->err_word.ptr, 4, cudaMemcpyDeviceToHost));
+    if (code != kErrNone) {
+        CK(cudaMemset(eng->err_word.ptr, 0, 4));
+        set_err(err, "device error %u (%s)", code,
+                code == kErrBadExpert ? "expert id out of range" : "bounded wait timed out in a GEMM pipeline");
+        return 0;
+    }
+    return 1;
+}
+
+int moe_b200_layer_forward_host(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const uint16_t* x,
+                                uint32_t T, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w,
+                                uint32_t* perm, char* err) {
+    if (!check_dims(cfg, err)) return 0;
+    if (!eng) {
+        set_err(err, "null engine");
+        return 0;
+    }
+    if (T == 0) return 1;
+    if (!x) {
+        set_err(err, "null input");
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    const uint32_t H = cfg->hidden, K = cfg->top_k;
+    CK(eng->hx.reserve((size_t)T * H * 2));
+    CK(eng->hy.reserve((size_t)T * H * 2));
+    CK(eng->hyf.reserve((size_t)T * H * 4));
+    CK(eng->hids.reserve((size_t)T * K * 4));
+    CK(eng->hw.reserve((size_t)T * K * 4));
+    CK(eng->hperm_out.reserve((size_t)T * K * 4));
+    cudaStream_t st = 0;
+    CK(cudaMemcpyAsync(eng->hx.ptr, x, (size_t)T * H * 2, cudaMemcpyHostToDevice, st));
+    if (!moe_b200_layer_forward(eng, cfg, eng->hx.as<uint16_t>(), T, y_bf16 ? eng->hy.as<uint16_t>() : nullptr,
+                                y_f32 ? eng->hyf.as<float>() : nullptr, eng->hids.as<int32_t>(),
+                                eng->hw.as<float>(), perm ? eng->hperm_out.as<uint32_t>() : nullptr, st, err)) {
+        return 0;
+    }
+    if (y_bf16) CK(cudaMemcpyAsync(y_bf16, eng->hy.ptr, (size_t)T * H * 2, cudaMemcpyDeviceToHost, st));
+    if (y_f32) CK(cudaMemcpyAsync(y_f32, eng->hyf.ptr, (size_t)T * H * 4, cudaMemcpyDeviceToHost, st));
+    if (topk_ids) CK(cudaMemcpyAsync(topk_ids, eng->hids.ptr, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st));
+    if (topk_w) CK(cudaMemcpyAsync(topk_w, eng->hw.ptr, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st));
+    if (perm) CK(cudaMemcpyAsync(perm, eng->hperm_out.ptr, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st));
+    return moe_b200_sync(eng, st, err);
+}
+
+int moe_b200_run_expert_triplet_f32(moe_b200_engine_t* eng, int layer, int expert, const float* hidden,
+                                    uint32_t hidden_count, float* scratch_gate, float* scratch_up,
+                                    uint32_t intermediate_count, float* out_hidden, uint32_t out_count) {
+    char* err = nullptr;
+    if (!eng || !hidden || !scratch_gate || !scratch_up || !out_hidden) return 0;
+    if (layer < 0 || (size_t)layer >= eng->layers.size()) return 0;
+    LayerWeights* L = &eng->layers[layer];
+    if (!L->E || !L->I || hidden_count != L->H || out_count != L->H || intermediate_count != L->I) return 0;
+    if (expert < -1 || expert >= (int)L->E) return 0;
+    const uint32_t slot = expert < 0 ? L->E : (uint32_t)expert;
+    if (!L->present[slot]) return 0;
+    CK(cudaSetDevice(eng->device));
+    const uint32_t H = L->H, I = L->I;
+    CK(eng->tri.reserve((size_t)(H + 2 * I + H) * 4));
+    float* dx = eng->tri.as<float>();
+    float* dg = dx + H;
+    float* du = dg + I;
+    float* dout = du + I;
+    CK(cudaMemcpy(dx, hidden, (size_t)H * 4, cudaMemcpyHostToDevice));
+    CK(launch_triplet_f32(L->gu.as<uint8_t>() + L->gu_stride * slot, L->dn.as<uint8_t>() + L->dn_stride * slot, dx,
+                          H, I, dg, du, dout, 0));
+    CK(cudaMemcpy(scratch_gate, dg, (size_t)I * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(scratch_up, du, (size_t)I * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(out_hidden, dout, (size_t)H * 4, cudaMemcpyDeviceToHost));
+    return 1;
+}
+
+int moe_b200_debug_dequant(moe_b200_engine_t* eng, int32_t layer, int32_t expert, int32_t proj, uint16_t* out,
+                           uint64_t out_elems, char* err) {
+    LayerWeights* L = get_layer(eng, layer, err);
+    if (!L) return 0;
+    if (expert < -1 || expert >= (int32_t)L->E || !L->I) {
+        set_err(err, "no such expert %d", expert);
+        return 0;
+    }
+    const uint32_t slot = expert < 0 ? L->E : (uint32_t)expert;
+    if (!L->present[slot]) {
+        set_err(err, "expert %d not uploaded", expert);
+        return 0;
+    }
+    const uint32_t rows = proj == MOE_B200_PROJ_DOWN ? L->H : L->I;
+    const uint32_t cols = proj == MOE_B200_PROJ_DOWN ? L->I : L->H;
+    if (!out || out_elems < (uint64_t)rows * cols) {
+        set_err(err, "output needs %llu elements", (unsigned long long)rows * cols);
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    const uint8_t* tiles = proj == MOE_B200_PROJ_DOWN ? L->dn.as<uint8_t>() + L->dn_stride * slot
+                                                      : L->gu.as<uint8_t>() + L->gu_stride * slot +
+                                                            (proj == MOE_B200_PROJ_UP ? kTileBytes : 0);
+    const uint32_t stride = proj == MOE_B200_PROJ_DOWN ? kTileBytes : 2 * kTileBytes;
+    DevBuf tmp;
+    CK(tmp.reserve((size_t)rows * cols * 2));
+    CK(launch_dequant_wtiles(tiles, rows, cols, stride, tmp.as<uint16_t>(), 0));
+    CK(cudaMemcpy(out, tmp.ptr, (size_t)rows * cols * 2, cudaMemcpyDeviceToHost));
+    tmp.release();
+    return 1;
+}
+
+int moe_b200_debug_read(moe_b200_engine_t* eng, int32_t which, void* dst, uint64_t bytes, char* err) {
+    if (!eng || !dst) {
+        set_err(err, "null argument");
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    CK(cudaDeviceSynchronize());
+    const void* src = nullptr;
+    uint64_t have = 0;
+    switch (which) {
+        case MOE_B200_BUF_LOGITS: src = eng->logits.ptr; have = (uint64_t)eng->last_T * eng->last_E * 4; break;
+        case MOE_B200_BUF_SCORES: src = eng->scores.ptr; have = (uint64_t)eng->last_T * eng->last_E * 4; break;
+        case MOE_B200_BUF_GROUP_COUNT: src = eng->g_count.ptr; have = (uint64_t)eng->last_G * 4; break;
+        case MOE_B200_BUF_GROUP_OFFSET: src = eng->g_offset.ptr; have = (uint64_t)(eng->last_G + 1) * 4; break;
+        case MOE_B200_BUF_ROW_TOKEN: src = eng->row_token.ptr; have = (uint64_t)eng->last_P * 4; break;
+        case MOE_B200_BUF_XPERM: src = eng->xperm.ptr; have = (uint64_t)eng->last_P * eng->last_Kp * 2; break;
+        case MOE_B200_BUF_HPERM: src = eng->hperm.ptr; have = (uint64_t)eng->last_P * eng->last_Ip * 2; break;
+        case MOE_B200_BUF_YPERM: src = eng->yperm.ptr; have = (uint64_t)eng->last_P * eng->last_H * 4; break;
+        default: set_err(err, "unknown buffer %d", which); return 0;
+    }
+    if (!src || bytes > have) {
+        set_err(err, "buffer %d holds %llu bytes, %llu requested", which, (unsigned long long)have,
+                (unsigned long long)bytes);
+        return 0;
+    }
+    CK(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+    return 1;
+}
+
+uint32_t moe_b200_last_launch_count(const moe_b200_engine_t* eng) { return eng ? eng->last_launches : 0; }
+
+int moe_b200_profile_enable(moe_b200_engine_t* eng, uint32_t max_calls, char* err) {
+    if (!eng) {
+        set_err(err, "null engine");
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
+    eng->prof_events.clear();
+    eng->prof_max = 0;
+    eng->prof_calls = 0;
+    if (max_calls == 0) return 1;
+    eng->prof_events.resize((size_t)max_calls * (MOE_B200_STAGES + 1));
+    for (auto& e : eng->prof_events) CK(cudaEventCreate(&e));
+    eng->prof_max = max_calls;
+    return 1;
+}
+
+int moe_b200_profile_read(moe_b200_engine_t* eng, float* stage_ms, uint32_t* calls, char* err) {
+    if (!eng || !stage_ms) {
+        set_err(err, "null argument");
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    for (int s = 0; s < MOE_B200_STAGES; ++s) stage_ms[s] = 0.f;
+    for (uint32_t c = 0; c < eng->prof_calls; ++c) {
+        cudaEvent_t* ev = &eng->prof_events[(size_t)c * (MOE_B200_STAGES + 1)];
+        CK(cudaEventSynchronize(ev[MOE_B200_STAGES]));
+        for (int s = 0; s < MOE_B200_STAGES; ++s) {
+            float ms = 0.f;
+            CK(cudaEventElapsedTime(&ms, ev[s], ev[s + 1]));
+            stage_ms[s] += ms;
+        }
+    }
+    if (calls) *calls = eng->prof_calls;
+    return 1;
+}
+
+int moe_b200_group_tokens_by_expert(const moe_b200_assignment_t* assignments, uint32_t n,
+                                    moe_b200_assignment_t* out_sorted, moe_b200_batch_t* out_batches,
+                                    uint32_t max_batches, uint32_t* out_batch_count) {
+    static_assert(sizeof(moe_b200_assignment_t) == sizeof(AssignRec), "assignment layout");
+    static_assert(sizeof(moe_b200_batch_t) == 4 * sizeof(uint32_t), "batch layout");
+    if (!assignments || n == 0 || !out_batch_count) {
+        if (out_batch_count) *out_batch_count = 0;
+        return 0;
+    }
+    if (n > (1u << 30)) return 0;
+    // Process-wide workspace on the current device; the utility has no
+    // engine handle (its signature is the reference's).
+    static std::mutex mu;
+    static DevBuf a, sorted, ord0, ord1, keys, tiles, rank, cnt, off, z0, z1, batches, bcount, errw;
+    static int dev = -1;
+    std::lock_guard<std::mutex> lock(mu);
+    char* err = nullptr;
+    int cur = 0;
+    CK(cudaGetDevice(&cur));
+    if (dev != cur) {
+        DevBuf* all[] = {&a, &sorted, &ord0, &ord1, &keys, &tiles, &rank, &cnt, &off, &z0, &z1, &batches, &bcount, &errw};
+        for (DevBuf* b : all) { b->ptr = nullptr; b->bytes = 0; }  // buffers of another device are abandoned
+        dev = cur;
+    }
+    const size_t rec = sizeof(AssignRec);
+    CK(a.reserve(n * rec));
+    CK(sorted.reserve(n * rec));
+    CK(ord0.reserve(n * 4));
+    CK(ord1.reserve(n * 4));
+    CK(keys.reserve(n * 4));
+    CK(tiles.reserve((size_t)sort_tiles(n) * 256 * 4));
+    CK(rank.reserve(n * 4));
+    CK(cnt.reserve(257 * 4));
+    CK(off.reserve(257 * 4));
+    CK(z0.reserve(257 * 4));
+    CK(z1.reserve(257 * 4));
+    CK(batches.reserve((size_t)n * 16));
+    CK(bcount.reserve(4));
+    CK(errw.reserve(4));
+    CK(cudaMemset(errw.ptr, 0, 4));
+    CK(cudaMemcpy(a.ptr, assignments, n * rec, cudaMemcpyHostToDevice));
+    // digit passes needed per field (least significant key first)
+    uint32_t mx[3] = {0, 0, 0};
+    for (uint32_t i = 0; i < n; ++i) {
+        mx[0] = std::max(mx[0], assignments[i].token_index);
+        mx[1] = std::max(mx[1], assignments[i].expert);
+        mx[2] = std::max(mx[2], assignments[i].layer);
+    }
+    GroupInfo gi{cnt.as<uint32_t>(), off.as<uint32_t>(), z0.as<uint32_t>(), z1.as<uint32_t>(), 1, 0, 0};
+    cudaStream_t st = 0;
+    CK(launch_iota(ord0.as<uint32_t>(), n, st));
+    uint32_t* in = ord0.as<uint32_t>();
+    uint32_t* out = ord1.as<uint32_t>();
+    for (int field = 0; field < 3; ++field) {
+        for (int shift = 0; shift < 32 && (shift == 0 || (mx[field] >> shift) != 0); shift += 8) {
+            if (mx[field] == 0) break;
+            CK(launch_group_pass(a.as<AssignRec>(), in, out, n, field, shift, keys.as<int32_t>(),
+                                 tiles.as<uint32_t>(), rank.as<uint32_t>(), gi, errw.as<uint32_t>(), st));
+            std::swap(in, out);
+        }
+    }
+    CK(launch_group_finish(a.as<AssignRec>(), in, n, sorted.as<AssignRec>(), batches.as<uint32_t>(),
+                           bcount.as<uint32_t>(), st));
+    uint32_t nb = 0;
+    CK(cudaMemcpy(&nb, bcount.ptr, 4, cudaMemcpyDeviceToHost));
+    if (out_sorted) CK(cudaMemcpy(out_sorted, sorted.ptr, n * rec, cudaMemcpyDeviceToHost));
+    if (out_batches && max_batches) {
+        CK(cudaMemcpy(out_batches, batches.ptr, (size_t)std::min(nb, max_batches) * 16, cudaMemcpyDeviceToHost));
+    }
+    *out_batch_count = nb;
+    return (!out_batches || nb <= max_batches) ? 1 : 0;
+}
+
+}  // extern "C"

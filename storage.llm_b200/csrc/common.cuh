@@ -1,0 +1,270 @@
+// Shared device helpers for the B200 (sm_100a) MoE expert-FFN kernels:
+// mbarriers with bounded waits, bulk / tensor (TMA) copies, tcgen05
+// (TMEM alloc, MMA, commit, loads and stores), and the repacked MXFP4 tile
+// geometry.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+namespace moe_b200 {
+
+// ---------------------------------------------------------------------------
+// Repacked MXFP4 weight tile ("wtile").
+//
+// A weight matrix [R rows x K cols] in the reference's GGUF layout (per row,
+// ceil(K/32) blocks of 17 bytes: E8M0 scale, then 16 code bytes holding
+// element j in the low nibble of byte j and element j+16 in the high nibble)
+// is repacked once at upload into tiles of 128 rows x 64 K-elements:
+//   bytes [0, 4096)     code words: word c (0..7) of row r (0..127) at
+//                       (c*128 + r)*4 holds elements 8c..8c+7 of the tile's
+//                       64; element 2i sits in nibble i and element 2i+1 in
+//                       nibble i+4, so one shift+mask yields a bf16x2 pair;
+//   bytes [4096, 4352)  E8M0 scale bytes: sub-block s (0..1, 32 elements
+//                       each) of row r at 4096 + s*128 + r.
+// Tiles are ordered (row_tile, k_tile) row-tile major.  Rows past R and
+// elements past K are zero codes.  Consecutive threads of a converter warp
+// read consecutive words, so the shared-memory reads are conflict-free.
+// ---------------------------------------------------------------------------
+constexpr int kTileRows = 128;
+constexpr int kTileK = 64;
+constexpr int kTileCodeBytes = kTileRows * kTileK / 2;        // 4096
+constexpr int kTileBytes = kTileCodeBytes + kTileRows * 2;    // 4352
+
+__host__ __device__ constexpr uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
+
+// ---------------------------------------------------------------------------
+// Error word shared by all kernels of one engine.  A wait that exceeds its
+// bound records where it gave up and returns instead of hanging the GPU.
+// ---------------------------------------------------------------------------
+enum : uint32_t {
+    kErrNone = 0,
+    kErrTimeoutLoadFull = 1,
+    kErrTimeoutLoadEmpty = 2,
+    kErrTimeoutAFull = 3,
+    kErrTimeoutAEmpty = 4,
+    kErrTimeoutAccFull = 5,
+    kErrTimeoutAccEmpty = 6,
+    kErrBadExpert = 16,
+};
+
+__device__ __forceinline__ void record_error(uint32_t* err, uint32_t code) {
+    if (err) atomicCAS(err, 0u, code);
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with the given parity; gives up after ~2^31 SM clocks
+// (about one second), records `code` and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long start = clock64();
+    while (true) {
+        for (int i = 0; i < 64; ++i) {
+            if (mbar_try_wait(bar, parity)) return true;
+        }
+        if (clock64() - start > (1ll << 31)) {
+            record_error(err, code);
+            return false;
+        }
+        if (err && *reinterpret_cast<volatile uint32_t*>(err) != 0) return false;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Bulk and tensor copies (no multicast anywhere in this library).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 (bf16 inputs, fp32 accumulate).
+__device__ __forceinline__ void mma_ts_bf16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives on `bar` once every tcgen05 operation this thread issued so far
+// has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+// Instruction descriptor for kind::f16: fp32 D, bf16 A and B, both K-major,
+// M = 128, N = n (multiple of 16, 16..256).
+__device__ __forceinline__ uint32_t idesc_bf16_m128(uint32_t n) {
+    return (1u << 4)            // D format f32
+           | (1u << 7)          // A format bf16
+           | (1u << 10)         // B format bf16
+           | ((n >> 3) << 17)   // N / 8
+           | ((128u >> 4) << 24);  // M / 16
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (the layout a TMA SWIZZLE_128B box of 64 bf16 per row
+// writes).  `addr` must lie in a 1024-byte aligned tile; advancing K by 16
+// elements inside the 128-byte swizzle row adds 32 bytes to the address.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFF) >> 4);   // start address
+    d |= (uint64_t)1 << 16;                   // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: 8 rows x 128 B
+    d |= (uint64_t)1 << 46;                   // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
+    return d;
+}
+
+#define MOE_TMEM_ST32(taddr, v)                                                                              \
+    asm volatile(                                                                                            \
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "  \
+        "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "    \
+        "%32};" ::"r"(taddr),                                                                                \
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),  \
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),      \
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),     \
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])                  \
+        : "memory")
+
+#define MOE_TMEM_LD32(taddr, v)                                                                              \
+    asm volatile(                                                                                            \
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "   \
+        "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "  \
+        "[%32];"                                                                                             \
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),   \
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),          \
+          "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),        \
+          "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),        \
+          "=r"(v[29]), "=r"(v[30]), "=r"(v[31])                                                              \
+        : "r"(taddr)                                                                                         \
+        : "memory")
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// MXFP4 decode helpers
+// ---------------------------------------------------------------------------
+// bf16x2 bit pattern of pair i (0..3) of a repacked code word: element 2i
+// (nibble i) in the low half, element 2i+1 (nibble i+4) in the high half.
+// A code (sign s, 3 magnitude bits m) becomes bf16 bits (s<<15)|(m<<6),
+// which is the E2M1 value times 2^-126 (exactly, subnormal for m=1).
+__device__ __forceinline__ uint32_t e2m1_pair_bits(uint32_t w, int i) {
+    const uint32_t v = w >> (4 * i);
+    return ((v << 6) & 0x01C001C0u) | ((v << 12) & 0x80008000u);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// Scale factors for E8M0 byte s: value = bits * 2^(s-1), applied as
+// f1 = 2^(min(s,128)-1) and, only for s > 128, f2 = 2^(s-128) so neither
+// factor overflows bf16.  Both are returned broadcast as bf16x2.
+__device__ __forceinline__ uint32_t e8m0_f1(uint32_t s) {
+    const uint32_t e = (s > 128u ? 128u : s) + 126u;
+    const uint32_t h = e << 7;
+    return h | (h << 16);
+}
+__device__ __forceinline__ uint32_t e8m0_f2(uint32_t s) {
+    const uint32_t h = (s - 1u) << 7;
+    return h | (h << 16);
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+}  // namespace moe_b200

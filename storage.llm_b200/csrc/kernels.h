@@ -1,0 +1,84 @@
+// Kernel launchers shared by the C-ABI layer (api.cu).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace moe_b200 {
+
+// Per-group (expert) routing results on the device, written by the scan
+// kernel and read by the grouped GEMMs' tile schedulers.
+struct GroupInfo {
+    uint32_t* count;        // [G] rows (token assignments) per group
+    uint32_t* offset;       // [G+1] first permuted row of each group
+    uint32_t* gu_tile_off;  // [G+1] prefix of gate/up GEMM tiles
+    uint32_t* dn_tile_off;  // [G+1] prefix of down GEMM tiles
+    uint32_t block_n;       // tokens per GEMM tile
+    uint32_t gu_row_tiles;  // ceil(I / 128)
+    uint32_t dn_row_tiles;  // ceil(H / 128)
+};
+
+struct GemmParams {
+    const uint8_t* wt;        // repacked weights of group 0; group g at wt + g * group_stride
+    uint64_t group_stride;    // bytes per group
+    uint32_t k_tiles;         // K / 64 (K padded to 64)
+    uint32_t m_valid;         // output columns to write (I padded to 64 for gate/up, H for down)
+    uint32_t groups;          // G
+    const uint32_t* count;
+    const uint32_t* offset;
+    const uint32_t* tile_off;
+    uint16_t* h_out;          // gate/up: [rows][h_stride] bf16 SiLU(gate)*up
+    uint32_t h_stride;
+    float* y_out;             // down: [rows][y_stride] f32
+    uint32_t y_stride;
+    uint32_t* err;
+};
+
+enum GemmMode : int { kGateUp = 0, kDown = 1 };
+
+cudaError_t launch_repack_mxfp4(const uint8_t* gguf, uint32_t rows, uint32_t cols, uint8_t* out,
+                                uint32_t tile_stride, cudaStream_t stream);
+cudaError_t launch_dequant_wtiles(const uint8_t* tiles, uint32_t rows, uint32_t cols, uint32_t tile_stride,
+                                  uint16_t* out, cudaStream_t stream);
+
+cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
+                          int sigmoid, int norm_topk, float routed_scale, float* logits, int32_t* ids, float* wout,
+                          float* scores, cudaStream_t st);
+uint32_t sort_tiles(uint32_t n);
+cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
+                           uint32_t* tile_counts, uint32_t* rank, GroupInfo gi, uint32_t* pos_of,
+                           uint32_t* row_token, uint32_t* row_assign, uint32_t* err, cudaStream_t st);
+// Generic pieces of the stable counting sort, used by the grouping utility.
+struct AssignRec {
+    uint32_t token_index, layer, expert;
+    float router_score;
+};
+cudaError_t launch_sort_count(const int32_t* keys, uint32_t n, uint32_t nb, uint32_t* tile_counts, uint32_t* rank,
+                              uint32_t* err, cudaStream_t st);
+cudaError_t launch_sort_scan(uint32_t* tile_counts, uint32_t ntiles, uint32_t nb, GroupInfo gi, cudaStream_t st);
+cudaError_t launch_group_pass(const AssignRec* a, const uint32_t* order_in, uint32_t* order_out, uint32_t n,
+                              int field, int shift, int32_t* keys, uint32_t* tile_counts, uint32_t* rank,
+                              GroupInfo gi, uint32_t* err, cudaStream_t st);
+cudaError_t launch_group_finish(const AssignRec* a, const uint32_t* order, uint32_t n, AssignRec* sorted,
+                                uint32_t* batches /* [n][4] */, uint32_t* batch_count, cudaStream_t st);
+cudaError_t launch_iota(uint32_t* v, uint32_t n, cudaStream_t st);
+cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token, uint32_t rows,
+                          uint16_t* xp, cudaStream_t st);
+cudaError_t launch_combine(const float* yp, uint32_t H, const uint32_t* pos_of, const float* w, uint32_t T,
+                           uint32_t K, int has_shared, uint32_t shared_off, uint16_t* y_bf16, float* y_f32,
+                           cudaStream_t st);
+
+// tcgen05 grouped GEMMs (gemm_tc.cu).  `tmap_b` covers the permuted
+// activation rows [rows x Kp] bf16 with a 64 x block_n box, 128-byte swizzle.
+constexpr uint32_t kBlockN = 128;
+cudaError_t launch_gemm_tc(int mode, const CUtensorMap& tmap_b, const GemmParams& p, int num_sms,
+                           cudaStream_t st);
+// CUDA-core grouped GEMMs used only to cross-check the tcgen05 kernels.
+cudaError_t launch_gemm_simt(int mode, const uint16_t* b, uint32_t b_stride, uint32_t rows, const GemmParams& p,
+                             uint32_t m_rows, cudaStream_t st);
+// fp32 single-token expert (gate/up/SiLU/down) for the triplet entry point.
+cudaError_t launch_triplet_f32(const uint8_t* gu_tiles, const uint8_t* dn_tiles, const float* x, uint32_t H,
+                               uint32_t I, float* gate_out, float* up_out, float* out, cudaStream_t st);
+
+}  // namespace moe_b200

@@ -1,0 +1,443 @@
+// Router top-k, token permutation into ragged per-expert groups, the gather
+// of permuted activation rows and the weighted unpermute/combine.
+//
+// Routing is bit-exact with the reference CPU path:
+//   logits   moe_dot_bf16_row (raw_forward_utils.cpp.inc:174-216): per
+//            (token, expert) 16 FMA chains over i = l, l+16, ..., lane sums
+//            b_l = s_l + s_{l+8}, then ((b0+b1)+b2)+...+b7;
+//   softmax  generation_router.cpp.inc:606-622: exp in double, denominator
+//            summed in double in expert order, p *= (float)(1/denom);
+//   sigmoid  :239-245, 1/(1+exp(-l)) in float;
+//   top-k    :640-674, k largest scores descending (equal scores: lower
+//            expert index first), optional renormalisation and scaling.
+// The permutation is the order of moe_pc_group_tokens_by_expert
+// (token_grouping.cpp.inc:47-55): sorted by expert, then token index.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace moe_b200 {
+
+// ---------------------------------------------------------------------------
+// Router logits.  Block = 256 threads = 16 "pair slots" x 16 lanes; lane l of
+// a slot owns the reference's FMA chain l.  A block covers kRouterTok tokens
+// and 32 experts (2 per slot); x is staged in shared memory in chunks.
+// ---------------------------------------------------------------------------
+constexpr int kRouterTok = 16;
+constexpr int kRouterChunk = 512;  // elements of H staged per step (multiple of 16)
+
+__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
+                                                            const uint16_t* __restrict__ w, uint32_t T,
+                                                            uint32_t E, uint32_t H, float* __restrict__ logits) {
+    __shared__ uint16_t xs[kRouterTok][kRouterChunk];
+    const int l = threadIdx.x & 15;
+    const int slot = threadIdx.x >> 4;
+    const uint32_t t0 = blockIdx.x * kRouterTok;
+    const uint32_t e0 = blockIdx.y * 32 + slot * 2;
+    float acc[kRouterTok][2];
+#pragma unroll
+    for (int t = 0; t < kRouterTok; ++t) acc[t][0] = acc[t][1] = 0.f;
+    const uint32_t main_end = H & ~15u;  // the 16-step main loop of the reference
+    for (uint32_t c0 = 0; c0 < main_end; c0 += kRouterChunk) {
+        const uint32_t clen = min((uint32_t)kRouterChunk, main_end - c0);
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < kRouterTok * clen; i += blockDim.x) {
+            const uint32_t tt = i / clen, kk = i % clen;
+            xs[tt][kk] = (t0 + tt < T) ? x[(uint64_t)(t0 + tt) * H + c0 + kk] : 0;
+        }
+        __syncthreads();
+        const uint16_t* w0 = w + (uint64_t)min(e0, E - 1) * H + c0;
+        const uint16_t* w1 = w + (uint64_t)min(e0 + 1, E - 1) * H + c0;
+        for (uint32_t i = l; i < clen; i += 16) {
+            const float a = bf16_bits_to_f32(w0[i]);
+            const float b = bf16_bits_to_f32(w1[i]);
+#pragma unroll
+            for (int t = 0; t < kRouterTok; ++t) {
+                const float xv = bf16_bits_to_f32(xs[t][i]);
+                acc[t][0] = __fmaf_rn(a, xv, acc[t][0]);
+                acc[t][1] = __fmaf_rn(b, xv, acc[t][1]);
+            }
+        }
+    }
+    // lane sums b_l = s_l + s_{l+8}, then the ordered 8-term sum, then the
+    // reference's 4-way and scalar tails (H % 16 != 0).
+    const unsigned full = 0xffffffffu;
+#pragma unroll
+    for (int t = 0; t < kRouterTok; ++t) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const float hi = __shfl_down_sync(full, acc[t][q], 8, 16);
+            float b = acc[t][q] + hi;  // valid on lanes 0..7
+            float s = __shfl_sync(full, b, 0, 16);
+#pragma unroll
+            for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __shfl_sync(full, b, j, 16));
+            if (l == 0) {
+                const uint32_t tt = t0 + t, e = e0 + q;
+                if (tt < T && e < E) {
+                    float out = 0.0f + s;
+                    const uint16_t* wr = w + (uint64_t)e * H;
+                    const uint16_t* xr = x + (uint64_t)tt * H;
+                    uint32_t i = main_end;
+                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                    for (; i + 3 < H; i += 4) {
+                        a0 = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), a0);
+                        a1 = __fmaf_rn(bf16_bits_to_f32(wr[i + 1]), bf16_bits_to_f32(xr[i + 1]), a1);
+                        a2 = __fmaf_rn(bf16_bits_to_f32(wr[i + 2]), bf16_bits_to_f32(xr[i + 2]), a2);
+                        a3 = __fmaf_rn(bf16_bits_to_f32(wr[i + 3]), bf16_bits_to_f32(xr[i + 3]), a3);
+                    }
+                    out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
+                    for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), out);
+                    logits[(uint64_t)tt * E + e] = out;
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Scores + top-k: one warp per token.
+// ---------------------------------------------------------------------------
+constexpr int kMaxExperts = 1024;
+
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, uint32_t T, uint32_t E,
+                                                          uint32_t K, int sigmoid, int norm_topk, float routed_scale,
+                                                          int32_t* __restrict__ ids, float* __restrict__ wout,
+                                                          float* __restrict__ scores_out) {
+    __shared__ float ps[8][kMaxExperts];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    float* p = ps[warp];
+    const float* lg = logits + (uint64_t)t * E;
+    if (sigmoid) {
+        for (uint32_t e = lane; e < E; e += 32) {
+            const float ex = (float)exp(-(double)lg[e]);
+            p[e] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+        }
+        __syncwarp();
+    } else {
+        float mx = -INFINITY;
+        for (uint32_t e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (uint32_t e = lane; e < E; e += 32) p[e] = (float)exp((double)lg[e] - (double)mx);
+        __syncwarp();
+        double denom = 0.0;
+        if (lane == 0) {
+            for (uint32_t e = 0; e < E; ++e) denom = __dadd_rn(denom, (double)p[e]);
+        }
+        denom = __shfl_sync(0xffffffffu, denom, 0);
+        const float inv = (float)(1.0 / denom);
+        for (uint32_t e = lane; e < E; e += 32) p[e] = __fmul_rn(p[e], inv);
+        __syncwarp();
+    }
+    if (scores_out) {
+        for (uint32_t e = lane; e < E; e += 32) scores_out[(uint64_t)t * E + e] = p[e];
+    }
+    // k rounds of arg-max; equal scores resolve to the lower expert index.
+    float sel_w[32];
+    int sel_i[32];
+    uint32_t taken_mask[kMaxExperts / 32];
+    for (uint32_t q = 0; q < (E + 31) / 32; ++q) taken_mask[q] = 0;
+    for (uint32_t j = 0; j < K; ++j) {
+        float best = -INFINITY;
+        int bi = 0x7fffffff;
+        for (uint32_t e = lane; e < E; e += 32) {
+            if ((taken_mask[e >> 5] >> (e & 31)) & 1u) continue;
+            const float v = p[e];
+            // e grows within a lane, so an equal score never displaces an
+            // earlier (lower) index here
+            if (bi == 0x7fffffff || v > best) {
+                best = v;
+                bi = (int)e;
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != 0x7fffffff && (bi == 0x7fffffff || ob > best || (ob == best && oi < bi))) {
+                best = ob;
+                bi = oi;
+            }
+        }
+        taken_mask[bi >> 5] |= 1u << (bi & 31);
+        if (j < 32) {
+            sel_w[j] = best;
+            sel_i[j] = bi;
+        }
+    }
+    if (lane == 0) {
+        float denom = 0.f;
+        for (uint32_t j = 0; j < K; ++j) denom = __fadd_rn(denom, sel_w[j]);
+        if (norm_topk && denom <= 0.f) denom = 1e-8f;
+        const float scale = sigmoid ? routed_scale : 1.0f;
+        for (uint32_t j = 0; j < K; ++j) {
+            float wv = sel_w[j];
+            if (norm_topk) wv = __fdiv_rn(wv, denom);
+            if (scale != 1.0f) wv = __fmul_rn(wv, scale);
+            ids[(uint64_t)t * K + j] = sel_i[j];
+            wout[(uint64_t)t * K + j] = wv;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Stable counting sort of n items by bucket (deterministic).
+//   count:   per 2048-item tile, per-bucket counts and each item's rank among
+//            earlier items of its bucket in the tile;
+//   scan:    per-bucket prefix over tiles, group sizes and offsets;
+//   scatter: destination = offset[bucket] + tile base + rank.
+// ---------------------------------------------------------------------------
+constexpr int kSortTile = 2048;  // 8 warps x 8 steps x 32 lanes
+
+__global__ void __launch_bounds__(256) sort_count_kernel(const int32_t* __restrict__ keys, uint32_t n,
+                                                         uint32_t nb, uint32_t* __restrict__ tile_counts,
+                                                         uint32_t* __restrict__ rank, uint32_t* __restrict__ err) {
+    extern __shared__ uint32_t cnt[];  // [8][nb]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t i = threadIdx.x; i < 8 * nb; i += blockDim.x) cnt[i] = 0;
+    __syncthreads();
+    const uint32_t base = blockIdx.x * kSortTile + warp * 256;
+    const unsigned lt = (1u << lane) - 1u;
+    uint32_t* wc = cnt + warp * nb;
+    for (int s = 0; s < 8; ++s) {
+        const uint32_t item = base + s * 32 + lane;
+        int32_t b = -1;
+        if (item < n) {
+            b = keys[item];
+            if (b < 0 || (uint32_t)b >= nb) {
+                record_error(err, kErrBadExpert);
+                b = -1;
+            }
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, b);
+        const uint32_t before = (b >= 0) ? wc[b] : 0;
+        __syncwarp();
+        if (b >= 0) {
+            rank[item] = before + __popc(peers & lt);
+            if ((int)(__ffs(peers) - 1) == lane) wc[b] = before + __popc(peers);
+        }
+        __syncwarp();
+    }
+    __syncthreads();
+    // exclusive prefix over the 8 warps per bucket; tile totals to global
+    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
+        uint32_t run = 0;
+        for (int w = 0; w < 8; ++w) {
+            const uint32_t c = cnt[w * nb + b];
+            cnt[w * nb + b] = run;
+            run += c;
+        }
+        tile_counts[(uint64_t)blockIdx.x * nb + b] = run;
+    }
+    __syncthreads();
+    for (int s = 0; s < 8; ++s) {
+        const uint32_t item = base + s * 32 + lane;
+        if (item < n) {
+            const int32_t b = keys[item];
+            if (b >= 0 && (uint32_t)b < nb) rank[item] += cnt[warp * nb + b];
+        }
+    }
+}
+
+// Single block: per-bucket prefix over tiles (in place: counts become
+// bases), group sizes, group offsets and the GEMM tile prefixes.
+// Group layout: buckets 0..nb-1 then, when `extra_rows` > 0, one extra group
+// (the shared expert) of `extra_rows` rows.
+__global__ void __launch_bounds__(1024) sort_scan_kernel(uint32_t* __restrict__ tile_counts, uint32_t ntiles,
+                                                         uint32_t nb, uint32_t extra_rows,
+                                                         GroupInfo gi) {
+    __shared__ uint32_t warp_sums[32];
+    const uint32_t G = nb + (extra_rows ? 1 : 0);
+    // 1) per-bucket column scan over tiles
+    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
+        uint32_t run = 0;
+        for (uint32_t t = 0; t < ntiles; ++t) {
+            const uint32_t c = tile_counts[(uint64_t)t * nb + b];
+            tile_counts[(uint64_t)t * nb + b] = run;
+            run += c;
+        }
+        gi.count[b] = run;
+    }
+    if (threadIdx.x == 0 && extra_rows) gi.count[nb] = extra_rows;
+    __syncthreads();
+    // 2) exclusive scans over groups of: rows, gate/up tiles, down tiles
+    uint32_t carry_rows = 0, carry_gu = 0, carry_dn = 0;
+    for (uint32_t g0 = 0; g0 < G; g0 += blockDim.x) {
+        const uint32_t g = g0 + threadIdx.x;
+        const uint32_t c = g < G ? gi.count[g] : 0;
+        const uint32_t ntile_n = ceil_div(c, gi.block_n);
+        uint32_t v[3] = {c, ntile_n * gi.gu_row_tiles, ntile_n * gi.dn_row_tiles};
+        uint32_t incl[3];
+        for (int q = 0; q < 3; ++q) {
+            uint32_t x = v[q];
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+                if ((threadIdx.x & 31) >= o) x += y;
+            }
+            if ((threadIdx.x & 31) == 31) warp_sums[threadIdx.x >> 5] = x;
+            __syncthreads();
+            if (threadIdx.x < 32) {
+                uint32_t s = warp_sums[threadIdx.x];
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(0xffffffffu, s, o);
+                    if (threadIdx.x >= o) s += y;
+                }
+                warp_sums[threadIdx.x] = s;
+            }
+            __syncthreads();
+            const uint32_t warp_prefix = (threadIdx.x >= 32) ? warp_sums[(threadIdx.x >> 5) - 1] : 0;
+            incl[q] = x + warp_prefix;
+            const uint32_t chunk_total = warp_sums[31];
+            __syncthreads();
+            const uint32_t carry = q == 0 ? carry_rows : (q == 1 ? carry_gu : carry_dn);
+            uint32_t* dst = q == 0 ? gi.offset : (q == 1 ? gi.gu_tile_off : gi.dn_tile_off);
+            if (g < G) dst[g] = carry + incl[q] - v[q];
+            if (q == 0) carry_rows += chunk_total;
+            else if (q == 1) carry_gu += chunk_total;
+            else carry_dn += chunk_total;
+        }
+    }
+    if (threadIdx.x == 0) {
+        gi.offset[G] = carry_rows;
+        gi.gu_tile_off[G] = carry_gu;
+        gi.dn_tile_off[G] = carry_dn;
+    }
+}
+
+// Destination of every assignment a = t*K + j, and for every permuted row:
+// its source token and assignment.  Shared-expert rows follow the routed
+// rows in token order.
+__global__ void scatter_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t K, uint32_t nb,
+                               const uint32_t* __restrict__ tile_base, const uint32_t* __restrict__ rank,
+                               GroupInfo gi, uint32_t shared_rows, uint32_t* __restrict__ pos_of,
+                               uint32_t* __restrict__ row_token, uint32_t* __restrict__ row_assign) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const int32_t b = ids[i];
+        if (b >= 0 && (uint32_t)b < nb) {
+            const uint32_t pos = gi.offset[b] + tile_base[(uint64_t)(i / kSortTile) * nb + b] + rank[i];
+            pos_of[i] = pos;
+            row_token[pos] = i / K;
+            row_assign[pos] = i;
+        }
+    } else if (i < n + shared_rows) {
+        const uint32_t t = i - n;
+        const uint32_t pos = gi.offset[nb] + t;
+        row_token[pos] = t;
+        row_assign[pos] = 0xffffffffu;
+    }
+}
+
+// X_perm[p][0..Kp) = x[row_token[p]][0..H) followed by zeros; 16-byte
+// vectors, one warp per row.
+__global__ void gather_rows_kernel(const uint16_t* __restrict__ x, uint32_t H, uint32_t Kp,
+                                   const uint32_t* __restrict__ row_token, uint32_t rows,
+                                   uint16_t* __restrict__ xp) {
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    for (uint32_t r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + (uint64_t)row_token[r] * H);
+        uint4* dst = reinterpret_cast<uint4*>(xp + (uint64_t)r * Kp);
+        const uint32_t nv = H / 8, nvp = Kp / 8;
+        for (uint32_t v = lane; v < nvp; v += 32) dst[v] = v < nv ? __ldg(src + v) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// y[t] = shared[t] + sum_j w[t,j] * yp[pos(t,j)], one fused multiply-add per
+// term in router order (generation_mlp.cpp.inc:1417-1431 via moe_axpy_f32).
+__global__ void combine_kernel(const float* __restrict__ yp, uint32_t H, const uint32_t* __restrict__ pos_of,
+                               const float* __restrict__ w, uint32_t T, uint32_t K, int has_shared,
+                               uint32_t shared_off, uint16_t* __restrict__ y_bf16, float* __restrict__ y_f32) {
+    for (uint32_t t = blockIdx.y; t < T; t += gridDim.y)
+    for (uint32_t h4 = blockIdx.x * blockDim.x + threadIdx.x; h4 * 4 < H; h4 += gridDim.x * blockDim.x) {
+        const uint32_t h = h4 * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has_shared) {
+            const float4 s = *reinterpret_cast<const float4*>(yp + (uint64_t)(shared_off + t) * H + h);
+            acc.x = 0.f + s.x;
+            acc.y = 0.f + s.y;
+            acc.z = 0.f + s.z;
+            acc.w = 0.f + s.w;
+        }
+        for (uint32_t j = 0; j < K; ++j) {
+            const uint32_t p = pos_of[(uint64_t)t * K + j];
+            const float wt = w[(uint64_t)t * K + j];
+            const float4 v = *reinterpret_cast<const float4*>(yp + (uint64_t)p * H + h);
+            acc.x = __fmaf_rn(wt, v.x, acc.x);
+            acc.y = __fmaf_rn(wt, v.y, acc.y);
+            acc.z = __fmaf_rn(wt, v.z, acc.z);
+            acc.w = __fmaf_rn(wt, v.w, acc.w);
+        }
+        if (y_f32) *reinterpret_cast<float4*>(y_f32 + (uint64_t)t * H + h) = acc;
+        if (y_bf16) {
+            uint2 o;
+            o.x = (uint32_t)f32_to_bf16_bits(acc.x) | ((uint32_t)f32_to_bf16_bits(acc.y) << 16);
+            o.y = (uint32_t)f32_to_bf16_bits(acc.z) | ((uint32_t)f32_to_bf16_bits(acc.w) << 16);
+            *reinterpret_cast<uint2*>(y_bf16 + (uint64_t)t * H + h) = o;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
+                          int sigmoid, int norm_topk, float routed_scale, float* logits, int32_t* ids, float* wout,
+                          float* scores, cudaStream_t st) {
+    if (T == 0) return cudaSuccess;
+    dim3 g1(ceil_div(T, kRouterTok), ceil_div(E, 32));
+    router_logits_kernel<<<g1, 256, 0, st>>>(x, w, T, E, H, logits);
+    router_topk_kernel<<<ceil_div(T, 8), 256, 0, st>>>(logits, T, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
+                                                       scores);
+    return cudaGetLastError();
+}
+
+uint32_t sort_tiles(uint32_t n) { return ceil_div(n, kSortTile); }
+
+cudaError_t launch_sort_count(const int32_t* keys, uint32_t n, uint32_t nb, uint32_t* tile_counts, uint32_t* rank,
+                              uint32_t* err, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    sort_count_kernel<<<sort_tiles(n), 256, 8 * nb * sizeof(uint32_t), st>>>(keys, n, nb, tile_counts, rank, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sort_scan(uint32_t* tile_counts, uint32_t ntiles, uint32_t nb, GroupInfo gi, cudaStream_t st) {
+    sort_scan_kernel<<<1, 1024, 0, st>>>(tile_counts, ntiles, nb, 0, gi);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
+                           uint32_t* tile_counts, uint32_t* rank, GroupInfo gi, uint32_t* pos_of,
+                           uint32_t* row_token, uint32_t* row_assign, uint32_t* err, cudaStream_t st) {
+    const uint32_t n = T * K;
+    const uint32_t nt = sort_tiles(n);
+    if (n > 0) {
+        sort_count_kernel<<<nt, 256, 8 * E * sizeof(uint32_t), st>>>(ids, n, E, tile_counts, rank, err);
+    }
+    sort_scan_kernel<<<1, 1024, 0, st>>>(tile_counts, nt, E, shared_rows, gi);
+    const uint32_t total = n + shared_rows;
+    if (total > 0) {
+        scatter_kernel<<<ceil_div(total, 256), 256, 0, st>>>(ids, n, K, E, tile_counts, rank, gi, shared_rows,
+                                                             pos_of, row_token, row_assign);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token, uint32_t rows,
+                          uint16_t* xp, cudaStream_t st) {
+    if (rows == 0) return cudaSuccess;
+    const uint32_t blocks = min(ceil_div(rows, 8), 148u * 8u);
+    gather_rows_kernel<<<blocks, 256, 0, st>>>(x, H, Kp, row_token, rows, xp);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const float* yp, uint32_t H, const uint32_t* pos_of, const float* w, uint32_t T,
+                           uint32_t K, int has_shared, uint32_t shared_off, uint16_t* y_bf16, float* y_f32,
+                           cudaStream_t st) {
+    if (T == 0) return cudaSuccess;
+    const uint32_t threads = 128;
+    dim3 grid(ceil_div(ceil_div(H, 4), threads), min(T, 65535u));
+    combine_kernel<<<grid, threads, 0, st>>>(yp, H, pos_of, w, T, K, has_shared, shared_off, y_bf16, y_f32);
+    return cudaGetLastError();
+}
+
+}  // namespace moe_b200

@@ -1,0 +1,172 @@
+"""CUDA path vs the oracle, through the C ABI (libmoe_b200.so).
+
+Bars:
+  * expert ids, weights and router scores: bit-exact;
+  * permutation order: exact (moe_pc_group_tokens_by_expert order);
+  * weight decode: bit-exact;
+  * layer output: max abs err <= 2e-2 and mean rel err <= 1e-2, where
+    mean rel err = mean(|y - y_ref|) / mean(|y_ref|) over all elements.
+"""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, golden, layer_from_golden
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MEAN_REL = 1e-2
+LAYER_FIXTURES = sorted(p.name for p in GOLDEN.glob("layer_*.npz"))
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def bf16_to_f32(b):
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def errors(y, ref):
+    d = np.abs(y.astype(np.float64) - ref.astype(np.float64))
+    return float(d.max()), float(d.mean() / max(np.abs(ref).mean(), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def L(pkg):
+    import moe_b200.lib as lib
+    return lib
+
+
+@pytest.fixture(scope="module")
+def engine(L):
+    e = L.Engine(0)
+    yield e
+    e.close()
+
+
+def decode_gguf(packed, rows, cols):
+    """Exact float32 values of GGUF MXFP4 rows (tensor_dot_cpu_kernels.cpp.inc:576-599)."""
+    tab = np.array([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6], np.float32)
+    nblk = (cols + 31) // 32
+    blk = packed.reshape(rows, nblk, 17)
+    s = blk[:, :, 0].astype(np.int32)
+    scale = np.where(s == 0, np.float32(2.0 ** -127), np.ldexp(np.float32(1), s - 127)).astype(np.float32)
+    q = blk[:, :, 1:]
+    codes = np.concatenate([q & 15, q >> 4], axis=2)  # [rows, nblk, 32]
+    vals = tab[codes] * scale[:, :, None]
+    return vals.reshape(rows, nblk * 32)[:, :cols]
+
+
+@pytest.mark.parametrize("scale_byte", [120, 127, 0, 1, 130, 200])
+def test_weight_decode_is_exact(engine, synth, scale_byte):
+    shape = synth.small_shape(hidden=80, intermediate=100, experts=2, top_k=1)
+    rng = np.random.default_rng(scale_byte)
+    li = synth.make_layer(shape, seed=9)
+    li.gate = synth.gen_mxfp4(rng, (2,), 100, 80, scale_byte=scale_byte)
+    engine.upload_layer(li)
+    for proj, src, rows, cols in ((0, li.gate[1], 100, 80), (1, li.up[1], 100, 80), (2, li.down[1], 80, 100)):
+        got = bf16_to_f32(engine.dequant(0, 1, proj, rows, cols))
+        want = decode_gguf(src, rows, cols)
+        assert np.array_equal(bits(got), bits(want)), (proj, scale_byte)
+
+
+@pytest.mark.parametrize("name", LAYER_FIXTURES)
+def test_layer_matches_reference_simt(name, engine, synth, L):
+    check_layer_fixture(name, 1, engine, synth, L)
+
+
+def check_layer_fixture(name, path, engine, synth, L):
+    g = golden(name)
+    li = layer_from_golden(synth, g)
+    engine.upload_layer(li)
+    cfg = L.Engine.cfg(li.shape, gemm_path=path)
+    out = engine.forward_host(cfg, li.x)
+    T, E, K = li.x.shape[0], li.shape.experts, li.shape.top_k
+    # routing: bit-exact
+    assert np.array_equal(out["ids"], g["ids"])
+    assert np.array_equal(bits(out["w"]), bits(g["w"]))
+    scores = engine.read(L.BUF_SCORES, (T, E), np.float32)
+    assert np.array_equal(bits(scores), bits(g["scores"]))
+    # permutation: sorted by (expert, token), the grouping utility's order
+    a = np.arange(T * K)
+    want = a[np.lexsort((a // K, out["ids"].ravel()))]
+    assert np.array_equal(out["perm"], want.astype(np.uint32))
+    counts = engine.read(L.BUF_GROUP_COUNT, (E + int(li.shape.shared),), np.uint32)
+    assert np.array_equal(counts[:E], np.bincount(out["ids"].ravel(), minlength=E))
+    # layer output within tolerance, fp32 and bf16 outputs
+    mx, mr = errors(out["y_f32"], g["y"])
+    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+    mx2, mr2 = errors(bf16_to_f32(out["y_bf16"]), g["y"])
+    assert mx2 <= MAX_ABS and mr2 <= MEAN_REL, (mx2, mr2)
+    engine.sync()
+
+
+def test_expert_triplet_matches_oracle(engine, synth, port):
+    shape = synth.small_shape(hidden=192, intermediate=160, experts=4, top_k=2)
+    li = synth.make_layer(shape, seed=12)
+    engine.upload_layer(li)
+    x = np.random.default_rng(3).standard_normal(192).astype(np.float32)
+    g, u, out = engine.expert_triplet(0, 2, x, 160)
+    import ctypes as C
+    import oracle
+    sg = np.zeros(160, np.float32)
+    su = np.zeros(160, np.float32)
+    ref = np.zeros(192, np.float32)
+    gate, up, down = (np.ascontiguousarray(a[2]) for a in (li.gate, li.up, li.down))
+    port.lib.mo_expert_triplet(gate.ctypes.data_as(oracle._u8p), up.ctypes.data_as(oracle._u8p),
+                               down.ctypes.data_as(oracle._u8p), x.ctypes.data_as(oracle._f32p), 192, 160,
+                               sg.ctypes.data_as(oracle._f32p), su.ctypes.data_as(oracle._f32p),
+                               ref.ctypes.data_as(oracle._f32p))
+    assert np.allclose(u, su, rtol=1e-4, atol=1e-6)
+    assert np.allclose(g, sg, rtol=1e-4, atol=1e-6)
+    assert np.allclose(out, ref, rtol=1e-4, atol=1e-6)
+    # the reference's shape checks (expert_triplet_cpu.cpp.inc:34-43)
+    with pytest.raises(Exception):
+        engine.expert_triplet(0, 2, x[:100], 160)
+
+
+def test_group_tokens_matches_reference_fixture(L):
+    g = golden("grouping.npz")
+    ok, out, batches, cnt = L.group_tokens_by_expert(g["token"], g["expert"], g["score"], g["layer"])
+    assert ok == int(g["ok"])
+    sorted_ = np.array([(a.token_index, a.layer, a.expert) for a in out[:len(g["token"])]], np.uint32)
+    assert np.array_equal(sorted_, g["sorted"])
+    b = np.array([(x.layer, x.expert, x.first_sorted_index, x.token_count) for x in batches[:cnt]], np.uint32)
+    assert np.array_equal(b, g["batches"])
+
+
+def test_group_tokens_edge_cases(L, port):
+    ok, out, batches, cnt = L.group_tokens_by_expert([9], [4])
+    assert ok == 1 and cnt == 1 and batches[0].expert == 4 and batches[0].token_count == 1
+    # too few batch slots -> 0, with the full count reported
+    ok, _, _, cnt = L.group_tokens_by_expert([0, 1, 2], [0, 1, 2], max_batches=2)
+    assert ok == 0 and cnt == 3
+    # large ids exercise every radix digit
+    rng = np.random.default_rng(4)
+    n = 5000
+    tok = rng.integers(0, 2 ** 31, n)
+    ex = rng.integers(0, 70000, n)
+    ly = rng.integers(0, 300, n)
+    ok, out, batches, cnt = L.group_tokens_by_expert(tok, ex, None, ly)
+    ok2, out2, batches2, cnt2 = port.group_tokens(tok, ex, None, ly)
+    assert ok == ok2 and cnt == cnt2
+    a = np.array([(x.token_index, x.layer, x.expert) for x in out[:n]])
+    b = np.array([(x.token_index, x.layer, x.expert) for x in out2[:n]])
+    assert np.array_equal(a, b)
+
+
+def test_invalid_arguments_fail_cleanly(engine, L, synth):
+    shape = synth.small_shape()
+    li = synth.make_layer(shape, seed=1)
+    engine.upload_layer(li)
+    bad = L.Engine.cfg(shape)
+    bad.top_k = 0
+    with pytest.raises(L.MoEError, match="top_k"):
+        engine.forward_host(bad, li.x)
+    bad = L.Engine.cfg(shape)
+    bad.hidden = 60
+    with pytest.raises(L.MoEError):
+        engine.forward_host(bad, li.x)
+    with pytest.raises(L.MoEError, match="shared"):
+        engine.forward_host(L.Engine.cfg(shape, use_shared=True), li.x)
