@@ -146,7 +146,7 @@ int make_tmap(moe_b200_engine* eng, CUtensorMap* map, void* base, uint64_t cols,
     }
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {64, kBlockN};
+    const cuuint32_t box[2] = {64, 32};  // 32 token rows per box; a tile issues as many as its N needs
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = eng->encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -356,7 +356,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     const uint32_t P = n + shared_rows;
     const uint32_t G = E + (shared ? 1 : 0);
     const uint32_t Kp = round_up(H, kTileK), Ip = round_up(I, kTileK);
-    const uint32_t rows_cap = std::max(P, kBlockN);
+    const uint32_t rows_cap = std::max(P, 32u);
     const uint32_t ntiles = sort_tiles(n);
 
     CK(eng->logits.reserve((size_t)T * E * 4));

@@ -20,8 +20,16 @@ namespace moe_b200 {
 // is repacked once at upload into tiles of 128 rows x 64 K-elements:
 //   bytes [0, 4096)     code words: word c (0..7) of row r (0..127) at
 //                       (c*128 + r)*4 holds elements 8c..8c+7 of the tile's
-//                       64; element 2i sits in nibble i and element 2i+1 in
-//                       nibble i+4, so one shift+mask yields a bf16x2 pair;
+//                       64.  Element 2i sits in the low half-word and 2i+1 at
+//                       the same place in the high half-word, so pair i
+//                       decodes to one bf16x2.  Within a half-word (sign s,
+//                       magnitude bits m2 m1 m0 of an E2M1 code):
+//                         pair 0: m at bits 0-2,  s at 9
+//                         pair 1: m at bits 3-5,  s at 12
+//                         pair 2: m at bits 6-8,  s at 15
+//                         pair 3: m0 m1 at 10-11, m2 at 14, s at 13
+//                       Pairs 0-2 then need one shift and one mask to land
+//                       on bf16 bits (m at 6-8, s at 15); pair 3 needs three.
 //   bytes [4096, 4352)  E8M0 scale bytes: sub-block s (0..1, 32 elements
 //                       each) of row r at 4096 + s*128 + r.
 // Tiles are ordered (row_tile, k_tile) row-tile major.  Rows past R and
@@ -91,19 +99,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity; gives up after ~2^31 SM clocks
-// (about one second), records `code` and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code) {
+// (about one second), records `code` and returns false.  `backoff` parks
+// the warp for a short sleep between polls, for waiters whose latency does
+// not matter (it leaves the issue slots to the converter warps).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code,
+                                          bool backoff = false) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long start = clock64();
     while (true) {
-        for (int i = 0; i < 64; ++i) {
+        for (int i = 0; i < 32; ++i) {
             if (mbar_try_wait(bar, parity)) return true;
+            if (backoff) __nanosleep(200);
         }
         if (clock64() - start > (1ll << 31)) {
             record_error(err, code);
             return false;
         }
-        if (err && *reinterpret_cast<volatile uint32_t*>(err) != 0) return false;
     }
 }
 
@@ -214,6 +225,19 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
         "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])                  \
         : "memory")
 
+#define MOE_TMEM_ST16(taddr, v)                                                                              \
+    asm volatile(                                                                                            \
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "  \
+        "%13, %14, %15, %16};" ::"r"(taddr),                                                                 \
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),  \
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])                   \
+        : "memory")
+
+#define MOE_TMEM_ST8(taddr, v)                                                                               \
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), \
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])      \
+                 : "memory")
+
 #define MOE_TMEM_LD32(taddr, v)                                                                              \
     asm volatile(                                                                                            \
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "   \
@@ -233,13 +257,25 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // ---------------------------------------------------------------------------
 // MXFP4 decode helpers
 // ---------------------------------------------------------------------------
-// bf16x2 bit pattern of pair i (0..3) of a repacked code word: element 2i
-// (nibble i) in the low half, element 2i+1 (nibble i+4) in the high half.
-// A code (sign s, 3 magnitude bits m) becomes bf16 bits (s<<15)|(m<<6),
-// which is the E2M1 value times 2^-126 (exactly, subnormal for m=1).
+// bf16x2 bit pattern of pair i (0..3) of a repacked code word (layout
+// above).  A code (sign s, 3 magnitude bits m) becomes bf16 bits
+// (s<<15)|(m<<6), the E2M1 value times 2^-126 (exactly; subnormal for m=1).
 __device__ __forceinline__ uint32_t e2m1_pair_bits(uint32_t w, int i) {
-    const uint32_t v = w >> (4 * i);
-    return ((v << 6) & 0x01C001C0u) | ((v << 12) & 0x80008000u);
+    constexpr uint32_t kMask = 0x81C081C0u;
+    if (i == 0) return (w << 6) & kMask;
+    if (i == 1) return (w << 3) & kMask;
+    if (i == 2) return w & kMask;
+    return ((w >> 4) & 0x00C000C0u) | ((w >> 6) & 0x01000100u) | ((w << 2) & 0x80008000u);
+}
+
+// Bit positions of element e (0..7) of a code word: returns the position of
+// magnitude bit b (0..2) or, for b == 3, of the sign.
+__host__ __device__ constexpr int code_bit_pos(int e, int b) {
+    const int base = (e & 1) ? 16 : 0;
+    const int pair = e >> 1;
+    if (pair < 3) return base + (b < 3 ? pair * 3 + b : pair * 3 + 9);
+    constexpr int p3[4] = {10, 11, 14, 13};
+    return base + p3[b];
 }
 
 __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {

@@ -15,11 +15,15 @@
 //          B), epilogue h = SiLU(gate) * up -> bf16 permuted intermediate.
 // kDown:   one tile = 128 down rows, epilogue writes fp32 expert outputs.
 //
-// Warp roles (320 threads, one CTA per SM, persistent over all tiles):
-//   warp 0     producer: bulk copy of the raw weight tile + TMA of the B box
-//   warp 1     TMEM owner and MMA issuer
-//   warps 2-5  converters (one TMEM lane quarter each)
-//   warps 6-9  epilogue  (one TMEM lane quarter each)
+// Warp roles (704 threads, one CTA per SM, persistent over all tiles):
+//   warp 0      producer: bulk copy of the raw weight tile + TMA boxes of
+//               32 token rows, only as many as the tile's N needs
+//   warp 1      TMEM owner and MMA issuer
+//   warps 2-17  converters: four groups of four warps, each group covering
+//               the four TMEM lane quarters; group g decodes a quarter of
+//               the stage (gate/up: projection g/2, K half g%2; down: K
+//               quarter g)
+//   warps 18-21 epilogue (one TMEM lane quarter each)
 // Every wait is bounded (common.cuh mbar_wait) and reports through p.err.
 #include "common.cuh"
 #include "kernels.h"
@@ -31,7 +35,8 @@ struct TcCfg {
     static constexpr int kBN = kBlockN;                                    // max tokens per tile
     static constexpr int kRaw = MODE == kGateUp ? 2 * kTileBytes : kTileBytes;
     static constexpr int kBBytes = kBN * 128;                              // 64 bf16 per row
-    static constexpr int kStages = MODE == kGateUp ? 6 : 8;
+    static constexpr int kSubRows = 32;                                    // rows per TMA box
+    static constexpr int kStages = MODE == kGateUp ? 8 : 10;
     static constexpr int kACols = MODE == kGateUp ? 64 : 32;               // TMEM columns per A stage
     static constexpr int kAStages = 256 / kACols;
     static constexpr int kAccCols = MODE == kGateUp ? 2 * kBN : kBN;
@@ -59,10 +64,16 @@ __device__ __forceinline__ void tile_coord(const GemmParams& p, uint32_t tile, T
     tc.nn = min(kBlockN, cnt - tc.n0);
 }
 
-__device__ __forceinline__ float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+// SiLU with the fast exponential and division: its error (a few ulp of
+// fp32) is far below the bf16 rounding of the intermediate it feeds.
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+constexpr int kConvWarps = 16;
+constexpr int kFirstEpiWarp = 2 + kConvWarps;
+constexpr int kThreads = (kFirstEpiWarp + 4) * 32;
 
 template <int MODE>
-__global__ void __launch_bounds__(320, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
                                                          const GemmParams p) {
     using C = TcCfg<MODE>;
     extern __shared__ uint8_t smem_raw[];
@@ -85,7 +96,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tc_kernel(const __grid_constant__
             mbar_init(&load_empty[i], 1);
         }
         for (int i = 0; i < C::kAStages; ++i) {
-            mbar_init(&a_full[i], 128);
+            mbar_init(&a_full[i], kConvWarps * 32);
             mbar_init(&a_empty[i], 1);
         }
         for (int i = 0; i < C::kAccs; ++i) {
@@ -117,12 +128,15 @@ __global__ void __launch_bounds__(320, 1) gemm_tc_kernel(const __grid_constant__
                 const uint8_t* wbase =
                     p.wt + (uint64_t)tc.g * p.group_stride + (uint64_t)tc.mt * p.k_tiles * C::kRaw;
                 const int32_t row0 = (int32_t)(p.offset[tc.g] + tc.n0);
+                const uint32_t n_sub = ceil_div(tc.nn, C::kSubRows);
                 for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
-                    if (!(ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty))) break;
-                    mbar_arrive_expect_tx(&load_full[stage], C::kBBytes + C::kRaw);
+                    if (!(ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty, true))) break;
+                    mbar_arrive_expect_tx(&load_full[stage], n_sub * C::kSubRows * 128 + C::kRaw);
                     bulk_g2s(raw_tiles + stage * C::kRaw, wbase + (uint64_t)kt * C::kRaw, C::kRaw, &load_full[stage]);
-                    tma_load_2d(b_tiles + stage * C::kBBytes, &tmap_b, (int32_t)(kt * kTileK), row0,
-                                &load_full[stage]);
+                    for (uint32_t sb = 0; sb < n_sub; ++sb) {
+                        tma_load_2d(b_tiles + stage * C::kBBytes + sb * C::kSubRows * 128, &tmap_b,
+                                    (int32_t)(kt * kTileK), row0 + (int32_t)(sb * C::kSubRows), &load_full[stage]);
+                    }
                     if (++stage == C::kStages) {
                         stage = 0;
                         phase ^= 1;
@@ -175,43 +189,52 @@ __global__ void __launch_bounds__(320, 1) gemm_tc_kernel(const __grid_constant__
                 }
             }
         }
-    } else if (warp < 6) {
+    } else if (warp < kFirstEpiWarp) {
         // ------------------------------------------------------------ converters
         const uint32_t quarter = warp & 3;
+        const uint32_t group = (warp - 2) >> 2;  // 0..3
         const uint32_t r = quarter * 32 + lane;  // weight row inside the tile == TMEM lane
         const uint32_t lane_addr = (quarter * 32) << 16;
+        // gate/up: projection group/2, words 4*(group%2) .. +3 (one scale block)
+        // down:    words 2*group, 2*group+1 (scale block group/2)
+        const uint32_t proj = MODE == kGateUp ? (group >> 1) : 0;
+        const uint32_t word0 = MODE == kGateUp ? (group & 1) * 4 : group * 2;
+        const uint32_t sblk = MODE == kGateUp ? (group & 1) : (group >> 1);
+        const uint32_t col = MODE == kGateUp ? proj * 32 + (group & 1) * 16 : group * 8;
         uint32_t stage = 0, phase = 0, astage = 0, aphase = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
             for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
                 if (!(ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull))) break;
+                const uint8_t* raw = raw_tiles + stage * C::kRaw + proj * kTileBytes;
+                const uint32_t* words = reinterpret_cast<const uint32_t*>(raw) + word0 * kTileRows + r;
+                const uint32_t sc = raw[kTileCodeBytes + sblk * kTileRows + r];
+                constexpr int kWords = MODE == kGateUp ? 4 : 2;
+                uint32_t w[kWords];
+#pragma unroll
+                for (int c = 0; c < kWords; ++c) w[c] = words[c * kTileRows];
+                const uint32_t f1 = e8m0_f1(sc);
+                uint32_t v[kWords * 4];
+#pragma unroll
+                for (int c = 0; c < kWords; ++c) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) v[c * 4 + i] = bf16x2_mul(e2m1_pair_bits(w[c], i), f1);
+                }
+                if (sc > 128u) {  // scales above 2^1: second factor
+                    const uint32_t f2 = e8m0_f2(sc);
+#pragma unroll
+                    for (int j = 0; j < kWords * 4; ++j) v[j] = bf16x2_mul(v[j], f2);
+                }
+                fence_proxy_async_smem();
                 if (!(ok = mbar_wait(&a_empty[astage], aphase ^ 1, p.err, kErrTimeoutAEmpty))) break;
                 tc_fence_after();
-#pragma unroll
-                for (int proj = 0; proj < (MODE == kGateUp ? 2 : 1); ++proj) {
-                    const uint8_t* raw = raw_tiles + stage * C::kRaw + proj * kTileBytes;
-                    const uint32_t* words = reinterpret_cast<const uint32_t*>(raw);
-                    const uint32_t s0 = raw[kTileCodeBytes + r];
-                    const uint32_t s1 = raw[kTileCodeBytes + kTileRows + r];
-                    const uint32_t f10 = e8m0_f1(s0), f11 = e8m0_f1(s1);
-                    uint32_t v[32];
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const uint32_t w = words[c * kTileRows + r];
-                        const uint32_t f1 = c < 4 ? f10 : f11;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) v[c * 4 + i] = bf16x2_mul(e2m1_pair_bits(w, i), f1);
-                    }
-                    if (s0 > 128u || s1 > 128u) {  // scales above 2^1: second factor
-                        const uint32_t f20 = e8m0_f2(s0 > 128u ? s0 : 128u), f21 = e8m0_f2(s1 > 128u ? s1 : 128u);
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = bf16x2_mul(v[j], j < 16 ? f20 : f21);
-                    }
-                    const uint32_t taddr = tmem + lane_addr + a_col0 + astage * C::kACols + proj * 32;
-                    MOE_TMEM_ST32(taddr, v);
+                const uint32_t taddr = tmem + lane_addr + a_col0 + astage * C::kACols + col;
+                if (MODE == kGateUp) {
+                    MOE_TMEM_ST16(taddr, v);
+                } else {
+                    MOE_TMEM_ST8(taddr, v);
                 }
                 tmem_wait_st();
-                fence_proxy_async_smem();
                 tc_fence_before();
                 mbar_arrive(&a_full[astage]);
                 if (++stage == C::kStages) {
@@ -234,7 +257,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tc_kernel(const __grid_constant__
         for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
             TileCoord tc;
             tile_coord(p, tile, tc);
-            if (!(ok = mbar_wait(&acc_full[acc], accphase, p.err, kErrTimeoutAccFull))) break;
+            if (!(ok = mbar_wait(&acc_full[acc], accphase, p.err, kErrTimeoutAccFull, true))) break;
             tc_fence_after();
             const uint32_t m = tc.mt * kTileRows + r;
             const bool valid = m < p.m_valid;
@@ -293,7 +316,7 @@ static cudaError_t launch_mode(const CUtensorMap& tmap_b, const GemmParams& p, i
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
     }
-    gemm_tc_kernel<MODE><<<num_sms, 320, C::kSmem, st>>>(tmap_b, p);
+    gemm_tc_kernel<MODE><<<num_sms, kThreads, C::kSmem, st>>>(tmap_b, p);
     return cudaGetLastError();
 }
 

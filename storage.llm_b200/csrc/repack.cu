@@ -39,8 +39,8 @@ __global__ void repack_mxfp4_kernel(const uint8_t* __restrict__ gguf, uint32_t r
                     const uint32_t i = k % 32;
                     code = i < 16 ? (blk[1 + i] & 0x0Fu) : (blk[1 + i - 16] >> 4);
                 }
-                const int nib = (e & 1) ? 4 + (e >> 1) : (e >> 1);
-                word |= code << (4 * nib);
+#pragma unroll
+                for (int b = 0; b < 4; ++b) word |= ((code >> b) & 1u) << code_bit_pos(e, b);
             }
         }
         reinterpret_cast<uint32_t*>(tile_base)[c * kTileRows + rr] = word;

@@ -22,31 +22,46 @@ namespace moe_b200 {
 // a slot owns the reference's FMA chain l.  A block covers kRouterTok tokens
 // and 32 experts (2 per slot); x is staged in shared memory in chunks.
 // ---------------------------------------------------------------------------
-constexpr int kRouterTok = 16;
-constexpr int kRouterChunk = 512;  // elements of H staged per step (multiple of 16)
+constexpr int kRouterChunk = 480;  // elements of H staged per step (multiple of 16; 48 KB static limit)
+constexpr int kRouterWPad = 8;     // row padding (bf16) against bank conflicts
 
+template <int kRouterTok>
 __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
                                                             const uint16_t* __restrict__ w, uint32_t T,
                                                             uint32_t E, uint32_t H, float* __restrict__ logits) {
-    __shared__ uint16_t xs[kRouterTok][kRouterChunk];
+    // x rows and the block's 32 router rows for one H chunk, staged with
+    // 16-byte loads; the FMA chains then read shared memory only.
+    __shared__ __align__(16) uint16_t xs[kRouterTok][kRouterChunk];
+    __shared__ __align__(16) uint16_t ws[32][kRouterChunk + kRouterWPad];
     const int l = threadIdx.x & 15;
     const int slot = threadIdx.x >> 4;
     const uint32_t t0 = blockIdx.x * kRouterTok;
-    const uint32_t e0 = blockIdx.y * 32 + slot * 2;
+    const uint32_t eb = blockIdx.y * 32;
+    const uint32_t e0 = eb + slot * 2;
     float acc[kRouterTok][2];
 #pragma unroll
     for (int t = 0; t < kRouterTok; ++t) acc[t][0] = acc[t][1] = 0.f;
     const uint32_t main_end = H & ~15u;  // the 16-step main loop of the reference
     for (uint32_t c0 = 0; c0 < main_end; c0 += kRouterChunk) {
         const uint32_t clen = min((uint32_t)kRouterChunk, main_end - c0);
+        const uint32_t cv = clen / 8;  // 16-byte vectors per row (H % 8 == 0)
         __syncthreads();
-        for (uint32_t i = threadIdx.x; i < kRouterTok * clen; i += blockDim.x) {
-            const uint32_t tt = i / clen, kk = i % clen;
-            xs[tt][kk] = (t0 + tt < T) ? x[(uint64_t)(t0 + tt) * H + c0 + kk] : 0;
+        for (uint32_t i = threadIdx.x; i < kRouterTok * cv; i += blockDim.x) {
+            const uint32_t tt = i / cv, kk = (i % cv) * 8;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (t0 + tt < T) v = __ldg(reinterpret_cast<const uint4*>(x + (uint64_t)(t0 + tt) * H + c0 + kk));
+            *reinterpret_cast<uint4*>(&xs[tt][kk]) = v;
+        }
+        for (uint32_t i = threadIdx.x; i < 32 * cv; i += blockDim.x) {
+            const uint32_t er = i / cv, kk = (i % cv) * 8;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (eb + er < E) v = __ldg(reinterpret_cast<const uint4*>(w + (uint64_t)(eb + er) * H + c0 + kk));
+            *reinterpret_cast<uint4*>(&ws[er][kk]) = v;
         }
         __syncthreads();
-        const uint16_t* w0 = w + (uint64_t)min(e0, E - 1) * H + c0;
-        const uint16_t* w1 = w + (uint64_t)min(e0 + 1, E - 1) * H + c0;
+        const uint16_t* w0 = ws[slot * 2];
+        const uint16_t* w1 = ws[slot * 2 + 1];
+#pragma unroll 4
         for (uint32_t i = l; i < clen; i += 16) {
             const float a = bf16_bits_to_f32(w0[i]);
             const float b = bf16_bits_to_f32(w1[i]);
@@ -384,8 +399,19 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
                           int sigmoid, int norm_topk, float routed_scale, float* logits, int32_t* ids, float* wout,
                           float* scores, cudaStream_t st) {
     if (T == 0) return cudaSuccess;
-    dim3 g1(ceil_div(T, kRouterTok), ceil_div(E, 32));
-    router_logits_kernel<<<g1, 256, 0, st>>>(x, w, T, E, H, logits);
+    // Tokens per block: the largest of 16/8/4/2/1 that still gives >= 2 blocks
+    // per SM, so decode-sized batches spread over the whole GPU.
+    const uint32_t eb = ceil_div(E, 32);
+    int tt = 16;
+    while (tt > 1 && ceil_div(T, tt) * eb < 296) tt >>= 1;
+    dim3 g1(ceil_div(T, tt), eb);
+    switch (tt) {
+        case 16: router_logits_kernel<16><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
+        case 8: router_logits_kernel<8><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
+        case 4: router_logits_kernel<4><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
+        case 2: router_logits_kernel<2><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
+        default: router_logits_kernel<1><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
+    }
     router_topk_kernel<<<ceil_div(T, 8), 256, 0, st>>>(logits, T, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
                                                        scores);
     return cudaGetLastError();
