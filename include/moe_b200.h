@@ -150,6 +150,31 @@ MOE_B200_API int moe_b200_group_tokens_by_expert(const moe_b200_assignment_t* as
                                     moe_b200_assignment_t* out_sorted_assignments, moe_b200_batch_t* out_batches,
                                     uint32_t max_batches, uint32_t* out_batch_count);
 
+/* Allocation-free form of moe_b200_group_tokens_by_expert, for callers that
+ * must not allocate device memory while they run -- an engine whose
+ * residency cache owns the whole VRAM budget, or code recording a CUDA graph
+ * (where cudaMalloc is not allowed).  No counterpart in the reference.
+ * Same inputs and outputs (host buffers) plus an error buffer; the result is
+ * identical to moe_b200_group_tokens_by_expert's.  It calls no cudaMalloc,
+ * cudaFree or allocating library routine: its scratch is a fixed device
+ * array of about 4.3 MB inside this library, which every GPU that loads the
+ * library holds until the process exits.  Limits and caveats:
+ *   - at most MOE_B200_NOALLOC_MAX_ASSIGNMENTS assignments; more returns 0
+ *     with a message in `err`;
+ *   - the first call on a device resolves the array's device address with
+ *     cudaGetSymbolAddress (with that device current), so make that first
+ *     call before any stream capture;
+ *   - every call shares the one array, which keeps the last call's contents;
+ *     calls are serialised within the process, and any other work that
+ *     overlaps a call on the GPU and touches the array would race with it;
+ *   - runs on the current device's legacy default stream and synchronises. */
+#define MOE_B200_NOALLOC_MAX_ASSIGNMENTS 65536u
+MOE_B200_API int moe_b200_group_tokens_by_expert_noalloc(const moe_b200_assignment_t* assignments,
+                                                         uint32_t assignment_count,
+                                                         moe_b200_assignment_t* out_sorted_assignments,
+                                                         moe_b200_batch_t* out_batches, uint32_t max_batches,
+                                                         uint32_t* out_batch_count, char* err);
+
 /* Test and diagnostics hooks (no reference counterpart). */
 enum {
     MOE_B200_PROJ_GATE = 0,

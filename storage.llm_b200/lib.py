@@ -81,6 +81,10 @@ def load(path: Path = LIB_PATH) -> C.CDLL:
     lib.moe_b200_group_tokens_by_expert.restype = C.c_int
     lib.moe_b200_group_tokens_by_expert.argtypes = [C.POINTER(Assignment), C.c_uint32, C.POINTER(Assignment),
                                                     C.POINTER(Batch), C.c_uint32, C.POINTER(C.c_uint32)]
+    lib.moe_b200_group_tokens_by_expert_noalloc.restype = C.c_int
+    lib.moe_b200_group_tokens_by_expert_noalloc.argtypes = [C.POINTER(Assignment), C.c_uint32,
+                                                            C.POINTER(Assignment), C.POINTER(Batch), C.c_uint32,
+                                                            C.POINTER(C.c_uint32), cp]
     lib.moe_b200_debug_dequant.restype = C.c_int
     lib.moe_b200_debug_dequant.argtypes = [vp, C.c_int32, C.c_int32, C.c_int32, vp, C.c_uint64, cp]
     lib.moe_b200_debug_read.restype = C.c_int
