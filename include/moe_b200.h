@@ -48,8 +48,9 @@ enum {
 };
 
 enum {
-    MOE_B200_GEMM_TCGEN05 = 0, /* tensor-core grouped GEMMs (the product path) */
-    MOE_B200_GEMM_SIMT = 1     /* CUDA-core grouped GEMMs, a cross-check for tests */
+    MOE_B200_GEMM_BLOCKSCALED = 0, /* tcgen05 kind::mxf8f6f4 block-scaled MMA on the E2M1 codes (default) */
+    MOE_B200_GEMM_SIMT = 1,        /* CUDA-core grouped GEMMs, a cross-check for tests */
+    MOE_B200_GEMM_TMEM_DECODE = 2  /* tcgen05 kind::f16 with weights decoded to bf16 in TMEM */
 };
 
 /* Explicit form of the routing metadata the reference reads from GGUF JSON

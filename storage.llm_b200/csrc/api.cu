@@ -76,6 +76,19 @@ struct LayerWeights {
     DevBuf dn;              // [E+1] groups of down tiles
     uint64_t gu_stride = 0, dn_stride = 0;
     std::vector<uint8_t> present;  // [E+1]; slot E = shared expert
+    // block-scaled form: packed E2M1 codes + E8M0 scale blocks
+    DevBuf bs_gu_codes, bs_gu_sfa, bs_dn_codes, bs_dn_sfa;
+    uint32_t rp_i = 0, rp_h = 0, kq = 0, iq = 0;  // rows padded to 128, K padded to 128
+    CUtensorMap tmap_gu_codes{}, tmap_dn_codes{};
+    void release_all() {
+        router.release();
+        gu.release();
+        dn.release();
+        bs_gu_codes.release();
+        bs_gu_sfa.release();
+        bs_dn_codes.release();
+        bs_dn_sfa.release();
+    }
 };
 
 uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
@@ -92,6 +105,11 @@ struct moe_b200_engine {
     DevBuf g_count, g_offset, g_gu_off, g_dn_off;
     DevBuf xperm, hperm, yperm;
     DevBuf err_word;
+    // block-scaled path: quantised activations and intermediate
+    DevBuf xq_hi, xq_lo, sx_hi, sx_lo, xb_hi, xb_lo, sfx_atoms, hb_hi, hb_lo, sfh_atoms;
+    CUtensorMap tmap_xhi{}, tmap_xlo{}, tmap_hhi{}, tmap_hlo{};
+    const void* bs_map_key[4] = {nullptr, nullptr, nullptr, nullptr};
+    uint64_t bs_map_dims[4][2] = {};
     // host-call staging
     DevBuf hx, hy, hyf, hids, hw, hperm_out, tri;
     CUtensorMap tmap_x{}, tmap_h{};
@@ -133,29 +151,41 @@ int check_dims(const moe_b200_layer_cfg_t* c, char* err) {
     return 1;
 }
 
-int make_tmap(moe_b200_engine* eng, CUtensorMap* map, void* base, uint64_t cols, uint64_t rows, char* err) {
-    if (!eng->encode) {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
-        if (!fn || q != cudaDriverEntryPointSuccess) {
-            set_err(err, "cuTensorMapEncodeTiled unavailable");
-            return 0;
-        }
-        eng->encode = reinterpret_cast<EncodeTiledFn>(fn);
+int get_encoder(moe_b200_engine* eng, char* err) {
+    if (eng->encode) return 1;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (!fn || q != cudaDriverEntryPointSuccess) {
+        set_err(err, "cuTensorMapEncodeTiled unavailable");
+        return 0;
     }
+    eng->encode = reinterpret_cast<EncodeTiledFn>(fn);
+    return 1;
+}
+
+// 2-D tiled tensor map with 128-byte swizzle.  `cols` counts elements of
+// `dtype`; `row_bytes` is the global row stride.
+int make_tmap2d(moe_b200_engine* eng, CUtensorMap* map, CUtensorMapDataType dtype, void* base, uint64_t cols,
+                uint64_t rows, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, char* err) {
+    if (!get_encoder(eng, err)) return 0;
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {64, 32};  // 32 token rows per box; a tile issues as many as its N needs
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = eng->encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = eng->encode(map, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_err(err, "cuTensorMapEncodeTiled failed (%d)", (int)r);
         return 0;
     }
     return 1;
+}
+
+// bf16 activation rows for the TMEM-decode path: 64-element x 32-row boxes.
+int make_tmap(moe_b200_engine* eng, CUtensorMap* map, void* base, uint64_t cols, uint64_t rows, char* err) {
+    return make_tmap2d(eng, map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, cols, rows, cols * 2, 64, 32, err);
 }
 
 LayerWeights* get_layer(moe_b200_engine* eng, int32_t layer, char* err) {
@@ -217,16 +247,14 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
     if (!eng) return;
     cudaSetDevice(eng->device);
     cudaDeviceSynchronize();
-    for (auto& l : eng->layers) {
-        l.router.release();
-        l.gu.release();
-        l.dn.release();
-    }
+    for (auto& l : eng->layers) l.release_all();
     DevBuf* bufs[] = {&eng->staging, &eng->logits, &eng->scores, &eng->ids, &eng->wts, &eng->tile_counts,
                       &eng->rank, &eng->pos_of, &eng->row_token, &eng->row_assign, &eng->g_count,
                       &eng->g_offset, &eng->g_gu_off, &eng->g_dn_off, &eng->xperm, &eng->hperm,
                       &eng->yperm, &eng->err_word, &eng->hx, &eng->hy, &eng->hyf, &eng->hids,
-                      &eng->hw, &eng->hperm_out, &eng->tri};
+                      &eng->hw, &eng->hperm_out, &eng->tri, &eng->xq_hi, &eng->xq_lo, &eng->sx_hi,
+                      &eng->sx_lo, &eng->xb_hi, &eng->xb_lo, &eng->sfx_atoms, &eng->hb_hi, &eng->hb_lo,
+                      &eng->sfh_atoms};
     for (DevBuf* b : bufs) b->release();
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
     delete eng;
@@ -243,8 +271,10 @@ int moe_b200_upload_router(moe_b200_engine_t* eng, int32_t layer, const uint16_t
     CK(cudaSetDevice(eng->device));
     if (L->E && (L->E != experts || L->H != hidden)) {
         // a new shape invalidates the layer's experts
-        L->gu.release();
-        L->dn.release();
+        DevBuf keep;
+        std::swap(keep, L->router);
+        L->release_all();
+        std::swap(keep, L->router);
         L->present.clear();
         L->I = 0;
     }
@@ -291,6 +321,26 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
         L->dn.release();
         CK(L->gu.reserve(L->gu_stride * (L->E + 1)));
         CK(L->dn.reserve(L->dn_stride * (L->E + 1)));
+        // block-scaled form
+        L->rp_i = round_up(intermediate, 128);
+        L->rp_h = round_up(hidden, 128);
+        L->kq = round_up(hidden, 128);
+        L->iq = round_up(intermediate, 128);
+        const uint64_t slots = L->E + 1;
+        L->bs_gu_codes.release();
+        L->bs_gu_sfa.release();
+        L->bs_dn_codes.release();
+        L->bs_dn_sfa.release();
+        CK(L->bs_gu_codes.reserve(slots * 2 * L->rp_i * (L->kq / 2)));
+        CK(L->bs_gu_sfa.reserve(slots * 2 * (L->rp_i / 128) * (L->kq / 128) * 512));
+        CK(L->bs_dn_codes.reserve(slots * L->rp_h * (L->iq / 2)));
+        CK(L->bs_dn_sfa.reserve(slots * (L->rp_h / 128) * (L->iq / 128) * 512));
+        if (!make_tmap2d(eng, &L->tmap_gu_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_gu_codes.ptr, L->kq,
+                         slots * 2 * L->rp_i, L->kq / 2, 128, 128, err) ||
+            !make_tmap2d(eng, &L->tmap_dn_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_dn_codes.ptr, L->iq,
+                         slots * L->rp_h, L->iq / 2, 128, 128, err)) {
+            return 0;
+        }
         L->present.assign(L->E + 1, 0);
     }
     const uint32_t slot = expert < 0 ? L->E : (uint32_t)expert;
@@ -312,6 +362,18 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
     CK(launch_repack_mxfp4(dsrc[0], intermediate, hidden, gu_dst, 2 * kTileBytes, 0));
     CK(launch_repack_mxfp4(dsrc[1], intermediate, hidden, gu_dst + kTileBytes, 2 * kTileBytes, 0));
     CK(launch_repack_mxfp4(dsrc[2], hidden, intermediate, dn_dst, kTileBytes, 0));
+    {
+        const uint64_t mti = L->rp_i / 128, kth = L->kq / 128, mth = L->rp_h / 128, kti = L->iq / 128;
+        for (int pj = 0; pj < 2; ++pj) {
+            const uint64_t m = (uint64_t)slot * 2 + pj;
+            CK(launch_repack_bs(dsrc[pj], intermediate, hidden, L->rp_i, L->kq,
+                                L->bs_gu_codes.as<uint8_t>() + m * L->rp_i * (L->kq / 2),
+                                L->bs_gu_sfa.as<uint8_t>() + m * mti * kth * 512, 0));
+        }
+        CK(launch_repack_bs(dsrc[2], hidden, intermediate, L->rp_h, L->iq,
+                            L->bs_dn_codes.as<uint8_t>() + (uint64_t)slot * L->rp_h * (L->iq / 2),
+                            L->bs_dn_sfa.as<uint8_t>() + (uint64_t)slot * mth * kti * 512, 0));
+    }
     CK(cudaDeviceSynchronize());
     L->present[slot] = 1;
     return 1;
@@ -372,23 +434,60 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     CK(eng->g_offset.reserve((size_t)(G + 1) * 4));
     CK(eng->g_gu_off.reserve((size_t)(G + 1) * 4));
     CK(eng->g_dn_off.reserve((size_t)(G + 1) * 4));
-    CK(eng->xperm.reserve((size_t)rows_cap * Kp * 2));
-    CK(eng->hperm.reserve((size_t)rows_cap * Ip * 2));
+    const bool bs = cfg->gemm_path == MOE_B200_GEMM_BLOCKSCALED;
+    const uint32_t Kq = L->kq, Iq = L->iq;  // K padded to 128 for the block-scaled path
+    // tokens per GEMM tile: 64 when groups are small on average (decode), else 128
+    const uint32_t block_n = (bs && (uint64_t)P <= 96ull * G) ? 64u : kBlockN;
     CK(eng->yperm.reserve((size_t)P * H * 4));
-
-    // tensor maps over the permuted activations and the intermediate
-    const uint64_t xrows = eng->xperm.bytes / ((uint64_t)Kp * 2), hrows = eng->hperm.bytes / ((uint64_t)Ip * 2);
-    if (eng->tmap_x_base != eng->xperm.ptr || eng->tmap_x_dims[0] != Kp || eng->tmap_x_dims[1] != xrows) {
-        if (!make_tmap(eng, &eng->tmap_x, eng->xperm.ptr, Kp, xrows, err)) return 0;
-        eng->tmap_x_base = eng->xperm.ptr;
-        eng->tmap_x_dims[0] = Kp;
-        eng->tmap_x_dims[1] = xrows;
-    }
-    if (eng->tmap_h_base != eng->hperm.ptr || eng->tmap_h_dims[0] != Ip || eng->tmap_h_dims[1] != hrows) {
-        if (!make_tmap(eng, &eng->tmap_h, eng->hperm.ptr, Ip, hrows, err)) return 0;
-        eng->tmap_h_base = eng->hperm.ptr;
-        eng->tmap_h_dims[0] = Ip;
-        eng->tmap_h_dims[1] = hrows;
+    if (bs) {
+        CK(eng->xq_hi.reserve((size_t)T * Kq));
+        CK(eng->xq_lo.reserve((size_t)T * Kq));
+        CK(eng->sx_hi.reserve((size_t)T * (Kq / 32)));
+        CK(eng->sx_lo.reserve((size_t)T * (Kq / 32)));
+        CK(eng->xb_hi.reserve((size_t)rows_cap * Kq));
+        CK(eng->xb_lo.reserve((size_t)rows_cap * Kq));
+        const size_t token_tiles = (size_t)P / block_n + G;  // upper bound of sum_g ceil(count_g / block_n)
+        CK(eng->sfx_atoms.reserve(token_tiles * (Kq / 128) * 1024));
+        CK(eng->hb_hi.reserve((size_t)rows_cap * Iq));
+        CK(eng->hb_lo.reserve((size_t)rows_cap * Iq));
+        CK(eng->sfh_atoms.reserve(token_tiles * (Iq / 128) * 1024));
+        // E4M3 activation / intermediate rows: 128-byte x 32-row boxes
+        struct MapSpec {
+            CUtensorMap* map;
+            DevBuf* buf;
+            uint32_t cols;
+        } specs[4] = {{&eng->tmap_xhi, &eng->xb_hi, Kq}, {&eng->tmap_xlo, &eng->xb_lo, Kq},
+                      {&eng->tmap_hhi, &eng->hb_hi, Iq}, {&eng->tmap_hlo, &eng->hb_lo, Iq}};
+        for (int i = 0; i < 4; ++i) {
+            const uint64_t rows = specs[i].buf->bytes / specs[i].cols;
+            if (eng->bs_map_key[i] != specs[i].buf->ptr || eng->bs_map_dims[i][0] != specs[i].cols ||
+                eng->bs_map_dims[i][1] != rows) {
+                if (!make_tmap2d(eng, specs[i].map, CU_TENSOR_MAP_DATA_TYPE_UINT8, specs[i].buf->ptr, specs[i].cols,
+                                 rows, specs[i].cols, 128, 32, err)) {
+                    return 0;
+                }
+                eng->bs_map_key[i] = specs[i].buf->ptr;
+                eng->bs_map_dims[i][0] = specs[i].cols;
+                eng->bs_map_dims[i][1] = rows;
+            }
+        }
+    } else {
+        CK(eng->xperm.reserve((size_t)rows_cap * Kp * 2));
+        CK(eng->hperm.reserve((size_t)rows_cap * Ip * 2));
+        // tensor maps over the permuted activations and the intermediate
+        const uint64_t xrows = eng->xperm.bytes / ((uint64_t)Kp * 2), hrows = eng->hperm.bytes / ((uint64_t)Ip * 2);
+        if (eng->tmap_x_base != eng->xperm.ptr || eng->tmap_x_dims[0] != Kp || eng->tmap_x_dims[1] != xrows) {
+            if (!make_tmap(eng, &eng->tmap_x, eng->xperm.ptr, Kp, xrows, err)) return 0;
+            eng->tmap_x_base = eng->xperm.ptr;
+            eng->tmap_x_dims[0] = Kp;
+            eng->tmap_x_dims[1] = xrows;
+        }
+        if (eng->tmap_h_base != eng->hperm.ptr || eng->tmap_h_dims[0] != Ip || eng->tmap_h_dims[1] != hrows) {
+            if (!make_tmap(eng, &eng->tmap_h, eng->hperm.ptr, Ip, hrows, err)) return 0;
+            eng->tmap_h_base = eng->hperm.ptr;
+            eng->tmap_h_dims[0] = Ip;
+            eng->tmap_h_dims[1] = hrows;
+        }
     }
 
     cudaEvent_t* ev = nullptr;
@@ -417,7 +516,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     gi.offset = eng->g_offset.as<uint32_t>();
     gi.gu_tile_off = eng->g_gu_off.as<uint32_t>();
     gi.dn_tile_off = eng->g_dn_off.as<uint32_t>();
-    gi.block_n = kBlockN;
+    gi.block_n = block_n;
     gi.gu_row_tiles = ceil_div(I, kTileRows);
     gi.dn_row_tiles = ceil_div(H, kTileRows);
     CK(launch_permute(ids, T, K, E, shared_rows, eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi,
@@ -425,6 +524,51 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
                       errw, st));
     launches += 3;
     mark(2);
+    if (bs) {
+        // activations -> exact hi/lo E4M3 terms per token, then per permuted row
+        CK(launch_quantize_rows(x, T, H, Kq, eng->xq_hi.as<uint8_t>(), eng->xq_lo.as<uint8_t>(),
+                                eng->sx_hi.as<uint8_t>(), eng->sx_lo.as<uint8_t>(), st));
+        CK(launch_gather_bs(eng->xq_hi.as<uint8_t>(), eng->xq_lo.as<uint8_t>(), eng->sx_hi.as<uint8_t>(),
+                            eng->sx_lo.as<uint8_t>(), Kq, eng->row_token.as<uint32_t>(), P, gi.offset,
+                            gi.gu_tile_off, G, gi.gu_row_tiles, block_n, eng->xb_hi.as<uint8_t>(),
+                            eng->xb_lo.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(), st));
+        launches += 2;
+        mark(3);
+        BsParams bp{};
+        bp.groups = G;
+        bp.count = gi.count;
+        bp.offset = gi.offset;
+        bp.err = errw;
+        // gate/up: K = H (padded Kq), M = I rows (padded rp_i), output h hi/lo
+        bp.tile_off = gi.gu_tile_off;
+        bp.rows_pad = L->rp_i;
+        bp.m_tiles = L->rp_i / 128;
+        bp.k_tiles = Kq / 128;
+        bp.sfa = L->bs_gu_sfa.as<uint8_t>();
+        bp.sfb_atoms = eng->sfx_atoms.as<uint8_t>();
+        bp.h_hi = eng->hb_hi.as<uint8_t>();
+        bp.h_lo = eng->hb_lo.as<uint8_t>();
+        bp.h_stride = Iq;
+        bp.sfh_atoms = eng->sfh_atoms.as<uint8_t>();
+        bp.m_valid = Iq;
+        CK(launch_gemm_bs(kGateUp, (int)block_n, L->tmap_gu_codes, eng->tmap_xhi, eng->tmap_xlo, bp, eng->num_sms,
+                          st));
+        launches += 1;
+        mark(4);
+        // down: K = I (padded Iq), M = H rows (padded rp_h), output fp32 rows
+        bp.tile_off = gi.dn_tile_off;
+        bp.rows_pad = L->rp_h;
+        bp.m_tiles = L->rp_h / 128;
+        bp.k_tiles = Iq / 128;
+        bp.sfa = L->bs_dn_sfa.as<uint8_t>();
+        bp.sfb_atoms = eng->sfh_atoms.as<uint8_t>();
+        bp.y_out = eng->yperm.as<float>();
+        bp.y_stride = H;
+        bp.m_valid = H;
+        CK(launch_gemm_bs(kDown, (int)block_n, L->tmap_dn_codes, eng->tmap_hhi, eng->tmap_hlo, bp, eng->num_sms, st));
+        launches += 1;
+        mark(5);
+    } else {
     CK(launch_gather(x, H, Kp, eng->row_token.as<uint32_t>(), P, eng->xperm.as<uint16_t>(), st));
     launches += 1;
     mark(3);
@@ -464,6 +608,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     }
     launches += 1;
     mark(5);
+    }
 
     CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), w, T, K, shared ? 1 : 0, n, y_bf16,
                       y_f32, st));
@@ -611,8 +756,8 @@ int moe_b200_debug_read(moe_b200_engine_t* eng, int32_t which, void* dst, uint64
         case MOE_B200_BUF_GROUP_COUNT: src = eng->g_count.ptr; have = (uint64_t)eng->last_G * 4; break;
         case MOE_B200_BUF_GROUP_OFFSET: src = eng->g_offset.ptr; have = (uint64_t)(eng->last_G + 1) * 4; break;
         case MOE_B200_BUF_ROW_TOKEN: src = eng->row_token.ptr; have = (uint64_t)eng->last_P * 4; break;
-        case MOE_B200_BUF_XPERM: src = eng->xperm.ptr; have = (uint64_t)eng->last_P * eng->last_Kp * 2; break;
-        case MOE_B200_BUF_HPERM: src = eng->hperm.ptr; have = (uint64_t)eng->last_P * eng->last_Ip * 2; break;
+        case MOE_B200_BUF_XPERM: src = eng->xperm.ptr; have = eng->xperm.bytes; break;
+        case MOE_B200_BUF_HPERM: src = eng->hperm.ptr; have = eng->hperm.bytes; break;
         case MOE_B200_BUF_YPERM: src = eng->yperm.ptr; have = (uint64_t)eng->last_P * eng->last_H * 4; break;
         default: set_err(err, "unknown buffer %d", which); return 0;
     }

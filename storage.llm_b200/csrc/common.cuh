@@ -225,6 +225,51 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
         "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])                  \
         : "memory")
 
+// ---------------------------------------------------------------------------
+// Block-scaled MMA (kind::mxf8f6f4): A = E2M1 weights, B = E4M3 activations,
+// E8M0 scale factors for both in TMEM.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+}
+
+// Instruction descriptor for kind::mxf8f6f4 block_scale: A E2M1, B E4M3,
+// E8M0 scales, both operands K-major, M = 128, N = n; `sf_id` selects the
+// byte of each 32-bit scale word (the 32-element K block inside a 128-K stage).
+__device__ __forceinline__ uint32_t idesc_bs_m128(uint32_t n, uint32_t sf_id) {
+    return (sf_id << 4)          // B scale-factor id
+           | (5u << 7)           // A format E2M1
+           | (0u << 10)          // B format E4M3
+           | ((n >> 3) << 17)    // N / 8
+           | (1u << 23)          // scale format E8M0
+           | ((128u >> 4) << 24) // M / 16
+           | (sf_id << 29);      // A scale-factor id
+}
+
+// Shared-memory descriptor of a 32 x 128-bit scale-factor block (no swizzle,
+// 16-byte rows, 8-row core matrices 128 bytes apart), the source of
+// tcgen05.cp.32x128b.
+__device__ __forceinline__ uint64_t smem_desc_sf(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFF) >> 4);
+    d |= (uint64_t)(128 >> 4) << 16;   // leading byte offset
+    d |= (uint64_t)(128 >> 4) << 32;   // stride byte offset: next 8 rows
+    d |= (uint64_t)1 << 46;            // descriptor version (sm_100)
+    return d;                          // layout type 0: no swizzle
+}
+
+// Copies a 32-row x 128-bit scale block from shared memory to TMEM columns
+// [taddr, taddr+4), replicated into all four lane quarters.
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 #define MOE_TMEM_ST16(taddr, v)                                                                              \
     asm volatile(                                                                                            \
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "  \

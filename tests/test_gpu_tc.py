@@ -11,9 +11,10 @@ pytestmark = pytest.mark.gpu
 LAYER_FIXTURES = sorted(p.name for p in GOLDEN.glob("layer_*.npz"))
 
 
+@pytest.mark.parametrize("path", [0, 2], ids=["blockscaled", "tmem_decode"])
 @pytest.mark.parametrize("name", LAYER_FIXTURES)
-def test_layer_matches_reference_tcgen05(name, engine, synth, L):
-    check_layer_fixture(name, 0, engine, synth, L)
+def test_layer_matches_reference_tcgen05(name, path, engine, synth, L):
+    check_layer_fixture(name, path, engine, synth, L)
 
 
 def test_tensor_core_path_matches_simt_path(engine, synth, L):
@@ -21,16 +22,35 @@ def test_tensor_core_path_matches_simt_path(engine, synth, L):
     li = synth.make_layer(shape, seed=31)
     engine.upload_layer(li)
     res = {}
-    for path in (L.GEMM_SIMT, L.GEMM_TCGEN05):
+    for path in (L.GEMM_SIMT, L.GEMM_TMEM_DECODE):
         out = engine.forward_host(L.Engine.cfg(shape, gemm_path=path), li.x)
         P = 200 * 3
         res[path] = dict(out=out, h=engine.read(L.BUF_HPERM, (P, 320), np.uint16),
                          y=engine.read(L.BUF_YPERM, (P, 256), np.float32))
     hs = bf16_to_f32(res[L.GEMM_SIMT]["h"])
-    ht = bf16_to_f32(res[L.GEMM_TCGEN05]["h"])
+    ht = bf16_to_f32(res[L.GEMM_TMEM_DECODE]["h"])
     # same products, different fp32 summation order, then bf16 rounding
     assert np.allclose(ht, hs, rtol=2 ** -7, atol=1e-4), np.abs(ht - hs).max()
-    ys, yt = res[L.GEMM_SIMT]["y"], res[L.GEMM_TCGEN05]["y"]
+    ys, yt = res[L.GEMM_SIMT]["y"], res[L.GEMM_TMEM_DECODE]["y"]
     assert np.allclose(yt, ys, rtol=1e-3, atol=1e-4), np.abs(yt - ys).max()
+
+
+@pytest.mark.parametrize("tokens,top_k,experts", [(200, 3, 8), (40, 2, 16), (700, 4, 8)])
+def test_blockscaled_expert_outputs_match_simt(engine, synth, L, tokens, top_k, experts):
+    """Per permuted row, the block-scaled GEMMs' fp32 expert outputs against
+    the CUDA-core path (same products; the intermediate is rounded as two
+    E4M3 terms instead of bf16, so the bar is a relative one)."""
+    shape = synth.small_shape(hidden=256, intermediate=320, experts=experts, top_k=top_k, tokens=tokens)
+    li = synth.make_layer(shape, seed=41 + tokens)
+    engine.upload_layer(li)
+    P, H = tokens * top_k, 256
+    out_s = engine.forward_host(L.Engine.cfg(shape, gemm_path=L.GEMM_SIMT), li.x)
+    ys = engine.read(L.BUF_YPERM, (P, H), np.float32)
+    out_b = engine.forward_host(L.Engine.cfg(shape, gemm_path=L.GEMM_BLOCKSCALED), li.x)
+    yb = engine.read(L.BUF_YPERM, (P, H), np.float32)
+    assert np.array_equal(out_s["ids"], out_b["ids"])
+    scale = np.abs(ys).mean()
+    assert np.abs(yb - ys).max() <= 0.05 * np.abs(ys).max() + 1e-6, np.abs(yb - ys).max()
+    assert np.abs(yb - ys).mean() <= 5e-3 * scale, (np.abs(yb - ys).mean(), scale)
 
 
