@@ -106,7 +106,7 @@ struct moe_b200_engine {
     DevBuf xperm, hperm, yperm;
     DevBuf err_word;
     // block-scaled path: quantised activations and intermediate
-    DevBuf xq_hi, xq_lo, sx_hi, sx_lo, xb_hi, xb_lo, sfx_atoms, hb_hi, hb_lo, sfh_atoms;
+    DevBuf xq_hi, xq_lo, sx_hi, sx_lo, xb_hi, xb_lo, sfx_atoms, hb_hi, hb_lo, sfh_atoms, gu_tiles, dn_tiles;
     CUtensorMap tmap_xhi{}, tmap_xlo{}, tmap_hhi{}, tmap_hlo{};
     const void* bs_map_key[4] = {nullptr, nullptr, nullptr, nullptr};
     uint64_t bs_map_dims[4][2] = {};
@@ -254,7 +254,7 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
                       &eng->yperm, &eng->err_word, &eng->hx, &eng->hy, &eng->hyf, &eng->hids,
                       &eng->hw, &eng->hperm_out, &eng->tri, &eng->xq_hi, &eng->xq_lo, &eng->sx_hi,
                       &eng->sx_lo, &eng->xb_hi, &eng->xb_lo, &eng->sfx_atoms, &eng->hb_hi, &eng->hb_lo,
-                      &eng->sfh_atoms};
+                      &eng->sfh_atoms, &eng->gu_tiles, &eng->dn_tiles};
     for (DevBuf* b : bufs) b->release();
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
     delete eng;
@@ -335,10 +335,12 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
         CK(L->bs_gu_sfa.reserve(slots * 2 * (L->rp_i / 128) * (L->kq / 128) * 512));
         CK(L->bs_dn_codes.reserve(slots * L->rp_h * (L->iq / 2)));
         CK(L->bs_dn_sfa.reserve(slots * (L->rp_h / 128) * (L->iq / 128) * 512));
-        if (!make_tmap2d(eng, &L->tmap_gu_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_gu_codes.ptr, L->kq,
-                         slots * 2 * L->rp_i, L->kq / 2, 128, 128, err) ||
-            !make_tmap2d(eng, &L->tmap_dn_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_dn_codes.ptr, L->iq,
-                         slots * L->rp_h, L->iq / 2, 128, 128, err)) {
+        // codes are 8 KB blocks of 128 rows x 128 K: a "tall" tensor of 128-element
+        // rows, one 128 x 128 box per block
+        if (!make_tmap2d(eng, &L->tmap_gu_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_gu_codes.ptr, 128,
+                         slots * 2 * L->rp_i * (L->kq / 128), 64, 128, 128, err) ||
+            !make_tmap2d(eng, &L->tmap_dn_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_dn_codes.ptr, 128,
+                         slots * L->rp_h * (L->iq / 128), 64, 128, 128, err)) {
             return 0;
         }
         L->present.assign(L->E + 1, 0);
@@ -451,6 +453,8 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         CK(eng->hb_hi.reserve((size_t)rows_cap * Iq));
         CK(eng->hb_lo.reserve((size_t)rows_cap * Iq));
         CK(eng->sfh_atoms.reserve(token_tiles * (Iq / 128) * 1024));
+        CK(eng->gu_tiles.reserve(token_tiles * (L->rp_i / 128) * sizeof(TileEntry)));
+        CK(eng->dn_tiles.reserve(token_tiles * (L->rp_h / 128) * sizeof(TileEntry)));
         // E4M3 activation / intermediate rows: 128-byte x 32-row boxes
         struct MapSpec {
             CUtensorMap* map;
@@ -525,6 +529,12 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     launches += 3;
     mark(2);
     if (bs) {
+        const uint32_t token_tiles = P / block_n + G;
+        CK(launch_build_tiles(gi.count, gi.offset, gi.gu_tile_off, G, L->rp_i / 128, block_n,
+                              token_tiles * (L->rp_i / 128), eng->gu_tiles.as<TileEntry>(), st));
+        CK(launch_build_tiles(gi.count, gi.offset, gi.dn_tile_off, G, L->rp_h / 128, block_n,
+                              token_tiles * (L->rp_h / 128), eng->dn_tiles.as<TileEntry>(), st));
+        launches += 2;
         // activations -> exact hi/lo E4M3 terms per token, then per permuted row
         CK(launch_quantize_rows(x, T, H, Kq, eng->xq_hi.as<uint8_t>(), eng->xq_lo.as<uint8_t>(),
                                 eng->sx_hi.as<uint8_t>(), eng->sx_lo.as<uint8_t>(), st));
@@ -541,10 +551,12 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         bp.err = errw;
         // gate/up: K = H (padded Kq), M = I rows (padded rp_i), output h hi/lo
         bp.tile_off = gi.gu_tile_off;
+        bp.tiles = eng->gu_tiles.as<TileEntry>();
         bp.rows_pad = L->rp_i;
         bp.m_tiles = L->rp_i / 128;
         bp.k_tiles = Kq / 128;
         bp.sfa = L->bs_gu_sfa.as<uint8_t>();
+        bp.a_codes = L->bs_gu_codes.as<uint8_t>();
         bp.sfb_atoms = eng->sfx_atoms.as<uint8_t>();
         bp.h_hi = eng->hb_hi.as<uint8_t>();
         bp.h_lo = eng->hb_lo.as<uint8_t>();
@@ -557,10 +569,12 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         mark(4);
         // down: K = I (padded Iq), M = H rows (padded rp_h), output fp32 rows
         bp.tile_off = gi.dn_tile_off;
+        bp.tiles = eng->dn_tiles.as<TileEntry>();
         bp.rows_pad = L->rp_h;
         bp.m_tiles = L->rp_h / 128;
         bp.k_tiles = Iq / 128;
         bp.sfa = L->bs_dn_sfa.as<uint8_t>();
+        bp.a_codes = L->bs_dn_codes.as<uint8_t>();
         bp.sfb_atoms = eng->sfh_atoms.as<uint8_t>();
         bp.y_out = eng->yperm.as<float>();
         bp.y_stride = H;

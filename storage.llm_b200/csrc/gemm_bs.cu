@@ -2,9 +2,11 @@
 // weights as they are stored -- E2M1 codes plus one E8M0 scale per 32 K --
 // so no SM instruction is spent decoding weights.
 //
-//   A  E2M1 weight codes, packed two per byte in HBM, TMA'd with the
-//      16U4_ALIGN16B type (each 16 codes land in 16 bytes of shared memory,
-//      the operand form kind::mxf8f6f4 reads), 128 rows x 128 K per box;
+//   A  E2M1 weight codes, packed two per byte in HBM as contiguous 8 KB
+//      blocks of 128 rows x 128 K, TMA'd with the 16U4_ALIGN16B type (each 16
+//      codes land in 16 bytes of shared memory, the operand form
+//      kind::mxf8f6f4 reads).  (Prefetching upcoming blocks into L2 was
+//      measured and lost time: it competes with the demand loads.);
 //   SFA the rows' E8M0 scales, one 512-byte block per 128 x 128 tile laid out
 //      as tcgen05.cp.32x128b.warpx4 expects (row r, K block j at byte
 //      (r%32)*16 + (r/32)*4 + j), copied to TMEM each stage;
@@ -36,16 +38,24 @@ namespace moe_b200 {
 
 template <int MODE, int BN>
 struct BsCfg {
+    // The down GEMM's 64-token tiles stack the hi and lo terms along N in one
+    // MMA (B rows 0-63 hi, 64-127 lo), reading the A tile once per K step.
+    // Elsewhere the hi and lo MMAs accumulate into the same columns, which
+    // keeps two gate+up accumulators in TMEM so the epilogue overlaps the next
+    // tile.
+    static constexpr bool kStackN = MODE == kDown && BN == 64;
     static constexpr int kNA = MODE == kGateUp ? 2 : 1;       // A operands per stage
     static constexpr int kABytes = 128 * 128;                 // smem bytes per A box
     static constexpr int kATx = 128 * 128 / 2;                // packed bytes the A box moves
     static constexpr int kBBytes = BN * 128;                  // smem bytes per B term (hi or lo)
     static constexpr int kSF = 512;
-    static constexpr int kStageBytes = kNA * kABytes + 2 * kBBytes + (kNA + 2) * kSF;
+    static constexpr int kSFB = kStackN ? 512 : 1024;         // activation scale bytes per stage
+    static constexpr int kSFStage = kNA * kSF + kSFB;         // scale bytes per stage
+    static constexpr int kStageBytes = kNA * kABytes + 2 * kBBytes + kNA * kSF + kSFB;
     static constexpr int kStages = (200 * 1024) / kStageBytes;
-    static constexpr int kAccCols = kNA * BN;
+    static constexpr int kAccCols = kNA * (kStackN ? 2 * BN : BN);
     static constexpr int kAccs = 256 / kAccCols >= 2 ? 2 : 1;
-    static constexpr int kSFCols = (kNA + 2) * 4;             // TMEM columns of scale factors per stage
+    static constexpr int kSFCols = kNA * 4 + kSFB / 128;      // TMEM columns of scale factors per stage
     static constexpr int kSmem = kStages * kStageBytes + 2048 /*two 1024 alignments*/ + 512 /*barriers*/;
     static_assert(kStages >= 3, "pipeline too shallow");
     static_assert(256 + kStages * kSFCols <= 512, "TMEM budget");
@@ -56,10 +66,10 @@ __device__ __forceinline__ float pow2f(int e) {
     return e >= -126 ? __int_as_float((e + 127) << 23) : __int_as_float(0x00400000);
 }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
+// Warp-wide maximum of non-negative floats in one redux.sync: their bit
+// patterns order like unsigned integers.
+__device__ __forceinline__ float warp_max_abs(float v) {
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
 }
 
 // Scale exponent for a 32-value block with absolute maximum `amax`: the block
@@ -79,10 +89,10 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
 // Splits the 32 values held by a warp (one per lane, one 32-element K block)
 // into hi + lo E4M3 terms with E8M0 scale bytes.  Warp-collective.
 __device__ __forceinline__ void split_e4m3_warp(float v, uint8_t& hi, uint8_t& lo, uint8_t& s_hi, uint8_t& s_lo) {
-    const int e1 = block_exp(warp_max(fabsf(v)));
+    const int e1 = block_exp(warp_max_abs(v));
     hi = __nv_cvt_float_to_fp8(v * pow2f(-e1), __NV_SATFINITE, __NV_E4M3);
     const float r = v - e4m3_to_f32(hi) * pow2f(e1);
-    const int e2 = block_exp(warp_max(fabsf(r)));
+    const int e2 = block_exp(warp_max_abs(r));
     lo = __nv_cvt_float_to_fp8(r * pow2f(-e2), __NV_SATFINITE, __NV_E4M3);
     s_hi = (uint8_t)(e1 + 127);
     s_lo = (uint8_t)(e2 + 127);
@@ -126,6 +136,7 @@ __global__ void gather_bs_kernel(const uint8_t* __restrict__ q_hi, const uint8_t
                                  const uint32_t* __restrict__ offset, const uint32_t* __restrict__ tile_off,
                                  uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* __restrict__ x_hi,
                                  uint8_t* __restrict__ x_lo, uint8_t* __restrict__ sf_atoms) {
+    const uint32_t atom_bytes = 1024, lo_off = 512;  // hi block, then lo block
     const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t nv = Kp / 16, nkt = Kp / 128;
@@ -152,17 +163,18 @@ __global__ void gather_bs_kernel(const uint8_t* __restrict__ q_hi, const uint8_t
         const uint32_t* wh = reinterpret_cast<const uint32_t*>(s_hi + (uint64_t)t * (Kp / 32));
         const uint32_t* wl = reinterpret_cast<const uint32_t*>(s_lo + (uint64_t)t * (Kp / 32));
         for (uint32_t kt = lane; kt < nkt; kt += 32) {
-            uint8_t* atom = sf_atoms + (tile * nkt + kt) * 1024;
+            uint8_t* atom = sf_atoms + (tile * nkt + kt) * atom_bytes;
             *reinterpret_cast<uint32_t*>(atom + pos) = __ldg(wh + kt);
-            *reinterpret_cast<uint32_t*>(atom + 512 + pos) = __ldg(wl + kt);
+            *reinterpret_cast<uint32_t*>(atom + lo_off + pos) = __ldg(wl + kt);
         }
     }
 }
 
 // ---------------------------------------------------------------------------
 // Weight repack for the block-scaled path (once per expert at upload).
-//   codes: row r of the matrix at codes + r * Kp/2, element 2j in the low
-//          nibble of byte j (zero past `cols`);
+//   codes: blocks [row_tile][k_tile] of 128 rows x 128 K, 8 KB each, row r of
+//          a block at r*64 bytes, element 2j in the low nibble of byte j
+//          (zero past `rows` / `cols`);
 //   sfa:   [row_tile][k_tile][512] scale blocks in the tcgen05.cp layout.
 // ---------------------------------------------------------------------------
 __global__ void repack_bs_kernel(const uint8_t* __restrict__ gguf, uint32_t rows, uint32_t cols, uint32_t rows_pad,
@@ -174,17 +186,21 @@ __global__ void repack_bs_kernel(const uint8_t* __restrict__ gguf, uint32_t rows
     for (uint64_t idx = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; idx < nbytes + nsf;
          idx += (uint64_t)gridDim.x * blockDim.x) {
         if (idx < nbytes) {
-            const uint32_t r = (uint32_t)(idx / (Kp / 2));
-            const uint32_t j = (uint32_t)(idx % (Kp / 2));
+            // idx walks the output: block (mt, kt), row rr, byte jb
+            const uint64_t blk = idx / 8192;
+            const uint32_t within = (uint32_t)(idx % 8192);
+            const uint32_t mt = (uint32_t)(blk / kt_n), kt = (uint32_t)(blk % kt_n);
+            const uint32_t r = mt * 128 + within / 64;
+            const uint32_t j = kt * 64 + within % 64;  // byte index along the row
             uint32_t b = 0;
             if (r < rows) {
                 const uint8_t* row = gguf + (uint64_t)r * gguf_row_bytes;
                 for (int h = 0; h < 2; ++h) {
                     const uint32_t k = 2 * j + h;
                     if (k < cols) {
-                        const uint8_t* blk = row + (k / 32) * 17;
+                        const uint8_t* gb = row + (k / 32) * 17;
                         const uint32_t i = k % 32;
-                        const uint32_t code = i < 16 ? (blk[1 + i] & 0x0Fu) : (blk[1 + i - 16] >> 4);
+                        const uint32_t code = i < 16 ? (gb[1 + i] & 0x0Fu) : (gb[1 + i - 16] >> 4);
                         b |= code << (4 * h);
                     }
                 }
@@ -239,21 +255,48 @@ struct BsTile {
     uint32_t g, mt, n0, nn;
 };
 
-template <int BN>
-__device__ __forceinline__ void bs_tile_coord(const BsParams& p, uint32_t tile, BsTile& tc) {
-    uint32_t lo = 0, hi = p.groups;
-    while (hi - lo > 1) {
-        const uint32_t mid = (lo + hi) >> 1;
-        if (p.tile_off[mid] <= tile) lo = mid;
-        else hi = mid;
+struct BsTileX {
+    uint32_t g, mt, row0, nn, ntile;
+};
+
+__device__ __forceinline__ BsTileX load_tile(const BsParams& p, uint32_t tile) {
+    const uint4 e = __ldg(reinterpret_cast<const uint4*>(p.tiles) + tile);
+    return BsTileX{e.x, e.y, e.z, e.w & 0xFFu, e.w >> 8};
+}
+
+// Tile table: tile index -> (group, weight row tile, first row, tokens, token
+// tile), in the order (group, row tile, token tile).  One thread per entry.
+__global__ void build_tiles_kernel(const uint32_t* __restrict__ count, const uint32_t* __restrict__ offset,
+                                   const uint32_t* __restrict__ tile_off, uint32_t groups, uint32_t m_tiles,
+                                   uint32_t block_n, uint32_t max_tiles, TileEntry* __restrict__ tiles) {
+    const uint32_t total = tile_off[groups];
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total && t < max_tiles;
+         t += gridDim.x * blockDim.x) {
+        uint32_t lo = 0, hi = groups;
+        while (hi - lo > 1) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (tile_off[mid] <= t) lo = mid;
+            else hi = mid;
+        }
+        const uint32_t local = t - tile_off[lo];
+        const uint32_t ntn = ceil_div(count[lo], block_n);
+        const uint32_t nt = local % ntn;
+        const uint32_t n0 = nt * block_n;
+        TileEntry e;
+        e.group = lo;
+        e.mt = local / ntn;
+        e.row0 = offset[lo] + n0;
+        e.nn_ntile = min(block_n, count[lo] - n0) | ((tile_off[lo] / m_tiles + nt) << 8);
+        tiles[t] = e;
     }
-    const uint32_t local = tile - p.tile_off[lo];
-    const uint32_t cnt = p.count[lo];
-    const uint32_t ntn = ceil_div(cnt, BN);
-    tc.g = lo;
-    tc.mt = local / ntn;
-    tc.n0 = (local % ntn) * BN;
-    tc.nn = min((uint32_t)BN, cnt - tc.n0);
+}
+
+cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, const uint32_t* tile_off,
+                               uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint32_t max_tiles,
+                               TileEntry* tiles, cudaStream_t st) {
+    const uint32_t blocks = max(1u, min(ceil_div(max_tiles, 256), 148u * 4u));
+    build_tiles_kernel<<<blocks, 256, 0, st>>>(count, offset, tile_off, groups, m_tiles, block_n, max_tiles, tiles);
+    return cudaGetLastError();
 }
 
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
@@ -267,8 +310,8 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     // scale-factor blocks first (small), then the 1024-aligned operand tiles
-    uint8_t* sf_base = smem;                                                  // [stages][kNA+2][512]
-    uint8_t* a_base = smem + C::kStages * (C::kNA + 2) * C::kSF;              // [stages][kNA][16 KB]
+    uint8_t* sf_base = smem;                                                  // [stages][kSFStage]
+    uint8_t* a_base = smem + C::kStages * C::kSFStage;                        // [stages][kNA][16 KB]
     a_base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(a_base) + 1023) & ~uintptr_t(1023));
     uint8_t* b_base = a_base + C::kStages * C::kNA * C::kABytes;              // [stages][2][kBBytes]
     uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + C::kStages * 2 * C::kBBytes);
@@ -311,32 +354,30 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
         uint32_t stage = 0, phase = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-            BsTile tc;
-            bs_tile_coord<BN>(p, tile, tc);
-            const uint32_t row0 = p.offset[tc.g] + tc.n0;
+            const BsTileX tc = load_tile(p, tile);
+            const uint32_t row0 = tc.row0;
             const uint32_t n_sub = ceil_div(tc.nn, 32);
-            const uint32_t ntile = p.tile_off[tc.g] / p.m_tiles + tc.n0 / BN;
+            const uint32_t ntile = tc.ntile;
+            const uint64_t blk0 = ((uint64_t)tc.g * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
             for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
                 ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
                     break;
                 }
-                uint8_t* sf = sf_base + stage * (C::kNA + 2) * C::kSF;
+                uint8_t* sf = sf_base + stage * C::kSFStage;
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&load_full[stage],
-                                          C::kNA * (C::kATx + C::kSF) + 2 * C::kSF + 2 * n_sub * 32 * 128);
-                    // activation scales: hi and lo blocks of this token tile and stage
-                    bulk_g2s(sf + C::kNA * C::kSF, p.sfb_atoms + ((uint64_t)ntile * p.k_tiles + kt) * 1024,
-                             2 * C::kSF, &load_full[stage]);
+                                          C::kNA * (C::kATx + C::kSF) + C::kSFB + 2 * n_sub * 32 * 128);
+                    // activation scales of this token tile and stage (hi and lo)
+                    bulk_g2s(sf + C::kNA * C::kSF, p.sfb_atoms + ((uint64_t)ntile * p.k_tiles + kt) * C::kSFB,
+                             C::kSFB, &load_full[stage]);
 #pragma unroll
                     for (int pj = 0; pj < C::kNA; ++pj) {
-                        const int32_t arow = (int32_t)(((uint64_t)tc.g * C::kNA + pj) * p.rows_pad + tc.mt * 128);
-                        tma_load_2d(a_base + (stage * C::kNA + pj) * C::kABytes, &tmap_a, (int32_t)(kt * 128), arow,
+                        const uint64_t b = blk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt;  // weight block
+                        tma_load_2d(a_base + (stage * C::kNA + pj) * C::kABytes, &tmap_a, 0, (int32_t)(b * 128),
                                     &load_full[stage]);
-                        const uint8_t* sfa_src =
-                            p.sfa + ((((uint64_t)tc.g * C::kNA + pj) * p.m_tiles + tc.mt) * p.k_tiles + kt) * 512;
-                        bulk_g2s(sf + pj * C::kSF, sfa_src, C::kSF, &load_full[stage]);
+                        bulk_g2s(sf + pj * C::kSF, p.sfa + b * 512, C::kSF, &load_full[stage]);
                     }
                     uint8_t* bh = b_base + stage * 2 * C::kBBytes;
                     for (uint32_t sb = 0; sb < n_sub; ++sb) {
@@ -359,32 +400,40 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
             uint32_t stage = 0, phase = 0, acc = 0, accphase = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-                BsTile tc;
-                bs_tile_coord<BN>(p, tile, tc);
-                const uint32_t n_mma = max(16u, (tc.nn + 15u) & ~15u);
+                const BsTileX tc = load_tile(p, tile);
+                // stacked: hi rows [0, BN) then lo rows [BN, BN + n_pad); else one term per MMA
+                const uint32_t n_pad = ceil_div(tc.nn, 32) * 32;
+                const uint32_t n_mma = C::kStackN ? BN + n_pad : max(16u, (tc.nn + 15u) & ~15u);
                 if (!(ok = mbar_wait(&acc_empty[acc], accphase ^ 1, p.err, kErrTimeoutAccEmpty))) break;
                 tc_fence_after();
                 const uint32_t d0 = tmem + acc * C::kAccCols;
                 for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
                     if (!(ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull))) break;
                     tc_fence_after();
-                    const uint8_t* sf = sf_base + stage * (C::kNA + 2) * C::kSF;
+                    const uint8_t* sf = sf_base + stage * C::kSFStage;
                     const uint32_t sfc = tmem + kSfCol0 + stage * C::kSFCols;
 #pragma unroll
-                    for (int q = 0; q < C::kNA + 2; ++q) tmem_cp_sf(sfc + q * 4, smem_desc_sf(smem_u32(sf + q * C::kSF)));
+                    for (int q = 0; q < C::kSFStage / 512; ++q) {
+                        tmem_cp_sf(sfc + q * 4, smem_desc_sf(smem_u32(sf + q * C::kSF)));
+                    }
+                    const uint32_t sfb = sfc + C::kNA * 4;
                     const uint32_t a_addr = smem_u32(a_base + stage * C::kNA * C::kABytes);
                     const uint32_t bh_addr = smem_u32(b_base + stage * 2 * C::kBBytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t idesc = idesc_bs_m128(n_mma, kk);
                         const uint64_t bhi = smem_desc_sw128(bh_addr + kk * 32);
-                        const uint64_t blo = smem_desc_sw128(bh_addr + C::kBBytes + kk * 32);
 #pragma unroll
                         for (int pj = 0; pj < C::kNA; ++pj) {
                             const uint64_t adesc = smem_desc_sw128(a_addr + pj * C::kABytes + kk * 32);
-                            const uint32_t d = d0 + pj * BN;
-                            mma_bs(d, adesc, bhi, idesc, sfc + pj * 4, sfc + C::kNA * 4, (kt | kk) != 0);
-                            mma_bs(d, adesc, blo, idesc, sfc + pj * 4, sfc + C::kNA * 4 + 4, 1);
+                            if (C::kStackN) {
+                                mma_bs(d0 + pj * 2 * BN, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
+                            } else {
+                                const uint64_t blo = smem_desc_sw128(bh_addr + C::kBBytes + kk * 32);
+                                const uint32_t d = d0 + pj * BN;
+                                mma_bs(d, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
+                                mma_bs(d, adesc, blo, idesc, sfc + pj * 4, sfb + 4, 1);
+                            }
                         }
                     }
                     mma_commit(&load_empty[stage]);
@@ -409,8 +458,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
         uint32_t acc = 0, accphase = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-            BsTile tc;
-            bs_tile_coord<BN>(p, tile, tc);
+            const BsTileX tc = load_tile(p, tile);
             ok = mbar_wait(&acc_full[acc], accphase, p.err, kErrTimeoutAccFull, true);
             if (!__all_sync(0xffffffffu, ok)) {
                 ok = false;
@@ -418,25 +466,42 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
             }
             tc_fence_after();
             const uint32_t m = tc.mt * 128 + r;
-            const uint64_t row0 = p.offset[tc.g] + tc.n0;
+            const uint64_t row0 = tc.row0;
             const uint32_t dbase = tmem + lane_addr + acc * C::kAccCols;
-            // scale block of the down GEMM for this token tile and 128-K stage (= mt)
-            uint8_t* h_atom = MODE == kGateUp
-                                  ? p.sfh_atoms + (((uint64_t)p.tile_off[tc.g] / p.m_tiles + tc.n0 / BN) *
-                                                       p.m_tiles + tc.mt) * 1024
-                                  : nullptr;
-            for (uint32_t c0 = 0; c0 < tc.nn; c0 += 32) {
-                uint32_t d[32];
-                MOE_TMEM_LD32(dbase + c0, d);
-                if (MODE == kGateUp) {
-                    uint32_t u[32];
-                    MOE_TMEM_LD32(dbase + BN + c0, u);
+            // scale block of the down GEMM for this token tile and 128-K stage
+            // (= mt), in the down GEMM's layout (stacked for 64-token tiles)
+            constexpr uint32_t kDnAtom = BN == 64 ? 512 : 1024, kDnLo = BN == 64 ? 8 : 512;
+            uint8_t* h_atom =
+                MODE == kGateUp ? p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * kDnAtom : nullptr;
+            // column of the hi / lo accumulator of output column c, per projection
+            constexpr uint32_t kLoOff = C::kStackN ? BN : 0;       // stacked: lo half follows hi
+            constexpr uint32_t kProjOff = C::kStackN ? 2 * BN : BN;
+            for (uint32_t c0 = 0; c0 < tc.nn; c0 += 16) {
+                float v0[16], v1[16];
+                {
+                    uint32_t a[16], b[16];
+                    MOE_TMEM_LD16(dbase + c0, a);
+                    if (C::kStackN) MOE_TMEM_LD16(dbase + kLoOff + c0, b);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
+                    for (int i = 0; i < 16; ++i) {
+                        v0[i] = __uint_as_float(a[i]) + (C::kStackN ? __uint_as_float(b[i]) : 0.f);
+                    }
+                }
+                if (MODE == kGateUp) {
+                    uint32_t a[16], b[16];
+                    MOE_TMEM_LD16(dbase + kProjOff + c0, a);
+                    if (C::kStackN) MOE_TMEM_LD16(dbase + kProjOff + kLoOff + c0, b);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        v1[i] = __uint_as_float(a[i]) + (C::kStackN ? __uint_as_float(b[i]) : 0.f);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
                         const uint32_t col = c0 + i;
                         if (col >= tc.nn) continue;  // uniform across the warp
-                        const float hv = silu_fast(__uint_as_float(d[i])) * __uint_as_float(u[i]);
+                        const float hv = silu_fast(v0[i]) * v1[i];
                         uint8_t hi, lo, sh, sl;
                         split_e4m3_warp(hv, hi, lo, sh, sl);
                         const uint64_t prow = row0 + col;
@@ -445,16 +510,13 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
                         if (lane == 0) {
                             const uint32_t pos = (col % 32) * 16 + (col / 32) * 4 + quarter;
                             h_atom[pos] = sh;
-                            h_atom[512 + pos] = sl;
+                            h_atom[pos + kDnLo] = sl;
                         }
                     }
-                } else {
-                    tmem_wait_ld();
-                    if (m < p.m_valid) {
+                } else if (m < p.m_valid) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            if (c0 + i < tc.nn) p.y_out[(row0 + c0 + i) * p.y_stride + m] = __uint_as_float(d[i]);
-                        }
+                    for (int i = 0; i < 16; ++i) {
+                        if (c0 + i < tc.nn) p.y_out[(row0 + c0 + i) * p.y_stride + m] = v0[i];
                     }
                 }
             }

@@ -37,12 +37,23 @@ struct GemmParams {
 
 enum GemmMode : int { kGateUp = 0, kDown = 1 };
 
+// One grouped-GEMM tile, precomputed after routing so the GEMM roles read
+// their work with a single 16-byte load.
+struct TileEntry {
+    uint32_t group;       // expert slot
+    uint32_t mt;          // weight row tile
+    uint32_t row0;        // first permuted row of the tile's tokens
+    uint32_t nn_ntile;    // tokens in the tile (low 8 bits) | token-tile index << 8
+};
+
 // Block-scaled grouped GEMM parameters (gemm_bs.cu).
 struct BsParams {
     uint32_t groups;
     const uint32_t* count;
     const uint32_t* offset;
     const uint32_t* tile_off;
+    const TileEntry* tiles;   // [tile_off[groups]] entries
+    const uint8_t* a_codes;   // weight blocks (8 KB each) in the order of the A tensor map
     uint32_t rows_pad;        // weight rows per matrix, padded to 128
     uint32_t m_tiles;         // rows_pad / 128
     uint32_t k_tiles;         // K (padded to 128) / 128
@@ -104,6 +115,9 @@ cudaError_t launch_gather_bs(const uint8_t* q_hi, const uint8_t* q_lo, const uin
                              uint32_t Kp, const uint32_t* row_token, uint32_t rows, const uint32_t* offset,
                              const uint32_t* tile_off, uint32_t groups, uint32_t m_tiles, uint32_t block_n,
                              uint8_t* x_hi, uint8_t* x_lo, uint8_t* sf_atoms, cudaStream_t st);
+cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, const uint32_t* tile_off,
+                               uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint32_t max_tiles,
+                               TileEntry* tiles, cudaStream_t st);
 cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tbh,
                            const CUtensorMap& tbl, const BsParams& p, int num_sms, cudaStream_t st);
 
