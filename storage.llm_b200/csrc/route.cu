@@ -18,91 +18,111 @@
 namespace moe_b200 {
 
 // ---------------------------------------------------------------------------
-// Router logits.  Block = 256 threads = 16 "pair slots" x 16 lanes; lane l of
-// a slot owns the reference's FMA chain l.  A block covers kRouterTok tokens
-// and 32 experts (2 per slot); x is staged in shared memory in chunks.
+// Router logits.  A block computes a 16-token x 16-expert tile: 256 threads =
+// 16 lane groups x 16 lanes, lane l of a group owning the reference's FMA
+// chain l (elements l, l+16, ...) for the group's 4 tokens x 4 experts (16
+// independent chains per thread).  Token and router rows are staged through
+// shared memory in 256-element chunks with cp.async, double-buffered.
 // ---------------------------------------------------------------------------
-constexpr int kRouterChunk = 480;  // elements of H staged per step (multiple of 16; 48 KB static limit)
-constexpr int kRouterWPad = 8;     // row padding (bf16) against bank conflicts
+constexpr int kRtTok = 16, kRtExp = 16;
+constexpr int kRtChunk = 256;               // elements per staged chunk (multiple of 16)
+constexpr int kRtStride = kRtChunk + 8;     // padded row (bf16) against bank conflicts
 
-template <int kRouterTok>
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+    const uint32_t d = smem_u32(dst);
+    const int n = valid ? 16 : 0;  // 0 source bytes -> zero fill
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
                                                             const uint16_t* __restrict__ w, uint32_t T,
                                                             uint32_t E, uint32_t H, float* __restrict__ logits) {
-    // x rows and the block's 32 router rows for one H chunk, staged with
-    // 16-byte loads; the FMA chains then read shared memory only.
-    __shared__ __align__(16) uint16_t xs[kRouterTok][kRouterChunk];
-    __shared__ __align__(16) uint16_t ws[32][kRouterChunk + kRouterWPad];
+    __shared__ __align__(16) uint16_t xs[2][kRtTok][kRtStride];
+    __shared__ __align__(16) uint16_t ws[2][kRtExp][kRtStride];
     const int l = threadIdx.x & 15;
-    const int slot = threadIdx.x >> 4;
-    const uint32_t t0 = blockIdx.x * kRouterTok;
-    const uint32_t eb = blockIdx.y * 32;
-    const uint32_t e0 = eb + slot * 2;
-    float acc[kRouterTok][2];
-#pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) acc[t][0] = acc[t][1] = 0.f;
+    const int grp = threadIdx.x >> 4;
+    const int gt = (grp >> 2) * 4, ge = (grp & 3) * 4;  // the group's first token / expert in the tile
+    const uint32_t t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp;
     const uint32_t main_end = H & ~15u;  // the 16-step main loop of the reference
-    for (uint32_t c0 = 0; c0 < main_end; c0 += kRouterChunk) {
-        const uint32_t clen = min((uint32_t)kRouterChunk, main_end - c0);
-        const uint32_t cv = clen / 8;  // 16-byte vectors per row (H % 8 == 0)
-        __syncthreads();
-        for (uint32_t i = threadIdx.x; i < kRouterTok * cv; i += blockDim.x) {
-            const uint32_t tt = i / cv, kk = (i % cv) * 8;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (t0 + tt < T) v = __ldg(reinterpret_cast<const uint4*>(x + (uint64_t)(t0 + tt) * H + c0 + kk));
-            *reinterpret_cast<uint4*>(&xs[tt][kk]) = v;
-        }
-        for (uint32_t i = threadIdx.x; i < 32 * cv; i += blockDim.x) {
-            const uint32_t er = i / cv, kk = (i % cv) * 8;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (eb + er < E) v = __ldg(reinterpret_cast<const uint4*>(w + (uint64_t)(eb + er) * H + c0 + kk));
-            *reinterpret_cast<uint4*>(&ws[er][kk]) = v;
-        }
-        __syncthreads();
-        const uint16_t* w0 = ws[slot * 2];
-        const uint16_t* w1 = ws[slot * 2 + 1];
-#pragma unroll 4
-        for (uint32_t i = l; i < clen; i += 16) {
-            const float a = bf16_bits_to_f32(w0[i]);
-            const float b = bf16_bits_to_f32(w1[i]);
-#pragma unroll
-            for (int t = 0; t < kRouterTok; ++t) {
-                const float xv = bf16_bits_to_f32(xs[t][i]);
-                acc[t][0] = __fmaf_rn(a, xv, acc[t][0]);
-                acc[t][1] = __fmaf_rn(b, xv, acc[t][1]);
+    const uint32_t nchunks = (main_end + kRtChunk - 1) / kRtChunk;
+
+    auto stage = [&](uint32_t c, int buf) {
+        const uint32_t c0 = c * kRtChunk;
+        const uint32_t clen = min((uint32_t)kRtChunk, main_end - c0);
+        const uint32_t vpr = clen / 8;  // 16-byte vectors per row
+        for (uint32_t i = threadIdx.x; i < 32 * vpr; i += blockDim.x) {
+            const uint32_t row = i / vpr, v = i % vpr;
+            if (row < kRtTok) {
+                const uint32_t t = t0 + row;
+                cp_async16(&xs[buf][row][v * 8], x + (uint64_t)min(t, T - 1) * H + c0 + v * 8, t < T);
+            } else {
+                const uint32_t e = e0 + row - kRtTok;
+                cp_async16(&ws[buf][row - kRtTok][v * 8], w + (uint64_t)min(e, E - 1) * H + c0 + v * 8, e < E);
             }
         }
+        cp_async_commit();
+    };
+
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+    if (nchunks > 0) stage(0, 0);
+    for (uint32_t c = 0; c < nchunks; ++c) {
+        const int buf = c & 1;
+        if (c + 1 < nchunks) {
+            stage(c + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const uint32_t clen = min((uint32_t)kRtChunk, main_end - c * kRtChunk);
+        for (uint32_t i = l; i < clen; i += 16) {
+            float xv[4], wv[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) xv[a] = bf16_bits_to_f32(xs[buf][gt + a][i]);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) wv[b] = bf16_bits_to_f32(ws[buf][ge + b][i]);
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = __fmaf_rn(wv[b], xv[a], acc[a][b]);
+        }
+        __syncthreads();
     }
     // lane sums b_l = s_l + s_{l+8}, then the ordered 8-term sum, then the
     // reference's 4-way and scalar tails (H % 16 != 0).
     const unsigned full = 0xffffffffu;
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) {
+    for (int a = 0; a < 4; ++a) {
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const float hi = __shfl_down_sync(full, acc[t][q], 8, 16);
-            float b = acc[t][q] + hi;  // valid on lanes 0..7
-            float s = __shfl_sync(full, b, 0, 16);
+        for (int b = 0; b < 4; ++b) {
+            const float hi = __shfl_down_sync(full, acc[a][b], 8, 16);
+            const float bl = acc[a][b] + hi;  // valid on lanes 0..7
+            float s = __shfl_sync(full, bl, 0, 16);
 #pragma unroll
-            for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __shfl_sync(full, b, j, 16));
-            if (l == 0) {
-                const uint32_t tt = t0 + t, e = e0 + q;
-                if (tt < T && e < E) {
-                    float out = 0.0f + s;
-                    const uint16_t* wr = w + (uint64_t)e * H;
-                    const uint16_t* xr = x + (uint64_t)tt * H;
-                    uint32_t i = main_end;
-                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                    for (; i + 3 < H; i += 4) {
-                        a0 = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), a0);
-                        a1 = __fmaf_rn(bf16_bits_to_f32(wr[i + 1]), bf16_bits_to_f32(xr[i + 1]), a1);
-                        a2 = __fmaf_rn(bf16_bits_to_f32(wr[i + 2]), bf16_bits_to_f32(xr[i + 2]), a2);
-                        a3 = __fmaf_rn(bf16_bits_to_f32(wr[i + 3]), bf16_bits_to_f32(xr[i + 3]), a3);
-                    }
-                    out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
-                    for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), out);
-                    logits[(uint64_t)tt * E + e] = out;
+            for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __shfl_sync(full, bl, j, 16));
+            const uint32_t tt = t0 + gt + a, e = e0 + ge + b;
+            if (l == 0 && tt < T && e < E) {
+                float out = 0.0f + s;
+                const uint16_t* wr = w + (uint64_t)e * H;
+                const uint16_t* xr = x + (uint64_t)tt * H;
+                uint32_t i = main_end;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                for (; i + 3 < H; i += 4) {
+                    a0 = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), a0);
+                    a1 = __fmaf_rn(bf16_bits_to_f32(wr[i + 1]), bf16_bits_to_f32(xr[i + 1]), a1);
+                    a2 = __fmaf_rn(bf16_bits_to_f32(wr[i + 2]), bf16_bits_to_f32(xr[i + 2]), a2);
+                    a3 = __fmaf_rn(bf16_bits_to_f32(wr[i + 3]), bf16_bits_to_f32(xr[i + 3]), a3);
                 }
+                out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
+                for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), out);
+                logits[(uint64_t)tt * E + e] = out;
             }
         }
     }
@@ -399,19 +419,8 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
                           int sigmoid, int norm_topk, float routed_scale, float* logits, int32_t* ids, float* wout,
                           float* scores, cudaStream_t st) {
     if (T == 0) return cudaSuccess;
-    // Tokens per block: the largest of 16/8/4/2/1 that still gives >= 2 blocks
-    // per SM, so decode-sized batches spread over the whole GPU.
-    const uint32_t eb = ceil_div(E, 32);
-    int tt = 16;
-    while (tt > 1 && ceil_div(T, tt) * eb < 296) tt >>= 1;
-    dim3 g1(ceil_div(T, tt), eb);
-    switch (tt) {
-        case 16: router_logits_kernel<16><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
-        case 8: router_logits_kernel<8><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
-        case 4: router_logits_kernel<4><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
-        case 2: router_logits_kernel<2><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
-        default: router_logits_kernel<1><<<g1, 256, 0, st>>>(x, w, T, E, H, logits); break;
-    }
+    dim3 g1(ceil_div(T, kRtTok), ceil_div(E, kRtExp));
+    router_logits_kernel<<<g1, 256, 0, st>>>(x, w, T, E, H, logits);
     router_topk_kernel<<<ceil_div(T, 8), 256, 0, st>>>(logits, T, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
                                                        scores);
     return cudaGetLastError();
