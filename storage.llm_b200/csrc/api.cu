@@ -106,10 +106,12 @@ struct moe_b200_engine {
     DevBuf xperm, hperm, yperm;
     DevBuf err_word;
     // block-scaled path: quantised activations and intermediate
-    DevBuf xq_hi, xq_lo, sx_hi, sx_lo, xb_hi, xb_lo, sfx_atoms, hb_hi, hb_lo, sfh_atoms, gu_tiles, dn_tiles;
-    CUtensorMap tmap_xhi{}, tmap_xlo{}, tmap_hhi{}, tmap_hlo{};
-    const void* bs_map_key[4] = {nullptr, nullptr, nullptr, nullptr};
-    uint64_t bs_map_dims[4][2] = {};
+    // (xq, sx, xb, hb hold a hi plane followed by a lo plane)
+    DevBuf xq, sx, xb, sfx_atoms, hb, sfh_atoms, gu_tiles, dn_tiles;
+    // 3-D maps over xb / hb: [0] 32-token box, [1] 128-token box
+    CUtensorMap tmap_xb[2]{}, tmap_hb[2]{};
+    const void* bs_map_key[2] = {nullptr, nullptr};
+    uint64_t bs_map_dims[2][2] = {};
     // host-call staging
     DevBuf hx, hy, hyf, hids, hw, hperm_out, tri;
     CUtensorMap tmap_x{}, tmap_h{};
@@ -178,6 +180,25 @@ int make_tmap2d(moe_b200_engine* eng, CUtensorMap* map, CUtensorMapDataType dtyp
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_err(err, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return 0;
+    }
+    return 1;
+}
+
+// 3-D map over [2][rows][cols] bytes (hi plane, lo plane) with a
+// {128, box_rows, 2} box and 128-byte swizzle: one copy brings both terms.
+int make_tmap_planes(moe_b200_engine* eng, CUtensorMap* map, void* base, uint64_t cols, uint64_t rows,
+                     uint32_t box_rows, char* err) {
+    if (!get_encoder(eng, err)) return 0;
+    const cuuint64_t dims[3] = {cols, rows, 2};
+    const cuuint64_t strides[2] = {cols, cols * rows};
+    const cuuint32_t box[3] = {128, box_rows, 2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = eng->encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_err(err, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
         return 0;
     }
     return 1;
@@ -252,9 +273,8 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
                       &eng->rank, &eng->pos_of, &eng->row_token, &eng->row_assign, &eng->g_count,
                       &eng->g_offset, &eng->g_gu_off, &eng->g_dn_off, &eng->xperm, &eng->hperm,
                       &eng->yperm, &eng->err_word, &eng->hx, &eng->hy, &eng->hyf, &eng->hids,
-                      &eng->hw, &eng->hperm_out, &eng->tri, &eng->xq_hi, &eng->xq_lo, &eng->sx_hi,
-                      &eng->sx_lo, &eng->xb_hi, &eng->xb_lo, &eng->sfx_atoms, &eng->hb_hi, &eng->hb_lo,
-                      &eng->sfh_atoms, &eng->gu_tiles, &eng->dn_tiles};
+                      &eng->hw, &eng->hperm_out, &eng->tri, &eng->xq, &eng->sx, &eng->xb,
+                      &eng->sfx_atoms, &eng->hb, &eng->sfh_atoms, &eng->gu_tiles, &eng->dn_tiles};
     for (DevBuf* b : bufs) b->release();
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
     delete eng;
@@ -368,13 +388,15 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
         const uint64_t mti = L->rp_i / 128, kth = L->kq / 128, mth = L->rp_h / 128, kti = L->iq / 128;
         for (int pj = 0; pj < 2; ++pj) {
             const uint64_t m = (uint64_t)slot * 2 + pj;
+            // scale blocks [slot][mt][kt][gate | up]: one bulk copy per stage brings both
             CK(launch_repack_bs(dsrc[pj], intermediate, hidden, L->rp_i, L->kq,
                                 L->bs_gu_codes.as<uint8_t>() + m * L->rp_i * (L->kq / 2),
-                                L->bs_gu_sfa.as<uint8_t>() + m * mti * kth * 512, 0));
+                                L->bs_gu_sfa.as<uint8_t>() + (uint64_t)slot * mti * kth * 1024 + pj * 512, 1024,
+                                0));
         }
         CK(launch_repack_bs(dsrc[2], hidden, intermediate, L->rp_h, L->iq,
                             L->bs_dn_codes.as<uint8_t>() + (uint64_t)slot * L->rp_h * (L->iq / 2),
-                            L->bs_dn_sfa.as<uint8_t>() + (uint64_t)slot * mth * kti * 512, 0));
+                            L->bs_dn_sfa.as<uint8_t>() + (uint64_t)slot * mth * kti * 512, 512, 0));
     }
     CK(cudaDeviceSynchronize());
     L->present[slot] = 1;
@@ -438,36 +460,32 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     CK(eng->g_dn_off.reserve((size_t)(G + 1) * 4));
     const bool bs = cfg->gemm_path == MOE_B200_GEMM_BLOCKSCALED;
     const uint32_t Kq = L->kq, Iq = L->iq;  // K padded to 128 for the block-scaled path
-    // tokens per GEMM tile: 64 when groups are small on average (decode), else 128
-    const uint32_t block_n = (bs && (uint64_t)P <= 96ull * G) ? 64u : kBlockN;
+    // tokens per GEMM tile: 32 when groups are small on average (decode), else 128
+    const uint32_t block_n = (bs && (uint64_t)P <= 48ull * G) ? 32u : kBlockN;
     CK(eng->yperm.reserve((size_t)P * H * 4));
     if (bs) {
-        CK(eng->xq_hi.reserve((size_t)T * Kq));
-        CK(eng->xq_lo.reserve((size_t)T * Kq));
-        CK(eng->sx_hi.reserve((size_t)T * (Kq / 32)));
-        CK(eng->sx_lo.reserve((size_t)T * (Kq / 32)));
-        CK(eng->xb_hi.reserve((size_t)rows_cap * Kq));
-        CK(eng->xb_lo.reserve((size_t)rows_cap * Kq));
+        CK(eng->xq.reserve((size_t)2 * T * Kq));
+        CK(eng->sx.reserve((size_t)2 * T * (Kq / 32)));
+        CK(eng->xb.reserve((size_t)2 * rows_cap * Kq));
+        CK(eng->hb.reserve((size_t)2 * rows_cap * Iq));
         const size_t token_tiles = (size_t)P / block_n + G;  // upper bound of sum_g ceil(count_g / block_n)
         CK(eng->sfx_atoms.reserve(token_tiles * (Kq / 128) * 1024));
-        CK(eng->hb_hi.reserve((size_t)rows_cap * Iq));
-        CK(eng->hb_lo.reserve((size_t)rows_cap * Iq));
         CK(eng->sfh_atoms.reserve(token_tiles * (Iq / 128) * 1024));
         CK(eng->gu_tiles.reserve(token_tiles * (L->rp_i / 128) * sizeof(TileEntry)));
         CK(eng->dn_tiles.reserve(token_tiles * (L->rp_h / 128) * sizeof(TileEntry)));
-        // E4M3 activation / intermediate rows: 128-byte x 32-row boxes
+        // the planes' row count is fixed by the buffer, so the maps only change
+        // when a buffer is reallocated or the geometry changes
         struct MapSpec {
-            CUtensorMap* map;
+            CUtensorMap* maps;
             DevBuf* buf;
             uint32_t cols;
-        } specs[4] = {{&eng->tmap_xhi, &eng->xb_hi, Kq}, {&eng->tmap_xlo, &eng->xb_lo, Kq},
-                      {&eng->tmap_hhi, &eng->hb_hi, Iq}, {&eng->tmap_hlo, &eng->hb_lo, Iq}};
-        for (int i = 0; i < 4; ++i) {
-            const uint64_t rows = specs[i].buf->bytes / specs[i].cols;
+        } specs[2] = {{eng->tmap_xb, &eng->xb, Kq}, {eng->tmap_hb, &eng->hb, Iq}};
+        for (int i = 0; i < 2; ++i) {
+            const uint64_t rows = specs[i].buf->bytes / (2ull * specs[i].cols);
             if (eng->bs_map_key[i] != specs[i].buf->ptr || eng->bs_map_dims[i][0] != specs[i].cols ||
                 eng->bs_map_dims[i][1] != rows) {
-                if (!make_tmap2d(eng, specs[i].map, CU_TENSOR_MAP_DATA_TYPE_UINT8, specs[i].buf->ptr, specs[i].cols,
-                                 rows, specs[i].cols, 128, 32, err)) {
+                if (!make_tmap_planes(eng, &specs[i].maps[0], specs[i].buf->ptr, specs[i].cols, rows, 32, err) ||
+                    !make_tmap_planes(eng, &specs[i].maps[1], specs[i].buf->ptr, specs[i].cols, rows, 128, err)) {
                     return 0;
                 }
                 eng->bs_map_key[i] = specs[i].buf->ptr;
@@ -536,12 +554,11 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
                               token_tiles * (L->rp_h / 128), eng->dn_tiles.as<TileEntry>(), st));
         launches += 2;
         // activations -> exact hi/lo E4M3 terms per token, then per permuted row
-        CK(launch_quantize_rows(x, T, H, Kq, eng->xq_hi.as<uint8_t>(), eng->xq_lo.as<uint8_t>(),
-                                eng->sx_hi.as<uint8_t>(), eng->sx_lo.as<uint8_t>(), st));
-        CK(launch_gather_bs(eng->xq_hi.as<uint8_t>(), eng->xq_lo.as<uint8_t>(), eng->sx_hi.as<uint8_t>(),
-                            eng->sx_lo.as<uint8_t>(), Kq, eng->row_token.as<uint32_t>(), P, gi.offset,
-                            gi.gu_tile_off, G, gi.gu_row_tiles, block_n, eng->xb_hi.as<uint8_t>(),
-                            eng->xb_lo.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(), st));
+        const uint64_t xb_rows = eng->xb.bytes / (2ull * Kq), hb_rows = eng->hb.bytes / (2ull * Iq);
+        CK(launch_quantize_rows(x, T, H, Kq, eng->xq.as<uint8_t>(), eng->sx.as<uint8_t>(), st));
+        CK(launch_gather_bs(eng->xq.as<uint8_t>(), eng->sx.as<uint8_t>(), T, Kq, eng->row_token.as<uint32_t>(), P,
+                            (uint32_t)xb_rows, gi.offset, gi.gu_tile_off, G, L->rp_i / 128, block_n,
+                            eng->xb.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(), st));
         launches += 2;
         mark(3);
         BsParams bp{};
@@ -558,13 +575,13 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         bp.sfa = L->bs_gu_sfa.as<uint8_t>();
         bp.a_codes = L->bs_gu_codes.as<uint8_t>();
         bp.sfb_atoms = eng->sfx_atoms.as<uint8_t>();
-        bp.h_hi = eng->hb_hi.as<uint8_t>();
-        bp.h_lo = eng->hb_lo.as<uint8_t>();
+        bp.h_out = eng->hb.as<uint8_t>();
+        bp.h_plane = hb_rows * Iq;
         bp.h_stride = Iq;
         bp.sfh_atoms = eng->sfh_atoms.as<uint8_t>();
         bp.m_valid = Iq;
-        CK(launch_gemm_bs(kGateUp, (int)block_n, L->tmap_gu_codes, eng->tmap_xhi, eng->tmap_xlo, bp, eng->num_sms,
-                          st));
+        const int bi = block_n == 32 ? 0 : 1;
+        CK(launch_gemm_bs(kGateUp, (int)block_n, L->tmap_gu_codes, eng->tmap_xb[bi], bp, eng->num_sms, st));
         launches += 1;
         mark(4);
         // down: K = I (padded Iq), M = H rows (padded rp_h), output fp32 rows
@@ -579,7 +596,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         bp.y_out = eng->yperm.as<float>();
         bp.y_stride = H;
         bp.m_valid = H;
-        CK(launch_gemm_bs(kDown, (int)block_n, L->tmap_dn_codes, eng->tmap_hhi, eng->tmap_hlo, bp, eng->num_sms, st));
+        CK(launch_gemm_bs(kDown, (int)block_n, L->tmap_dn_codes, eng->tmap_hb[bi], bp, eng->num_sms, st));
         launches += 1;
         mark(5);
     } else {

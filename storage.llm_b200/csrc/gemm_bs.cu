@@ -2,19 +2,27 @@
 // weights as they are stored -- E2M1 codes plus one E8M0 scale per 32 K --
 // so no SM instruction is spent decoding weights.
 //
-//   A  E2M1 weight codes, packed two per byte in HBM as contiguous 8 KB
-//      blocks of 128 rows x 128 K, TMA'd with the 16U4_ALIGN16B type (each 16
-//      codes land in 16 bytes of shared memory, the operand form
-//      kind::mxf8f6f4 reads).  (Prefetching upcoming blocks into L2 was
-//      measured and lost time: it competes with the demand loads.);
-//   SFA the rows' E8M0 scales, one 512-byte block per 128 x 128 tile laid out
-//      as tcgen05.cp.32x128b.warpx4 expects (row r, K block j at byte
-//      (r%32)*16 + (r/32)*4 + j), copied to TMEM each stage;
-//   B  activations as two E4M3 terms, hi and lo, each with its own E8M0
-//      scale per 32 K (SFB).  A bf16 value has 8 significant bits and splits
-//      exactly into hi (4 bits) + lo (4 bits), so W.x = W.x_hi + W.x_lo is
-//      the same product the bf16 path computes;
-//   D  fp32 in TMEM: per K step, MMA(A, B_hi) then MMA(A, B_lo) accumulate.
+//   A   E2M1 weight codes, packed two per byte in HBM as contiguous 8 KB
+//       blocks of 128 rows x 128 K, TMA'd with the 16U4_ALIGN16B type (each
+//       16 codes land in 16 bytes of shared memory, the operand form
+//       kind::mxf8f6f4 reads);
+//   SFA the rows' E8M0 scales, one 512-byte block per 128 x 128 tile in the
+//       layout tcgen05.cp.32x128b.warpx4 expects (row r, K block j at byte
+//       (r%32)*16 + (r/32)*4 + j); the gate and up blocks of a tile are
+//       adjacent so one bulk copy brings both;
+//   B   activations as two E4M3 terms, hi and lo, each with an E8M0 scale per
+//       32 K (SFB).  A bf16 value has 8 significant bits and splits exactly
+//       into hi (4 bits) + lo (4 bits), so W.x = W.x_hi + W.x_lo is the product
+//       the bf16 path computes.  The hi and lo planes sit in one allocation
+//       and one 3-D TMA box brings both;
+//   D   fp32 in TMEM.
+//
+// Two tile shapes:
+//   32-token tiles (decode-sized groups): B rows 0-31 hi, 32-63 lo, one
+//     MMA of N = 64 per K step, so the A tile is read from shared memory once;
+//     the accumulator halves are summed in the epilogue;
+//   128-token tiles (prefill): the hi and lo MMAs accumulate into the same
+//     columns (N up to 128 each).
 //
 // kGateUp: gate and up tiles of the same 128 intermediate rows share B; the
 //          epilogue computes h = SiLU(gate) * up and writes it already split
@@ -22,11 +30,11 @@
 //          block of the down GEMM), so the down GEMM reads it directly.
 // kDown:   the epilogue writes fp32 expert outputs for the combine.
 //
-// Warp roles (192 threads, one CTA per SM, persistent over all tiles):
-//   warp 0     producer: TMA of the A and B boxes and bulk copies of the
-//              weight and activation scale blocks -- all asynchronous, so a
-//              stage costs the producer no memory round trip
-//   warp 1     TMEM owner, scale-factor copies and MMA issue
+// Warp roles (192 threads, one CTA per SM, persistent over a precomputed tile
+// table):
+//   warp 0     producer: per stage one bulk copy of the weight scales, one of
+//              the activation scales, the A boxes, and one B box
+//   warp 1     TMEM owner, scale-factor copies (tcgen05.cp) and MMA issue
 //   warps 2-5  epilogue, one TMEM lane quarter each
 // All waits are bounded and report through p.err.
 #include <cuda_fp8.h>
@@ -38,28 +46,36 @@ namespace moe_b200 {
 
 template <int MODE, int BN>
 struct BsCfg {
-    // The down GEMM's 64-token tiles stack the hi and lo terms along N in one
-    // MMA (B rows 0-63 hi, 64-127 lo), reading the A tile once per K step.
-    // Elsewhere the hi and lo MMAs accumulate into the same columns, which
-    // keeps two gate+up accumulators in TMEM so the epilogue overlaps the next
-    // tile.
-    static constexpr bool kStackN = MODE == kDown && BN == 64;
+    static_assert(BN == 32 || BN == 128, "tile width");
+    static constexpr bool kStackN = BN == 32;
     static constexpr int kNA = MODE == kGateUp ? 2 : 1;       // A operands per stage
     static constexpr int kABytes = 128 * 128;                 // smem bytes per A box
     static constexpr int kATx = 128 * 128 / 2;                // packed bytes the A box moves
     static constexpr int kBBytes = BN * 128;                  // smem bytes per B term (hi or lo)
-    static constexpr int kSF = 512;
+    static constexpr int kSFA = kNA * 512;                    // weight scale bytes per stage
     static constexpr int kSFB = kStackN ? 512 : 1024;         // activation scale bytes per stage
-    static constexpr int kSFStage = kNA * kSF + kSFB;         // scale bytes per stage
-    static constexpr int kStageBytes = kNA * kABytes + 2 * kBBytes + kNA * kSF + kSFB;
-    static constexpr int kStages = (200 * 1024) / kStageBytes;
+    static constexpr int kSFStage = kSFA + kSFB;
+    static constexpr int kStageBytes = kNA * kABytes + 2 * kBBytes + kSFStage;
+    static constexpr int kStages = (210 * 1024) / kStageBytes;
     static constexpr int kAccCols = kNA * (kStackN ? 2 * BN : BN);
     static constexpr int kAccs = 256 / kAccCols >= 2 ? 2 : 1;
-    static constexpr int kSFCols = kNA * 4 + kSFB / 128;      // TMEM columns of scale factors per stage
+    static constexpr int kSFCols = kSFStage / 128;            // TMEM columns of scale factors per stage
     static constexpr int kSmem = kStages * kStageBytes + 2048 /*two 1024 alignments*/ + 512 /*barriers*/;
     static_assert(kStages >= 3, "pipeline too shallow");
     static_assert(256 + kStages * kSFCols <= 512, "TMEM budget");
+    static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
+
+// Byte offsets of a token row's hi and lo scale words inside a stage's
+// activation scale block (the tcgen05.cp layout over the B rows).
+template <int BN>
+__device__ __forceinline__ uint32_t sfb_pos_hi(uint32_t rr) {
+    return BN == 32 ? rr * 16 : (rr % 32) * 16 + (rr / 32) * 4;
+}
+template <int BN>
+__device__ __forceinline__ uint32_t sfb_pos_lo(uint32_t rr) {
+    return BN == 32 ? rr * 16 + 4 : 512 + (rr % 32) * 16 + (rr / 32) * 4;
+}
 
 __device__ __forceinline__ float pow2f(int e) {
     // exact 2^e for e in [-127, 127]
@@ -100,14 +116,14 @@ __device__ __forceinline__ void split_e4m3_warp(float v, uint8_t& hi, uint8_t& l
 
 // ---------------------------------------------------------------------------
 // Activation quantisation: one warp per (token, 32-element block).
-//   q_hi/q_lo [T][Kp] E4M3 bytes, s_hi/s_lo [T][Kp/32] E8M0 bytes.
+//   q [2][T][Kp] E4M3 bytes (hi plane, lo plane), s [2][T][Kp/32] E8M0 bytes.
 // ---------------------------------------------------------------------------
 __global__ void quantize_rows_kernel(const uint16_t* __restrict__ x, uint32_t T, uint32_t H, uint32_t Kp,
-                                     uint8_t* __restrict__ q_hi, uint8_t* __restrict__ q_lo,
-                                     uint8_t* __restrict__ s_hi, uint8_t* __restrict__ s_lo) {
+                                     uint8_t* __restrict__ q, uint8_t* __restrict__ sc) {
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t nblk = Kp / 32;
     const uint64_t total = (uint64_t)T * nblk;
+    const uint64_t qplane = (uint64_t)T * Kp, splane = (uint64_t)T * nblk;
     const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     for (uint64_t wb = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wb < total; wb += warps) {
         const uint32_t t = (uint32_t)(wb / nblk), b = (uint32_t)(wb % nblk);
@@ -115,40 +131,38 @@ __global__ void quantize_rows_kernel(const uint16_t* __restrict__ x, uint32_t T,
         const float v = k < H ? bf16_bits_to_f32(x[(uint64_t)t * H + k]) : 0.f;
         uint8_t hi, lo, sh, sl;
         split_e4m3_warp(v, hi, lo, sh, sl);
-        q_hi[(uint64_t)t * Kp + k] = hi;
-        q_lo[(uint64_t)t * Kp + k] = lo;
+        q[(uint64_t)t * Kp + k] = hi;
+        q[qplane + (uint64_t)t * Kp + k] = lo;
         if (lane == 0) {
-            s_hi[(uint64_t)t * nblk + b] = sh;
-            s_lo[(uint64_t)t * nblk + b] = sl;
+            sc[(uint64_t)t * nblk + b] = sh;
+            sc[splane + (uint64_t)t * nblk + b] = sl;
         }
     }
 }
 
 // Permuted rows for the block-scaled GEMM: the E4M3 bytes of each row's token
-// and its scale bytes, the latter written straight into the scale blocks the
-// GEMM's producer bulk-copies: one 1024-byte block per (token tile, 128-K
-// stage) holding the hi block then the lo block, row r of the tile at byte
-// (r%32)*16 + (r/32)*4 + j for K block j -- the tcgen05.cp.32x128b layout.
-// Token tile t of group g is tile_off[g]/m_tiles + (row - offset[g]) / BN.
-__global__ void gather_bs_kernel(const uint8_t* __restrict__ q_hi, const uint8_t* __restrict__ q_lo,
-                                 const uint8_t* __restrict__ s_hi, const uint8_t* __restrict__ s_lo, uint32_t Kp,
-                                 const uint32_t* __restrict__ row_token, uint32_t rows,
-                                 const uint32_t* __restrict__ offset, const uint32_t* __restrict__ tile_off,
-                                 uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* __restrict__ x_hi,
-                                 uint8_t* __restrict__ x_lo, uint8_t* __restrict__ sf_atoms) {
-    const uint32_t atom_bytes = 1024, lo_off = 512;  // hi block, then lo block
+// (both planes) and its scale words, the latter written straight into the
+// blocks the GEMM's producer bulk-copies: one block per (token tile, 128-K
+// stage) in the layout of sfb_pos_hi / sfb_pos_lo.  Token tile t of group g
+// is tile_off[g] / m_tiles + (row - offset[g]) / block_n.
+template <int BN>
+__global__ void gather_bs_kernel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sc, uint32_t T,
+                                 uint32_t Kp, const uint32_t* __restrict__ row_token, uint32_t rows,
+                                 uint32_t rows_cap, const uint32_t* __restrict__ offset,
+                                 const uint32_t* __restrict__ tile_off, uint32_t groups, uint32_t m_tiles,
+                                 uint8_t* __restrict__ xb, uint8_t* __restrict__ sf_atoms) {
+    constexpr uint32_t kAtom = BN == 32 ? 512 : 1024;
     const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t nv = Kp / 16, nkt = Kp / 128;
+    const uint64_t qplane = (uint64_t)T * Kp, xplane = (uint64_t)rows_cap * Kp;
+    const uint64_t splane = (uint64_t)T * (Kp / 32);
     for (uint32_t r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
         const uint32_t t = row_token[r];
-        const uint4* sh = reinterpret_cast<const uint4*>(q_hi + (uint64_t)t * Kp);
-        const uint4* sl = reinterpret_cast<const uint4*>(q_lo + (uint64_t)t * Kp);
-        uint4* dh = reinterpret_cast<uint4*>(x_hi + (uint64_t)r * Kp);
-        uint4* dl = reinterpret_cast<uint4*>(x_lo + (uint64_t)r * Kp);
-        for (uint32_t v = lane; v < nv; v += 32) {
-            dh[v] = __ldg(sh + v);
-            dl[v] = __ldg(sl + v);
+        for (int pl = 0; pl < 2; ++pl) {
+            const uint4* src = reinterpret_cast<const uint4*>(q + pl * qplane + (uint64_t)t * Kp);
+            uint4* dst = reinterpret_cast<uint4*>(xb + pl * xplane + (uint64_t)r * Kp);
+            for (uint32_t v = lane; v < nv; v += 32) dst[v] = __ldg(src + v);
         }
         uint32_t lo = 0, hi = groups;  // group owning row r
         while (hi - lo > 1) {
@@ -157,15 +171,14 @@ __global__ void gather_bs_kernel(const uint8_t* __restrict__ q_hi, const uint8_t
             else hi = mid;
         }
         const uint32_t n = r - offset[lo];
-        const uint64_t tile = tile_off[lo] / m_tiles + n / block_n;
-        const uint32_t rr = n % block_n;
-        const uint32_t pos = (rr % 32) * 16 + (rr / 32) * 4;
-        const uint32_t* wh = reinterpret_cast<const uint32_t*>(s_hi + (uint64_t)t * (Kp / 32));
-        const uint32_t* wl = reinterpret_cast<const uint32_t*>(s_lo + (uint64_t)t * (Kp / 32));
+        const uint64_t tile = tile_off[lo] / m_tiles + n / BN;
+        const uint32_t rr = n % BN;
+        const uint32_t* wh = reinterpret_cast<const uint32_t*>(sc + (uint64_t)t * (Kp / 32));
+        const uint32_t* wl = reinterpret_cast<const uint32_t*>(sc + splane + (uint64_t)t * (Kp / 32));
         for (uint32_t kt = lane; kt < nkt; kt += 32) {
-            uint8_t* atom = sf_atoms + (tile * nkt + kt) * atom_bytes;
-            *reinterpret_cast<uint32_t*>(atom + pos) = __ldg(wh + kt);
-            *reinterpret_cast<uint32_t*>(atom + lo_off + pos) = __ldg(wl + kt);
+            uint8_t* atom = sf_atoms + (tile * nkt + kt) * kAtom;
+            *reinterpret_cast<uint32_t*>(atom + sfb_pos_hi<BN>(rr)) = __ldg(wh + kt);
+            *reinterpret_cast<uint32_t*>(atom + sfb_pos_lo<BN>(rr)) = __ldg(wl + kt);
         }
     }
 }
@@ -175,10 +188,13 @@ __global__ void gather_bs_kernel(const uint8_t* __restrict__ q_hi, const uint8_t
 //   codes: blocks [row_tile][k_tile] of 128 rows x 128 K, 8 KB each, row r of
 //          a block at r*64 bytes, element 2j in the low nibble of byte j
 //          (zero past `rows` / `cols`);
-//   sfa:   [row_tile][k_tile][512] scale blocks in the tcgen05.cp layout.
+//   sfa:   one 512-byte scale block per (row_tile, k_tile) in the tcgen05.cp
+//          layout, consecutive blocks `sf_stride` bytes apart (the gate and up
+//          blocks of a tile are interleaved: stride 1024, up at +512).
 // ---------------------------------------------------------------------------
 __global__ void repack_bs_kernel(const uint8_t* __restrict__ gguf, uint32_t rows, uint32_t cols, uint32_t rows_pad,
-                                 uint32_t Kp, uint8_t* __restrict__ codes, uint8_t* __restrict__ sfa) {
+                                 uint32_t Kp, uint8_t* __restrict__ codes, uint8_t* __restrict__ sfa,
+                                 uint32_t sf_stride) {
     const uint32_t gguf_row_bytes = ceil_div(cols, 32) * 17;
     const uint32_t kt_n = Kp / 128;
     const uint64_t nbytes = (uint64_t)rows_pad * (Kp / 2);
@@ -186,7 +202,6 @@ __global__ void repack_bs_kernel(const uint8_t* __restrict__ gguf, uint32_t rows
     for (uint64_t idx = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; idx < nbytes + nsf;
          idx += (uint64_t)gridDim.x * blockDim.x) {
         if (idx < nbytes) {
-            // idx walks the output: block (mt, kt), row rr, byte jb
             const uint64_t blk = idx / 8192;
             const uint32_t within = (uint32_t)(idx % 8192);
             const uint32_t mt = (uint32_t)(blk / kt_n), kt = (uint32_t)(blk % kt_n);
@@ -210,51 +225,51 @@ __global__ void repack_bs_kernel(const uint8_t* __restrict__ gguf, uint32_t rows
             const uint64_t q = idx - nbytes;
             const uint32_t r = (uint32_t)(q / (Kp / 32));
             const uint32_t blk = (uint32_t)(q % (Kp / 32));
-            uint8_t s = 0;
-            if (r < rows && blk * 32 < cols) s = gguf[(uint64_t)r * gguf_row_bytes + blk * 17];
+            uint8_t sv = 0;
+            if (r < rows && blk * 32 < cols) sv = gguf[(uint64_t)r * gguf_row_bytes + blk * 17];
             const uint32_t mt = r / 128, rr = r % 128, kt = blk / 4, j = blk % 4;
-            sfa[((uint64_t)mt * kt_n + kt) * 512 + (rr % 32) * 16 + (rr / 32) * 4 + j] = s;
+            sfa[((uint64_t)mt * kt_n + kt) * sf_stride + (rr % 32) * 16 + (rr / 32) * 4 + j] = sv;
         }
     }
 }
 
 cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, uint32_t rows_pad, uint32_t Kp,
-                             uint8_t* codes, uint8_t* sfa, cudaStream_t st) {
+                             uint8_t* codes, uint8_t* sfa, uint32_t sf_stride, cudaStream_t st) {
     const uint64_t work = (uint64_t)rows_pad * (Kp / 2) + (uint64_t)rows_pad * (Kp / 32);
     const uint64_t blocks = (work + 255) / 256;
     repack_bs_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, st>>>(gguf, rows, cols, rows_pad,
-                                                                                       Kp, codes, sfa);
+                                                                                       Kp, codes, sfa, sf_stride);
     return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_rows(const uint16_t* x, uint32_t T, uint32_t H, uint32_t Kp, uint8_t* q_hi,
-                                 uint8_t* q_lo, uint8_t* s_hi, uint8_t* s_lo, cudaStream_t st) {
+cudaError_t launch_quantize_rows(const uint16_t* x, uint32_t T, uint32_t H, uint32_t Kp, uint8_t* q, uint8_t* sc,
+                                 cudaStream_t st) {
     if (T == 0) return cudaSuccess;
     const uint64_t warps = (uint64_t)T * (Kp / 32);
     const uint64_t blocks = (warps + 7) / 8;
-    quantize_rows_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, st>>>(x, T, H, Kp, q_hi, q_lo,
-                                                                                           s_hi, s_lo);
+    quantize_rows_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, st>>>(x, T, H, Kp, q, sc);
     return cudaGetLastError();
 }
 
-cudaError_t launch_gather_bs(const uint8_t* q_hi, const uint8_t* q_lo, const uint8_t* s_hi, const uint8_t* s_lo,
-                             uint32_t Kp, const uint32_t* row_token, uint32_t rows, const uint32_t* offset,
-                             const uint32_t* tile_off, uint32_t groups, uint32_t m_tiles, uint32_t block_n,
-                             uint8_t* x_hi, uint8_t* x_lo, uint8_t* sf_atoms, cudaStream_t st) {
+cudaError_t launch_gather_bs(const uint8_t* q, const uint8_t* sc, uint32_t T, uint32_t Kp, const uint32_t* row_token,
+                             uint32_t rows, uint32_t rows_cap, const uint32_t* offset, const uint32_t* tile_off,
+                             uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* xb, uint8_t* sf_atoms,
+                             cudaStream_t st) {
     if (rows == 0) return cudaSuccess;
     const uint32_t blocks = min(ceil_div(rows, 8), 148u * 8u);
-    gather_bs_kernel<<<blocks, 256, 0, st>>>(q_hi, q_lo, s_hi, s_lo, Kp, row_token, rows, offset, tile_off, groups,
-                                             m_tiles, block_n, x_hi, x_lo, sf_atoms);
+    if (block_n == 32) {
+        gather_bs_kernel<32><<<blocks, 256, 0, st>>>(q, sc, T, Kp, row_token, rows, rows_cap, offset, tile_off,
+                                                     groups, m_tiles, xb, sf_atoms);
+    } else {
+        gather_bs_kernel<128><<<blocks, 256, 0, st>>>(q, sc, T, Kp, row_token, rows, rows_cap, offset, tile_off,
+                                                      groups, m_tiles, xb, sf_atoms);
+    }
     return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
 // The grouped GEMM
 // ---------------------------------------------------------------------------
-struct BsTile {
-    uint32_t g, mt, n0, nn;
-};
-
 struct BsTileX {
     uint32_t g, mt, row0, nn, ntile;
 };
@@ -303,17 +318,16 @@ __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f 
 
 template <int MODE, int BN>
 __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                                                         const __grid_constant__ CUtensorMap tmap_b_hi,
-                                                         const __grid_constant__ CUtensorMap tmap_b_lo,
+                                                         const __grid_constant__ CUtensorMap tmap_b,
                                                          const BsParams p) {
     using C = BsCfg<MODE, BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    // scale-factor blocks first (small), then the 1024-aligned operand tiles
+    // scale blocks first (small), then the 1024-aligned operand tiles
     uint8_t* sf_base = smem;                                                  // [stages][kSFStage]
     uint8_t* a_base = smem + C::kStages * C::kSFStage;                        // [stages][kNA][16 KB]
     a_base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(a_base) + 1023) & ~uintptr_t(1023));
-    uint8_t* b_base = a_base + C::kStages * C::kNA * C::kABytes;              // [stages][2][kBBytes]
+    uint8_t* b_base = a_base + C::kStages * C::kNA * C::kABytes;              // [stages][hi, lo][kBBytes]
     uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + C::kStages * 2 * C::kBBytes);
     uint64_t* load_full = bars;
     uint64_t* load_empty = load_full + C::kStages;
@@ -335,8 +349,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
     }
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmap_a);
-        prefetch_tmap(&tmap_b_hi);
-        prefetch_tmap(&tmap_b_lo);
+        prefetch_tmap(&tmap_b);
     }
     if (warp == 1) {
         tmem_alloc(tmem_holder, 512);
@@ -351,46 +364,34 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
-        uint32_t stage = 0, phase = 0;
-        bool ok = true;
-        for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-            const BsTileX tc = load_tile(p, tile);
-            const uint32_t row0 = tc.row0;
-            const uint32_t n_sub = ceil_div(tc.nn, 32);
-            const uint32_t ntile = tc.ntile;
-            const uint64_t blk0 = ((uint64_t)tc.g * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
-            for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
-                ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty);
-                if (!__all_sync(0xffffffffu, ok)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t* sf = sf_base + stage * C::kSFStage;
-                if (lane == 0) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+                const BsTileX tc = load_tile(p, tile);
+                const uint64_t ablk0 = ((uint64_t)tc.g * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
+                const uint64_t sblk0 = ((uint64_t)tc.g * p.m_tiles + tc.mt) * p.k_tiles;
+                for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
+                    if (!(ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty))) break;
+                    uint8_t* sf = sf_base + stage * C::kSFStage;
                     mbar_arrive_expect_tx(&load_full[stage],
-                                          C::kNA * (C::kATx + C::kSF) + C::kSFB + 2 * n_sub * 32 * 128);
-                    // activation scales of this token tile and stage (hi and lo)
-                    bulk_g2s(sf + C::kNA * C::kSF, p.sfb_atoms + ((uint64_t)ntile * p.k_tiles + kt) * C::kSFB,
-                             C::kSFB, &load_full[stage]);
+                                          C::kNA * C::kATx + C::kSFStage + 2 * C::kBBytes);
+                    bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, &load_full[stage]);
+                    bulk_g2s(sf + C::kSFA, p.sfb_atoms + ((uint64_t)tc.ntile * p.k_tiles + kt) * C::kSFB, C::kSFB,
+                             &load_full[stage]);
 #pragma unroll
                     for (int pj = 0; pj < C::kNA; ++pj) {
-                        const uint64_t b = blk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt;  // weight block
+                        const uint64_t b = ablk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt;  // weight block
                         tma_load_2d(a_base + (stage * C::kNA + pj) * C::kABytes, &tmap_a, 0, (int32_t)(b * 128),
                                     &load_full[stage]);
-                        bulk_g2s(sf + pj * C::kSF, p.sfa + b * 512, C::kSF, &load_full[stage]);
                     }
-                    uint8_t* bh = b_base + stage * 2 * C::kBBytes;
-                    for (uint32_t sb = 0; sb < n_sub; ++sb) {
-                        tma_load_2d(bh + sb * 32 * 128, &tmap_b_hi, (int32_t)(kt * 128), (int32_t)(row0 + sb * 32),
-                                    &load_full[stage]);
-                        tma_load_2d(bh + C::kBBytes + sb * 32 * 128, &tmap_b_lo, (int32_t)(kt * 128),
-                                    (int32_t)(row0 + sb * 32), &load_full[stage]);
+                    // hi and lo planes of the tile's token rows in one 3-D box
+                    tma_load_3d(b_base + stage * 2 * C::kBBytes, &tmap_b, (int32_t)(kt * 128), (int32_t)tc.row0, 0,
+                                &load_full[stage]);
+                    if (++stage == C::kStages) {
+                        stage = 0;
+                        phase ^= 1;
                     }
-                }
-                __syncwarp();
-                if (++stage == C::kStages) {
-                    stage = 0;
-                    phase ^= 1;
                 }
             }
         }
@@ -401,9 +402,8 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
                 const BsTileX tc = load_tile(p, tile);
-                // stacked: hi rows [0, BN) then lo rows [BN, BN + n_pad); else one term per MMA
-                const uint32_t n_pad = ceil_div(tc.nn, 32) * 32;
-                const uint32_t n_mma = C::kStackN ? BN + n_pad : max(16u, (tc.nn + 15u) & ~15u);
+                // stacked: hi rows [0, BN) then lo rows [BN, 2 BN); else one term per MMA
+                const uint32_t n_mma = C::kStackN ? 2 * BN : max(16u, (tc.nn + 15u) & ~15u);
                 if (!(ok = mbar_wait(&acc_empty[acc], accphase ^ 1, p.err, kErrTimeoutAccEmpty))) break;
                 tc_fence_after();
                 const uint32_t d0 = tmem + acc * C::kAccCols;
@@ -414,22 +414,22 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
                     const uint32_t sfc = tmem + kSfCol0 + stage * C::kSFCols;
 #pragma unroll
                     for (int q = 0; q < C::kSFStage / 512; ++q) {
-                        tmem_cp_sf(sfc + q * 4, smem_desc_sf(smem_u32(sf + q * C::kSF)));
+                        tmem_cp_sf(sfc + q * 4, smem_desc_sf(smem_u32(sf + q * 512)));
                     }
                     const uint32_t sfb = sfc + C::kNA * 4;
                     const uint32_t a_addr = smem_u32(a_base + stage * C::kNA * C::kABytes);
-                    const uint32_t bh_addr = smem_u32(b_base + stage * 2 * C::kBBytes);
+                    const uint32_t b_addr = smem_u32(b_base + stage * 2 * C::kBBytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t idesc = idesc_bs_m128(n_mma, kk);
-                        const uint64_t bhi = smem_desc_sw128(bh_addr + kk * 32);
+                        const uint64_t bhi = smem_desc_sw128(b_addr + kk * 32);
 #pragma unroll
                         for (int pj = 0; pj < C::kNA; ++pj) {
                             const uint64_t adesc = smem_desc_sw128(a_addr + pj * C::kABytes + kk * 32);
                             if (C::kStackN) {
                                 mma_bs(d0 + pj * 2 * BN, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
                             } else {
-                                const uint64_t blo = smem_desc_sw128(bh_addr + C::kBBytes + kk * 32);
+                                const uint64_t blo = smem_desc_sw128(b_addr + C::kBBytes + kk * 32);
                                 const uint32_t d = d0 + pj * BN;
                                 mma_bs(d, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
                                 mma_bs(d, adesc, blo, idesc, sfc + pj * 4, sfb + 4, 1);
@@ -468,13 +468,10 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
             const uint32_t m = tc.mt * 128 + r;
             const uint64_t row0 = tc.row0;
             const uint32_t dbase = tmem + lane_addr + acc * C::kAccCols;
-            // scale block of the down GEMM for this token tile and 128-K stage
-            // (= mt), in the down GEMM's layout (stacked for 64-token tiles)
-            constexpr uint32_t kDnAtom = BN == 64 ? 512 : 1024, kDnLo = BN == 64 ? 8 : 512;
+            // the down GEMM's scale block for this token tile and 128-K stage (= mt)
             uint8_t* h_atom =
-                MODE == kGateUp ? p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * kDnAtom : nullptr;
-            // column of the hi / lo accumulator of output column c, per projection
-            constexpr uint32_t kLoOff = C::kStackN ? BN : 0;       // stacked: lo half follows hi
+                MODE == kGateUp ? p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * C::kSFB : nullptr;
+            constexpr uint32_t kLoOff = C::kStackN ? BN : 0;        // stacked: lo half follows hi
             constexpr uint32_t kProjOff = C::kStackN ? 2 * BN : BN;
             for (uint32_t c0 = 0; c0 < tc.nn; c0 += 16) {
                 float v0[16], v1[16];
@@ -505,12 +502,11 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
                         uint8_t hi, lo, sh, sl;
                         split_e4m3_warp(hv, hi, lo, sh, sl);
                         const uint64_t prow = row0 + col;
-                        p.h_hi[prow * p.h_stride + m] = hi;
-                        p.h_lo[prow * p.h_stride + m] = lo;
+                        p.h_out[prow * p.h_stride + m] = hi;
+                        p.h_out[p.h_plane + prow * p.h_stride + m] = lo;
                         if (lane == 0) {
-                            const uint32_t pos = (col % 32) * 16 + (col / 32) * 4 + quarter;
-                            h_atom[pos] = sh;
-                            h_atom[pos + kDnLo] = sl;
+                            h_atom[sfb_pos_hi<BN>(col) + quarter] = sh;
+                            h_atom[sfb_pos_lo<BN>(col) + quarter] = sl;
                         }
                     }
                 } else if (m < p.m_valid) {
@@ -536,8 +532,8 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
 }
 
 template <int MODE, int BN>
-static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tbh, const CUtensorMap& tbl,
-                                  const BsParams& p, int num_sms, cudaStream_t st) {
+static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p, int num_sms,
+                                  cudaStream_t st) {
     using C = BsCfg<MODE, BN>;
     static uint64_t attr_set = 0;  // one bit per device
     int dev = 0;
@@ -548,18 +544,18 @@ static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tbh,
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
     }
-    gemm_bs_kernel<MODE, BN><<<num_sms, 192, C::kSmem, st>>>(ta, tbh, tbl, p);
+    gemm_bs_kernel<MODE, BN><<<num_sms, 192, C::kSmem, st>>>(ta, tb, p);
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tbh,
-                           const CUtensorMap& tbl, const BsParams& p, int num_sms, cudaStream_t st) {
+cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
+                           int num_sms, cudaStream_t st) {
     if (mode == kGateUp) {
-        return block_n == 64 ? launch_bs_mode<kGateUp, 64>(ta, tbh, tbl, p, num_sms, st)
-                             : launch_bs_mode<kGateUp, 128>(ta, tbh, tbl, p, num_sms, st);
+        return block_n == 32 ? launch_bs_mode<kGateUp, 32>(ta, tb, p, num_sms, st)
+                             : launch_bs_mode<kGateUp, 128>(ta, tb, p, num_sms, st);
     }
-    return block_n == 64 ? launch_bs_mode<kDown, 64>(ta, tbh, tbl, p, num_sms, st)
-                         : launch_bs_mode<kDown, 128>(ta, tbh, tbl, p, num_sms, st);
+    return block_n == 32 ? launch_bs_mode<kDown, 32>(ta, tb, p, num_sms, st)
+                         : launch_bs_mode<kDown, 128>(ta, tb, p, num_sms, st);
 }
 
 }  // namespace moe_b200

@@ -57,15 +57,15 @@ struct BsParams {
     uint32_t rows_pad;        // weight rows per matrix, padded to 128
     uint32_t m_tiles;         // rows_pad / 128
     uint32_t k_tiles;         // K (padded to 128) / 128
-    const uint8_t* sfa;       // [groups][proj][m_tiles][k_tiles][512] weight scale blocks
-    const uint8_t* sfb_atoms; // [token tiles][k_tiles][hi 512 | lo 512] activation scale blocks
-    uint8_t* h_hi;            // gate/up output: [rows][h_stride] E4M3 hi/lo terms of SiLU(gate)*up
-    uint8_t* h_lo;
+    const uint8_t* sfa;       // weight scale blocks, [groups][m_tiles][k_tiles][proj][512]
+    const uint8_t* sfb_atoms; // activation scale blocks, [token tiles][k_tiles][512 (32-token) | 1024 (128-token)]
+    uint8_t* h_out;           // gate/up output: [hi, lo][rows][h_stride] E4M3 terms of SiLU(gate)*up
+    uint64_t h_plane;         // bytes between the hi and lo planes of h_out
     uint32_t h_stride;
-    uint8_t* sfh_atoms;       // gate/up output: the down GEMM's scale blocks, [token tiles][I/128][1024]
-    float* y_out;             // down output [rows][y_stride]
+    uint8_t* sfh_atoms;       // gate/up output: the down GEMM's scale blocks (same layout as sfb_atoms)
+    float* y_out;             // down: [rows][y_stride] f32
     uint32_t y_stride;
-    uint32_t m_valid;
+    uint32_t m_valid;         // output rows to write (down)
     uint32_t* err;
 };
 
@@ -108,18 +108,21 @@ cudaError_t launch_gemm_tc(int mode, const CUtensorMap& tmap_b, const GemmParams
                            cudaStream_t st);
 // Block-scaled tcgen05 grouped GEMMs (gemm_bs.cu) and their data preparation.
 cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, uint32_t rows_pad, uint32_t Kp,
-                             uint8_t* codes, uint8_t* sfa, cudaStream_t st);
-cudaError_t launch_quantize_rows(const uint16_t* x, uint32_t T, uint32_t H, uint32_t Kp, uint8_t* q_hi,
-                                 uint8_t* q_lo, uint8_t* s_hi, uint8_t* s_lo, cudaStream_t st);
-cudaError_t launch_gather_bs(const uint8_t* q_hi, const uint8_t* q_lo, const uint8_t* s_hi, const uint8_t* s_lo,
-                             uint32_t Kp, const uint32_t* row_token, uint32_t rows, const uint32_t* offset,
-                             const uint32_t* tile_off, uint32_t groups, uint32_t m_tiles, uint32_t block_n,
-                             uint8_t* x_hi, uint8_t* x_lo, uint8_t* sf_atoms, cudaStream_t st);
+                             uint8_t* codes, uint8_t* sfa, uint32_t sf_stride, cudaStream_t st);
+// q [2][T][Kp] E4M3 (hi, lo planes), sc [2][T][Kp/32] E8M0.
+cudaError_t launch_quantize_rows(const uint16_t* x, uint32_t T, uint32_t H, uint32_t Kp, uint8_t* q, uint8_t* sc,
+                                 cudaStream_t st);
+// xb [2][rows_cap][Kp] permuted rows; sf_atoms per (token tile, 128-K stage).
+cudaError_t launch_gather_bs(const uint8_t* q, const uint8_t* sc, uint32_t T, uint32_t Kp, const uint32_t* row_token,
+                             uint32_t rows, uint32_t rows_cap, const uint32_t* offset, const uint32_t* tile_off,
+                             uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* xb, uint8_t* sf_atoms,
+                             cudaStream_t st);
 cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, const uint32_t* tile_off,
                                uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint32_t max_tiles,
                                TileEntry* tiles, cudaStream_t st);
-cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tbh,
-                           const CUtensorMap& tbl, const BsParams& p, int num_sms, cudaStream_t st);
+// `tb` is a 3-D map over [2][rows][K] E4M3 bytes with a {128, block_n, 2} box.
+cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
+                           int num_sms, cudaStream_t st);
 
 // CUDA-core grouped GEMMs used only to cross-check the tcgen05 kernels.
 cudaError_t launch_gemm_simt(int mode, const uint16_t* b, uint32_t b_stride, uint32_t rows, const GemmParams& p,
