@@ -203,6 +203,20 @@ def config_dict(shape, args):
             "l2": "inputs_exceed_l2"}
 
 
+def profiled_traffic(args):
+    """DRAM bytes (read + write) per launch of the gate/up GEMM, from the ncu
+    capture summarised under profiles/ for this workload (None without one)."""
+    if args.config != 1 or args.tokens != 256:
+        return None
+    f = ROOT / "profiles" / "gemm_bs_gate_up_c1_t256.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip())
+    return None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -264,7 +278,6 @@ def main():
     launches_per_step = eng.launches()
 
     # ---- device-timed region: inputs resident in HBM ----
-    eng.profile_enable(args.steps)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
@@ -277,14 +290,21 @@ def main():
         torch.cuda.synchronize()
     eng.sync(sp)
     ms = start.elapsed_time(end)
-    stage_ms, prof_calls = eng.profile_read()
-    eng.profile_enable(0)
     if dist:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
     value = T * args.steps * world / (ms / 1000.0)
+
+    # ---- per-stage breakdown: the same steps again with events between the
+    # stages (kept out of the headline region above) ----
+    eng.profile_enable(args.steps)
+    for _ in range(args.steps):
+        step()
+    eng.sync(sp)
+    stage_ms, prof_calls = eng.profile_read()
+    eng.profile_enable(0)
 
     # ---- end to end through the host-buffer C-ABI call ----
     xh = torch.from_numpy(li.x.view(np.int16)).pin_memory()
@@ -321,8 +341,11 @@ def main():
     counts = eng.read(L.BUF_GROUP_COUNT, (shape.experts,), np.uint32)
     distinct = int((counts > 0).sum())
     P = T * K
-    Kp = (H + 63) // 64 * 64
-    Ip = (shape.intermediate + 63) // 64 * 64
+    # algorithmic bytes: MXFP4 weights of the experts routed to (17 bytes per
+    # 32 elements) + the permuted activation rows in + the intermediate rows
+    # out, both at 2 bytes per element (bf16, or the E4M3 hi/lo pair)
+    Kp = H
+    Ip = shape.intermediate
     gu_weight_bytes = distinct * 2 * shape.intermediate * H * 17 / 32
     gu_bytes = gu_weight_bytes + P * Kp * 2 + P * Ip * 2
     gu_ms = stage_ms["gate_up"] / max(prof_calls, 1)
@@ -337,9 +360,9 @@ def main():
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": config_dict(shape, args),
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2 + T * K * 8},
-        "roofline": {"kernel": "gemm_tc_kernel<gate_up>", "bound": "hbm", "achieved": achieved, "peak": hbm,
+        "roofline": {"kernel": "gemm_bs_kernel<gate_up>", "bound": "hbm", "achieved": achieved, "peak": hbm,
                      "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_kind,
-                     "traffic": None, "algorithmic_bytes_per_launch": gu_bytes,
+                     "traffic": profiled_traffic(args), "algorithmic_bytes_per_launch": gu_bytes,
                      "launch_ms": gu_ms, "distinct_experts": distinct},
         "stages_ms_per_step": {k: v / max(prof_calls, 1) for k, v in stage_ms.items()},
         "down_gemm": {"achieved_gbs": dn_bytes / (dn_ms / 1000.0) / 1e9, "launch_ms": dn_ms},

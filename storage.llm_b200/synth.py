@@ -97,6 +97,17 @@ def gen_mxfp4(rng: np.random.Generator, lead: tuple, rows: int, cols: int,
     return out.reshape(lead + (rows, nblk * MXFP4_BLOCK_BYTES))
 
 
+def jitter_scales(packed: np.ndarray, rng: np.random.Generator, spread: int, up: int = 0) -> np.ndarray:
+    """Copy of GGUF MXFP4 bytes with every block's E8M0 scale byte moved by a
+    seeded offset in [-spread, up] (real checkpoints vary their scales per
+    32-element block; the default generator uses one scale everywhere)."""
+    shp = packed.shape
+    blk = packed.reshape(shp[:-1] + (shp[-1] // MXFP4_BLOCK_BYTES, MXFP4_BLOCK_BYTES)).copy()
+    off = rng.integers(-spread, up + 1, size=blk.shape[:-1])
+    blk[..., 0] = np.clip(blk[..., 0].astype(np.int64) + off, 0, 254).astype(np.uint8)
+    return blk.reshape(shp)
+
+
 def target_popularity(skew: str, experts: int, rng: np.random.Generator) -> np.ndarray:
     if skew == "zipf1.1":
         ranks = np.arange(1, experts + 1, dtype=np.float64)
