@@ -253,6 +253,18 @@ __device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_
         : "memory");
 }
 
+// Same MMA with A read from tensor memory ([a_tmem]: lane 0, first column of
+// the 128-row A slice; one 32-bit column per 4 bytes of each row).
+__device__ __forceinline__ void mma_bs_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], [%1], %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+}
+
 // Instruction descriptor for kind::mxf8f6f4 block_scale: A E2M1, B E4M3,
 // E8M0 scales, both operands K-major, M = 128, N = n; `sf_id` selects the
 // byte of each 32-bit scale word (the 32-element K block inside a 128-K stage).
@@ -295,6 +307,11 @@ __device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
 #define MOE_TMEM_ST8(taddr, v)                                                                               \
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), \
                  "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])      \
+                 : "memory")
+
+#define MOE_TMEM_ST4(taddr, v)                                                                               \
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v[0]),      \
+                 "r"(v[1]), "r"(v[2]), "r"(v[3])                                                              \
                  : "memory")
 
 #define MOE_TMEM_LD16(taddr, v)                                                                              \

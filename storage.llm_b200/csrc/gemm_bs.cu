@@ -6,10 +6,11 @@
 //       blocks of 128 rows x 128 K, TMA'd with the 16U4_ALIGN16B type (each
 //       16 codes land in 16 bytes of shared memory, the operand form
 //       kind::mxf8f6f4 reads);
-//   SFA the rows' E8M0 scales, one 512-byte block per 128 x 128 tile in the
-//       layout tcgen05.cp.32x128b.warpx4 expects (row r, K block j at byte
-//       (r%32)*16 + (r/32)*4 + j); the gate and up blocks of a tile are
-//       adjacent so one bulk copy brings both;
+//   SFA the rows' E8M0 scales, one 512-byte block per 128 x 128 tile (row r,
+//       K block j at byte (r%32)*16 + (r/32)*4 + j); the gate and up blocks
+//       of a tile are adjacent so one bulk copy brings both.  Scale-factor
+//       warps store every block into each TMEM lane quarter (lane l holds
+//       bytes [16 l, 16 l + 16)) with tcgen05.st, off the tensor pipe;
 //   B   activations as two E4M3 terms, hi and lo, each with an E8M0 scale per
 //       32 K (SFB).  A bf16 value has 8 significant bits and splits exactly
 //       into hi (4 bits) + lo (4 bits), so W.x = W.x_hi + W.x_lo is the product
@@ -30,12 +31,13 @@
 //          block of the down GEMM), so the down GEMM reads it directly.
 // kDown:   the epilogue writes fp32 expert outputs for the combine.
 //
-// Warp roles (192 threads, one CTA per SM, persistent over a precomputed tile
+// Warp roles (320 threads, one CTA per SM, persistent over a precomputed tile
 // table):
 //   warp 0     producer: per stage one bulk copy of the weight scales, one of
 //              the activation scales, the A boxes, and one B box
-//   warp 1     TMEM owner, scale-factor copies (tcgen05.cp) and MMA issue
+//   warp 1     TMEM owner and MMA issue
 //   warps 2-5  epilogue, one TMEM lane quarter each
+//   warps 6-9  scale factors into TMEM, one lane quarter each
 // All waits are bounded and report through p.err.
 #include <cuda_fp8.h>
 
@@ -317,7 +319,7 @@ cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, co
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 template <int MODE, int BN>
-__global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
+__global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                          const __grid_constant__ CUtensorMap tmap_b,
                                                          const BsParams p) {
     using C = BsCfg<MODE, BN>;
@@ -331,7 +333,8 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
     uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + C::kStages * 2 * C::kBBytes);
     uint64_t* load_full = bars;
     uint64_t* load_empty = load_full + C::kStages;
-    uint64_t* acc_full = load_empty + C::kStages;
+    uint64_t* sf_full = load_empty + C::kStages;   // scale factors stored in TMEM
+    uint64_t* acc_full = sf_full + C::kStages;
     uint64_t* acc_empty = acc_full + C::kAccs;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + C::kAccs);
 
@@ -340,6 +343,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
         for (int i = 0; i < C::kStages; ++i) {
             mbar_init(&load_full[i], 1);
             mbar_init(&load_empty[i], 1);
+            mbar_init(&sf_full[i], 4);
         }
         for (int i = 0; i < C::kAccs; ++i) {
             mbar_init(&acc_full[i], 1);
@@ -408,14 +412,12 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
                 tc_fence_after();
                 const uint32_t d0 = tmem + acc * C::kAccCols;
                 for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
+                    // operands landed (observed here too, so this thread's MMAs
+                    // are ordered after the copies) and the scale factors are in TMEM
                     if (!(ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull))) break;
+                    if (!(ok = mbar_wait(&sf_full[stage], phase, p.err, kErrTimeoutAFull))) break;
                     tc_fence_after();
-                    const uint8_t* sf = sf_base + stage * C::kSFStage;
                     const uint32_t sfc = tmem + kSfCol0 + stage * C::kSFCols;
-#pragma unroll
-                    for (int q = 0; q < C::kSFStage / 512; ++q) {
-                        tmem_cp_sf(sfc + q * 4, smem_desc_sf(smem_u32(sf + q * 512)));
-                    }
                     const uint32_t sfb = sfc + C::kNA * 4;
                     const uint32_t a_addr = smem_u32(a_base + stage * C::kNA * C::kABytes);
                     const uint32_t b_addr = smem_u32(b_base + stage * 2 * C::kBBytes);
@@ -447,6 +449,42 @@ __global__ void __launch_bounds__(192, 1) gemm_bs_kernel(const __grid_constant__
                 if (++acc == C::kAccs) {
                     acc = 0;
                     accphase ^= 1;
+                }
+            }
+        }
+    } else if (warp >= 6) {
+        // ------------------------------------------------------------ scale factors
+        // Each warp stores the stage's scale blocks into its TMEM lane quarter
+        // of the stage's scale columns: lane l of every quarter holds bytes
+        // [16 l, 16 l + 16) of each 512-byte block (the layout the MMA reads).
+        // Doing this with tcgen05.st here keeps it off the tensor pipe.  The
+        // slot of stage u is free once stage u's operands have landed: the
+        // producer reloaded it only after the MMAs of stage u - kStages were done.
+        const uint32_t lane_addr = ((warp & 3) * 32) << 16;
+        uint32_t stage = 0, phase = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+            for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
+                ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull, true);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* sf = sf_base + stage * C::kSFStage + lane * 16;
+                const uint32_t col = tmem + lane_addr + kSfCol0 + stage * C::kSFCols;
+#pragma unroll
+                for (int q = 0; q < C::kSFStage / 512; ++q) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(sf + q * 512);
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                    MOE_TMEM_ST4(col + q * 4, w);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sf_full[stage]);
+                if (++stage == C::kStages) {
+                    stage = 0;
+                    phase ^= 1;
                 }
             }
         }
@@ -544,7 +582,7 @@ static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, 
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
     }
-    gemm_bs_kernel<MODE, BN><<<num_sms, 192, C::kSmem, st>>>(ta, tb, p);
+    gemm_bs_kernel<MODE, BN><<<num_sms, 320, C::kSmem, st>>>(ta, tb, p);
     return cudaGetLastError();
 }
 
