@@ -106,8 +106,8 @@ struct moe_b200_engine {
     DevBuf xperm, hperm, yperm;
     DevBuf err_word;
     // block-scaled path: quantised activations and intermediate
-    // (xq, sx, xb, hb hold a hi plane followed by a lo plane)
-    DevBuf xq, sx, xb, sfx_atoms, hb, sfh_atoms, gu_tiles, dn_tiles;
+    // (xb, hb hold a hi plane followed by a lo plane)
+    DevBuf xb, sfx_atoms, hb, sfh_atoms, gu_tiles, dn_tiles;
     // 3-D maps over xb / hb: [0] 32-token box, [1] 128-token box
     CUtensorMap tmap_xb[2]{}, tmap_hb[2]{};
     const void* bs_map_key[2] = {nullptr, nullptr};
@@ -273,7 +273,7 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
                       &eng->rank, &eng->pos_of, &eng->row_token, &eng->row_assign, &eng->g_count,
                       &eng->g_offset, &eng->g_gu_off, &eng->g_dn_off, &eng->xperm, &eng->hperm,
                       &eng->yperm, &eng->err_word, &eng->hx, &eng->hy, &eng->hyf, &eng->hids,
-                      &eng->hw, &eng->hperm_out, &eng->tri, &eng->xq, &eng->sx, &eng->xb,
+                      &eng->hw, &eng->hperm_out, &eng->tri, &eng->xb,
                       &eng->sfx_atoms, &eng->hb, &eng->sfh_atoms, &eng->gu_tiles, &eng->dn_tiles};
     for (DevBuf* b : bufs) b->release();
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
@@ -464,11 +464,9 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     const uint32_t block_n = (bs && (uint64_t)P <= 48ull * G) ? 32u : kBlockN;
     CK(eng->yperm.reserve((size_t)P * H * 4));
     if (bs) {
-        CK(eng->xq.reserve((size_t)2 * T * Kq));
-        CK(eng->sx.reserve((size_t)2 * T * (Kq / 32)));
         CK(eng->xb.reserve((size_t)2 * rows_cap * Kq));
         CK(eng->hb.reserve((size_t)2 * rows_cap * Iq));
-        const size_t token_tiles = (size_t)P / block_n + G;  // upper bound of sum_g ceil(count_g / block_n)
+        const size_t token_tiles = (size_t)P / block_n + G;
         CK(eng->sfx_atoms.reserve(token_tiles * (Kq / 128) * 1024));
         CK(eng->sfh_atoms.reserve(token_tiles * (Iq / 128) * 1024));
         CK(eng->gu_tiles.reserve(token_tiles * (L->rp_i / 128) * sizeof(TileEntry)));
@@ -529,8 +527,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     const int sigmoid = cfg->score_func == MOE_B200_SCORE_SIGMOID;
     const float rscale = cfg->routed_scale > 0.f ? cfg->routed_scale : 1.0f;
     CK(launch_router(x, L->router.as<uint16_t>(), T, E, H, K, sigmoid, cfg->norm_topk, rscale,
-                     eng->logits.as<float>(), ids, w, eng->scores.as<float>(), st));
-    launches += 2;
+                     eng->logits.as<float>(), ids, w, eng->scores.as<float>(), errw, st, &launches));
     mark(1);
 
     GroupInfo gi;
@@ -541,25 +538,35 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     gi.block_n = block_n;
     gi.gu_row_tiles = ceil_div(I, kTileRows);
     gi.dn_row_tiles = ceil_div(H, kTileRows);
-    CK(launch_permute(ids, T, K, E, shared_rows, eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi,
-                      eng->pos_of.as<uint32_t>(), eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(),
-                      errw, st));
-    launches += 3;
+    const uint32_t token_tiles = P / block_n + G;  // upper bound of sum_g ceil(count_g / block_n)
+    if (route_small_fits(T * K, E)) {
+        // decode-sized batch: sort, offsets and both tile tables in one block
+        CK(launch_route_small(ids, T, K, E, shared_rows, gi, bs ? eng->gu_tiles.as<TileEntry>() : nullptr,
+                              token_tiles * (L->rp_i / 128), bs ? eng->dn_tiles.as<TileEntry>() : nullptr,
+                              token_tiles * (L->rp_h / 128), eng->pos_of.as<uint32_t>(),
+                              eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(), errw, st));
+        launches += 1;
+    } else {
+        CK(launch_permute(ids, T, K, E, shared_rows, eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi,
+                          eng->pos_of.as<uint32_t>(), eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(),
+                          errw, st));
+        launches += 3;
+        if (bs) {
+            CK(launch_build_tiles(gi.count, gi.offset, gi.gu_tile_off, G, L->rp_i / 128, block_n,
+                                  token_tiles * (L->rp_i / 128), eng->gu_tiles.as<TileEntry>(), st));
+            CK(launch_build_tiles(gi.count, gi.offset, gi.dn_tile_off, G, L->rp_h / 128, block_n,
+                                  token_tiles * (L->rp_h / 128), eng->dn_tiles.as<TileEntry>(), st));
+            launches += 2;
+        }
+    }
     mark(2);
     if (bs) {
-        const uint32_t token_tiles = P / block_n + G;
-        CK(launch_build_tiles(gi.count, gi.offset, gi.gu_tile_off, G, L->rp_i / 128, block_n,
-                              token_tiles * (L->rp_i / 128), eng->gu_tiles.as<TileEntry>(), st));
-        CK(launch_build_tiles(gi.count, gi.offset, gi.dn_tile_off, G, L->rp_h / 128, block_n,
-                              token_tiles * (L->rp_h / 128), eng->dn_tiles.as<TileEntry>(), st));
-        launches += 2;
-        // activations -> exact hi/lo E4M3 terms per token, then per permuted row
+        // permuted rows of x as exact hi/lo E4M3 terms + their scale blocks
         const uint64_t xb_rows = eng->xb.bytes / (2ull * Kq), hb_rows = eng->hb.bytes / (2ull * Iq);
-        CK(launch_quantize_rows(x, T, H, Kq, eng->xq.as<uint8_t>(), eng->sx.as<uint8_t>(), st));
-        CK(launch_gather_bs(eng->xq.as<uint8_t>(), eng->sx.as<uint8_t>(), T, Kq, eng->row_token.as<uint32_t>(), P,
-                            (uint32_t)xb_rows, gi.offset, gi.gu_tile_off, G, L->rp_i / 128, block_n,
-                            eng->xb.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(), st));
-        launches += 2;
+        CK(launch_gather_quant_bs(x, H, Kq, eng->row_token.as<uint32_t>(), P, (uint32_t)xb_rows, gi.offset,
+                                  gi.gu_tile_off, G, L->rp_i / 128, block_n, eng->xb.as<uint8_t>(),
+                                  eng->sfx_atoms.as<uint8_t>(), st));
+        launches += 1;
         mark(3);
         BsParams bp{};
         bp.groups = G;

@@ -101,7 +101,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase with the given parity; gives up after ~2^31 SM clocks
 // (about one second), records `code` and returns false.  `backoff` parks
 // the warp for a short sleep between polls, for waiters whose latency does
-// not matter (it leaves the issue slots to the converter warps).
+// not matter (it leaves the issue slots to the warps on the critical path).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code,
                                           bool backoff = false) {
     if (mbar_try_wait(bar, parity)) return true;

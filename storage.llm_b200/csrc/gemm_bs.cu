@@ -41,6 +41,8 @@
 // All waits are bounded and report through p.err.
 #include <cuda_fp8.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -117,70 +119,58 @@ __device__ __forceinline__ void split_e4m3_warp(float v, uint8_t& hi, uint8_t& l
 }
 
 // ---------------------------------------------------------------------------
-// Activation quantisation: one warp per (token, 32-element block).
-//   q [2][T][Kp] E4M3 bytes (hi plane, lo plane), s [2][T][Kp/32] E8M0 bytes.
+// Permuted activation rows for the block-scaled GEMM, quantised on the way:
+// one warp per (permuted row, 128-element K stage).  Lane l splits elements
+// 128 kt + 32 j + l (j = 0..3, four 32-element blocks) of the row's token
+// into exact hi + lo E4M3 terms, writes them to the hi and lo planes of xb
+// ([2][rows_cap][Kp]) and the stage's four hi and four lo scale bytes, as
+// one 32-bit word each, straight into the scale block the GEMM's producer
+// bulk-copies for (token tile, kt), at sfb_pos_hi / sfb_pos_lo.  Token tile
+// of row r in group g: tile_off[g] / m_tiles + (r - offset[g]) / block_n.
 // ---------------------------------------------------------------------------
-__global__ void quantize_rows_kernel(const uint16_t* __restrict__ x, uint32_t T, uint32_t H, uint32_t Kp,
-                                     uint8_t* __restrict__ q, uint8_t* __restrict__ sc) {
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t nblk = Kp / 32;
-    const uint64_t total = (uint64_t)T * nblk;
-    const uint64_t qplane = (uint64_t)T * Kp, splane = (uint64_t)T * nblk;
-    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
-    for (uint64_t wb = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wb < total; wb += warps) {
-        const uint32_t t = (uint32_t)(wb / nblk), b = (uint32_t)(wb % nblk);
-        const uint32_t k = b * 32 + lane;
-        const float v = k < H ? bf16_bits_to_f32(x[(uint64_t)t * H + k]) : 0.f;
-        uint8_t hi, lo, sh, sl;
-        split_e4m3_warp(v, hi, lo, sh, sl);
-        q[(uint64_t)t * Kp + k] = hi;
-        q[qplane + (uint64_t)t * Kp + k] = lo;
-        if (lane == 0) {
-            sc[(uint64_t)t * nblk + b] = sh;
-            sc[splane + (uint64_t)t * nblk + b] = sl;
-        }
-    }
-}
-
-// Permuted rows for the block-scaled GEMM: the E4M3 bytes of each row's token
-// (both planes) and its scale words, the latter written straight into the
-// blocks the GEMM's producer bulk-copies: one block per (token tile, 128-K
-// stage) in the layout of sfb_pos_hi / sfb_pos_lo.  Token tile t of group g
-// is tile_off[g] / m_tiles + (row - offset[g]) / block_n.
 template <int BN>
-__global__ void gather_bs_kernel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sc, uint32_t T,
-                                 uint32_t Kp, const uint32_t* __restrict__ row_token, uint32_t rows,
-                                 uint32_t rows_cap, const uint32_t* __restrict__ offset,
-                                 const uint32_t* __restrict__ tile_off, uint32_t groups, uint32_t m_tiles,
-                                 uint8_t* __restrict__ xb, uint8_t* __restrict__ sf_atoms) {
+__global__ void __launch_bounds__(256) gather_quant_bs_kernel(
+    const uint16_t* __restrict__ x, uint32_t H, uint32_t Kp, const uint32_t* __restrict__ row_token, uint32_t rows,
+    uint32_t rows_cap, const uint32_t* __restrict__ offset, const uint32_t* __restrict__ tile_off, uint32_t groups,
+    uint32_t m_tiles, uint8_t* __restrict__ xb, uint8_t* __restrict__ sf_atoms) {
     constexpr uint32_t kAtom = BN == 32 ? 512 : 1024;
-    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     const uint32_t lane = threadIdx.x & 31;
-    const uint32_t nv = Kp / 16, nkt = Kp / 128;
-    const uint64_t qplane = (uint64_t)T * Kp, xplane = (uint64_t)rows_cap * Kp;
-    const uint64_t splane = (uint64_t)T * (Kp / 32);
-    for (uint32_t r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
-        const uint32_t t = row_token[r];
-        for (int pl = 0; pl < 2; ++pl) {
-            const uint4* src = reinterpret_cast<const uint4*>(q + pl * qplane + (uint64_t)t * Kp);
-            uint4* dst = reinterpret_cast<uint4*>(xb + pl * xplane + (uint64_t)r * Kp);
-            for (uint32_t v = lane; v < nv; v += 32) dst[v] = __ldg(src + v);
+    const uint32_t nkt = Kp / 128;
+    const uint64_t tasks = (uint64_t)rows * nkt;
+    const uint64_t xplane = (uint64_t)rows_cap * Kp;
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    for (uint64_t task = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; task < tasks; task += warps) {
+        const uint32_t r = (uint32_t)(task / nkt), kt = (uint32_t)(task % nkt);
+        const uint16_t* xr = x + (uint64_t)row_token[r] * H;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t k = kt * 128 + j * 32 + lane;
+            v[j] = k < H ? bf16_bits_to_f32(__ldg(xr + k)) : 0.f;
         }
-        uint32_t lo = 0, hi = groups;  // group owning row r
-        while (hi - lo > 1) {
-            const uint32_t mid = (lo + hi) >> 1;
-            if (offset[mid] <= r) lo = mid;
-            else hi = mid;
+        uint32_t shw = 0, slw = 0;
+        uint8_t* dh = xb + (uint64_t)r * Kp + kt * 128 + lane;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint8_t hi, lo, sh, sl;
+            split_e4m3_warp(v[j], hi, lo, sh, sl);
+            dh[j * 32] = hi;
+            dh[xplane + j * 32] = lo;
+            shw |= (uint32_t)sh << (8 * j);
+            slw |= (uint32_t)sl << (8 * j);
         }
-        const uint32_t n = r - offset[lo];
-        const uint64_t tile = tile_off[lo] / m_tiles + n / BN;
-        const uint32_t rr = n % BN;
-        const uint32_t* wh = reinterpret_cast<const uint32_t*>(sc + (uint64_t)t * (Kp / 32));
-        const uint32_t* wl = reinterpret_cast<const uint32_t*>(sc + splane + (uint64_t)t * (Kp / 32));
-        for (uint32_t kt = lane; kt < nkt; kt += 32) {
+        if (lane == 0) {
+            uint32_t lo = 0, hi = groups;  // group owning row r
+            while (hi - lo > 1) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (offset[mid] <= r) lo = mid;
+                else hi = mid;
+            }
+            const uint32_t n = r - offset[lo];
+            const uint64_t tile = tile_off[lo] / m_tiles + n / BN;
             uint8_t* atom = sf_atoms + (tile * nkt + kt) * kAtom;
-            *reinterpret_cast<uint32_t*>(atom + sfb_pos_hi<BN>(rr)) = __ldg(wh + kt);
-            *reinterpret_cast<uint32_t*>(atom + sfb_pos_lo<BN>(rr)) = __ldg(wl + kt);
+            *reinterpret_cast<uint32_t*>(atom + sfb_pos_hi<BN>(n % BN)) = shw;
+            *reinterpret_cast<uint32_t*>(atom + sfb_pos_lo<BN>(n % BN)) = slw;
         }
     }
 }
@@ -244,27 +234,19 @@ cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, 
     return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_rows(const uint16_t* x, uint32_t T, uint32_t H, uint32_t Kp, uint8_t* q, uint8_t* sc,
-                                 cudaStream_t st) {
-    if (T == 0) return cudaSuccess;
-    const uint64_t warps = (uint64_t)T * (Kp / 32);
-    const uint64_t blocks = (warps + 7) / 8;
-    quantize_rows_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, st>>>(x, T, H, Kp, q, sc);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_gather_bs(const uint8_t* q, const uint8_t* sc, uint32_t T, uint32_t Kp, const uint32_t* row_token,
-                             uint32_t rows, uint32_t rows_cap, const uint32_t* offset, const uint32_t* tile_off,
-                             uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* xb, uint8_t* sf_atoms,
-                             cudaStream_t st) {
+cudaError_t launch_gather_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token,
+                                   uint32_t rows, uint32_t rows_cap, const uint32_t* offset, const uint32_t* tile_off,
+                                   uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* xb, uint8_t* sf_atoms,
+                                   cudaStream_t st) {
     if (rows == 0) return cudaSuccess;
-    const uint32_t blocks = min(ceil_div(rows, 8), 148u * 8u);
+    const uint64_t tasks = (uint64_t)rows * (Kp / 128);
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((tasks + 7) / 8, 148ull * 8ull);
     if (block_n == 32) {
-        gather_bs_kernel<32><<<blocks, 256, 0, st>>>(q, sc, T, Kp, row_token, rows, rows_cap, offset, tile_off,
-                                                     groups, m_tiles, xb, sf_atoms);
+        gather_quant_bs_kernel<32><<<blocks, 256, 0, st>>>(x, H, Kp, row_token, rows, rows_cap, offset, tile_off,
+                                                           groups, m_tiles, xb, sf_atoms);
     } else {
-        gather_bs_kernel<128><<<blocks, 256, 0, st>>>(q, sc, T, Kp, row_token, rows, rows_cap, offset, tile_off,
-                                                      groups, m_tiles, xb, sf_atoms);
+        gather_quant_bs_kernel<128><<<blocks, 256, 0, st>>>(x, H, Kp, row_token, rows, rows_cap, offset, tile_off,
+                                                            groups, m_tiles, xb, sf_atoms);
     }
     return cudaGetLastError();
 }
@@ -465,7 +447,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
             for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
-                ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull, true);
+                ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
                     break;

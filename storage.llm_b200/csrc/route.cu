@@ -12,6 +12,8 @@
 //            expert index first), optional renormalisation and scaling.
 // The permutation is the order of moe_pc_group_tokens_by_expert
 // (token_grouping.cpp.inc:47-55): sorted by expert, then token index.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -129,31 +131,26 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
 }
 
 // ---------------------------------------------------------------------------
-// Scores + top-k: one warp per token.
+// Scores + top-k of one token, by one warp.  `p` holds the token's E logits
+// on entry (shared memory; may alias nothing else) and its scores on exit.
 // ---------------------------------------------------------------------------
 constexpr int kMaxExperts = 1024;
 
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, uint32_t T, uint32_t E,
-                                                          uint32_t K, int sigmoid, int norm_topk, float routed_scale,
-                                                          int32_t* __restrict__ ids, float* __restrict__ wout,
-                                                          float* __restrict__ scores_out) {
-    __shared__ float ps[8][kMaxExperts];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t t = blockIdx.x * 8 + warp;
-    if (t >= T) return;
-    float* p = ps[warp];
-    const float* lg = logits + (uint64_t)t * E;
+__device__ void topk_token(float* p, uint32_t t, uint32_t E, uint32_t K, int sigmoid, int norm_topk,
+                           float routed_scale, int32_t* __restrict__ ids, float* __restrict__ wout,
+                           float* __restrict__ scores_out) {
+    const int lane = threadIdx.x & 31;
     if (sigmoid) {
         for (uint32_t e = lane; e < E; e += 32) {
-            const float ex = (float)exp(-(double)lg[e]);
+            const float ex = (float)exp(-(double)p[e]);
             p[e] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
         }
         __syncwarp();
     } else {
         float mx = -INFINITY;
-        for (uint32_t e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+        for (uint32_t e = lane; e < E; e += 32) mx = fmaxf(mx, p[e]);
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        for (uint32_t e = lane; e < E; e += 32) p[e] = (float)exp((double)lg[e] - (double)mx);
+        for (uint32_t e = lane; e < E; e += 32) p[e] = (float)exp((double)p[e] - (double)mx);
         __syncwarp();
         double denom = 0.0;
         if (lane == 0) {
@@ -211,6 +208,118 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
             ids[(uint64_t)t * K + j] = sel_i[j];
             wout[(uint64_t)t * K + j] = wv;
         }
+    }
+}
+
+// Top-k over logits in global memory: one warp per token.
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, uint32_t T, uint32_t E,
+                                                          uint32_t K, int sigmoid, int norm_topk, float routed_scale,
+                                                          int32_t* __restrict__ ids, float* __restrict__ wout,
+                                                          float* __restrict__ scores_out) {
+    __shared__ float ps[8][kMaxExperts];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    for (uint32_t e = lane; e < E; e += 32) ps[warp][e] = logits[(uint64_t)t * E + e];
+    __syncwarp();
+    topk_token(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+}
+
+// ---------------------------------------------------------------------------
+// Router for small batches, logits and top-k in one kernel.  A block holds
+// the rows of `tb` tokens and all E router rows in shared memory, brought
+// in by one bulk copy per row before any arithmetic (no staging loop to wait
+// on), computes the tb x E logits with the same 16-chain FMA order as
+// router_logits_kernel, then runs the top-k of its tokens.
+// ---------------------------------------------------------------------------
+constexpr int kRfMaxDots = 64;          // tb * E per block
+constexpr uint32_t kRfSmemMax = 200 * 1024;
+
+__global__ void __launch_bounds__(256) router_fused_kernel(const uint16_t* __restrict__ x,
+                                                           const uint16_t* __restrict__ w, uint32_t T, uint32_t E,
+                                                           uint32_t H, uint32_t K, uint32_t tb, int sigmoid,
+                                                           int norm_topk, float routed_scale,
+                                                           float* __restrict__ logits, int32_t* __restrict__ ids,
+                                                           float* __restrict__ wout, float* __restrict__ scores,
+                                                           uint32_t* __restrict__ err) {
+    extern __shared__ __align__(16) uint8_t rf_smem[];
+    __shared__ uint64_t bar;
+    uint16_t* xs = reinterpret_cast<uint16_t*>(rf_smem);  // [tb][H]
+    uint16_t* ws = xs + (size_t)tb * H;                    // [E][H]
+    float* lg = reinterpret_cast<float*>(ws + (size_t)E * H);  // [tb][E]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t t0 = blockIdx.x * tb;
+    const uint32_t nt = min(tb, T - t0);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t rowb = H * 2;
+        if (lane == 0) mbar_arrive_expect_tx(&bar, (nt + E) * rowb);
+        __syncwarp();
+        for (uint32_t r = lane; r < nt + E; r += 32) {
+            if (r < nt) {
+                bulk_g2s(xs + (size_t)r * H, x + (uint64_t)(t0 + r) * H, rowb, &bar);
+            } else {
+                bulk_g2s(ws + (size_t)(r - nt) * H, w + (uint64_t)(r - nt) * H, rowb, &bar);
+            }
+        }
+    }
+    const bool ok = mbar_wait(&bar, 0, err, kErrTimeoutLoadFull);
+    if (!__syncthreads_and(ok)) return;
+
+    const int l = threadIdx.x & 15;
+    const uint32_t half = (threadIdx.x >> 4) & 1;
+    const uint32_t ndots = nt * E;
+    const uint32_t main_end = H & ~15u;
+    const unsigned full = 0xffffffffu;
+    // a warp's two 16-lane groups take dots [base, base + 8) together, so
+    // both run the same number of iterations (the shuffles span the warp)
+    for (uint32_t base = warp * 8; base < ndots; base += 64) {
+        const uint16_t* xr[4];
+        const uint16_t* wr[4];
+        uint32_t dd[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            dd[j] = base + half * 4 + j;
+            const uint32_t d = dd[j] < ndots ? dd[j] : 0;
+            xr[j] = xs + (size_t)(d / E) * H;
+            wr[j] = ws + (size_t)(d % E) * H;
+        }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (uint32_t i = l; i < main_end; i += 16) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[j] = __fmaf_rn(bf16_bits_to_f32(wr[j][i]), bf16_bits_to_f32(xr[j][i]), acc[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float hi = __shfl_down_sync(full, acc[j], 8, 16);
+            const float bl = acc[j] + hi;  // valid on lanes 0..7
+            float s = __shfl_sync(full, bl, 0, 16);
+#pragma unroll
+            for (int q = 1; q < 8; ++q) s = __fadd_rn(s, __shfl_sync(full, bl, q, 16));
+            if (l == 0 && dd[j] < ndots) {
+                float out = 0.0f + s;
+                uint32_t i = main_end;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                for (; i + 3 < H; i += 4) {
+                    a0 = __fmaf_rn(bf16_bits_to_f32(wr[j][i]), bf16_bits_to_f32(xr[j][i]), a0);
+                    a1 = __fmaf_rn(bf16_bits_to_f32(wr[j][i + 1]), bf16_bits_to_f32(xr[j][i + 1]), a1);
+                    a2 = __fmaf_rn(bf16_bits_to_f32(wr[j][i + 2]), bf16_bits_to_f32(xr[j][i + 2]), a2);
+                    a3 = __fmaf_rn(bf16_bits_to_f32(wr[j][i + 3]), bf16_bits_to_f32(xr[j][i + 3]), a3);
+                }
+                out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
+                for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[j][i]), bf16_bits_to_f32(xr[j][i]), out);
+                lg[dd[j]] = out;
+                logits[(uint64_t)t0 * E + dd[j]] = out;
+            }
+        }
+    }
+    __syncthreads();
+    for (uint32_t tt = warp; tt < nt; tt += 8) {
+        topk_token(lg + (size_t)tt * E, t0 + tt, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores);
     }
 }
 
@@ -338,6 +447,164 @@ __global__ void __launch_bounds__(1024) sort_scan_kernel(uint32_t* __restrict__ 
     }
 }
 
+// ---------------------------------------------------------------------------
+// The whole permutation of a decode-sized batch in one block: the stable
+// counting sort (same order as sort_count/sort_scan/scatter: by expert, then
+// assignment index), the group sizes, offsets and GEMM tile prefixes, and
+// the two tile tables of the block-scaled GEMMs (build_tiles_kernel's
+// entries).  1024 threads; warp w sorts the contiguous segment
+// [w * seg, (w + 1) * seg) of the assignments, seg a multiple of 32.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kSmallN = 8192;  // assignments (8 per lane)
+constexpr uint32_t kSmallE = 256;   // experts
+
+__device__ __forceinline__ void fill_tiles(const uint32_t* cnt, const uint32_t* off, const uint32_t* toff,
+                                           uint32_t G, uint32_t m_tiles, uint32_t block_n, TileEntry* tiles,
+                                           uint32_t max_tiles) {
+    const uint32_t total = toff[G];
+    for (uint32_t t = threadIdx.x; t < total && t < max_tiles; t += blockDim.x) {
+        uint32_t lo = 0, hi = G;
+        while (hi - lo > 1) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (toff[mid] <= t) lo = mid;
+            else hi = mid;
+        }
+        const uint32_t local = t - toff[lo];
+        const uint32_t ntn = ceil_div(cnt[lo], block_n);
+        const uint32_t nt = local % ntn;
+        const uint32_t n0 = nt * block_n;
+        TileEntry e;
+        e.group = lo;
+        e.mt = local / ntn;
+        e.row0 = off[lo] + n0;
+        e.nn_ntile = min(block_n, cnt[lo] - n0) | ((toff[lo] / m_tiles + nt) << 8);
+        tiles[t] = e;
+    }
+}
+
+__global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t K,
+                                                           uint32_t E, uint32_t shared_rows, GroupInfo gi,
+                                                           TileEntry* __restrict__ gu_tiles, uint32_t gu_max,
+                                                           TileEntry* __restrict__ dn_tiles, uint32_t dn_max,
+                                                           uint32_t* __restrict__ pos_of,
+                                                           uint32_t* __restrict__ row_token,
+                                                           uint32_t* __restrict__ row_assign,
+                                                           uint32_t* __restrict__ err) {
+    __shared__ uint32_t cnt[32][kSmallE];  // per-warp counts, then each warp's base within the expert
+    __shared__ uint32_t gcnt[kSmallE + 2], goff[kSmallE + 2], gut[kSmallE + 2], dnt[kSmallE + 2];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t G = E + (shared_rows ? 1 : 0);
+    for (uint32_t i = threadIdx.x; i < 32 * kSmallE; i += blockDim.x) (&cnt[0][0])[i] = 0;
+    __syncthreads();
+    const uint32_t seg = ceil_div(ceil_div(n, 32u), 32u) * 32u;
+    const uint32_t s0 = warp * seg;
+    const unsigned lt = (1u << lane) - 1u;
+    uint32_t rk[kSmallN / 1024];
+    int32_t bk[kSmallN / 1024];
+#pragma unroll
+    for (uint32_t s = 0; s < kSmallN / 1024; ++s) {
+        const uint32_t i = s0 + s * 32 + lane;
+        int32_t b = -1;
+        if (s * 32 < seg && i < n) {
+            b = ids[i];
+            if (b < 0 || (uint32_t)b >= E) {
+                record_error(err, kErrBadExpert);
+                b = -1;
+            }
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, b);
+        const uint32_t before = b >= 0 ? cnt[warp][b] : 0;
+        __syncwarp();
+        rk[s] = before + __popc(peers & lt);
+        bk[s] = b;
+        if (b >= 0 && (int)(__ffs(peers) - 1) == (int)lane) cnt[warp][b] = before + __popc(peers);
+        __syncwarp();
+    }
+    __syncthreads();
+    // per expert: exclusive prefix over the warps (stable: warp w's
+    // assignments precede warp w + 1's), and the expert's total
+    for (uint32_t b = threadIdx.x; b < E; b += blockDim.x) {
+        uint32_t run = 0;
+        for (uint32_t w = 0; w < 32; ++w) {
+            const uint32_t c = cnt[w][b];
+            cnt[w][b] = run;
+            run += c;
+        }
+        gcnt[b] = run;
+    }
+    if (threadIdx.x == 0 && shared_rows) gcnt[E] = shared_rows;
+    __syncthreads();
+    // exclusive scans over the groups (warp 0, up to 9 groups per lane)
+    if (warp == 0) {
+        const uint32_t per = ceil_div(G, 32u);
+        uint32_t a = 0, bsum = 0, c = 0;
+        for (uint32_t q = 0; q < per; ++q) {
+            const uint32_t g = lane * per + q;
+            if (g < G) {
+                const uint32_t ntn = ceil_div(gcnt[g], gi.block_n);
+                a += gcnt[g];
+                bsum += ntn * gi.gu_row_tiles;
+                c += ntn * gi.dn_row_tiles;
+            }
+        }
+        uint32_t ia = a, ib = bsum, ic = c;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t ya = __shfl_up_sync(0xffffffffu, ia, o);
+            const uint32_t yb = __shfl_up_sync(0xffffffffu, ib, o);
+            const uint32_t yc = __shfl_up_sync(0xffffffffu, ic, o);
+            if ((int)lane >= o) {
+                ia += ya;
+                ib += yb;
+                ic += yc;
+            }
+        }
+        uint32_t ra = ia - a, rb = ib - bsum, rc = ic - c;
+        for (uint32_t q = 0; q < per; ++q) {
+            const uint32_t g = lane * per + q;
+            if (g < G) {
+                const uint32_t ntn = ceil_div(gcnt[g], gi.block_n);
+                goff[g] = ra;
+                gut[g] = rb;
+                dnt[g] = rc;
+                ra += gcnt[g];
+                rb += ntn * gi.gu_row_tiles;
+                rc += ntn * gi.dn_row_tiles;
+            }
+        }
+        if (lane == 31) {
+            goff[G] = ia;
+            gut[G] = ib;
+            dnt[G] = ic;
+        }
+    }
+    __syncthreads();
+    for (uint32_t g = threadIdx.x; g <= G; g += blockDim.x) {
+        if (g < G) gi.count[g] = gcnt[g];
+        gi.offset[g] = goff[g];
+        gi.gu_tile_off[g] = gut[g];
+        gi.dn_tile_off[g] = dnt[g];
+    }
+    // destinations
+#pragma unroll
+    for (uint32_t s = 0; s < kSmallN / 1024; ++s) {
+        const uint32_t i = s0 + s * 32 + lane;
+        const int32_t b = bk[s];
+        if (b >= 0) {
+            const uint32_t pos = goff[b] + cnt[warp][b] + rk[s];
+            pos_of[i] = pos;
+            row_token[pos] = i / K;
+            row_assign[pos] = i;
+        }
+    }
+    for (uint32_t t = threadIdx.x; t < shared_rows; t += blockDim.x) {
+        const uint32_t pos = goff[E] + t;
+        row_token[pos] = t;
+        row_assign[pos] = 0xffffffffu;
+    }
+    if (gu_tiles) fill_tiles(gcnt, goff, gut, G, gi.gu_row_tiles, gi.block_n, gu_tiles, gu_max);
+    if (dn_tiles) fill_tiles(gcnt, goff, dnt, G, gi.dn_row_tiles, gi.block_n, dn_tiles, dn_max);
+}
+
 // Destination of every assignment a = t*K + j, and for every permuted row:
 // its source token and assignment.  Shared-expert rows follow the routed
 // rows in token order.
@@ -415,14 +682,46 @@ __global__ void combine_kernel(const float* __restrict__ yp, uint32_t H, const u
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
+// Tokens per block for router_fused_kernel, or 0 when that kernel does not
+// apply (rows not 16-byte aligned, too many experts for one block's shared
+// memory, or a batch large enough that the tiled kernel's reuse wins).
+static uint32_t router_fused_tb(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H) {
+    if (H % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return 0;
+    if (E == 0 || E > (uint32_t)kRfMaxDots) return 0;
+    uint32_t tb = std::max(1u, ceil_div(T, 148u));
+    tb = std::min(tb, (uint32_t)kRfMaxDots / E);
+    while (tb > 1 && ((uint64_t)(tb + E) * H * 2 + (uint64_t)tb * E * 4) > kRfSmemMax) --tb;
+    if ((uint64_t)(tb + E) * H * 2 + (uint64_t)tb * E * 4 > kRfSmemMax) return 0;
+    if (ceil_div(T, tb) > 4u * 148u) return 0;
+    return tb;
+}
+
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
                           int sigmoid, int norm_topk, float routed_scale, float* logits, int32_t* ids, float* wout,
-                          float* scores, cudaStream_t st) {
+                          float* scores, uint32_t* err, cudaStream_t st, uint32_t* launches) {
     if (T == 0) return cudaSuccess;
+    const uint32_t tb = router_fused_tb(x, w, T, E, H);
+    if (tb) {
+        static uint64_t attr_set = 0;  // one bit per device
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 64 && !((attr_set >> dev) & 1u)) {
+            e = cudaFuncSetAttribute(router_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRfSmemMax);
+            if (e != cudaSuccess) return e;
+            attr_set |= 1ull << dev;
+        }
+        const size_t smem = (size_t)(tb + E) * H * 2 + (size_t)tb * E * 4;
+        router_fused_kernel<<<ceil_div(T, tb), 256, smem, st>>>(x, w, T, E, H, K, tb, sigmoid, norm_topk,
+                                                               routed_scale, logits, ids, wout, scores, err);
+        if (launches) *launches += 1;
+        return cudaGetLastError();
+    }
     dim3 g1(ceil_div(T, kRtTok), ceil_div(E, kRtExp));
     router_logits_kernel<<<g1, 256, 0, st>>>(x, w, T, E, H, logits);
     router_topk_kernel<<<ceil_div(T, 8), 256, 0, st>>>(logits, T, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
                                                        scores);
+    if (launches) *launches += 2;
     return cudaGetLastError();
 }
 
@@ -454,6 +753,17 @@ cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t 
         scatter_kernel<<<ceil_div(total, 256), 256, 0, st>>>(ids, n, K, E, tile_counts, rank, gi, shared_rows,
                                                              pos_of, row_token, row_assign);
     }
+    return cudaGetLastError();
+}
+
+bool route_small_fits(uint32_t n, uint32_t E) { return n <= kSmallN && E <= kSmallE; }
+
+cudaError_t launch_route_small(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
+                               GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max, TileEntry* dn_tiles,
+                               uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token, uint32_t* row_assign,
+                               uint32_t* err, cudaStream_t st) {
+    route_small_kernel<<<1, 1024, 0, st>>>(ids, T * K, K, E, shared_rows, gi, gu_tiles, gu_max, dn_tiles, dn_max,
+                                           pos_of, row_token, row_assign, err);
     return cudaGetLastError();
 }
 

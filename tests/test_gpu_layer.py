@@ -170,3 +170,25 @@ def test_invalid_arguments_fail_cleanly(engine, L, synth):
         engine.forward_host(bad, li.x)
     with pytest.raises(L.MoEError, match="shared"):
         engine.forward_host(L.Engine.cfg(shape, use_shared=True), li.x)
+
+
+@pytest.mark.parametrize("tokens,top_k,experts", [(2048, 4, 8), (2049, 4, 8), (300, 8, 256), (100, 2, 300)],
+                         ids=["n8192_single_block", "n8196_multi_kernel", "e256_single_block", "e300_multi_kernel"])
+@pytest.mark.parametrize("path", [0, 1], ids=["blockscaled", "simt"])
+def test_permutation_paths_match_reference_order(engine, synth, L, port, tokens, top_k, experts, path):
+    """Batches on both sides of the single-block permutation's limits (8192
+    assignments, 256 experts): the permuted order is the reference grouping
+    order and the layer output matches the oracle."""
+    shape = synth.small_shape(hidden=128, intermediate=128, experts=experts, top_k=top_k, tokens=tokens)
+    li = synth.make_layer(shape, seed=5 + tokens + experts)
+    engine.upload_layer(li)
+    out = engine.forward_host(L.Engine.cfg(shape, gemm_path=path), li.x)
+    a = np.arange(tokens * top_k)
+    want = a[np.lexsort((a // top_k, out["ids"].ravel()))]
+    assert np.array_equal(out["perm"], want.astype(np.uint32))
+    counts = engine.read(L.BUF_GROUP_COUNT, (experts,), np.uint32)
+    assert np.array_equal(counts, np.bincount(out["ids"].ravel(), minlength=experts))
+    y_ref, ids, _, _ = port.moe_layer(li)
+    assert np.array_equal(out["ids"], ids)
+    mx, mr = errors(out["y_f32"], y_ref)
+    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
