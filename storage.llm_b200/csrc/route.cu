@@ -226,16 +226,113 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 }
 
 // ---------------------------------------------------------------------------
-// Router for small batches, logits and top-k in one kernel.  A block holds
-// the rows of `tb` tokens and all E router rows in shared memory, brought
-// in by one bulk copy per row before any arithmetic (no staging loop to wait
-// on), computes the tb x E logits with the same 16-chain FMA order as
-// router_logits_kernel, then runs the top-k of its tokens.
+// Scores + top-k of one token for E <= 32 * EPL experts, by one warp, all in
+// registers (expert e = lane + 32 q in slot q).  Same arithmetic and order as
+// topk_token: double exp, the softmax denominator summed in double in expert
+// order (every lane runs the same chain), equal scores to the lower index.
+// Requires K <= 32.
 // ---------------------------------------------------------------------------
-constexpr int kRfMaxDots = 64;          // tb * E per block
+template <int EPL>
+__device__ void topk_token_reg(const float* lg, uint32_t t, uint32_t E, uint32_t K, int sigmoid, int norm_topk,
+                               float routed_scale, int32_t* __restrict__ ids, float* __restrict__ wout,
+                               float* __restrict__ scores_out) {
+    const uint32_t lane = threadIdx.x & 31;
+    const unsigned full = 0xffffffffu;
+    float v[EPL];
+#pragma unroll
+    for (int q = 0; q < EPL; ++q) {
+        const uint32_t e = lane + 32 * q;
+        v[q] = e < E ? lg[e] : 0.f;
+    }
+    if (sigmoid) {
+#pragma unroll
+        for (int q = 0; q < EPL; ++q) {
+            const float ex = (float)exp(-(double)v[q]);
+            v[q] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+        }
+    } else {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < EPL; ++q)
+            if (lane + 32 * q < E) mx = fmaxf(mx, v[q]);
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(full, mx, o));
+#pragma unroll
+        for (int q = 0; q < EPL; ++q) v[q] = (float)exp((double)v[q] - (double)mx);
+        double denom = 0.0;
+#pragma unroll
+        for (int q = 0; q < EPL; ++q) {
+            float all[32];
+#pragma unroll
+            for (int s = 0; s < 32; ++s) all[s] = __shfl_sync(full, v[q], s);
+#pragma unroll
+            for (int s = 0; s < 32; ++s)
+                if (32 * q + s < (int)E) denom = __dadd_rn(denom, (double)all[s]);
+        }
+        const float inv = (float)(1.0 / denom);
+#pragma unroll
+        for (int q = 0; q < EPL; ++q) v[q] = __fmul_rn(v[q], inv);
+    }
+    if (scores_out) {
+#pragma unroll
+        for (int q = 0; q < EPL; ++q)
+            if (lane + 32 * q < E) scores_out[(uint64_t)t * E + lane + 32 * q] = v[q];
+    }
+    uint32_t taken = 0;  // bit q: slot q selected
+    float my_w = 0.f;
+    int my_i = 0;
+    for (uint32_t j = 0; j < K; ++j) {
+        float best = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int q = 0; q < EPL; ++q) {
+            const uint32_t e = lane + 32 * q;
+            if (e < E && !((taken >> q) & 1u) && (bi == 0x7fffffff || v[q] > best)) {
+                best = v[q];
+                bi = (int)e;
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(full, best, o);
+            const int oi = __shfl_xor_sync(full, bi, o);
+            if (oi != 0x7fffffff && (bi == 0x7fffffff || ob > best || (ob == best && oi < bi))) {
+                best = ob;
+                bi = oi;
+            }
+        }
+        if ((uint32_t)(bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (lane == j) {
+            my_w = best;
+            my_i = bi;
+        }
+    }
+    float denom = 0.f;
+    for (uint32_t j = 0; j < K; ++j) denom = __fadd_rn(denom, __shfl_sync(full, my_w, j));
+    if (lane < K) {
+        if (norm_topk && denom <= 0.f) denom = 1e-8f;
+        const float scale = sigmoid ? routed_scale : 1.0f;
+        float wv = my_w;
+        if (norm_topk) wv = __fdiv_rn(wv, denom);
+        if (scale != 1.0f) wv = __fmul_rn(wv, scale);
+        ids[(uint64_t)t * K + lane] = my_i;
+        wout[(uint64_t)t * K + lane] = wv;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Router for small batches, logits and top-k in one kernel.  A block holds
+// the rows of `tb` tokens and all E <= 64 router rows in shared memory (row
+// pitch 2H + 32 bytes, so the rows a warp reads fall in different banks),
+// brought in by one bulk copy per row before any arithmetic.  Eight threads
+// per (token, expert) dot product: thread m owns the reference's FMA chains
+// 2m and 2m + 1 (elements 16 i + 2m, 16 i + 2m + 1, one 4-byte load per
+// operand), so the 16-chain order of router_logits_kernel is kept exactly.
+// Then one warp per token runs the top-k.
+// ---------------------------------------------------------------------------
+constexpr int kRfMaxDots = 64;          // tb * E per block (8 threads each, 512 threads)
+constexpr int kRfMaxE = 64;
 constexpr uint32_t kRfSmemMax = 200 * 1024;
 
-__global__ void __launch_bounds__(256) router_fused_kernel(const uint16_t* __restrict__ x,
+__global__ void __launch_bounds__(512) router_fused_kernel(const uint16_t* __restrict__ x,
                                                            const uint16_t* __restrict__ w, uint32_t T, uint32_t E,
                                                            uint32_t H, uint32_t K, uint32_t tb, int sigmoid,
                                                            int norm_topk, float routed_scale,
@@ -244,10 +341,11 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const uint16_t* __res
                                                            uint32_t* __restrict__ err) {
     extern __shared__ __align__(16) uint8_t rf_smem[];
     __shared__ uint64_t bar;
-    uint16_t* xs = reinterpret_cast<uint16_t*>(rf_smem);  // [tb][H]
-    uint16_t* ws = xs + (size_t)tb * H;                    // [E][H]
-    float* lg = reinterpret_cast<float*>(ws + (size_t)E * H);  // [tb][E]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t pitch = H * 2 + 32;  // bytes per staged row
+    uint8_t* xs = rf_smem;                               // [tb] rows
+    uint8_t* ws = rf_smem + (size_t)tb * pitch;          // [E] rows
+    float* lg = reinterpret_cast<float*>(ws + (size_t)E * pitch);  // [tb][E]
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t t0 = blockIdx.x * tb;
     const uint32_t nt = min(tb, T - t0);
     if (threadIdx.x == 0) {
@@ -261,65 +359,69 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const uint16_t* __res
         __syncwarp();
         for (uint32_t r = lane; r < nt + E; r += 32) {
             if (r < nt) {
-                bulk_g2s(xs + (size_t)r * H, x + (uint64_t)(t0 + r) * H, rowb, &bar);
+                bulk_g2s(xs + (size_t)r * pitch, x + (uint64_t)(t0 + r) * H, rowb, &bar);
             } else {
-                bulk_g2s(ws + (size_t)(r - nt) * H, w + (uint64_t)(r - nt) * H, rowb, &bar);
+                bulk_g2s(ws + (size_t)(r - nt) * pitch, w + (uint64_t)(r - nt) * H, rowb, &bar);
             }
         }
     }
     const bool ok = mbar_wait(&bar, 0, err, kErrTimeoutLoadFull);
     if (!__syncthreads_and(ok)) return;
 
-    const int l = threadIdx.x & 15;
-    const uint32_t half = (threadIdx.x >> 4) & 1;
+    const uint32_t m = threadIdx.x & 7;
+    const uint32_t d = threadIdx.x >> 3;  // dot: token d / E, expert d % E
     const uint32_t ndots = nt * E;
+    const uint32_t dv = d < ndots ? d : 0;  // idle threads shadow dot 0 (the shuffles span 8 lanes)
+    const uint8_t* xr = xs + (size_t)(dv / E) * pitch;
+    const uint8_t* wr = ws + (size_t)(dv % E) * pitch;
     const uint32_t main_end = H & ~15u;
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
+    for (uint32_t i = 0; i < main_end; i += 16) {
+        const uint32_t xv = *reinterpret_cast<const uint32_t*>(xr + (i + 2 * m) * 2);
+        const uint32_t wv = *reinterpret_cast<const uint32_t*>(wr + (i + 2 * m) * 2);
+        a0 = __fmaf_rn(__uint_as_float(wv << 16), __uint_as_float(xv << 16), a0);
+        a1 = __fmaf_rn(__uint_as_float(wv & 0xffff0000u), __uint_as_float(xv & 0xffff0000u), a1);
+    }
+    // b_c = s_c + s_{c+8} (chains c = 2m + q, m < 4), then ((b0 + b1) + b2) + ... + b7
     const unsigned full = 0xffffffffu;
-    // a warp's two 16-lane groups take dots [base, base + 8) together, so
-    // both run the same number of iterations (the shuffles span the warp)
-    for (uint32_t base = warp * 8; base < ndots; base += 64) {
-        const uint16_t* xr[4];
-        const uint16_t* wr[4];
-        uint32_t dd[4];
+    const float b0 = a0 + __shfl_down_sync(full, a0, 4, 8);
+    const float b1 = a1 + __shfl_down_sync(full, a1, 4, 8);
+    float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            dd[j] = base + half * 4 + j;
-            const uint32_t d = dd[j] < ndots ? dd[j] : 0;
-            xr[j] = xs + (size_t)(d / E) * H;
-            wr[j] = ws + (size_t)(d % E) * H;
+    for (int q = 0; q < 4; ++q) {
+        const float c0 = __shfl_sync(full, b0, q, 8);
+        const float c1 = __shfl_sync(full, b1, q, 8);
+        s = q == 0 ? __fadd_rn(c0, c1) : __fadd_rn(__fadd_rn(s, c0), c1);
+    }
+    if (m == 0 && d < ndots) {
+        const uint16_t* xe = reinterpret_cast<const uint16_t*>(xr);
+        const uint16_t* we = reinterpret_cast<const uint16_t*>(wr);
+        float out = 0.0f + s;
+        uint32_t i = main_end;
+        float t0a = 0.f, t1a = 0.f, t2a = 0.f, t3a = 0.f;
+        for (; i + 3 < H; i += 4) {
+            t0a = __fmaf_rn(bf16_bits_to_f32(we[i]), bf16_bits_to_f32(xe[i]), t0a);
+            t1a = __fmaf_rn(bf16_bits_to_f32(we[i + 1]), bf16_bits_to_f32(xe[i + 1]), t1a);
+            t2a = __fmaf_rn(bf16_bits_to_f32(we[i + 2]), bf16_bits_to_f32(xe[i + 2]), t2a);
+            t3a = __fmaf_rn(bf16_bits_to_f32(we[i + 3]), bf16_bits_to_f32(xe[i + 3]), t3a);
         }
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (uint32_t i = l; i < main_end; i += 16) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) acc[j] = __fmaf_rn(bf16_bits_to_f32(wr[j][i]), bf16_bits_to_f32(xr[j][i]), acc[j]);
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float hi = __shfl_down_sync(full, acc[j], 8, 16);
-            const float bl = acc[j] + hi;  // valid on lanes 0..7
-            float s = __shfl_sync(full, bl, 0, 16);
-#pragma unroll
-            for (int q = 1; q < 8; ++q) s = __fadd_rn(s, __shfl_sync(full, bl, q, 16));
-            if (l == 0 && dd[j] < ndots) {
-                float out = 0.0f + s;
-                uint32_t i = main_end;
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                for (; i + 3 < H; i += 4) {
-                    a0 = __fmaf_rn(bf16_bits_to_f32(wr[j][i]), bf16_bits_to_f32(xr[j][i]), a0);
-                    a1 = __fmaf_rn(bf16_bits_to_f32(wr[j][i + 1]), bf16_bits_to_f32(xr[j][i + 1]), a1);
-                    a2 = __fmaf_rn(bf16_bits_to_f32(wr[j][i + 2]), bf16_bits_to_f32(xr[j][i + 2]), a2);
-                    a3 = __fmaf_rn(bf16_bits_to_f32(wr[j][i + 3]), bf16_bits_to_f32(xr[j][i + 3]), a3);
-                }
-                out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
-                for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[j][i]), bf16_bits_to_f32(xr[j][i]), out);
-                lg[dd[j]] = out;
-                logits[(uint64_t)t0 * E + dd[j]] = out;
-            }
-        }
+        out = __fadd_rn(out, __fadd_rn(__fadd_rn(t0a, t1a), __fadd_rn(t2a, t3a)));
+        for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(we[i]), bf16_bits_to_f32(xe[i]), out);
+        lg[d] = out;
+        logits[(uint64_t)t0 * E + d] = out;
     }
     __syncthreads();
-    for (uint32_t tt = warp; tt < nt; tt += 8) {
-        topk_token(lg + (size_t)tt * E, t0 + tt, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores);
+    for (uint32_t tt = warp; tt < nt; tt += 16) {
+        if (E <= 32 && K <= 32) {
+            topk_token_reg<1>(lg + (size_t)tt * E, t0 + tt, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
+                              scores);
+        } else if (K <= 32) {
+            topk_token_reg<2>(lg + (size_t)tt * E, t0 + tt, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
+                              scores);
+        } else {
+            topk_token(lg + (size_t)tt * E, t0 + tt, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores);
+        }
     }
 }
 
@@ -687,11 +789,12 @@ __global__ void combine_kernel(const float* __restrict__ yp, uint32_t H, const u
 // memory, or a batch large enough that the tiled kernel's reuse wins).
 static uint32_t router_fused_tb(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H) {
     if (H % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return 0;
-    if (E == 0 || E > (uint32_t)kRfMaxDots) return 0;
+    if (E == 0 || E > (uint32_t)kRfMaxE) return 0;
+    auto smem = [&](uint32_t tb) { return (uint64_t)(tb + E) * (H * 2 + 32) + (uint64_t)tb * E * 4; };
     uint32_t tb = std::max(1u, ceil_div(T, 148u));
     tb = std::min(tb, (uint32_t)kRfMaxDots / E);
-    while (tb > 1 && ((uint64_t)(tb + E) * H * 2 + (uint64_t)tb * E * 4) > kRfSmemMax) --tb;
-    if ((uint64_t)(tb + E) * H * 2 + (uint64_t)tb * E * 4 > kRfSmemMax) return 0;
+    while (tb > 1 && smem(tb) > kRfSmemMax) --tb;
+    if (smem(tb) > kRfSmemMax) return 0;
     if (ceil_div(T, tb) > 4u * 148u) return 0;
     return tb;
 }
@@ -711,8 +814,8 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
             if (e != cudaSuccess) return e;
             attr_set |= 1ull << dev;
         }
-        const size_t smem = (size_t)(tb + E) * H * 2 + (size_t)tb * E * 4;
-        router_fused_kernel<<<ceil_div(T, tb), 256, smem, st>>>(x, w, T, E, H, K, tb, sigmoid, norm_topk,
+        const size_t smem = (size_t)(tb + E) * (H * 2 + 32) + (size_t)tb * E * 4;
+        router_fused_kernel<<<ceil_div(T, tb), 512, smem, st>>>(x, w, T, E, H, K, tb, sigmoid, norm_topk,
                                                                routed_scale, logits, ids, wout, scores, err);
         if (launches) *launches += 1;
         return cudaGetLastError();
