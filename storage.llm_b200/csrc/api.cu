@@ -544,7 +544,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         CK(launch_route_small(ids, T, K, E, shared_rows, gi, bs ? eng->gu_tiles.as<TileEntry>() : nullptr,
                               token_tiles * (L->rp_i / 128), bs ? eng->dn_tiles.as<TileEntry>() : nullptr,
                               token_tiles * (L->rp_h / 128), eng->pos_of.as<uint32_t>(),
-                              eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(), errw, st));
+                              eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(), errw, st, true));
         launches += 1;
     } else {
         CK(launch_permute(ids, T, K, E, shared_rows, eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi,
@@ -565,7 +565,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         const uint64_t xb_rows = eng->xb.bytes / (2ull * Kq), hb_rows = eng->hb.bytes / (2ull * Iq);
         CK(launch_gather_quant_bs(x, H, Kq, eng->row_token.as<uint32_t>(), P, (uint32_t)xb_rows, gi.offset,
                                   gi.gu_tile_off, G, L->rp_i / 128, block_n, eng->xb.as<uint8_t>(),
-                                  eng->sfx_atoms.as<uint8_t>(), st));
+                                  eng->sfx_atoms.as<uint8_t>(), st, true));
         launches += 1;
         mark(3);
         BsParams bp{};
@@ -588,7 +588,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         bp.sfh_atoms = eng->sfh_atoms.as<uint8_t>();
         bp.m_valid = Iq;
         const int bi = block_n == 32 ? 0 : 1;
-        CK(launch_gemm_bs(kGateUp, (int)block_n, L->tmap_gu_codes, eng->tmap_xb[bi], bp, eng->num_sms, st));
+        CK(launch_gemm_bs(kGateUp, (int)block_n, L->tmap_gu_codes, eng->tmap_xb[bi], bp, eng->num_sms, st, true));
         launches += 1;
         mark(4);
         // down: K = I (padded Iq), M = H rows (padded rp_h), output fp32 rows
@@ -603,7 +603,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         bp.y_out = eng->yperm.as<float>();
         bp.y_stride = H;
         bp.m_valid = H;
-        CK(launch_gemm_bs(kDown, (int)block_n, L->tmap_dn_codes, eng->tmap_hb[bi], bp, eng->num_sms, st));
+        CK(launch_gemm_bs(kDown, (int)block_n, L->tmap_dn_codes, eng->tmap_hb[bi], bp, eng->num_sms, st, true));
         launches += 1;
         mark(5);
     } else {
@@ -649,7 +649,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     }
 
     CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), w, T, K, shared ? 1 : 0, n, y_bf16,
-                      y_f32, st));
+                      y_f32, st, bs));
     launches += 1;
     mark(6);
     if (perm) {

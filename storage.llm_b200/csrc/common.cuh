@@ -4,6 +4,8 @@
 // geometry.
 #pragma once
 
+#include <utility>
+
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -116,6 +118,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
             return false;
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor in the
+// stream still runs; pdl_wait() blocks the calling thread until the
+// predecessor grid has completed and its writes are visible.  pdl_trigger()
+// lets this grid's own dependent launch early.  Both are no-ops for a
+// kernel launched the ordinary way.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... Exp, typename... Act>
+inline cudaError_t launch_kernel(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 bool pdl, Act&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl ? attr : nullptr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
 }
 
 // ---------------------------------------------------------------------------

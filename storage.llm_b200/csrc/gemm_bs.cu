@@ -137,6 +137,10 @@ __global__ void __launch_bounds__(256) gather_quant_bs_kernel(
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t nkt = Kp / 128;
     const uint64_t tasks = (uint64_t)rows * nkt;
+    // the permutation first; only then may the gate/up GEMM launch (its
+    // prologue reads the tile table the permutation wrote)
+    pdl_wait();
+    pdl_trigger();
     const uint64_t xplane = (uint64_t)rows_cap * Kp;
     const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     for (uint64_t task = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; task < tasks; task += warps) {
@@ -237,18 +241,16 @@ cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, 
 cudaError_t launch_gather_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token,
                                    uint32_t rows, uint32_t rows_cap, const uint32_t* offset, const uint32_t* tile_off,
                                    uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* xb, uint8_t* sf_atoms,
-                                   cudaStream_t st) {
+                                   cudaStream_t st, bool pdl) {
     if (rows == 0) return cudaSuccess;
     const uint64_t tasks = (uint64_t)rows * (Kp / 128);
     const uint32_t blocks = (uint32_t)std::min<uint64_t>((tasks + 7) / 8, 148ull * 8ull);
     if (block_n == 32) {
-        gather_quant_bs_kernel<32><<<blocks, 256, 0, st>>>(x, H, Kp, row_token, rows, rows_cap, offset, tile_off,
-                                                           groups, m_tiles, xb, sf_atoms);
-    } else {
-        gather_quant_bs_kernel<128><<<blocks, 256, 0, st>>>(x, H, Kp, row_token, rows, rows_cap, offset, tile_off,
-                                                            groups, m_tiles, xb, sf_atoms);
+        return launch_kernel(gather_quant_bs_kernel<32>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, row_token,
+                             rows, rows_cap, offset, tile_off, groups, m_tiles, xb, sf_atoms);
     }
-    return cudaGetLastError();
+    return launch_kernel(gather_quant_bs_kernel<128>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, row_token, rows,
+                         rows_cap, offset, tile_off, groups, m_tiles, xb, sf_atoms);
 }
 
 // ---------------------------------------------------------------------------
@@ -345,6 +347,11 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    // The tile table and weights were ready before this grid launched (the
+    // previous kernel triggers only after its own wait); the activations
+    // (B and its scales) come from the previous kernel and are read only
+    // after pdl_wait() in the producer.
+    pdl_trigger();
     const uint32_t total = p.tile_off[p.groups];
     constexpr uint32_t kSfCol0 = 256;
 
@@ -353,6 +360,27 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         if (lane == 0) {
             uint32_t stage = 0, phase = 0;
             bool ok = true;
+            // weights of the first tile's first stages before waiting for the
+            // previous kernel: they do not depend on it
+            uint32_t pre = 0;
+            if (blockIdx.x < total) {
+                const BsTileX tc = load_tile(p, blockIdx.x);
+                const uint64_t ablk0 = ((uint64_t)tc.g * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
+                const uint64_t sblk0 = ((uint64_t)tc.g * p.m_tiles + tc.mt) * p.k_tiles;
+                pre = min((uint32_t)C::kStages, p.k_tiles);
+                for (uint32_t kt = 0; kt < pre; ++kt) {
+                    uint8_t* sf = sf_base + kt * C::kSFStage;
+                    mbar_arrive_expect_tx(&load_full[kt], C::kNA * C::kATx + C::kSFStage + 2 * C::kBBytes);
+                    bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, &load_full[kt]);
+#pragma unroll
+                    for (int pj = 0; pj < C::kNA; ++pj) {
+                        const uint64_t b = ablk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt;
+                        tma_load_2d(a_base + (kt * C::kNA + pj) * C::kABytes, &tmap_a, 0, (int32_t)(b * 128),
+                                    &load_full[kt]);
+                    }
+                }
+            }
+            pdl_wait();
             for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
                 const BsTileX tc = load_tile(p, tile);
                 const uint64_t ablk0 = ((uint64_t)tc.g * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
@@ -360,13 +388,16 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
                     if (!(ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty))) break;
                     uint8_t* sf = sf_base + stage * C::kSFStage;
-                    mbar_arrive_expect_tx(&load_full[stage],
-                                          C::kNA * C::kATx + C::kSFStage + 2 * C::kBBytes);
-                    bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, &load_full[stage]);
+                    const bool prefetched = tile == blockIdx.x && kt < pre;
+                    if (!prefetched) {
+                        mbar_arrive_expect_tx(&load_full[stage], C::kNA * C::kATx + C::kSFStage + 2 * C::kBBytes);
+                        bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, &load_full[stage]);
+                    }
                     bulk_g2s(sf + C::kSFA, p.sfb_atoms + ((uint64_t)tc.ntile * p.k_tiles + kt) * C::kSFB, C::kSFB,
                              &load_full[stage]);
 #pragma unroll
                     for (int pj = 0; pj < C::kNA; ++pj) {
+                        if (prefetched) break;
                         const uint64_t b = ablk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt;  // weight block
                         tma_load_2d(a_base + (stage * C::kNA + pj) * C::kABytes, &tmap_a, 0, (int32_t)(b * 128),
                                     &load_full[stage]);
@@ -553,7 +584,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
 
 template <int MODE, int BN>
 static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p, int num_sms,
-                                  cudaStream_t st) {
+                                  cudaStream_t st, bool pdl) {
     using C = BsCfg<MODE, BN>;
     static uint64_t attr_set = 0;  // one bit per device
     int dev = 0;
@@ -564,18 +595,17 @@ static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, 
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
     }
-    gemm_bs_kernel<MODE, BN><<<num_sms, 320, C::kSmem, st>>>(ta, tb, p);
-    return cudaGetLastError();
+    return launch_kernel(gemm_bs_kernel<MODE, BN>, dim3(num_sms), dim3(320), C::kSmem, st, pdl, ta, tb, p);
 }
 
 cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
-                           int num_sms, cudaStream_t st) {
+                           int num_sms, cudaStream_t st, bool pdl) {
     if (mode == kGateUp) {
-        return block_n == 32 ? launch_bs_mode<kGateUp, 32>(ta, tb, p, num_sms, st)
-                             : launch_bs_mode<kGateUp, 128>(ta, tb, p, num_sms, st);
+        return block_n == 32 ? launch_bs_mode<kGateUp, 32>(ta, tb, p, num_sms, st, pdl)
+                             : launch_bs_mode<kGateUp, 128>(ta, tb, p, num_sms, st, pdl);
     }
-    return block_n == 32 ? launch_bs_mode<kDown, 32>(ta, tb, p, num_sms, st)
-                         : launch_bs_mode<kDown, 128>(ta, tb, p, num_sms, st);
+    return block_n == 32 ? launch_bs_mode<kDown, 32>(ta, tb, p, num_sms, st, pdl)
+                         : launch_bs_mode<kDown, 128>(ta, tb, p, num_sms, st, pdl);
 }
 
 }  // namespace moe_b200

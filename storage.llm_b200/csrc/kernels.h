@@ -88,7 +88,7 @@ bool route_small_fits(uint32_t n, uint32_t E);
 cudaError_t launch_route_small(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
                                GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max, TileEntry* dn_tiles,
                                uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token, uint32_t* row_assign,
-                               uint32_t* err, cudaStream_t st);
+                               uint32_t* err, cudaStream_t st, bool pdl);
 // Generic pieces of the stable counting sort, used by the grouping utility.
 struct AssignRec {
     uint32_t token_index, layer, expert;
@@ -107,7 +107,7 @@ cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint
                           uint16_t* xp, cudaStream_t st);
 cudaError_t launch_combine(const float* yp, uint32_t H, const uint32_t* pos_of, const float* w, uint32_t T,
                            uint32_t K, int has_shared, uint32_t shared_off, uint16_t* y_bf16, float* y_f32,
-                           cudaStream_t st);
+                           cudaStream_t st, bool pdl);
 
 // tcgen05 grouped GEMMs (gemm_tc.cu).  `tmap_b` covers the permuted
 // activation rows [rows x Kp] bf16 with a 64 x block_n box, 128-byte swizzle.
@@ -115,6 +115,9 @@ constexpr uint32_t kBlockN = 128;
 cudaError_t launch_gemm_tc(int mode, const CUtensorMap& tmap_b, const GemmParams& p, int num_sms,
                            cudaStream_t st);
 // Block-scaled tcgen05 grouped GEMMs (gemm_bs.cu) and their data preparation.
+// Launchers taking `pdl` launch with programmatic stream serialization: the
+// kernel may start while its predecessor drains and waits (griddepcontrol)
+// before reading what the predecessor wrote.
 cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, uint32_t rows_pad, uint32_t Kp,
                              uint8_t* codes, uint8_t* sfa, uint32_t sf_stride, cudaStream_t st);
 // xb [2][rows_cap][Kp]: permuted rows of x as exact hi/lo E4M3 terms; their
@@ -122,13 +125,13 @@ cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, 
 cudaError_t launch_gather_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token,
                                    uint32_t rows, uint32_t rows_cap, const uint32_t* offset, const uint32_t* tile_off,
                                    uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* xb, uint8_t* sf_atoms,
-                                   cudaStream_t st);
+                                   cudaStream_t st, bool pdl);
 cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, const uint32_t* tile_off,
                                uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint32_t max_tiles,
                                TileEntry* tiles, cudaStream_t st);
 // `tb` is a 3-D map over [2][rows][K] E4M3 bytes with a {128, block_n, 2} box.
 cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
-                           int num_sms, cudaStream_t st);
+                           int num_sms, cudaStream_t st, bool pdl);
 
 // CUDA-core grouped GEMMs used only to cross-check the tcgen05 kernels.
 cudaError_t launch_gemm_simt(int mode, const uint16_t* b, uint32_t b_stride, uint32_t rows, const GemmParams& p,

@@ -348,6 +348,7 @@ __global__ void __launch_bounds__(512) router_fused_kernel(const uint16_t* __res
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t t0 = blockIdx.x * tb;
     const uint32_t nt = min(tb, T - t0);
+    pdl_trigger();  // the permutation kernel may launch now; it waits for the ids
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         fence_mbar_init();
@@ -596,6 +597,8 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __rest
     __shared__ uint32_t gcnt[kSmallE + 2], goff[kSmallE + 2], gut[kSmallE + 2], dnt[kSmallE + 2];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t G = E + (shared_rows ? 1 : 0);
+    pdl_wait();  // the router's ids
+    pdl_trigger();
     for (uint32_t i = threadIdx.x; i < 32 * kSmallE; i += blockDim.x) (&cnt[0][0])[i] = 0;
     __syncthreads();
     const uint32_t seg = ceil_div(ceil_div(n, 32u), 32u) * 32u;
@@ -751,6 +754,7 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, uint32_t H, u
 __global__ void combine_kernel(const float* __restrict__ yp, uint32_t H, const uint32_t* __restrict__ pos_of,
                                const float* __restrict__ w, uint32_t T, uint32_t K, int has_shared,
                                uint32_t shared_off, uint16_t* __restrict__ y_bf16, float* __restrict__ y_f32) {
+    pdl_wait();  // the down GEMM's rows
     for (uint32_t t = blockIdx.y; t < T; t += gridDim.y)
     for (uint32_t h4 = blockIdx.x * blockDim.x + threadIdx.x; h4 * 4 < H; h4 += gridDim.x * blockDim.x) {
         const uint32_t h = h4 * 4;
@@ -864,10 +868,9 @@ bool route_small_fits(uint32_t n, uint32_t E) { return n <= kSmallN && E <= kSma
 cudaError_t launch_route_small(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
                                GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max, TileEntry* dn_tiles,
                                uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token, uint32_t* row_assign,
-                               uint32_t* err, cudaStream_t st) {
-    route_small_kernel<<<1, 1024, 0, st>>>(ids, T * K, K, E, shared_rows, gi, gu_tiles, gu_max, dn_tiles, dn_max,
-                                           pos_of, row_token, row_assign, err);
-    return cudaGetLastError();
+                               uint32_t* err, cudaStream_t st, bool pdl) {
+    return launch_kernel(route_small_kernel, dim3(1), dim3(1024), 0, st, pdl, ids, T * K, K, E, shared_rows, gi,
+                         gu_tiles, gu_max, dn_tiles, dn_max, pos_of, row_token, row_assign, err);
 }
 
 cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token, uint32_t rows,
@@ -880,12 +883,12 @@ cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint
 
 cudaError_t launch_combine(const float* yp, uint32_t H, const uint32_t* pos_of, const float* w, uint32_t T,
                            uint32_t K, int has_shared, uint32_t shared_off, uint16_t* y_bf16, float* y_f32,
-                           cudaStream_t st) {
+                           cudaStream_t st, bool pdl) {
     if (T == 0) return cudaSuccess;
     const uint32_t threads = 128;
     dim3 grid(ceil_div(ceil_div(H, 4), threads), min(T, 65535u));
-    combine_kernel<<<grid, threads, 0, st>>>(yp, H, pos_of, w, T, K, has_shared, shared_off, y_bf16, y_f32);
-    return cudaGetLastError();
+    return launch_kernel(combine_kernel, grid, dim3(threads), 0, st, pdl, yp, H, pos_of, w, T, K, has_shared,
+                         shared_off, y_bf16, y_f32);
 }
 
 }  // namespace moe_b200
