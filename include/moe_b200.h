@@ -176,6 +176,43 @@ MOE_B200_API int moe_b200_group_tokens_by_expert_noalloc(const moe_b200_assignme
                                                          moe_b200_batch_t* out_batches, uint32_t max_batches,
                                                          uint32_t* out_batch_count, char* err);
 
+/* ------------------------------------------------------------------------
+ * Expert parallelism over GPUs (one process and one engine per GPU).
+ * Replaces the reference's single-process expert loop
+ * (generation_mlp.cpp.inc:1023-1431) when the experts are spread over
+ * several devices; the reference has no multi-device counterpart.
+ *
+ * Rank r of `world` owns experts [r*E/world, (r+1)*E/world) (E must split
+ * evenly); the router and the shared expert are replicated and each rank
+ * feeds its own tokens.  Every rank uploads the router, its own experts and
+ * (if used) the shared expert, then all ranks call
+ * moe_b200_ep_layer_forward together.  The exchange uses NCCL, opened at
+ * run time (libnccl.so.2); the call synchronises its stream once, after the
+ * per-rank row counts are exchanged, to size the row exchange.
+ * ------------------------------------------------------------------------ */
+#define MOE_B200_EP_UID_BYTES 128
+/* A fresh communicator id (ncclGetUniqueId); create it on one rank and
+ * hand the bytes to every rank. */
+MOE_B200_API int moe_b200_ep_unique_id(uint8_t* out_uid, char* err);
+/* Joins the communicator (collective over all `world` ranks). */
+MOE_B200_API int moe_b200_ep_init(moe_b200_engine_t* engine, int rank, int world, const uint8_t* uid, char* err);
+/* This rank's expert block for a layer of `experts` experts. */
+MOE_B200_API int moe_b200_ep_local_experts(moe_b200_engine_t* engine, uint32_t experts, uint32_t* first,
+                                           uint32_t* count, char* err);
+/* The layer on this rank's T tokens (device pointers, caller's stream; the
+ * same outputs as moe_b200_layer_forward for those tokens).  Block-scaled
+ * GEMM path only.  T may be 0 (the rank still serves its experts). */
+MOE_B200_API int moe_b200_ep_layer_forward(moe_b200_engine_t* engine, const moe_b200_layer_cfg_t* cfg,
+                                           const uint16_t* x_bf16, uint32_t tokens, uint16_t* y_bf16, float* y_f32,
+                                           int32_t* topk_ids, float* topk_w, void* stream, char* err);
+/* Host-pointer variant (copies in, runs, copies out, synchronises). */
+MOE_B200_API int moe_b200_ep_layer_forward_host(moe_b200_engine_t* engine, const moe_b200_layer_cfg_t* cfg,
+                                                const uint16_t* x_bf16, uint32_t tokens, uint16_t* y_bf16,
+                                                float* y_f32, int32_t* topk_ids, float* topk_w, char* err);
+/* Rows this rank sent to / received from each rank in its last call
+ * (arrays of `world` entries): the load balance of the exchange. */
+MOE_B200_API int moe_b200_ep_last_counts(moe_b200_engine_t* engine, uint32_t* sent, uint32_t* received, char* err);
+
 /* Test and diagnostics hooks (no reference counterpart). */
 enum {
     MOE_B200_PROJ_GATE = 0,

@@ -4,7 +4,8 @@
 
 The library is the product: the C ABI of include/moe_b200.h.  It links only
 the CUDA runtime (the driver's tensor-map encoder is fetched at run time with
-cudaGetDriverEntryPoint), so it loads on any host with the NVIDIA driver.
+cudaGetDriverEntryPoint, NCCL for the expert-parallel entry points is opened
+with dlopen), so it loads on any host with the NVIDIA driver.
 """
 from __future__ import annotations
 
@@ -18,7 +19,8 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OBJ = HERE / "_build"
 LIB = HERE / "libmoe_b200.so"
-SOURCES = ["api.cu", "route.cu", "repack.cu", "gemm_tc.cu", "gemm_simt.cu", "group.cu", "group_noalloc.cu", "gemm_bs.cu"]
+SOURCES = ["api.cu", "route.cu", "repack.cu", "gemm_tc.cu", "gemm_simt.cu", "group.cu", "group_noalloc.cu", "gemm_bs.cu",
+           "ep.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -33,7 +35,7 @@ def flags(debug: bool) -> list[str]:
 def compile_one(src: str, debug: bool) -> Path:
     out = OBJ / (Path(src).stem + ".o")
     srcp = CSRC / src
-    deps = [srcp, CSRC / "common.cuh", CSRC / "kernels.h", HERE.parent / "include" / "moe_b200.h"]
+    deps = [srcp, CSRC / "common.cuh", CSRC / "kernels.h", CSRC / "engine.h", HERE.parent / "include" / "moe_b200.h"]
     if out.exists() and all(out.stat().st_mtime >= d.stat().st_mtime for d in deps):
         return out
     cmd = [NVCC] + flags(debug) + ["-c", str(srcp), "-o", str(out)]
@@ -53,7 +55,7 @@ def build(debug: bool = False) -> Path:
     if LIB.exists() and all(LIB.stat().st_mtime >= o.stat().st_mtime for o in objs):
         return LIB
     # static CUDA runtime: the library needs only the driver at run time
-    cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", str(LIB)] + [str(o) for o in objs]
+    cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", str(LIB)] + [str(o) for o in objs] + ["-ldl"]
     subprocess.run(cmd, check=True)
     return LIB
 

@@ -2,8 +2,7 @@
 // device weight cache, workspace and the per-layer launch sequence
 //   router -> permute (count/scan/scatter) -> gather -> gate/up GEMM ->
 //   down GEMM -> combine
-// all enqueued on the caller's stream with no host synchronisation, so the
-// sequence can be captured in a CUDA graph.
+// all enqueued on the caller's stream with no host synchronisation.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -16,118 +15,12 @@
 #include <new>
 #include <vector>
 
-#include "../../include/moe_b200.h"
-#include "common.cuh"
-#include "kernels.h"
+#include "engine.h"
 
 using namespace moe_b200;
 
-namespace {
 
-void set_err(char* err, const char* fmt, ...) {
-    if (!err) return;
-    va_list ap;
-    va_start(ap, fmt);
-    vsnprintf(err, MOE_B200_ERR_LEN, fmt, ap);
-    va_end(ap);
-}
-
-#define CK(call)                                                                                   \
-    do {                                                                                           \
-        cudaError_t e_ = (call);                                                                   \
-        if (e_ != cudaSuccess) {                                                                   \
-            set_err(err, "%s failed: %s", #call, cudaGetErrorString(e_));                          \
-            return 0;                                                                              \
-        }                                                                                          \
-    } while (0)
-
-// Device buffer that only grows.
-struct DevBuf {
-    void* ptr = nullptr;
-    size_t bytes = 0;
-    cudaError_t reserve(size_t want) {
-        if (want <= bytes) return cudaSuccess;
-        if (ptr) cudaFree(ptr);
-        ptr = nullptr;
-        bytes = 0;
-        cudaError_t e = cudaMalloc(&ptr, want);
-        if (e == cudaSuccess) bytes = want;
-        return e;
-    }
-    void release() {
-        if (ptr) cudaFree(ptr);
-        ptr = nullptr;
-        bytes = 0;
-    }
-    template <class T>
-    T* as() const {
-        return static_cast<T*>(ptr);
-    }
-};
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-struct LayerWeights {
-    uint32_t E = 0, H = 0, I = 0;
-    DevBuf router;          // bf16 [E x H]
-    DevBuf gu;              // [E+1] groups of interleaved gate/up tiles
-    DevBuf dn;              // [E+1] groups of down tiles
-    uint64_t gu_stride = 0, dn_stride = 0;
-    std::vector<uint8_t> present;  // [E+1]; slot E = shared expert
-    // block-scaled form: packed E2M1 codes + E8M0 scale blocks
-    DevBuf bs_gu_codes, bs_gu_sfa, bs_dn_codes, bs_dn_sfa;
-    uint32_t rp_i = 0, rp_h = 0, kq = 0, iq = 0;  // rows padded to 128, K padded to 128
-    CUtensorMap tmap_gu_codes{}, tmap_dn_codes{};
-    void release_all() {
-        router.release();
-        gu.release();
-        dn.release();
-        bs_gu_codes.release();
-        bs_gu_sfa.release();
-        bs_dn_codes.release();
-        bs_dn_sfa.release();
-    }
-};
-
-uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
-
-}  // namespace
-
-struct moe_b200_engine {
-    int device = 0;
-    int num_sms = 148;
-    std::vector<LayerWeights> layers;
-    DevBuf staging;  // GGUF bytes copied from the host before the repack
-    // workspace
-    DevBuf logits, scores, ids, wts, tile_counts, rank, pos_of, row_token, row_assign;
-    DevBuf g_count, g_offset, g_gu_off, g_dn_off;
-    DevBuf xperm, hperm, yperm;
-    DevBuf err_word;
-    // block-scaled path: quantised activations and intermediate
-    // (xb, hb hold a hi plane followed by a lo plane)
-    DevBuf xb, sfx_atoms, hb, sfh_atoms, gu_tiles, dn_tiles;
-    // 3-D maps over xb / hb: [0] 32-token box, [1] 128-token box
-    CUtensorMap tmap_xb[2]{}, tmap_hb[2]{};
-    const void* bs_map_key[2] = {nullptr, nullptr};
-    uint64_t bs_map_dims[2][2] = {};
-    // host-call staging
-    DevBuf hx, hy, hyf, hids, hw, hperm_out, tri;
-    CUtensorMap tmap_x{}, tmap_h{};
-    void* tmap_x_base = nullptr;
-    void* tmap_h_base = nullptr;
-    uint64_t tmap_x_dims[2] = {0, 0}, tmap_h_dims[2] = {0, 0};
-    EncodeTiledFn encode = nullptr;
-    // last-forward geometry (debug reads)
-    uint32_t last_T = 0, last_E = 0, last_G = 0, last_P = 0, last_Kp = 0, last_Ip = 0, last_H = 0;
-    uint32_t last_launches = 0;
-    // stage profiling
-    std::vector<cudaEvent_t> prof_events;  // [max_calls][MOE_B200_STAGES + 1]
-    uint32_t prof_max = 0, prof_calls = 0;
-};
-
-namespace {
+namespace moe_b200 {
 
 int check_dims(const moe_b200_layer_cfg_t* c, char* err) {
     if (!c) {
@@ -221,6 +114,136 @@ LayerWeights* get_layer(moe_b200_engine* eng, int32_t layer, char* err) {
     return &eng->layers[layer];
 }
 
+int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cudaStream_t st, cudaEvent_t* ev,
+                    uint32_t* launches, char* err) {
+    auto mark = [&](int i) {
+        if (ev) cudaEventRecord(ev[i], st);
+    };
+    const uint32_t H = L->H;
+    const uint32_t n = job.T * job.K;
+    const uint32_t P = n + job.shared_rows;
+    const uint32_t G = job.E + (job.shared_rows ? 1 : 0);
+    const uint32_t Kq = L->kq, Iq = L->iq;  // K padded to 128
+    const uint32_t rows_cap = std::max(P, 32u);
+    // tokens per GEMM tile: 32 when groups are small on average (decode), else 128
+    const uint32_t block_n = (uint64_t)P <= 48ull * G ? 32u : kBlockN;
+    const uint32_t ntiles = sort_tiles(n);
+    const uint32_t token_tiles = P / block_n + G;  // upper bound of sum_g ceil(count_g / block_n)
+    uint32_t* errw = eng->err_word.as<uint32_t>();
+
+    CK(eng->tile_counts.reserve((size_t)std::max(ntiles, 1u) * std::max(job.E, 1u) * 4));
+    CK(eng->rank.reserve((size_t)std::max(n, 1u) * 4));
+    CK(eng->pos_of.reserve((size_t)std::max(n, 1u) * 4));
+    CK(eng->row_token.reserve((size_t)P * 4));
+    CK(eng->row_assign.reserve((size_t)P * 4));
+    CK(eng->g_count.reserve((size_t)(G + 1) * 4));
+    CK(eng->g_offset.reserve((size_t)(G + 1) * 4));
+    CK(eng->g_gu_off.reserve((size_t)(G + 1) * 4));
+    CK(eng->g_dn_off.reserve((size_t)(G + 1) * 4));
+    CK(eng->xb.reserve((size_t)2 * rows_cap * Kq));
+    CK(eng->hb.reserve((size_t)2 * rows_cap * Iq));
+    CK(eng->sfx_atoms.reserve((size_t)token_tiles * (Kq / 128) * 1024));
+    CK(eng->sfh_atoms.reserve((size_t)token_tiles * (Iq / 128) * 1024));
+    CK(eng->gu_tiles.reserve((size_t)token_tiles * (L->rp_i / 128) * sizeof(TileEntry)));
+    CK(eng->dn_tiles.reserve((size_t)token_tiles * (L->rp_h / 128) * sizeof(TileEntry)));
+    // the planes' row count is fixed by the buffer, so the maps only change
+    // when a buffer is reallocated or the geometry changes
+    struct MapSpec {
+        CUtensorMap* maps;
+        DevBuf* buf;
+        uint32_t cols;
+    } specs[2] = {{eng->tmap_xb, &eng->xb, Kq}, {eng->tmap_hb, &eng->hb, Iq}};
+    for (int i = 0; i < 2; ++i) {
+        const uint64_t rows = specs[i].buf->bytes / (2ull * specs[i].cols);
+        if (eng->bs_map_key[i] != specs[i].buf->ptr || eng->bs_map_dims[i][0] != specs[i].cols ||
+            eng->bs_map_dims[i][1] != rows) {
+            if (!make_tmap_planes(eng, &specs[i].maps[0], specs[i].buf->ptr, specs[i].cols, rows, 32, err) ||
+                !make_tmap_planes(eng, &specs[i].maps[1], specs[i].buf->ptr, specs[i].cols, rows, 128, err)) {
+                return 0;
+            }
+            eng->bs_map_key[i] = specs[i].buf->ptr;
+            eng->bs_map_dims[i][0] = specs[i].cols;
+            eng->bs_map_dims[i][1] = rows;
+        }
+    }
+
+    GroupInfo gi;
+    gi.count = eng->g_count.as<uint32_t>();
+    gi.offset = eng->g_offset.as<uint32_t>();
+    gi.gu_tile_off = eng->g_gu_off.as<uint32_t>();
+    gi.dn_tile_off = eng->g_dn_off.as<uint32_t>();
+    gi.block_n = block_n;
+    gi.gu_row_tiles = L->rp_i / 128;
+    gi.dn_row_tiles = L->rp_h / 128;
+    if (route_small_fits(n, job.E)) {
+        // decode-sized batch: sort, offsets and both tile tables in one block
+        CK(launch_route_small(job.ids, job.T, job.K, job.E, job.shared_rows, job.shared_base, gi,
+                              eng->gu_tiles.as<TileEntry>(), token_tiles * (L->rp_i / 128),
+                              eng->dn_tiles.as<TileEntry>(), token_tiles * (L->rp_h / 128),
+                              eng->pos_of.as<uint32_t>(), eng->row_token.as<uint32_t>(),
+                              eng->row_assign.as<uint32_t>(), errw, st, true));
+        *launches += 1;
+    } else {
+        CK(launch_permute(job.ids, job.T, job.K, job.E, job.shared_rows, job.shared_base,
+                          eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi, eng->pos_of.as<uint32_t>(),
+                          eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(), errw, st));
+        CK(launch_build_tiles(gi.count, gi.offset, gi.gu_tile_off, G, L->rp_i / 128, block_n,
+                              token_tiles * (L->rp_i / 128), eng->gu_tiles.as<TileEntry>(), st));
+        CK(launch_build_tiles(gi.count, gi.offset, gi.dn_tile_off, G, L->rp_h / 128, block_n,
+                              token_tiles * (L->rp_h / 128), eng->dn_tiles.as<TileEntry>(), st));
+        *launches += 5;
+    }
+    mark(2);
+    // permuted source rows as exact hi/lo E4M3 terms + their scale blocks
+    const uint64_t xb_rows = eng->xb.bytes / (2ull * Kq), hb_rows = eng->hb.bytes / (2ull * Iq);
+    CK(launch_gather_quant_bs(job.src, H, Kq, eng->row_token.as<uint32_t>(), P, (uint32_t)xb_rows, gi.offset,
+                              gi.gu_tile_off, G, L->rp_i / 128, block_n, eng->xb.as<uint8_t>(),
+                              eng->sfx_atoms.as<uint8_t>(), st, true));
+    *launches += 1;
+    mark(3);
+    BsParams bp{};
+    bp.groups = G;
+    bp.count = gi.count;
+    bp.offset = gi.offset;
+    bp.err = errw;
+    bp.group_slot = job.group_slot;
+    // gate/up: K = H (padded Kq), M = I rows (padded rp_i), output h hi/lo
+    bp.tile_off = gi.gu_tile_off;
+    bp.tiles = eng->gu_tiles.as<TileEntry>();
+    bp.rows_pad = L->rp_i;
+    bp.m_tiles = L->rp_i / 128;
+    bp.k_tiles = Kq / 128;
+    bp.sfa = L->bs_gu_sfa.as<uint8_t>();
+    bp.a_codes = L->bs_gu_codes.as<uint8_t>();
+    bp.sfb_atoms = eng->sfx_atoms.as<uint8_t>();
+    bp.h_out = eng->hb.as<uint8_t>();
+    bp.h_plane = hb_rows * Iq;
+    bp.h_stride = Iq;
+    bp.sfh_atoms = eng->sfh_atoms.as<uint8_t>();
+    bp.m_valid = Iq;
+    const int bi = block_n == 32 ? 0 : 1;
+    CK(launch_gemm_bs(kGateUp, (int)block_n, L->tmap_gu_codes, eng->tmap_xb[bi], bp, eng->num_sms, st, true));
+    *launches += 1;
+    mark(4);
+    // down: K = I (padded Iq), M = H rows (padded rp_h), output fp32 rows
+    bp.tile_off = gi.dn_tile_off;
+    bp.tiles = eng->dn_tiles.as<TileEntry>();
+    bp.rows_pad = L->rp_h;
+    bp.m_tiles = L->rp_h / 128;
+    bp.k_tiles = Iq / 128;
+    bp.sfa = L->bs_dn_sfa.as<uint8_t>();
+    bp.a_codes = L->bs_dn_codes.as<uint8_t>();
+    bp.sfb_atoms = eng->sfh_atoms.as<uint8_t>();
+    bp.y_out = job.y;
+    bp.y_stride = H;
+    bp.m_valid = H;
+    bp.y_row_map = job.y_by_source ? eng->row_token.as<uint32_t>() : nullptr;
+    CK(launch_gemm_bs(kDown, (int)block_n, L->tmap_dn_codes, eng->tmap_hb[bi], bp, eng->num_sms, st, true));
+    *launches += 1;
+    mark(5);
+    return 1;
+}
+
 }  // namespace
 
 extern "C" {
@@ -277,6 +300,7 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
                       &eng->sfx_atoms, &eng->hb, &eng->sfh_atoms, &eng->gu_tiles, &eng->dn_tiles};
     for (DevBuf* b : bufs) b->release();
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
+    ep_release(eng->ep);
     delete eng;
 }
 
@@ -459,39 +483,8 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     CK(eng->g_gu_off.reserve((size_t)(G + 1) * 4));
     CK(eng->g_dn_off.reserve((size_t)(G + 1) * 4));
     const bool bs = cfg->gemm_path == MOE_B200_GEMM_BLOCKSCALED;
-    const uint32_t Kq = L->kq, Iq = L->iq;  // K padded to 128 for the block-scaled path
-    // tokens per GEMM tile: 32 when groups are small on average (decode), else 128
-    const uint32_t block_n = (bs && (uint64_t)P <= 48ull * G) ? 32u : kBlockN;
     CK(eng->yperm.reserve((size_t)P * H * 4));
-    if (bs) {
-        CK(eng->xb.reserve((size_t)2 * rows_cap * Kq));
-        CK(eng->hb.reserve((size_t)2 * rows_cap * Iq));
-        const size_t token_tiles = (size_t)P / block_n + G;
-        CK(eng->sfx_atoms.reserve(token_tiles * (Kq / 128) * 1024));
-        CK(eng->sfh_atoms.reserve(token_tiles * (Iq / 128) * 1024));
-        CK(eng->gu_tiles.reserve(token_tiles * (L->rp_i / 128) * sizeof(TileEntry)));
-        CK(eng->dn_tiles.reserve(token_tiles * (L->rp_h / 128) * sizeof(TileEntry)));
-        // the planes' row count is fixed by the buffer, so the maps only change
-        // when a buffer is reallocated or the geometry changes
-        struct MapSpec {
-            CUtensorMap* maps;
-            DevBuf* buf;
-            uint32_t cols;
-        } specs[2] = {{eng->tmap_xb, &eng->xb, Kq}, {eng->tmap_hb, &eng->hb, Iq}};
-        for (int i = 0; i < 2; ++i) {
-            const uint64_t rows = specs[i].buf->bytes / (2ull * specs[i].cols);
-            if (eng->bs_map_key[i] != specs[i].buf->ptr || eng->bs_map_dims[i][0] != specs[i].cols ||
-                eng->bs_map_dims[i][1] != rows) {
-                if (!make_tmap_planes(eng, &specs[i].maps[0], specs[i].buf->ptr, specs[i].cols, rows, 32, err) ||
-                    !make_tmap_planes(eng, &specs[i].maps[1], specs[i].buf->ptr, specs[i].cols, rows, 128, err)) {
-                    return 0;
-                }
-                eng->bs_map_key[i] = specs[i].buf->ptr;
-                eng->bs_map_dims[i][0] = specs[i].cols;
-                eng->bs_map_dims[i][1] = rows;
-            }
-        }
-    } else {
+    if (!bs) {
         CK(eng->xperm.reserve((size_t)rows_cap * Kp * 2));
         CK(eng->hperm.reserve((size_t)rows_cap * Ip * 2));
         // tensor maps over the permuted activations and the intermediate
@@ -530,83 +523,33 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
                      eng->logits.as<float>(), ids, w, eng->scores.as<float>(), errw, st, &launches));
     mark(1);
 
+    if (bs) {
+        BsJob job{};
+        job.ids = ids;
+        job.T = T;
+        job.K = K;
+        job.E = E;
+        job.shared_rows = shared_rows;
+        job.shared_base = 0;
+        job.src = x;
+        job.group_slot = nullptr;
+        job.y = eng->yperm.as<float>();
+        job.y_by_source = false;
+        if (!run_blockscaled(eng, L, job, st, ev, &launches, err)) return 0;
+    } else {
     GroupInfo gi;
     gi.count = eng->g_count.as<uint32_t>();
     gi.offset = eng->g_offset.as<uint32_t>();
     gi.gu_tile_off = eng->g_gu_off.as<uint32_t>();
     gi.dn_tile_off = eng->g_dn_off.as<uint32_t>();
-    gi.block_n = block_n;
+    gi.block_n = kBlockN;
     gi.gu_row_tiles = ceil_div(I, kTileRows);
     gi.dn_row_tiles = ceil_div(H, kTileRows);
-    const uint32_t token_tiles = P / block_n + G;  // upper bound of sum_g ceil(count_g / block_n)
-    if (route_small_fits(T * K, E)) {
-        // decode-sized batch: sort, offsets and both tile tables in one block
-        CK(launch_route_small(ids, T, K, E, shared_rows, gi, bs ? eng->gu_tiles.as<TileEntry>() : nullptr,
-                              token_tiles * (L->rp_i / 128), bs ? eng->dn_tiles.as<TileEntry>() : nullptr,
-                              token_tiles * (L->rp_h / 128), eng->pos_of.as<uint32_t>(),
-                              eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(), errw, st, true));
-        launches += 1;
-    } else {
-        CK(launch_permute(ids, T, K, E, shared_rows, eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi,
-                          eng->pos_of.as<uint32_t>(), eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(),
-                          errw, st));
-        launches += 3;
-        if (bs) {
-            CK(launch_build_tiles(gi.count, gi.offset, gi.gu_tile_off, G, L->rp_i / 128, block_n,
-                                  token_tiles * (L->rp_i / 128), eng->gu_tiles.as<TileEntry>(), st));
-            CK(launch_build_tiles(gi.count, gi.offset, gi.dn_tile_off, G, L->rp_h / 128, block_n,
-                                  token_tiles * (L->rp_h / 128), eng->dn_tiles.as<TileEntry>(), st));
-            launches += 2;
-        }
-    }
+    CK(launch_permute(ids, T, K, E, shared_rows, 0, eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi,
+                      eng->pos_of.as<uint32_t>(), eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(),
+                      errw, st));
+    launches += 3;
     mark(2);
-    if (bs) {
-        // permuted rows of x as exact hi/lo E4M3 terms + their scale blocks
-        const uint64_t xb_rows = eng->xb.bytes / (2ull * Kq), hb_rows = eng->hb.bytes / (2ull * Iq);
-        CK(launch_gather_quant_bs(x, H, Kq, eng->row_token.as<uint32_t>(), P, (uint32_t)xb_rows, gi.offset,
-                                  gi.gu_tile_off, G, L->rp_i / 128, block_n, eng->xb.as<uint8_t>(),
-                                  eng->sfx_atoms.as<uint8_t>(), st, true));
-        launches += 1;
-        mark(3);
-        BsParams bp{};
-        bp.groups = G;
-        bp.count = gi.count;
-        bp.offset = gi.offset;
-        bp.err = errw;
-        // gate/up: K = H (padded Kq), M = I rows (padded rp_i), output h hi/lo
-        bp.tile_off = gi.gu_tile_off;
-        bp.tiles = eng->gu_tiles.as<TileEntry>();
-        bp.rows_pad = L->rp_i;
-        bp.m_tiles = L->rp_i / 128;
-        bp.k_tiles = Kq / 128;
-        bp.sfa = L->bs_gu_sfa.as<uint8_t>();
-        bp.a_codes = L->bs_gu_codes.as<uint8_t>();
-        bp.sfb_atoms = eng->sfx_atoms.as<uint8_t>();
-        bp.h_out = eng->hb.as<uint8_t>();
-        bp.h_plane = hb_rows * Iq;
-        bp.h_stride = Iq;
-        bp.sfh_atoms = eng->sfh_atoms.as<uint8_t>();
-        bp.m_valid = Iq;
-        const int bi = block_n == 32 ? 0 : 1;
-        CK(launch_gemm_bs(kGateUp, (int)block_n, L->tmap_gu_codes, eng->tmap_xb[bi], bp, eng->num_sms, st, true));
-        launches += 1;
-        mark(4);
-        // down: K = I (padded Iq), M = H rows (padded rp_h), output fp32 rows
-        bp.tile_off = gi.dn_tile_off;
-        bp.tiles = eng->dn_tiles.as<TileEntry>();
-        bp.rows_pad = L->rp_h;
-        bp.m_tiles = L->rp_h / 128;
-        bp.k_tiles = Iq / 128;
-        bp.sfa = L->bs_dn_sfa.as<uint8_t>();
-        bp.a_codes = L->bs_dn_codes.as<uint8_t>();
-        bp.sfb_atoms = eng->sfh_atoms.as<uint8_t>();
-        bp.y_out = eng->yperm.as<float>();
-        bp.y_stride = H;
-        bp.m_valid = H;
-        CK(launch_gemm_bs(kDown, (int)block_n, L->tmap_dn_codes, eng->tmap_hb[bi], bp, eng->num_sms, st, true));
-        launches += 1;
-        mark(5);
-    } else {
     CK(launch_gather(x, H, Kp, eng->row_token.as<uint32_t>(), P, eng->xperm.as<uint16_t>(), st));
     launches += 1;
     mark(3);
@@ -648,8 +591,8 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     mark(5);
     }
 
-    CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), w, T, K, shared ? 1 : 0, n, y_bf16,
-                      y_f32, st, bs));
+    CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), w, T, K,
+                      shared ? eng->yperm.as<float>() + (size_t)n * H : nullptr, y_bf16, y_f32, st, bs));
     launches += 1;
     mark(6);
     if (perm) {

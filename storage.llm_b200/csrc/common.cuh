@@ -148,7 +148,7 @@ inline cudaError_t launch_kernel(void (*kernel)(Exp...), dim3 grid, dim3 block, 
 }
 
 // ---------------------------------------------------------------------------
-// Bulk and tensor copies (no multicast anywhere in this library).
+// Bulk and tensor copies; each one fills only the issuing CTA's shared memory.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(

@@ -1,0 +1,161 @@
+// Engine internals shared by the C-ABI translation units (api.cu, ep.cu):
+// device buffers, the per-layer weight cache, the engine handle and the
+// block-scaled expert pipeline both the single-device and the
+// expert-parallel forward run.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace moe_b200 {
+
+inline void set_err(char* err, const char* fmt, ...) {
+    if (!err) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, MOE_B200_ERR_LEN, fmt, ap);
+    va_end(ap);
+}
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) {                                                                   \
+            set_err(err, "%s failed: %s", #call, cudaGetErrorString(e_));                          \
+            return 0;                                                                              \
+        }                                                                                          \
+    } while (0)
+
+// Device buffer that only grows.
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    cudaError_t reserve(size_t want) {
+        if (want <= bytes) return cudaSuccess;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMalloc(&ptr, want);
+        if (e == cudaSuccess) bytes = want;
+        return e;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(ptr);
+    }
+};
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct LayerWeights {
+    uint32_t E = 0, H = 0, I = 0;
+    DevBuf router;          // bf16 [E x H]
+    DevBuf gu;              // [E+1] groups of interleaved gate/up tiles
+    DevBuf dn;              // [E+1] groups of down tiles
+    uint64_t gu_stride = 0, dn_stride = 0;
+    std::vector<uint8_t> present;  // [E+1]; slot E = shared expert
+    // block-scaled form: packed E2M1 codes + E8M0 scale blocks
+    DevBuf bs_gu_codes, bs_gu_sfa, bs_dn_codes, bs_dn_sfa;
+    uint32_t rp_i = 0, rp_h = 0, kq = 0, iq = 0;  // rows padded to 128, K padded to 128
+    CUtensorMap tmap_gu_codes{}, tmap_dn_codes{};
+    void release_all() {
+        router.release();
+        gu.release();
+        dn.release();
+        bs_gu_codes.release();
+        bs_gu_sfa.release();
+        bs_dn_codes.release();
+        bs_dn_sfa.release();
+    }
+};
+
+inline uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+
+struct EpState;
+void ep_release(EpState* ep);
+
+}  // namespace moe_b200
+
+struct moe_b200_engine {
+    using DevBuf = moe_b200::DevBuf;
+    using LayerWeights = moe_b200::LayerWeights;
+    using EncodeTiledFn = moe_b200::EncodeTiledFn;
+    int device = 0;
+    int num_sms = 148;
+    std::vector<LayerWeights> layers;
+    DevBuf staging;  // GGUF bytes copied from the host before the repack
+    // workspace
+    DevBuf logits, scores, ids, wts, tile_counts, rank, pos_of, row_token, row_assign;
+    DevBuf g_count, g_offset, g_gu_off, g_dn_off;
+    DevBuf xperm, hperm, yperm;
+    DevBuf err_word;
+    // block-scaled path: quantised activations and intermediate
+    // (xb, hb hold a hi plane followed by a lo plane)
+    DevBuf xb, sfx_atoms, hb, sfh_atoms, gu_tiles, dn_tiles;
+    // 3-D maps over xb / hb: [0] 32-token box, [1] 128-token box
+    CUtensorMap tmap_xb[2]{}, tmap_hb[2]{};
+    const void* bs_map_key[2] = {nullptr, nullptr};
+    uint64_t bs_map_dims[2][2] = {};
+    // host-call staging
+    DevBuf hx, hy, hyf, hids, hw, hperm_out, tri;
+    CUtensorMap tmap_x{}, tmap_h{};
+    void* tmap_x_base = nullptr;
+    void* tmap_h_base = nullptr;
+    uint64_t tmap_x_dims[2] = {0, 0}, tmap_h_dims[2] = {0, 0};
+    EncodeTiledFn encode = nullptr;
+    // last-forward geometry (debug reads)
+    uint32_t last_T = 0, last_E = 0, last_G = 0, last_P = 0, last_Kp = 0, last_Ip = 0, last_H = 0;
+    uint32_t last_launches = 0;
+    // stage profiling
+    std::vector<cudaEvent_t> prof_events;  // [max_calls][MOE_B200_STAGES + 1]
+    uint32_t prof_max = 0, prof_calls = 0;
+    // expert parallelism (ep.cu); null until moe_b200_ep_init
+    moe_b200::EpState* ep = nullptr;
+};
+
+
+namespace moe_b200 {
+
+int check_dims(const moe_b200_layer_cfg_t* c, char* err);
+LayerWeights* get_layer(moe_b200_engine* eng, int32_t layer, char* err);
+
+// One run of the block-scaled expert pipeline: permutation of T*K
+// assignments into E routed groups (+ an extra shared-expert group of
+// `shared_rows` rows), quantise-on-gather, gate/up GEMM, down GEMM.
+struct BsJob {
+    const int32_t* ids;          // group of each assignment a, device [T*K]
+    uint32_t T, K;               // assignment a reads source row a / K
+    uint32_t E;                  // routed groups
+    uint32_t shared_rows;        // rows of the shared-expert group (0: none) ...
+    uint32_t shared_base;        // ... reading source rows shared_base + t
+    const uint16_t* src;         // source rows, bf16 [*, H], device
+    const uint32_t* group_slot;  // weight slot of each group (device); null: routed group g -> slot g,
+                                 // shared group -> slot E of the layer
+    float* y;                    // expert outputs, fp32 rows [*, H]
+    bool y_by_source;            // row of y: the source row (else the permuted row)
+};
+
+// Enqueues the pipeline on `st`; fills the engine's permutation buffers
+// (pos_of: permuted row of each assignment).  `ev`, when not null, receives
+// stage marks 2..5.  Adds its kernel launches to *launches.
+int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cudaStream_t st, cudaEvent_t* ev,
+                    uint32_t* launches, char* err);
+
+}  // namespace moe_b200

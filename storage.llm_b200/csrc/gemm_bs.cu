@@ -365,8 +365,9 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
             uint32_t pre = 0;
             if (blockIdx.x < total) {
                 const BsTileX tc = load_tile(p, blockIdx.x);
-                const uint64_t ablk0 = ((uint64_t)tc.g * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
-                const uint64_t sblk0 = ((uint64_t)tc.g * p.m_tiles + tc.mt) * p.k_tiles;
+                const uint32_t slot = p.group_slot ? __ldg(p.group_slot + tc.g) : tc.g;
+                const uint64_t ablk0 = ((uint64_t)slot * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
+                const uint64_t sblk0 = ((uint64_t)slot * p.m_tiles + tc.mt) * p.k_tiles;
                 pre = min((uint32_t)C::kStages, p.k_tiles);
                 for (uint32_t kt = 0; kt < pre; ++kt) {
                     uint8_t* sf = sf_base + kt * C::kSFStage;
@@ -383,8 +384,9 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
             pdl_wait();
             for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
                 const BsTileX tc = load_tile(p, tile);
-                const uint64_t ablk0 = ((uint64_t)tc.g * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
-                const uint64_t sblk0 = ((uint64_t)tc.g * p.m_tiles + tc.mt) * p.k_tiles;
+                const uint32_t slot = p.group_slot ? __ldg(p.group_slot + tc.g) : tc.g;  // weights of the group
+                const uint64_t ablk0 = ((uint64_t)slot * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
+                const uint64_t sblk0 = ((uint64_t)slot * p.m_tiles + tc.mt) * p.k_tiles;
                 for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
                     if (!(ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty))) break;
                     uint8_t* sf = sf_base + stage * C::kSFStage;
@@ -563,7 +565,11 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 } else if (m < p.m_valid) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        if (c0 + i < tc.nn) p.y_out[(row0 + c0 + i) * p.y_stride + m] = v0[i];
+                        if (c0 + i < tc.nn) {
+                            const uint64_t prow = row0 + c0 + i;
+                            const uint64_t orow = p.y_row_map ? __ldg(p.y_row_map + prow) : prow;
+                            p.y_out[orow * p.y_stride + m] = v0[i];
+                        }
                     }
                 }
             }

@@ -66,6 +66,8 @@ struct BsParams {
     float* y_out;             // down: [rows][y_stride] f32
     uint32_t y_stride;
     uint32_t m_valid;         // output rows to write (down)
+    const uint32_t* group_slot;  // weight slot of each group; null: the group index itself
+    const uint32_t* y_row_map;   // down: output row of each permuted row; null: the permuted row
     uint32_t* err;
 };
 
@@ -79,16 +81,20 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
                           int sigmoid, int norm_topk, float routed_scale, float* logits, int32_t* ids, float* wout,
                           float* scores, uint32_t* err, cudaStream_t st, uint32_t* launches);
 uint32_t sort_tiles(uint32_t n);
+// Permutation of T*K assignments (assignment a reads source row a / K) into
+// E groups, plus an extra group of `shared_rows` rows whose source rows are
+// shared_base + t.
 cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
-                           uint32_t* tile_counts, uint32_t* rank, GroupInfo gi, uint32_t* pos_of,
-                           uint32_t* row_token, uint32_t* row_assign, uint32_t* err, cudaStream_t st);
+                           uint32_t shared_base, uint32_t* tile_counts, uint32_t* rank, GroupInfo gi,
+                           uint32_t* pos_of, uint32_t* row_token, uint32_t* row_assign, uint32_t* err,
+                           cudaStream_t st);
 // Single-block permutation + tile tables for n <= 8192 assignments and
 // E <= 256 experts (route_small_fits); tile tables may be null.
 bool route_small_fits(uint32_t n, uint32_t E);
 cudaError_t launch_route_small(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
-                               GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max, TileEntry* dn_tiles,
-                               uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token, uint32_t* row_assign,
-                               uint32_t* err, cudaStream_t st, bool pdl);
+                               uint32_t shared_base, GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max,
+                               TileEntry* dn_tiles, uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token,
+                               uint32_t* row_assign, uint32_t* err, cudaStream_t st, bool pdl);
 // Generic pieces of the stable counting sort, used by the grouping utility.
 struct AssignRec {
     uint32_t token_index, layer, expert;
@@ -105,9 +111,9 @@ cudaError_t launch_group_finish(const AssignRec* a, const uint32_t* order, uint3
 cudaError_t launch_iota(uint32_t* v, uint32_t n, cudaStream_t st);
 cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token, uint32_t rows,
                           uint16_t* xp, cudaStream_t st);
+// y[t] = ys[t] (shared expert rows, may be null) + sum_j w[t,j] * yp[pos_of[t*K+j]].
 cudaError_t launch_combine(const float* yp, uint32_t H, const uint32_t* pos_of, const float* w, uint32_t T,
-                           uint32_t K, int has_shared, uint32_t shared_off, uint16_t* y_bf16, float* y_f32,
-                           cudaStream_t st, bool pdl);
+                           uint32_t K, const float* ys, uint16_t* y_bf16, float* y_f32, cudaStream_t st, bool pdl);
 
 // tcgen05 grouped GEMMs (gemm_tc.cu).  `tmap_b` covers the permuted
 // activation rows [rows x Kp] bf16 with a 64 x block_n box, 128-byte swizzle.

@@ -586,7 +586,8 @@ __device__ __forceinline__ void fill_tiles(const uint32_t* cnt, const uint32_t* 
 }
 
 __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t K,
-                                                           uint32_t E, uint32_t shared_rows, GroupInfo gi,
+                                                           uint32_t E, uint32_t shared_rows, uint32_t shared_base,
+                                                           GroupInfo gi,
                                                            TileEntry* __restrict__ gu_tiles, uint32_t gu_max,
                                                            TileEntry* __restrict__ dn_tiles, uint32_t dn_max,
                                                            uint32_t* __restrict__ pos_of,
@@ -703,7 +704,7 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __rest
     }
     for (uint32_t t = threadIdx.x; t < shared_rows; t += blockDim.x) {
         const uint32_t pos = goff[E] + t;
-        row_token[pos] = t;
+        row_token[pos] = shared_base + t;
         row_assign[pos] = 0xffffffffu;
     }
     if (gu_tiles) fill_tiles(gcnt, goff, gut, G, gi.gu_row_tiles, gi.block_n, gu_tiles, gu_max);
@@ -715,7 +716,7 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __rest
 // rows in token order.
 __global__ void scatter_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t K, uint32_t nb,
                                const uint32_t* __restrict__ tile_base, const uint32_t* __restrict__ rank,
-                               GroupInfo gi, uint32_t shared_rows, uint32_t* __restrict__ pos_of,
+                               GroupInfo gi, uint32_t shared_rows, uint32_t shared_base, uint32_t* __restrict__ pos_of,
                                uint32_t* __restrict__ row_token, uint32_t* __restrict__ row_assign) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) {
@@ -729,7 +730,7 @@ __global__ void scatter_kernel(const int32_t* __restrict__ ids, uint32_t n, uint
     } else if (i < n + shared_rows) {
         const uint32_t t = i - n;
         const uint32_t pos = gi.offset[nb] + t;
-        row_token[pos] = t;
+        row_token[pos] = shared_base + t;
         row_assign[pos] = 0xffffffffu;
     }
 }
@@ -749,18 +750,19 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, uint32_t H, u
     }
 }
 
-// y[t] = shared[t] + sum_j w[t,j] * yp[pos(t,j)], one fused multiply-add per
-// term in router order (generation_mlp.cpp.inc:1417-1431 via moe_axpy_f32).
+// y[t] = ys[t] + sum_j w[t,j] * yp[pos(t,j)], one fused multiply-add per
+// term in router order (generation_mlp.cpp.inc:1417-1431 via moe_axpy_f32);
+// ys (the shared expert's rows) may be null.
 __global__ void combine_kernel(const float* __restrict__ yp, uint32_t H, const uint32_t* __restrict__ pos_of,
-                               const float* __restrict__ w, uint32_t T, uint32_t K, int has_shared,
-                               uint32_t shared_off, uint16_t* __restrict__ y_bf16, float* __restrict__ y_f32) {
+                               const float* __restrict__ w, uint32_t T, uint32_t K, const float* __restrict__ ys,
+                               uint16_t* __restrict__ y_bf16, float* __restrict__ y_f32) {
     pdl_wait();  // the down GEMM's rows
     for (uint32_t t = blockIdx.y; t < T; t += gridDim.y)
     for (uint32_t h4 = blockIdx.x * blockDim.x + threadIdx.x; h4 * 4 < H; h4 += gridDim.x * blockDim.x) {
         const uint32_t h = h4 * 4;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (has_shared) {
-            const float4 s = *reinterpret_cast<const float4*>(yp + (uint64_t)(shared_off + t) * H + h);
+        if (ys) {
+            const float4 s = *reinterpret_cast<const float4*>(ys + (uint64_t)t * H + h);
             acc.x = 0.f + s.x;
             acc.y = 0.f + s.y;
             acc.z = 0.f + s.z;
@@ -847,7 +849,7 @@ cudaError_t launch_sort_scan(uint32_t* tile_counts, uint32_t ntiles, uint32_t nb
 }
 
 cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
-                           uint32_t* tile_counts, uint32_t* rank, GroupInfo gi, uint32_t* pos_of,
+                           uint32_t shared_base, uint32_t* tile_counts, uint32_t* rank, GroupInfo gi, uint32_t* pos_of,
                            uint32_t* row_token, uint32_t* row_assign, uint32_t* err, cudaStream_t st) {
     const uint32_t n = T * K;
     const uint32_t nt = sort_tiles(n);
@@ -858,7 +860,7 @@ cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t 
     const uint32_t total = n + shared_rows;
     if (total > 0) {
         scatter_kernel<<<ceil_div(total, 256), 256, 0, st>>>(ids, n, K, E, tile_counts, rank, gi, shared_rows,
-                                                             pos_of, row_token, row_assign);
+                                                             shared_base, pos_of, row_token, row_assign);
     }
     return cudaGetLastError();
 }
@@ -866,11 +868,11 @@ cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t 
 bool route_small_fits(uint32_t n, uint32_t E) { return n <= kSmallN && E <= kSmallE; }
 
 cudaError_t launch_route_small(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
-                               GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max, TileEntry* dn_tiles,
-                               uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token, uint32_t* row_assign,
-                               uint32_t* err, cudaStream_t st, bool pdl) {
-    return launch_kernel(route_small_kernel, dim3(1), dim3(1024), 0, st, pdl, ids, T * K, K, E, shared_rows, gi,
-                         gu_tiles, gu_max, dn_tiles, dn_max, pos_of, row_token, row_assign, err);
+                               uint32_t shared_base, GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max,
+                               TileEntry* dn_tiles, uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token,
+                               uint32_t* row_assign, uint32_t* err, cudaStream_t st, bool pdl) {
+    return launch_kernel(route_small_kernel, dim3(1), dim3(1024), 0, st, pdl, ids, T * K, K, E, shared_rows,
+                         shared_base, gi, gu_tiles, gu_max, dn_tiles, dn_max, pos_of, row_token, row_assign, err);
 }
 
 cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token, uint32_t rows,
@@ -882,13 +884,12 @@ cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint
 }
 
 cudaError_t launch_combine(const float* yp, uint32_t H, const uint32_t* pos_of, const float* w, uint32_t T,
-                           uint32_t K, int has_shared, uint32_t shared_off, uint16_t* y_bf16, float* y_f32,
-                           cudaStream_t st, bool pdl) {
+                           uint32_t K, const float* ys, uint16_t* y_bf16, float* y_f32, cudaStream_t st, bool pdl) {
     if (T == 0) return cudaSuccess;
     const uint32_t threads = 128;
     dim3 grid(ceil_div(ceil_div(H, 4), threads), min(T, 65535u));
-    return launch_kernel(combine_kernel, grid, dim3(threads), 0, st, pdl, yp, H, pos_of, w, T, K, has_shared,
-                         shared_off, y_bf16, y_f32);
+    return launch_kernel(combine_kernel, grid, dim3(threads), 0, st, pdl, yp, H, pos_of, w, T, K, ys, y_bf16,
+                         y_f32);
 }
 
 }  // namespace moe_b200

@@ -17,6 +17,7 @@ HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libmoe_b200.so"
 HEADER = HERE.parent / "include" / "moe_b200.h"
 ERR_LEN = 160
+EP_UID_BYTES = 128
 
 SCORE_SOFTMAX, SCORE_SIGMOID = 0, 1
 GEMM_BLOCKSCALED, GEMM_SIMT, GEMM_TMEM_DECODE = 0, 1, 2
@@ -96,6 +97,18 @@ def load(path: Path = LIB_PATH) -> C.CDLL:
     lib.moe_b200_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_uint32), cp]
     lib.moe_b200_last_launch_count.restype = C.c_uint32
     lib.moe_b200_last_launch_count.argtypes = [vp]
+    lib.moe_b200_ep_unique_id.restype = C.c_int
+    lib.moe_b200_ep_unique_id.argtypes = [vp, cp]
+    lib.moe_b200_ep_init.restype = C.c_int
+    lib.moe_b200_ep_init.argtypes = [vp, C.c_int, C.c_int, vp, cp]
+    lib.moe_b200_ep_local_experts.restype = C.c_int
+    lib.moe_b200_ep_local_experts.argtypes = [vp, C.c_uint32, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), cp]
+    lib.moe_b200_ep_layer_forward.restype = C.c_int
+    lib.moe_b200_ep_layer_forward.argtypes = [vp, C.POINTER(LayerCfg), vp, C.c_uint32, vp, vp, vp, vp, vp, cp]
+    lib.moe_b200_ep_layer_forward_host.restype = C.c_int
+    lib.moe_b200_ep_layer_forward_host.argtypes = [vp, C.POINTER(LayerCfg), vp, C.c_uint32, vp, vp, vp, vp, cp]
+    lib.moe_b200_ep_last_counts.restype = C.c_int
+    lib.moe_b200_ep_last_counts.argtypes = [vp, vp, vp, cp]
     _lib = lib
     return lib
 
@@ -193,6 +206,59 @@ class Engine:
 
     def sync(self, stream: int = 0):
         self._check(self.lib.moe_b200_sync(self.h, stream, self.err))
+
+    # -- expert parallelism ------------------------------------------------
+    @staticmethod
+    def ep_unique_id() -> bytes:
+        lib = load()
+        buf = (C.c_uint8 * EP_UID_BYTES)()
+        err = C.create_string_buffer(ERR_LEN)
+        if not lib.moe_b200_ep_unique_id(buf, err):
+            raise MoEError(err.value.decode(errors="replace"))
+        return bytes(buf)
+
+    def ep_init(self, rank: int, world: int, uid: bytes):
+        buf = (C.c_uint8 * EP_UID_BYTES).from_buffer_copy(uid)
+        self._check(self.lib.moe_b200_ep_init(self.h, rank, world, buf, self.err))
+
+    def ep_local_experts(self, experts: int):
+        first, count = C.c_uint32(0), C.c_uint32(0)
+        self._check(self.lib.moe_b200_ep_local_experts(self.h, experts, C.byref(first), C.byref(count), self.err))
+        return first.value, count.value
+
+    def upload_layer_ep(self, li, layer: int = 0):
+        """Router, this rank's expert block and the shared expert."""
+        s = li.shape
+        first, count = self.ep_local_experts(s.experts)
+        self.upload_router(layer, np.ascontiguousarray(li.router), s.experts, s.hidden)
+        for e in range(first, first + count):
+            self.upload_expert(layer, e, np.ascontiguousarray(li.gate[e]), np.ascontiguousarray(li.up[e]),
+                               np.ascontiguousarray(li.down[e]), s.hidden, s.intermediate)
+        if li.shared_gate is not None:
+            self.upload_expert(layer, -1, np.ascontiguousarray(li.shared_gate), np.ascontiguousarray(li.shared_up),
+                               np.ascontiguousarray(li.shared_down), s.hidden, s.intermediate)
+
+    def ep_forward(self, cfg: LayerCfg, x, tokens: int, y_bf16=None, y_f32=None, ids=None, w=None, stream: int = 0):
+        self._check(self.lib.moe_b200_ep_layer_forward(self.h, C.byref(cfg), _ptr(x), tokens, _ptr(y_bf16),
+                                                       _ptr(y_f32), _ptr(ids), _ptr(w), stream, self.err))
+
+    def ep_forward_host(self, cfg: LayerCfg, x: np.ndarray, want_f32: bool = True):
+        T = x.shape[0]
+        H, K = cfg.hidden, cfg.top_k
+        y = np.zeros((T, H), np.uint16)
+        yf = np.zeros((T, H), np.float32) if want_f32 else None
+        ids = np.zeros((T, K), np.int32)
+        w = np.zeros((T, K), np.float32)
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        self._check(self.lib.moe_b200_ep_layer_forward_host(self.h, C.byref(cfg), _ptr(x), T, _ptr(y), _ptr(yf),
+                                                            _ptr(ids), _ptr(w), self.err))
+        return dict(y_bf16=y, y_f32=yf, ids=ids, w=w)
+
+    def ep_last_counts(self, world: int):
+        sent = np.zeros(world, np.uint32)
+        recv = np.zeros(world, np.uint32)
+        self._check(self.lib.moe_b200_ep_last_counts(self.h, _ptr(sent), _ptr(recv), self.err))
+        return sent, recv
 
     STAGES = ("router", "permute", "gather", "gate_up", "down", "combine")
 

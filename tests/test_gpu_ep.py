@@ -1,0 +1,105 @@
+"""Expert-parallel forward on two GPUs (moe_b200_ep_layer_forward over NCCL).
+
+Each rank owns half of the experts and feeds its own tokens; its output must
+match the CPU oracle's layer on those tokens under the same bars as the
+single-device tests (routing bit-exact, output within tolerance).  Cases
+cover a decode-sized batch, an idle rank (no tokens, still serving its
+experts) with the shared expert, and a batch past the single-block
+permutation limit.  Skipped with fewer than two GPUs.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+MAX_ABS = 2e-2
+MEAN_REL = 1e-2
+
+
+def _gpus():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _rank_main(rank, uid, case, q):
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    sys.path.insert(0, os.path.join(os.path.dirname(here), "oracle"))
+    from conftest import load_pkg
+    import oracle as O
+
+    load_pkg()
+    import moe_b200.lib as L
+    import moe_b200.synth as synth
+
+    H, I, E, K, tokens, shared = case
+    shape = synth.small_shape(hidden=H, intermediate=I, experts=E, top_k=K, tokens=8, shared=shared)
+    li = synth.make_layer(shape, seed=23)
+    T = tokens[rank]
+    x = synth.gen_tokens(shape, T, seed=500 + rank, mu=None) if T else np.zeros((0, H), np.uint16)
+    eng = L.Engine(rank)
+    try:
+        eng.ep_init(rank, WORLD, uid)
+        eng.upload_layer_ep(li)
+        cfg = L.Engine.cfg(shape, gemm_path=L.GEMM_BLOCKSCALED)
+        out = eng.ep_forward_host(cfg, x)
+        sent, recv = eng.ep_last_counts(WORLD)
+        res = dict(rank=rank, sent=sent.tolist(), recv=recv.tolist())
+        if T:
+            y_ref, ids_ref, w_ref, _ = O.Port().moe_layer(li, x)
+            d = np.abs(out["y_f32"].astype(np.float64) - y_ref)
+            res.update(ids_ok=bool(np.array_equal(out["ids"], ids_ref)),
+                       w_ok=bool(np.array_equal(out["w"].view(np.uint32), w_ref.view(np.uint32))),
+                       max_abs=float(d.max()), mean_rel=float(d.mean() / max(np.abs(y_ref).mean(), 1e-30)))
+        q.put(res)
+    except Exception as e:  # report, then let the parent fail the test
+        q.put(dict(rank=rank, error=repr(e)))
+        raise
+    finally:
+        eng.close()
+
+
+CASES = [
+    (256, 320, 8, 2, (40, 40), False),
+    (256, 320, 8, 3, (64, 0), True),
+    (128, 128, 8, 4, (2100, 700), False),
+]
+
+
+@pytest.mark.skipif(_gpus() < WORLD, reason="needs two GPUs")
+@pytest.mark.parametrize("case", CASES, ids=["decode", "idle_rank_shared", "past_single_block_sort"])
+def test_expert_parallel_forward_matches_oracle(case):
+    import multiprocessing as mp
+    from conftest import load_pkg
+
+    load_pkg()
+    import moe_b200.lib as L
+
+    uid = L.Engine.ep_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, uid, case, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    results = sorted((q.get(timeout=240) for _ in range(WORLD)), key=lambda r: r["rank"])
+    for p in procs:
+        p.join(timeout=120)
+    for r in results:
+        assert "error" not in r, r
+    for p in procs:
+        assert p.exitcode == 0
+    tokens, K = case[4], case[3]
+    # every assignment crossed once each way
+    assert sum(sum(r["sent"]) for r in results) == sum(tokens) * K
+    assert results[0]["sent"][1] == results[1]["recv"][0] and results[1]["sent"][0] == results[0]["recv"][1]
+    for r in results:
+        if tokens[r["rank"]]:
+            assert r["ids_ok"] and r["w_ok"], r
+            assert r["max_abs"] <= MAX_ABS and r["mean_rel"] <= MEAN_REL, r
