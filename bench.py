@@ -29,10 +29,13 @@ grouped GEMM, weighted combine.
 L2: the 423 MB of expert weights a step streams exceed the 126 MB L2, so no
 flush is needed between steps ("l2": "inputs_exceed_l2").
 
-Multi-GPU (torchrun, N ranks): expert-parallel sharding is not built yet;
-every rank runs its own replica of the layer on its own token batch (weak
-scaling, no collective on the data path) and value sums the ranks' tokens
-over the slowest rank's time.
+Multi-GPU (torchrun, N ranks): expert parallelism.  Rank r owns experts
+[r*E/N, (r+1)*E/N) and its own batch of `--tokens` tokens (weak scaling);
+each step is moe_b200_ep_layer_forward on every rank: local router, NCCL
+all-to-allv of the assignment rows to their experts' owners, the local
+block-scaled expert GEMMs, the reverse exchange and the combine.  value sums
+the ranks' tokens over the slowest rank's CUDA-event time; the line also
+reports the exchange's load balance (max / mean rows received per rank).
 """
 from __future__ import annotations
 
@@ -199,7 +202,7 @@ def config_dict(shape, args):
                         + (f", skew {shape.skew}" if shape.skew else ""),
             "hidden": shape.hidden, "experts": shape.experts, "top_k": shape.top_k,
             "intermediate": shape.intermediate, "tokens_per_step": args.tokens, "shared_expert": shape.shared,
-            "parallelism": f"replica{args.gpus}" if args.gpus > 1 else "single",
+            "parallelism": f"ep{args.gpus}" if args.gpus > 1 else "single",
             "l2": "inputs_exceed_l2"}
 
 
@@ -215,6 +218,129 @@ def profiled_traffic(args):
         if line.startswith("traffic_bytes_per_launch:"):
             return float(line.split(":", 1)[1].strip())
     return None
+
+
+class StdoutToStderr:
+    """Points file descriptor 1 at stderr for the block: NCCL prints its
+    version line to stdout when a communicator starts, and stdout carries
+    only the one JSON line."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *a):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+
+
+def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
+    """--gpus N > 1: moe_b200_ep_layer_forward on every rank (see the module docstring)."""
+    import ctypes as C
+    import torch
+    import moe_b200.lib as L
+
+    T, H, K = args.tokens, shape.hidden, shape.top_k
+    eng = L.Engine(local)
+    with StdoutToStderr():
+        uid = [L.Engine.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        eng.ep_init(rank, world, uid[0])
+        dist.barrier()
+    eng.upload_layer_ep(li)
+    cfg = L.Engine.cfg(shape, gemm_path=L.GEMM_BLOCKSCALED)
+    x = torch.from_numpy(li.x.view(np.int16)).cuda()
+    y = torch.empty((T, H), dtype=torch.int16, device="cuda")
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        eng.ep_forward(cfg, x, T, y_bf16=y, ids=ids, w=w, stream=sp)
+
+    for _ in range(args.warmup):
+        step()
+    eng.sync(sp)
+    launches_per_step = eng.launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    dist.barrier()
+    value = T * args.steps * world / (ms / 1000.0)
+    sent, recv = eng.ep_last_counts(world)
+    rows = torch.tensor([float(recv.sum())], device="cuda")
+    rows_all = [torch.zeros_like(rows) for _ in range(world)]
+    dist.all_gather(rows_all, rows)
+    rows_all = [float(r.item()) for r in rows_all]
+    imbalance = max(rows_all) / max(np.mean(rows_all), 1e-9)
+
+    # end to end through the host-pointer C-ABI call
+    xh = torch.from_numpy(li.x.view(np.int16)).pin_memory()
+    yh = torch.empty((T, H), dtype=torch.int16).pin_memory()
+    idsh = torch.empty((T, K), dtype=torch.int32).pin_memory()
+    wh = torch.empty((T, K), dtype=torch.float32).pin_memory()
+    lib = L.load()
+
+    def step_host():
+        ok = lib.moe_b200_ep_layer_forward_host(eng.h, C.byref(cfg), xh.data_ptr(), T, yh.data_ptr(), None,
+                                                idsh.data_ptr(), wh.data_ptr(), eng.err)
+        if not ok:
+            raise L.MoEError(eng.err.value.decode())
+
+    for _ in range(3):
+        step_host()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e2e_steps = max(10, args.steps // 2)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        step_host()
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = T * e2e_steps * world / float(t.item())
+
+    # whole-layer HBM roofline of one rank: its expert block's MXFP4 bytes
+    # (every local expert is routed to at these batch sizes) + its token rows
+    hbm, _, peak_kind = measured_peaks()
+    e_loc = shape.experts // world
+    layer_bytes = e_loc * 3 * shape.intermediate * H * 17 / 32 + T * H * 2 * 2 + 2 * T * K * H * 2
+    achieved = layer_bytes / (ms / args.steps / 1000.0) / 1e9
+    result = {
+        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": config_dict(shape, args),
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2 * world,
+                "d2h_bytes_per_step": (T * H * 2 + T * K * 8) * world},
+        "roofline": {"kernel": "whole layer on one expert-parallel rank", "bound": "hbm", "achieved": achieved,
+                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_kind,
+                     "traffic": None, "algorithmic_bytes_per_launch": layer_bytes,
+                     "launch_ms": ms / args.steps},
+        "expert_parallel": {"experts_per_gpu": e_loc, "rows_received_per_rank": rows_all,
+                            "load_imbalance_max_over_mean": imbalance},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    eng.close()
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def main():
@@ -258,6 +384,8 @@ def main():
     li = synth.make_layer(shape, seed=0, tokens=args.tokens)
     if world > 1:  # each rank its own token batch (weak scaling)
         li.x = synth.gen_tokens(shape, args.tokens, seed=100 + rank, mu=li.mu)
+        run_expert_parallel(args, shape, li, metric, rank, world, local, dist)
+        return
     eng = L.Engine(local)
     eng.upload_layer(li)
     cfg = L.Engine.cfg(shape)
