@@ -136,6 +136,7 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     CK(eng->pos_of.reserve((size_t)std::max(n, 1u) * 4));
     CK(eng->row_token.reserve((size_t)P * 4));
     CK(eng->row_assign.reserve((size_t)P * 4));
+    CK(eng->row_info.reserve((size_t)P * 4));
     CK(eng->g_count.reserve((size_t)(G + 1) * 4));
     CK(eng->g_offset.reserve((size_t)(G + 1) * 4));
     CK(eng->g_gu_off.reserve((size_t)(G + 1) * 4));
@@ -181,12 +182,13 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
                               eng->gu_tiles.as<TileEntry>(), token_tiles * (L->rp_i / 128),
                               eng->dn_tiles.as<TileEntry>(), token_tiles * (L->rp_h / 128),
                               eng->pos_of.as<uint32_t>(), eng->row_token.as<uint32_t>(),
-                              eng->row_assign.as<uint32_t>(), errw, st, true));
+                              eng->row_assign.as<uint32_t>(), eng->row_info.as<uint32_t>(), errw, st, true));
         *launches += 1;
     } else {
         CK(launch_permute(job.ids, job.T, job.K, job.E, job.shared_rows, job.shared_base,
                           eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi, eng->pos_of.as<uint32_t>(),
-                          eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(), errw, st));
+                          eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(),
+                          eng->row_info.as<uint32_t>(), errw, st));
         CK(launch_build_tiles(gi.count, gi.offset, gi.gu_tile_off, G, L->rp_i / 128, block_n,
                               token_tiles * (L->rp_i / 128), eng->gu_tiles.as<TileEntry>(), st));
         CK(launch_build_tiles(gi.count, gi.offset, gi.dn_tile_off, G, L->rp_h / 128, block_n,
@@ -196,9 +198,9 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     mark(2);
     // permuted source rows as exact hi/lo E4M3 terms + their scale blocks
     const uint64_t xb_rows = eng->xb.bytes / (2ull * Kq), hb_rows = eng->hb.bytes / (2ull * Iq);
-    CK(launch_gather_quant_bs(job.src, H, Kq, eng->row_token.as<uint32_t>(), P, (uint32_t)xb_rows, gi.offset,
-                              gi.gu_tile_off, G, L->rp_i / 128, block_n, eng->xb.as<uint8_t>(),
-                              eng->sfx_atoms.as<uint8_t>(), st, true));
+    CK(launch_gather_quant_bs(job.src, H, Kq, eng->row_token.as<uint32_t>(), eng->row_info.as<uint32_t>(), P,
+                              (uint32_t)xb_rows, block_n, eng->xb.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(), st,
+                              true));
     *launches += 1;
     mark(3);
     BsParams bp{};
@@ -293,7 +295,7 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
     cudaDeviceSynchronize();
     for (auto& l : eng->layers) l.release_all();
     DevBuf* bufs[] = {&eng->staging, &eng->logits, &eng->scores, &eng->ids, &eng->wts, &eng->tile_counts,
-                      &eng->rank, &eng->pos_of, &eng->row_token, &eng->row_assign, &eng->g_count,
+                      &eng->rank, &eng->pos_of, &eng->row_token, &eng->row_assign, &eng->row_info, &eng->g_count,
                       &eng->g_offset, &eng->g_gu_off, &eng->g_dn_off, &eng->xperm, &eng->hperm,
                       &eng->yperm, &eng->err_word, &eng->hx, &eng->hy, &eng->hyf, &eng->hids,
                       &eng->hw, &eng->hperm_out, &eng->tri, &eng->xb,
@@ -547,7 +549,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     gi.dn_row_tiles = ceil_div(H, kTileRows);
     CK(launch_permute(ids, T, K, E, shared_rows, 0, eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi,
                       eng->pos_of.as<uint32_t>(), eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(),
-                      errw, st));
+                      nullptr, errw, st));
     launches += 3;
     mark(2);
     CK(launch_gather(x, H, Kp, eng->row_token.as<uint32_t>(), P, eng->xperm.as<uint16_t>(), st));

@@ -102,7 +102,7 @@ struct moe_b200_engine {
     std::vector<LayerWeights> layers;
     DevBuf staging;  // GGUF bytes copied from the host before the repack
     // workspace
-    DevBuf logits, scores, ids, wts, tile_counts, rank, pos_of, row_token, row_assign;
+    DevBuf logits, scores, ids, wts, tile_counts, rank, pos_of, row_token, row_assign, row_info;
     DevBuf g_count, g_offset, g_gu_off, g_dn_off;
     DevBuf xperm, hperm, yperm;
     DevBuf err_word;

@@ -308,11 +308,11 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
         if (route_small_fits(n, W)) {
             CK(launch_route_small(ep->dest.as<int32_t>(), T, K, W, 0, 0, gd, nullptr, 0, nullptr, 0,
                                   ep->pos.as<uint32_t>(), ep->row_tok.as<uint32_t>(), ep->row_asg.as<uint32_t>(),
-                                  errw, st, true));
+                                  nullptr, errw, st, true));
         } else {
             CK(launch_permute(ep->dest.as<int32_t>(), T, K, W, 0, 0, ep->tile_counts.as<uint32_t>(),
                               ep->rank_buf.as<uint32_t>(), gd, ep->pos.as<uint32_t>(), ep->row_tok.as<uint32_t>(),
-                              ep->row_asg.as<uint32_t>(), errw, st));
+                              ep->row_asg.as<uint32_t>(), nullptr, errw, st));
         }
         CK(launch_kernel(ep_pack_kernel, dim3(std::min(ceil_div(n, 8u), 148u * 8u)), dim3(256), 0, st, true, x, H,
                          K, e_per, (const int32_t*)ids, (const uint32_t*)ep->row_asg.as<uint32_t>(), n,

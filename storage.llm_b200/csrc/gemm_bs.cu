@@ -39,8 +39,6 @@
 //   warps 2-5  epilogue, one TMEM lane quarter each
 //   warps 6-9  scale factors into TMEM, one lane quarter each
 // All waits are bounded and report through p.err.
-#include <cuda_fp8.h>
-
 #include <algorithm>
 
 #include "common.cuh"
@@ -101,80 +99,110 @@ __device__ __forceinline__ int block_exp(float amax) {
     return e < -127 ? -127 : (e > 127 ? 127 : e);
 }
 
-__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
-    const __half_raw hr = __nv_cvt_fp8_to_halfraw(b, __NV_E4M3);
-    return __half2float(__half(hr));
+// Round-to-nearest-even of y (|y| < 448) to E4M3: returns the code byte and
+// the rounded value.  Normal range (|y| >= 2^-6): keep 3 mantissa bits of the
+// fp32 pattern (RNE on the 20 dropped bits; a carry into the exponent is the
+// correct next binade).  Subnormal range: multiples of 2^-9, rounded by adding
+// and subtracting 1.5 * 2^14 (whose fp32 ulp is 2^-9); the multiple m = 0..8 is
+// the code (m = 8 is 2^-6, code 0x08, the smallest normal).  Pure integer and
+// fp32 add/multiply arithmetic: no conversion instruction.
+__device__ __forceinline__ uint32_t e4m3_rne(float y, float& q) {
+    const uint32_t sign = __float_as_uint(y) & 0x80000000u;
+    const float ay = fabsf(y);
+    uint32_t code;
+    if (ay >= 0.015625f) {
+        uint32_t b = __float_as_uint(ay);
+        b = (b + 0x7FFFFu + ((b >> 20) & 1u)) & 0xFFF00000u;
+        q = __uint_as_float(b);
+        code = ((((b >> 23) - 120u) << 3) | ((b >> 20) & 7u));
+    } else {
+        const float t = __fadd_rn(ay, 24576.0f);  // 24576 = 0x46C00000; t = 24576 + m * 2^-9
+        q = __fsub_rn(t, 24576.0f);
+        code = __float_as_uint(t) - 0x46C00000u;
+    }
+    q = __uint_as_float(__float_as_uint(q) | sign);
+    return code | (sign >> 24);
 }
 
 // Splits the 32 values held by a warp (one per lane, one 32-element K block)
 // into hi + lo E4M3 terms with E8M0 scale bytes.  Warp-collective.
 __device__ __forceinline__ void split_e4m3_warp(float v, uint8_t& hi, uint8_t& lo, uint8_t& s_hi, uint8_t& s_lo) {
     const int e1 = block_exp(warp_max_abs(v));
-    hi = __nv_cvt_float_to_fp8(v * pow2f(-e1), __NV_SATFINITE, __NV_E4M3);
-    const float r = v - e4m3_to_f32(hi) * pow2f(e1);
+    float qh;
+    hi = (uint8_t)e4m3_rne(v * pow2f(-e1), qh);
+    const float r = v - qh * pow2f(e1);
     const int e2 = block_exp(warp_max_abs(r));
-    lo = __nv_cvt_float_to_fp8(r * pow2f(-e2), __NV_SATFINITE, __NV_E4M3);
+    float ql;
+    lo = (uint8_t)e4m3_rne(r * pow2f(-e2), ql);
     s_hi = (uint8_t)(e1 + 127);
     s_lo = (uint8_t)(e2 + 127);
 }
 
 // ---------------------------------------------------------------------------
 // Permuted activation rows for the block-scaled GEMM, quantised on the way:
-// one warp per (permuted row, 128-element K stage).  Lane l splits elements
-// 128 kt + 32 j + l (j = 0..3, four 32-element blocks) of the row's token
-// into exact hi + lo E4M3 terms, writes them to the hi and lo planes of xb
-// ([2][rows_cap][Kp]) and the stage's four hi and four lo scale bytes, as
-// one 32-bit word each, straight into the scale block the GEMM's producer
-// bulk-copies for (token tile, kt), at sfb_pos_hi / sfb_pos_lo.  Token tile
-// of row r in group g: tile_off[g] / m_tiles + (r - offset[g]) / block_n.
+// one warp per (permuted row, chunk of kGqChunk 128-element K stages).  For
+// stage kt lane l splits elements 128 kt + 32 j + l (j = 0..3, four 32-element
+// blocks) of the row's token into exact hi + lo E4M3 terms, writes them to the
+// hi and lo planes of xb ([2][rows_cap][Kp]) and the stage's four hi and four
+// lo scale bytes, as one 32-bit word each, straight into the scale block the
+// GEMM's producer bulk-copies for (token tile, kt), at sfb_pos_hi / sfb_pos_lo.
+// The row's token tile and index in it come from the permutation (row_info).
 // ---------------------------------------------------------------------------
+constexpr uint32_t kGqChunk = 4;
+
 template <int BN>
-__global__ void __launch_bounds__(256) gather_quant_bs_kernel(
-    const uint16_t* __restrict__ x, uint32_t H, uint32_t Kp, const uint32_t* __restrict__ row_token, uint32_t rows,
-    uint32_t rows_cap, const uint32_t* __restrict__ offset, const uint32_t* __restrict__ tile_off, uint32_t groups,
-    uint32_t m_tiles, uint8_t* __restrict__ xb, uint8_t* __restrict__ sf_atoms) {
+__global__ void __launch_bounds__(256) gather_quant_bs_kernel(const uint16_t* __restrict__ x, uint32_t H,
+                                                              uint32_t Kp, const uint32_t* __restrict__ row_token,
+                                                              const uint32_t* __restrict__ row_info, uint32_t rows,
+                                                              uint32_t rows_cap, uint8_t* __restrict__ xb,
+                                                              uint8_t* __restrict__ sf_atoms) {
     constexpr uint32_t kAtom = BN == 32 ? 512 : 1024;
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t nkt = Kp / 128;
-    const uint64_t tasks = (uint64_t)rows * nkt;
+    const uint32_t chunks = (nkt + kGqChunk - 1) / kGqChunk;
+    const uint64_t tasks = (uint64_t)rows * chunks;
+    const uint64_t xplane = (uint64_t)rows_cap * Kp;
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     // the permutation first; only then may the gate/up GEMM launch (its
     // prologue reads the tile table the permutation wrote)
     pdl_wait();
     pdl_trigger();
-    const uint64_t xplane = (uint64_t)rows_cap * Kp;
-    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     for (uint64_t task = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; task < tasks; task += warps) {
-        const uint32_t r = (uint32_t)(task / nkt), kt = (uint32_t)(task % nkt);
-        const uint16_t* xr = x + (uint64_t)row_token[r] * H;
-        float v[4];
+        const uint32_t r = (uint32_t)(task / chunks);
+        const uint32_t kt0 = (uint32_t)(task % chunks) * kGqChunk;
+        const uint16_t* xr = x + (uint64_t)__ldg(row_token + r) * H;
+        const uint32_t info = __ldg(row_info + r);
+        uint8_t* atoms = sf_atoms + (uint64_t)(info >> 8) * nkt * kAtom;
+        const uint32_t pos_h = sfb_pos_hi<BN>(info & 0xFFu), pos_l = sfb_pos_lo<BN>(info & 0xFFu);
+        uint8_t* dh = xb + (uint64_t)r * Kp + lane;
+        float v[kGqChunk][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t k = kt * 128 + j * 32 + lane;
-            v[j] = k < H ? bf16_bits_to_f32(__ldg(xr + k)) : 0.f;
-        }
-        uint32_t shw = 0, slw = 0;
-        uint8_t* dh = xb + (uint64_t)r * Kp + kt * 128 + lane;
+        for (uint32_t c = 0; c < kGqChunk; ++c) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint8_t hi, lo, sh, sl;
-            split_e4m3_warp(v[j], hi, lo, sh, sl);
-            dh[j * 32] = hi;
-            dh[xplane + j * 32] = lo;
-            shw |= (uint32_t)sh << (8 * j);
-            slw |= (uint32_t)sl << (8 * j);
-        }
-        if (lane == 0) {
-            uint32_t lo = 0, hi = groups;  // group owning row r
-            while (hi - lo > 1) {
-                const uint32_t mid = (lo + hi) >> 1;
-                if (offset[mid] <= r) lo = mid;
-                else hi = mid;
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t k = (kt0 + c) * 128 + j * 32 + lane;
+                v[c][j] = (kt0 + c < nkt && k < H) ? bf16_bits_to_f32(__ldg(xr + k)) : 0.f;
             }
-            const uint32_t n = r - offset[lo];
-            const uint64_t tile = tile_off[lo] / m_tiles + n / BN;
-            uint8_t* atom = sf_atoms + (tile * nkt + kt) * kAtom;
-            *reinterpret_cast<uint32_t*>(atom + sfb_pos_hi<BN>(n % BN)) = shw;
-            *reinterpret_cast<uint32_t*>(atom + sfb_pos_lo<BN>(n % BN)) = slw;
+        }
+#pragma unroll
+        for (uint32_t c = 0; c < kGqChunk; ++c) {
+            const uint32_t kt = kt0 + c;
+            if (kt >= nkt) break;  // uniform across the warp
+            uint32_t shw = 0, slw = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint8_t hi, lo, sh, sl;
+                split_e4m3_warp(v[c][j], hi, lo, sh, sl);
+                dh[kt * 128 + j * 32] = hi;
+                dh[xplane + kt * 128 + j * 32] = lo;
+                shw |= (uint32_t)sh << (8 * j);
+                slw |= (uint32_t)sl << (8 * j);
+            }
+            if (lane == 0) {
+                uint8_t* atom = atoms + (uint64_t)kt * kAtom;
+                *reinterpret_cast<uint32_t*>(atom + pos_h) = shw;
+                *reinterpret_cast<uint32_t*>(atom + pos_l) = slw;
+            }
         }
     }
 }
@@ -239,18 +267,17 @@ cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, 
 }
 
 cudaError_t launch_gather_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token,
-                                   uint32_t rows, uint32_t rows_cap, const uint32_t* offset, const uint32_t* tile_off,
-                                   uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* xb, uint8_t* sf_atoms,
-                                   cudaStream_t st, bool pdl) {
+                                   const uint32_t* row_info, uint32_t rows, uint32_t rows_cap, uint32_t block_n,
+                                   uint8_t* xb, uint8_t* sf_atoms, cudaStream_t st, bool pdl) {
     if (rows == 0) return cudaSuccess;
-    const uint64_t tasks = (uint64_t)rows * (Kp / 128);
+    const uint64_t tasks = (uint64_t)rows * ((Kp / 128 + kGqChunk - 1) / kGqChunk);
     const uint32_t blocks = (uint32_t)std::min<uint64_t>((tasks + 7) / 8, 148ull * 8ull);
     if (block_n == 32) {
         return launch_kernel(gather_quant_bs_kernel<32>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, row_token,
-                             rows, rows_cap, offset, tile_off, groups, m_tiles, xb, sf_atoms);
+                             row_info, rows, rows_cap, xb, sf_atoms);
     }
-    return launch_kernel(gather_quant_bs_kernel<128>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, row_token, rows,
-                         rows_cap, offset, tile_off, groups, m_tiles, xb, sf_atoms);
+    return launch_kernel(gather_quant_bs_kernel<128>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, row_token,
+                         row_info, rows, rows_cap, xb, sf_atoms);
 }
 
 // ---------------------------------------------------------------------------

@@ -83,18 +83,19 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
 uint32_t sort_tiles(uint32_t n);
 // Permutation of T*K assignments (assignment a reads source row a / K) into
 // E groups, plus an extra group of `shared_rows` rows whose source rows are
-// shared_base + t.
+// shared_base + t.  row_info (may be null): per permuted row, its gate/up
+// token tile << 8 | its index in the tile (gi.block_n, gi.gu_row_tiles).
 cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
                            uint32_t shared_base, uint32_t* tile_counts, uint32_t* rank, GroupInfo gi,
-                           uint32_t* pos_of, uint32_t* row_token, uint32_t* row_assign, uint32_t* err,
-                           cudaStream_t st);
+                           uint32_t* pos_of, uint32_t* row_token, uint32_t* row_assign, uint32_t* row_info,
+                           uint32_t* err, cudaStream_t st);
 // Single-block permutation + tile tables for n <= 8192 assignments and
 // E <= 256 experts (route_small_fits); tile tables may be null.
 bool route_small_fits(uint32_t n, uint32_t E);
 cudaError_t launch_route_small(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
                                uint32_t shared_base, GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max,
                                TileEntry* dn_tiles, uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token,
-                               uint32_t* row_assign, uint32_t* err, cudaStream_t st, bool pdl);
+                               uint32_t* row_assign, uint32_t* row_info, uint32_t* err, cudaStream_t st, bool pdl);
 // Generic pieces of the stable counting sort, used by the grouping utility.
 struct AssignRec {
     uint32_t token_index, layer, expert;
@@ -127,11 +128,11 @@ cudaError_t launch_gemm_tc(int mode, const CUtensorMap& tmap_b, const GemmParams
 cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, uint32_t rows_pad, uint32_t Kp,
                              uint8_t* codes, uint8_t* sfa, uint32_t sf_stride, cudaStream_t st);
 // xb [2][rows_cap][Kp]: permuted rows of x as exact hi/lo E4M3 terms; their
-// scale words go to sf_atoms, one block per (token tile, 128-K stage).
+// scale words go to sf_atoms, one block per (token tile, 128-K stage), at the
+// tile and index the permutation recorded in row_info.
 cudaError_t launch_gather_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token,
-                                   uint32_t rows, uint32_t rows_cap, const uint32_t* offset, const uint32_t* tile_off,
-                                   uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint8_t* xb, uint8_t* sf_atoms,
-                                   cudaStream_t st, bool pdl);
+                                   const uint32_t* row_info, uint32_t rows, uint32_t rows_cap, uint32_t block_n,
+                                   uint8_t* xb, uint8_t* sf_atoms, cudaStream_t st, bool pdl);
 cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, const uint32_t* tile_off,
                                uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint32_t max_tiles,
                                TileEntry* tiles, cudaStream_t st);

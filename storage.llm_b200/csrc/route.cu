@@ -585,6 +585,12 @@ __device__ __forceinline__ void fill_tiles(const uint32_t* cnt, const uint32_t* 
     }
 }
 
+// Gate/up token tile of the n-th row of a group whose gate/up tiles start at
+// tile_off, and the row's index inside that tile: (tile << 8) | index.
+__device__ __forceinline__ uint32_t row_tile_info(uint32_t tile_off, uint32_t n, const GroupInfo& gi) {
+    return ((tile_off / gi.gu_row_tiles + n / gi.block_n) << 8) | (n % gi.block_n);
+}
+
 __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t K,
                                                            uint32_t E, uint32_t shared_rows, uint32_t shared_base,
                                                            GroupInfo gi,
@@ -593,6 +599,7 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __rest
                                                            uint32_t* __restrict__ pos_of,
                                                            uint32_t* __restrict__ row_token,
                                                            uint32_t* __restrict__ row_assign,
+                                                           uint32_t* __restrict__ row_info,
                                                            uint32_t* __restrict__ err) {
     __shared__ uint32_t cnt[32][kSmallE];  // per-warp counts, then each warp's base within the expert
     __shared__ uint32_t gcnt[kSmallE + 2], goff[kSmallE + 2], gut[kSmallE + 2], dnt[kSmallE + 2];
@@ -696,16 +703,19 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __rest
         const uint32_t i = s0 + s * 32 + lane;
         const int32_t b = bk[s];
         if (b >= 0) {
-            const uint32_t pos = goff[b] + cnt[warp][b] + rk[s];
+            const uint32_t n = cnt[warp][b] + rk[s];
+            const uint32_t pos = goff[b] + n;
             pos_of[i] = pos;
             row_token[pos] = i / K;
             row_assign[pos] = i;
+            if (row_info) row_info[pos] = row_tile_info(gut[b], n, gi);
         }
     }
     for (uint32_t t = threadIdx.x; t < shared_rows; t += blockDim.x) {
         const uint32_t pos = goff[E] + t;
         row_token[pos] = shared_base + t;
         row_assign[pos] = 0xffffffffu;
+        if (row_info) row_info[pos] = row_tile_info(gut[E], t, gi);
     }
     if (gu_tiles) fill_tiles(gcnt, goff, gut, G, gi.gu_row_tiles, gi.block_n, gu_tiles, gu_max);
     if (dn_tiles) fill_tiles(gcnt, goff, dnt, G, gi.dn_row_tiles, gi.block_n, dn_tiles, dn_max);
@@ -717,21 +727,25 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __rest
 __global__ void scatter_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t K, uint32_t nb,
                                const uint32_t* __restrict__ tile_base, const uint32_t* __restrict__ rank,
                                GroupInfo gi, uint32_t shared_rows, uint32_t shared_base, uint32_t* __restrict__ pos_of,
-                               uint32_t* __restrict__ row_token, uint32_t* __restrict__ row_assign) {
+                               uint32_t* __restrict__ row_token, uint32_t* __restrict__ row_assign,
+                               uint32_t* __restrict__ row_info) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) {
         const int32_t b = ids[i];
         if (b >= 0 && (uint32_t)b < nb) {
-            const uint32_t pos = gi.offset[b] + tile_base[(uint64_t)(i / kSortTile) * nb + b] + rank[i];
+            const uint32_t n = tile_base[(uint64_t)(i / kSortTile) * nb + b] + rank[i];
+            const uint32_t pos = gi.offset[b] + n;
             pos_of[i] = pos;
             row_token[pos] = i / K;
             row_assign[pos] = i;
+            if (row_info) row_info[pos] = row_tile_info(gi.gu_tile_off[b], n, gi);
         }
     } else if (i < n + shared_rows) {
         const uint32_t t = i - n;
         const uint32_t pos = gi.offset[nb] + t;
         row_token[pos] = shared_base + t;
         row_assign[pos] = 0xffffffffu;
+        if (row_info) row_info[pos] = row_tile_info(gi.gu_tile_off[nb], t, gi);
     }
 }
 
@@ -850,7 +864,8 @@ cudaError_t launch_sort_scan(uint32_t* tile_counts, uint32_t ntiles, uint32_t nb
 
 cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
                            uint32_t shared_base, uint32_t* tile_counts, uint32_t* rank, GroupInfo gi, uint32_t* pos_of,
-                           uint32_t* row_token, uint32_t* row_assign, uint32_t* err, cudaStream_t st) {
+                           uint32_t* row_token, uint32_t* row_assign, uint32_t* row_info, uint32_t* err,
+                           cudaStream_t st) {
     const uint32_t n = T * K;
     const uint32_t nt = sort_tiles(n);
     if (n > 0) {
@@ -860,7 +875,7 @@ cudaError_t launch_permute(const int32_t* ids, uint32_t T, uint32_t K, uint32_t 
     const uint32_t total = n + shared_rows;
     if (total > 0) {
         scatter_kernel<<<ceil_div(total, 256), 256, 0, st>>>(ids, n, K, E, tile_counts, rank, gi, shared_rows,
-                                                             shared_base, pos_of, row_token, row_assign);
+                                                             shared_base, pos_of, row_token, row_assign, row_info);
     }
     return cudaGetLastError();
 }
@@ -870,9 +885,10 @@ bool route_small_fits(uint32_t n, uint32_t E) { return n <= kSmallN && E <= kSma
 cudaError_t launch_route_small(const int32_t* ids, uint32_t T, uint32_t K, uint32_t E, uint32_t shared_rows,
                                uint32_t shared_base, GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max,
                                TileEntry* dn_tiles, uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token,
-                               uint32_t* row_assign, uint32_t* err, cudaStream_t st, bool pdl) {
+                               uint32_t* row_assign, uint32_t* row_info, uint32_t* err, cudaStream_t st, bool pdl) {
     return launch_kernel(route_small_kernel, dim3(1), dim3(1024), 0, st, pdl, ids, T * K, K, E, shared_rows,
-                         shared_base, gi, gu_tiles, gu_max, dn_tiles, dn_max, pos_of, row_token, row_assign, err);
+                         shared_base, gi, gu_tiles, gu_max, dn_tiles, dn_max, pos_of, row_token, row_assign,
+                         row_info, err);
 }
 
 cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token, uint32_t rows,
