@@ -281,6 +281,15 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     ms = float(t.item())
     dist.barrier()
     value = T * args.steps * world / (ms / 1000.0)
+    # per-phase breakdown: the same steps again with events between phases
+    eng.profile_enable(args.steps)
+    for _ in range(args.steps):
+        step()
+    eng.sync(sp)
+    phase_ms, prof_calls = eng.profile_read()
+    eng.profile_enable(0)
+    ep_phases = dict(zip(("router", "dispatch", "counts_sync", "row_exchange", "local_experts",
+                          "return_combine"), [v / max(prof_calls, 1) for v in phase_ms.values()]))
     sent, recv = eng.ep_last_counts(world)
     rows = torch.tensor([float(recv.sum())], device="cuda")
     rows_all = [torch.zeros_like(rows) for _ in range(world)]
@@ -332,7 +341,7 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
                      "traffic": None, "algorithmic_bytes_per_launch": layer_bytes,
                      "launch_ms": ms / args.steps},
         "expert_parallel": {"experts_per_gpu": e_loc, "rows_received_per_rank": rows_all,
-                            "load_imbalance_max_over_mean": imbalance},
+                            "load_imbalance_max_over_mean": imbalance, "phase_ms_rank0": ep_phases},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }

@@ -125,8 +125,11 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     const uint32_t G = job.E + (job.shared_rows ? 1 : 0);
     const uint32_t Kq = L->kq, Iq = L->iq;  // K padded to 128
     const uint32_t rows_cap = std::max(P, 32u);
-    // tokens per GEMM tile: 32 when groups are small on average (decode), else 128
-    const uint32_t block_n = (uint64_t)P <= 48ull * G ? 32u : kBlockN;
+    // tokens per GEMM tile: 32 while the groups average at most 48 rows
+    // (decode), 64 up to 256 rows, else 128 (prefill): wider tiles re-read
+    // each weight block from L2 fewer times and issue fewer MMAs per token
+    const uint64_t avg_x = G ? (uint64_t)P / G : 0;
+    const uint32_t block_n = avg_x <= 48 ? 32u : (avg_x <= 256 ? 64u : kBlockN);
     const uint32_t ntiles = sort_tiles(n);
     const uint32_t token_tiles = P / block_n + G;  // upper bound of sum_g ceil(count_g / block_n)
     uint32_t* errw = eng->err_word.as<uint32_t>();
@@ -159,7 +162,8 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
         if (eng->bs_map_key[i] != specs[i].buf->ptr || eng->bs_map_dims[i][0] != specs[i].cols ||
             eng->bs_map_dims[i][1] != rows) {
             if (!make_tmap_planes(eng, &specs[i].maps[0], specs[i].buf->ptr, specs[i].cols, rows, 32, err) ||
-                !make_tmap_planes(eng, &specs[i].maps[1], specs[i].buf->ptr, specs[i].cols, rows, 128, err)) {
+                !make_tmap_planes(eng, &specs[i].maps[1], specs[i].buf->ptr, specs[i].cols, rows, 64, err) ||
+                !make_tmap_planes(eng, &specs[i].maps[2], specs[i].buf->ptr, specs[i].cols, rows, 128, err)) {
                 return 0;
             }
             eng->bs_map_key[i] = specs[i].buf->ptr;
@@ -223,7 +227,7 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     bp.h_stride = Iq;
     bp.sfh_atoms = eng->sfh_atoms.as<uint8_t>();
     bp.m_valid = Iq;
-    const int bi = block_n == 32 ? 0 : 1;
+    const int bi = block_n == 32 ? 0 : (block_n == 64 ? 1 : 2);
     CK(launch_gemm_bs(kGateUp, (int)block_n, L->tmap_gu_codes, eng->tmap_xb[bi], bp, eng->num_sms, st, true));
     *launches += 1;
     mark(4);

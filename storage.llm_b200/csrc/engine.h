@@ -109,8 +109,8 @@ struct moe_b200_engine {
     // block-scaled path: quantised activations and intermediate
     // (xb, hb hold a hi plane followed by a lo plane)
     DevBuf xb, sfx_atoms, hb, sfh_atoms, gu_tiles, dn_tiles;
-    // 3-D maps over xb / hb: [0] 32-token box, [1] 128-token box
-    CUtensorMap tmap_xb[2]{}, tmap_hb[2]{};
+    // 3-D maps over xb / hb: [0] 32-token box, [1] 64-token box, [2] 128-token box
+    CUtensorMap tmap_xb[3]{}, tmap_hb[3]{};
     const void* bs_map_key[2] = {nullptr, nullptr};
     uint64_t bs_map_dims[2][2] = {};
     // host-call staging

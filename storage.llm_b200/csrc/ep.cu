@@ -264,6 +264,18 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     const uint32_t n = T * K;
     uint32_t* errw = eng->err_word.as<uint32_t>();
     uint32_t launches = 0;
+    // stage marks (moe_b200_profile_enable): 0 start, 1 router, 2 dispatch
+    // sort + pack, 3 count exchange + host read, 4 row exchange, 5 local
+    // experts, 6 return exchange + combine
+    cudaEvent_t* ev = nullptr;
+    if (eng->prof_max && eng->prof_calls < eng->prof_max) {
+        ev = &eng->prof_events[(size_t)eng->prof_calls * (MOE_B200_STAGES + 1)];
+        ++eng->prof_calls;
+    }
+    auto mark = [&](int i) {
+        if (ev) cudaEventRecord(ev[i], st);
+    };
+    mark(0);
 
     // 1. router on the local tokens
     CK(eng->logits.reserve((size_t)std::max(T, 1u) * E * 4));
@@ -279,6 +291,7 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
                          eng->logits.as<float>(), ids, w, eng->scores.as<float>(), errw, st, &launches));
     }
 
+    mark(1);
     // 2. dispatch: stable sort by owner rank, then pack the send buffers
     CK(ep->dest.reserve((size_t)std::max(n, 1u) * 4));
     CK(ep->pos.reserve((size_t)std::max(n, 1u) * 4));
@@ -322,6 +335,7 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
         CK(cudaMemsetAsync(ep->cnt.ptr, 0, (size_t)(W + 1) * 4, st));
     }
 
+    mark(2);
     // 3. counts, then the rows and their local expert indices
     const NcclApi& nc = nccl();
     NCK(nc.GroupStart());
@@ -332,6 +346,7 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     NCK(nc.GroupEnd());
     CK(cudaMemcpyAsync(ep->h_cnt, ep->cnt.ptr, W * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaMemcpyAsync(ep->h_cnt + W, ep->recv_cnt.ptr, W * 4, cudaMemcpyDeviceToHost, st));
+    mark(3);
     CK(cudaStreamSynchronize(st));
     std::vector<uint32_t> scnt(ep->h_cnt, ep->h_cnt + W), rcnt(ep->h_cnt + W, ep->h_cnt + 2 * W);
     std::vector<uint64_t> soff(W + 1, 0), roff(W + 1, 0);
@@ -352,25 +367,37 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     CK(ep->recv_meta.reserve((size_t)std::max(n_recv, 1u) * 4));
     CK(ep->yloc.reserve((size_t)std::max(rows, 1u) * H * 4));
     CK(ep->ret.reserve((size_t)std::max(n, 1u) * H * 4));
-    NCK(nc.GroupStart());
-    for (uint32_t q = 0; q < W; ++q) {
-        if (scnt[q]) {
-            NCK(nc.Send(ep->send_x.as<uint16_t>() + soff[q] * H, (size_t)scnt[q] * H * 2, ncclUint8, (int)q, comm,
-                        st));
-            NCK(nc.Send(ep->send_meta.as<int32_t>() + soff[q], scnt[q], ncclInt32, (int)q, comm, st));
-        }
-        if (rcnt[q]) {
-            NCK(nc.Recv(ep->recv_x.as<uint16_t>() + roff[q] * H, (size_t)rcnt[q] * H * 2, ncclUint8, (int)q, comm,
-                        st));
-            NCK(nc.Recv(ep->recv_meta.as<int32_t>() + roff[q], rcnt[q], ncclInt32, (int)q, comm, st));
-        }
+    const uint32_t me = (uint32_t)ep->rank;
+    // this rank's own rows: a device copy, not a NCCL self-exchange
+    if (scnt[me]) {
+        CK(cudaMemcpyAsync(ep->recv_x.as<uint16_t>() + roff[me] * H, ep->send_x.as<uint16_t>() + soff[me] * H,
+                           (size_t)scnt[me] * H * 2, cudaMemcpyDeviceToDevice, st));
+        CK(cudaMemcpyAsync(ep->recv_meta.as<int32_t>() + roff[me], ep->send_meta.as<int32_t>() + soff[me],
+                           (size_t)scnt[me] * 4, cudaMemcpyDeviceToDevice, st));
     }
-    NCK(nc.GroupEnd());
+    if (W > 1) {
+        NCK(nc.GroupStart());
+        for (uint32_t q = 0; q < W; ++q) {
+            if (q == me) continue;
+            if (scnt[q]) {
+                NCK(nc.Send(ep->send_x.as<uint16_t>() + soff[q] * H, (size_t)scnt[q] * H * 2, ncclUint8, (int)q,
+                            comm, st));
+                NCK(nc.Send(ep->send_meta.as<int32_t>() + soff[q], scnt[q], ncclInt32, (int)q, comm, st));
+            }
+            if (rcnt[q]) {
+                NCK(nc.Recv(ep->recv_x.as<uint16_t>() + roff[q] * H, (size_t)rcnt[q] * H * 2, ncclUint8, (int)q,
+                            comm, st));
+                NCK(nc.Recv(ep->recv_meta.as<int32_t>() + roff[q], rcnt[q], ncclInt32, (int)q, comm, st));
+            }
+        }
+        NCK(nc.GroupEnd());
+    }
     if (shared_rows) {
         CK(cudaMemcpyAsync(ep->recv_x.as<uint16_t>() + (size_t)n_recv * H, x, (size_t)T * H * 2,
                            cudaMemcpyDeviceToDevice, st));
     }
 
+    mark(4);
     // 4. local experts (+ the shared expert on the local tokens)
     if (ep->slots_key[0] != e0 || ep->slots_key[1] != e_per || ep->slots_key[2] != E) {
         std::vector<uint32_t> slots(e_per + 1);
@@ -397,17 +424,27 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
         if (!run_blockscaled(eng, L, job, st, nullptr, &launches, err)) return 0;
     }
 
+    mark(5);
     // 5. expert rows back to their sources
-    NCK(nc.GroupStart());
-    for (uint32_t q = 0; q < W; ++q) {
-        if (rcnt[q]) {
-            NCK(nc.Send(ep->yloc.as<float>() + roff[q] * H, (size_t)rcnt[q] * H, ncclFloat32, (int)q, comm, st));
-        }
-        if (scnt[q]) {
-            NCK(nc.Recv(ep->ret.as<float>() + soff[q] * H, (size_t)scnt[q] * H, ncclFloat32, (int)q, comm, st));
-        }
+    if (scnt[me]) {
+        CK(cudaMemcpyAsync(ep->ret.as<float>() + soff[me] * H, ep->yloc.as<float>() + roff[me] * H,
+                           (size_t)scnt[me] * H * 4, cudaMemcpyDeviceToDevice, st));
     }
-    NCK(nc.GroupEnd());
+    if (W > 1) {
+        NCK(nc.GroupStart());
+        for (uint32_t q = 0; q < W; ++q) {
+            if (q == me) continue;
+            if (rcnt[q]) {
+                NCK(nc.Send(ep->yloc.as<float>() + roff[q] * H, (size_t)rcnt[q] * H, ncclFloat32, (int)q, comm,
+                            st));
+            }
+            if (scnt[q]) {
+                NCK(nc.Recv(ep->ret.as<float>() + soff[q] * H, (size_t)scnt[q] * H, ncclFloat32, (int)q, comm,
+                            st));
+            }
+        }
+        NCK(nc.GroupEnd());
+    }
 
     // 6. combine in router order
     if (T > 0) {
@@ -415,6 +452,7 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
                           shared ? ep->yloc.as<float>() + (size_t)n_recv * H : nullptr, y_bf16, y_f32, st, false));
         launches += 1;
     }
+    mark(6);
     eng->last_launches = launches;
     return 1;
 }

@@ -48,8 +48,8 @@ namespace moe_b200 {
 
 template <int MODE, int BN>
 struct BsCfg {
-    static_assert(BN == 32 || BN == 128, "tile width");
-    static constexpr bool kStackN = BN == 32;
+    static_assert(BN == 32 || BN == 64 || BN == 128, "tile width");
+    static constexpr bool kStackN = BN <= 64;
     static constexpr int kNA = MODE == kGateUp ? 2 : 1;       // A operands per stage
     static constexpr int kABytes = 128 * 128;                 // smem bytes per A box
     static constexpr int kATx = 128 * 128 / 2;                // packed bytes the A box moves
@@ -70,13 +70,16 @@ struct BsCfg {
 
 // Byte offsets of a token row's hi and lo scale words inside a stage's
 // activation scale block (the tcgen05.cp layout over the B rows).
+// Stacked tiles (32 or 64 tokens): hi rows [0, BN), lo rows [BN, 2 BN) of one
+// 512-byte block; 128-token tiles: a hi block, then a lo block.
+__device__ __forceinline__ uint32_t sf_row_pos(uint32_t row) { return (row % 32) * 16 + (row / 32) * 4; }
 template <int BN>
 __device__ __forceinline__ uint32_t sfb_pos_hi(uint32_t rr) {
-    return BN == 32 ? rr * 16 : (rr % 32) * 16 + (rr / 32) * 4;
+    return sf_row_pos(rr);
 }
 template <int BN>
 __device__ __forceinline__ uint32_t sfb_pos_lo(uint32_t rr) {
-    return BN == 32 ? rr * 16 + 4 : 512 + (rr % 32) * 16 + (rr / 32) * 4;
+    return BN <= 64 ? sf_row_pos(BN + rr) : 512 + sf_row_pos(rr);
 }
 
 __device__ __forceinline__ float pow2f(int e) {
@@ -156,7 +159,7 @@ __global__ void __launch_bounds__(256) gather_quant_bs_kernel(const uint16_t* __
                                                               const uint32_t* __restrict__ row_info, uint32_t rows,
                                                               uint32_t rows_cap, uint8_t* __restrict__ xb,
                                                               uint8_t* __restrict__ sf_atoms) {
-    constexpr uint32_t kAtom = BN == 32 ? 512 : 1024;
+    constexpr uint32_t kAtom = BN <= 64 ? 512 : 1024;
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t nkt = Kp / 128;
     const uint32_t chunks = (nkt + kGqChunk - 1) / kGqChunk;
@@ -274,6 +277,10 @@ cudaError_t launch_gather_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, c
     const uint32_t blocks = (uint32_t)std::min<uint64_t>((tasks + 7) / 8, 148ull * 8ull);
     if (block_n == 32) {
         return launch_kernel(gather_quant_bs_kernel<32>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, row_token,
+                             row_info, rows, rows_cap, xb, sf_atoms);
+    }
+    if (block_n == 64) {
+        return launch_kernel(gather_quant_bs_kernel<64>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, row_token,
                              row_info, rows, rows_cap, xb, sf_atoms);
     }
     return launch_kernel(gather_quant_bs_kernel<128>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, row_token,
@@ -634,11 +641,13 @@ static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, 
 cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
                            int num_sms, cudaStream_t st, bool pdl) {
     if (mode == kGateUp) {
-        return block_n == 32 ? launch_bs_mode<kGateUp, 32>(ta, tb, p, num_sms, st, pdl)
-                             : launch_bs_mode<kGateUp, 128>(ta, tb, p, num_sms, st, pdl);
+        if (block_n == 32) return launch_bs_mode<kGateUp, 32>(ta, tb, p, num_sms, st, pdl);
+        if (block_n == 64) return launch_bs_mode<kGateUp, 64>(ta, tb, p, num_sms, st, pdl);
+        return launch_bs_mode<kGateUp, 128>(ta, tb, p, num_sms, st, pdl);
     }
-    return block_n == 32 ? launch_bs_mode<kDown, 32>(ta, tb, p, num_sms, st, pdl)
-                         : launch_bs_mode<kDown, 128>(ta, tb, p, num_sms, st, pdl);
+    if (block_n == 32) return launch_bs_mode<kDown, 32>(ta, tb, p, num_sms, st, pdl);
+    if (block_n == 64) return launch_bs_mode<kDown, 64>(ta, tb, p, num_sms, st, pdl);
+    return launch_bs_mode<kDown, 128>(ta, tb, p, num_sms, st, pdl);
 }
 
 }  // namespace moe_b200
