@@ -244,6 +244,11 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     bp.y_stride = H;
     bp.m_valid = H;
     bp.y_row_map = job.y_by_source ? eng->row_token.as<uint32_t>() : nullptr;
+    bp.ret_ptrs = job.ret_ptrs;
+    bp.ret_roff = job.ret_roff;
+    bp.ret_base = job.ret_base;
+    bp.ret_rows = job.ret_rows;
+    bp.ret_world = job.ret_world;
     CK(launch_gemm_bs(kDown, (int)block_n, L->tmap_dn_codes, eng->tmap_hb[bi], bp, eng->num_sms, st, true));
     *launches += 1;
     mark(5);

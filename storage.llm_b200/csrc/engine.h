@@ -150,6 +150,13 @@ struct BsJob {
                                  // shared group -> slot E of the layer
     float* y;                    // expert outputs, fp32 rows [*, H]
     bool y_by_source;            // row of y: the source row (else the permuted row)
+    // expert parallelism: source rows below ret_rows are other ranks' tokens,
+    // stored by the down GEMM into their return buffers (see BsParams)
+    float* const* ret_ptrs = nullptr;
+    const uint32_t* ret_roff = nullptr;
+    const uint32_t* ret_base = nullptr;
+    uint32_t ret_rows = 0;
+    uint32_t ret_world = 0;
 };
 
 // Enqueues the pipeline on `st`; fills the engine's permutation buffers

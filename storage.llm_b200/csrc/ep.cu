@@ -4,27 +4,32 @@
 // router and the shared expert are replicated, tokens are data-parallel.
 // One layer call on the rank's own T tokens:
 //   1. router + top-k on the local tokens (full E);
-//   2. dispatch: a stable sort of the T*K assignments by owner rank, then a
-//      pack kernel writing each assignment's token row (bf16 [H]) and its
-//      expert index local to the owner into the send buffers;
-//   3. NCCL: per-rank row counts (one 4-byte send/recv per peer), one host
-//      read of the counts to size the exchange, then grouped send/recv of
-//      the rows and their expert indices (an all-to-allv);
-//   4. the block-scaled pipeline on the received rows, grouped by (local
-//      expert, source rank, source order); the shared expert's rows (the
-//      rank's own tokens) ride along as the extra group.  The down GEMM
-//      writes each output row at its receive position;
-//   5. NCCL: the fp32 expert rows go back to their source ranks (the
-//      reverse all-to-allv), landing at the positions they were sent from;
-//   6. the combine of the single-device path: shared row + the K expert rows
-//      in router order, one fused multiply-add each.
-// Because every row's expert output and the combine order are the same as on
-// one device, a rank's result equals the single-device result for its
-// tokens wherever both pick the same GEMM tile width.
+//   2. a stable sort of the T*K assignments by owner rank;
+//   3. NCCL all-gather of the per-rank row counts (the W x W count matrix),
+//      read once on the host: every rank then knows where each of its rows
+//      lands in every other rank's receive buffer;
+//   4. dispatch kernel: each assignment's token row (bf16 [H]) and its
+//      owner-local expert index are stored straight into the owner's receive
+//      buffer over NVLink (peer memory opened with CUDA IPC);
+//   5. exchange barrier (a 4-byte NCCL all-reduce), then the block-scaled
+//      pipeline on the received rows, grouped by (local expert, source rank,
+//      source order); the shared expert's rows (the rank's own tokens) ride
+//      along as the extra group.  The down GEMM's epilogue stores every
+//      expert row straight into its source rank's return buffer, at the
+//      position the row was sent from: compute and the return exchange are
+//      one kernel, tile by tile;
+//   6. barrier, then the single-device combine: shared row + the K expert
+//      rows in router order, one fused multiply-add each.
+// Every row's expert output and the combine order are those of one device,
+// so a rank's result equals the single-device result for its tokens wherever
+// both pick the same GEMM tile width.
 //
-// NCCL is opened at run time (the copy the process already loaded, e.g.
-// PyTorch's, else libnccl.so.2), so the library loads without it and only
-// these entry points report its absence.
+// The receive and return buffers are symmetric: each rank allocates its own
+// and maps every peer's; they grow collectively (all ranks decide from the
+// same count matrix) and their IPC handles are re-exchanged then.  NCCL is
+// opened at run time (the copy the process already loaded, e.g. PyTorch's,
+// else libnccl.so.2), so the library loads without it and only these entry
+// points report its absence.
 #include <dlfcn.h>
 #include <nccl.h>  // types and prototypes only; no link-time dependency
 
@@ -46,6 +51,8 @@ struct NcclApi {
     decltype(&ncclGroupEnd) GroupEnd = nullptr;
     decltype(&ncclSend) Send = nullptr;
     decltype(&ncclRecv) Recv = nullptr;
+    decltype(&ncclAllGather) AllGather = nullptr;
+    decltype(&ncclAllReduce) AllReduce = nullptr;
     decltype(&ncclGetErrorString) GetErrorString = nullptr;
 };
 
@@ -63,9 +70,11 @@ const NcclApi& nccl() {
         api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
         api.Send = reinterpret_cast<decltype(api.Send)>(dlsym(h, "ncclSend"));
         api.Recv = reinterpret_cast<decltype(api.Recv)>(dlsym(h, "ncclRecv"));
+        api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
+        api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
         api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
         api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.GroupStart && api.GroupEnd &&
-                 api.Send && api.Recv && api.GetErrorString;
+                 api.Send && api.Recv && api.AllGather && api.AllReduce && api.GetErrorString;
     });
     return api;
 }
@@ -87,47 +96,142 @@ __global__ void ep_owner_kernel(const int32_t* __restrict__ ids, uint32_t n, uin
     }
 }
 
-// Send buffers in owner order: row p carries the token row of assignment
-// row_asg[p] and that assignment's expert index local to its owner.  One
-// warp per row, 16-byte vectors (H is a multiple of 8).
-__global__ void ep_pack_kernel(const uint16_t* __restrict__ x, uint32_t H, uint32_t K, uint32_t e_per,
-                               const int32_t* __restrict__ ids, const uint32_t* __restrict__ row_asg, uint32_t n,
-                               uint16_t* __restrict__ send_x, int32_t* __restrict__ send_meta) {
+// Dispatch: row p of the owner-ordered assignment list (p in [soff[q],
+// soff[q+1]) goes to rank q) is stored into rank q's receive buffer at row
+// dst_off[q] + p - soff[q]: the assignment's token row and its expert index
+// local to q.  One warp per row, 16-byte stores (H is a multiple of 8), into
+// peer memory for q != this rank.
+__global__ void ep_dispatch_kernel(const uint16_t* __restrict__ x, uint32_t H, uint32_t K, uint32_t e_per,
+                                   const int32_t* __restrict__ ids, const uint32_t* __restrict__ row_asg, uint32_t n,
+                                   const uint32_t* __restrict__ soff, const uint32_t* __restrict__ dst_off,
+                                   uint16_t* const* __restrict__ peer_x, int32_t* const* __restrict__ peer_meta,
+                                   uint32_t world) {
     pdl_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     for (uint32_t p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < n; p += warps) {
+        uint32_t q = 0;
+        while (q + 1 < world && __ldg(soff + q + 1) <= p) ++q;
+        const uint64_t row = (uint64_t)__ldg(dst_off + q) + p - __ldg(soff + q);
         const uint32_t a = row_asg[p];
         const uint4* src = reinterpret_cast<const uint4*>(x + (uint64_t)(a / K) * H);
-        uint4* dst = reinterpret_cast<uint4*>(send_x + (uint64_t)p * H);
+        uint4* dst = reinterpret_cast<uint4*>(peer_x[q] + row * H);
         for (uint32_t v = lane; v < H / 8; v += 32) dst[v] = __ldg(src + v);
-        if (lane == 0) send_meta[p] = ids[a] % (int32_t)e_per;
+        if (lane == 0) peer_meta[q][row] = ids[a] % (int32_t)e_per;
     }
+    __threadfence_system();  // peer stores before the exchange barrier
 }
 
 }  // namespace
+
+// A buffer every rank allocates and every peer maps (CUDA IPC).
+struct SymBuf {
+    DevBuf local;
+    std::vector<void*> peer;  // peer[q]: rank q's buffer as mapped here (this rank's own: local)
+};
 
 struct EpState {
     void* comm = nullptr;  // ncclComm_t
     int rank = 0, world = 1;
     // dispatch permutation (by owner rank)
     DevBuf dest, pos, row_tok, row_asg, cnt, off, gu_off, dn_off, tile_counts, rank_buf;
-    DevBuf recv_cnt, slots;
-    DevBuf send_x, send_meta, recv_x, recv_meta, yloc, ret;
-    uint32_t* h_cnt = nullptr;  // pinned: [world] sent, [world] received
+    DevBuf mat;        // W x W row counts: mat[r][q] = rows rank r sends to rank q
+    DevBuf small;      // per call: dst_off[W], roff[W+1], sbase[W]
+    DevBuf ptrs;       // device copies of the peer pointers: x[W], meta[W], ret[W]
+    DevBuf barrier_word, slots, yloc, handles;
+    SymBuf recv_x, recv_meta, ret;  // receive rows, their expert indices; returned expert rows
+    std::vector<uint64_t> cap_x, cap_meta, cap_ret;  // every rank's capacities (bytes), the same on all ranks
+    uint32_t* h_mat = nullptr;    // pinned [W x W]
+    uint32_t* h_small = nullptr;  // pinned [3W + 1]
     std::vector<uint32_t> last_sent, last_recv;
     uint32_t slots_key[3] = {~0u, ~0u, ~0u};
 };
 
+void close_peers(EpState* ep, SymBuf& b) {
+    for (size_t q = 0; q < b.peer.size(); ++q) {
+        if ((int)q != ep->rank && b.peer[q]) cudaIpcCloseMemHandle(b.peer[q]);
+    }
+    b.peer.assign(ep->world, nullptr);
+}
+
 void ep_release(EpState* ep) {
     if (!ep) return;
+    close_peers(ep, ep->recv_x);
+    close_peers(ep, ep->recv_meta);
+    close_peers(ep, ep->ret);
     if (ep->comm && nccl().ok) nccl().CommDestroy(static_cast<ncclComm_t>(ep->comm));
     DevBuf* bufs[] = {&ep->dest, &ep->pos, &ep->row_tok, &ep->row_asg, &ep->cnt, &ep->off, &ep->gu_off,
-                      &ep->dn_off, &ep->tile_counts, &ep->rank_buf, &ep->recv_cnt, &ep->slots, &ep->send_x,
-                      &ep->send_meta, &ep->recv_x, &ep->recv_meta, &ep->yloc, &ep->ret};
+                      &ep->dn_off, &ep->tile_counts, &ep->rank_buf, &ep->mat, &ep->small, &ep->ptrs,
+                      &ep->barrier_word, &ep->slots, &ep->yloc, &ep->handles, &ep->recv_x.local,
+                      &ep->recv_meta.local, &ep->ret.local};
     for (DevBuf* b : bufs) b->release();
-    if (ep->h_cnt) cudaFreeHost(ep->h_cnt);
+    if (ep->h_mat) cudaFreeHost(ep->h_mat);
+    if (ep->h_small) cudaFreeHost(ep->h_small);
     delete ep;
+}
+
+// Makes every rank's receive/return buffers at least as large as this call
+// needs (all ranks decide from the same count matrix and token counts, so
+// they agree without talking), then re-exchanges the IPC handles.
+// Collective; the stream must be idle on every rank (it is: the count
+// matrix was just read with a stream synchronisation).
+int ep_ensure_capacity(EpState* ep, const std::vector<uint64_t>& need_x, const std::vector<uint64_t>& need_meta,
+                       const std::vector<uint64_t>& need_ret, cudaStream_t st, char* err) {
+    const uint32_t W = (uint32_t)ep->world, me = (uint32_t)ep->rank;
+    bool grow = false;
+    for (uint32_t q = 0; q < W; ++q) {
+        grow = grow || need_x[q] > ep->cap_x[q] || need_meta[q] > ep->cap_meta[q] || need_ret[q] > ep->cap_ret[q];
+    }
+    if (!grow) return 1;
+    const NcclApi& nc = nccl();
+    ncclComm_t comm = static_cast<ncclComm_t>(ep->comm);
+    auto bump = [](uint64_t need, uint64_t cap) {
+        return need > cap ? std::max<uint64_t>(need + need / 4, 1u << 16) : cap;
+    };
+    for (uint32_t q = 0; q < W; ++q) {
+        ep->cap_x[q] = bump(need_x[q], ep->cap_x[q]);
+        ep->cap_meta[q] = bump(need_meta[q], ep->cap_meta[q]);
+        ep->cap_ret[q] = bump(need_ret[q], ep->cap_ret[q]);
+    }
+    // nobody may still use an old mapping when a rank frees its old buffer
+    close_peers(ep, ep->recv_x);
+    close_peers(ep, ep->recv_meta);
+    close_peers(ep, ep->ret);
+    NCK(nc.AllReduce(ep->barrier_word.ptr, ep->barrier_word.ptr, 1, ncclUint32, ncclSum, comm, st));
+    CK(cudaStreamSynchronize(st));
+    SymBuf* bufs[3] = {&ep->recv_x, &ep->recv_meta, &ep->ret};
+    const uint64_t caps[3] = {ep->cap_x[me], ep->cap_meta[me], ep->cap_ret[me]};
+    for (int i = 0; i < 3; ++i) CK(bufs[i]->local.reserve(caps[i]));
+    cudaIpcMemHandle_t mine[3];
+    for (int i = 0; i < 3; ++i) CK(cudaIpcGetMemHandle(&mine[i], bufs[i]->local.ptr));
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    CK(ep->handles.reserve(hb * 3 * (W + 1)));
+    uint8_t* d_h = ep->handles.as<uint8_t>();
+    CK(cudaMemcpyAsync(d_h, mine, hb * 3, cudaMemcpyHostToDevice, st));
+    NCK(nc.AllGather(d_h, d_h + hb * 3, hb * 3, ncclUint8, comm, st));
+    std::vector<cudaIpcMemHandle_t> all(3 * W);
+    CK(cudaMemcpyAsync(all.data(), d_h + hb * 3, hb * 3 * W, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    for (uint32_t q = 0; q < W; ++q) {
+        for (int i = 0; i < 3; ++i) {
+            if (q == me) {
+                bufs[i]->peer[q] = bufs[i]->local.ptr;
+            } else {
+                void* ptr = nullptr;
+                CK(cudaIpcOpenMemHandle(&ptr, all[3 * q + i], cudaIpcMemLazyEnablePeerAccess));
+                bufs[i]->peer[q] = ptr;
+            }
+        }
+    }
+    std::vector<void*> dev_ptrs(3 * W);
+    for (uint32_t q = 0; q < W; ++q) {
+        dev_ptrs[q] = ep->recv_x.peer[q];
+        dev_ptrs[W + q] = ep->recv_meta.peer[q];
+        dev_ptrs[2 * W + q] = ep->ret.peer[q];
+    }
+    CK(ep->ptrs.reserve(sizeof(void*) * 3 * W));
+    CK(cudaMemcpy(ep->ptrs.ptr, dev_ptrs.data(), sizeof(void*) * 3 * W, cudaMemcpyHostToDevice));
+    return 1;
 }
 
 }  // namespace moe_b200
@@ -187,8 +291,16 @@ int moe_b200_ep_init(moe_b200_engine_t* eng, int rank, int world, const uint8_t*
         return 0;
     }
     ep->comm = comm;
-    if (cudaMallocHost(&ep->h_cnt, sizeof(uint32_t) * 2 * world) != cudaSuccess) {
-        set_err(err, "pinned allocation failed");
+    ep->recv_x.peer.assign(world, nullptr);
+    ep->recv_meta.peer.assign(world, nullptr);
+    ep->ret.peer.assign(world, nullptr);
+    ep->cap_x.assign(world, 0);
+    ep->cap_meta.assign(world, 0);
+    ep->cap_ret.assign(world, 0);
+    if (cudaMallocHost(&ep->h_mat, sizeof(uint32_t) * world * world) != cudaSuccess ||
+        cudaMallocHost(&ep->h_small, sizeof(uint32_t) * (3 * world + 1)) != cudaSuccess ||
+        ep->barrier_word.reserve(4) != cudaSuccess || cudaMemset(ep->barrier_word.ptr, 0, 4) != cudaSuccess) {
+        set_err(err, "allocation failed");
         ep_release(ep);
         return 0;
     }
@@ -292,7 +404,7 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     }
 
     mark(1);
-    // 2. dispatch: stable sort by owner rank, then pack the send buffers
+    // 2. stable sort of the assignments by owner rank
     CK(ep->dest.reserve((size_t)std::max(n, 1u) * 4));
     CK(ep->pos.reserve((size_t)std::max(n, 1u) * 4));
     CK(ep->row_tok.reserve((size_t)std::max(n, 1u) * 4));
@@ -303,9 +415,7 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     CK(ep->off.reserve((size_t)(W + 1) * 4));
     CK(ep->gu_off.reserve((size_t)(W + 1) * 4));
     CK(ep->dn_off.reserve((size_t)(W + 1) * 4));
-    CK(ep->recv_cnt.reserve((size_t)W * 4));
-    CK(ep->send_x.reserve((size_t)std::max(n, 1u) * H * 2));
-    CK(ep->send_meta.reserve((size_t)std::max(n, 1u) * 4));
+    CK(ep->mat.reserve((size_t)W * W * 4));
     GroupInfo gd;
     gd.count = ep->cnt.as<uint32_t>();
     gd.offset = ep->off.as<uint32_t>();
@@ -327,78 +437,90 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
                               ep->rank_buf.as<uint32_t>(), gd, ep->pos.as<uint32_t>(), ep->row_tok.as<uint32_t>(),
                               ep->row_asg.as<uint32_t>(), nullptr, errw, st));
         }
-        CK(launch_kernel(ep_pack_kernel, dim3(std::min(ceil_div(n, 8u), 148u * 8u)), dim3(256), 0, st, true, x, H,
-                         K, e_per, (const int32_t*)ids, (const uint32_t*)ep->row_asg.as<uint32_t>(), n,
-                         ep->send_x.as<uint16_t>(), ep->send_meta.as<int32_t>()));
-        launches += 4;
+        launches += 2;
     } else {
         CK(cudaMemsetAsync(ep->cnt.ptr, 0, (size_t)(W + 1) * 4, st));
+        CK(cudaMemsetAsync(ep->off.ptr, 0, (size_t)(W + 1) * 4, st));
     }
-
     mark(2);
-    // 3. counts, then the rows and their local expert indices
+
+    // 3. the W x W count matrix, read once on the host
     const NcclApi& nc = nccl();
-    NCK(nc.GroupStart());
-    for (uint32_t q = 0; q < W; ++q) {
-        NCK(nc.Send(ep->cnt.as<uint32_t>() + q, 1, ncclUint32, (int)q, comm, st));
-        NCK(nc.Recv(ep->recv_cnt.as<uint32_t>() + q, 1, ncclUint32, (int)q, comm, st));
-    }
-    NCK(nc.GroupEnd());
-    CK(cudaMemcpyAsync(ep->h_cnt, ep->cnt.ptr, W * 4, cudaMemcpyDeviceToHost, st));
-    CK(cudaMemcpyAsync(ep->h_cnt + W, ep->recv_cnt.ptr, W * 4, cudaMemcpyDeviceToHost, st));
-    mark(3);
+    NCK(nc.AllGather(ep->cnt.ptr, ep->mat.ptr, W, ncclUint32, comm, st));
+    CK(cudaMemcpyAsync(ep->h_mat, ep->mat.ptr, (size_t)W * W * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
-    std::vector<uint32_t> scnt(ep->h_cnt, ep->h_cnt + W), rcnt(ep->h_cnt + W, ep->h_cnt + 2 * W);
-    std::vector<uint64_t> soff(W + 1, 0), roff(W + 1, 0);
-    for (uint32_t q = 0; q < W; ++q) {
-        soff[q + 1] = soff[q] + scnt[q];
-        roff[q + 1] = roff[q] + rcnt[q];
+    const uint32_t me = (uint32_t)ep->rank;
+    auto M = [&](uint32_t r, uint32_t q) -> uint64_t { return ep->h_mat[(size_t)r * W + q]; };
+    std::vector<uint64_t> n_of(W, 0), recv_of(W, 0);
+    for (uint32_t r = 0; r < W; ++r) {
+        for (uint32_t q = 0; q < W; ++q) {
+            n_of[r] += M(r, q);
+            recv_of[q] += M(r, q);
+        }
     }
-    if (soff[W] != n) {
-        set_err(err, "dispatch counted %llu rows for %u assignments", (unsigned long long)soff[W], n);
+    if (n_of[me] != n) {
+        set_err(err, "dispatch counted %llu rows for %u assignments", (unsigned long long)n_of[me], n);
         return 0;
     }
-    ep->last_sent = scnt;
-    ep->last_recv = rcnt;
-    const uint32_t n_recv = (uint32_t)roff[W];
+    const uint32_t n_recv = (uint32_t)recv_of[me];
     const uint32_t shared_rows = shared ? T : 0;
     const uint32_t rows = n_recv + shared_rows;  // rows the local experts run on
-    CK(ep->recv_x.reserve((size_t)std::max(rows, 1u) * H * 2));
-    CK(ep->recv_meta.reserve((size_t)std::max(n_recv, 1u) * 4));
-    CK(ep->yloc.reserve((size_t)std::max(rows, 1u) * H * 4));
-    CK(ep->ret.reserve((size_t)std::max(n, 1u) * H * 4));
-    const uint32_t me = (uint32_t)ep->rank;
-    // this rank's own rows: a device copy, not a NCCL self-exchange
-    if (scnt[me]) {
-        CK(cudaMemcpyAsync(ep->recv_x.as<uint16_t>() + roff[me] * H, ep->send_x.as<uint16_t>() + soff[me] * H,
-                           (size_t)scnt[me] * H * 2, cudaMemcpyDeviceToDevice, st));
-        CK(cudaMemcpyAsync(ep->recv_meta.as<int32_t>() + roff[me], ep->send_meta.as<int32_t>() + soff[me],
-                           (size_t)scnt[me] * 4, cudaMemcpyDeviceToDevice, st));
-    }
-    if (W > 1) {
-        NCK(nc.GroupStart());
+    {
+        std::vector<uint64_t> need_x(W), need_meta(W), need_ret(W);
         for (uint32_t q = 0; q < W; ++q) {
-            if (q == me) continue;
-            if (scnt[q]) {
-                NCK(nc.Send(ep->send_x.as<uint16_t>() + soff[q] * H, (size_t)scnt[q] * H * 2, ncclUint8, (int)q,
-                            comm, st));
-                NCK(nc.Send(ep->send_meta.as<int32_t>() + soff[q], scnt[q], ncclInt32, (int)q, comm, st));
-            }
-            if (rcnt[q]) {
-                NCK(nc.Recv(ep->recv_x.as<uint16_t>() + roff[q] * H, (size_t)rcnt[q] * H * 2, ncclUint8, (int)q,
-                            comm, st));
-                NCK(nc.Recv(ep->recv_meta.as<int32_t>() + roff[q], rcnt[q], ncclInt32, (int)q, comm, st));
-            }
+            const uint64_t tq = n_of[q] / K;  // rank q's tokens
+            need_x[q] = (recv_of[q] + (shared ? tq : 0)) * H * 2 + 16;
+            need_meta[q] = recv_of[q] * 4 + 16;
+            need_ret[q] = n_of[q] * H * 4 + 16;
         }
-        NCK(nc.GroupEnd());
+        if (!ep_ensure_capacity(ep, need_x, need_meta, need_ret, st, err)) return 0;
     }
-    if (shared_rows) {
-        CK(cudaMemcpyAsync(ep->recv_x.as<uint16_t>() + (size_t)n_recv * H, x, (size_t)T * H * 2,
-                           cudaMemcpyDeviceToDevice, st));
+    // where this rank's rows land in each owner's buffer, where each source's
+    // rows sit in this rank's receive buffer, and where each source expects
+    // its returned rows
+    ep->last_sent.assign(W, 0);
+    ep->last_recv.assign(W, 0);
+    uint32_t* hs = ep->h_small;  // dst_off[W], roff[W+1], sbase[W]
+    for (uint32_t q = 0; q < W; ++q) {
+        uint64_t o = 0;
+        for (uint32_t r = 0; r < me; ++r) o += M(r, q);
+        hs[q] = (uint32_t)o;
+        ep->last_sent[q] = (uint32_t)M(me, q);
+        ep->last_recv[q] = (uint32_t)M(q, me);
     }
+    hs[W] = 0;
+    for (uint32_t r = 0; r < W; ++r) hs[W + 1 + r] = hs[W + r] + (uint32_t)M(r, me);
+    for (uint32_t r = 0; r < W; ++r) {
+        uint64_t o = 0;
+        for (uint32_t q = 0; q < me; ++q) o += M(r, q);
+        hs[2 * W + 1 + r] = (uint32_t)o;
+    }
+    CK(ep->small.reserve((size_t)(3 * W + 1) * 4));
+    CK(cudaMemcpyAsync(ep->small.ptr, hs, (size_t)(3 * W + 1) * 4, cudaMemcpyHostToDevice, st));
+    const uint32_t* d_dst_off = ep->small.as<uint32_t>();
+    const uint32_t* d_roff = d_dst_off + W;
+    const uint32_t* d_sbase = d_roff + W + 1;
+    void** d_ptrs = ep->ptrs.as<void*>();
 
+    // 4. dispatch into the owners' receive buffers
+    if (n > 0) {
+        CK(launch_kernel(ep_dispatch_kernel, dim3(std::min(ceil_div(n, 8u), 148u * 8u)), dim3(256), 0, st, false, x,
+                         H, K, e_per, (const int32_t*)ids, (const uint32_t*)ep->row_asg.as<uint32_t>(), n,
+                         (const uint32_t*)ep->off.as<uint32_t>(), d_dst_off,
+                         reinterpret_cast<uint16_t* const*>(d_ptrs), reinterpret_cast<int32_t* const*>(d_ptrs + W),
+                         W));
+        launches += 1;
+    }
+    uint16_t* recv_x = ep->recv_x.local.as<uint16_t>();
+    if (shared_rows) {
+        CK(cudaMemcpyAsync(recv_x + (size_t)n_recv * H, x, (size_t)T * H * 2, cudaMemcpyDeviceToDevice, st));
+    }
+    NCK(nc.AllReduce(ep->barrier_word.ptr, ep->barrier_word.ptr, 1, ncclUint32, ncclSum, comm, st));
+    mark(3);
     mark(4);
-    // 4. local experts (+ the shared expert on the local tokens)
+
+    // 5. local experts (+ the shared expert on the local tokens); the down
+    //    GEMM stores other ranks' rows into their return buffers
     if (ep->slots_key[0] != e0 || ep->slots_key[1] != e_per || ep->slots_key[2] != E) {
         std::vector<uint32_t> slots(e_per + 1);
         for (uint32_t g = 0; g < e_per; ++g) slots[g] = e0 + g;
@@ -409,46 +531,32 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
         ep->slots_key[1] = e_per;
         ep->slots_key[2] = E;
     }
+    CK(ep->yloc.reserve((size_t)std::max(rows, 1u) * H * 4));
     if (rows > 0) {
         BsJob job{};
-        job.ids = ep->recv_meta.as<int32_t>();
+        job.ids = ep->recv_meta.local.as<int32_t>();
         job.T = n_recv;
         job.K = 1;
         job.E = e_per;
         job.shared_rows = shared_rows;
         job.shared_base = n_recv;
-        job.src = ep->recv_x.as<uint16_t>();
+        job.src = recv_x;
         job.group_slot = ep->slots.as<uint32_t>();
         job.y = ep->yloc.as<float>();
         job.y_by_source = true;
+        job.ret_ptrs = reinterpret_cast<float* const*>(d_ptrs + 2 * W);
+        job.ret_roff = d_roff;
+        job.ret_base = d_sbase;
+        job.ret_rows = n_recv;
+        job.ret_world = W;
         if (!run_blockscaled(eng, L, job, st, nullptr, &launches, err)) return 0;
     }
-
     mark(5);
-    // 5. expert rows back to their sources
-    if (scnt[me]) {
-        CK(cudaMemcpyAsync(ep->ret.as<float>() + soff[me] * H, ep->yloc.as<float>() + roff[me] * H,
-                           (size_t)scnt[me] * H * 4, cudaMemcpyDeviceToDevice, st));
-    }
-    if (W > 1) {
-        NCK(nc.GroupStart());
-        for (uint32_t q = 0; q < W; ++q) {
-            if (q == me) continue;
-            if (rcnt[q]) {
-                NCK(nc.Send(ep->yloc.as<float>() + roff[q] * H, (size_t)rcnt[q] * H, ncclFloat32, (int)q, comm,
-                            st));
-            }
-            if (scnt[q]) {
-                NCK(nc.Recv(ep->ret.as<float>() + soff[q] * H, (size_t)scnt[q] * H, ncclFloat32, (int)q, comm,
-                            st));
-            }
-        }
-        NCK(nc.GroupEnd());
-    }
 
-    // 6. combine in router order
+    // 6. once every rank's rows are back: combine in router order
+    NCK(nc.AllReduce(ep->barrier_word.ptr, ep->barrier_word.ptr, 1, ncclUint32, ncclSum, comm, st));
     if (T > 0) {
-        CK(launch_combine(ep->ret.as<float>(), H, ep->pos.as<uint32_t>(), w, T, K,
+        CK(launch_combine(ep->ret.local.as<float>(), H, ep->pos.as<uint32_t>(), w, T, K,
                           shared ? ep->yloc.as<float>() + (size_t)n_recv * H : nullptr, y_bf16, y_f32, st, false));
         launches += 1;
     }

@@ -602,7 +602,15 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                         if (c0 + i < tc.nn) {
                             const uint64_t prow = row0 + c0 + i;
                             const uint64_t orow = p.y_row_map ? __ldg(p.y_row_map + prow) : prow;
-                            p.y_out[orow * p.y_stride + m] = v0[i];
+                            float* dst = p.y_out + orow * p.y_stride;
+                            if (p.ret_ptrs && orow < p.ret_rows) {
+                                // another rank's token: into its return buffer over NVLink
+                                uint32_t r = 0;
+                                while (r + 1 < p.ret_world && __ldg(p.ret_roff + r + 1) <= orow) ++r;
+                                dst = p.ret_ptrs[r] +
+                                      ((uint64_t)__ldg(p.ret_base + r) + orow - __ldg(p.ret_roff + r)) * p.y_stride;
+                            }
+                            dst[m] = v0[i];
                         }
                     }
                 }
@@ -614,6 +622,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 accphase ^= 1;
             }
         }
+        if (MODE == kDown && p.ret_ptrs) __threadfence_system();  // peer stores before the exchange barrier
     }
 
     tc_fence_before();

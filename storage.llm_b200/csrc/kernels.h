@@ -68,6 +68,15 @@ struct BsParams {
     uint32_t m_valid;         // output rows to write (down)
     const uint32_t* group_slot;  // weight slot of each group; null: the group index itself
     const uint32_t* y_row_map;   // down: output row of each permuted row; null: the permuted row
+    // down, expert parallelism: output rows below ret_rows belong to other
+    // ranks' tokens and are stored straight into the source rank's return
+    // buffer (peer memory): rows [ret_roff[r], ret_roff[r+1]) came from rank
+    // r and go to ret_ptrs[r] starting at row ret_base[r].  Null: y_out only.
+    float* const* ret_ptrs;
+    const uint32_t* ret_roff;
+    const uint32_t* ret_base;
+    uint32_t ret_rows;
+    uint32_t ret_world;
     uint32_t* err;
 };
 
