@@ -237,6 +237,36 @@ class StdoutToStderr:
         os.close(self.saved)
 
 
+def calibrate_placement(shape, li, rank, world, dist, tokens):
+    """Expert placement with replication from a calibration batch (not the
+    timed tokens): per-expert routing counts summed over the ranks, experts
+    whose load exceeds a rank's share split into replicas, replicas placed
+    largest first on the least-loaded rank not yet holding that expert.
+    Every rank computes the same placement from the same counts."""
+    import torch
+    import moe_b200.synth as synth
+    xc = synth.gen_tokens(shape, tokens, seed=900 + rank, mu=li.mu)
+    xf = (xc.astype(np.uint32) << 16).view(np.float32)
+    wf = (np.ascontiguousarray(li.router).astype(np.uint32) << 16).view(np.float32)
+    logits = xf @ wf.T  # routing decisions only; the layer itself routes exactly
+    top = np.argsort(-logits, axis=1, kind="stable")[:, :shape.top_k]
+    counts = torch.tensor(np.bincount(top.ravel(), minlength=shape.experts).astype(np.float64), device="cuda")
+    dist.all_reduce(counts)
+    counts = counts.cpu().numpy()
+    E = shape.experts
+    share = counts.sum() / world
+    reps = [int(min(world, max(1, np.ceil(c / max(share, 1.0))))) for c in counts]
+    items = sorted(((counts[e] / reps[e], e) for e in range(E) for _ in range(reps[e])), key=lambda t: (-t[0], t[1]))
+    load = np.zeros(world)
+    placement = [[] for _ in range(E)]
+    for w_, e in items:
+        order = sorted(range(world), key=lambda q: (load[q], q))
+        q = next(q for q in order if q not in placement[e])
+        placement[e].append(q)
+        load[q] += w_
+    return placement, (load.max() / max(load.mean(), 1e-9))
+
+
 def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     """--gpus N > 1: moe_b200_ep_layer_forward on every rank (see the module docstring)."""
     import ctypes as C
@@ -250,6 +280,8 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
         dist.broadcast_object_list(uid, src=0)
         eng.ep_init(rank, world, uid[0])
         dist.barrier()
+    placement, planned_imbalance = calibrate_placement(shape, li, rank, world, dist, T)
+    eng.ep_set_placement(placement)
     eng.upload_layer_ep(li)
     cfg = L.Engine.cfg(shape, gemm_path=L.GEMM_BLOCKSCALED)
     x = torch.from_numpy(li.x.view(np.int16)).cuda()
@@ -327,7 +359,7 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     # whole-layer HBM roofline of one rank: its expert block's MXFP4 bytes
     # (every local expert is routed to at these batch sizes) + its token rows
     hbm, _, peak_kind = measured_peaks()
-    e_loc = shape.experts // world
+    e_loc = len(eng.ep_local_expert_list(shape.experts))
     layer_bytes = e_loc * 3 * shape.intermediate * H * 17 / 32 + T * H * 2 * 2 + 2 * T * K * H * 2
     achieved = layer_bytes / (ms / args.steps / 1000.0) / 1e9
     result = {
@@ -341,6 +373,9 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
                      "traffic": None, "algorithmic_bytes_per_launch": layer_bytes,
                      "launch_ms": ms / args.steps},
         "expert_parallel": {"experts_per_gpu": e_loc, "rows_received_per_rank": rows_all,
+                            "placement": "replicated, calibrated on a separate batch",
+                            "replicas_per_expert": [len(r) for r in placement],
+                            "planned_imbalance": planned_imbalance,
                             "load_imbalance_max_over_mean": imbalance, "phase_ms_rank0": ep_phases},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),

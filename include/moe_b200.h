@@ -182,13 +182,15 @@ MOE_B200_API int moe_b200_group_tokens_by_expert_noalloc(const moe_b200_assignme
  * (generation_mlp.cpp.inc:1023-1431) when the experts are spread over
  * several devices; the reference has no multi-device counterpart.
  *
- * Rank r of `world` owns experts [r*E/world, (r+1)*E/world) (E must split
- * evenly); the router and the shared expert are replicated and each rank
- * feeds its own tokens.  Every rank uploads the router, its own experts and
- * (if used) the shared expert, then all ranks call
- * moe_b200_ep_layer_forward together.  The exchange uses NCCL, opened at
- * run time (libnccl.so.2); the call synchronises its stream once, after the
- * per-rank row counts are exchanged, to size the row exchange.
+ * By default rank r of `world` owns experts [r*E/world, (r+1)*E/world);
+ * moe_b200_ep_set_placement spreads and replicates them instead.  The
+ * router and the shared expert are replicated and each rank feeds its own
+ * tokens.  Every rank uploads the router, its own experts and (if used) the
+ * shared expert, then all ranks call moe_b200_ep_layer_forward together.
+ * Rows move over NVLink peer memory (CUDA IPC mappings of every rank's
+ * receive and return buffers); NCCL, opened at run time (libnccl.so.2),
+ * carries the per-rank row counts and two barriers; the call synchronises
+ * its stream once, after the counts arrive, to size the exchange.
  * ------------------------------------------------------------------------ */
 #define MOE_B200_EP_UID_BYTES 128
 /* A fresh communicator id (ncclGetUniqueId); create it on one rank and
@@ -196,9 +198,22 @@ MOE_B200_API int moe_b200_group_tokens_by_expert_noalloc(const moe_b200_assignme
 MOE_B200_API int moe_b200_ep_unique_id(uint8_t* out_uid, char* err);
 /* Joins the communicator (collective over all `world` ranks). */
 MOE_B200_API int moe_b200_ep_init(moe_b200_engine_t* engine, int rank, int world, const uint8_t* uid, char* err);
-/* This rank's expert block for a layer of `experts` experts. */
+/* This rank's expert block for a layer of `experts` experts under the
+ * default placement (contiguous blocks). */
 MOE_B200_API int moe_b200_ep_local_experts(moe_b200_engine_t* engine, uint32_t experts, uint32_t* first,
                                            uint32_t* count, char* err);
+/* Expert placement with replication (load balance under skewed routing):
+ * expert e lives on replica_count[e] ranks, listed consecutively in
+ * replica_ranks; the tokens routed to a replicated expert are spread over its
+ * replicas in turn (token index modulo the replica count).  Every rank must
+ * set the same placement, upload the experts of its list
+ * (moe_b200_ep_local_expert_list) and call the forward afterwards. */
+MOE_B200_API int moe_b200_ep_set_placement(moe_b200_engine_t* engine, uint32_t experts,
+                                           const uint32_t* replica_count, const uint32_t* replica_ranks, char* err);
+/* This rank's experts under the current placement (the default one when none
+ * was set), ascending; `capacity` entries available in `out`. */
+MOE_B200_API int moe_b200_ep_local_expert_list(moe_b200_engine_t* engine, uint32_t experts, uint32_t* out,
+                                               uint32_t capacity, uint32_t* count, char* err);
 /* The layer on this rank's T tokens (device pointers, caller's stream; the
  * same outputs as moe_b200_layer_forward for those tokens).  Block-scaled
  * GEMM path only.  T may be 0 (the rank still serves its experts). */

@@ -88,21 +88,30 @@ const NcclApi& nccl() {
         }                                                                              \
     } while (0)
 
-// dest[a] = owner rank of assignment a's expert.
-__global__ void ep_owner_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t e_per,
-                                int32_t* __restrict__ dest) {
+// Destination of assignment a (token a / K, expert e = ids[a]): the expert's
+// replicas are rep_ranks[rep_off[e] .. rep_off[e+1]); tokens take them in
+// turn (token index modulo the replica count).  meta[a] = the expert's index
+// in the destination's local expert list.
+__global__ void ep_owner_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t K, uint32_t E,
+                                const uint32_t* __restrict__ rep_off, const uint32_t* __restrict__ rep_ranks,
+                                const uint32_t* __restrict__ local_idx, int32_t* __restrict__ dest,
+                                int32_t* __restrict__ meta) {
     for (uint32_t a = blockIdx.x * blockDim.x + threadIdx.x; a < n; a += gridDim.x * blockDim.x) {
-        dest[a] = ids[a] / (int32_t)e_per;
+        const uint32_t e = (uint32_t)ids[a];
+        const uint32_t r0 = __ldg(rep_off + e), nr = __ldg(rep_off + e + 1) - r0;
+        const uint32_t q = __ldg(rep_ranks + r0 + (a / K) % nr);
+        dest[a] = (int32_t)q;
+        meta[a] = (int32_t)__ldg(local_idx + (uint64_t)q * E + e);
     }
 }
 
 // Dispatch: row p of the owner-ordered assignment list (p in [soff[q],
 // soff[q+1]) goes to rank q) is stored into rank q's receive buffer at row
 // dst_off[q] + p - soff[q]: the assignment's token row and its expert index
-// local to q.  One warp per row, 16-byte stores (H is a multiple of 8), into
+// in q's local list (meta).  One warp per row, 16-byte stores (H is a multiple of 8), into
 // peer memory for q != this rank.
-__global__ void ep_dispatch_kernel(const uint16_t* __restrict__ x, uint32_t H, uint32_t K, uint32_t e_per,
-                                   const int32_t* __restrict__ ids, const uint32_t* __restrict__ row_asg, uint32_t n,
+__global__ void ep_dispatch_kernel(const uint16_t* __restrict__ x, uint32_t H, uint32_t K,
+                                   const int32_t* __restrict__ meta, const uint32_t* __restrict__ row_asg, uint32_t n,
                                    const uint32_t* __restrict__ soff, const uint32_t* __restrict__ dst_off,
                                    uint16_t* const* __restrict__ peer_x, int32_t* const* __restrict__ peer_meta,
                                    uint32_t world) {
@@ -117,7 +126,7 @@ __global__ void ep_dispatch_kernel(const uint16_t* __restrict__ x, uint32_t H, u
         const uint4* src = reinterpret_cast<const uint4*>(x + (uint64_t)(a / K) * H);
         uint4* dst = reinterpret_cast<uint4*>(peer_x[q] + row * H);
         for (uint32_t v = lane; v < H / 8; v += 32) dst[v] = __ldg(src + v);
-        if (lane == 0) peer_meta[q][row] = ids[a] % (int32_t)e_per;
+        if (lane == 0) peer_meta[q][row] = meta[a];
     }
     __threadfence_system();  // peer stores before the exchange barrier
 }
@@ -144,7 +153,12 @@ struct EpState {
     uint32_t* h_mat = nullptr;    // pinned [W x W]
     uint32_t* h_small = nullptr;  // pinned [3W + 1]
     std::vector<uint32_t> last_sent, last_recv;
-    uint32_t slots_key[3] = {~0u, ~0u, ~0u};
+    // expert placement (identical on every rank): replicas of expert e are
+    // rep_ranks[rep_off[e] .. rep_off[e+1]); this rank's experts in order
+    uint32_t place_E = 0;
+    std::vector<uint32_t> rep_off, rep_ranks, local_list;
+    DevBuf d_rep_off, d_rep_ranks, d_local_idx, meta;
+    bool slots_dirty = true;
 };
 
 void close_peers(EpState* ep, SymBuf& b) {
@@ -163,11 +177,52 @@ void ep_release(EpState* ep) {
     DevBuf* bufs[] = {&ep->dest, &ep->pos, &ep->row_tok, &ep->row_asg, &ep->cnt, &ep->off, &ep->gu_off,
                       &ep->dn_off, &ep->tile_counts, &ep->rank_buf, &ep->mat, &ep->small, &ep->ptrs,
                       &ep->barrier_word, &ep->slots, &ep->yloc, &ep->handles, &ep->recv_x.local,
-                      &ep->recv_meta.local, &ep->ret.local};
+                      &ep->recv_meta.local, &ep->ret.local, &ep->d_rep_off, &ep->d_rep_ranks,
+                      &ep->d_local_idx, &ep->meta};
     for (DevBuf* b : bufs) b->release();
     if (ep->h_mat) cudaFreeHost(ep->h_mat);
     if (ep->h_small) cudaFreeHost(ep->h_small);
     delete ep;
+}
+
+// Installs a placement (replica lists per expert) and its device tables.
+int ep_apply_placement(EpState* ep, uint32_t E, const std::vector<uint32_t>& rep_off,
+                       const std::vector<uint32_t>& rep_ranks, char* err) {
+    const uint32_t W = (uint32_t)ep->world, me = (uint32_t)ep->rank;
+    std::vector<uint32_t> local_idx((size_t)W * E, 0xFFFFFFFFu);
+    std::vector<uint32_t> next(W, 0), mine;
+    for (uint32_t e = 0; e < E; ++e) {
+        for (uint32_t i = rep_off[e]; i < rep_off[e + 1]; ++i) {
+            const uint32_t q = rep_ranks[i];
+            local_idx[(size_t)q * E + e] = next[q]++;
+            if (q == me) mine.push_back(e);
+        }
+    }
+    CK(ep->d_rep_off.reserve(rep_off.size() * 4));
+    CK(ep->d_rep_ranks.reserve(std::max<size_t>(rep_ranks.size(), 1) * 4));
+    CK(ep->d_local_idx.reserve(local_idx.size() * 4));
+    CK(cudaMemcpy(ep->d_rep_off.ptr, rep_off.data(), rep_off.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(ep->d_rep_ranks.ptr, rep_ranks.data(), rep_ranks.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(ep->d_local_idx.ptr, local_idx.data(), local_idx.size() * 4, cudaMemcpyHostToDevice));
+    ep->place_E = E;
+    ep->rep_off = rep_off;
+    ep->rep_ranks = rep_ranks;
+    ep->local_list = mine;
+    ep->slots_dirty = true;
+    return 1;
+}
+
+// The default placement: contiguous blocks of E/W experts, one replica each.
+int ep_default_placement(EpState* ep, uint32_t E, char* err) {
+    const uint32_t W = (uint32_t)ep->world;
+    if (E == 0 || E % W != 0) {
+        set_err(err, "%u experts do not split evenly over %u ranks (set a placement)", E, W);
+        return 0;
+    }
+    std::vector<uint32_t> off(E + 1), ranks(E);
+    for (uint32_t e = 0; e <= E; ++e) off[e] = e;
+    for (uint32_t e = 0; e < E; ++e) ranks[e] = e / (E / W);
+    return ep_apply_placement(ep, E, off, ranks, err);
 }
 
 // Makes every rank's receive/return buffers at least as large as this call
@@ -324,6 +379,66 @@ int moe_b200_ep_local_experts(moe_b200_engine_t* eng, uint32_t experts, uint32_t
     return 1;
 }
 
+int moe_b200_ep_set_placement(moe_b200_engine_t* eng, uint32_t experts, const uint32_t* replica_count,
+                              const uint32_t* replica_ranks, char* err) {
+    if (!eng || !eng->ep) {
+        set_err(err, "expert parallelism not initialised (moe_b200_ep_init)");
+        return 0;
+    }
+    if (experts == 0 || !replica_count || !replica_ranks) {
+        set_err(err, "empty placement");
+        return 0;
+    }
+    const uint32_t W = (uint32_t)eng->ep->world;
+    std::vector<uint32_t> off(experts + 1, 0);
+    for (uint32_t e = 0; e < experts; ++e) {
+        if (replica_count[e] == 0 || replica_count[e] > W) {
+            set_err(err, "expert %u has %u replicas (1..%u)", e, replica_count[e], W);
+            return 0;
+        }
+        off[e + 1] = off[e] + replica_count[e];
+    }
+    std::vector<uint32_t> ranks(replica_ranks, replica_ranks + off[experts]);
+    for (uint32_t e = 0; e < experts; ++e) {
+        for (uint32_t i = off[e]; i < off[e + 1]; ++i) {
+            if (ranks[i] >= W) {
+                set_err(err, "expert %u placed on rank %u of %u", e, ranks[i], W);
+                return 0;
+            }
+            for (uint32_t j = off[e]; j < i; ++j) {
+                if (ranks[j] == ranks[i]) {
+                    set_err(err, "expert %u placed twice on rank %u", e, ranks[i]);
+                    return 0;
+                }
+            }
+        }
+    }
+    CK(cudaSetDevice(eng->device));
+    return ep_apply_placement(eng->ep, experts, off, ranks, err);
+}
+
+int moe_b200_ep_local_expert_list(moe_b200_engine_t* eng, uint32_t experts, uint32_t* out, uint32_t capacity,
+                                  uint32_t* count, char* err) {
+    if (!eng || !eng->ep) {
+        set_err(err, "expert parallelism not initialised (moe_b200_ep_init)");
+        return 0;
+    }
+    EpState* ep = eng->ep;
+    if (ep->place_E != experts) {
+        CK(cudaSetDevice(eng->device));
+        if (!ep_default_placement(ep, experts, err)) return 0;
+    }
+    if (count) *count = (uint32_t)ep->local_list.size();
+    if (out) {
+        if (capacity < ep->local_list.size()) {
+            set_err(err, "%zu local experts do not fit in %u entries", ep->local_list.size(), capacity);
+            return 0;
+        }
+        for (size_t i = 0; i < ep->local_list.size(); ++i) out[i] = ep->local_list[i];
+    }
+    return 1;
+}
+
 int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const uint16_t* x,
                               uint32_t T, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w,
                               void* stream, char* err) {
@@ -346,12 +461,9 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
                 H, I);
         return 0;
     }
-    if (E % W != 0) {
-        set_err(err, "%u experts do not split evenly over %u ranks", E, W);
-        return 0;
-    }
-    const uint32_t e_per = E / W, e0 = (uint32_t)ep->rank * e_per;
-    for (uint32_t e = e0; e < e0 + e_per; ++e) {
+    if (ep->place_E != E && !ep_default_placement(ep, E, err)) return 0;
+    const uint32_t e_loc = (uint32_t)ep->local_list.size();
+    for (uint32_t e : ep->local_list) {
         if (!L->present[e]) {
             set_err(err, "local expert %u of layer %d was never uploaded", e, cfg->layer);
             return 0;
@@ -425,8 +537,10 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     gd.gu_row_tiles = 1;
     gd.dn_row_tiles = 1;
     if (n > 0) {
-        ep_owner_kernel<<<std::min(ceil_div(n, 256u), 148u * 4u), 256, 0, st>>>(ids, n, e_per,
-                                                                               ep->dest.as<int32_t>());
+        CK(ep->meta.reserve((size_t)n * 4));
+        ep_owner_kernel<<<std::min(ceil_div(n, 256u), 148u * 4u), 256, 0, st>>>(
+            ids, n, K, E, ep->d_rep_off.as<uint32_t>(), ep->d_rep_ranks.as<uint32_t>(),
+            ep->d_local_idx.as<uint32_t>(), ep->dest.as<int32_t>(), ep->meta.as<int32_t>());
         CK(cudaGetLastError());
         if (route_small_fits(n, W)) {
             CK(launch_route_small(ep->dest.as<int32_t>(), T, K, W, 0, 0, gd, nullptr, 0, nullptr, 0,
@@ -505,7 +619,7 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     // 4. dispatch into the owners' receive buffers
     if (n > 0) {
         CK(launch_kernel(ep_dispatch_kernel, dim3(std::min(ceil_div(n, 8u), 148u * 8u)), dim3(256), 0, st, false, x,
-                         H, K, e_per, (const int32_t*)ids, (const uint32_t*)ep->row_asg.as<uint32_t>(), n,
+                         H, K, (const int32_t*)ep->meta.as<int32_t>(), (const uint32_t*)ep->row_asg.as<uint32_t>(), n,
                          (const uint32_t*)ep->off.as<uint32_t>(), d_dst_off,
                          reinterpret_cast<uint16_t* const*>(d_ptrs), reinterpret_cast<int32_t* const*>(d_ptrs + W),
                          W));
@@ -521,15 +635,12 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
 
     // 5. local experts (+ the shared expert on the local tokens); the down
     //    GEMM stores other ranks' rows into their return buffers
-    if (ep->slots_key[0] != e0 || ep->slots_key[1] != e_per || ep->slots_key[2] != E) {
-        std::vector<uint32_t> slots(e_per + 1);
-        for (uint32_t g = 0; g < e_per; ++g) slots[g] = e0 + g;
-        slots[e_per] = E;  // the shared expert's slot
+    if (ep->slots_dirty) {
+        std::vector<uint32_t> slots(ep->local_list);
+        slots.push_back(E);  // the shared expert's slot
         CK(ep->slots.reserve(slots.size() * 4));
         CK(cudaMemcpy(ep->slots.ptr, slots.data(), slots.size() * 4, cudaMemcpyHostToDevice));
-        ep->slots_key[0] = e0;
-        ep->slots_key[1] = e_per;
-        ep->slots_key[2] = E;
+        ep->slots_dirty = false;
     }
     CK(ep->yloc.reserve((size_t)std::max(rows, 1u) * H * 4));
     if (rows > 0) {
@@ -537,7 +648,7 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
         job.ids = ep->recv_meta.local.as<int32_t>();
         job.T = n_recv;
         job.K = 1;
-        job.E = e_per;
+        job.E = e_loc;
         job.shared_rows = shared_rows;
         job.shared_base = n_recv;
         job.src = recv_x;

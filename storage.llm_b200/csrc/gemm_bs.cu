@@ -560,6 +560,49 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 MODE == kGateUp ? p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * C::kSFB : nullptr;
             constexpr uint32_t kLoOff = C::kStackN ? BN : 0;        // stacked: lo half follows hi
             constexpr uint32_t kProjOff = C::kStackN ? 2 * BN : BN;
+            if (MODE == kGateUp && C::kStackN) {
+                // Drain gate and up (hi + lo halves summed) into registers and
+                // release the accumulator before the SiLU / hi-lo split, so the
+                // next tile's MMAs overlap this tile's math.
+                float g[BN], u[BN];
+#pragma unroll
+                for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 16) {
+                    if (c0 < tc.nn) {  // uniform across the warp
+                        uint32_t a[16], b[16], c[16], d[16];
+                        MOE_TMEM_LD16(dbase + c0, a);
+                        MOE_TMEM_LD16(dbase + kLoOff + c0, b);
+                        MOE_TMEM_LD16(dbase + kProjOff + c0, c);
+                        MOE_TMEM_LD16(dbase + kProjOff + kLoOff + c0, d);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            g[c0 + i] = __uint_as_float(a[i]) + __uint_as_float(b[i]);
+                            u[c0 + i] = __uint_as_float(c[i]) + __uint_as_float(d[i]);
+                        }
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&acc_empty[acc]);
+#pragma unroll
+                for (uint32_t col = 0; col < (uint32_t)BN; ++col) {
+                    if (col >= tc.nn) break;  // uniform across the warp
+                    const float hv = silu_fast(g[col]) * u[col];
+                    uint8_t hi, lo, sh, sl;
+                    split_e4m3_warp(hv, hi, lo, sh, sl);
+                    const uint64_t prow = row0 + col;
+                    p.h_out[prow * p.h_stride + m] = hi;
+                    p.h_out[p.h_plane + prow * p.h_stride + m] = lo;
+                    if (lane == 0) {
+                        h_atom[sfb_pos_hi<BN>(col) + quarter] = sh;
+                        h_atom[sfb_pos_lo<BN>(col) + quarter] = sl;
+                    }
+                }
+                if (++acc == C::kAccs) {
+                    acc = 0;
+                    accphase ^= 1;
+                }
+                continue;
+            }
             for (uint32_t c0 = 0; c0 < tc.nn; c0 += 16) {
                 float v0[16], v1[16];
                 {
@@ -597,20 +640,31 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                         }
                     }
                 } else if (m < p.m_valid) {
+                    if (!p.ret_ptrs) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        if (c0 + i < tc.nn) {
-                            const uint64_t prow = row0 + c0 + i;
-                            const uint64_t orow = p.y_row_map ? __ldg(p.y_row_map + prow) : prow;
-                            float* dst = p.y_out + orow * p.y_stride;
-                            if (p.ret_ptrs && orow < p.ret_rows) {
-                                // another rank's token: into its return buffer over NVLink
-                                uint32_t r = 0;
-                                while (r + 1 < p.ret_world && __ldg(p.ret_roff + r + 1) <= orow) ++r;
-                                dst = p.ret_ptrs[r] +
-                                      ((uint64_t)__ldg(p.ret_base + r) + orow - __ldg(p.ret_roff + r)) * p.y_stride;
+                        for (int i = 0; i < 16; ++i) {
+                            if (c0 + i < tc.nn) {
+                                const uint64_t prow = row0 + c0 + i;
+                                const uint64_t orow = p.y_row_map ? __ldg(p.y_row_map + prow) : prow;
+                                p.y_out[orow * p.y_stride + m] = v0[i];
                             }
-                            dst[m] = v0[i];
+                        }
+                    } else {
+                        // expert parallelism: another rank's token goes into its
+                        // return buffer over NVLink
+                        for (int i = 0; i < 16; ++i) {
+                            if (c0 + i < tc.nn) {
+                                const uint64_t prow = row0 + c0 + i;
+                                const uint64_t orow = p.y_row_map ? __ldg(p.y_row_map + prow) : prow;
+                                float* dst = p.y_out + orow * p.y_stride;
+                                if (orow < p.ret_rows) {
+                                    uint32_t r = 0;
+                                    while (r + 1 < p.ret_world && __ldg(p.ret_roff + r + 1) <= orow) ++r;
+                                    dst = p.ret_ptrs[r] +
+                                          ((uint64_t)__ldg(p.ret_base + r) + orow - __ldg(p.ret_roff + r)) * p.y_stride;
+                                }
+                                dst[m] = v0[i];
+                            }
                         }
                     }
                 }

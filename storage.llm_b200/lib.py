@@ -107,6 +107,10 @@ def load(path: Path = LIB_PATH) -> C.CDLL:
     lib.moe_b200_ep_layer_forward.argtypes = [vp, C.POINTER(LayerCfg), vp, C.c_uint32, vp, vp, vp, vp, vp, cp]
     lib.moe_b200_ep_layer_forward_host.restype = C.c_int
     lib.moe_b200_ep_layer_forward_host.argtypes = [vp, C.POINTER(LayerCfg), vp, C.c_uint32, vp, vp, vp, vp, cp]
+    lib.moe_b200_ep_set_placement.restype = C.c_int
+    lib.moe_b200_ep_set_placement.argtypes = [vp, C.c_uint32, vp, vp, cp]
+    lib.moe_b200_ep_local_expert_list.restype = C.c_int
+    lib.moe_b200_ep_local_expert_list.argtypes = [vp, C.c_uint32, vp, C.c_uint32, C.POINTER(C.c_uint32), cp]
     lib.moe_b200_ep_last_counts.restype = C.c_int
     lib.moe_b200_ep_last_counts.argtypes = [vp, vp, vp, cp]
     _lib = lib
@@ -226,12 +230,24 @@ class Engine:
         self._check(self.lib.moe_b200_ep_local_experts(self.h, experts, C.byref(first), C.byref(count), self.err))
         return first.value, count.value
 
+    def ep_set_placement(self, replicas):
+        """replicas[e] = list of ranks holding expert e (the same on every rank)."""
+        cnt = np.array([len(r) for r in replicas], np.uint32)
+        ranks = np.array([q for r in replicas for q in r], np.uint32)
+        self._check(self.lib.moe_b200_ep_set_placement(self.h, len(replicas), _ptr(cnt), _ptr(ranks), self.err))
+
+    def ep_local_expert_list(self, experts: int):
+        out = np.zeros(experts, np.uint32)
+        cnt = C.c_uint32(0)
+        self._check(self.lib.moe_b200_ep_local_expert_list(self.h, experts, _ptr(out), experts, C.byref(cnt),
+                                                           self.err))
+        return [int(e) for e in out[:cnt.value]]
+
     def upload_layer_ep(self, li, layer: int = 0):
-        """Router, this rank's expert block and the shared expert."""
+        """Router, this rank's experts (current placement) and the shared expert."""
         s = li.shape
-        first, count = self.ep_local_experts(s.experts)
         self.upload_router(layer, np.ascontiguousarray(li.router), s.experts, s.hidden)
-        for e in range(first, first + count):
+        for e in self.ep_local_expert_list(s.experts):
             self.upload_expert(layer, e, np.ascontiguousarray(li.gate[e]), np.ascontiguousarray(li.up[e]),
                                np.ascontiguousarray(li.down[e]), s.hidden, s.intermediate)
         if li.shared_gate is not None:

@@ -39,7 +39,8 @@ def _rank_main(rank, uid, case, q):
     import moe_b200.lib as L
     import moe_b200.synth as synth
 
-    H, I, E, K, tokens, shared = case
+    H, I, E, K, tokens, shared = case[:6]
+    placement = case[6] if len(case) > 6 else None
     shape = synth.small_shape(hidden=H, intermediate=I, experts=E, top_k=K, tokens=8, shared=shared)
     li = synth.make_layer(shape, seed=23)
     T = tokens[rank]
@@ -47,6 +48,8 @@ def _rank_main(rank, uid, case, q):
     eng = L.Engine(rank)
     try:
         eng.ep_init(rank, WORLD, uid)
+        if placement:
+            eng.ep_set_placement(placement)
         eng.upload_layer_ep(li)
         cfg = L.Engine.cfg(shape, gemm_path=L.GEMM_BLOCKSCALED)
         out = eng.ep_forward_host(cfg, x)
@@ -66,15 +69,19 @@ def _rank_main(rank, uid, case, q):
         eng.close()
 
 
+# expert 0 replicated on both ranks, the rest spread out of order
+REPLICATED = [[0, 1], [1], [0], [1], [1], [0], [0], [1]]
 CASES = [
     (256, 320, 8, 2, (40, 40), False),
     (256, 320, 8, 3, (64, 0), True),
     (128, 128, 8, 4, (2100, 700), False),
+    (256, 320, 8, 3, (96, 80), True, REPLICATED),
 ]
 
 
 @pytest.mark.skipif(_gpus() < WORLD, reason="needs two GPUs")
-@pytest.mark.parametrize("case", CASES, ids=["decode", "idle_rank_shared", "past_single_block_sort"])
+@pytest.mark.parametrize("case", CASES, ids=["decode", "idle_rank_shared", "past_single_block_sort",
+                                            "replicated_placement"])
 def test_expert_parallel_forward_matches_oracle(case):
     import multiprocessing as mp
     from conftest import load_pkg
