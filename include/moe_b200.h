@@ -113,7 +113,8 @@ MOE_B200_API int moe_b200_upload_expert(moe_b200_engine_t* engine, int32_t layer
  * per-token moe_layer_moe_mlp_f32 expert phase (generation_mlp.cpp.inc:
  * 874-1431) and fills the batched slot moe_layer_moe_mlp_batched_f32
  * (generation_api_batch.cpp.inc:68-78).
- *   x_bf16    [tokens x H] expert input (the router input)
+ *   x_bf16    [tokens x H] expert input (the router input); 8-byte aligned
+ *             (16-byte aligned rows take the single-kernel router)
  *   y_bf16    [tokens x H] output mlp = shared + sum_j w_j * expert_j(x) (may be NULL)
  *   y_f32     [tokens x H] the same in fp32 (may be NULL)
  *   topk_ids  [tokens x k] selected experts, descending score (may be NULL)

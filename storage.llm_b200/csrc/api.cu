@@ -121,6 +121,10 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     };
     const uint32_t H = L->H;
     const uint32_t n = job.T * job.K;
+    if (reinterpret_cast<uintptr_t>(job.src) & 7) {
+        set_err(err, "activation rows must start on an 8-byte boundary");
+        return 0;
+    }
     const uint32_t P = n + job.shared_rows;
     const uint32_t G = job.E + (job.shared_rows ? 1 : 0);
     const uint32_t Kq = L->kq, Iq = L->iq;  // K padded to 128

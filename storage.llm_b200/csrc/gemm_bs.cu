@@ -141,15 +141,54 @@ __device__ __forceinline__ void split_e4m3_warp(float v, uint8_t& hi, uint8_t& l
     s_lo = (uint8_t)(e2 + 127);
 }
 
+// Hi/lo split of four consecutive values held by each lane, a 32-element
+// block spanning 8 consecutive lanes (lanes 8j .. 8j+7 hold block j): the
+// same block maximum, exponents and rounding as split_e4m3_warp, with the
+// maximum taken by three shuffles inside the 8-lane group.  Returns the four
+// hi and four lo code bytes packed low-to-high and the block's scale bytes.
+__device__ __forceinline__ void split_e4m3_x4(const float v[4], uint32_t& hi4, uint32_t& lo4, uint8_t& s_hi,
+                                              uint8_t& s_lo) {
+    auto group_max = [](float a) {
+        uint32_t u = __float_as_uint(a);
+        u = max(u, __shfl_xor_sync(0xffffffffu, u, 1));
+        u = max(u, __shfl_xor_sync(0xffffffffu, u, 2));
+        u = max(u, __shfl_xor_sync(0xffffffffu, u, 4));
+        return __uint_as_float(u);  // non-negative floats order like their bit patterns
+    };
+    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    const int e1 = block_exp(group_max(m));
+    float r[4];
+    hi4 = 0;
+    const float inv1 = pow2f(-e1), sc1 = pow2f(e1);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float q;
+        hi4 |= e4m3_rne(v[i] * inv1, q) << (8 * i);
+        r[i] = v[i] - q * sc1;
+    }
+    m = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
+    const int e2 = block_exp(group_max(m));
+    lo4 = 0;
+    const float inv2 = pow2f(-e2);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float q;
+        lo4 |= e4m3_rne(r[i] * inv2, q) << (8 * i);
+    }
+    s_hi = (uint8_t)(e1 + 127);
+    s_lo = (uint8_t)(e2 + 127);
+}
+
 // ---------------------------------------------------------------------------
 // Permuted activation rows for the block-scaled GEMM, quantised on the way:
 // one warp per (permuted row, chunk of kGqChunk 128-element K stages).  For
-// stage kt lane l splits elements 128 kt + 32 j + l (j = 0..3, four 32-element
-// blocks) of the row's token into exact hi + lo E4M3 terms, writes them to the
-// hi and lo planes of xb ([2][rows_cap][Kp]) and the stage's four hi and four
-// lo scale bytes, as one 32-bit word each, straight into the scale block the
-// GEMM's producer bulk-copies for (token tile, kt), at sfb_pos_hi / sfb_pos_lo.
-// The row's token tile and index in it come from the permutation (row_info).
+// stage kt lane l holds elements 128 kt + 4 l .. + 3 (one 8-byte load), so
+// 32-element block j is lanes 8j .. 8j+7; the lane writes its four hi and
+// four lo code bytes with one 4-byte store per plane of xb ([2][rows_cap][Kp]).
+// The stage's four hi and four lo scale bytes go, as one 32-bit word each,
+// straight into the scale block the GEMM's producer bulk-copies for (token
+// tile, kt), at sfb_pos_hi / sfb_pos_lo.  The row's token tile and index in
+// it come from the permutation (row_info).
 // ---------------------------------------------------------------------------
 constexpr uint32_t kGqChunk = 4;
 
@@ -177,29 +216,31 @@ __global__ void __launch_bounds__(256) gather_quant_bs_kernel(const uint16_t* __
         const uint32_t info = __ldg(row_info + r);
         uint8_t* atoms = sf_atoms + (uint64_t)(info >> 8) * nkt * kAtom;
         const uint32_t pos_h = sfb_pos_hi<BN>(info & 0xFFu), pos_l = sfb_pos_lo<BN>(info & 0xFFu);
-        uint8_t* dh = xb + (uint64_t)r * Kp + lane;
-        float v[kGqChunk][4];
+        uint32_t* dh = reinterpret_cast<uint32_t*>(xb + (uint64_t)r * Kp) + lane;
+        uint32_t* dl = reinterpret_cast<uint32_t*>(xb + xplane + (uint64_t)r * Kp) + lane;
+        uint2 raw[kGqChunk];
 #pragma unroll
         for (uint32_t c = 0; c < kGqChunk; ++c) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t k = (kt0 + c) * 128 + j * 32 + lane;
-                v[c][j] = (kt0 + c < nkt && k < H) ? bf16_bits_to_f32(__ldg(xr + k)) : 0.f;
-            }
+            const uint32_t k = (kt0 + c) * 128 + lane * 4;  // H % 8 == 0: four elements all in or all out
+            raw[c] = (kt0 + c < nkt && k < H) ? __ldg(reinterpret_cast<const uint2*>(xr + k)) : make_uint2(0, 0);
         }
 #pragma unroll
         for (uint32_t c = 0; c < kGqChunk; ++c) {
             const uint32_t kt = kt0 + c;
             if (kt >= nkt) break;  // uniform across the warp
+            const float v[4] = {__uint_as_float(raw[c].x << 16), __uint_as_float(raw[c].x & 0xffff0000u),
+                                __uint_as_float(raw[c].y << 16), __uint_as_float(raw[c].y & 0xffff0000u)};
+            uint32_t hi4, lo4;
+            uint8_t sh, sl;
+            split_e4m3_x4(v, hi4, lo4, sh, sl);
+            dh[kt * 32] = hi4;
+            dl[kt * 32] = lo4;
+            // block j's scale bytes sit in lane 8j; gather them into one word
             uint32_t shw = 0, slw = 0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                uint8_t hi, lo, sh, sl;
-                split_e4m3_warp(v[c][j], hi, lo, sh, sl);
-                dh[kt * 128 + j * 32] = hi;
-                dh[xplane + kt * 128 + j * 32] = lo;
-                shw |= (uint32_t)sh << (8 * j);
-                slw |= (uint32_t)sl << (8 * j);
+                shw |= (uint32_t)(uint8_t)__shfl_sync(0xffffffffu, (uint32_t)sh, 8 * j) << (8 * j);
+                slw |= (uint32_t)(uint8_t)__shfl_sync(0xffffffffu, (uint32_t)sl, 8 * j) << (8 * j);
             }
             if (lane == 0) {
                 uint8_t* atom = atoms + (uint64_t)kt * kAtom;
