@@ -102,6 +102,27 @@ int make_tmap(moe_b200_engine* eng, CUtensorMap* map, void* base, uint64_t cols,
     return make_tmap2d(eng, map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, cols, rows, cols * 2, 64, 32, err);
 }
 
+// Tensor maps for the TMA-fed router logits kernel (x [T x H] and the router
+// rows w [E x H], bf16, no swizzle).  Returns false when the batch takes
+// another router kernel or a map cannot be made (the router then stages
+// rows itself).
+bool router_tmaps(moe_b200_engine* eng, const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H,
+                  CUtensorMap* tx, CUtensorMap* tw) {
+    if (!router_wants_tma(x, w, T, E, H)) return false;
+    char err[MOE_B200_ERR_LEN];
+    if (!get_encoder(eng, err)) return false;
+    auto enc = [&](CUtensorMap* m, const uint16_t* base, uint32_t rows, uint32_t box_rows) {
+        const cuuint64_t dims[2] = {H, rows};
+        const cuuint64_t strides[1] = {(cuuint64_t)H * 2};
+        const cuuint32_t box[2] = {128, box_rows};
+        const cuuint32_t estr[2] = {1, 1};
+        return eng->encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    return enc(tx, x, T, router_box_rows(true)) && enc(tw, w, E, router_box_rows(false));
+}
+
 LayerWeights* get_layer(moe_b200_engine* eng, int32_t layer, char* err) {
     if (!eng) {
         set_err(err, "null engine");
@@ -534,8 +555,11 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
 
     const int sigmoid = cfg->score_func == MOE_B200_SCORE_SIGMOID;
     const float rscale = cfg->routed_scale > 0.f ? cfg->routed_scale : 1.0f;
+    CUtensorMap rtx, rtw;
+    const bool rt_tma = router_tmaps(eng, x, L->router.as<uint16_t>(), T, E, H, &rtx, &rtw);
     CK(launch_router(x, L->router.as<uint16_t>(), T, E, H, K, sigmoid, cfg->norm_topk, rscale,
-                     eng->logits.as<float>(), ids, w, eng->scores.as<float>(), errw, st, &launches));
+                     eng->logits.as<float>(), ids, w, eng->scores.as<float>(), errw, st, &launches,
+                     rt_tma ? &rtx : nullptr, rt_tma ? &rtw : nullptr));
     mark(1);
 
     if (bs) {

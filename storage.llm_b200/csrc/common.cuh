@@ -57,6 +57,7 @@ enum : uint32_t {
     kErrTimeoutAEmpty = 4,
     kErrTimeoutAccFull = 5,
     kErrTimeoutAccEmpty = 6,
+    kErrTimeoutRouterLoad = 7,
     kErrBadExpert = 16,
 };
 

@@ -135,6 +135,8 @@ namespace moe_b200 {
 
 int check_dims(const moe_b200_layer_cfg_t* c, char* err);
 LayerWeights* get_layer(moe_b200_engine* eng, int32_t layer, char* err);
+bool router_tmaps(moe_b200_engine* eng, const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H,
+                  CUtensorMap* tx, CUtensorMap* tw);
 
 // One run of the block-scaled expert pipeline: permutation of T*K
 // assignments into E routed groups (+ an extra shared-expert group of

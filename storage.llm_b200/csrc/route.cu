@@ -7,7 +7,8 @@
 //            b_l = s_l + s_{l+8}, then ((b0+b1)+b2)+...+b7;
 //   softmax  generation_router.cpp.inc:606-622: exp in double, denominator
 //            summed in double in expert order, p *= (float)(1/denom);
-//   sigmoid  :239-245, 1/(1+exp(-l)) in float;
+//   sigmoid  :239-245, 1/(1+expf(-l)) in float, expf being the host C
+//            library's (libm_expf below reproduces it bit for bit);
 //   top-k    :640-674, k largest scores descending (equal scores: lower
 //            expert index first), optional renormalisation and scaling.
 // The permutation is the order of moe_pc_group_tokens_by_expert
@@ -20,121 +21,309 @@
 namespace moe_b200 {
 
 // ---------------------------------------------------------------------------
-// Router logits.  A block computes a 16-token x 16-expert tile: 256 threads =
-// 16 lane groups x 16 lanes, lane l of a group owning the reference's FMA
-// chain l (elements l, l+16, ...) for the group's 4 tokens x 4 experts (16
-// independent chains per thread).  Token and router rows are staged through
-// shared memory in 256-element chunks with cp.async, double-buffered.
+// Router logits for large batches.  A block computes a 32-token x 64-expert
+// tile.  The reference accumulates each dot product in 16 FMA chains (chain l
+// takes elements l, l+16, ...); here a quad of lanes shares a dot's 16
+// chains, lane q owning chains 4q..4q+3, and each lane does this for 8 tokens
+// x 4 experts: 128 independent chains, advanced two at a time by packed fp32
+// FMAs (fma.rn.f32x2, each half an IEEE fp32 FMA), fed by 12 16-byte shared
+// loads per 16 elements.  The chains read an fp32 copy of each 128-element
+// chunk of the rows, so the FMA loop does no conversions.  Within a warp the
+// two token sub-groups read adjacent rows and the fp32 row stride is 16 words
+// past a multiple of 32, so the 8 distinct x addresses of a quarter-warp
+// cover the 32 banks once.  Each dot's 16 chains are combined exactly as the
+// reference does: b_l = s_l + s_{l+8}, then ((b0+b1)+b2)+...+b7, then the
+// 4-way and scalar tails (H % 16 != 0).
+//
+// router_logits_tma_kernel (16-byte aligned rows) specialises warps: one
+// lane brings each chunk's token and router rows in with two TMA copies into
+// a 3-deep bf16 ring, two warps convert ring entries into a 2-deep fp32 ring,
+// eight warps run the FMA chains; mbarriers hand the buffers along, so
+// copies, conversion and FMAs of different chunks overlap.
+// router_logits_kernel (rows only 8-byte aligned) stages with 8-byte
+// cp.async and converts in lockstep with the FMAs.
 // ---------------------------------------------------------------------------
-constexpr int kRtTok = 16, kRtExp = 16;
-constexpr int kRtChunk = 256;               // elements per staged chunk (multiple of 16)
-constexpr int kRtStride = kRtChunk + 8;     // padded row (bf16) against bank conflicts
+constexpr int kRtRT = 8;                         // tokens per lane (x 4 experts x 4 chains)
+constexpr int kRtTok = 4 * kRtRT, kRtExp = 64;   // block tile
+constexpr int kRtK = 128;                        // elements per chunk (multiple of 16)
+constexpr int kRtS = kRtK + 16;                  // fp32 row stride in words (== 16 mod 32)
+constexpr int kRtRows = kRtTok + kRtExp;
+constexpr int kRtRing = 3;                       // bf16 chunk buffers
+constexpr int kRtF32Ring = 2;                    // fp32 chunk buffers (TMA kernel)
+constexpr size_t kRtF32Bytes = (size_t)kRtRows * kRtS * 4;
+constexpr size_t kRtRawBytes = (size_t)kRtRows * kRtK * 2;
+constexpr size_t kRtSmem = kRtF32Bytes + kRtRing * kRtRawBytes;
+constexpr size_t kRtTmaSmem = kRtF32Ring * kRtF32Bytes + kRtRing * kRtRawBytes + 128;
+constexpr int kRtFmaWarps = 8, kRtCvtWarps = 2;
+constexpr int kRtTmaThreads = 32 * (kRtFmaWarps + kRtCvtWarps + 1);
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-    const uint32_t d = smem_u32(dst);
-    const int n = valid ? 16 : 0;  // 0 source bytes -> zero fill
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
-                                                            const uint16_t* __restrict__ w, uint32_t T,
-                                                            uint32_t E, uint32_t H, float* __restrict__ logits) {
-    __shared__ __align__(16) uint16_t xs[2][kRtTok][kRtStride];
-    __shared__ __align__(16) uint16_t ws[2][kRtExp][kRtStride];
-    const int l = threadIdx.x & 15;
-    const int grp = threadIdx.x >> 4;
-    const int gt = (grp >> 2) * 4, ge = (grp & 3) * 4;  // the group's first token / expert in the tile
-    const uint32_t t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp;
-    const uint32_t main_end = H & ~15u;  // the 16-step main loop of the reference
-    const uint32_t nchunks = (main_end + kRtChunk - 1) / kRtChunk;
+// d.lo += a.lo * b.lo, d.hi += a.hi * b.hi, each rounded once (IEEE fp32 FMA)
+__device__ __forceinline__ void fma_f32x2(unsigned long long& d, unsigned long long a, unsigned long long b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
 
-    auto stage = [&](uint32_t c, int buf) {
-        const uint32_t c0 = c * kRtChunk;
-        const uint32_t clen = min((uint32_t)kRtChunk, main_end - c0);
-        const uint32_t vpr = clen / 8;  // 16-byte vectors per row
-        for (uint32_t i = threadIdx.x; i < 32 * vpr; i += blockDim.x) {
-            const uint32_t row = i / vpr, v = i % vpr;
-            if (row < kRtTok) {
-                const uint32_t t = t0 + row;
-                cp_async16(&xs[buf][row][v * 8], x + (uint64_t)min(t, T - 1) * H + c0 + v * 8, t < T);
-            } else {
-                const uint32_t e = e0 + row - kRtTok;
-                cp_async16(&ws[buf][row - kRtTok][v * 8], w + (uint64_t)min(e, E - 1) * H + c0 + v * 8, e < E);
-            }
-        }
-        cp_async_commit();
-    };
+// 8 bf16 of raw row r, column group v -> fp32 row r of `fs`
+__device__ __forceinline__ void rt_convert8(const uint16_t* raw, float* fs, uint32_t r, uint32_t v) {
+    const uint4 u = *reinterpret_cast<const uint4*>(raw + (size_t)r * kRtK + v * 8);
+    float4 lo, hi;
+    lo.x = __uint_as_float(u.x << 16); lo.y = __uint_as_float(u.x & 0xffff0000u);
+    lo.z = __uint_as_float(u.y << 16); lo.w = __uint_as_float(u.y & 0xffff0000u);
+    hi.x = __uint_as_float(u.z << 16); hi.y = __uint_as_float(u.z & 0xffff0000u);
+    hi.z = __uint_as_float(u.w << 16); hi.w = __uint_as_float(u.w & 0xffff0000u);
+    float4* d = reinterpret_cast<float4*>(fs + (size_t)r * kRtS + v * 8);
+    d[0] = lo;
+    d[1] = hi;
+}
 
-    float acc[4][4];
+// The FMA lanes' share of the block: 8 warps, tile rows and accumulators.
+struct RtLane {
+    int q, trow, erow;
+    unsigned long long acc[kRtRT][4][2];
+    __device__ __forceinline__ RtLane(int warp, int lane) {
+        const int pos = lane >> 2;
+        q = lane & 3;
+        // token rows: trow + 2a (a < kRtRT); expert rows: kRtTok + erow + 4b (b < 4)
+        trow = (warp & 1) * (2 * kRtRT) + (pos & 1);
+        erow = (warp >> 1) * 16 + (pos >> 1);
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < kRtRT; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-    if (nchunks > 0) stage(0, 0);
-    for (uint32_t c = 0; c < nchunks; ++c) {
-        const int buf = c & 1;
-        if (c + 1 < nchunks) {
-            stage(c + 1, buf ^ 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
-        const uint32_t clen = min((uint32_t)kRtChunk, main_end - c * kRtChunk);
-        for (uint32_t i = l; i < clen; i += 16) {
-            float xv[4], wv[4];
-#pragma unroll
-            for (int a = 0; a < 4; ++a) xv[a] = bf16_bits_to_f32(xs[buf][gt + a][i]);
-#pragma unroll
-            for (int b = 0; b < 4; ++b) wv[b] = bf16_bits_to_f32(ws[buf][ge + b][i]);
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) acc[a][b] = __fmaf_rn(wv[b], xv[a], acc[a][b]);
-        }
-        __syncthreads();
+            for (int b = 0; b < 4; ++b) acc[a][b][0] = acc[a][b][1] = 0ull;
     }
-    // lane sums b_l = s_l + s_{l+8}, then the ordered 8-term sum, then the
-    // reference's 4-way and scalar tails (H % 16 != 0).
-    const unsigned full = 0xffffffffu;
+    // the 16-element steps of one chunk of the fp32 tile `fs`
+    __device__ __forceinline__ void chunk(const float* fs, uint32_t clen) {
+        const float* xp = fs + (size_t)trow * kRtS + 4 * q;
+        const float* wp = fs + (size_t)(kRtTok + erow) * kRtS + 4 * q;
+#pragma unroll 1
+        for (uint32_t k = 0; k < clen; k += 16) {
+            ulonglong2 wv[4];
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
+            for (int b = 0; b < 4; ++b) wv[b] = *reinterpret_cast<const ulonglong2*>(wp + (size_t)(4 * b) * kRtS + k);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const float hi = __shfl_down_sync(full, acc[a][b], 8, 16);
-            const float bl = acc[a][b] + hi;  // valid on lanes 0..7
-            float s = __shfl_sync(full, bl, 0, 16);
+            for (int a = 0; a < kRtRT; ++a) {
+                const ulonglong2 xv = *reinterpret_cast<const ulonglong2*>(xp + (size_t)(2 * a) * kRtS + k);
 #pragma unroll
-            for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __shfl_sync(full, bl, j, 16));
-            const uint32_t tt = t0 + gt + a, e = e0 + ge + b;
-            if (l == 0 && tt < T && e < E) {
-                float out = 0.0f + s;
-                const uint16_t* wr = w + (uint64_t)e * H;
-                const uint16_t* xr = x + (uint64_t)tt * H;
-                uint32_t i = main_end;
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                for (; i + 3 < H; i += 4) {
-                    a0 = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), a0);
-                    a1 = __fmaf_rn(bf16_bits_to_f32(wr[i + 1]), bf16_bits_to_f32(xr[i + 1]), a1);
-                    a2 = __fmaf_rn(bf16_bits_to_f32(wr[i + 2]), bf16_bits_to_f32(xr[i + 2]), a2);
-                    a3 = __fmaf_rn(bf16_bits_to_f32(wr[i + 3]), bf16_bits_to_f32(xr[i + 3]), a3);
+                for (int b = 0; b < 4; ++b) {
+                    fma_f32x2(acc[a][b][0], wv[b].x, xv.x);
+                    fma_f32x2(acc[a][b][1], wv[b].y, xv.y);
                 }
-                out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
-                for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), out);
-                logits[(uint64_t)tt * E + e] = out;
             }
+        }
+    }
+    // Lane q holds chains 4q..4q+3.  b_l = s_l + s_{l+8} lands on q = 0
+    // (l < 4) and q = 1 (4 <= l < 8); q = 0 sums b0..b3 in order and q = 1
+    // continues with b4..b7, then adds the tails and stores.
+    __device__ __forceinline__ void finish(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                           uint32_t t0, uint32_t e0, uint32_t T, uint32_t E, uint32_t H,
+                                           float* __restrict__ logits) {
+        const unsigned full_mask = 0xffffffffu;
+        const int lane = threadIdx.x & 31;
+        const uint32_t main_end = H & ~15u;
+#pragma unroll
+        for (int a = 0; a < kRtRT; ++a) {
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const float sc[4] = {__uint_as_float((uint32_t)acc[a][b][0]),
+                                     __uint_as_float((uint32_t)(acc[a][b][0] >> 32)),
+                                     __uint_as_float((uint32_t)acc[a][b][1]),
+                                     __uint_as_float((uint32_t)(acc[a][b][1] >> 32))};
+                float bl[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) bl[c] = __fadd_rn(sc[c], __shfl_xor_sync(full_mask, sc[c], 2));
+                float s = __fadd_rn(__fadd_rn(__fadd_rn(bl[0], bl[1]), bl[2]), bl[3]);
+                const float s0 = __shfl_sync(full_mask, s, lane & ~3);
+                s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, bl[0]), bl[1]), bl[2]), bl[3]);
+                const uint32_t tt = t0 + trow + 2 * a, e = e0 + erow + 4 * b;
+                if (q == 1 && tt < T && e < E) {
+                    float out = 0.0f + s;
+                    if (main_end < H) {
+                        const uint16_t* wr = w + (uint64_t)e * H;
+                        const uint16_t* xr = x + (uint64_t)tt * H;
+                        uint32_t i = main_end;
+                        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                        for (; i + 3 < H; i += 4) {
+                            a0 = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), a0);
+                            a1 = __fmaf_rn(bf16_bits_to_f32(wr[i + 1]), bf16_bits_to_f32(xr[i + 1]), a1);
+                            a2 = __fmaf_rn(bf16_bits_to_f32(wr[i + 2]), bf16_bits_to_f32(xr[i + 2]), a2);
+                            a3 = __fmaf_rn(bf16_bits_to_f32(wr[i + 3]), bf16_bits_to_f32(xr[i + 3]), a3);
+                        }
+                        out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
+                        for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), out);
+                    }
+                    logits[(uint64_t)tt * E + e] = out;
+                }
+            }
+        }
+    }
+};
+
+__global__ void __launch_bounds__(kRtTmaThreads, 1)
+    router_logits_tma_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                             const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, uint32_t T, uint32_t E,
+                             uint32_t H, float* __restrict__ logits, uint32_t* err) {
+    extern __shared__ __align__(128) unsigned char rt_smem[];
+    float* fs = reinterpret_cast<float*>(rt_smem);                                       // [kRtF32Ring][rows][kRtS]
+    uint16_t* raw = reinterpret_cast<uint16_t*>(rt_smem + kRtF32Ring * kRtF32Bytes);      // [kRtRing][rows][kRtK]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rt_smem + kRtF32Ring * kRtF32Bytes + kRtRing * kRtRawBytes);
+    uint64_t* raw_full = bars;                      // TMA bytes landed
+    uint64_t* raw_empty = bars + kRtRing;           // converters done reading
+    uint64_t* f32_full = bars + 2 * kRtRing;        // converters done writing
+    uint64_t* f32_empty = bars + 2 * kRtRing + kRtF32Ring;  // FMA warps done reading
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t e0 = blockIdx.x * kRtExp, t0 = blockIdx.y * kRtTok;
+    const uint32_t main_end = H & ~15u;
+    const uint32_t nchunks = (main_end + kRtK - 1) / kRtK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRtRing; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kRtCvtWarps);
+        }
+        for (int i = 0; i < kRtF32Ring; ++i) {
+            mbar_init(&f32_full[i], kRtCvtWarps);
+            mbar_init(&f32_empty[i], kRtFmaWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp < kRtFmaWarps) {
+        RtLane ln(warp, lane);
+        for (uint32_t c = 0; c < nchunks; ++c) {
+            const uint32_t s = c % kRtF32Ring;
+            mbar_wait(&f32_full[s], (c / kRtF32Ring) & 1, err, kErrTimeoutRouterLoad);
+            ln.chunk(fs + (size_t)s * kRtRows * kRtS, min((uint32_t)kRtK, main_end - c * kRtK));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&f32_empty[s]);
+        }
+        ln.finish(x, w, t0, e0, T, E, H, logits);
+    } else if (warp < kRtFmaWarps + kRtCvtWarps) {
+        const uint32_t ct = threadIdx.x - 32 * kRtFmaWarps;  // 0..63
+        constexpr int kVpr = kRtK / 8, kPer = kRtRows * kVpr / (32 * kRtCvtWarps);
+        static_assert(kRtRows * kVpr % (32 * kRtCvtWarps) == 0, "whole conversion rounds");
+        for (uint32_t c = 0; c < nchunks; ++c) {
+            const uint32_t rs = c % kRtRing, s = c % kRtF32Ring;
+            mbar_wait(&raw_full[rs], (c / kRtRing) & 1, err, kErrTimeoutRouterLoad);
+            mbar_wait(&f32_empty[s], ((c / kRtF32Ring) & 1) ^ 1, err, kErrTimeoutRouterLoad);
+            const uint16_t* src = raw + (size_t)rs * kRtRows * kRtK;
+            float* dst = fs + (size_t)s * kRtRows * kRtS;
+#pragma unroll 8
+            for (int j = 0; j < kPer; ++j) {
+                const uint32_t i = ct + 32u * kRtCvtWarps * j;
+                rt_convert8(src, dst, i / kVpr, i % kVpr);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&f32_full[s]);
+                mbar_arrive(&raw_empty[rs]);
+            }
+        }
+    } else if (lane == 0) {  // producer
+        for (uint32_t c = 0; c < nchunks; ++c) {
+            const uint32_t rs = c % kRtRing;
+            mbar_wait(&raw_empty[rs], ((c / kRtRing) & 1) ^ 1, err, kErrTimeoutRouterLoad, true);
+            mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)kRtRawBytes);
+            uint16_t* dst = raw + (size_t)rs * kRtRows * kRtK;
+            tma_load_2d(dst, &tmap_x, (int32_t)(c * kRtK), (int32_t)t0, &raw_full[rs]);
+            tma_load_2d(dst + (size_t)kRtTok * kRtK, &tmap_w, (int32_t)(c * kRtK), (int32_t)e0, &raw_full[rs]);
         }
     }
 }
 
-// ---------------------------------------------------------------------------
-// Scores + top-k of one token, by one warp.  `p` holds the token's E logits
-// on entry (shared memory; may alias nothing else) and its scores on exit.
-// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256, 1) router_logits_kernel(const uint16_t* __restrict__ x,
+                                                               const uint16_t* __restrict__ w, uint32_t T,
+                                                               uint32_t E, uint32_t H, float* __restrict__ logits) {
+    extern __shared__ __align__(128) unsigned char rt_smem[];
+    float* fs = reinterpret_cast<float*>(rt_smem);                        // [rows][kRtS]
+    uint16_t* raw = reinterpret_cast<uint16_t*>(rt_smem + kRtF32Bytes);  // [kRtRing][rows][kRtK]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t e0 = blockIdx.x * kRtExp, t0 = blockIdx.y * kRtTok;
+    const uint32_t main_end = H & ~15u;
+    const uint32_t nchunks = (main_end + kRtK - 1) / kRtK;
+
+    // Row r of the tile: a token row (r < kRtTok) or a router row; rows past
+    // T or E repeat the last one (their dots are computed and not stored).
+    auto row_ptr = [&](uint32_t r) -> const uint16_t* {
+        if (r < (uint32_t)kRtTok) return x + (uint64_t)min(t0 + r, T - 1) * H;
+        return w + (uint64_t)min(e0 + r - kRtTok, E - 1) * H;
+    };
+    auto stage = [&](uint32_t c) {  // chunk c into ring slot c % kRtRing
+        const uint32_t c0 = c * kRtK;
+        const uint32_t vpr = min((uint32_t)kRtK, main_end - c0) / 4;
+        uint16_t* dst = raw + (size_t)(c % kRtRing) * kRtRows * kRtK;
+        for (uint32_t i = threadIdx.x; i < kRtRows * vpr; i += blockDim.x) {
+            const uint32_t r = i / vpr, v = i % vpr;
+            cp_async8(dst + (size_t)r * kRtK + v * 4, row_ptr(r) + c0 + v * 4);
+        }
+        cp_async_commit();
+    };
+
+    RtLane ln(warp, lane);
+    for (uint32_t c = 0; c + 1 < kRtRing && c < nchunks; ++c) stage(c);
+    for (uint32_t c = 0; c < nchunks; ++c) {
+        if (c + 1 < nchunks) cp_async_wait<kRtRing - 2>();
+        else cp_async_wait<0>();
+        __syncthreads();  // chunk c visible to all; every lane done with chunk c - 1's fp32 tile
+        if (c + kRtRing - 1 < nchunks) stage(c + kRtRing - 1);  // into the slot chunk c - 1 used
+        const uint32_t clen = min((uint32_t)kRtK, main_end - c * kRtK);
+        const uint16_t* src = raw + (size_t)(c % kRtRing) * kRtRows * kRtK;
+        const uint32_t vpr = clen / 8;
+        for (uint32_t i = threadIdx.x; i < kRtRows * vpr; i += blockDim.x) rt_convert8(src, fs, i / vpr, i % vpr);
+        __syncthreads();
+        ln.chunk(fs, clen);
+    }
+    ln.finish(x, w, t0, e0, T, E, H, logits);
+}
+
 constexpr int kMaxExperts = 1024;
+
+// ---------------------------------------------------------------------------
+// expf as the reference's host C library computes it (glibc >= 2.28 on
+// x86-64 with FMA; the algorithm published in ARM's optimized-routines):
+// with N = 32, z = x * N / ln2 is split into k = round(z) and r = z - k
+// (r by one FMA, |r| <= 1/2); 2^(k/N) is a table entry 2^((k mod N)/N) with
+// k / N added to its exponent; 2^(r/N) is the cubic 1 + c2 r + c1 r^2 +
+// c0 r^3 evaluated by FMAs in double; the product is rounded once to float.
+// The table holds 2^(i/32) rounded to double, minus i/32 in the exponent
+// field.  Checked equal to the C library's expf for every float in
+// [-103.97, 88.72]; outside that range expf is 0 or +inf.
+// ---------------------------------------------------------------------------
+__device__ const uint64_t kExp2Tab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+
+__device__ __forceinline__ float libm_expf(float x) {
+    if (x != x) return x;
+    if (x > 0x1.62e42ep6f) return INFINITY;
+    if (x < -0x1.9fe368p6f) return 0.0f;
+    const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
+    const double c0 = 0x1.c6af84b912394p-5 / (32.0 * 32.0 * 32.0);
+    const double c1 = 0x1.ebfce50fac4f3p-3 / (32.0 * 32.0);
+    const double c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+    const double shift = 0x1.8p+52;
+    const double xd = (double)x;
+    const double z = __dmul_rn(inv_ln2_n, xd);
+    double kd = __dadd_rn(z, shift);
+    const uint64_t ki = (uint64_t)__double_as_longlong(kd);
+    kd = __dsub_rn(kd, shift);
+    const double r = __fma_rn(inv_ln2_n, xd, -kd);
+    const double s = __longlong_as_double((long long)(kExp2Tab[ki % 32] + (ki << 47)));
+    const double p = __fma_rn(__fma_rn(c0, r, c1), __dmul_rn(r, r), __fma_rn(c2, r, 1.0));
+    return __double2float_rn(__dmul_rn(p, s));
+}
 
 __device__ void topk_token(float* p, uint32_t t, uint32_t E, uint32_t K, int sigmoid, int norm_topk,
                            float routed_scale, int32_t* __restrict__ ids, float* __restrict__ wout,
@@ -142,7 +331,7 @@ __device__ void topk_token(float* p, uint32_t t, uint32_t E, uint32_t K, int sig
     const int lane = threadIdx.x & 31;
     if (sigmoid) {
         for (uint32_t e = lane; e < E; e += 32) {
-            const float ex = (float)exp(-(double)p[e]);
+            const float ex = libm_expf(-p[e]);
             p[e] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
         }
         __syncwarp();
@@ -211,20 +400,6 @@ __device__ void topk_token(float* p, uint32_t t, uint32_t E, uint32_t K, int sig
     }
 }
 
-// Top-k over logits in global memory: one warp per token.
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, uint32_t T, uint32_t E,
-                                                          uint32_t K, int sigmoid, int norm_topk, float routed_scale,
-                                                          int32_t* __restrict__ ids, float* __restrict__ wout,
-                                                          float* __restrict__ scores_out) {
-    __shared__ float ps[8][kMaxExperts];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t t = blockIdx.x * 8 + warp;
-    if (t >= T) return;
-    for (uint32_t e = lane; e < E; e += 32) ps[warp][e] = logits[(uint64_t)t * E + e];
-    __syncwarp();
-    topk_token(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
-}
-
 // ---------------------------------------------------------------------------
 // Scores + top-k of one token for E <= 32 * EPL experts, by one warp, all in
 // registers (expert e = lane + 32 q in slot q).  Same arithmetic and order as
@@ -247,7 +422,7 @@ __device__ void topk_token_reg(const float* lg, uint32_t t, uint32_t E, uint32_t
     if (sigmoid) {
 #pragma unroll
         for (int q = 0; q < EPL; ++q) {
-            const float ex = (float)exp(-(double)v[q]);
+            const float ex = libm_expf(-v[q]);
             v[q] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
         }
     } else {
@@ -315,6 +490,30 @@ __device__ void topk_token_reg(const float* lg, uint32_t t, uint32_t E, uint32_t
         if (scale != 1.0f) wv = __fmul_rn(wv, scale);
         ids[(uint64_t)t * K + lane] = my_i;
         wout[(uint64_t)t * K + lane] = wv;
+    }
+}
+
+// Top-k over logits in global memory: one warp per token.
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, uint32_t T, uint32_t E,
+                                                          uint32_t K, int sigmoid, int norm_topk, float routed_scale,
+                                                          int32_t* __restrict__ ids, float* __restrict__ wout,
+                                                          float* __restrict__ scores_out) {
+    __shared__ float ps[8][kMaxExperts];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    for (uint32_t e = lane; e < E; e += 32) ps[warp][e] = logits[(uint64_t)t * E + e];
+    __syncwarp();
+    if (K <= 32 && E <= 32) {
+        topk_token_reg<1>(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+    } else if (K <= 32 && E <= 64) {
+        topk_token_reg<2>(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+    } else if (K <= 32 && E <= 128) {
+        topk_token_reg<4>(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+    } else if (K <= 32 && E <= 256) {
+        topk_token_reg<8>(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+    } else {
+        topk_token(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
     }
 }
 
@@ -819,9 +1018,18 @@ static uint32_t router_fused_tb(const uint16_t* x, const uint16_t* w, uint32_t T
     return tb;
 }
 
+uint32_t router_box_rows(bool tokens) { return tokens ? kRtTok : kRtExp; }
+
+bool router_wants_tma(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H) {
+    if (T == 0 || router_fused_tb(x, w, T, E, H)) return false;
+    return H % 8 == 0 && !(reinterpret_cast<uintptr_t>(x) & 15) && !(reinterpret_cast<uintptr_t>(w) & 15) &&
+           (H & ~15u) > 0;
+}
+
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
                           int sigmoid, int norm_topk, float routed_scale, float* logits, int32_t* ids, float* wout,
-                          float* scores, uint32_t* err, cudaStream_t st, uint32_t* launches) {
+                          float* scores, uint32_t* err, cudaStream_t st, uint32_t* launches,
+                          const CUtensorMap* tmap_x, const CUtensorMap* tmap_w) {
     if (T == 0) return cudaSuccess;
     const uint32_t tb = router_fused_tb(x, w, T, E, H);
     if (tb) {
@@ -840,8 +1048,25 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
         if (launches) *launches += 1;
         return cudaGetLastError();
     }
-    dim3 g1(ceil_div(T, kRtTok), ceil_div(E, kRtExp));
-    router_logits_kernel<<<g1, 256, 0, st>>>(x, w, T, E, H, logits);
+    static uint64_t rt_attr = 0;  // one bit per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 64 && !((rt_attr >> dev) & 1u)) {
+        e = cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRtSmem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(router_logits_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kRtTmaSmem);
+        if (e != cudaSuccess) return e;
+        rt_attr |= 1ull << dev;
+    }
+    if (ceil_div(T, kRtTok) > 65535u) return cudaErrorInvalidValue;  // grid y limit: T <= 2,097,120
+    dim3 g1(ceil_div(E, kRtExp), ceil_div(T, kRtTok));
+    if (tmap_x && tmap_w)
+        router_logits_tma_kernel<<<g1, kRtTmaThreads, kRtTmaSmem, st>>>(*tmap_x, *tmap_w, x, w, T, E, H, logits,
+                                                                         err);
+    else
+        router_logits_kernel<<<g1, 256, kRtSmem, st>>>(x, w, T, E, H, logits);
     router_topk_kernel<<<ceil_div(T, 8), 256, 0, st>>>(logits, T, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
                                                        scores);
     if (launches) *launches += 2;

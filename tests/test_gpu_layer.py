@@ -192,3 +192,36 @@ def test_permutation_paths_match_reference_order(engine, synth, L, port, tokens,
     assert np.array_equal(out["ids"], ids)
     mx, mr = errors(out["y_f32"], y_ref)
     assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+
+
+@pytest.mark.parametrize("tokens,experts,hidden,offset,sigmoid", [
+    (600, 128, 200, 0, False),   # H % 16 == 8: the reference's 4-way tail
+    (333, 256, 264, 4, False),   # rows only 8-byte aligned (8-byte staging copies)
+    (1501, 72, 136, 0, True),    # partial token and expert tiles; sigmoid (C-library expf) scores
+    (260, 300, 2056, 0, False),  # several staged chunks, the top-k past 256 experts
+], ids=["tail", "aligned8", "partial_sigmoid", "chunks_e300"])
+def test_tiled_router_matches_oracle(engine, synth, L, port, tokens, experts, hidden, offset, sigmoid):
+    """Batches too large for the single-kernel router: logits, scores, ids and
+    weights are bit-identical to the oracle's, including the reference's
+    4-way and scalar tails and activation rows that are only 8-byte aligned."""
+    import torch
+    K = 4
+    shape = synth.small_shape(hidden=hidden, intermediate=64, experts=experts, top_k=K, tokens=tokens)
+    li = synth.make_layer(shape, seed=11 + tokens + experts)
+    engine.upload_layer(li)
+    rs = 2.5 if sigmoid else 1.0
+    cfg = L.Engine.cfg(shape, score_func=L.SCORE_SIGMOID if sigmoid else L.SCORE_SOFTMAX, norm_topk=sigmoid,
+                       routed_scale=rs)
+    flat = torch.zeros(offset + tokens * hidden, dtype=torch.int16, device="cuda")
+    x = flat[offset:].view(tokens, hidden)
+    x.copy_(torch.from_numpy(li.x.view(np.int16)))
+    ids = torch.empty((tokens, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((tokens, K), dtype=torch.float32, device="cuda")
+    yf = torch.empty((tokens, hidden), dtype=torch.float32, device="cuda")
+    engine.forward(cfg, x, tokens, y_f32=yf, ids=ids, w=w)
+    engine.sync()
+    ids_ref, w_ref, scores_ref, _ = port.router_topk(li, score_sigmoid=int(sigmoid), norm_topk=int(sigmoid), routed_scale=rs)
+    scores = engine.read(L.BUF_SCORES, (tokens, experts), np.float32)
+    assert np.array_equal(bits(scores), bits(scores_ref))
+    assert np.array_equal(ids.cpu().numpy(), ids_ref)
+    assert np.array_equal(bits(w.cpu().numpy()), bits(w_ref))
