@@ -23,17 +23,19 @@ namespace moe_b200 {
 // ---------------------------------------------------------------------------
 // Router logits for large batches.  A block computes a 32-token x 64-expert
 // tile.  The reference accumulates each dot product in 16 FMA chains (chain l
-// takes elements l, l+16, ...); here a quad of lanes shares a dot's 16
-// chains, lane q owning chains 4q..4q+3, and each lane does this for 8 tokens
-// x 4 experts: 128 independent chains, advanced two at a time by packed fp32
-// FMAs (fma.rn.f32x2, each half an IEEE fp32 FMA), fed by 12 16-byte shared
-// loads per 16 elements.  The chains read an fp32 copy of each 128-element
-// chunk of the rows, so the FMA loop does no conversions.  Within a warp the
-// two token sub-groups read adjacent rows and the fp32 row stride is 16 words
-// past a multiple of 32, so the 8 distinct x addresses of a quarter-warp
-// cover the 32 banks once.  Each dot's 16 chains are combined exactly as the
-// reference does: b_l = s_l + s_{l+8}, then ((b0+b1)+b2)+...+b7, then the
-// 4-way and scalar tails (H % 16 != 0).
+// takes elements l, l+16, ...).  Here lane l of a 16-lane half-warp runs chain
+// l for 16 tokens x 8 experts (128 independent chains), two tokens at a time
+// with packed fp32 FMAs (fma.rn.f32x2, each half an IEEE fp32 FMA).  Per 16
+// elements a lane does 24 four-byte shared loads for 128 FMAs; the two
+// half-warps read the same token rows (one broadcast wavefront) and adjacent
+// router rows whose fp32 row stride is 16 words past a multiple of 32 (disjoint
+// banks, one wavefront): 0.19 wavefronts per FMA, under the shared-memory
+// pipe's 0.25 at the FMA peak.  The chains read an fp32 copy of each
+// 128-element chunk of the rows, so the FMA loop does no conversions.  At the
+// end each lane's chain sums go through shared memory so that one lane holds
+// all 16 chains of a dot, which it combines exactly as the reference does:
+// b_l = s_l + s_{l+8}, then ((b0+b1)+b2)+...+b7, then the 4-way and scalar
+// tails (H % 16 != 0).
 //
 // router_logits_tma_kernel (16-byte aligned rows) specialises warps: one
 // lane brings each chunk's token and router rows in with two TMA copies into
@@ -43,8 +45,7 @@ namespace moe_b200 {
 // router_logits_kernel (rows only 8-byte aligned) stages with 8-byte
 // cp.async and converts in lockstep with the FMAs.
 // ---------------------------------------------------------------------------
-constexpr int kRtRT = 8;                         // tokens per lane (x 4 experts x 4 chains)
-constexpr int kRtTok = 4 * kRtRT, kRtExp = 64;   // block tile
+constexpr int kRtTok = 32, kRtExp = 64;          // block tile
 constexpr int kRtK = 128;                        // elements per chunk (multiple of 16)
 constexpr int kRtS = kRtK + 16;                  // fp32 row stride in words (== 16 mod 32)
 constexpr int kRtRows = kRtTok + kRtExp;
@@ -52,8 +53,13 @@ constexpr int kRtRing = 3;                       // bf16 chunk buffers
 constexpr int kRtF32Ring = 2;                    // fp32 chunk buffers (TMA kernel)
 constexpr size_t kRtF32Bytes = (size_t)kRtRows * kRtS * 4;
 constexpr size_t kRtRawBytes = (size_t)kRtRows * kRtK * 2;
-constexpr size_t kRtSmem = kRtF32Bytes + kRtRing * kRtRawBytes;
-constexpr size_t kRtTmaSmem = kRtF32Ring * kRtF32Bytes + kRtRing * kRtRawBytes + 128;
+constexpr int kRtDots = 256;                     // dots per warp (16 tokens x 16 experts)
+constexpr int kRtScratch = kRtDots * 17 + 16;    // floats of a warp's transpose area
+constexpr size_t kRtScratchBytes = 8ull * kRtScratch * 4;
+constexpr size_t kRtSmem = std::max(kRtF32Bytes + kRtRing * kRtRawBytes, kRtScratchBytes);
+constexpr size_t kRtTmaRings = kRtF32Ring * kRtF32Bytes + kRtRing * kRtRawBytes;
+static_assert(kRtScratchBytes <= kRtTmaRings, "transpose area inside the rings");
+constexpr size_t kRtTmaSmem = kRtTmaRings + 128;
 constexpr int kRtFmaWarps = 8, kRtCvtWarps = 2;
 constexpr int kRtTmaThreads = 32 * (kRtFmaWarps + kRtCvtWarps + 1);
 
@@ -64,6 +70,11 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+__device__ __forceinline__ unsigned long long pack_f32x2(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
 // d.lo += a.lo * b.lo, d.hi += a.hi * b.hi, each rounded once (IEEE fp32 FMA)
 __device__ __forceinline__ void fma_f32x2(unsigned long long& d, unsigned long long a, unsigned long long b) {
     asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
@@ -82,83 +93,83 @@ __device__ __forceinline__ void rt_convert8(const uint16_t* raw, float* fs, uint
     d[1] = hi;
 }
 
-// The FMA lanes' share of the block: 8 warps, tile rows and accumulators.
+// One FMA warp's share of the block tile: tokens tg*16 + a (a < 16), experts
+// eg*16 + 2j + p (j < 8) for half-warp p, chain l = lane % 16.
 struct RtLane {
-    int q, trow, erow;
-    unsigned long long acc[kRtRT][4][2];
+    int l, p, tg, eg;
+    unsigned long long acc[8][8];  // [token pair i][expert j]: lo token 2i, hi token 2i+1
     __device__ __forceinline__ RtLane(int warp, int lane) {
-        const int pos = lane >> 2;
-        q = lane & 3;
-        // token rows: trow + 2a (a < kRtRT); expert rows: kRtTok + erow + 4b (b < 4)
-        trow = (warp & 1) * (2 * kRtRT) + (pos & 1);
-        erow = (warp >> 1) * 16 + (pos >> 1);
+        l = lane & 15;
+        p = lane >> 4;
+        tg = warp & 1;
+        eg = warp >> 1;
 #pragma unroll
-        for (int a = 0; a < kRtRT; ++a)
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int b = 0; b < 4; ++b) acc[a][b][0] = acc[a][b][1] = 0ull;
+            for (int j = 0; j < 8; ++j) acc[i][j] = 0ull;
     }
     // the 16-element steps of one chunk of the fp32 tile `fs`
     __device__ __forceinline__ void chunk(const float* fs, uint32_t clen) {
-        const float* xp = fs + (size_t)trow * kRtS + 4 * q;
-        const float* wp = fs + (size_t)(kRtTok + erow) * kRtS + 4 * q;
+        const float* xp = fs + (size_t)(tg * 16) * kRtS + l;
+        const float* wp = fs + (size_t)(kRtTok + eg * 16 + p) * kRtS + l;
 #pragma unroll 1
         for (uint32_t k = 0; k < clen; k += 16) {
-            ulonglong2 wv[4];
+            unsigned long long wd[8];
 #pragma unroll
-            for (int b = 0; b < 4; ++b) wv[b] = *reinterpret_cast<const ulonglong2*>(wp + (size_t)(4 * b) * kRtS + k);
+            for (int j = 0; j < 8; ++j) {
+                const float wv = wp[(size_t)(2 * j) * kRtS + k];
+                wd[j] = pack_f32x2(wv, wv);
+            }
 #pragma unroll
-            for (int a = 0; a < kRtRT; ++a) {
-                const ulonglong2 xv = *reinterpret_cast<const ulonglong2*>(xp + (size_t)(2 * a) * kRtS + k);
+            for (int i = 0; i < 8; ++i) {
+                const unsigned long long xv = pack_f32x2(xp[(size_t)(2 * i) * kRtS + k], xp[(size_t)(2 * i + 1) * kRtS + k]);
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    fma_f32x2(acc[a][b][0], wv[b].x, xv.x);
-                    fma_f32x2(acc[a][b][1], wv[b].y, xv.y);
-                }
+                for (int j = 0; j < 8; ++j) fma_f32x2(acc[i][j], xv, wd[j]);
             }
         }
     }
-    // Lane q holds chains 4q..4q+3.  b_l = s_l + s_{l+8} lands on q = 0
-    // (l < 4) and q = 1 (4 <= l < 8); q = 0 sums b0..b3 in order and q = 1
-    // continues with b4..b7, then adds the tails and stores.
-    __device__ __forceinline__ void finish(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
-                                           uint32_t t0, uint32_t e0, uint32_t T, uint32_t E, uint32_t H,
-                                           float* __restrict__ logits) {
-        const unsigned full_mask = 0xffffffffu;
+    // `sc`: this warp's transpose area (kRtScratch floats), free for its use.
+    __device__ __forceinline__ void finish(float* sc, const uint16_t* __restrict__ x,
+                                           const uint16_t* __restrict__ w, uint32_t t0, uint32_t e0, uint32_t T,
+                                           uint32_t E, uint32_t H, float* __restrict__ logits) {
+        // dot d = p*128 + a*8 + j keeps its 16 chain sums at d*17 + (d/128)*16
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int d0 = p * 128 + (2 * i) * 8 + j;
+                sc[d0 * 17 + p * 16 + l] = __uint_as_float((uint32_t)acc[i][j]);
+                sc[(d0 + 8) * 17 + p * 16 + l] = __uint_as_float((uint32_t)(acc[i][j] >> 32));
+            }
+        __syncwarp();
         const int lane = threadIdx.x & 31;
         const uint32_t main_end = H & ~15u;
+#pragma unroll 1
+        for (int m = 0; m < kRtDots / 32; ++m) {
+            const int d = lane + 32 * m;
+            const int dp = d >> 7, a = (d & 127) >> 3, j = d & 7;
+            const float* s = sc + d * 17 + dp * 16;
+            float sum = __fadd_rn(s[0], s[8]);
 #pragma unroll
-        for (int a = 0; a < kRtRT; ++a) {
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const float sc[4] = {__uint_as_float((uint32_t)acc[a][b][0]),
-                                     __uint_as_float((uint32_t)(acc[a][b][0] >> 32)),
-                                     __uint_as_float((uint32_t)acc[a][b][1]),
-                                     __uint_as_float((uint32_t)(acc[a][b][1] >> 32))};
-                float bl[4];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) bl[c] = __fadd_rn(sc[c], __shfl_xor_sync(full_mask, sc[c], 2));
-                float s = __fadd_rn(__fadd_rn(__fadd_rn(bl[0], bl[1]), bl[2]), bl[3]);
-                const float s0 = __shfl_sync(full_mask, s, lane & ~3);
-                s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, bl[0]), bl[1]), bl[2]), bl[3]);
-                const uint32_t tt = t0 + trow + 2 * a, e = e0 + erow + 4 * b;
-                if (q == 1 && tt < T && e < E) {
-                    float out = 0.0f + s;
-                    if (main_end < H) {
-                        const uint16_t* wr = w + (uint64_t)e * H;
-                        const uint16_t* xr = x + (uint64_t)tt * H;
-                        uint32_t i = main_end;
-                        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                        for (; i + 3 < H; i += 4) {
-                            a0 = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), a0);
-                            a1 = __fmaf_rn(bf16_bits_to_f32(wr[i + 1]), bf16_bits_to_f32(xr[i + 1]), a1);
-                            a2 = __fmaf_rn(bf16_bits_to_f32(wr[i + 2]), bf16_bits_to_f32(xr[i + 2]), a2);
-                            a3 = __fmaf_rn(bf16_bits_to_f32(wr[i + 3]), bf16_bits_to_f32(xr[i + 3]), a3);
-                        }
-                        out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
-                        for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), out);
+            for (int c = 1; c < 8; ++c) sum = __fadd_rn(sum, __fadd_rn(s[c], s[c + 8]));
+            const uint32_t tt = t0 + tg * 16 + a, e = e0 + eg * 16 + 2 * j + dp;
+            if (tt < T && e < E) {
+                float out = 0.0f + sum;
+                if (main_end < H) {
+                    const uint16_t* wr = w + (uint64_t)e * H;
+                    const uint16_t* xr = x + (uint64_t)tt * H;
+                    uint32_t i = main_end;
+                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                    for (; i + 3 < H; i += 4) {
+                        a0 = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), a0);
+                        a1 = __fmaf_rn(bf16_bits_to_f32(wr[i + 1]), bf16_bits_to_f32(xr[i + 1]), a1);
+                        a2 = __fmaf_rn(bf16_bits_to_f32(wr[i + 2]), bf16_bits_to_f32(xr[i + 2]), a2);
+                        a3 = __fmaf_rn(bf16_bits_to_f32(wr[i + 3]), bf16_bits_to_f32(xr[i + 3]), a3);
                     }
-                    logits[(uint64_t)tt * E + e] = out;
+                    out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
+                    for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[i]), bf16_bits_to_f32(xr[i]), out);
                 }
+                logits[(uint64_t)tt * E + e] = out;
             }
         }
     }
@@ -171,7 +182,7 @@ __global__ void __launch_bounds__(kRtTmaThreads, 1)
     extern __shared__ __align__(128) unsigned char rt_smem[];
     float* fs = reinterpret_cast<float*>(rt_smem);                                       // [kRtF32Ring][rows][kRtS]
     uint16_t* raw = reinterpret_cast<uint16_t*>(rt_smem + kRtF32Ring * kRtF32Bytes);      // [kRtRing][rows][kRtK]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(rt_smem + kRtF32Ring * kRtF32Bytes + kRtRing * kRtRawBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rt_smem + kRtTmaRings);
     uint64_t* raw_full = bars;                      // TMA bytes landed
     uint64_t* raw_empty = bars + kRtRing;           // converters done reading
     uint64_t* f32_full = bars + 2 * kRtRing;        // converters done writing
@@ -203,7 +214,11 @@ __global__ void __launch_bounds__(kRtTmaThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&f32_empty[s]);
         }
-        ln.finish(x, w, t0, e0, T, E, H, logits);
+        // every FMA warp is past its last chunk; the converters and the
+        // producer finished before the last chunk could be read, so both
+        // rings are free for the transpose
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kRtFmaWarps) : "memory");
+        ln.finish(reinterpret_cast<float*>(rt_smem) + (size_t)warp * kRtScratch, x, w, t0, e0, T, E, H, logits);
     } else if (warp < kRtFmaWarps + kRtCvtWarps) {
         const uint32_t ct = threadIdx.x - 32 * kRtFmaWarps;  // 0..63
         constexpr int kVpr = kRtK / 8, kPer = kRtRows * kVpr / (32 * kRtCvtWarps);
@@ -279,7 +294,8 @@ __global__ void __launch_bounds__(256, 1) router_logits_kernel(const uint16_t* _
         __syncthreads();
         ln.chunk(fs, clen);
     }
-    ln.finish(x, w, t0, e0, T, E, H, logits);
+    __syncthreads();  // tile and ring free for the transpose
+    ln.finish(reinterpret_cast<float*>(rt_smem) + (size_t)warp * kRtScratch, x, w, t0, e0, T, E, H, logits);
 }
 
 constexpr int kMaxExperts = 1024;
