@@ -1,10 +1,13 @@
 // Expert parallelism across GPUs (one process and one engine per GPU).
 //
-// Rank r of W owns the contiguous expert block [r*E/W, (r+1)*E/W); the
-// router and the shared expert are replicated, tokens are data-parallel.
-// One layer call on the rank's own T tokens:
+// By default rank r of W owns the contiguous expert block
+// [r*E/W, (r+1)*E/W); moe_b200_ep_set_placement installs any other placement,
+// with an expert replicated on several ranks (its tokens then take the
+// replicas in turn).  The router and the shared expert are replicated, tokens
+// are data-parallel.  One layer call on the rank's own T tokens:
 //   1. router + top-k on the local tokens (full E);
-//   2. a stable sort of the T*K assignments by owner rank;
+//   2. owner rank of each assignment (the replica tables), then a stable
+//      sort of the T*K assignments by owner rank;
 //   3. NCCL all-gather of the per-rank row counts (the W x W count matrix),
 //      read once on the host: every rank then knows where each of its rows
 //      lands in every other rank's receive buffer;
