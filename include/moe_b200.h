@@ -67,6 +67,14 @@ typedef struct {
     float routed_scale;    /* applied for sigmoid routers only (:669-674); 0 -> 1 */
     int32_t use_shared;    /* add the layer's always-on shared expert (generation_mlp.cpp.inc:833-860) */
     int32_t gemm_path;     /* MOE_B200_GEMM_* */
+    /* Group limit of sigmoid routers (generation_router.cpp.inc:484-558):
+     * with n_group > 1, 0 < topk_group < n_group and experts % n_group == 0,
+     * only the topk_group groups with the largest top-2 score sums keep their
+     * scores, the others' are zeroed before the top-k.  0 = none (the
+     * reference skips the limit for any other combination, and so does this
+     * library); n_group <= 256. */
+    uint32_t n_group;
+    uint32_t topk_group;
 } moe_b200_layer_cfg_t;
 
 /* Same layout as moe_token_expert_assignment_t / moe_expert_batch_t

@@ -131,15 +131,59 @@ float mo_bf16_dot_row(const uint16_t* w, const float* x, uint32_t n) {
 /* x / (1 + exp(-x)) with the exact libm exp: generation_silu.cpp.inc:20-26. */
 float mo_silu(float x) { return x / (1.0f + expf(-x)); }
 
+/* Group limit of sigmoid routers (generation_router.cpp.inc:484-558),
+ * applied when n_group > 1, 0 < topk_group < n_group and E % n_group == 0:
+ * each group's score is the sum of its two largest scores (best0/best1
+ * updated from 0 in expert order; the largest alone for one expert per
+ * group), the topk_group best groups keep their scores and the other groups'
+ * scores become 0.  The reference picks the groups with std::nth_element,
+ * whose order among equal group scores is unspecified; this restatement
+ * takes the lower group index first and counts such ties in *ties. */
+static void mo_group_limit(const mo_layer_t* L, float* p, uint32_t* ties) {
+    const uint32_t E = L->experts, G = L->n_group, TG = L->topk_group;
+    if (G <= 1 || TG == 0 || TG >= G || E % G != 0) return;
+    const uint32_t epg = E / G;
+    float* gs = (float*)malloc(sizeof(float) * G);
+    unsigned char* keep = (unsigned char*)calloc(G, 1);
+    if (!gs || !keep) { free(gs); free(keep); return; }
+    for (uint32_t g = 0; g < G; ++g) {
+        float b0 = 0.0f, b1 = 0.0f;
+        for (uint32_t e = g * epg; e < (g + 1) * epg; ++e) {
+            const float v = p[e];
+            if (v > b0) { b1 = b0; b0 = v; } else if (v > b1) { b1 = v; }
+        }
+        gs[g] = epg > 1 ? b0 + b1 : b0;
+    }
+    for (uint32_t j = 0; j < TG; ++j) {
+        int32_t best = -1;
+        for (uint32_t g = 0; g < G; ++g)
+            if (!keep[g] && (best < 0 || gs[g] > gs[best])) best = (int32_t)g;
+        keep[best] = 1;
+    }
+    if (ties) {
+        for (uint32_t g = 0; g < G; ++g) {
+            if (!keep[g]) continue;
+            for (uint32_t h = 0; h < G; ++h)
+                if (!keep[h] && gs[h] == gs[g]) { ++*ties; break; }
+        }
+    }
+    for (uint32_t g = 0; g < G; ++g)
+        if (!keep[g])
+            for (uint32_t e = g * epg; e < (g + 1) * epg; ++e) p[e] = 0.0f;
+    free(gs);
+    free(keep);
+}
+
 /* Router scores (generation_router.cpp.inc:188-237, 587-623): logits by the
  * bf16 row dot, then softmax with exp in double, the denominator summed in
  * double in expert order, and each score multiplied by (float)(1/denom); or
- * sigmoid 1/(1+exp(-l)) in float (:239-245). */
-void mo_router_scores(const mo_layer_t* L, const float* x, float* p) {
+ * sigmoid 1/(1+exp(-l)) in float (:239-245) followed by the group limit. */
+static void mo_router_scores_t(const mo_layer_t* L, const float* x, float* p, uint32_t* ties) {
     const uint32_t E = L->experts, H = L->hidden;
     for (uint32_t e = 0; e < E; ++e) p[e] = mo_bf16_dot_row(L->router_bf16 + (uint64_t)e * H, x, H);
     if (L->score_sigmoid) {
         for (uint32_t e = 0; e < E; ++e) p[e] = 1.0f / (1.0f + expf(-p[e]));
+        mo_group_limit(L, p, ties);
         return;
     }
     float mx = -INFINITY;
@@ -152,6 +196,8 @@ void mo_router_scores(const mo_layer_t* L, const float* x, float* p) {
     const float inv = (float)(1.0 / denom);
     for (uint32_t e = 0; e < E; ++e) p[e] *= inv;
 }
+
+void mo_router_scores(const mo_layer_t* L, const float* x, float* p) { mo_router_scores_t(L, x, p, NULL); }
 
 /* Top-k of the router scores (generation_router.cpp.inc:640-674): the k
  * largest scores in descending order.  The reference uses
@@ -167,7 +213,7 @@ int mo_router_topk(const mo_layer_t* L, const float* x, int32_t* ids, float* w, 
     float* p = (float*)malloc(sizeof(float) * E);
     unsigned char* taken = (unsigned char*)calloc(E, 1);
     if (!p || !taken) { free(p); free(taken); return 0; }
-    mo_router_scores(L, x, p);
+    mo_router_scores_t(L, x, p, ties);
     for (uint32_t j = 0; j < K; ++j) {
         int32_t best = -1;
         for (uint32_t e = 0; e < E; ++e) {

@@ -37,6 +37,8 @@ typedef struct {
     const uint8_t* shared_gate;    /* optional always-on expert */
     const uint8_t* shared_up;
     const uint8_t* shared_down;
+    uint32_t n_group;        /* group limit of sigmoid routers: groups ... */
+    uint32_t topk_group;     /* ... of which this many keep their scores; 0 = none */
 } mo_layer_t;
 
 float mo_e8m0_to_f32(uint8_t v);

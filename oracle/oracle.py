@@ -49,7 +49,8 @@ class MoLayer(C.Structure):
     _fields_ = [("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("experts", C.c_uint32),
                 ("top_k", C.c_uint32), ("score_sigmoid", C.c_int32), ("norm_topk", C.c_int32),
                 ("routed_scale", C.c_float), ("router_bf16", _u16p), ("gate", _u8p), ("up", _u8p),
-                ("down", _u8p), ("shared_gate", _u8p), ("shared_up", _u8p), ("shared_down", _u8p)]
+                ("down", _u8p), ("shared_gate", _u8p), ("shared_up", _u8p), ("shared_down", _u8p),
+                ("n_group", C.c_uint32), ("topk_group", C.c_uint32)]
 
 
 class RefLayer(C.Structure):
@@ -100,7 +101,7 @@ class Port:
         L.mo_moe_layer.argtypes = [C.POINTER(MoLayer), _u16p, C.c_uint32, _f32p, _i32p, _f32p,
                                    C.c_uint32, _u32p]
 
-    def _layer(self, li, score_sigmoid=0, norm_topk=None, routed_scale=1.0):
+    def _layer(self, li, score_sigmoid=0, norm_topk=None, routed_scale=1.0, n_group=0, topk_group=0):
         s = li.shape
         keep = dict(router=_c(li.router, np.uint16), gate=_c(li.gate, np.uint8), up=_c(li.up, np.uint8),
                     down=_c(li.down, np.uint8), sg=_c(li.shared_gate, np.uint8),
@@ -109,7 +110,7 @@ class Port:
         L = MoLayer(s.hidden, s.intermediate, s.experts, s.top_k, int(score_sigmoid), int(nt),
                     float(routed_scale), _p(keep["router"], _u16p), _p(keep["gate"], _u8p),
                     _p(keep["up"], _u8p), _p(keep["down"], _u8p), _p(keep["sg"], _u8p),
-                    _p(keep["su"], _u8p), _p(keep["sd"], _u8p))
+                    _p(keep["su"], _u8p), _p(keep["sd"], _u8p), int(n_group), int(topk_group))
         return L, keep
 
     def moe_layer(self, li, x=None, threads: int = 0, **kw):
@@ -262,12 +263,15 @@ def bf16_to_f32(b: np.ndarray) -> np.ndarray:
 
 
 def metadata_json(top_k: int, norm_topk: bool = False, sigmoid: bool = False,
-                  routed_scale: float = 1.0) -> str:
+                  routed_scale: float = 1.0, n_group: int = 0, topk_group: int = 0) -> str:
     """GGUF metadata keys the reference router reads
-    (generation_router.cpp.inc:361-482)."""
+    (generation_router.cpp.inc:361-558)."""
     parts = [f'"num_experts_per_tok":{int(top_k)}', f'"norm_topk_prob":{"true" if norm_topk else "false"}']
     if sigmoid:
         parts.append('"scoring_func":"sigmoid"')
         if routed_scale != 1.0:
             parts.append(f'"routed_scaling_factor":{routed_scale!r}')
+    if n_group:
+        parts.append(f'"n_group":{int(n_group)}')
+        parts.append(f'"topk_group":{int(topk_group)}')
     return "{" + ",".join(parts) + "}"

@@ -43,6 +43,11 @@ int check_dims(const moe_b200_layer_cfg_t* c, char* err) {
         set_err(err, "top_k=%u outside 1..min(32, experts)", c->top_k);
         return 0;
     }
+    if (c->score_func == MOE_B200_SCORE_SIGMOID && c->n_group > 256 && c->topk_group > 0 &&
+        c->topk_group < c->n_group && c->experts % c->n_group == 0) {
+        set_err(err, "n_group=%u: group limits of more than 256 groups are not supported", c->n_group);
+        return 0;
+    }
     return 1;
 }
 
@@ -557,7 +562,8 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     const float rscale = cfg->routed_scale > 0.f ? cfg->routed_scale : 1.0f;
     CUtensorMap rtx, rtw;
     const bool rt_tma = router_tmaps(eng, x, L->router.as<uint16_t>(), T, E, H, &rtx, &rtw);
-    CK(launch_router(x, L->router.as<uint16_t>(), T, E, H, K, sigmoid, cfg->norm_topk, rscale,
+    CK(launch_router(x, L->router.as<uint16_t>(), T, E, H, K,
+                     RouteCfg{sigmoid, cfg->norm_topk, rscale, cfg->n_group, cfg->topk_group},
                      eng->logits.as<float>(), ids, w, eng->scores.as<float>(), errw, st, &launches,
                      rt_tma ? &rtx : nullptr, rt_tma ? &rtw : nullptr));
     mark(1);

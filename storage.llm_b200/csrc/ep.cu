@@ -516,7 +516,8 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
         const float rscale = cfg->routed_scale > 0.f ? cfg->routed_scale : 1.0f;
         CUtensorMap rtx, rtw;
         const bool rt_tma = router_tmaps(eng, x, L->router.as<uint16_t>(), T, E, H, &rtx, &rtw);
-        CK(launch_router(x, L->router.as<uint16_t>(), T, E, H, K, sigmoid, cfg->norm_topk, rscale,
+        CK(launch_router(x, L->router.as<uint16_t>(), T, E, H, K,
+                         RouteCfg{sigmoid, cfg->norm_topk, rscale, cfg->n_group, cfg->topk_group},
                          eng->logits.as<float>(), ids, w, eng->scores.as<float>(), errw, st, &launches,
                          rt_tma ? &rtx : nullptr, rt_tma ? &rtw : nullptr));
     }

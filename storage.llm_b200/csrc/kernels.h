@@ -88,10 +88,18 @@ cudaError_t launch_dequant_wtiles(const uint8_t* tiles, uint32_t rows, uint32_t 
 // Logits + top-k; adds the number of kernels it launched to *launches.
 // tmap_x / tmap_w (both or neither): router_tmap_x / router_tmap_w maps of
 // x and w, for the TMA-fed logits kernel of large batches.
+// Routing semantics (generation_router.cpp.inc:560-682).
+struct RouteCfg {
+    int sigmoid;          // sigmoid scores (else softmax)
+    int norm_topk;        // renormalise the k weights
+    float routed_scale;   // sigmoid routers: weights scaled by this
+    uint32_t n_group;     // group limit (sigmoid routers): groups ...
+    uint32_t topk_group;  // ... of which this many keep their scores; 0: none
+};
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
-                          int sigmoid, int norm_topk, float routed_scale, float* logits, int32_t* ids, float* wout,
-                          float* scores, uint32_t* err, cudaStream_t st, uint32_t* launches,
-                          const CUtensorMap* tmap_x = nullptr, const CUtensorMap* tmap_w = nullptr);
+                          const RouteCfg& rc, float* logits, int32_t* ids, float* wout, float* scores, uint32_t* err,
+                          cudaStream_t st, uint32_t* launches, const CUtensorMap* tmap_x = nullptr,
+                          const CUtensorMap* tmap_w = nullptr);
 // Box of the router's tensor maps: 128 bf16 columns x box_rows rows, no
 // swizzle (router_box_rows(true) for x, (false) for w).
 uint32_t router_box_rows(bool tokens);

@@ -341,9 +341,72 @@ __device__ __forceinline__ float libm_expf(float x) {
     return __double2float_rn(__dmul_rn(p, s));
 }
 
-__device__ void topk_token(float* p, uint32_t t, uint32_t E, uint32_t K, int sigmoid, int norm_topk,
-                           float routed_scale, int32_t* __restrict__ ids, float* __restrict__ wout,
-                           float* __restrict__ scores_out) {
+// Group limit of sigmoid routers (generation_router.cpp.inc:484-558) on the
+// scores p[0, E) of one token, by one warp (p in shared memory).  Group g is
+// experts [g*E/G, (g+1)*E/G); its score is the sum of its two largest scores
+// (the largest alone for one expert per group), kept by the reference's
+// running best0/best1 update from 0.  The TG groups with the largest scores
+// keep their experts' scores, the others' are set to 0.  Equal group scores
+// resolve to the lower group index (the reference's nth_element leaves that
+// order open).  G <= 256.
+__device__ void group_limit_warp(float* p, uint32_t E, uint32_t G, uint32_t TG) {
+    const unsigned full = 0xffffffffu;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t epg = E / G;
+    float gs[8];  // scores of groups lane + 32 m
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        const uint32_t g = lane + 32 * m;
+        float b0 = 0.0f, b1 = 0.0f;
+        if (g < G) {
+            for (uint32_t e = g * epg; e < (g + 1) * epg; ++e) {
+                const float v = p[e];
+                if (v > b0) {
+                    b1 = b0;
+                    b0 = v;
+                } else if (v > b1) {
+                    b1 = v;
+                }
+            }
+        }
+        gs[m] = epg > 1 ? __fadd_rn(b0, b1) : b0;
+    }
+    uint32_t kept = 0;  // bit m: group lane + 32 m kept
+    for (uint32_t j = 0; j < TG; ++j) {
+        float best = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const uint32_t g = lane + 32 * m;
+            if (g < G && !((kept >> m) & 1u) && (bi == 0x7fffffff || gs[m] > best)) {
+                best = gs[m];
+                bi = (int)g;
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(full, best, o);
+            const int oi = __shfl_xor_sync(full, bi, o);
+            if (oi != 0x7fffffff && (bi == 0x7fffffff || ob > best || (ob == best && oi < bi))) {
+                best = ob;
+                bi = oi;
+            }
+        }
+        if ((uint32_t)(bi & 31) == lane) kept |= 1u << (bi >> 5);
+    }
+    __syncwarp();
+    for (uint32_t r = 0; r < (E + 31) / 32; ++r) {
+        const uint32_t e = lane + 32 * r;
+        const uint32_t g = (e < E ? e : 0) / epg;
+        const uint32_t owner_bits = __shfl_sync(full, kept, g & 31);
+        if (e < E && !((owner_bits >> (g >> 5)) & 1u)) p[e] = 0.0f;
+    }
+    __syncwarp();
+}
+
+__device__ void topk_token(float* p, uint32_t t, uint32_t E, uint32_t K, const RouteCfg& rc,
+                           int32_t* __restrict__ ids, float* __restrict__ wout, float* __restrict__ scores_out) {
+    const int sigmoid = rc.sigmoid, norm_topk = rc.norm_topk;
+    const float routed_scale = rc.routed_scale;
     const int lane = threadIdx.x & 31;
     if (sigmoid) {
         for (uint32_t e = lane; e < E; e += 32) {
@@ -351,6 +414,7 @@ __device__ void topk_token(float* p, uint32_t t, uint32_t E, uint32_t K, int sig
             p[e] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
         }
         __syncwarp();
+        if (rc.n_group) group_limit_warp(p, E, rc.n_group, rc.topk_group);
     } else {
         float mx = -INFINITY;
         for (uint32_t e = lane; e < E; e += 32) mx = fmaxf(mx, p[e]);
@@ -424,9 +488,10 @@ __device__ void topk_token(float* p, uint32_t t, uint32_t E, uint32_t K, int sig
 // Requires K <= 32.
 // ---------------------------------------------------------------------------
 template <int EPL>
-__device__ void topk_token_reg(const float* lg, uint32_t t, uint32_t E, uint32_t K, int sigmoid, int norm_topk,
-                               float routed_scale, int32_t* __restrict__ ids, float* __restrict__ wout,
-                               float* __restrict__ scores_out) {
+__device__ void topk_token_reg(float* lg, uint32_t t, uint32_t E, uint32_t K, const RouteCfg& rc,
+                               int32_t* __restrict__ ids, float* __restrict__ wout, float* __restrict__ scores_out) {
+    const int sigmoid = rc.sigmoid, norm_topk = rc.norm_topk;
+    const float routed_scale = rc.routed_scale;
     const uint32_t lane = threadIdx.x & 31;
     const unsigned full = 0xffffffffu;
     float v[EPL];
@@ -440,6 +505,16 @@ __device__ void topk_token_reg(const float* lg, uint32_t t, uint32_t E, uint32_t
         for (int q = 0; q < EPL; ++q) {
             const float ex = libm_expf(-v[q]);
             v[q] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+        }
+        if (rc.n_group) {  // through the token's shared-memory row
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < EPL; ++q)
+                if (lane + 32 * q < E) lg[lane + 32 * q] = v[q];
+            __syncwarp();
+            group_limit_warp(lg, E, rc.n_group, rc.topk_group);
+#pragma unroll
+            for (int q = 0; q < EPL; ++q) v[q] = lane + 32 * q < E ? lg[lane + 32 * q] : 0.f;
         }
     } else {
         float mx = -INFINITY;
@@ -511,7 +586,7 @@ __device__ void topk_token_reg(const float* lg, uint32_t t, uint32_t E, uint32_t
 
 // Top-k over logits in global memory: one warp per token.
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, uint32_t T, uint32_t E,
-                                                          uint32_t K, int sigmoid, int norm_topk, float routed_scale,
+                                                          uint32_t K, RouteCfg rc,
                                                           int32_t* __restrict__ ids, float* __restrict__ wout,
                                                           float* __restrict__ scores_out) {
     __shared__ float ps[8][kMaxExperts];
@@ -521,15 +596,15 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     for (uint32_t e = lane; e < E; e += 32) ps[warp][e] = logits[(uint64_t)t * E + e];
     __syncwarp();
     if (K <= 32 && E <= 32) {
-        topk_token_reg<1>(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+        topk_token_reg<1>(ps[warp], t, E, K, rc, ids, wout, scores_out);
     } else if (K <= 32 && E <= 64) {
-        topk_token_reg<2>(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+        topk_token_reg<2>(ps[warp], t, E, K, rc, ids, wout, scores_out);
     } else if (K <= 32 && E <= 128) {
-        topk_token_reg<4>(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+        topk_token_reg<4>(ps[warp], t, E, K, rc, ids, wout, scores_out);
     } else if (K <= 32 && E <= 256) {
-        topk_token_reg<8>(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+        topk_token_reg<8>(ps[warp], t, E, K, rc, ids, wout, scores_out);
     } else {
-        topk_token(ps[warp], t, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores_out);
+        topk_token(ps[warp], t, E, K, rc, ids, wout, scores_out);
     }
 }
 
@@ -549,8 +624,7 @@ constexpr uint32_t kRfSmemMax = 200 * 1024;
 
 __global__ void __launch_bounds__(512) router_fused_kernel(const uint16_t* __restrict__ x,
                                                            const uint16_t* __restrict__ w, uint32_t T, uint32_t E,
-                                                           uint32_t H, uint32_t K, uint32_t tb, int sigmoid,
-                                                           int norm_topk, float routed_scale,
+                                                           uint32_t H, uint32_t K, uint32_t tb, RouteCfg rc,
                                                            float* __restrict__ logits, int32_t* __restrict__ ids,
                                                            float* __restrict__ wout, float* __restrict__ scores,
                                                            uint32_t* __restrict__ err) {
@@ -630,13 +704,11 @@ __global__ void __launch_bounds__(512) router_fused_kernel(const uint16_t* __res
     __syncthreads();
     for (uint32_t tt = warp; tt < nt; tt += 16) {
         if (E <= 32 && K <= 32) {
-            topk_token_reg<1>(lg + (size_t)tt * E, t0 + tt, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
-                              scores);
+            topk_token_reg<1>(lg + (size_t)tt * E, t0 + tt, E, K, rc, ids, wout, scores);
         } else if (K <= 32) {
-            topk_token_reg<2>(lg + (size_t)tt * E, t0 + tt, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
-                              scores);
+            topk_token_reg<2>(lg + (size_t)tt * E, t0 + tt, E, K, rc, ids, wout, scores);
         } else {
-            topk_token(lg + (size_t)tt * E, t0 + tt, E, K, sigmoid, norm_topk, routed_scale, ids, wout, scores);
+            topk_token(lg + (size_t)tt * E, t0 + tt, E, K, rc, ids, wout, scores);
         }
     }
 }
@@ -1043,10 +1115,15 @@ bool router_wants_tma(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t
 }
 
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
-                          int sigmoid, int norm_topk, float routed_scale, float* logits, int32_t* ids, float* wout,
-                          float* scores, uint32_t* err, cudaStream_t st, uint32_t* launches,
-                          const CUtensorMap* tmap_x, const CUtensorMap* tmap_w) {
+                          const RouteCfg& rc_in, float* logits, int32_t* ids, float* wout, float* scores,
+                          uint32_t* err, cudaStream_t st, uint32_t* launches, const CUtensorMap* tmap_x,
+                          const CUtensorMap* tmap_w) {
     if (T == 0) return cudaSuccess;
+    RouteCfg rc = rc_in;
+    // the group limit applies under the reference's conditions only
+    if (!(rc.sigmoid && rc.n_group > 1 && rc.topk_group > 0 && rc.topk_group < rc.n_group && E % rc.n_group == 0))
+        rc.n_group = rc.topk_group = 0;
+    if (rc.n_group > 256) return cudaErrorInvalidValue;
     const uint32_t tb = router_fused_tb(x, w, T, E, H);
     if (tb) {
         static uint64_t attr_set = 0;  // one bit per device
@@ -1059,8 +1136,8 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
             attr_set |= 1ull << dev;
         }
         const size_t smem = (size_t)(tb + E) * (H * 2 + 32) + (size_t)tb * E * 4;
-        router_fused_kernel<<<ceil_div(T, tb), 512, smem, st>>>(x, w, T, E, H, K, tb, sigmoid, norm_topk,
-                                                               routed_scale, logits, ids, wout, scores, err);
+        router_fused_kernel<<<ceil_div(T, tb), 512, smem, st>>>(x, w, T, E, H, K, tb, rc, logits, ids, wout,
+                                                               scores, err);
         if (launches) *launches += 1;
         return cudaGetLastError();
     }
@@ -1083,8 +1160,7 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
                                                                          err);
     else
         router_logits_kernel<<<g1, 256, kRtSmem, st>>>(x, w, T, E, H, logits);
-    router_topk_kernel<<<ceil_div(T, 8), 256, 0, st>>>(logits, T, E, K, sigmoid, norm_topk, routed_scale, ids, wout,
-                                                       scores);
+    router_topk_kernel<<<ceil_div(T, 8), 256, 0, st>>>(logits, T, E, K, rc, ids, wout, scores);
     if (launches) *launches += 2;
     return cudaGetLastError();
 }

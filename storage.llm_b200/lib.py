@@ -34,7 +34,7 @@ class LayerCfg(C.Structure):
     _fields_ = [("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("experts", C.c_uint32),
                 ("top_k", C.c_uint32), ("layer", C.c_int32), ("score_func", C.c_int32),
                 ("norm_topk", C.c_int32), ("routed_scale", C.c_float), ("use_shared", C.c_int32),
-                ("gemm_path", C.c_int32)]
+                ("gemm_path", C.c_int32), ("n_group", C.c_uint32), ("topk_group", C.c_uint32)]
 
 
 class Assignment(C.Structure):
@@ -181,11 +181,12 @@ class Engine:
 
     @staticmethod
     def cfg(shape, layer: int = 0, gemm_path: int = GEMM_TCGEN05, score_func: int = SCORE_SOFTMAX,
-            norm_topk: Optional[bool] = None, routed_scale: float = 1.0, use_shared: Optional[bool] = None):
+            norm_topk: Optional[bool] = None, routed_scale: float = 1.0, use_shared: Optional[bool] = None,
+            n_group: int = 0, topk_group: int = 0):
         nt = shape.norm_topk if norm_topk is None else norm_topk
         us = shape.shared if use_shared is None else use_shared
         return LayerCfg(shape.hidden, shape.intermediate, shape.experts, shape.top_k, layer, score_func, int(nt),
-                        routed_scale, int(us), gemm_path)
+                        routed_scale, int(us), gemm_path, n_group, topk_group)
 
     # -- forward ----------------------------------------------------------
     def forward(self, cfg: LayerCfg, x, tokens: int, y_bf16=None, y_f32=None, ids=None, w=None, perm=None,

@@ -6,7 +6,7 @@ oracle/_ref/libmoe_ref.so by oracle/Makefile) on seeded synthetic inputs and
 recording its outputs here.  Run it in a checkout that has the reference
 sources (MOE_REFERENCE_ROOT, default /root/reference):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [name-prefix]
 
 Small cases store every input; full-size cases store the seed and a sha256 of
 the regenerated inputs, so a test can prove it regenerated the same bytes.
@@ -80,6 +80,30 @@ def sigmoid_case():
     print("router_sigmoid")
 
 
+# name -> (experts, n_group, topk_group, top_k, seed): DeepSeek-style group
+# limits (generation_router.cpp.inc:484-558), one with a single expert per
+# group
+GROUP_LIMIT_CASES = {
+    "router_group_limit": (32, 8, 3, 4, 13),
+    "router_group_limit_e1": (16, 16, 5, 3, 14),
+}
+
+
+def group_limit_case(name, experts, n_group, topk_group, top_k, seed):
+    shape = synth.small_shape(name=name, top_k=top_k, experts=experts, tokens=40)
+    li = synth.make_layer(shape, seed=seed)
+    ref = oracle.Ref(oracle.metadata_json(top_k, norm_topk=True, sigmoid=True, routed_scale=2.5,
+                                          n_group=n_group, topk_group=topk_group))
+    try:
+        ids, w, scores = ref.router_topk(li)
+    finally:
+        ref.close()
+    np.savez_compressed(OUT / f"{name}.npz", router=li.router, x=li.x, ids=ids, w=w, scores=scores,
+                        hidden=shape.hidden, experts=experts, top_k=top_k, norm_topk=1, routed_scale=2.5,
+                        n_group=n_group, topk_group=topk_group)
+    print(name)
+
+
 def grouping_case():
     rng = np.random.default_rng(11)
     n = 300
@@ -115,15 +139,24 @@ def decode_tables():
     print("decode_tables")
 
 
-def main():
+def main(only=None):
+    """Writes every fixture, or only those whose name starts with `only`."""
     if not oracle.REF_SO.exists():
         oracle.build(ref=True)
-    decode_tables()
-    grouping_case()
-    sigmoid_case()
+    want = (lambda n: only is None or n.startswith(only))
+    if want("decode_tables"):
+        decode_tables()
+    if want("grouping"):
+        grouping_case()
+    if want("router_sigmoid"):
+        sigmoid_case()
+    for name, args in GROUP_LIMIT_CASES.items():
+        if want(name):
+            group_limit_case(name, *args)
     for name, (shape, seed, tokens, store) in LAYER_CASES.items():
-        layer_case(name, shape, seed, tokens, store)
+        if want("layer_" + name):
+            layer_case(name, shape, seed, tokens, store)
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1] if len(sys.argv) > 1 else None)

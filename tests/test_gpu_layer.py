@@ -225,3 +225,30 @@ def test_tiled_router_matches_oracle(engine, synth, L, port, tokens, experts, hi
     assert np.array_equal(bits(scores), bits(scores_ref))
     assert np.array_equal(ids.cpu().numpy(), ids_ref)
     assert np.array_equal(bits(w.cpu().numpy()), bits(w_ref))
+
+
+@pytest.mark.parametrize("tokens,experts,n_group,topk_group,top_k", [
+    (24, 32, 8, 3, 4),      # single-kernel router, one register slot per lane
+    (40, 64, 8, 2, 6),      # single-kernel router, two slots
+    (64, 32, 32, 5, 3),     # one expert per group
+    (700, 128, 8, 4, 8),    # tiled router, register top-k
+    (300, 256, 8, 4, 8),    # tiled router, 256 experts in 8 groups
+    (100, 320, 10, 4, 8),   # tiled router, top-k past 256 experts
+], ids=["fused_e32", "fused_e64", "one_per_group", "tiled_e128", "tiled_e256", "tiled_e320"])
+def test_group_limited_router_matches_oracle(engine, synth, L, port, tokens, experts, n_group, topk_group, top_k):
+    """Sigmoid routing with the group limit (generation_router.cpp.inc:484-558):
+    the limited scores, ids and weights are bit-identical to the oracle's,
+    which is pinned to the compiled reference by the group-limit fixtures."""
+    shape = synth.small_shape(hidden=128, intermediate=64, experts=experts, top_k=top_k, tokens=tokens)
+    li = synth.make_layer(shape, seed=31 + tokens + experts)
+    engine.upload_layer(li)
+    cfg = L.Engine.cfg(shape, score_func=L.SCORE_SIGMOID, norm_topk=True, routed_scale=2.5, n_group=n_group,
+                       topk_group=topk_group)
+    out = engine.forward_host(cfg, li.x)
+    ids_ref, w_ref, scores_ref, ties = port.router_topk(li, score_sigmoid=1, norm_topk=1, routed_scale=2.5,
+                                                        n_group=n_group, topk_group=topk_group)
+    assert ties == 0
+    scores = engine.read(L.BUF_SCORES, (tokens, experts), np.float32)
+    assert np.array_equal(bits(scores), bits(scores_ref))
+    assert np.array_equal(out["ids"], ids_ref)
+    assert np.array_equal(bits(out["w"]), bits(w_ref))

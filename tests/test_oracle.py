@@ -57,6 +57,23 @@ def test_sigmoid_router_fixture(port, synth):
     assert np.array_equal(bits(scores), bits(g["scores"]))
 
 
+@pytest.mark.parametrize("name", ["router_group_limit.npz", "router_group_limit_e1.npz"])
+def test_group_limit_router_fixture(port, synth, name):
+    """Sigmoid router with a DeepSeek-style group limit, against the compiled
+    reference's own output (generation_router.cpp.inc:484-558)."""
+    g = golden(name)
+    shape = synth.small_shape(top_k=int(g["top_k"]), experts=int(g["experts"]), hidden=int(g["hidden"]),
+                              tokens=g["x"].shape[0])
+    li = synth.LayerInputs(shape, g["router"], None, None, None, g["x"])
+    ids, w, scores, ties = port.router_topk(li, score_sigmoid=1, norm_topk=int(g["norm_topk"]),
+                                            routed_scale=float(g["routed_scale"]), n_group=int(g["n_group"]),
+                                            topk_group=int(g["topk_group"]))
+    assert ties == 0
+    assert np.array_equal(bits(scores), bits(g["scores"]))
+    assert np.array_equal(ids, g["ids"])
+    assert np.array_equal(bits(w), bits(g["w"]))
+
+
 def test_grouping_fixture(port):
     g = golden("grouping.npz")
     ok, out, batches, cnt = port.group_tokens(g["token"], g["expert"], g["score"], g["layer"])
