@@ -97,9 +97,8 @@ __device__ __forceinline__ float warp_max_abs(float v) {
 // maps into [128, 256) of E4M3's range (no overflow; E4M3 keeps 4 significant
 // bits anywhere in its normal range, so the exact choice costs no precision).
 __device__ __forceinline__ int block_exp(float amax) {
-    if (!(amax > 0.f)) return -127;
     const int e = (int)((__float_as_uint(amax) >> 23) & 0xFF) - 127 - 7;
-    return e < -127 ? -127 : (e > 127 ? 127 : e);
+    return amax > 0.f ? max(-127, min(127, e)) : -127;
 }
 
 // Round-to-nearest-even of y (|y| < 448) to E4M3: returns the code byte and
@@ -108,23 +107,20 @@ __device__ __forceinline__ int block_exp(float amax) {
 // correct next binade).  Subnormal range: multiples of 2^-9, rounded by adding
 // and subtracting 1.5 * 2^14 (whose fp32 ulp is 2^-9); the multiple m = 0..8 is
 // the code (m = 8 is 2^-6, code 0x08, the smallest normal).  Pure integer and
-// fp32 add/multiply arithmetic: no conversion instruction.
+// fp32 add/multiply arithmetic: no conversion instruction.  Both ranges are
+// computed and one is selected, so the code has no per-lane branch.
 __device__ __forceinline__ uint32_t e4m3_rne(float y, float& q) {
     const uint32_t sign = __float_as_uint(y) & 0x80000000u;
     const float ay = fabsf(y);
-    uint32_t code;
-    if (ay >= 0.015625f) {
-        uint32_t b = __float_as_uint(ay);
-        b = (b + 0x7FFFFu + ((b >> 20) & 1u)) & 0xFFF00000u;
-        q = __uint_as_float(b);
-        code = ((((b >> 23) - 120u) << 3) | ((b >> 20) & 7u));
-    } else {
-        const float t = __fadd_rn(ay, 24576.0f);  // 24576 = 0x46C00000; t = 24576 + m * 2^-9
-        q = __fsub_rn(t, 24576.0f);
-        code = __float_as_uint(t) - 0x46C00000u;
-    }
-    q = __uint_as_float(__float_as_uint(q) | sign);
-    return code | (sign >> 24);
+    uint32_t b = __float_as_uint(ay);
+    b = (b + 0x7FFFFu + ((b >> 20) & 1u)) & 0xFFF00000u;
+    const uint32_t code_n = ((((b >> 23) - 120u) << 3) | ((b >> 20) & 7u));
+    const float t = __fadd_rn(ay, 24576.0f);  // 24576 = 0x46C00000; t = 24576 + m * 2^-9
+    const float q_s = __fsub_rn(t, 24576.0f);
+    const uint32_t code_s = __float_as_uint(t) - 0x46C00000u;
+    const bool normal = ay >= 0.015625f;
+    q = __uint_as_float((normal ? b : __float_as_uint(q_s)) | sign);
+    return (normal ? code_n : code_s) | (sign >> 24);
 }
 
 // Splits the 32 values held by a warp (one per lane, one 32-element K block)
@@ -377,6 +373,48 @@ cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, co
 
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
+// Gate/up epilogue for 8 token columns of one row m: SiLU(gate) * up, split
+// into hi/lo E4M3 with the down GEMM's block scales, stored.  The 8 chains
+// are independent and the code is branch-free (columns at or past nn are
+// computed; their stores are predicated off, and lane j stores column j's
+// scale bytes), so the latencies overlap and no per-column divergence
+// handling is needed.
+template <int BN>
+__device__ __forceinline__ void gu_store8(const float* g, const float* u, uint32_t c0, uint32_t nn, uint64_t row0,
+                                          uint32_t m, uint32_t lane, uint32_t quarter, const BsParams& p,
+                                          uint8_t* h_atom) {
+    uint8_t hi[8], lo[8], sh[8], sl[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) split_e4m3_warp(silu_fast(g[j]) * u[j], hi[j], lo[j], sh[j], sl[j]);
+    uint8_t* hp = p.h_out + (row0 + c0) * p.h_stride + m;
+    uint8_t* lp = hp + p.h_plane;
+    if (c0 + 8 <= nn) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            hp[(uint64_t)j * p.h_stride] = hi[j];
+            lp[(uint64_t)j * p.h_stride] = lo[j];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (c0 + j < nn) {
+                hp[(uint64_t)j * p.h_stride] = hi[j];
+                lp[(uint64_t)j * p.h_stride] = lo[j];
+            }
+        }
+    }
+    uint8_t s_h = sh[0], s_l = sl[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) {
+        s_h = lane == (uint32_t)j ? sh[j] : s_h;
+        s_l = lane == (uint32_t)j ? sl[j] : s_l;
+    }
+    if (lane < 8 && c0 + lane < nn) {
+        h_atom[sfb_pos_hi<BN>(c0 + lane) + quarter] = s_h;
+        h_atom[sfb_pos_lo<BN>(c0 + lane) + quarter] = s_l;
+    }
+}
+
 template <int MODE, int BN>
 __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                          const __grid_constant__ CUtensorMap tmap_b,
@@ -625,18 +663,9 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 tc_fence_before();
                 mbar_arrive(&acc_empty[acc]);
 #pragma unroll
-                for (uint32_t col = 0; col < (uint32_t)BN; ++col) {
-                    if (col >= tc.nn) break;  // uniform across the warp
-                    const float hv = silu_fast(g[col]) * u[col];
-                    uint8_t hi, lo, sh, sl;
-                    split_e4m3_warp(hv, hi, lo, sh, sl);
-                    const uint64_t prow = row0 + col;
-                    p.h_out[prow * p.h_stride + m] = hi;
-                    p.h_out[p.h_plane + prow * p.h_stride + m] = lo;
-                    if (lane == 0) {
-                        h_atom[sfb_pos_hi<BN>(col) + quarter] = sh;
-                        h_atom[sfb_pos_lo<BN>(col) + quarter] = sl;
-                    }
+                for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 8) {
+                    if (c0 >= tc.nn) break;  // uniform across the warp
+                    gu_store8<BN>(g + c0, u + c0, c0, tc.nn, row0, m, lane, quarter, p, h_atom);
                 }
                 if (++acc == C::kAccs) {
                     acc = 0;
@@ -644,68 +673,78 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 }
                 continue;
             }
-            for (uint32_t c0 = 0; c0 < tc.nn; c0 += 16) {
-                float v0[16], v1[16];
-                {
-                    uint32_t a[16], b[16];
+            if (MODE == kGateUp) {
+                for (uint32_t c0 = 0; c0 < tc.nn; c0 += 16) {
+                    uint32_t a[16], b[16], c[16], d[16];
                     MOE_TMEM_LD16(dbase + c0, a);
-                    if (C::kStackN) MOE_TMEM_LD16(dbase + kLoOff + c0, b);
+                    MOE_TMEM_LD16(dbase + kProjOff + c0, c);
+                    if (C::kStackN) {
+                        MOE_TMEM_LD16(dbase + kLoOff + c0, b);
+                        MOE_TMEM_LD16(dbase + kProjOff + kLoOff + c0, d);
+                    }
                     tmem_wait_ld();
+                    float v0[16], v1[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         v0[i] = __uint_as_float(a[i]) + (C::kStackN ? __uint_as_float(b[i]) : 0.f);
+                        v1[i] = __uint_as_float(c[i]) + (C::kStackN ? __uint_as_float(d[i]) : 0.f);
                     }
+                    gu_store8<BN>(v0, v1, c0, tc.nn, row0, m, lane, quarter, p, h_atom);
+                    if (c0 + 8 < tc.nn) gu_store8<BN>(v0 + 8, v1 + 8, c0 + 8, tc.nn, row0, m, lane, quarter, p, h_atom);
                 }
-                if (MODE == kGateUp) {
-                    uint32_t a[16], b[16];
-                    MOE_TMEM_LD16(dbase + kProjOff + c0, a);
-                    if (C::kStackN) MOE_TMEM_LD16(dbase + kProjOff + kLoOff + c0, b);
+            } else {
+                // 32 token columns per round: all TMEM loads, one wait, the stores
+                for (uint32_t c0 = 0; c0 < tc.nn; c0 += 32) {
+                    uint32_t a0[16], a1[16], b0[16], b1[16];
+                    MOE_TMEM_LD16(dbase + c0, a0);
+                    MOE_TMEM_LD16(dbase + c0 + 16, a1);
+                    if (C::kStackN) {
+                        MOE_TMEM_LD16(dbase + kLoOff + c0, b0);
+                        MOE_TMEM_LD16(dbase + kLoOff + c0 + 16, b1);
+                    }
                     tmem_wait_ld();
+                    float v0[32];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        v1[i] = __uint_as_float(a[i]) + (C::kStackN ? __uint_as_float(b[i]) : 0.f);
+                        v0[i] = __uint_as_float(a0[i]) + (C::kStackN ? __uint_as_float(b0[i]) : 0.f);
+                        v0[16 + i] = __uint_as_float(a1[i]) + (C::kStackN ? __uint_as_float(b1[i]) : 0.f);
                     }
+                    if (!p.ret_ptrs && !p.y_row_map) {
+                        // permuted rows in order: straight-line stores (the tail
+                        // chunk's are predicated)
+                        float* yp = p.y_out + (row0 + c0) * p.y_stride + m;
+                        if (m < p.m_valid) {
+                            if (c0 + 32 <= tc.nn) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const uint32_t col = c0 + i;
-                        if (col >= tc.nn) continue;  // uniform across the warp
-                        const float hv = silu_fast(v0[i]) * v1[i];
-                        uint8_t hi, lo, sh, sl;
-                        split_e4m3_warp(hv, hi, lo, sh, sl);
-                        const uint64_t prow = row0 + col;
-                        p.h_out[prow * p.h_stride + m] = hi;
-                        p.h_out[p.h_plane + prow * p.h_stride + m] = lo;
-                        if (lane == 0) {
-                            h_atom[sfb_pos_hi<BN>(col) + quarter] = sh;
-                            h_atom[sfb_pos_lo<BN>(col) + quarter] = sl;
-                        }
-                    }
-                } else if (m < p.m_valid) {
-                    if (!p.ret_ptrs) {
+                                for (int i = 0; i < 32; ++i) yp[(uint64_t)i * p.y_stride] = v0[i];
+                            } else {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            if (c0 + i < tc.nn) {
-                                const uint64_t prow = row0 + c0 + i;
-                                const uint64_t orow = p.y_row_map ? __ldg(p.y_row_map + prow) : prow;
-                                p.y_out[orow * p.y_stride + m] = v0[i];
+                                for (int i = 0; i < 32; ++i)
+                                    if (c0 + i < tc.nn) yp[(uint64_t)i * p.y_stride] = v0[i];
                             }
                         }
                     } else {
-                        // expert parallelism: another rank's token goes into its
-                        // return buffer over NVLink
-                        for (int i = 0; i < 16; ++i) {
-                            if (c0 + i < tc.nn) {
-                                const uint64_t prow = row0 + c0 + i;
-                                const uint64_t orow = p.y_row_map ? __ldg(p.y_row_map + prow) : prow;
-                                float* dst = p.y_out + orow * p.y_stride;
-                                if (orow < p.ret_rows) {
-                                    uint32_t r = 0;
-                                    while (r + 1 < p.ret_world && __ldg(p.ret_roff + r + 1) <= orow) ++r;
-                                    dst = p.ret_ptrs[r] +
-                                          ((uint64_t)__ldg(p.ret_base + r) + orow - __ldg(p.ret_roff + r)) * p.y_stride;
-                                }
-                                dst[m] = v0[i];
+                        // rows by source token (and, with expert parallelism,
+                        // other ranks' rows into their return buffers over
+                        // NVLink): lane i resolves the destination row of chunk
+                        // column i once, the pointers are shuffled out
+                        uint64_t my_dst = 0;
+                        if (c0 + lane < tc.nn) {
+                            const uint64_t prow = row0 + c0 + lane;
+                            const uint64_t orow = p.y_row_map ? __ldg(p.y_row_map + prow) : prow;
+                            float* dst = p.y_out + orow * p.y_stride;
+                            if (p.ret_ptrs && orow < p.ret_rows) {
+                                uint32_t r = 0;
+                                while (r + 1 < p.ret_world && __ldg(p.ret_roff + r + 1) <= orow) ++r;
+                                dst = p.ret_ptrs[r] +
+                                      ((uint64_t)__ldg(p.ret_base + r) + orow - __ldg(p.ret_roff + r)) * p.y_stride;
                             }
+                            my_dst = reinterpret_cast<uint64_t>(dst);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            float* dst = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, my_dst, i));
+                            if (m < p.m_valid && c0 + i < tc.nn) dst[m] = v0[i];
                         }
                     }
                 }
