@@ -373,19 +373,39 @@ cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, co
 
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-// Gate/up epilogue for 8 token columns of one row m: SiLU(gate) * up, split
-// into hi/lo E4M3 with the down GEMM's block scales, stored.  The 8 chains
+// Gate/up epilogue for 8 token columns of one row m: h = SiLU(gate) * up,
+// split into hi/lo E4M3 with the down GEMM's block scales, stored.  The 8 chains
 // are independent and the code is branch-free (columns at or past nn are
 // computed; their stores are predicated off, and lane j stores column j's
 // scale bytes), so the latencies overlap and no per-column divergence
 // handling is needed.
 template <int BN>
-__device__ __forceinline__ void gu_store8(const float* g, const float* u, uint32_t c0, uint32_t nn, uint64_t row0,
-                                          uint32_t m, uint32_t lane, uint32_t quarter, const BsParams& p,
-                                          uint8_t* h_atom) {
+__device__ __forceinline__ void h_store8(const float* hv, uint32_t c0, uint32_t nn, uint64_t row0, uint32_t m,
+                                         uint32_t lane, uint32_t quarter, const BsParams& p, uint8_t* h_atom) {
+    // split_e4m3_warp for the 8 values, written phase by phase (all block
+    // maxima of a phase back to back) so the independent chains overlap
+    // around the warp reductions
     uint8_t hi[8], lo[8], sh[8], sl[8];
+    float mx[8], r[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) split_e4m3_warp(silu_fast(g[j]) * u[j], hi[j], lo[j], sh[j], sl[j]);
+    for (int j = 0; j < 8; ++j) mx[j] = warp_max_abs(hv[j]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int e1 = block_exp(mx[j]);
+        float qh;
+        hi[j] = (uint8_t)e4m3_rne(hv[j] * pow2f(-e1), qh);
+        r[j] = hv[j] - qh * pow2f(e1);
+        sh[j] = (uint8_t)(e1 + 127);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mx[j] = warp_max_abs(r[j]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int e2 = block_exp(mx[j]);
+        float ql;
+        lo[j] = (uint8_t)e4m3_rne(r[j] * pow2f(-e2), ql);
+        sl[j] = (uint8_t)(e2 + 127);
+    }
     uint8_t* hp = p.h_out + (row0 + c0) * p.h_stride + m;
     uint8_t* lp = hp + p.h_plane;
     if (c0 + 8 <= nn) {
@@ -415,11 +435,85 @@ __device__ __forceinline__ void gu_store8(const float* g, const float* u, uint32
     }
 }
 
+template <int BN>
+__device__ __forceinline__ void gu_store8(const float* g, const float* u, uint32_t c0, uint32_t nn, uint64_t row0,
+                                          uint32_t m, uint32_t lane, uint32_t quarter, const BsParams& p,
+                                          uint8_t* h_atom) {
+    float hv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hv[j] = silu_fast(g[j]) * u[j];
+    h_store8<BN>(hv, c0, nn, row0, m, lane, quarter, p, h_atom);
+}
+
+// One warp group's share [cb, cb + W) of a gate/up tile's token columns (the
+// group's four warps cover the 128 TMEM lanes): drain, release the group's
+// share of the accumulator, then SiLU * up, the hi/lo split and the stores.
+// Stacked tiles drain into registers first, so the release comes before the
+// math and the next tile's MMAs overlap it.
+template <int BN, int W>
+__device__ __forceinline__ void gu_tile_part(const BsParams& p, const BsTileX& tc, uint32_t dbase, uint32_t cb,
+                                             uint32_t m, uint32_t lane, uint32_t quarter, uint8_t* h_atom,
+                                             uint64_t* acc_empty_bar) {
+    constexpr bool kStackN = BN <= 64;
+    constexpr uint32_t kLoOff = kStackN ? BN : 0;  // stacked: lo half follows hi
+    constexpr uint32_t kProjOff = kStackN ? 2 * BN : BN;
+    if constexpr (kStackN) {
+        float g[W], u[W];
+#pragma unroll
+        for (uint32_t j0 = 0; j0 < (uint32_t)W; j0 += 16) {
+            const uint32_t c0 = cb + j0;
+            if (c0 < tc.nn) {  // uniform across the warp
+                uint32_t a[16], b[16], c[16], d[16];
+                MOE_TMEM_LD16(dbase + c0, a);
+                MOE_TMEM_LD16(dbase + kLoOff + c0, b);
+                MOE_TMEM_LD16(dbase + kProjOff + c0, c);
+                MOE_TMEM_LD16(dbase + kProjOff + kLoOff + c0, d);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    g[j0 + i] = __uint_as_float(a[i]) + __uint_as_float(b[i]);
+                    u[j0 + i] = __uint_as_float(c[i]) + __uint_as_float(d[i]);
+                }
+            }
+        }
+        tc_fence_before();
+        mbar_arrive(acc_empty_bar);
+#pragma unroll
+        for (uint32_t j0 = 0; j0 < (uint32_t)W; j0 += 8) {
+            const uint32_t c0 = cb + j0;
+            if (c0 >= tc.nn) break;  // uniform across the warp
+            gu_store8<BN>(g + j0, u + j0, c0, tc.nn, tc.row0, m, lane, quarter, p, h_atom);
+        }
+    } else {
+        for (uint32_t c0 = cb; c0 < cb + W && c0 < tc.nn; c0 += 16) {
+            uint32_t a[16], c[16];
+            MOE_TMEM_LD16(dbase + c0, a);
+            MOE_TMEM_LD16(dbase + kProjOff + c0, c);
+            tmem_wait_ld();
+            float v0[16], v1[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                v0[i] = __uint_as_float(a[i]);
+                v1[i] = __uint_as_float(c[i]);
+            }
+            gu_store8<BN>(v0, v1, c0, tc.nn, tc.row0, m, lane, quarter, p, h_atom);
+            if (c0 + 8 < tc.nn) gu_store8<BN>(v0 + 8, v1 + 8, c0 + 8, tc.nn, tc.row0, m, lane, quarter, p, h_atom);
+        }
+        tc_fence_before();
+        mbar_arrive(acc_empty_bar);
+    }
+}
+
 template <int MODE, int BN>
 __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                          const __grid_constant__ CUtensorMap tmap_b,
                                                          const BsParams p) {
     using C = BsCfg<MODE, BN>;
+    // gate/up with one accumulator: the scale-factor warps drain and store the
+    // upper half of each tile's columns (the MMAs wait for the whole
+    // accumulator anyway), halving the epilogue's time per tile
+    constexpr bool kGuSplit = MODE == kGateUp && C::kAccs == 1;
+    constexpr int kGuW = kGuSplit ? BN / 2 : BN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     // scale blocks first (small), then the 1024-aligned operand tiles
@@ -444,7 +538,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         }
         for (int i = 0; i < C::kAccs; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 128);
+            mbar_init(&acc_empty[i], kGuSplit ? 256 : 128);
         }
         fence_mbar_init();
     }
@@ -589,7 +683,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         // slot of stage u is free once stage u's operands have landed: the
         // producer reloaded it only after the MMAs of stage u - kStages were done.
         const uint32_t lane_addr = ((warp & 3) * 32) << 16;
-        uint32_t stage = 0, phase = 0;
+        uint32_t stage = 0, phase = 0, eaccphase = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
             for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
@@ -615,6 +709,21 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                     phase ^= 1;
                 }
             }
+            if constexpr (kGuSplit) {
+                if (!ok) break;
+                const BsTileX tc = load_tile(p, tile);
+                ok = mbar_wait(&acc_full[0], eaccphase, p.err, kErrTimeoutAccFull, true);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t quarter = warp & 3;
+                uint8_t* h_atom = p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * C::kSFB;
+                gu_tile_part<BN, kGuW>(p, tc, tmem + lane_addr, BN / 2, tc.mt * 128 + quarter * 32 + lane, lane,
+                                       quarter, h_atom, &acc_empty[0]);
+                eaccphase ^= 1;
+            }
         }
     } else {
         // ------------------------------------------------------------ epilogue
@@ -639,60 +748,15 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 MODE == kGateUp ? p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * C::kSFB : nullptr;
             constexpr uint32_t kLoOff = C::kStackN ? BN : 0;        // stacked: lo half follows hi
             constexpr uint32_t kProjOff = C::kStackN ? 2 * BN : BN;
-            if (MODE == kGateUp && C::kStackN) {
-                // Drain gate and up (hi + lo halves summed) into registers and
-                // release the accumulator before the SiLU / hi-lo split, so the
-                // next tile's MMAs overlap this tile's math.
-                float g[BN], u[BN];
-#pragma unroll
-                for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 16) {
-                    if (c0 < tc.nn) {  // uniform across the warp
-                        uint32_t a[16], b[16], c[16], d[16];
-                        MOE_TMEM_LD16(dbase + c0, a);
-                        MOE_TMEM_LD16(dbase + kLoOff + c0, b);
-                        MOE_TMEM_LD16(dbase + kProjOff + c0, c);
-                        MOE_TMEM_LD16(dbase + kProjOff + kLoOff + c0, d);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            g[c0 + i] = __uint_as_float(a[i]) + __uint_as_float(b[i]);
-                            u[c0 + i] = __uint_as_float(c[i]) + __uint_as_float(d[i]);
-                        }
-                    }
-                }
-                tc_fence_before();
-                mbar_arrive(&acc_empty[acc]);
-#pragma unroll
-                for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 8) {
-                    if (c0 >= tc.nn) break;  // uniform across the warp
-                    gu_store8<BN>(g + c0, u + c0, c0, tc.nn, row0, m, lane, quarter, p, h_atom);
-                }
+            if constexpr (MODE == kGateUp) {
+                gu_tile_part<BN, kGuW>(p, tc, dbase, 0, m, lane, quarter, h_atom, &acc_empty[acc]);
                 if (++acc == C::kAccs) {
                     acc = 0;
                     accphase ^= 1;
                 }
                 continue;
             }
-            if (MODE == kGateUp) {
-                for (uint32_t c0 = 0; c0 < tc.nn; c0 += 16) {
-                    uint32_t a[16], b[16], c[16], d[16];
-                    MOE_TMEM_LD16(dbase + c0, a);
-                    MOE_TMEM_LD16(dbase + kProjOff + c0, c);
-                    if (C::kStackN) {
-                        MOE_TMEM_LD16(dbase + kLoOff + c0, b);
-                        MOE_TMEM_LD16(dbase + kProjOff + kLoOff + c0, d);
-                    }
-                    tmem_wait_ld();
-                    float v0[16], v1[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        v0[i] = __uint_as_float(a[i]) + (C::kStackN ? __uint_as_float(b[i]) : 0.f);
-                        v1[i] = __uint_as_float(c[i]) + (C::kStackN ? __uint_as_float(d[i]) : 0.f);
-                    }
-                    gu_store8<BN>(v0, v1, c0, tc.nn, row0, m, lane, quarter, p, h_atom);
-                    if (c0 + 8 < tc.nn) gu_store8<BN>(v0 + 8, v1 + 8, c0 + 8, tc.nn, row0, m, lane, quarter, p, h_atom);
-                }
-            } else {
+            {
                 // 32 token columns per round: all TMEM loads, one wait, the stores
                 for (uint32_t c0 = 0; c0 < tc.nn; c0 += 32) {
                     uint32_t a0[16], a1[16], b0[16], b1[16];
