@@ -101,38 +101,41 @@ __device__ __forceinline__ int block_exp(float amax) {
     return amax > 0.f ? max(-127, min(127, e)) : -127;
 }
 
-// Round-to-nearest-even of y (|y| < 448) to E4M3: returns the code byte and
-// the rounded value.  Normal range (|y| >= 2^-6): keep 3 mantissa bits of the
-// fp32 pattern (RNE on the 20 dropped bits; a carry into the exponent is the
+// The value of round-to-nearest-even of y (|y| < 448) to E4M3 (the code
+// itself comes from the hardware conversion, cvt_e4m3x2, which rounds the
+// same way).  Normal range (|y| >= 2^-6): keep 3 mantissa bits of the fp32
+// pattern (RNE on the 20 dropped bits; a carry into the exponent is the
 // correct next binade).  Subnormal range: multiples of 2^-9, rounded by adding
-// and subtracting 1.5 * 2^14 (whose fp32 ulp is 2^-9); the multiple m = 0..8 is
-// the code (m = 8 is 2^-6, code 0x08, the smallest normal).  Pure integer and
-// fp32 add/multiply arithmetic: no conversion instruction.  Both ranges are
+// and subtracting 1.5 * 2^14 (whose fp32 ulp is 2^-9).  Both ranges are
 // computed and one is selected, so the code has no per-lane branch.
-__device__ __forceinline__ uint32_t e4m3_rne(float y, float& q) {
+__device__ __forceinline__ float e4m3_rne_value(float y) {
     const uint32_t sign = __float_as_uint(y) & 0x80000000u;
     const float ay = fabsf(y);
     uint32_t b = __float_as_uint(ay);
     b = (b + 0x7FFFFu + ((b >> 20) & 1u)) & 0xFFF00000u;
-    const uint32_t code_n = ((((b >> 23) - 120u) << 3) | ((b >> 20) & 7u));
-    const float t = __fadd_rn(ay, 24576.0f);  // 24576 = 0x46C00000; t = 24576 + m * 2^-9
-    const float q_s = __fsub_rn(t, 24576.0f);
-    const uint32_t code_s = __float_as_uint(t) - 0x46C00000u;
-    const bool normal = ay >= 0.015625f;
-    q = __uint_as_float((normal ? b : __float_as_uint(q_s)) | sign);
-    return (normal ? code_n : code_s) | (sign >> 24);
+    const float q_s = __fsub_rn(__fadd_rn(ay, 24576.0f), 24576.0f);
+    return __uint_as_float((ay >= 0.015625f ? b : __float_as_uint(q_s)) | sign);
+}
+
+// Two fp32 values to E4M3 codes by the hardware conversion (round to nearest
+// even, saturating finite; no saturation happens for |y| < 448): the first
+// argument in the low byte.  One conversion per two values; the rounded value
+// a residual needs comes from e4m3_rne_value.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+    uint16_t d;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(hi), "f"(lo));
+    return d;
 }
 
 // Splits the 32 values held by a warp (one per lane, one 32-element K block)
 // into hi + lo E4M3 terms with E8M0 scale bytes.  Warp-collective.
 __device__ __forceinline__ void split_e4m3_warp(float v, uint8_t& hi, uint8_t& lo, uint8_t& s_hi, uint8_t& s_lo) {
     const int e1 = block_exp(warp_max_abs(v));
-    float qh;
-    hi = (uint8_t)e4m3_rne(v * pow2f(-e1), qh);
-    const float r = v - qh * pow2f(e1);
+    const float y = v * pow2f(-e1);
+    hi = (uint8_t)cvt_e4m3x2(y, 0.0f);
+    const float r = v - e4m3_rne_value(y) * pow2f(e1);
     const int e2 = block_exp(warp_max_abs(r));
-    float ql;
-    lo = (uint8_t)e4m3_rne(r * pow2f(-e2), ql);
+    lo = (uint8_t)cvt_e4m3x2(r * pow2f(-e2), 0.0f);
     s_hi = (uint8_t)(e1 + 127);
     s_lo = (uint8_t)(e2 + 127);
 }
@@ -154,23 +157,18 @@ __device__ __forceinline__ void split_e4m3_x4(const float v[4], uint32_t& hi4, u
     float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     const int e1 = block_exp(group_max(m));
     float r[4];
-    hi4 = 0;
     const float inv1 = pow2f(-e1), sc1 = pow2f(e1);
+    float y[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        float q;
-        hi4 |= e4m3_rne(v[i] * inv1, q) << (8 * i);
-        r[i] = v[i] - q * sc1;
+        y[i] = v[i] * inv1;
+        r[i] = v[i] - e4m3_rne_value(y[i]) * sc1;
     }
+    hi4 = cvt_e4m3x2(y[0], y[1]) | (cvt_e4m3x2(y[2], y[3]) << 16);
     m = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
     const int e2 = block_exp(group_max(m));
-    lo4 = 0;
     const float inv2 = pow2f(-e2);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float q;
-        lo4 |= e4m3_rne(r[i] * inv2, q) << (8 * i);
-    }
+    lo4 = cvt_e4m3x2(r[0] * inv2, r[1] * inv2) | (cvt_e4m3x2(r[2] * inv2, r[3] * inv2) << 16);
     s_hi = (uint8_t)(e1 + 127);
     s_lo = (uint8_t)(e2 + 127);
 }
@@ -392,9 +390,9 @@ __device__ __forceinline__ void h_store8(const float* hv, uint32_t c0, uint32_t 
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int e1 = block_exp(mx[j]);
-        float qh;
-        hi[j] = (uint8_t)e4m3_rne(hv[j] * pow2f(-e1), qh);
-        r[j] = hv[j] - qh * pow2f(e1);
+        const float y = hv[j] * pow2f(-e1);
+        hi[j] = (uint8_t)cvt_e4m3x2(y, 0.0f);
+        r[j] = hv[j] - e4m3_rne_value(y) * pow2f(e1);
         sh[j] = (uint8_t)(e1 + 127);
     }
 #pragma unroll
@@ -402,8 +400,7 @@ __device__ __forceinline__ void h_store8(const float* hv, uint32_t c0, uint32_t 
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int e2 = block_exp(mx[j]);
-        float ql;
-        lo[j] = (uint8_t)e4m3_rne(r[j] * pow2f(-e2), ql);
+        lo[j] = (uint8_t)cvt_e4m3x2(r[j] * pow2f(-e2), 0.0f);
         sl[j] = (uint8_t)(e2 + 127);
     }
     uint8_t* hp = p.h_out + (row0 + c0) * p.h_stride + m;
