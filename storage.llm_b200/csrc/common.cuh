@@ -58,6 +58,7 @@ enum : uint32_t {
     kErrTimeoutAccFull = 5,
     kErrTimeoutAccEmpty = 6,
     kErrTimeoutRouterLoad = 7,
+    kErrTimeoutPeer = 8,
     kErrBadExpert = 16,
 };
 

@@ -8,21 +8,29 @@
 //   1. router + top-k on the local tokens (full E);
 //   2. owner rank of each assignment (the replica tables), then a stable
 //      sort of the T*K assignments by owner rank;
-//   3. NCCL all-gather of the per-rank row counts (the W x W count matrix),
-//      read once on the host: every rank then knows where each of its rows
-//      lands in every other rank's receive buffer;
-//   4. dispatch kernel: each assignment's token row (bf16 [H]) and its
-//      owner-local expert index are stored straight into the owner's receive
-//      buffer over NVLink (peer memory opened with CUDA IPC);
-//   5. exchange barrier (a 4-byte NCCL all-reduce), then the block-scaled
+//   3. count exchange kernel: this rank's per-owner row counts are stored
+//      into row `me` of every rank's W x W count matrix (peer memory), a
+//      device barrier, then the matrix goes to mapped host memory and the
+//      kernel derives where this rank's rows land in every owner's receive
+//      buffer;
+//   4. dispatch kernel, enqueued before the host reads the counts: each
+//      assignment's token row (bf16 [H]) and its owner-local expert index
+//      are stored straight into the owner's receive buffer over NVLink (peer
+//      memory opened with CUDA IPC); the host meanwhile reads the matrix
+//      (polling the mapped flag, no stream synchronisation), and in the rare
+//      call where a buffer must grow, all ranks grow and dispatch again;
+//   5. device barrier, then the block-scaled
 //      pipeline on the received rows, grouped by (local expert, source rank,
 //      source order); the shared expert's rows (the rank's own tokens) ride
 //      along as the extra group.  The down GEMM's epilogue stores every
 //      expert row straight into its source rank's return buffer, at the
 //      position the row was sent from: compute and the return exchange are
 //      one kernel, tile by tile;
-//   6. barrier, then the single-device combine: shared row + the K expert
-//      rows in router order, one fused multiply-add each.
+//   6. device barrier, then the single-device combine: shared row + the K
+//      expert rows in router order, one fused multiply-add each.
+// The device barriers store an epoch into every rank's control words
+// (st.release.sys over NVLink) and wait, bounded, for every rank's; NCCL
+// remains for set-up (IPC handle exchange when buffers grow).
 // Every row's expert output and the combine order are those of one device,
 // so a rank's result equals the single-device result for its tokens wherever
 // both pick the same GEMM tile width.
@@ -37,6 +45,9 @@
 #include <nccl.h>  // types and prototypes only; no link-time dependency
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstring>
 #include <mutex>
 
 #include "engine.h"
@@ -111,20 +122,23 @@ __global__ void ep_owner_kernel(const int32_t* __restrict__ ids, uint32_t n, uin
 // Dispatch: row p of the owner-ordered assignment list (p in [soff[q],
 // soff[q+1]) goes to rank q) is stored into rank q's receive buffer at row
 // dst_off[q] + p - soff[q]: the assignment's token row and its expert index
-// in q's local list (meta).  One warp per row, 16-byte stores (H is a multiple of 8), into
-// peer memory for q != this rank.
+// in q's local list (meta).  One warp per row, 16-byte stores (H is a
+// multiple of 8), into peer memory for q != this rank.  Rows past rank q's
+// capacity (cap_rows[q]) are skipped: the host, which learns the counts while
+// this runs, grows the buffers and dispatches again.
 __global__ void ep_dispatch_kernel(const uint16_t* __restrict__ x, uint32_t H, uint32_t K,
                                    const int32_t* __restrict__ meta, const uint32_t* __restrict__ row_asg, uint32_t n,
                                    const uint32_t* __restrict__ soff, const uint32_t* __restrict__ dst_off,
-                                   uint16_t* const* __restrict__ peer_x, int32_t* const* __restrict__ peer_meta,
-                                   uint32_t world) {
+                                   const uint32_t* __restrict__ cap_rows, uint16_t* const* __restrict__ peer_x,
+                                   int32_t* const* __restrict__ peer_meta, uint32_t world) {
     pdl_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     for (uint32_t p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < n; p += warps) {
         uint32_t q = 0;
         while (q + 1 < world && __ldg(soff + q + 1) <= p) ++q;
-        const uint64_t row = (uint64_t)__ldg(dst_off + q) + p - __ldg(soff + q);
+        const uint64_t row = (uint64_t)dst_off[q] + p - __ldg(soff + q);
+        if (row >= __ldg(cap_rows + q)) continue;  // rank q's buffer grows first; this call then dispatches again
         const uint32_t a = row_asg[p];
         const uint4* src = reinterpret_cast<const uint4*>(x + (uint64_t)(a / K) * H);
         uint4* dst = reinterpret_cast<uint4*>(peer_x[q] + row * H);
@@ -132,6 +146,89 @@ __global__ void ep_dispatch_kernel(const uint16_t* __restrict__ x, uint32_t H, u
         if (lane == 0) peer_meta[q][row] = meta[a];
     }
     __threadfence_system();  // peer stores before the exchange barrier
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Barrier over the ranks through their control buffers (word q of rank r's
+// buffer: the last barrier epoch rank q reached, as seen by r).  One block,
+// thread q < W handles rank q: this rank's earlier stores (peer memory
+// included) are fenced, its arrival is stored into every rank's word `me`,
+// then thread q waits until rank q's arrival shows here.  Epochs only grow,
+// so a rank that is already one barrier ahead still counts.  Each wait gives
+// up after ~1 s of SM clocks, recording kErrTimeoutPeer.
+__device__ void ep_barrier(uint32_t* const* peer_ctrl, uint32_t me, uint32_t W, uint32_t epoch, uint32_t* err) {
+    const uint32_t q = threadIdx.x;
+    __threadfence_system();
+    __syncthreads();
+    if (q < W) st_release_sys(peer_ctrl[q] + me, epoch);
+    if (q < W) {
+        const uint32_t* f = peer_ctrl[me] + q;
+        const long long t0 = clock64();
+        while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
+            if (clock64() - t0 > (1ll << 31)) {
+                record_error(err, kErrTimeoutPeer);
+                break;
+            }
+            __nanosleep(100);
+        }
+    }
+    __syncthreads();
+}
+
+__global__ void ep_barrier_kernel(uint32_t* const* peer_ctrl, uint32_t me, uint32_t W, uint32_t epoch,
+                                  uint32_t* err) {
+    ep_barrier(peer_ctrl, me, W, epoch, err);
+}
+
+// The W x W row-count matrix without NCCL: this rank's counts cnt[W] go into
+// row `me` of every rank's matrix (words W + me*W .. of its control buffer),
+// a barrier, then the whole matrix is copied to pinned host memory followed by
+// the epoch in the word after it (stored last, release), which the host polls.
+__global__ void ep_counts_kernel(const uint32_t* __restrict__ cnt, uint32_t* const* peer_ctrl, uint32_t me,
+                                 uint32_t W, uint32_t epoch, uint32_t* host_ctrl, uint32_t* __restrict__ small,
+                                 uint32_t* err) {
+    pdl_wait();
+    for (uint32_t i = threadIdx.x; i < W * W; i += blockDim.x) {
+        const uint32_t q = i / W, j = i % W;
+        peer_ctrl[q][W + me * W + j] = cnt[j];
+    }
+    ep_barrier(peer_ctrl, me, W, epoch, err);
+    const uint32_t* mat = peer_ctrl[me] + W;
+    for (uint32_t i = threadIdx.x; i < W * W; i += blockDim.x) host_ctrl[i] = ld_relaxed_sys(mat + i);
+    // small: dst_off[q] = where this rank's rows start in rank q's receive
+    // buffer; roff[r] = where rank r's rows start in this rank's; sbase[r] =
+    // where rank r expects the rows it sent here, in its return buffer
+    if (threadIdx.x == 0) {
+        uint32_t acc = 0;
+        small[W] = 0;
+        for (uint32_t r = 0; r < W; ++r) {
+            acc += ld_relaxed_sys(mat + r * W + me);
+            small[W + 1 + r] = acc;
+        }
+        for (uint32_t q = 0; q < W; ++q) {
+            uint32_t o = 0, b = 0;
+            for (uint32_t r = 0; r < me; ++r) o += ld_relaxed_sys(mat + r * W + q);
+            for (uint32_t j = 0; j < me; ++j) b += ld_relaxed_sys(mat + q * W + j);
+            small[q] = o;
+            small[2 * W + 1 + q] = b;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) st_release_sys(host_ctrl + W * W, epoch);
 }
 
 }  // namespace
@@ -147,14 +244,20 @@ struct EpState {
     int rank = 0, world = 1;
     // dispatch permutation (by owner rank)
     DevBuf dest, pos, row_tok, row_asg, cnt, off, gu_off, dn_off, tile_counts, rank_buf;
-    DevBuf mat;        // W x W row counts: mat[r][q] = rows rank r sends to rank q
-    DevBuf small;      // per call: dst_off[W], roff[W+1], sbase[W]
+    DevBuf small;      // per call, written on the device: dst_off[W], roff[W+1], sbase[W]
     DevBuf ptrs;       // device copies of the peer pointers: x[W], meta[W], ret[W]
     DevBuf barrier_word, slots, yloc, handles;
     SymBuf recv_x, recv_meta, ret;  // receive rows, their expert indices; returned expert rows
     std::vector<uint64_t> cap_x, cap_meta, cap_ret;  // every rank's capacities (bytes), the same on all ranks
-    uint32_t* h_mat = nullptr;    // pinned [W x W]
-    uint32_t* h_small = nullptr;  // pinned [3W + 1]
+    // control words for the device-side count exchange and barriers: per rank
+    // [W] barrier epochs + [W x W] count matrix, mapped on every peer
+    SymBuf ctrl;
+    DevBuf ctrl_ptrs;             // device copy of ctrl.peer
+    uint32_t epoch = 0;           // barriers taken so far (the same on every rank)
+    uint32_t* h_ctrl = nullptr;   // mapped pinned [W x W] matrix + [1] epoch
+    uint32_t* d_h_ctrl = nullptr; // its device address
+    DevBuf cap_rows;              // [W] rows each rank's receive buffers hold (for H = cap_rows_H)
+    uint32_t cap_rows_H = 0, cap_gen = 0, cap_rows_gen = ~0u;
     std::vector<uint32_t> last_sent, last_recv;
     // expert placement (identical on every rank): replicas of expert e are
     // rep_ranks[rep_off[e] .. rep_off[e+1]); this rank's experts in order
@@ -176,15 +279,15 @@ void ep_release(EpState* ep) {
     close_peers(ep, ep->recv_x);
     close_peers(ep, ep->recv_meta);
     close_peers(ep, ep->ret);
+    close_peers(ep, ep->ctrl);
     if (ep->comm && nccl().ok) nccl().CommDestroy(static_cast<ncclComm_t>(ep->comm));
     DevBuf* bufs[] = {&ep->dest, &ep->pos, &ep->row_tok, &ep->row_asg, &ep->cnt, &ep->off, &ep->gu_off,
-                      &ep->dn_off, &ep->tile_counts, &ep->rank_buf, &ep->mat, &ep->small, &ep->ptrs,
+                      &ep->dn_off, &ep->tile_counts, &ep->rank_buf, &ep->small, &ep->ptrs,
                       &ep->barrier_word, &ep->slots, &ep->yloc, &ep->handles, &ep->recv_x.local,
                       &ep->recv_meta.local, &ep->ret.local, &ep->d_rep_off, &ep->d_rep_ranks,
-                      &ep->d_local_idx, &ep->meta};
+                      &ep->d_local_idx, &ep->meta, &ep->ctrl.local, &ep->ctrl_ptrs, &ep->cap_rows};
     for (DevBuf* b : bufs) b->release();
-    if (ep->h_mat) cudaFreeHost(ep->h_mat);
-    if (ep->h_small) cudaFreeHost(ep->h_small);
+    if (ep->h_ctrl) cudaFreeHost(ep->h_ctrl);
     delete ep;
 }
 
@@ -241,6 +344,10 @@ int ep_ensure_capacity(EpState* ep, const std::vector<uint64_t>& need_x, const s
         grow = grow || need_x[q] > ep->cap_x[q] || need_meta[q] > ep->cap_meta[q] || need_ret[q] > ep->cap_ret[q];
     }
     if (!grow) return 1;
+    ++ep->cap_gen;
+    // this rank's own kernels (a dispatch into the old buffers) finish
+    // before any mapping closes
+    CK(cudaStreamSynchronize(st));
     const NcclApi& nc = nccl();
     ncclComm_t comm = static_cast<ncclComm_t>(ep->comm);
     auto bump = [](uint64_t need, uint64_t cap) {
@@ -289,6 +396,52 @@ int ep_ensure_capacity(EpState* ep, const std::vector<uint64_t>& need_x, const s
     }
     CK(ep->ptrs.reserve(sizeof(void*) * 3 * W));
     CK(cudaMemcpy(ep->ptrs.ptr, dev_ptrs.data(), sizeof(void*) * 3 * W, cudaMemcpyHostToDevice));
+    return 1;
+}
+
+// Maps every rank's control buffer (collective, once per group).
+int ep_map_ctrl(EpState* ep, char* err) {
+    const uint32_t W = (uint32_t)ep->world, me = (uint32_t)ep->rank;
+    const NcclApi& nc = nccl();
+    ncclComm_t comm = static_cast<ncclComm_t>(ep->comm);
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, ep->ctrl.local.ptr));
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    DevBuf& d_h = ep->handles;
+    CK(d_h.reserve(hb * (W + 1)));
+    CK(cudaMemcpy(d_h.ptr, &mine, hb, cudaMemcpyHostToDevice));
+    NCK(nc.AllGather(d_h.ptr, d_h.as<uint8_t>() + hb, hb, ncclUint8, comm, 0));
+    std::vector<cudaIpcMemHandle_t> all(W);
+    CK(cudaMemcpy(all.data(), d_h.as<uint8_t>() + hb, hb * W, cudaMemcpyDeviceToHost));
+    for (uint32_t q = 0; q < W; ++q) {
+        if (q == me) {
+            ep->ctrl.peer[q] = ep->ctrl.local.ptr;
+        } else {
+            void* ptr = nullptr;
+            CK(cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess));
+            ep->ctrl.peer[q] = ptr;
+        }
+    }
+    CK(ep->ctrl_ptrs.reserve(sizeof(void*) * W));
+    CK(cudaMemcpy(ep->ctrl_ptrs.ptr, ep->ctrl.peer.data(), sizeof(void*) * W, cudaMemcpyHostToDevice));
+    // every rank has mapped every buffer before anyone stores into them
+    NCK(nc.AllReduce(ep->barrier_word.ptr, ep->barrier_word.ptr, 1, ncclUint32, ncclSum, comm, 0));
+    CK(cudaDeviceSynchronize());
+    return 1;
+}
+
+// Waits (host) for the count matrix of barrier `epoch`; ~10 s at most.
+int ep_wait_counts(EpState* ep, uint32_t epoch, char* err) {
+    const uint32_t W = (uint32_t)ep->world;
+    volatile uint32_t* flag = ep->h_ctrl + W * W;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint64_t i = 0; *flag != epoch; ++i) {
+        if ((i & 1023) == 0 && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10)) {
+            set_err(err, "expert-parallel count exchange timed out (a rank missing?)");
+            return 0;
+        }
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
     return 1;
 }
 
@@ -355,10 +508,19 @@ int moe_b200_ep_init(moe_b200_engine_t* eng, int rank, int world, const uint8_t*
     ep->cap_x.assign(world, 0);
     ep->cap_meta.assign(world, 0);
     ep->cap_ret.assign(world, 0);
-    if (cudaMallocHost(&ep->h_mat, sizeof(uint32_t) * world * world) != cudaSuccess ||
-        cudaMallocHost(&ep->h_small, sizeof(uint32_t) * (3 * world + 1)) != cudaSuccess ||
-        ep->barrier_word.reserve(4) != cudaSuccess || cudaMemset(ep->barrier_word.ptr, 0, 4) != cudaSuccess) {
+    ep->ctrl.peer.assign(world, nullptr);
+    const size_t ctrl_bytes = sizeof(uint32_t) * (world + world * world);
+    if (cudaHostAlloc(&ep->h_ctrl, sizeof(uint32_t) * (world * world + 1), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(&ep->d_h_ctrl, ep->h_ctrl, 0) != cudaSuccess ||
+        ep->barrier_word.reserve(4) != cudaSuccess || cudaMemset(ep->barrier_word.ptr, 0, 4) != cudaSuccess ||
+        ep->ctrl.local.reserve(ctrl_bytes) != cudaSuccess ||
+        cudaMemset(ep->ctrl.local.ptr, 0, ctrl_bytes) != cudaSuccess) {
         set_err(err, "allocation failed");
+        ep_release(ep);
+        return 0;
+    }
+    memset(ep->h_ctrl, 0, sizeof(uint32_t) * (world * world + 1));
+    if (!ep_map_ctrl(ep, err)) {
         ep_release(ep);
         return 0;
     }
@@ -487,7 +649,6 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     }
     CK(cudaSetDevice(eng->device));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    ncclComm_t comm = static_cast<ncclComm_t>(ep->comm);
     const uint32_t n = T * K;
     uint32_t* errw = eng->err_word.as<uint32_t>();
     uint32_t launches = 0;
@@ -534,7 +695,6 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     CK(ep->off.reserve((size_t)(W + 1) * 4));
     CK(ep->gu_off.reserve((size_t)(W + 1) * 4));
     CK(ep->dn_off.reserve((size_t)(W + 1) * 4));
-    CK(ep->mat.reserve((size_t)W * W * 4));
     GroupInfo gd;
     gd.count = ep->cnt.as<uint32_t>();
     gd.offset = ep->off.as<uint32_t>();
@@ -565,13 +725,53 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     }
     mark(2);
 
-    // 3. the W x W count matrix, read once on the host
-    const NcclApi& nc = nccl();
-    NCK(nc.AllGather(ep->cnt.ptr, ep->mat.ptr, W, ncclUint32, comm, st));
-    CK(cudaMemcpyAsync(ep->h_mat, ep->mat.ptr, (size_t)W * W * 4, cudaMemcpyDeviceToHost, st));
-    CK(cudaStreamSynchronize(st));
+    // 3. the W x W count matrix (peer stores + a device barrier; copied to
+    //    mapped host memory, and the offsets derived on the device), then
+    // 4. the dispatch into the owners' receive buffers, enqueued before the
+    //    host reads the counts (rows that do not fit are skipped and sent
+    //    again below after the buffers grow)
     const uint32_t me = (uint32_t)ep->rank;
-    auto M = [&](uint32_t r, uint32_t q) -> uint64_t { return ep->h_mat[(size_t)r * W + q]; };
+    uint32_t* const* d_ctrl = ep->ctrl_ptrs.as<uint32_t*>();
+    CK(ep->small.reserve((size_t)(3 * W + 1) * 4));
+    const uint32_t* d_dst_off = ep->small.as<uint32_t>();
+    const uint32_t* d_roff = d_dst_off + W;
+    const uint32_t* d_sbase = d_roff + W + 1;
+    auto upload_caps = [&]() -> int {
+        std::vector<uint32_t> c(W);
+        for (uint32_t q = 0; q < W; ++q)
+            c[q] = (uint32_t)std::min<uint64_t>({ep->cap_x[q] / (2ull * H), ep->cap_meta[q] / 4, 0xFFFFFFFFull});
+        CK(ep->cap_rows.reserve((size_t)W * 4));
+        CK(cudaMemcpyAsync(ep->cap_rows.ptr, c.data(), (size_t)W * 4, cudaMemcpyHostToDevice, st));
+        ep->cap_rows_H = H;
+        ep->cap_rows_gen = ep->cap_gen;
+        return 1;
+    };
+    auto dispatch = [&]() -> int {
+        if (ep->cap_rows_H != H || ep->cap_rows_gen != ep->cap_gen) {
+            if (!upload_caps()) return 0;
+        }
+        // the peer pointer table as of now: growing the buffers replaces it
+        void** d_ptrs = ep->ptrs.as<void*>();
+        if (n > 0 && d_ptrs) {
+            CK(launch_kernel(ep_dispatch_kernel, dim3(std::min(ceil_div(n, 8u), 148u * 8u)), dim3(256), 0, st, false,
+                             x, H, K, (const int32_t*)ep->meta.as<int32_t>(),
+                             (const uint32_t*)ep->row_asg.as<uint32_t>(), n, (const uint32_t*)ep->off.as<uint32_t>(),
+                             d_dst_off, (const uint32_t*)ep->cap_rows.as<uint32_t>(),
+                             reinterpret_cast<uint16_t* const*>(d_ptrs), reinterpret_cast<int32_t* const*>(d_ptrs + W),
+                             W));
+            launches += 1;
+        }
+        CK(launch_kernel(ep_barrier_kernel, dim3(1), dim3(32), 0, st, false, d_ctrl, me, W, ++ep->epoch, errw));
+        launches += 1;
+        return 1;
+    };
+    const uint32_t e_counts = ++ep->epoch;
+    CK(launch_kernel(ep_counts_kernel, dim3(1), dim3(32), 0, st, false, (const uint32_t*)ep->cnt.as<uint32_t>(),
+                     d_ctrl, me, W, e_counts, ep->d_h_ctrl, ep->small.as<uint32_t>(), errw));
+    launches += 1;
+    if (!dispatch()) return 0;
+    if (!ep_wait_counts(ep, e_counts, err)) return 0;
+    auto M = [&](uint32_t r, uint32_t q) -> uint64_t { return ep->h_ctrl[(size_t)r * W + q]; };
     std::vector<uint64_t> n_of(W, 0), recv_of(W, 0);
     for (uint32_t r = 0; r < W; ++r) {
         for (uint32_t q = 0; q < W; ++q) {
@@ -594,49 +794,22 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
             need_meta[q] = recv_of[q] * 4 + 16;
             need_ret[q] = n_of[q] * H * 4 + 16;
         }
+        const uint32_t gen = ep->cap_gen;
         if (!ep_ensure_capacity(ep, need_x, need_meta, need_ret, st, err)) return 0;
+        // grown (every rank decides alike): send again into the new buffers
+        if (ep->cap_gen != gen && !dispatch()) return 0;
     }
-    // where this rank's rows land in each owner's buffer, where each source's
-    // rows sit in this rank's receive buffer, and where each source expects
-    // its returned rows
     ep->last_sent.assign(W, 0);
     ep->last_recv.assign(W, 0);
-    uint32_t* hs = ep->h_small;  // dst_off[W], roff[W+1], sbase[W]
     for (uint32_t q = 0; q < W; ++q) {
-        uint64_t o = 0;
-        for (uint32_t r = 0; r < me; ++r) o += M(r, q);
-        hs[q] = (uint32_t)o;
         ep->last_sent[q] = (uint32_t)M(me, q);
         ep->last_recv[q] = (uint32_t)M(q, me);
     }
-    hs[W] = 0;
-    for (uint32_t r = 0; r < W; ++r) hs[W + 1 + r] = hs[W + r] + (uint32_t)M(r, me);
-    for (uint32_t r = 0; r < W; ++r) {
-        uint64_t o = 0;
-        for (uint32_t q = 0; q < me; ++q) o += M(r, q);
-        hs[2 * W + 1 + r] = (uint32_t)o;
-    }
-    CK(ep->small.reserve((size_t)(3 * W + 1) * 4));
-    CK(cudaMemcpyAsync(ep->small.ptr, hs, (size_t)(3 * W + 1) * 4, cudaMemcpyHostToDevice, st));
-    const uint32_t* d_dst_off = ep->small.as<uint32_t>();
-    const uint32_t* d_roff = d_dst_off + W;
-    const uint32_t* d_sbase = d_roff + W + 1;
-    void** d_ptrs = ep->ptrs.as<void*>();
-
-    // 4. dispatch into the owners' receive buffers
-    if (n > 0) {
-        CK(launch_kernel(ep_dispatch_kernel, dim3(std::min(ceil_div(n, 8u), 148u * 8u)), dim3(256), 0, st, false, x,
-                         H, K, (const int32_t*)ep->meta.as<int32_t>(), (const uint32_t*)ep->row_asg.as<uint32_t>(), n,
-                         (const uint32_t*)ep->off.as<uint32_t>(), d_dst_off,
-                         reinterpret_cast<uint16_t* const*>(d_ptrs), reinterpret_cast<int32_t* const*>(d_ptrs + W),
-                         W));
-        launches += 1;
-    }
     uint16_t* recv_x = ep->recv_x.local.as<uint16_t>();
+    void** d_ptrs = ep->ptrs.as<void*>();
     if (shared_rows) {
         CK(cudaMemcpyAsync(recv_x + (size_t)n_recv * H, x, (size_t)T * H * 2, cudaMemcpyDeviceToDevice, st));
     }
-    NCK(nc.AllReduce(ep->barrier_word.ptr, ep->barrier_word.ptr, 1, ncclUint32, ncclSum, comm, st));
     mark(3);
     mark(4);
 
@@ -672,7 +845,8 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     mark(5);
 
     // 6. once every rank's rows are back: combine in router order
-    NCK(nc.AllReduce(ep->barrier_word.ptr, ep->barrier_word.ptr, 1, ncclUint32, ncclSum, comm, st));
+    CK(launch_kernel(ep_barrier_kernel, dim3(1), dim3(32), 0, st, false, d_ctrl, me, W, ++ep->epoch, errw));
+    launches += 1;
     if (T > 0) {
         CK(launch_combine(ep->ret.local.as<float>(), H, ep->pos.as<uint32_t>(), w, T, K,
                           shared ? ep->yloc.as<float>() + (size_t)n_recv * H : nullptr, y_bf16, y_f32, st, false));
