@@ -320,11 +320,16 @@ moe_b200_engine_t* moe_b200_create(const moe_b200_init_t* init, char* err) {
     eng->num_sms = prop.multiProcessorCount;
     eng->layers.resize(layers);
     if (eng->err_word.reserve(sizeof(uint32_t)) != cudaSuccess ||
-        cudaMemset(eng->err_word.ptr, 0, sizeof(uint32_t)) != cudaSuccess) {
+        cudaMemset(eng->err_word.ptr, 0, sizeof(uint32_t)) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&eng->hstream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMallocHost(&eng->h_err, sizeof(uint32_t)) != cudaSuccess) {
         set_err(err, "device allocation failed");
+        if (eng->hstream) cudaStreamDestroy(eng->hstream);
+        eng->err_word.release();
         delete eng;
         return nullptr;
     }
+    *eng->h_err = 0;
     return eng;
 }
 
@@ -342,6 +347,8 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
     for (DevBuf* b : bufs) b->release();
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
     ep_release(eng->ep);
+    if (eng->hstream) cudaStreamDestroy(eng->hstream);
+    if (eng->h_err) cudaFreeHost(eng->h_err);
     delete eng;
 }
 
@@ -660,13 +667,19 @@ int moe_b200_sync(moe_b200_engine_t* eng, void* stream, char* err) {
         return 0;
     }
     CK(cudaSetDevice(eng->device));
-    CK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
-    uint32_t code = 0;
-    CK(cudaMemcpy(&code, eng->err_word.ptr, 4, cudaMemcpyDeviceToHost));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the error word rides the stream: one synchronisation covers both
+    CK(cudaMemcpyAsync(eng->h_err, eng->err_word.ptr, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    const uint32_t code = *eng->h_err;
     if (code != kErrNone) {
-        CK(cudaMemset(eng->err_word.ptr, 0, 4));
-        set_err(err, "device error %u (%s)", code,
-                code == kErrBadExpert ? "expert id out of range" : "bounded wait timed out in a GEMM pipeline");
+        CK(cudaMemsetAsync(eng->err_word.ptr, 0, 4, st));
+        CK(cudaStreamSynchronize(st));
+        const char* what = code == kErrBadExpert            ? "expert id out of range"
+                           : code == kErrTimeoutRouterLoad  ? "bounded wait timed out in the router"
+                           : code == kErrTimeoutPeer        ? "bounded wait for another rank timed out"
+                                                            : "bounded wait timed out in a GEMM pipeline";
+        set_err(err, "device error %u (%s)", code, what);
         return 0;
     }
     return 1;
@@ -693,7 +706,7 @@ int moe_b200_layer_forward_host(moe_b200_engine_t* eng, const moe_b200_layer_cfg
     CK(eng->hids.reserve((size_t)T * K * 4));
     CK(eng->hw.reserve((size_t)T * K * 4));
     CK(eng->hperm_out.reserve((size_t)T * K * 4));
-    cudaStream_t st = 0;
+    cudaStream_t st = eng->hstream;
     CK(cudaMemcpyAsync(eng->hx.ptr, x, (size_t)T * H * 2, cudaMemcpyHostToDevice, st));
     if (!moe_b200_layer_forward(eng, cfg, eng->hx.as<uint16_t>(), T, y_bf16 ? eng->hy.as<uint16_t>() : nullptr,
                                 y_f32 ? eng->hyf.as<float>() : nullptr, eng->hids.as<int32_t>(),

@@ -115,6 +115,10 @@ struct moe_b200_engine {
     uint64_t bs_map_dims[2][2] = {};
     // host-call staging
     DevBuf hx, hy, hyf, hids, hw, hperm_out, tri;
+    // host-buffer entry points: their own non-blocking stream, and a pinned
+    // word the error code is copied into before the one synchronisation
+    cudaStream_t hstream = nullptr;
+    uint32_t* h_err = nullptr;
     CUtensorMap tmap_x{}, tmap_h{};
     void* tmap_x_base = nullptr;
     void* tmap_h_base = nullptr;

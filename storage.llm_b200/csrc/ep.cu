@@ -877,7 +877,7 @@ int moe_b200_ep_layer_forward_host(moe_b200_engine_t* eng, const moe_b200_layer_
     CK(eng->hyf.reserve(t1 * H * 4));
     CK(eng->hids.reserve(t1 * K * 4));
     CK(eng->hw.reserve(t1 * K * 4));
-    cudaStream_t st = 0;
+    cudaStream_t st = eng->hstream;
     if (T > 0) CK(cudaMemcpyAsync(eng->hx.ptr, x, (size_t)T * H * 2, cudaMemcpyHostToDevice, st));
     if (!moe_b200_ep_layer_forward(eng, cfg, eng->hx.as<uint16_t>(), T, y_bf16 ? eng->hy.as<uint16_t>() : nullptr,
                                    y_f32 ? eng->hyf.as<float>() : nullptr, eng->hids.as<int32_t>(),
