@@ -232,9 +232,17 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     mark(2);
     // permuted source rows as exact hi/lo E4M3 terms + their scale blocks
     const uint64_t xb_rows = eng->xb.bytes / (2ull * Kq), hb_rows = eng->hb.bytes / (2ull * Iq);
-    CK(launch_gather_quant_bs(job.src, H, Kq, eng->row_token.as<uint32_t>(), eng->row_info.as<uint32_t>(), P,
-                              (uint32_t)xb_rows, block_n, eng->xb.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(), st,
-                              true));
+    if (job.K > 1 && job.K <= 32 && (job.shared_rows == 0 || (job.shared_base == 0 && job.shared_rows == job.T))) {
+        // each token row feeds K (+1 shared) permuted rows: split it once
+        CK(launch_scatter_quant_bs(job.src, H, Kq, job.T, job.K, eng->pos_of.as<uint32_t>(),
+                                   job.shared_rows ? gi.offset + job.E : nullptr, eng->row_info.as<uint32_t>(), P,
+                                   (uint32_t)xb_rows, block_n, eng->xb.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(),
+                                   st, true));
+    } else {
+        CK(launch_gather_quant_bs(job.src, H, Kq, eng->row_token.as<uint32_t>(), eng->row_info.as<uint32_t>(), P,
+                                  (uint32_t)xb_rows, block_n, eng->xb.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(),
+                                  st, true));
+    }
     *launches += 1;
     mark(3);
     BsParams bp{};

@@ -304,6 +304,114 @@ cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, 
     return cudaGetLastError();
 }
 
+// The same planes and scale words as gather_quant_bs_kernel, computed once
+// per token instead of once per permuted row: a warp takes (token t, chunk
+// of kGqChunk K stages), reads and splits the token's row once, and stores
+// the codes and scale words at each of the token's permuted rows:
+// pos_of[t*K + j] for its K routed assignments, and shared_off[0] + t for
+// the shared expert's row when shared_off is set.  Positions at or past
+// `rows` (an assignment the permutation rejected) are skipped.  The split
+// depends only on the values, so the bytes equal the per-row gather's.
+template <int BN>
+__global__ void __launch_bounds__(256) scatter_quant_bs_kernel(const uint16_t* __restrict__ x, uint32_t H,
+                                                               uint32_t Kp, uint32_t T, uint32_t K,
+                                                               const uint32_t* __restrict__ pos_of,
+                                                               const uint32_t* __restrict__ shared_off,
+                                                               const uint32_t* __restrict__ row_info, uint32_t rows,
+                                                               uint32_t rows_cap, uint8_t* __restrict__ xb,
+                                                               uint8_t* __restrict__ sf_atoms) {
+    constexpr uint32_t kAtom = BN <= 64 ? 512 : 1024;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t nkt = Kp / 128;
+    const uint32_t chunks = (nkt + kGqChunk - 1) / kGqChunk;
+    const uint64_t tasks = (uint64_t)T * chunks;
+    const uint64_t xplane = (uint64_t)rows_cap * Kp;
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    pdl_wait();  // the permutation (positions, row info) first
+    pdl_trigger();
+    for (uint64_t task = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; task < tasks; task += warps) {
+        const uint32_t t = (uint32_t)(task / chunks);
+        const uint32_t kt0 = (uint32_t)(task % chunks) * kGqChunk;
+        // lane j < K: the token's j-th routed row; the shared row separately
+        uint32_t my_pos = 0xFFFFFFFFu, my_info = 0;
+        if (lane < K) {
+            const uint32_t q = __ldg(pos_of + (uint64_t)t * K + lane);
+            if (q < rows) {
+                my_pos = q;
+                my_info = __ldg(row_info + q);
+            }
+        }
+        uint32_t sh_pos = 0xFFFFFFFFu, sh_info = 0;
+        if (shared_off) {
+            const uint32_t q = __ldg(shared_off) + t;
+            if (q < rows) {
+                sh_pos = q;
+                sh_info = __ldg(row_info + q);
+            }
+        }
+        const uint16_t* xr = x + (uint64_t)t * H;
+        uint2 raw[kGqChunk];
+#pragma unroll
+        for (uint32_t c = 0; c < kGqChunk; ++c) {
+            const uint32_t k = (kt0 + c) * 128 + lane * 4;  // H % 8 == 0: four elements all in or all out
+            raw[c] = (kt0 + c < nkt && k < H) ? __ldg(reinterpret_cast<const uint2*>(xr + k)) : make_uint2(0, 0);
+        }
+#pragma unroll
+        for (uint32_t c = 0; c < kGqChunk; ++c) {
+            const uint32_t kt = kt0 + c;
+            if (kt >= nkt) break;  // uniform across the warp
+            const float v[4] = {__uint_as_float(raw[c].x << 16), __uint_as_float(raw[c].x & 0xffff0000u),
+                                __uint_as_float(raw[c].y << 16), __uint_as_float(raw[c].y & 0xffff0000u)};
+            uint32_t hi4, lo4;
+            uint8_t sh, sl;
+            split_e4m3_x4(v, hi4, lo4, sh, sl);
+            // block j's scale bytes sit in lane 8j; gather them into one word
+            uint32_t shw = 0, slw = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                shw |= (uint32_t)(uint8_t)__shfl_sync(0xffffffffu, (uint32_t)sh, 8 * j) << (8 * j);
+                slw |= (uint32_t)(uint8_t)__shfl_sync(0xffffffffu, (uint32_t)sl, 8 * j) << (8 * j);
+            }
+            auto put = [&](uint32_t pos, uint32_t info) {
+                uint32_t* dh = reinterpret_cast<uint32_t*>(xb + (uint64_t)pos * Kp) + lane;
+                dh[kt * 32] = hi4;
+                reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(dh) + xplane)[kt * 32] = lo4;
+                if (lane == 0) {
+                    uint8_t* atom = sf_atoms + ((uint64_t)(info >> 8) * nkt + kt) * kAtom;
+                    *reinterpret_cast<uint32_t*>(atom + sfb_pos_hi<BN>(info & 0xFFu)) = shw;
+                    *reinterpret_cast<uint32_t*>(atom + sfb_pos_lo<BN>(info & 0xFFu)) = slw;
+                }
+            };
+            for (uint32_t j = 0; j < K; ++j) {
+                const uint32_t pos = __shfl_sync(0xffffffffu, my_pos, j);
+                const uint32_t info = __shfl_sync(0xffffffffu, my_info, j);
+                if (pos != 0xFFFFFFFFu) put(pos, info);  // uniform across the warp
+            }
+            if (sh_pos != 0xFFFFFFFFu) put(sh_pos, sh_info);
+        }
+    }
+}
+
+cudaError_t launch_scatter_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, uint32_t T, uint32_t K,
+                                    const uint32_t* pos_of, const uint32_t* shared_off, const uint32_t* row_info,
+                                    uint32_t rows, uint32_t rows_cap, uint32_t block_n, uint8_t* xb,
+                                    uint8_t* sf_atoms, cudaStream_t st, bool pdl) {
+    if (T == 0) return cudaSuccess;
+    if (K > 32) return cudaErrorInvalidValue;
+    const uint64_t tasks = (uint64_t)T * ((Kp / 128 + kGqChunk - 1) / kGqChunk);
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((tasks + 7) / 8, 148ull * 8ull);
+    if (block_n == 32) {
+        return launch_kernel(scatter_quant_bs_kernel<32>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, T, K,
+                             pos_of, shared_off, row_info, rows, rows_cap, xb, sf_atoms);
+    }
+    if (block_n == 64) {
+        return launch_kernel(scatter_quant_bs_kernel<64>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, T, K,
+                             pos_of, shared_off, row_info, rows, rows_cap, xb, sf_atoms);
+    }
+    return launch_kernel(scatter_quant_bs_kernel<128>, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, T, K, pos_of,
+                         shared_off, row_info, rows, rows_cap, xb, sf_atoms);
+}
+
 cudaError_t launch_gather_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token,
                                    const uint32_t* row_info, uint32_t rows, uint32_t rows_cap, uint32_t block_n,
                                    uint8_t* xb, uint8_t* sf_atoms, cudaStream_t st, bool pdl) {

@@ -158,6 +158,12 @@ cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, 
 cudaError_t launch_gather_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token,
                                    const uint32_t* row_info, uint32_t rows, uint32_t rows_cap, uint32_t block_n,
                                    uint8_t* xb, uint8_t* sf_atoms, cudaStream_t st, bool pdl);
+// The same planes, split once per token row of x [T x H] and stored at the
+// token's permuted rows pos_of[t*K + j] (and shared_off[0] + t when set).
+cudaError_t launch_scatter_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, uint32_t T, uint32_t K,
+                                    const uint32_t* pos_of, const uint32_t* shared_off, const uint32_t* row_info,
+                                    uint32_t rows, uint32_t rows_cap, uint32_t block_n, uint8_t* xb,
+                                    uint8_t* sf_atoms, cudaStream_t st, bool pdl);
 cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, const uint32_t* tile_off,
                                uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint32_t max_tiles,
                                TileEntry* tiles, cudaStream_t st);
