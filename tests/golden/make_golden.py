@@ -4,7 +4,7 @@ The reference ships no tests, golden vectors or fixtures, so parity is pinned
 by running the reference's own CPU hot path (compiled from its sources into
 oracle/_ref/libmoe_ref.so by oracle/Makefile) on seeded synthetic inputs and
 recording its outputs here.  Run it in a checkout that has the reference
-sources (MOE_REFERENCE_ROOT, default /root/reference):
+sources (MOE_REFERENCE_ROOT; its default is set in oracle/oracle.py):
 
     python tests/golden/make_golden.py [name-prefix]
 
