@@ -110,3 +110,72 @@ def test_expert_parallel_forward_matches_oracle(case):
         if tokens[r["rank"]]:
             assert r["ids_ok"] and r["w_ok"], r
             assert r["max_abs"] <= MAX_ABS and r["mean_rel"] <= MEAN_REL, r
+
+
+def _absent_rank_main(rank, uid, q, done):
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    from conftest import load_pkg
+
+    load_pkg()
+    import moe_b200.lib as L
+    import moe_b200.synth as synth
+
+    shape = synth.small_shape(hidden=256, intermediate=320, experts=8, top_k=2, tokens=40)
+    li = synth.make_layer(shape, seed=29)
+    x = synth.gen_tokens(shape, 40, seed=700 + rank, mu=None)
+    eng = L.Engine(rank)
+    try:
+        eng.ep_init(rank, WORLD, uid)
+        eng.upload_layer_ep(li)
+        cfg = L.Engine.cfg(shape, gemm_path=L.GEMM_BLOCKSCALED)
+        eng.ep_forward_host(cfg, x)  # both ranks: buffers sized, peers mapped
+        if rank == 0:
+            # rank 1 stays away from this call: every device barrier gives up
+            # after its bounded wait and the call reports it
+            try:
+                eng.ep_forward_host(cfg, x)
+                msg = "no error"
+            except L.MoEError as e:
+                msg = str(e)
+            eng.sync()  # the error was reported once; the context still works
+            q.put(dict(rank=0, msg=msg))
+            done.set()
+        else:
+            done.wait(timeout=120)  # keep the buffers mapped until rank 0 is done
+            q.put(dict(rank=1))
+    except Exception as e:
+        q.put(dict(rank=rank, error=repr(e)))
+        done.set()
+        raise
+    finally:
+        eng.close()
+
+
+@pytest.mark.skipif(_gpus() < WORLD, reason="needs two GPUs")
+def test_absent_rank_times_out_with_an_error():
+    """A rank that skips a collective call: the other rank's count exchange and
+    barriers wait about a second each, record the timeout and return; the call
+    fails with that message instead of hanging, and the context stays usable."""
+    import multiprocessing as mp
+    from conftest import load_pkg
+
+    load_pkg()
+    import moe_b200.lib as L
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    uid = L.Engine.ep_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    done = ctx.Event()
+    procs = [ctx.Process(target=_absent_rank_main, args=(r, uid, q, done)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    results = sorted((q.get(timeout=240) for _ in range(WORLD)), key=lambda r: r["rank"])
+    for p in procs:
+        p.join(timeout=120)
+    for r in results:
+        assert "error" not in r, r
+    for p in procs:
+        assert p.exitcode == 0
+    assert "another rank timed out" in results[0]["msg"], results[0]
