@@ -86,6 +86,10 @@ def sigmoid_case():
 GROUP_LIMIT_CASES = {
     "router_group_limit": (32, 8, 3, 4, 13),
     "router_group_limit_e1": (16, 16, 5, 3, 14),
+    # combinations the reference ignores: groups not dividing the experts,
+    # and as many kept groups as groups
+    "router_group_limit_uneven": (16, 3, 1, 3, 15),
+    "router_group_limit_all": (16, 4, 4, 3, 16),
 }
 
 

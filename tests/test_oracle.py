@@ -57,7 +57,8 @@ def test_sigmoid_router_fixture(port, synth):
     assert np.array_equal(bits(scores), bits(g["scores"]))
 
 
-@pytest.mark.parametrize("name", ["router_group_limit.npz", "router_group_limit_e1.npz"])
+@pytest.mark.parametrize("name", ["router_group_limit.npz", "router_group_limit_e1.npz",
+                                  "router_group_limit_uneven.npz", "router_group_limit_all.npz"])
 def test_group_limit_router_fixture(port, synth, name):
     """Sigmoid router with a DeepSeek-style group limit, against the compiled
     reference's own output (generation_router.cpp.inc:484-558)."""
