@@ -234,7 +234,10 @@ def test_tiled_router_matches_oracle(engine, synth, L, port, tokens, experts, hi
     (700, 128, 8, 4, 8),    # tiled router, register top-k
     (300, 256, 8, 4, 8),    # tiled router, 256 experts in 8 groups
     (100, 320, 10, 4, 8),   # tiled router, top-k past 256 experts
-], ids=["fused_e32", "fused_e64", "one_per_group", "tiled_e128", "tiled_e256", "tiled_e320"])
+    (40, 16, 3, 1, 3),      # groups do not divide the experts: no limit (as the reference)
+    (40, 16, 4, 4, 3),      # every group kept: no limit
+], ids=["fused_e32", "fused_e64", "one_per_group", "tiled_e128", "tiled_e256", "tiled_e320", "ignored_uneven",
+        "ignored_all"])
 def test_group_limited_router_matches_oracle(engine, synth, L, port, tokens, experts, n_group, topk_group, top_k):
     """Sigmoid routing with the group limit (generation_router.cpp.inc:484-558):
     the limited scores, ids and weights are bit-identical to the oracle's,
