@@ -342,11 +342,11 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
         if not ok:
             raise L.MoEError(eng.err.value.decode())
 
-    for _ in range(3):
+    for _ in range(10):
         step_host()
     dist.barrier()
     torch.cuda.synchronize()
-    e2e_steps = max(10, args.steps // 2)
+    e2e_steps = max(50, args.steps)  # host wall clock: a longer window for a steadier figure
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         step_host()
@@ -492,12 +492,12 @@ def main():
         if not ok:
             raise L.MoEError(eng.err.value.decode())
 
-    for _ in range(3):
+    for _ in range(10):
         step_host()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    e2e_steps = max(10, args.steps // 2)
+    e2e_steps = max(50, args.steps)  # host wall clock: a longer window for a steadier figure
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         step_host()
