@@ -476,6 +476,10 @@ int moe_b200_ep_init(moe_b200_engine_t* eng, int rank, int world, const uint8_t*
         set_err(err, "rank %d outside 0..%d", rank, world - 1);
         return 0;
     }
+    if (world > 32) {  // one lane per rank in the device barriers; one node holds at most 8 GPUs anyway
+        set_err(err, "world of %d ranks: at most 32 supported", world);
+        return 0;
+    }
     if (!nccl().ok) {
         set_err(err, "NCCL (libnccl.so.2) not available");
         return 0;
