@@ -225,7 +225,13 @@ MOE_B200_API int moe_b200_ep_local_expert_list(moe_b200_engine_t* engine, uint32
                                                uint32_t capacity, uint32_t* count, char* err);
 /* The layer on this rank's T tokens (device pointers, caller's stream; the
  * same outputs as moe_b200_layer_forward for those tokens).  Block-scaled
- * GEMM path only.  T may be 0 (the rank still serves its experts). */
+ * GEMM path only.  T may be 0 (the rank still serves its experts).
+ * Collective: every rank calls it, in the same order.  The host returns once
+ * the row counts are known (the device work continues on the stream).  If a
+ * rank misses a call, the others' device waits give up after about a second
+ * each and the call (or the next moe_b200_sync) reports "bounded wait for
+ * another rank timed out"; the group is then out of step and must be set up
+ * again with moe_b200_ep_init on every rank. */
 MOE_B200_API int moe_b200_ep_layer_forward(moe_b200_engine_t* engine, const moe_b200_layer_cfg_t* cfg,
                                            const uint16_t* x_bf16, uint32_t tokens, uint16_t* y_bf16, float* y_f32,
                                            int32_t* topk_ids, float* topk_w, void* stream, char* err);
