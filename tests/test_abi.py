@@ -76,3 +76,54 @@ def test_create_without_gpu_fails_loudly(lib, pkg):
         pytest.skip("a GPU is present")
     with pytest.raises(L.MoEError):
         L.Engine(0)
+
+
+CPP_CLIENT = r"""
+// A C++ caller in the style of the binding in INTEGRATION.md.
+#include <cstdio>
+#include <cstring>
+#include "moe_b200.h"
+
+int main() {
+    char err[MOE_B200_ERR_LEN] = {0};
+    moe_b200_init_t init{0, 1};
+    moe_b200_engine_t* eng = moe_b200_create(&init, err);
+    if (!eng) {
+        // no B200 here: the library must say why instead of falling back
+        std::printf("no-engine:%s\n", err[0] ? err : "(empty)");
+        return err[0] ? 0 : 2;
+    }
+    moe_b200_layer_cfg_t cfg{};
+    cfg.hidden = 60;  // not a multiple of 8: rejected before any device work
+    cfg.intermediate = 64;
+    cfg.experts = 8;
+    cfg.top_k = 2;
+    const int ok = moe_b200_layer_forward_host(eng, &cfg, nullptr, 1, nullptr, nullptr, nullptr, nullptr,
+                                               nullptr, err);
+    moe_b200_destroy(eng);
+    std::printf("engine:%d:%s\n", ok, err);
+    return ok == 0 && err[0] ? 0 : 3;
+}
+"""
+
+
+def test_cpp_client_builds_links_and_fails_loudly_without_a_b200(lib, pkg, tmp_path):
+    """The header compiles as C++, a client links against the library, and
+    without a B200 engine creation fails with a message (no CPU path); on a
+    B200 host the same client gets an argument error instead."""
+    import shutil
+    import subprocess
+    import moe_b200.lib as L
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        pytest.skip("no C++ compiler")
+    root = Path(__file__).resolve().parents[1]
+    src = tmp_path / "client.cpp"
+    src.write_text(CPP_CLIENT)
+    exe = tmp_path / "client"
+    so = Path(L.LIB_PATH)
+    subprocess.run([cxx, "-std=c++17", "-I", str(root / "include"), str(src), "-o", str(exe), str(so),
+                    f"-Wl,-rpath,{so.parent}"], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+    assert r.stdout.startswith(("no-engine:", "engine:0:")), r.stdout
