@@ -199,7 +199,8 @@ def test_permutation_paths_match_reference_order(engine, synth, L, port, tokens,
     (333, 256, 264, 4, False),   # rows only 8-byte aligned (8-byte staging copies)
     (1501, 72, 136, 0, True),    # partial token and expert tiles; sigmoid (C-library expf) scores
     (260, 300, 2056, 0, False),  # several staged chunks, the top-k past 256 experts
-], ids=["tail", "aligned8", "partial_sigmoid", "chunks_e300"])
+    (8, 128, 256, 0, False),     # fewer tokens than one tile (the copy box overhangs the rows)
+], ids=["tail", "aligned8", "partial_sigmoid", "chunks_e300", "decode_e128"])
 def test_tiled_router_matches_oracle(engine, synth, L, port, tokens, experts, hidden, offset, sigmoid):
     """Batches too large for the single-kernel router: logits, scores, ids and
     weights are bit-identical to the oracle's, including the reference's
