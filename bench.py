@@ -29,13 +29,16 @@ grouped GEMM, weighted combine.
 L2: the 423 MB of expert weights a step streams exceed the 126 MB L2, so no
 flush is needed between steps ("l2": "inputs_exceed_l2").
 
-Multi-GPU (torchrun, N ranks): expert parallelism.  Rank r owns experts
-[r*E/N, (r+1)*E/N) and its own batch of `--tokens` tokens (weak scaling);
-each step is moe_b200_ep_layer_forward on every rank: local router, NCCL
-all-to-allv of the assignment rows to their experts' owners, the local
-block-scaled expert GEMMs, the reverse exchange and the combine.  value sums
-the ranks' tokens over the slowest rank's CUDA-event time; the line also
-reports the exchange's load balance (max / mean rows received per rank).
+Multi-GPU (torchrun, N ranks): expert parallelism.  Experts are placed over
+the ranks from a separate calibration batch (hot experts replicated), each
+rank has its own batch of `--tokens` tokens (weak scaling); each step is
+moe_b200_ep_layer_forward on every rank: local router, a device-side count
+exchange, the assignment rows stored into their experts' owners over NVLink,
+the local block-scaled expert GEMMs whose down-projection epilogue stores the
+rows back to their source ranks, device barriers, and the combine.  value
+sums the ranks' tokens over the slowest rank's CUDA-event time; the line also
+reports the exchange's load balance (max / mean rows received per rank) and
+a per-phase breakdown on rank 0.
 """
 from __future__ import annotations
 
