@@ -334,8 +334,11 @@ int ep_default_placement(EpState* ep, uint32_t E, char* err) {
 // Makes every rank's receive/return buffers at least as large as this call
 // needs (all ranks decide from the same count matrix and token counts, so
 // they agree without talking), then re-exchanges the IPC handles.
-// Collective; the stream must be idle on every rank (it is: the count
-// matrix was just read with a stream synchronisation).
+// Collective.  Before any mapping closes, this rank's stream is drained (a
+// dispatch into the old buffers may still run), and a barrier makes sure no
+// rank still uses a mapping its owner is about to free.  These collectives
+// are NCCL's and have no timeout: after a peer timed out in the count
+// exchange, ranks can disagree on growing, and the next such call can block.
 int ep_ensure_capacity(EpState* ep, const std::vector<uint64_t>& need_x, const std::vector<uint64_t>& need_meta,
                        const std::vector<uint64_t>& need_ret, cudaStream_t st, char* err) {
     const uint32_t W = (uint32_t)ep->world, me = (uint32_t)ep->rank;
