@@ -26,8 +26,14 @@ grouped GEMM, weighted combine.
             cores over one 256-token batch (kind "reference"), or the C
             restatement when that library is absent (kind "port").
 
-L2: the 423 MB of expert weights a step streams exceed the 126 MB L2, so no
-flush is needed between steps ("l2": "inputs_exceed_l2").
+L2: no flush between steps; instead the weights a step reads are never
+still cached when they are read again.  At the headline workload one layer's
+routed experts are 423 MB against the 126 MB L2.  Where one layer's touched
+weights are smaller (config 0, small token counts, a rank's expert block at 4
+or 8 GPUs), the layer is uploaded into several layer slots -- as a model's
+consecutive MoE layers would be -- and the steps cycle through them, so that
+at least twice the L2 is read between two uses of one copy
+("weight_copies_cycled" in `config`).
 
 Multi-GPU (torchrun, N ranks): expert parallelism.  Experts are placed over
 the ranks from a separate calibration batch (hot experts replicated), each
@@ -45,6 +51,7 @@ from __future__ import annotations
 import argparse
 import importlib.util
 import json
+import math
 import os
 import subprocess
 import sys
@@ -74,6 +81,21 @@ def measured_peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     return 6650.0, 1590.0, "fallback"
+
+
+L2_BYTES = 126e6    # B200 L2
+MAX_COPIES = 16     # layer slots the engines are created with
+
+
+def expert_bytes(shape) -> float:
+    """MXFP4 bytes of one expert triplet (17 bytes per 32 weights)."""
+    return 3 * shape.intermediate * shape.hidden * 17 / 32
+
+
+def weight_copies(touched_bytes: float) -> int:
+    """Layer copies the timed steps cycle through so that at least twice the
+    L2 is read between two uses of one copy's weights."""
+    return int(max(1, min(MAX_COPIES, math.ceil(2 * L2_BYTES / max(touched_bytes, 1.0)))))
 
 
 class ClockSampler:
@@ -199,14 +221,18 @@ def run_reference(args, shape, metric):
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def config_dict(shape, args):
-    return {"workload": f"config{args.config}: H{shape.hidden} E{shape.experts} top{shape.top_k} "
-                        f"I{shape.intermediate} SwiGLU MXFP4, {args.tokens} tokens/step"
-                        + (f", skew {shape.skew}" if shape.skew else ""),
-            "hidden": shape.hidden, "experts": shape.experts, "top_k": shape.top_k,
-            "intermediate": shape.intermediate, "tokens_per_step": args.tokens, "shared_expert": shape.shared,
-            "parallelism": f"ep{args.gpus}" if args.gpus > 1 else "single",
-            "l2": "inputs_exceed_l2"}
+def config_dict(shape, args, copies: int = 1, touched_bytes: float | None = None):
+    d = {"workload": f"config{args.config}: H{shape.hidden} E{shape.experts} top{shape.top_k} "
+                     f"I{shape.intermediate} SwiGLU MXFP4, {args.tokens} tokens/step"
+                     + (f", skew {shape.skew}" if shape.skew else ""),
+         "hidden": shape.hidden, "experts": shape.experts, "top_k": shape.top_k,
+         "intermediate": shape.intermediate, "tokens_per_step": args.tokens, "shared_expert": shape.shared,
+         "parallelism": f"ep{args.gpus}" if args.gpus > 1 else "single",
+         "l2": "inputs_exceed_l2"}
+    if touched_bytes is not None:  # the GPU arms: weights read between two uses of one copy
+        d["weight_copies_cycled"] = copies
+        d["weight_bytes_between_reuses"] = touched_bytes * copies
+    return d
 
 
 def profiled_traffic(args):
@@ -277,7 +303,7 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     import moe_b200.lib as L
 
     T, H, K = args.tokens, shape.hidden, shape.top_k
-    eng = L.Engine(local)
+    eng = L.Engine(local, max_layers=MAX_COPIES)
     with StdoutToStderr():
         uid = [L.Engine.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
@@ -285,8 +311,20 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
         dist.barrier()
     placement, planned_imbalance = calibrate_placement(shape, li, rank, world, dist, T)
     eng.ep_set_placement(placement)
-    eng.upload_layer_ep(li)
-    cfg = L.Engine.cfg(shape, gemm_path=L.GEMM_BLOCKSCALED)
+    # copies of the layer to cycle through, from the smallest expert block
+    # any rank holds (the placement is the same on every rank, so is this)
+    min_block = min(sum(q in reps for reps in placement) for q in range(world))
+    touched = (min_block + (1 if shape.shared else 0)) * expert_bytes(shape)
+    copies = weight_copies(touched)
+    for layer in range(copies):
+        eng.upload_layer_ep(li, layer=layer)
+    cfgs = [L.Engine.cfg(shape, layer=layer, gemm_path=L.GEMM_BLOCKSCALED) for layer in range(copies)]
+    calls = [0]
+
+    def next_cfg():
+        calls[0] += 1
+        return cfgs[(calls[0] - 1) % copies]
+
     x = torch.from_numpy(li.x.view(np.int16)).cuda()
     y = torch.empty((T, H), dtype=torch.int16, device="cuda")
     ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
@@ -295,7 +333,7 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     sp = stream.cuda_stream
 
     def step():
-        eng.ep_forward(cfg, x, T, y_bf16=y, ids=ids, w=w, stream=sp)
+        eng.ep_forward(next_cfg(), x, T, y_bf16=y, ids=ids, w=w, stream=sp)
 
     for _ in range(args.warmup):
         step()
@@ -340,8 +378,8 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     lib = L.load()
 
     def step_host():
-        ok = lib.moe_b200_ep_layer_forward_host(eng.h, C.byref(cfg), xh.data_ptr(), T, yh.data_ptr(), None,
-                                                idsh.data_ptr(), wh.data_ptr(), eng.err)
+        ok = lib.moe_b200_ep_layer_forward_host(eng.h, C.byref(next_cfg()), xh.data_ptr(), T, yh.data_ptr(),
+                                                None, idsh.data_ptr(), wh.data_ptr(), eng.err)
         if not ok:
             raise L.MoEError(eng.err.value.decode())
 
@@ -368,7 +406,8 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     result = {
         "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": config_dict(shape, args),
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": config_dict(shape, args, copies, touched),
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2 * world,
                 "d2h_bytes_per_step": (T * H * 2 + T * K * 8) * world},
         "roofline": {"kernel": "whole layer on one expert-parallel rank", "bound": "hbm", "achieved": achieved,
@@ -433,7 +472,7 @@ def main():
         li.x = synth.gen_tokens(shape, args.tokens, seed=100 + rank, mu=li.mu)
         run_expert_parallel(args, shape, li, metric, rank, world, local, dist)
         return
-    eng = L.Engine(local)
+    eng = L.Engine(local, max_layers=MAX_COPIES)
     eng.upload_layer(li)
     cfg = L.Engine.cfg(shape)
     T, H, K = args.tokens, shape.hidden, shape.top_k
@@ -444,8 +483,24 @@ def main():
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
 
+    # one call tells which experts the batch routes to, hence the weight
+    # bytes a step reads and how many copies of the layer to cycle through
+    eng.forward(cfg, x, T, y_bf16=y, ids=ids, w=w, stream=sp)
+    eng.sync(sp)
+    routed = int((eng.read(L.BUF_GROUP_COUNT, (shape.experts,), np.uint32) > 0).sum())
+    touched = (routed + (1 if shape.shared else 0)) * expert_bytes(shape)
+    copies = weight_copies(touched)
+    for layer in range(1, copies):
+        eng.upload_layer(li, layer=layer)
+    cfgs = [cfg] + [L.Engine.cfg(shape, layer=layer) for layer in range(1, copies)]
+    calls = [0]
+
+    def next_cfg():
+        calls[0] += 1
+        return cfgs[(calls[0] - 1) % copies]
+
     def step():
-        eng.forward(cfg, x, T, y_bf16=y, ids=ids, w=w, stream=sp)
+        eng.forward(next_cfg(), x, T, y_bf16=y, ids=ids, w=w, stream=sp)
 
     for _ in range(args.warmup):
         step()
@@ -490,7 +545,7 @@ def main():
     import ctypes as C
 
     def step_host():
-        ok = lib.moe_b200_layer_forward_host(eng.h, C.byref(cfg), xh.data_ptr(), T, yh.data_ptr(), None,
+        ok = lib.moe_b200_layer_forward_host(eng.h, C.byref(next_cfg()), xh.data_ptr(), T, yh.data_ptr(), None,
                                              idsh.data_ptr(), wh.data_ptr(), None, eng.err)
         if not ok:
             raise L.MoEError(eng.err.value.decode())
@@ -532,7 +587,8 @@ def main():
     result = {
         "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": config_dict(shape, args),
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": config_dict(shape, args, copies, touched),
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2 + T * K * 8},
         "roofline": {"kernel": "gemm_bs_kernel<gate_up>", "bound": "hbm", "achieved": achieved, "peak": hbm,
