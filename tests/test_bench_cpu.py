@@ -20,3 +20,24 @@ def test_reference_arm_prints_one_json_line():
     assert d["metric"] == "MoE-layer tokens/sec" and d["value"] > 0 and d["higher_is_better"]
     assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_weight_copies_keep_reuse_distance_past_l2():
+    """Between two uses of one layer copy's weights the steps read at least
+    twice the L2: one copy at the headline workload, several where a step
+    touches little (config 0, one expert on a rank)."""
+    import importlib.util
+    root = Path(__file__).resolve().parents[1]
+    spec = importlib.util.spec_from_file_location("bench_mod", root / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    bench.load_pkg()
+    import moe_b200.synth as synth
+    c0, c1 = synth.CONFIGS[0], synth.CONFIGS[1]
+    assert bench.weight_copies(32 * bench.expert_bytes(c1)) == 1       # 423 MB routed per step
+    assert bench.weight_copies(8 * bench.expert_bytes(c0)) == 7        # config 0: 37 MB
+    assert bench.weight_copies(bench.expert_bytes(c1)) == bench.MAX_COPIES
+    for touched in (1e6, 3e7, 1.3e8, 2.6e8, 5e8):
+        n = bench.weight_copies(touched)
+        assert 1 <= n <= bench.MAX_COPIES
+        assert n * touched >= 2 * bench.L2_BYTES or n == bench.MAX_COPIES
