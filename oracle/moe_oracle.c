@@ -131,6 +131,38 @@ float mo_bf16_dot_row(const uint16_t* w, const float* x, uint32_t n) {
 /* x / (1 + exp(-x)) with the exact libm exp: generation_silu.cpp.inc:20-26. */
 float mo_silu(float x) { return x / (1.0f + expf(-x)); }
 
+/* GELU, erf form: 0.5 x (1 + erf(x / sqrt 2)) (generation_silu.cpp.inc:28-30). */
+static float mo_gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f)); }
+
+/* GELU, tanh form (generation_mlp.cpp.inc:94-97).  The reference's build
+ * fuses x + 0.044715 x^3 into one multiply-add on the last product. */
+static float mo_gelu_tanh(float x) {
+    const float k = 0.7978845608028654f;
+    return 0.5f * x * (1.0f + tanhf(k * fmaf(0.044715f * x * x, x, x)));
+}
+
+/* act(gate) * up for activation mode 0 SiLU, 1 GELU (erf), 2 GELU (tanh)
+ * (moe_generation_gated_activation_cached, generation_mlp.cpp.inc:99-104). */
+float mo_gated_activation(int32_t mode, float gate, float up) {
+    if (mode == 2) return mo_gelu_tanh(gate) * up;
+    return (mode == 1 ? mo_gelu_erf(gate) : mo_silu(gate)) * up;
+}
+
+/* RMSNorm with a weight vector (moe_apply_rmsnorm_common_weight_f32,
+ * generation_mlp.cpp.inc:145-175): the sum of squares in double, in element
+ * order (the reference's build fuses each step into a double multiply-add),
+ * the mean rounded to float, 1 / sqrt(mean + eps) in float, then
+ * x * norm * w -- or x * norm * (1 + w) for Gemma models (the unit offset,
+ * raw_forward_utils.cpp.inc:322-328).  eps <= 0 means 1e-6. */
+int mo_rmsnorm(const float* in, const float* w, uint32_t n, float eps, int32_t unit_offset, float* out) {
+    if (!in || !w || !out || n == 0) return 0;
+    double ss = 0.0;
+    for (uint32_t i = 0; i < n; ++i) ss = fma((double)in[i], (double)in[i], ss);
+    const float norm = 1.0f / sqrtf((float)(ss / (double)n) + (eps > 0.0f ? eps : 1.0e-6f));
+    for (uint32_t i = 0; i < n; ++i) out[i] = in[i] * norm * (unit_offset ? (1.0f + w[i]) : w[i]);
+    return 1;
+}
+
 /* Group limit of sigmoid routers (generation_router.cpp.inc:484-558),
  * applied when n_group > 1, 0 < topk_group < n_group and E % n_group == 0:
  * each group's score is the sum of its two largest scores (best0/best1
@@ -300,18 +332,39 @@ int mo_group_tokens_by_expert(const mo_assignment_t* a, uint32_t n, mo_assignmen
 
 /* One expert: gate/up row dots, SiLU(gate)*up, then down row dots
  * (expert_triplet_cpu.cpp.inc:22-106, generation_mlp.cpp.inc:1346-1404). */
-int mo_expert_triplet(const uint8_t* gate, const uint8_t* up, const uint8_t* down,
-                      const float* x, uint32_t H, uint32_t I,
-                      float* sg, float* su, float* out) {
+static void mo_triplet_act(int32_t mode, const uint8_t* gate, const uint8_t* up, const uint8_t* down,
+                           const float* x, uint32_t H, uint32_t I, float* sg, float* su, float* out) {
     const uint64_t row_h = (uint64_t)((H + 31u) / 32u) * 17u;
     const uint64_t row_i = (uint64_t)((I + 31u) / 32u) * 17u;
     for (uint32_t r = 0; r < I; ++r) {
         sg[r] = mo_mxfp4_dot_row(gate + r * row_h, x, H);
         su[r] = mo_mxfp4_dot_row(up + r * row_h, x, H);
-        sg[r] = mo_silu(sg[r]) * su[r];
+        sg[r] = mo_gated_activation(mode, sg[r], su[r]);
     }
     for (uint32_t r = 0; r < H; ++r) out[r] = mo_mxfp4_dot_row(down + r * row_i, sg, I);
+}
+
+int mo_expert_triplet(const uint8_t* gate, const uint8_t* up, const uint8_t* down,
+                      const float* x, uint32_t H, uint32_t I,
+                      float* sg, float* su, float* out) {
+    mo_triplet_act(0, gate, up, down, x, H, I, sg, su, out);
     return 1;
+}
+
+/* Per-expert output scale (moe_layer_apply_expert_down_scale_f32,
+ * generation_mlp.cpp.inc:514-570): one scale for every expert, one per
+ * expert, or one per (expert, element); a count that fits none of these
+ * leaves the row unscaled, as in the reference. */
+static void mo_down_scale(const mo_layer_t* L, uint32_t expert, float* v) {
+    const uint64_t n = L->down_scale_count, E = L->experts, H = L->hidden;
+    if (!L->down_scale || n == 0) return;
+    if (n == 1) {
+        for (uint64_t i = 0; i < H; ++i) v[i] *= L->down_scale[0];
+    } else if (n == E && expert < E) {
+        for (uint64_t i = 0; i < H; ++i) v[i] *= L->down_scale[expert];
+    } else if ((uint64_t)expert * H <= n && H <= n - (uint64_t)expert * H) {
+        for (uint64_t i = 0; i < H; ++i) v[i] *= L->down_scale[(uint64_t)expert * H + i];
+    }
 }
 
 /* dst += alpha * src with one fused multiply-add per element: the AVX2
@@ -324,6 +377,7 @@ static void mo_axpy(float* dst, const float* src, float alpha, uint32_t n) {
 typedef struct {
     const mo_layer_t* L;
     const uint16_t* x_bf16;
+    const float* hidden;
     float* y;
     int32_t* ids;
     float* w;
@@ -332,59 +386,95 @@ typedef struct {
     int ok;
 } mo_layer_job;
 
-/* One token through the layer in moe_layer_moe_mlp_f32 order
- * (generation_mlp.cpp.inc:776-1442): shared expert into mlp first
- * (:839-860, gate scalar 1 with no shared-gate tensor), router top-k (:874),
- * gate/up/act and down for each selected expert, then mlp += w_e * y_e in
- * router order (:1417-1431).  y receives mlp, before the residual add. */
+/* One token through the block in moe_layer_moe_mlp_f32 order
+ * (generation_mlp.cpp.inc:776-1442):
+ *   shared input = x; routed input = RMSNorm(hidden) with pre_norm2 when
+ *     given (:820-831, moe_layer_moe_norm_f32 :234-250), else x; the router
+ *     reads the routed input (:866-876);
+ *   shared expert (:839-860): act(gate)*up, down; RMSNorm with post_norm1
+ *     (:853-856); mlp += out * g, g = sigmoid(shared_gate_inp . x) or 1
+ *     (moe_layer_shared_expert_gate_f32 :478-512) -- mlp is still 0 there,
+ *     so the reference's fused multiply-add is the plain product;
+ *   router top-k, gate/up/act and down for each selected expert;
+ *   per expert in router order (:1417-1431): RMSNorm with post_norm2, the
+ *     down scale, mlp += w_e * y_e;
+ *   y = RMSNorm(mlp) with post_norm (moe_add_mlp_residual_f32 :572-594),
+ *     else mlp: what the block adds to hidden. */
 static void* mo_layer_worker(void* arg) {
     mo_layer_job* j = (mo_layer_job*)arg;
     const mo_layer_t* L = j->L;
     const uint32_t H = L->hidden, I = L->intermediate, K = L->top_k;
     const uint64_t gu_bytes = (uint64_t)I * ((H + 31u) / 32u) * 17u;
     const uint64_t d_bytes = (uint64_t)H * ((I + 31u) / 32u) * 17u;
+    const int32_t act = L->activation;
     float* x = (float*)malloc(sizeof(float) * H);
+    float* xe = (float*)malloc(sizeof(float) * H);
     float* mlp = (float*)malloc(sizeof(float) * H);
     float* out = (float*)malloc(sizeof(float) * H);
+    float* tmp = (float*)malloc(sizeof(float) * H);
     float* sg = (float*)malloc(sizeof(float) * I);
     float* su = (float*)malloc(sizeof(float) * I);
     int32_t* ids = (int32_t*)malloc(sizeof(int32_t) * K);
     float* w = (float*)malloc(sizeof(float) * K);
-    j->ok = x && mlp && out && sg && su && ids && w;
+    j->ok = x && xe && mlp && out && tmp && sg && su && ids && w && (!L->pre_norm2 || j->hidden);
     for (uint32_t t = j->t0; j->ok && t < j->t1; ++t) {
         for (uint32_t h = 0; h < H; ++h) x[h] = mo_bf16(j->x_bf16[(uint64_t)t * H + h]);
+        const float* xr = x;
+        if (L->pre_norm2) {
+            mo_rmsnorm(j->hidden + (uint64_t)t * H, L->pre_norm2, H, L->norm_eps, L->norm_unit_offset, xe);
+            xr = xe;
+        }
         memset(mlp, 0, sizeof(float) * H);
         if (L->shared_gate && L->shared_up && L->shared_down) {
-            mo_expert_triplet(L->shared_gate, L->shared_up, L->shared_down, x, H, I, sg, su, out);
-            for (uint32_t h = 0; h < H; ++h) mlp[h] = mlp[h] + out[h] * 1.0f;
+            mo_triplet_act(act, L->shared_gate, L->shared_up, L->shared_down, x, H, I, sg, su, out);
+            float g = 1.0f;
+            if (L->shared_gate_inp) g = 1.0f / (1.0f + expf(-mo_bf16_dot_row(L->shared_gate_inp, x, H)));
+            const float* so = out;
+            if (L->post_norm1) {
+                mo_rmsnorm(out, L->post_norm1, H, L->norm_eps, L->norm_unit_offset, tmp);
+                so = tmp;
+            }
+            for (uint32_t h = 0; h < H; ++h) mlp[h] = fmaf(so[h], g, mlp[h]);
         }
-        if (!mo_router_topk(L, x, ids, w, &j->ties)) { j->ok = 0; break; }
+        if (!mo_router_topk(L, xr, ids, w, &j->ties)) { j->ok = 0; break; }
         for (uint32_t e = 0; e < K; ++e) {
             const uint64_t ex = (uint64_t)ids[e];
-            mo_expert_triplet(L->gate + ex * gu_bytes, L->up + ex * gu_bytes, L->down + ex * d_bytes,
-                              x, H, I, sg, su, out);
+            mo_triplet_act(act, L->gate + ex * gu_bytes, L->up + ex * gu_bytes, L->down + ex * d_bytes,
+                           xr, H, I, sg, su, out);
+            if (L->post_norm2) {
+                mo_rmsnorm(out, L->post_norm2, H, L->norm_eps, L->norm_unit_offset, tmp);
+                memcpy(out, tmp, sizeof(float) * H);
+            }
+            mo_down_scale(L, (uint32_t)ex, out);
             mo_axpy(mlp, out, w[e], H);
         }
-        memcpy(j->y + (uint64_t)t * H, mlp, sizeof(float) * H);
+        float* yt = j->y + (uint64_t)t * H;
+        if (L->post_norm) {
+            mo_rmsnorm(mlp, L->post_norm, H, L->norm_eps, L->norm_unit_offset, yt);
+        } else {
+            memcpy(yt, mlp, sizeof(float) * H);
+        }
         if (j->ids) memcpy(j->ids + (uint64_t)t * K, ids, sizeof(int32_t) * K);
         if (j->w) memcpy(j->w + (uint64_t)t * K, w, sizeof(float) * K);
     }
-    free(x); free(mlp); free(out); free(sg); free(su); free(ids); free(w);
+    free(x); free(xe); free(mlp); free(out); free(tmp); free(sg); free(su); free(ids); free(w);
     return NULL;
 }
 
 /* Tokens are independent, so splitting them over threads does not change
  * any result. */
-int mo_moe_layer(const mo_layer_t* L, const uint16_t* x_bf16, uint32_t tokens,
+int mo_moe_block(const mo_layer_t* L, const uint16_t* x_bf16, const float* hidden, uint32_t tokens,
                  float* y, int32_t* ids, float* w, uint32_t threads, uint32_t* ties) {
     if (!L || !x_bf16 || !y || L->top_k == 0 || L->top_k > L->experts) return 0;
+    if (L->pre_norm2 && !hidden) return 0;
     if (threads == 0) threads = 1;
     if (threads > tokens) threads = tokens ? tokens : 1;
     mo_layer_job* jobs = (mo_layer_job*)calloc(threads, sizeof(mo_layer_job));
     pthread_t* th = (pthread_t*)calloc(threads, sizeof(pthread_t));
     if (!jobs || !th) { free(jobs); free(th); return 0; }
     for (uint32_t i = 0; i < threads; ++i) {
-        jobs[i].L = L; jobs[i].x_bf16 = x_bf16; jobs[i].y = y; jobs[i].ids = ids; jobs[i].w = w;
+        jobs[i].L = L; jobs[i].x_bf16 = x_bf16; jobs[i].hidden = hidden;
+        jobs[i].y = y; jobs[i].ids = ids; jobs[i].w = w;
         jobs[i].t0 = (uint32_t)((uint64_t)tokens * i / threads);
         jobs[i].t1 = (uint32_t)((uint64_t)tokens * (i + 1) / threads);
         if (i > 0) pthread_create(&th[i], NULL, mo_layer_worker, &jobs[i]);
@@ -401,4 +491,9 @@ int mo_moe_layer(const mo_layer_t* L, const uint16_t* x_bf16, uint32_t tokens,
     free(jobs);
     free(th);
     return ok;
+}
+
+int mo_moe_layer(const mo_layer_t* L, const uint16_t* x_bf16, uint32_t tokens,
+                 float* y, int32_t* ids, float* w, uint32_t threads, uint32_t* ties) {
+    return mo_moe_block(L, x_bf16, NULL, tokens, y, ids, w, threads, ties);
 }

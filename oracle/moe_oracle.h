@@ -39,6 +39,18 @@ typedef struct {
     const uint8_t* shared_down;
     uint32_t n_group;        /* group limit of sigmoid routers: groups ... */
     uint32_t topk_group;     /* ... of which this many keep their scores; 0 = none */
+    /* Optional parts of Gemma-style MoE blocks around the experts; zero /
+     * NULL = absent, which is the plain layer above. */
+    int32_t activation;      /* 0 SiLU, 1 GELU (erf), 2 GELU (tanh form) */
+    int32_t norm_unit_offset;      /* RMSNorm multiplies by (1 + w) instead of w */
+    float norm_eps;                /* RMSNorm epsilon; <= 0 means 1e-6 */
+    const float* pre_norm2;        /* [H] routed experts and router read RMSNorm(hidden) */
+    const float* post_norm1;       /* [H] RMSNorm of the shared expert's output */
+    const float* post_norm2;       /* [H] RMSNorm of each routed expert's output */
+    const float* post_norm;        /* [H] RMSNorm of the block output */
+    const float* down_scale;       /* 1 (all experts), E (per expert) or E*H (per element) */
+    uint64_t down_scale_count;
+    const uint16_t* shared_gate_inp;  /* [H] bf16: shared expert x sigmoid(row . x) */
 } mo_layer_t;
 
 float mo_e8m0_to_f32(uint8_t v);
@@ -46,6 +58,8 @@ float mo_mxfp4_value(uint8_t code);
 float mo_mxfp4_dot_row(const uint8_t* packed, const float* x, uint32_t cols);
 float mo_bf16_dot_row(const uint16_t* w, const float* x, uint32_t cols);
 float mo_silu(float x);
+float mo_gated_activation(int32_t mode, float gate, float up);
+int mo_rmsnorm(const float* in, const float* w, uint32_t n, float eps, int32_t unit_offset, float* out);
 void mo_router_scores(const mo_layer_t* L, const float* x, float* scores);
 int mo_router_topk(const mo_layer_t* L, const float* x, int32_t* ids, float* w, uint32_t* ties);
 int mo_group_tokens_by_expert(const mo_assignment_t* a, uint32_t n, mo_assignment_t* sorted,
@@ -54,6 +68,10 @@ int mo_expert_triplet(const uint8_t* gate, const uint8_t* up, const uint8_t* dow
                       const float* x, uint32_t hidden, uint32_t intermediate,
                       float* scratch_gate, float* scratch_up, float* out);
 int mo_moe_layer(const mo_layer_t* L, const uint16_t* x_bf16, uint32_t tokens,
+                 float* y, int32_t* ids, float* w, uint32_t threads, uint32_t* ties);
+/* The layer with the residual stream `hidden` [T x H] beside its normed
+ * form x (needed only with pre_norm2); y = what the block adds to hidden. */
+int mo_moe_block(const mo_layer_t* L, const uint16_t* x_bf16, const float* hidden, uint32_t tokens,
                  float* y, int32_t* ids, float* w, uint32_t threads, uint32_t* ties);
 
 #ifdef __cplusplus

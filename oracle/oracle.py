@@ -14,7 +14,9 @@ from __future__ import annotations
 import ctypes as C
 import os
 import subprocess
+from dataclasses import dataclass
 from pathlib import Path
+from typing import Optional
 
 import numpy as np
 
@@ -50,13 +52,22 @@ class MoLayer(C.Structure):
                 ("top_k", C.c_uint32), ("score_sigmoid", C.c_int32), ("norm_topk", C.c_int32),
                 ("routed_scale", C.c_float), ("router_bf16", _u16p), ("gate", _u8p), ("up", _u8p),
                 ("down", _u8p), ("shared_gate", _u8p), ("shared_up", _u8p), ("shared_down", _u8p),
-                ("n_group", C.c_uint32), ("topk_group", C.c_uint32)]
+                ("n_group", C.c_uint32), ("topk_group", C.c_uint32),
+                ("activation", C.c_int32), ("norm_unit_offset", C.c_int32), ("norm_eps", C.c_float),
+                ("pre_norm2", _f32p), ("post_norm1", _f32p), ("post_norm2", _f32p), ("post_norm", _f32p),
+                ("down_scale", _f32p), ("down_scale_count", C.c_uint64), ("shared_gate_inp", _u16p)]
 
 
 class RefLayer(C.Structure):
     _fields_ = [("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("experts", C.c_uint32),
                 ("top_k", C.c_uint32), ("router_bf16", _u16p), ("gate", _u8p), ("up", _u8p),
                 ("down", _u8p), ("shared_gate", _u8p), ("shared_up", _u8p), ("shared_down", _u8p)]
+
+
+class RefBlock(C.Structure):
+    _fields_ = [("base", RefLayer), ("eps", C.c_float), ("pre_norm2", _f32p), ("post_norm1", _f32p),
+                ("post_norm2", _f32p), ("post_norm", _f32p), ("down_scale", _f32p),
+                ("down_scale_count", C.c_uint64), ("shared_gate_inp", _u16p)]
 
 
 class Assignment(C.Structure):
@@ -71,6 +82,35 @@ class Batch(C.Structure):
 
 def _c(a, dtype):
     return None if a is None else np.ascontiguousarray(a, dtype=dtype)
+
+
+@dataclass
+class Block:
+    """Optional parts of a Gemma-style MoE block around the experts
+    (generation_mlp.cpp.inc:94-104, 145-175, 234-250, 380-429, 478-570);
+    the defaults are the plain layer.  Norm weights and scales are float32;
+    `shared_gate_inp` is a bf16 row (uint16)."""
+    activation: int = 0                  # 0 SiLU, 1 GELU (erf), 2 GELU (tanh form)
+    unit_offset: bool = False            # RMSNorm by (1 + w): Gemma models
+    eps: float = 1e-6
+    pre_norm2: Optional[np.ndarray] = None    # [H] routed experts read RMSNorm(hidden)
+    post_norm1: Optional[np.ndarray] = None   # [H] shared expert output
+    post_norm2: Optional[np.ndarray] = None   # [H] each routed expert's output
+    post_norm: Optional[np.ndarray] = None    # [H] block output
+    down_scale: Optional[np.ndarray] = None   # [1], [E] or [E*H]
+    shared_gate_inp: Optional[np.ndarray] = None  # [H] bf16
+
+    def metadata(self) -> list[str]:
+        """GGUF metadata entries through which the reference learns the
+        activation and the unit offset (raw_forward_utils.cpp.inc:322-350)."""
+        parts = []
+        if self.activation == 2:
+            parts.append('"hidden_activation":"gelu_pytorch_tanh"')
+        elif self.activation == 1:
+            parts.append('"hidden_activation":"gelu"')
+        if self.unit_offset:
+            parts.append('"general.architecture":"gemma3"')
+        return parts
 
 
 class Port:
@@ -100,6 +140,13 @@ class Port:
         L.mo_moe_layer.restype = C.c_int
         L.mo_moe_layer.argtypes = [C.POINTER(MoLayer), _u16p, C.c_uint32, _f32p, _i32p, _f32p,
                                    C.c_uint32, _u32p]
+        L.mo_moe_block.restype = C.c_int
+        L.mo_moe_block.argtypes = [C.POINTER(MoLayer), _u16p, _f32p, C.c_uint32, _f32p, _i32p, _f32p,
+                                   C.c_uint32, _u32p]
+        L.mo_gated_activation.restype = C.c_float
+        L.mo_gated_activation.argtypes = [C.c_int32, C.c_float, C.c_float]
+        L.mo_rmsnorm.restype = C.c_int
+        L.mo_rmsnorm.argtypes = [_f32p, _f32p, C.c_uint32, C.c_float, C.c_int32, _f32p]
 
     def _layer(self, li, score_sigmoid=0, norm_topk=None, routed_scale=1.0, n_group=0, topk_group=0):
         s = li.shape
@@ -126,6 +173,35 @@ class Port:
                                    threads or (os.cpu_count() or 1), C.byref(ties))
         if not ok:
             raise RuntimeError("oracle layer failed")
+        return y, ids, w, ties.value
+
+    def moe_block(self, li, blk: Block, hidden=None, x=None, threads: int = 0, **kw):
+        """The layer with the block's optional parts; `hidden` [T x H] f32 is
+        the residual stream (needed with pre_norm2).  Returns y (what the
+        block adds to hidden), ids, w, ties."""
+        x = _c(li.x if x is None else x, np.uint16)
+        T = x.shape[0]
+        L, keep = self._layer(li, **kw)
+        H, K = li.shape.hidden, li.shape.top_k
+        keep.update(pn2=_c(blk.pre_norm2, np.float32), n1=_c(blk.post_norm1, np.float32),
+                    n2=_c(blk.post_norm2, np.float32), n=_c(blk.post_norm, np.float32),
+                    ds=_c(blk.down_scale, np.float32), sgi=_c(blk.shared_gate_inp, np.uint16),
+                    hid=_c(hidden, np.float32))
+        L.activation, L.norm_unit_offset, L.norm_eps = int(blk.activation), int(blk.unit_offset), float(blk.eps)
+        L.pre_norm2, L.post_norm1 = _p(keep["pn2"], _f32p), _p(keep["n1"], _f32p)
+        L.post_norm2, L.post_norm = _p(keep["n2"], _f32p), _p(keep["n"], _f32p)
+        L.down_scale = _p(keep["ds"], _f32p)
+        L.down_scale_count = 0 if keep["ds"] is None else keep["ds"].size
+        L.shared_gate_inp = _p(keep["sgi"], _u16p)
+        y = np.zeros((T, H), np.float32)
+        ids = np.zeros((T, K), np.int32)
+        w = np.zeros((T, K), np.float32)
+        ties = C.c_uint32(0)
+        ok = self.lib.mo_moe_block(C.byref(L), _p(x, _u16p), _p(keep["hid"], _f32p), T, _p(y, _f32p),
+                                   _p(ids, _i32p), _p(w, _f32p), threads or (os.cpu_count() or 1),
+                                   C.byref(ties))
+        if not ok:
+            raise RuntimeError("oracle block failed")
         return y, ids, w, ties.value
 
     def router_topk(self, li, x=None, **kw):
@@ -189,6 +265,13 @@ class Ref:
                                       C.c_uint32, _i32p, _f32p, _f32p]
         L.ref_moe_layer.restype = C.c_int
         L.ref_moe_layer.argtypes = [C.c_void_p, C.POINTER(RefLayer), _u16p, C.c_uint32, _f32p, _i32p, _f32p]
+        L.ref_moe_block.restype = C.c_int
+        L.ref_moe_block.argtypes = [C.c_void_p, C.POINTER(RefBlock), _u16p, _f32p, C.c_uint32, _f32p, _i32p,
+                                    _f32p]
+        L.ref_gated_activation.restype = C.c_float
+        L.ref_gated_activation.argtypes = [C.c_int32, C.c_float, C.c_float]
+        L.ref_rmsnorm.restype = C.c_int
+        L.ref_rmsnorm.argtypes = [C.c_void_p, _f32p, C.c_uint32, _f32p, C.c_float, _f32p]
         L.ref_group_tokens_by_expert.restype = C.c_int
         L.ref_group_tokens_by_expert.argtypes = [C.POINTER(Assignment), C.c_uint32, C.POINTER(Assignment),
                                                  C.POINTER(Batch), C.c_uint32, _u32p]
@@ -216,6 +299,32 @@ class Ref:
         if not self.lib.ref_moe_layer(self.engine, C.byref(d), _p(x, _u16p), T, _p(y, _f32p), _p(ids, _i32p),
                                       _p(w, _f32p)):
             raise RuntimeError("reference layer failed")
+        return y, ids, w
+
+    def moe_block(self, li, blk: Block, hidden=None, x=None):
+        """The block with its optional parts (the engine's metadata must
+        carry blk.metadata()); returns y (what the block adds to hidden),
+        ids, w."""
+        s = li.shape
+        x = _c(li.x if x is None else x, np.uint16)
+        T = x.shape[0]
+        keep = [_c(li.router, np.uint16), _c(li.gate, np.uint8), _c(li.up, np.uint8), _c(li.down, np.uint8),
+                _c(li.shared_gate, np.uint8), _c(li.shared_up, np.uint8), _c(li.shared_down, np.uint8),
+                _c(blk.pre_norm2, np.float32), _c(blk.post_norm1, np.float32), _c(blk.post_norm2, np.float32),
+                _c(blk.post_norm, np.float32), _c(blk.down_scale, np.float32),
+                _c(blk.shared_gate_inp, np.uint16), _c(hidden, np.float32)]
+        base = RefLayer(s.hidden, s.intermediate, s.experts, s.top_k, _p(keep[0], _u16p), _p(keep[1], _u8p),
+                        _p(keep[2], _u8p), _p(keep[3], _u8p), _p(keep[4], _u8p), _p(keep[5], _u8p),
+                        _p(keep[6], _u8p))
+        d = RefBlock(base, float(blk.eps), _p(keep[7], _f32p), _p(keep[8], _f32p), _p(keep[9], _f32p),
+                     _p(keep[10], _f32p), _p(keep[11], _f32p), 0 if keep[11] is None else keep[11].size,
+                     _p(keep[12], _u16p))
+        y = np.zeros((T, s.hidden), np.float32)
+        ids = np.zeros((T, s.top_k), np.int32)
+        w = np.zeros((T, s.top_k), np.float32)
+        if not self.lib.ref_moe_block(self.engine, C.byref(d), _p(x, _u16p), _p(keep[13], _f32p), T,
+                                      _p(y, _f32p), _p(ids, _i32p), _p(w, _f32p)):
+            raise RuntimeError("reference block failed")
         return y, ids, w
 
     def router_topk(self, li, x=None):
@@ -263,10 +372,14 @@ def bf16_to_f32(b: np.ndarray) -> np.ndarray:
 
 
 def metadata_json(top_k: int, norm_topk: bool = False, sigmoid: bool = False,
-                  routed_scale: float = 1.0, n_group: int = 0, topk_group: int = 0) -> str:
+                  routed_scale: float = 1.0, n_group: int = 0, topk_group: int = 0,
+                  block: Optional[Block] = None) -> str:
     """GGUF metadata keys the reference router reads
-    (generation_router.cpp.inc:361-558)."""
+    (generation_router.cpp.inc:361-558), plus the block's activation and
+    norm style."""
     parts = [f'"num_experts_per_tok":{int(top_k)}', f'"norm_topk_prob":{"true" if norm_topk else "false"}']
+    if block is not None:
+        parts += block.metadata()
     if sigmoid:
         parts.append('"scoring_func":"sigmoid"')
         if routed_scale != 1.0:

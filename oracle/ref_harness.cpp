@@ -19,6 +19,9 @@
 //   down       moe_parallel_rows(k*H) -> moe_dot_gguf_mxfp4_row
 //                                             generation_mlp.cpp.inc:1378-1413
 //   combine    moe_axpy_f32 in router order   generation_mlp.cpp.inc:1415-1431
+// ref_moe_block adds the optional parts of Gemma-style blocks around the
+// experts through the reference's own functions for them (the MoE pre-norm,
+// post-FFW norms 1/2/final, expert down scales, shared-expert gate).
 // Weights are passed in the reference's GGUF MXFP4 byte layout (17-byte
 // blocks per 32 K-elements, tensor_layout.cpp.inc:174-176).
 #include "moe_engine/src/moe_pc_engine.cpp"
@@ -243,6 +246,183 @@ int ref_moe_layer(void* eng, const ref_layer_desc* d, const uint16_t* x_bf16,
         if (out_w) for (uint32_t j = 0; j < K; ++j) out_w[(uint64_t)t * K + j] = w[j];
     }
     return 1;
+}
+
+// Optional parts of Gemma-style MoE blocks around the experts.  Each is
+// registered under the first tensor-name suffix the reference looks up for
+// it, exactly where moe_map_layer_common_tensor (generation_mlp.cpp.inc:25-62)
+// finds its cached tensors; absent parts are removed from that cache.
+typedef struct {
+    ref_layer_desc base;
+    float eps;                     // RMSNorm epsilon (the model's rms_norm_eps)
+    const float* pre_norm2;        // [H]  pre_ffw_norm_2.weight
+    const float* post_norm1;       // [H]  post_ffw_norm_1.weight
+    const float* post_norm2;       // [H]  post_ffw_norm_2.weight
+    const float* post_norm;        // [H]  post_ffw_norm.weight
+    const float* down_scale;       // [down_scale_count]  ffn_down_exps.scale
+    uint64_t down_scale_count;
+    const uint16_t* shared_gate_inp;  // [H] bf16  shared_expert_gate.weight
+} ref_block_desc;
+
+namespace {
+
+uint64_t common_key(int32_t layer, const char* suffix) {
+    return ((uint64_t)(uint32_t)layer << 32) | moe_fnv1a_hash_string(suffix) | 0x80000000ull;
+}
+
+void put_common(moe_pc_engine* engine, int32_t layer, const char* suffix, const void* data, uint64_t count,
+                uint32_t rows, uint32_t cols, uint8_t encoding, uint8_t format) {
+    std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
+    const uint64_t key = common_key(layer, suffix);
+    if (!data) {
+        engine->raw_tensor_cache.erase(key);
+        return;
+    }
+    moe_raw_tensor_cache_entry e{};
+    e.base = reinterpret_cast<const uint8_t*>(data);
+    e.bytes = count * (encoding == moe_RAW_SCALAR_F32 ? 4ull : 2ull);
+    e.rows = rows;
+    e.cols = cols;
+    e.scalar_encoding = encoding;
+    e.weight_format = format;
+    engine->raw_tensor_cache[key] = e;
+}
+
+}  // namespace
+
+// The MoE block for T tokens, one token at a time, composed from the
+// reference's own functions in moe_layer_moe_mlp_f32's order
+// (generation_mlp.cpp.inc:776-1442): the routed input is
+// moe_layer_moe_norm_f32(hidden) when pre_ffw_norm_2 exists (:826-831), the
+// shared expert is gated by moe_layer_shared_expert_gate_f32 and normalised
+// by moe_layer_post_ffw_norm1_f32 (:849-859), each routed output goes
+// through moe_layer_post_ffw_norm2_f32 and moe_layer_apply_expert_down_scale_f32
+// before moe_axpy_f32 (:1417-1430), and the block output through
+// moe_layer_post_ffw_norm_f32 (moe_add_mlp_residual_f32 :572-594).  The
+// activation and the norms' unit offset come from the engine metadata.
+// y_f32 receives what the block adds to `hidden`.
+int ref_moe_block(void* eng, const ref_block_desc* bd, const uint16_t* x_bf16, const float* hidden,
+                  uint32_t tokens, float* y_f32, int32_t* out_ids, float* out_w) {
+    mxcsr_guard guard;
+    moe_pc_engine* engine = static_cast<moe_pc_engine*>(eng);
+    if (!engine || !bd || !x_bf16 || !y_f32) return 0;
+    if (bd->pre_norm2 && !hidden) return 0;
+    const ref_layer_desc* d = &bd->base;
+    const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, K = d->top_k;
+    const int32_t layer = 0;
+    const uint64_t row_h = (uint64_t)((H + 31u) / 32u) * 17u;
+    const uint64_t row_i = (uint64_t)((I + 31u) / 32u) * 17u;
+    const uint64_t expert_gu_bytes = (uint64_t)I * row_h;
+    const uint64_t expert_d_bytes = (uint64_t)H * row_i;
+    const uint8_t F32 = moe_RAW_SCALAR_F32, BF16 = moe_RAW_SCALAR_BF16;
+    const uint8_t RAW_F32 = moe_WEIGHT_ENCODING_RAW_FP32, RAW_BF16 = moe_WEIGHT_ENCODING_RAW_BF16;
+    {
+        moe_raw_tensor_cache_entry r{};
+        r.base = reinterpret_cast<const uint8_t*>(d->router_bf16);
+        r.bytes = (uint64_t)E * H * 2ull;
+        r.rows = E;
+        r.cols = H;
+        r.scalar_encoding = BF16;
+        r.weight_format = RAW_BF16;
+        std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
+        engine->raw_tensor_cache[router_cache_key(layer)] = r;
+    }
+    put_common(engine, layer, "pre_ffw_norm_2.weight", bd->pre_norm2, H, H, 0, F32, RAW_F32);
+    put_common(engine, layer, "post_ffw_norm_1.weight", bd->post_norm1, H, H, 0, F32, RAW_F32);
+    put_common(engine, layer, "post_ffw_norm_2.weight", bd->post_norm2, H, H, 0, F32, RAW_F32);
+    put_common(engine, layer, "post_ffw_norm.weight", bd->post_norm, H, H, 0, F32, RAW_F32);
+    put_common(engine, layer, "ffn_down_exps.scale", bd->down_scale, bd->down_scale_count,
+               (uint32_t)bd->down_scale_count, 0, F32, RAW_F32);
+    put_common(engine, layer, "shared_expert_gate.weight", bd->shared_gate_inp, H, 1, H, BF16, RAW_BF16);
+    const int activation_mode = moe_engine_gelu_activation_mode(engine);
+    const float eps = bd->eps;
+
+    std::vector<float> x(H), xe(H), mlp(H), tmp(H), shared_gate(I), shared_out(H);
+    std::vector<float> gate_pool((uint64_t)K * I), out_pool((uint64_t)K * H);
+    std::vector<int> ids;
+    std::vector<float> w, logits;
+    std::vector<uint32_t> order;
+    for (uint32_t t = 0; t < tokens; ++t) {
+        for (uint32_t h = 0; h < H; ++h) x[h] = bf16_to_f32(x_bf16[(uint64_t)t * H + h]);
+        std::fill(mlp.begin(), mlp.end(), 0.0f);
+        const float* expert_input = x.data();
+        if (hidden && moe_layer_moe_norm_f32(engine, layer, hidden + (uint64_t)t * H, H, xe.data(), eps)) {
+            expert_input = xe.data();
+        }
+        if (d->shared_gate && d->shared_up && d->shared_down) {
+            if (!moe_parallel_rows(engine, I, 0, [&](uint32_t row) {
+                    const float g = moe_dot_gguf_mxfp4_row(d->shared_gate + row * row_h, x.data(), H);
+                    const float u = moe_dot_gguf_mxfp4_row(d->shared_up + row * row_h, x.data(), H);
+                    shared_gate[row] = moe_generation_gated_activation_cached(activation_mode, g, u);
+                    return 1;
+                })) return 0;
+            if (!moe_parallel_rows(engine, H, 0, [&](uint32_t row) {
+                    shared_out[row] = moe_dot_gguf_mxfp4_row(d->shared_down + row * row_i, shared_gate.data(), I);
+                    return 1;
+                })) return 0;
+            float g = 1.0f;
+            if (!moe_layer_shared_expert_gate_f32(engine, layer, x.data(), H, &g)) return 0;
+            const float* so = shared_out.data();
+            if (moe_layer_post_ffw_norm1_f32(engine, layer, shared_out.data(), H, tmp.data(), eps)) so = tmp.data();
+            for (uint32_t i = 0; i < H; ++i) mlp[i] += so[i] * g;
+        }
+        if (!moe_router_topk_f32(engine, layer, expert_input, H, E, K, &ids, &w, &logits, &order)) return 0;
+        if (ids.size() != K) return 0;
+        if (!moe_parallel_rows(engine, K * I, 0, [&](uint32_t flat_row) {
+                const uint32_t e = flat_row / I;
+                const uint32_t r = flat_row % I;
+                const uint64_t ex = (uint64_t)ids[e];
+                const float g = moe_dot_gguf_mxfp4_row(d->gate + ex * expert_gu_bytes + r * row_h, expert_input, H);
+                const float u = moe_dot_gguf_mxfp4_row(d->up + ex * expert_gu_bytes + r * row_h, expert_input, H);
+                gate_pool[(uint64_t)e * I + r] = moe_generation_gated_activation_cached(activation_mode, g, u);
+                return 1;
+            })) return 0;
+        if (!moe_parallel_rows(engine, K * H, 0, [&](uint32_t flat_row) {
+                const uint32_t e = flat_row / H;
+                const uint32_t r = flat_row % H;
+                const uint64_t ex = (uint64_t)ids[e];
+                out_pool[(uint64_t)e * H + r] = moe_dot_gguf_mxfp4_row(
+                    d->down + ex * expert_d_bytes + r * row_i, gate_pool.data() + (uint64_t)e * I, I);
+                return 1;
+            })) return 0;
+        for (uint32_t e = 0; e < K; ++e) {
+            float* out = out_pool.data() + (uint64_t)e * H;
+            if (moe_layer_post_ffw_norm2_f32(engine, layer, out, H, tmp.data(), eps)) {
+                std::memcpy(out, tmp.data(), (size_t)H * sizeof(float));
+            }
+            if (!moe_layer_apply_expert_down_scale_f32(engine, layer, ids[e], E, out, H)) return 0;
+            moe_axpy_f32(mlp.data(), out, w[e], H);
+        }
+        float* yt = y_f32 + (uint64_t)t * H;
+        if (!moe_layer_post_ffw_norm_f32(engine, layer, mlp.data(), H, yt, eps)) {
+            std::memcpy(yt, mlp.data(), (size_t)H * sizeof(float));
+        }
+        if (out_ids) for (uint32_t j = 0; j < K; ++j) out_ids[(uint64_t)t * K + j] = ids[j];
+        if (out_w) for (uint32_t j = 0; j < K; ++j) out_w[(uint64_t)t * K + j] = w[j];
+    }
+    return 1;
+}
+
+// The reference's gated activation for an explicit mode
+// (generation_mlp.cpp.inc:99-104) and RMSNorm with a weight vector
+// (moe_apply_rmsnorm_common_weight_f32 :145-175; the unit offset follows
+// the engine's metadata), for direct known-answer tables.
+float ref_gated_activation(int32_t mode, float gate, float up) {
+    mxcsr_guard guard;
+    return moe_generation_gated_activation_cached(mode, gate, up);
+}
+
+int ref_rmsnorm(void* eng, const float* w, uint32_t n, const float* in, float eps, float* out) {
+    mxcsr_guard guard;
+    moe_pc_engine* engine = static_cast<moe_pc_engine*>(eng);
+    moe_raw_tensor_cache_entry e{};
+    e.base = reinterpret_cast<const uint8_t*>(w);
+    e.bytes = (uint64_t)n * 4ull;
+    e.rows = n;
+    e.cols = 0;
+    e.scalar_encoding = moe_RAW_SCALAR_F32;
+    e.weight_format = moe_WEIGHT_ENCODING_RAW_FP32;
+    return moe_apply_rmsnorm_common_weight_f32(engine, e, in, n, out, eps);
 }
 
 // The reference's public grouping utility (token_grouping.cpp.inc:1-83) is

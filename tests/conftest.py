@@ -71,3 +71,13 @@ def layer_from_golden(synth, g):
         li = synth.make_layer(shape, seed=int(g["seed"]), tokens=int(g["tokens"]))
     assert li.digest() == str(g["digest"]), "regenerated inputs differ from the golden record"
     return li
+
+
+BLOCK_PARTS = ("pre_norm2", "post_norm1", "post_norm2", "post_norm", "down_scale", "shared_gate_inp")
+
+
+def block_from_golden(oracle_mod, g):
+    """The block options and residual-stream input of a block fixture."""
+    blk = oracle_mod.Block(activation=int(g["activation"]), unit_offset=bool(int(g["unit_offset"])),
+                           eps=float(g["eps"]), **{k: g[k] for k in BLOCK_PARTS if k in g})
+    return blk, g["hidden_in"]

@@ -108,6 +108,98 @@ def group_limit_case(name, experts, n_group, topk_group, top_k, seed):
     print(name)
 
 
+# name -> (shape, seed, options): Gemma-style MoE blocks -- the optional
+# activation, norms, down scales and shared-expert gate around the experts
+# (generation_mlp.cpp.inc:94-104, 145-175, 234-250, 380-429, 478-570)
+BLOCK_CASES = {
+    # everything on: GELU (tanh), Gemma norms, routed input from RMSNorm(hidden),
+    # per-expert down scale, gated shared expert
+    "block_gemma": (synth.small_shape(name="block_gemma", shared=True, top_k=3, experts=12, tokens=16), 31,
+                    dict(activation=2, unit_offset=True, eps=1e-6, pre_norm2=True, post_norm1=True,
+                         post_norm2=True, post_norm=True, down_scale="expert", shared_gate_inp=True)),
+    # GELU (erf), plain norms on the routed outputs only, one global scale
+    "block_gelu_erf": (synth.small_shape(name="block_gelu_erf", top_k=2, experts=8, tokens=16), 32,
+                       dict(activation=1, eps=1e-5, post_norm2=True, down_scale="global")),
+    # SiLU, ragged shape, a scale per (expert, element), output norm only
+    "block_silu_vector": (synth.small_shape(name="block_silu_vector", hidden=80, intermediate=100, top_k=3,
+                                            experts=8, tokens=20), 33,
+                          dict(activation=0, post_norm=True, down_scale="element")),
+}
+
+
+def block_inputs(shape, seed, opts):
+    """Seeded block tensors: norm weights ~N(0, 0.3), scales in [0.5, 2),
+    the shared gate row bf16 ~N(0, 0.05), hidden ~N(0, 4)."""
+    rng = np.random.default_rng(seed)
+    H, E = shape.hidden, shape.experts
+    vec = lambda: (rng.standard_normal(H) * 0.3).astype(np.float32)
+    scale = {"global": 1, "expert": E, "element": E * H}.get(opts.get("down_scale"))
+    gate_row = None
+    if opts.get("shared_gate_inp"):
+        gate_row = ((rng.standard_normal(H) * 0.05).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    blk = oracle.Block(activation=opts.get("activation", 0), unit_offset=opts.get("unit_offset", False),
+                       eps=opts.get("eps", 1e-6),
+                       pre_norm2=vec() if opts.get("pre_norm2") else None,
+                       post_norm1=vec() if opts.get("post_norm1") else None,
+                       post_norm2=vec() if opts.get("post_norm2") else None,
+                       post_norm=vec() if opts.get("post_norm") else None,
+                       down_scale=rng.uniform(0.5, 2.0, scale).astype(np.float32) if scale else None,
+                       shared_gate_inp=gate_row)
+    hidden = (rng.standard_normal((shape.tokens, H)) * 2.0).astype(np.float32)
+    return blk, hidden
+
+
+def block_case(name, shape, seed, opts):
+    li = synth.make_layer(shape, seed=seed)
+    blk, hidden = block_inputs(shape, seed + 1000, opts)
+    ref = oracle.Ref(oracle.metadata_json(shape.top_k, norm_topk=shape.norm_topk, block=blk))
+    try:
+        y, ids, w = ref.moe_block(li, blk, hidden=hidden)
+    finally:
+        ref.close()
+    rec = dict(hidden=shape.hidden, intermediate=shape.intermediate, experts=shape.experts, top_k=shape.top_k,
+               tokens=shape.tokens, shared=int(shape.shared), norm_topk=int(shape.norm_topk), skew="", seed=seed,
+               digest=li.digest(), ids=ids, w=w, y=y, router=li.router, gate=li.gate, up=li.up, down=li.down,
+               x=li.x, hidden_in=hidden, activation=blk.activation, unit_offset=int(blk.unit_offset), eps=blk.eps)
+    if shape.shared:
+        rec.update(shared_gate=li.shared_gate, shared_up=li.shared_up, shared_down=li.shared_down)
+    for k in ("pre_norm2", "post_norm1", "post_norm2", "post_norm", "down_scale", "shared_gate_inp"):
+        if getattr(blk, k) is not None:
+            rec[k] = getattr(blk, k)
+    np.savez_compressed(OUT / f"{name}.npz", **rec)
+    print(name)
+
+
+def block_tables():
+    """Known answers of the reference's gated activations (GELU erf and tanh
+    forms) and of its RMSNorm, plain and with the Gemma unit offset."""
+    rng = np.random.default_rng(34)
+    xs = np.concatenate([rng.standard_normal(300).astype(np.float32) * 5,
+                         np.array([0.0, -0.0, 20.0, -20.0, 1e-30, -1e-30, 9.0, -9.0], np.float32)])
+    ups = rng.standard_normal(xs.size).astype(np.float32)
+    norm_in = [(rng.standard_normal(n) * s).astype(np.float32) for n, s in ((64, 1.0), (80, 30.0), (7, 1e-3))]
+    norm_w = [(rng.standard_normal(v.size) * 0.3).astype(np.float32) for v in norm_in]
+    rec = dict(act_x=xs, act_up=ups)
+    ref = oracle.Ref(oracle.metadata_json(2))
+    gemma = oracle.Ref(oracle.metadata_json(2, block=oracle.Block(unit_offset=True)))
+    try:
+        for mode in (0, 1, 2):
+            rec[f"act{mode}"] = np.array([ref.lib.ref_gated_activation(mode, float(a), float(u))
+                                          for a, u in zip(xs, ups)], np.float32)
+        P = lambda a: a.ctypes.data_as(oracle._f32p)
+        for i, (v, w) in enumerate(zip(norm_in, norm_w)):
+            for tag, r in (("plain", ref), ("unit", gemma)):
+                out = np.zeros_like(v)
+                assert r.lib.ref_rmsnorm(r.engine, P(w), v.size, P(v), 1e-6, P(out))
+                rec[f"norm{i}_{tag}"] = out
+            rec[f"norm{i}_in"], rec[f"norm{i}_w"] = v, w
+    finally:
+        ref.close()
+        gemma.close()
+    np.savez_compressed(OUT / "block_tables.npz", **rec)
+    print("block_tables")
+
+
 def grouping_case():
     rng = np.random.default_rng(11)
     n = 300
@@ -160,6 +252,11 @@ def main(only=None):
     for name, (shape, seed, tokens, store) in LAYER_CASES.items():
         if want("layer_" + name):
             layer_case(name, shape, seed, tokens, store)
+    for name, (shape, seed, opts) in BLOCK_CASES.items():
+        if want(name):
+            block_case(name, shape, seed, opts)
+    if want("block_tables"):
+        block_tables()
 
 
 if __name__ == "__main__":
