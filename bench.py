@@ -1,4 +1,4 @@
-"""Benchmark of the B200 MoE expert-FFN layer (the BASELINE.json metric).
+"""Benchmark of the B200 MoE expert-FFN layer: MoE-layer tokens/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--config 1] [--tokens 256]

@@ -79,7 +79,8 @@ def test_create_without_gpu_fails_loudly(lib, pkg):
 
 
 CPP_CLIENT = r"""
-// A C++ caller in the style of the binding in INTEGRATION.md.
+// A C++ caller in the style of the reference engine's binding: create an
+// engine, report its error text, no exceptions across the boundary.
 #include <cstdio>
 #include <cstring>
 #include "moe_b200.h"
