@@ -212,3 +212,37 @@ def test_port_matches_reference_block_fresh_seeds(seed, ref_lib, port, synth):
         assert np.array_equal(i1, i2)
         assert np.array_equal(bits(w1), bits(w2))
         assert np.array_equal(bits(y1), bits(y2))
+
+
+EXTREME_SHAPES = {
+    # one 8-element partial block per row, a one-row intermediate
+    "h8_i1": dict(hidden=8, intermediate=1, experts=4, top_k=2, tokens=5),
+    # a single expert (softmax over one score), with the shared expert
+    "e1_shared": dict(hidden=40, intermediate=33, experts=1, top_k=1, tokens=3, shared=True),
+    # every expert selected, renormalised
+    "k_eq_e": dict(hidden=64, intermediate=32, experts=6, top_k=6, tokens=4, norm_topk=True),
+    # one token, 32 of 40 experts (the largest k), ragged blocks on both sides
+    "t1_k32": dict(hidden=72, intermediate=40, experts=40, top_k=32, tokens=1),
+}
+
+
+@pytest.mark.parametrize("name", sorted(EXTREME_SHAPES))
+def test_port_matches_reference_extreme_shapes(name, ref_lib, port, synth):
+    """The oracle the GPU tests compare against, pinned to the compiled
+    reference where shapes are at their limits: partial 32-element blocks,
+    one intermediate row, one expert, k = E, k = 32, one token."""
+    shape = synth.small_shape(name=name, **EXTREME_SHAPES[name])
+    li = synth.make_layer(shape, seed=51)
+    ref = ref_lib.Ref(ref_lib.metadata_json(shape.top_k, norm_topk=shape.norm_topk))
+    try:
+        y2, i2, w2 = ref.moe_layer(li)
+        _, _, s2 = ref.router_topk(li)
+    finally:
+        ref.close()
+    y1, i1, w1, ties = port.moe_layer(li)
+    _, _, s1, _ = port.router_topk(li)
+    assert ties == 0
+    assert np.array_equal(bits(s1), bits(s2))
+    assert np.array_equal(i1, i2)
+    assert np.array_equal(bits(w1), bits(w2))
+    assert np.array_equal(bits(y1), bits(y2))
