@@ -387,7 +387,7 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
         step_host()
     dist.barrier()
     torch.cuda.synchronize()
-    e2e_steps = max(50, args.steps)  # host wall clock: a longer window for a steadier figure
+    e2e_steps = max(200, args.steps)  # host wall clock: a longer window for a steadier figure
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         step_host()
@@ -555,7 +555,7 @@ def main():
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    e2e_steps = max(50, args.steps)  # host wall clock: a longer window for a steadier figure
+    e2e_steps = max(200, args.steps)  # host wall clock: a longer window for a steadier figure
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         step_host()
