@@ -281,9 +281,17 @@ def calibrate_placement(shape, li, rank, world, dist, tokens):
     top = np.argsort(-logits, axis=1, kind="stable")[:, :shape.top_k]
     counts = torch.tensor(np.bincount(top.ravel(), minlength=shape.experts).astype(np.float64), device="cuda")
     dist.all_reduce(counts)
-    counts = counts.cpu().numpy()
-    E = shape.experts
-    share = counts.sum() / world
+    return place_replicas(counts.cpu().numpy(), world)
+
+
+def place_replicas(counts, world):
+    """Replica placement from per-expert routing counts: an expert whose load
+    exceeds one rank's share gets that many replicas (at most `world`), each
+    carrying an equal part of its load; replicas go largest first to the
+    least-loaded rank not yet holding that expert (lower rank on ties).
+    Returns (replica ranks per expert, planned max / mean rank load)."""
+    E = len(counts)
+    share = float(np.sum(counts)) / world
     reps = [int(min(world, max(1, np.ceil(c / max(share, 1.0))))) for c in counts]
     items = sorted(((counts[e] / reps[e], e) for e in range(E) for _ in range(reps[e])), key=lambda t: (-t[0], t[1]))
     load = np.zeros(world)

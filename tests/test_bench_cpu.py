@@ -41,3 +41,40 @@ def test_weight_copies_keep_reuse_distance_past_l2():
         n = bench.weight_copies(touched)
         assert 1 <= n <= bench.MAX_COPIES
         assert n * touched >= 2 * bench.L2_BYTES or n == bench.MAX_COPIES
+
+
+def test_replica_placement_invariants():
+    """The bench's expert placement for multi-GPU runs: every expert on 1 to
+    world distinct ranks, hot experts split by their load, every rank used
+    when there are enough replicas, and no rank above the mean load by more
+    than one replica's share (greedy largest-first placement)."""
+    import importlib.util
+    import numpy as np
+    root = Path(__file__).resolve().parents[1]
+    spec = importlib.util.spec_from_file_location("bench_mod2", root / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    rng = np.random.default_rng(3)
+    for trial in range(60):
+        E = int(rng.choice([8, 32, 128, 256]))
+        world = int(rng.choice([1, 2, 4, 8]))
+        if trial % 2:
+            counts = (1.0 / np.arange(1, E + 1) ** 1.1) * 4096  # Zipf(1.1) loads
+            rng.shuffle(counts)
+        else:
+            counts = rng.integers(0, 200, E).astype(np.float64)
+        placement, imbalance = bench.place_replicas(counts, world)
+        assert len(placement) == E
+        share = counts.sum() / world
+        load = np.zeros(world)
+        for e, ranks in enumerate(placement):
+            assert 1 <= len(ranks) <= world and len(set(ranks)) == len(ranks)
+            assert all(0 <= q < world for q in ranks)
+            assert len(ranks) == min(world, max(1, int(np.ceil(counts[e] / max(share, 1.0)))))
+            for q in ranks:
+                load[q] += counts[e] / len(ranks)
+        if sum(len(r) for r in placement) >= world and counts.sum() > 0:
+            assert all(any(q in r for r in placement) for q in range(world))
+        biggest = max(counts[e] / len(r) for e, r in enumerate(placement))
+        assert load.max() <= load.mean() + biggest + 1e-9
+        assert abs(imbalance - load.max() / max(load.mean(), 1e-9)) < 1e-9
