@@ -210,9 +210,38 @@ static void mo_group_limit(const mo_layer_t* L, float* p, uint32_t* ties) {
  * bf16 row dot, then softmax with exp in double, the denominator summed in
  * double in expert order, and each score multiplied by (float)(1/denom); or
  * sigmoid 1/(1+exp(-l)) in float (:239-245) followed by the group limit. */
+/* Scaled router input (moe_prepare_scaled_router_input_f32,
+ * generation_router.cpp.inc:316-359), used when the layer has an
+ * ffn_gate_inp.scale tensor: x * norm * scale * (1 / sqrt(H)) with norm =
+ * 1 / sqrt(mean(x^2) + 1e-6) (sum of squares in double, fused as in the
+ * reference's build), one scale for every element or one per element; any
+ * other count scales by 1. */
+static void mo_scaled_router_input(const mo_layer_t* L, const float* x, float* out) {
+    const uint32_t H = L->hidden;
+    double ss = 0.0;
+    for (uint32_t i = 0; i < H; ++i) ss = fma((double)x[i], (double)x[i], ss);
+    const float norm = 1.0f / sqrtf((float)(ss / (double)H) + 1.0e-6f);
+    const float inv_sqrt_hidden = 1.0f / sqrtf((float)H);
+    for (uint32_t i = 0; i < H; ++i) {
+        float scale = 1.0f;
+        if (L->router_scale_count == 1u) scale = L->router_scale[0];
+        else if (L->router_scale_count >= H) scale = L->router_scale[i];
+        out[i] = x[i] * norm * scale * inv_sqrt_hidden;
+    }
+}
+
 static void mo_router_scores_t(const mo_layer_t* L, const float* x, float* p, uint32_t* ties) {
     const uint32_t E = L->experts, H = L->hidden;
+    float* xs = NULL;
+    if (L->router_scale && L->router_scale_count) {
+        xs = (float*)malloc(sizeof(float) * H);
+        if (xs) {
+            mo_scaled_router_input(L, x, xs);
+            x = xs;
+        }
+    }
     for (uint32_t e = 0; e < E; ++e) p[e] = mo_bf16_dot_row(L->router_bf16 + (uint64_t)e * H, x, H);
+    free(xs);
     if (L->score_sigmoid) {
         for (uint32_t e = 0; e < E; ++e) p[e] = 1.0f / (1.0f + expf(-p[e]));
         mo_group_limit(L, p, ties);
@@ -390,7 +419,8 @@ typedef struct {
  * (generation_mlp.cpp.inc:776-1442):
  *   shared input = x; routed input = RMSNorm(hidden) with pre_norm2 when
  *     given (:820-831, moe_layer_moe_norm_f32 :234-250), else x; the router
- *     reads the routed input (:866-876);
+ *     reads the routed input, or hidden when the layer has a router input
+ *     scale, which it then scales itself (:866-876);
  *   shared expert (:839-860): act(gate)*up, down; RMSNorm with post_norm1
  *     (:853-856); mlp += out * g, g = sigmoid(shared_gate_inp . x) or 1
  *     (moe_layer_shared_expert_gate_f32 :478-512) -- mlp is still 0 there,
@@ -416,7 +446,8 @@ static void* mo_layer_worker(void* arg) {
     float* su = (float*)malloc(sizeof(float) * I);
     int32_t* ids = (int32_t*)malloc(sizeof(int32_t) * K);
     float* w = (float*)malloc(sizeof(float) * K);
-    j->ok = x && xe && mlp && out && tmp && sg && su && ids && w && (!L->pre_norm2 || j->hidden);
+    j->ok = x && xe && mlp && out && tmp && sg && su && ids && w &&
+            (!(L->pre_norm2 || L->router_scale) || j->hidden);
     for (uint32_t t = j->t0; j->ok && t < j->t1; ++t) {
         for (uint32_t h = 0; h < H; ++h) x[h] = mo_bf16(j->x_bf16[(uint64_t)t * H + h]);
         const float* xr = x;
@@ -436,7 +467,10 @@ static void* mo_layer_worker(void* arg) {
             }
             for (uint32_t h = 0; h < H; ++h) mlp[h] = fmaf(so[h], g, mlp[h]);
         }
-        if (!mo_router_topk(L, xr, ids, w, &j->ties)) { j->ok = 0; break; }
+        /* with a router scale the router reads the residual stream itself
+         * (generation_mlp.cpp.inc:866-871) */
+        const float* rin = L->router_scale ? j->hidden + (uint64_t)t * H : xr;
+        if (!mo_router_topk(L, rin, ids, w, &j->ties)) { j->ok = 0; break; }
         for (uint32_t e = 0; e < K; ++e) {
             const uint64_t ex = (uint64_t)ids[e];
             mo_triplet_act(act, L->gate + ex * gu_bytes, L->up + ex * gu_bytes, L->down + ex * d_bytes,
@@ -466,7 +500,7 @@ static void* mo_layer_worker(void* arg) {
 int mo_moe_block(const mo_layer_t* L, const uint16_t* x_bf16, const float* hidden, uint32_t tokens,
                  float* y, int32_t* ids, float* w, uint32_t threads, uint32_t* ties) {
     if (!L || !x_bf16 || !y || L->top_k == 0 || L->top_k > L->experts) return 0;
-    if (L->pre_norm2 && !hidden) return 0;
+    if ((L->pre_norm2 || L->router_scale) && !hidden) return 0;
     if (threads == 0) threads = 1;
     if (threads > tokens) threads = tokens ? tokens : 1;
     mo_layer_job* jobs = (mo_layer_job*)calloc(threads, sizeof(mo_layer_job));

@@ -51,6 +51,10 @@ typedef struct {
     const float* down_scale;       /* 1 (all experts), E (per expert) or E*H (per element) */
     uint64_t down_scale_count;
     const uint16_t* shared_gate_inp;  /* [H] bf16: shared expert x sigmoid(row . x) */
+    /* Router input scale (ffn_gate_inp.scale): the router then reads
+     * hidden * rms^-1 * scale / sqrt(H) of the residual stream (needs hidden). */
+    const float* router_scale;     /* 1 (one for all elements) or H values */
+    uint64_t router_scale_count;
 } mo_layer_t;
 
 float mo_e8m0_to_f32(uint8_t v);

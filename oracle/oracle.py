@@ -55,7 +55,8 @@ class MoLayer(C.Structure):
                 ("n_group", C.c_uint32), ("topk_group", C.c_uint32),
                 ("activation", C.c_int32), ("norm_unit_offset", C.c_int32), ("norm_eps", C.c_float),
                 ("pre_norm2", _f32p), ("post_norm1", _f32p), ("post_norm2", _f32p), ("post_norm", _f32p),
-                ("down_scale", _f32p), ("down_scale_count", C.c_uint64), ("shared_gate_inp", _u16p)]
+                ("down_scale", _f32p), ("down_scale_count", C.c_uint64), ("shared_gate_inp", _u16p),
+                ("router_scale", _f32p), ("router_scale_count", C.c_uint64)]
 
 
 class RefLayer(C.Structure):
@@ -67,7 +68,8 @@ class RefLayer(C.Structure):
 class RefBlock(C.Structure):
     _fields_ = [("base", RefLayer), ("eps", C.c_float), ("pre_norm2", _f32p), ("post_norm1", _f32p),
                 ("post_norm2", _f32p), ("post_norm", _f32p), ("down_scale", _f32p),
-                ("down_scale_count", C.c_uint64), ("shared_gate_inp", _u16p)]
+                ("down_scale_count", C.c_uint64), ("shared_gate_inp", _u16p), ("router_scale", _f32p),
+                ("router_scale_count", C.c_uint64)]
 
 
 class Assignment(C.Structure):
@@ -99,6 +101,7 @@ class Block:
     post_norm: Optional[np.ndarray] = None    # [H] block output
     down_scale: Optional[np.ndarray] = None   # [1], [E] or [E*H]
     shared_gate_inp: Optional[np.ndarray] = None  # [H] bf16
+    router_scale: Optional[np.ndarray] = None     # [1] or [H]: the router reads scaled hidden
 
     def metadata(self) -> list[str]:
         """GGUF metadata entries through which the reference learns the
@@ -186,13 +189,15 @@ class Port:
         keep.update(pn2=_c(blk.pre_norm2, np.float32), n1=_c(blk.post_norm1, np.float32),
                     n2=_c(blk.post_norm2, np.float32), n=_c(blk.post_norm, np.float32),
                     ds=_c(blk.down_scale, np.float32), sgi=_c(blk.shared_gate_inp, np.uint16),
-                    hid=_c(hidden, np.float32))
+                    rs=_c(blk.router_scale, np.float32), hid=_c(hidden, np.float32))
         L.activation, L.norm_unit_offset, L.norm_eps = int(blk.activation), int(blk.unit_offset), float(blk.eps)
         L.pre_norm2, L.post_norm1 = _p(keep["pn2"], _f32p), _p(keep["n1"], _f32p)
         L.post_norm2, L.post_norm = _p(keep["n2"], _f32p), _p(keep["n"], _f32p)
         L.down_scale = _p(keep["ds"], _f32p)
         L.down_scale_count = 0 if keep["ds"] is None else keep["ds"].size
         L.shared_gate_inp = _p(keep["sgi"], _u16p)
+        L.router_scale = _p(keep["rs"], _f32p)
+        L.router_scale_count = 0 if keep["rs"] is None else keep["rs"].size
         y = np.zeros((T, H), np.float32)
         ids = np.zeros((T, K), np.int32)
         w = np.zeros((T, K), np.float32)
@@ -312,13 +317,13 @@ class Ref:
                 _c(li.shared_gate, np.uint8), _c(li.shared_up, np.uint8), _c(li.shared_down, np.uint8),
                 _c(blk.pre_norm2, np.float32), _c(blk.post_norm1, np.float32), _c(blk.post_norm2, np.float32),
                 _c(blk.post_norm, np.float32), _c(blk.down_scale, np.float32),
-                _c(blk.shared_gate_inp, np.uint16), _c(hidden, np.float32)]
+                _c(blk.shared_gate_inp, np.uint16), _c(hidden, np.float32), _c(blk.router_scale, np.float32)]
         base = RefLayer(s.hidden, s.intermediate, s.experts, s.top_k, _p(keep[0], _u16p), _p(keep[1], _u8p),
                         _p(keep[2], _u8p), _p(keep[3], _u8p), _p(keep[4], _u8p), _p(keep[5], _u8p),
                         _p(keep[6], _u8p))
         d = RefBlock(base, float(blk.eps), _p(keep[7], _f32p), _p(keep[8], _f32p), _p(keep[9], _f32p),
                      _p(keep[10], _f32p), _p(keep[11], _f32p), 0 if keep[11] is None else keep[11].size,
-                     _p(keep[12], _u16p))
+                     _p(keep[12], _u16p), _p(keep[14], _f32p), 0 if keep[14] is None else keep[14].size)
         y = np.zeros((T, s.hidden), np.float32)
         ids = np.zeros((T, s.top_k), np.int32)
         w = np.zeros((T, s.top_k), np.float32)

@@ -47,6 +47,19 @@ uint64_t router_cache_key(int32_t layer) {
     return ((uint64_t)(uint32_t)layer << 32) | suffix_hash | 0x80000000ull;
 }
 
+// Key of the router's input scale tensor (moe_map_router_scale_tensor,
+// generation_router.cpp.inc:272-314).
+uint64_t router_scale_key(int32_t layer) {
+    return ((uint64_t)(uint32_t)layer << 32) | moe_router_fnv1a_hash_string("ffn_gate_inp.scale") | 0x80000000ull;
+}
+
+// The plain router and layer entry points model layers without a router
+// input scale: drop one a block call may have left in this engine's cache.
+void clear_router_scale(moe_pc_engine* engine, int32_t layer) {
+    std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
+    engine->raw_tensor_cache.erase(router_scale_key(layer));
+}
+
 float bf16_to_f32(uint16_t v) {
     uint32_t bits = (uint32_t)v << 16;
     float out;
@@ -128,6 +141,7 @@ int ref_router_topk(void* eng, const uint16_t* router_bf16, uint32_t experts,
     moe_pc_engine* engine = static_cast<moe_pc_engine*>(eng);
     if (!engine || !router_bf16 || !x_bf16) return 0;
     const int32_t layer = 0;
+    clear_router_scale(engine, layer);
     moe_raw_tensor_cache_entry entry{};
     entry.base = reinterpret_cast<const uint8_t*>(router_bf16);
     entry.bytes = (uint64_t)experts * hidden * 2ull;
@@ -172,6 +186,7 @@ int ref_moe_layer(void* eng, const ref_layer_desc* d, const uint16_t* x_bf16,
     if (!engine || !d || !x_bf16 || !y_f32) return 0;
     const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, K = d->top_k;
     const int32_t layer = 0;
+    clear_router_scale(engine, layer);
     const uint64_t row_h = (uint64_t)((H + 31u) / 32u) * 17u;
     const uint64_t row_i = (uint64_t)((I + 31u) / 32u) * 17u;
     const uint64_t expert_gu_bytes = (uint64_t)I * row_h;
@@ -262,6 +277,8 @@ typedef struct {
     const float* down_scale;       // [down_scale_count]  ffn_down_exps.scale
     uint64_t down_scale_count;
     const uint16_t* shared_gate_inp;  // [H] bf16  shared_expert_gate.weight
+    const float* router_scale;        // [router_scale_count]  ffn_gate_inp.scale
+    uint64_t router_scale_count;
 } ref_block_desc;
 
 namespace {
@@ -306,7 +323,7 @@ int ref_moe_block(void* eng, const ref_block_desc* bd, const uint16_t* x_bf16, c
     mxcsr_guard guard;
     moe_pc_engine* engine = static_cast<moe_pc_engine*>(eng);
     if (!engine || !bd || !x_bf16 || !y_f32) return 0;
-    if (bd->pre_norm2 && !hidden) return 0;
+    if ((bd->pre_norm2 || bd->router_scale) && !hidden) return 0;
     const ref_layer_desc* d = &bd->base;
     const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, K = d->top_k;
     const int32_t layer = 0;
@@ -334,6 +351,24 @@ int ref_moe_block(void* eng, const ref_block_desc* bd, const uint16_t* x_bf16, c
     put_common(engine, layer, "ffn_down_exps.scale", bd->down_scale, bd->down_scale_count,
                (uint32_t)bd->down_scale_count, 0, F32, RAW_F32);
     put_common(engine, layer, "shared_expert_gate.weight", bd->shared_gate_inp, H, 1, H, BF16, RAW_BF16);
+    {
+        // the router's own lookup of its input scale (moe_map_router_scale_tensor,
+        // generation_router.cpp.inc:272-314) keys it with the router's hash
+        const uint64_t key = router_scale_key(layer);
+        std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
+        if (bd->router_scale && bd->router_scale_count) {
+            moe_raw_tensor_cache_entry e{};
+            e.base = reinterpret_cast<const uint8_t*>(bd->router_scale);
+            e.bytes = bd->router_scale_count * 4ull;
+            e.rows = (uint32_t)bd->router_scale_count;
+            e.cols = 0;
+            e.scalar_encoding = F32;
+            e.weight_format = RAW_F32;
+            engine->raw_tensor_cache[key] = e;
+        } else {
+            engine->raw_tensor_cache.erase(key);
+        }
+    }
     const int activation_mode = moe_engine_gelu_activation_mode(engine);
     const float eps = bd->eps;
 
@@ -366,7 +401,11 @@ int ref_moe_block(void* eng, const ref_block_desc* bd, const uint16_t* x_bf16, c
             if (moe_layer_post_ffw_norm1_f32(engine, layer, shared_out.data(), H, tmp.data(), eps)) so = tmp.data();
             for (uint32_t i = 0; i < H; ++i) mlp[i] += so[i] * g;
         }
-        if (!moe_router_topk_f32(engine, layer, expert_input, H, E, K, &ids, &w, &logits, &order)) return 0;
+        // a router with its own input scale reads the residual stream
+        // (generation_mlp.cpp.inc:866-871) and scales it inside
+        // moe_router_topk_f32 (generation_router.cpp.inc:584-587)
+        const float* router_input = bd->router_scale ? hidden + (uint64_t)t * H : expert_input;
+        if (!moe_router_topk_f32(engine, layer, router_input, H, E, K, &ids, &w, &logits, &order)) return 0;
         if (ids.size() != K) return 0;
         if (!moe_parallel_rows(engine, K * I, 0, [&](uint32_t flat_row) {
                 const uint32_t e = flat_row / I;

@@ -73,7 +73,7 @@ def layer_from_golden(synth, g):
     return li
 
 
-BLOCK_PARTS = ("pre_norm2", "post_norm1", "post_norm2", "post_norm", "down_scale", "shared_gate_inp")
+BLOCK_PARTS = ("pre_norm2", "post_norm1", "post_norm2", "post_norm", "down_scale", "shared_gate_inp", "router_scale")
 
 
 def block_from_golden(oracle_mod, g):

@@ -124,6 +124,14 @@ BLOCK_CASES = {
     "block_silu_vector": (synth.small_shape(name="block_silu_vector", hidden=80, intermediate=100, top_k=3,
                                             experts=8, tokens=20), 33,
                           dict(activation=0, post_norm=True, down_scale="element")),
+    # router input scale (ffn_gate_inp.scale, generation_router.cpp.inc:316-359):
+    # the router reads the scaled residual stream; per element with the MoE
+    # pre-norm, and one scale for all elements
+    "block_router_scale": (synth.small_shape(name="block_router_scale", top_k=3, experts=16, tokens=16), 35,
+                           dict(activation=0, pre_norm2=True, router_scale="element")),
+    "block_router_scalar": (synth.small_shape(name="block_router_scalar", shared=True, top_k=2, experts=8,
+                                              tokens=16), 36,
+                            dict(activation=2, unit_offset=True, router_scale="scalar", post_norm=True)),
 }
 
 
@@ -145,6 +153,9 @@ def block_inputs(shape, seed, opts):
                        post_norm=vec() if opts.get("post_norm") else None,
                        down_scale=rng.uniform(0.5, 2.0, scale).astype(np.float32) if scale else None,
                        shared_gate_inp=gate_row)
+    rscale = {"scalar": 1, "element": H}.get(opts.get("router_scale"))
+    if rscale:
+        blk.router_scale = rng.uniform(0.2, 3.0, rscale).astype(np.float32)
     hidden = (rng.standard_normal((shape.tokens, H)) * 2.0).astype(np.float32)
     return blk, hidden
 
@@ -163,7 +174,7 @@ def block_case(name, shape, seed, opts):
                x=li.x, hidden_in=hidden, activation=blk.activation, unit_offset=int(blk.unit_offset), eps=blk.eps)
     if shape.shared:
         rec.update(shared_gate=li.shared_gate, shared_up=li.shared_up, shared_down=li.shared_down)
-    for k in ("pre_norm2", "post_norm1", "post_norm2", "post_norm", "down_scale", "shared_gate_inp"):
+    for k in ("pre_norm2", "post_norm1", "post_norm2", "post_norm", "down_scale", "shared_gate_inp", "router_scale"):
         if getattr(blk, k) is not None:
             rec[k] = getattr(blk, k)
     np.savez_compressed(OUT / f"{name}.npz", **rec)

@@ -142,7 +142,8 @@ def test_port_matches_reference_fresh_seeds(seed, ref_lib, port, synth):
 
 
 def test_block_fixtures_exist():
-    assert BLOCK_FIXTURES == ["block_gelu_erf.npz", "block_gemma.npz", "block_silu_vector.npz"]
+    assert BLOCK_FIXTURES == ["block_gelu_erf.npz", "block_gemma.npz", "block_router_scalar.npz",
+                              "block_router_scale.npz", "block_silu_vector.npz"]
 
 
 @pytest.mark.parametrize("name", BLOCK_FIXTURES)
@@ -197,7 +198,8 @@ def test_port_matches_reference_block_fresh_seeds(seed, ref_lib, port, synth):
     mg = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mg)
     opts = dict(activation=seed % 3, unit_offset=bool(seed % 2), pre_norm2=True, post_norm1=True,
-                post_norm2=True, post_norm=True, down_scale="element", shared_gate_inp=True)
+                post_norm2=True, post_norm=True, down_scale="element", shared_gate_inp=True,
+                router_scale="element" if seed % 2 else "scalar")
     for shape in (synth.small_shape(name="f1", shared=True, tokens=6, experts=8, top_k=2),
                   synth.small_shape(name="f2", hidden=80, intermediate=100, tokens=5, experts=8, top_k=3)):
         li = synth.make_layer(shape, seed=seed)
