@@ -55,7 +55,13 @@ enum {
 
 /* Explicit form of the routing metadata the reference reads from GGUF JSON
  * keys (num_experts_per_tok, scoring_func, norm_topk_prob,
- * routed_scaling_factor: generation_router.cpp.inc:361-482). */
+ * routed_scaling_factor: generation_router.cpp.inc:361-482).
+ * The layer is SiLU-gated with no tensors around the experts besides the
+ * optional shared expert.  GELU activations, post-FFW norms, the MoE
+ * pre-norm, expert down scales, a shared-expert gate and a router input
+ * scale (generation_mlp.cpp.inc:94-104, 234-250, 380-570;
+ * generation_router.cpp.inc:316-359) have no fields here: layers that have
+ * them are not run by this library. */
 typedef struct {
     uint32_t hidden;       /* H, multiple of 8 */
     uint32_t intermediate; /* I */
