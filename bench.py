@@ -152,7 +152,7 @@ class ClockSampler:
         return {"sm_mhz": float(np.median(load)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(li, seconds: float = 8.0):
+def cpu_baseline(li, seconds: float = 12.0):
     """The reference's CPU layer (or the C restatement) on this host's cores."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle  # test infrastructure: the timed CPU baseline only
@@ -175,7 +175,7 @@ def cpu_baseline(li, seconds: float = 8.0):
         run()
         reps += 1
         el = time.perf_counter() - t0
-        if el >= seconds or reps >= 20:
+        if el >= seconds or reps >= 40:
             break
     T = li.x.shape[0]
     try:
