@@ -248,3 +248,30 @@ def test_port_matches_reference_extreme_shapes(name, ref_lib, port, synth):
     assert np.array_equal(i1, i2)
     assert np.array_equal(bits(w1), bits(w2))
     assert np.array_equal(bits(y1), bits(y2))
+
+
+def test_oracle_struct_layout(oracle_mod, tmp_path):
+    """The ctypes mirror of mo_layer_t has the C header's size and field
+    offsets (compiled with the host C compiler)."""
+    import ctypes
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    inc = oracle_mod.HERE
+    L = oracle_mod.MoLayer
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "moe_oracle.h"', "int main(void) {",
+             'printf("size %zu\\n", sizeof(mo_layer_t));']
+    for fname, _ in L._fields_:
+        lines.append(f'printf("{fname} %zu\\n", offsetof(mo_layer_t, {fname}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(inc), str(src), "-o", str(exe)], check=True)
+    got = dict(l.rsplit(" ", 1) for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                         check=True).stdout.split("\n") if l)
+    assert int(got["size"]) == ctypes.sizeof(L)
+    for fname, _ in L._fields_:
+        assert int(got[fname]) == getattr(L, fname).offset, fname
