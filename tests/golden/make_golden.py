@@ -246,10 +246,36 @@ def decode_tables():
     print("decode_tables")
 
 
+def provenance():
+    """Records what the fixtures' bits depend on: the compiler and -march of
+    the reference build (oracle/Makefile) and the host's FMA/AVX2 support
+    (the reference's dot products take their AVX2 + FMA branches)."""
+    import json
+    import platform
+    import re
+    import subprocess
+    mk = (ROOT / "oracle" / "Makefile").read_text()
+    march = re.search(r"^MARCH \?= (.*)$", mk, re.M).group(1).strip()
+    cxx = subprocess.run(["g++", "--version"], capture_output=True, text=True).stdout.splitlines()[0]
+    flags, model = set(), ""
+    for line in Path("/proc/cpuinfo").read_text().splitlines():
+        if line.startswith("flags") and not flags:
+            flags = set(line.split(":", 1)[1].split())
+        if line.startswith("model name") and not model:
+            model = line.split(":", 1)[1].strip()
+    rec = {"compiler": cxx, "march": march, "cxxflags": "-std=c++17 -O3 -DNDEBUG -pthread",
+           "host_cpu": model, "machine": platform.machine(),
+           "host_flags": {f: f in flags for f in ("avx2", "fma", "f16c", "avx512f")}}
+    (OUT / "provenance.json").write_text(json.dumps(rec, indent=1) + "\n")
+    print("provenance", rec["march"], rec["host_flags"])
+
+
 def main(only=None):
-    """Writes every fixture, or only those whose name starts with `only`."""
+    """Writes every fixture, or only those whose name starts with `only`,
+    and the record of the build they came from."""
     if not oracle.REF_SO.exists():
         oracle.build(ref=True)
+    provenance()
     want = (lambda n: only is None or n.startswith(only))
     if want("decode_tables"):
         decode_tables()
