@@ -167,23 +167,30 @@ MOE_B200_API int moe_b200_group_tokens_by_expert(const moe_b200_assignment_t* as
                                     uint32_t max_batches, uint32_t* out_batch_count);
 
 /* Allocation-free form of moe_b200_group_tokens_by_expert, for callers that
- * must not allocate device memory while they run -- an engine whose
- * residency cache owns the whole VRAM budget, or code recording a CUDA graph
- * (where cudaMalloc is not allowed).  No counterpart in the reference.
- * Same inputs and outputs (host buffers) plus an error buffer; the result is
- * identical to moe_b200_group_tokens_by_expert's.  It calls no cudaMalloc,
- * cudaFree or allocating library routine: its scratch is a fixed device
- * array of about 4.3 MB inside this library, which every GPU that loads the
- * library holds until the process exits.  Limits and caveats:
+ * must not allocate device memory while they run: an engine whose residency
+ * cache owns the whole VRAM budget (every byte it has not handed out already
+ * holds expert weights, so a cudaMalloc mid-layer would fail or evict).  No
+ * counterpart in the reference.  Same inputs and outputs (host buffers) plus
+ * an error buffer; the result is identical to
+ * moe_b200_group_tokens_by_expert's, including the return of 0 with
+ * *out_batch_count = the full batch count when more than max_batches
+ * batches exist.  It calls no cudaMalloc, cudaFree or allocating library
+ * routine: its scratch is a fixed device array of about 4.3 MB inside this
+ * library, which every GPU that loads the library holds until the process
+ * exits.  Limits and caveats:
  *   - at most MOE_B200_NOALLOC_MAX_ASSIGNMENTS assignments; more returns 0
  *     with a message in `err`;
+ *   - it copies the assignments in and the results out with synchronous
+ *     copies on the current device's legacy default stream, so it must run
+ *     outside any stream capture (before or between captures, never while
+ *     a stream of the process is being recorded into a graph);
  *   - the first call on a device resolves the array's device address with
- *     cudaGetSymbolAddress (with that device current), so make that first
- *     call before any stream capture;
+ *     cudaGetSymbolAddress (with that device current) and keeps it; the kept
+ *     address does not survive cudaDeviceReset, so do not call it again
+ *     after resetting a device in the same process;
  *   - every call shares the one array, which keeps the last call's contents;
  *     calls are serialised within the process, and any other work that
- *     overlaps a call on the GPU and touches the array would race with it;
- *   - runs on the current device's legacy default stream and synchronises. */
+ *     overlaps a call on the GPU and touches the array would race with it. */
 #define MOE_B200_NOALLOC_MAX_ASSIGNMENTS 65536u
 MOE_B200_API int moe_b200_group_tokens_by_expert_noalloc(const moe_b200_assignment_t* assignments,
                                                          uint32_t assignment_count,
@@ -203,9 +210,13 @@ MOE_B200_API int moe_b200_group_tokens_by_expert_noalloc(const moe_b200_assignme
  * tokens.  Every rank uploads the router, its own experts and (if used) the
  * shared expert, then all ranks call moe_b200_ep_layer_forward together.
  * Rows move over NVLink peer memory (CUDA IPC mappings of every rank's
- * receive and return buffers); NCCL, opened at run time (libnccl.so.2),
- * carries the per-rank row counts and two barriers; the call synchronises
- * its stream once, after the counts arrive, to size the exchange.
+ * receive and return buffers), stored by this library's own kernels; the
+ * per-rank row counts and the barriers between the phases are device-side
+ * peer stores too (bounded waits).  NCCL, opened at run time
+ * (libnccl.so.2), is used only at set-up: to create the communicator and to
+ * exchange the IPC handles when the buffers grow.  The host reads the W x W
+ * row counts from mapped memory while the dispatch runs, to size the local
+ * expert work, and does not synchronise the stream.
  * ------------------------------------------------------------------------ */
 #define MOE_B200_EP_UID_BYTES 128
 /* A fresh communicator id (ncclGetUniqueId); create it on one rank and

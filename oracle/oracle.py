@@ -24,7 +24,10 @@ HERE = Path(__file__).resolve().parent
 REF_DIR = HERE / "_ref"
 PORT_SO = REF_DIR / "libmoe_port.so"
 REF_SO = REF_DIR / "libmoe_ref.so"
-REFERENCE_ROOT = Path(os.environ.get("MOE_REFERENCE_ROOT", "/root/reference"))
+# The reference checkout: MOE_REFERENCE_ROOT when set, else a directory named
+# "reference" beside this repository's root.  Only builds of the reference
+# library need it; without it build() makes the port alone.
+REFERENCE_ROOT = Path(os.environ.get("MOE_REFERENCE_ROOT") or (HERE.parent.parent / "reference"))
 
 _u8p = C.POINTER(C.c_uint8)
 _u16p = C.POINTER(C.c_uint16)

@@ -2,8 +2,7 @@
 //
 // Some callers cannot allocate device memory while they run a layer: an
 // engine whose residency cache owns the whole VRAM budget (every byte it does
-// not hand out is already holding expert weights), or code recording a
-// stream into a CUDA graph, where cudaMalloc is not allowed.  This entry point
+// not hand out is already holding expert weights).  This entry point
 // therefore never calls cudaMalloc, cudaFree or any allocating library
 // routine.  Its working memory is the fixed array below, which every GPU that
 // loads this library holds for the life of the process.
@@ -24,7 +23,10 @@ using namespace moe_b200;
 namespace {
 
 constexpr uint32_t kMaxN = MOE_B200_NOALLOC_MAX_ASSIGNMENTS;
-constexpr uint32_t kTilesMax = (kMaxN + 2047) / 2048;
+// rows of per-bucket counts the sort needs at the maximum size: one per
+// kSortTile items (sort_tiles in route.cu)
+constexpr uint32_t kTilesMax = (kMaxN + kSortTile - 1) / kSortTile;
+static_assert(kTilesMax * kSortTile >= kMaxN, "scratch tile-count rows cover the largest accepted input");
 
 // Carve-up of the scratch array (byte offsets, each 256-aligned).
 constexpr size_t align256(size_t v) { return (v + 255) / 256 * 256; }

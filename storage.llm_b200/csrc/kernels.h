@@ -105,6 +105,10 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
 uint32_t router_box_rows(bool tokens);
 // Whether launch_router would use the TMA-fed kernel for this batch.
 bool router_wants_tma(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H);
+// Items per tile of the stable counting sort (8 warps x 8 steps x 32 lanes);
+// sort_tiles(n) = ceil(n / kSortTile) tiles, each with a row of per-bucket
+// counts in the tile_counts buffer.
+constexpr uint32_t kSortTile = 2048;
 uint32_t sort_tiles(uint32_t n);
 // Permutation of T*K assignments (assignment a reads source row a / K) into
 // E groups, plus an extra group of `shared_rows` rows whose source rows are

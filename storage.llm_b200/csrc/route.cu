@@ -720,7 +720,7 @@ __global__ void __launch_bounds__(512) router_fused_kernel(const uint16_t* __res
 //   scan:    per-bucket prefix over tiles, group sizes and offsets;
 //   scatter: destination = offset[bucket] + tile base + rank.
 // ---------------------------------------------------------------------------
-constexpr int kSortTile = 2048;  // 8 warps x 8 steps x 32 lanes
+static_assert(kSortTile == 8 * 8 * 32, "a sort tile is 8 warps x 8 steps x 32 lanes");
 
 __global__ void __launch_bounds__(256) sort_count_kernel(const int32_t* __restrict__ keys, uint32_t n,
                                                          uint32_t nb, uint32_t* __restrict__ tile_counts,

@@ -83,7 +83,12 @@ def gen_mxfp4(rng: np.random.Generator, lead: tuple, rows: int, cols: int,
     nblk = (cols + MXFP4_BLOCK - 1) // MXFP4_BLOCK
     out = np.empty(lead + (rows, nblk, MXFP4_BLOCK_BYTES), dtype=np.uint8)
     out[..., 0] = scale_byte
-    out[..., 1:] = rng.integers(0, 256, size=lead + (rows, nblk, 16), dtype=np.uint8)
+    # one leading index (expert) at a time: the same bytes as one draw of the
+    # whole array (each chunk is a multiple of 4 bytes, so the generator's
+    # 32-bit words split evenly), without a second full-size temporary
+    flat = out.reshape((-1, rows, nblk, MXFP4_BLOCK_BYTES))
+    for i in range(flat.shape[0]):
+        flat[i, ..., 1:] = rng.integers(0, 256, size=(rows, nblk, 16), dtype=np.uint8)
     tail = cols % MXFP4_BLOCK
     if tail:
         # Elements past `cols` in the last block are never read by the
@@ -160,7 +165,7 @@ class LayerInputs:
         for a in (self.router, self.gate, self.up, self.down, self.x,
                   self.shared_gate, self.shared_up, self.shared_down):
             if a is not None:
-                h.update(np.ascontiguousarray(a).tobytes())
+                h.update(np.ascontiguousarray(a).reshape(-1).view(np.uint8))
         return h.hexdigest()
 
 

@@ -44,6 +44,11 @@ LAYER_CASES = {
     "c0": (synth.CONFIGS[0], 0, None, False),
     "c1_t8": (synth.CONFIGS[1], 0, 8, False),
     "c3_t16": (synth.CONFIGS[3], 0, 16, False),
+    # decode at one token (the engine's per-token call) and a mid-sweep batch
+    "c1_t1": (synth.CONFIGS[1], 0, 1, False),
+    "c1_t32": (synth.CONFIGS[1], 0, 32, False),
+    # the largest configuration: H=7168, 256 experts, top-8, shared expert
+    "c4_t8": (synth.CONFIGS[4], 0, 8, False),
 }
 
 

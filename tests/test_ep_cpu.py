@@ -1,7 +1,8 @@
 """Expert-parallel layer design on CPU ranks (gloo, world size 2).
 
-The exchange moe_b200_ep_layer_forward runs over NCCL, restated with the
-oracle as the per-rank compute: each rank routes its own tokens, sorts the
+The exchange moe_b200_ep_layer_forward runs over NVLink peer stores (this
+library's own kernels), restated here over gloo collectives with the oracle
+as the per-rank compute: each rank routes its own tokens, sorts the
 assignments stably by owner rank (experts in contiguous blocks of E/world),
 sends every assignment's token row and its owner-local expert index with an
 all-to-allv, the owners run the expert triplet on the rows they receive, the

@@ -11,8 +11,9 @@ the ones whose cost does not grow with the batch, plus a seeded sample:
     <= 1e-2 against the oracle layer run on those tokens alone (a token's
     output does not depend on the other tokens of the batch).
 Inputs are the bench's own (synth.make_layer(shape, seed=0, tokens=T)).
-Config 4 (16,384 tokens of H = 7168 with a shared expert) runs through the
-bench only.
+Config 4 (16,384 tokens of H = 7168, 256 experts, top-8, one shared expert)
+is the largest: its bf16 output rounding alone is close to the 2e-2 bar, so
+the test prints the sample's measured error for the fp32 and bf16 outputs.
 """
 import numpy as np
 import pytest
@@ -56,7 +57,7 @@ def token_sample(config, tokens):
     return np.sort(rng.choice(tokens, size=min(SAMPLE, tokens), replace=False))
 
 
-@pytest.mark.parametrize("config", [1, 3, 2], ids=["c1_decode_t256", "c3_t4096", "c2_prefill_8k"])
+@pytest.mark.parametrize("config", [1, 3, 2, 4], ids=["c1_decode_t256", "c3_t4096", "c2_prefill_8k", "c4_t16384"])
 def test_full_size_configuration(engine, synth, L, port, config):
     shape = synth.CONFIGS[config]
     T = full_size_tokens(synth, config)
@@ -82,4 +83,9 @@ def test_full_size_configuration(engine, synth, L, port, config):
     assert np.array_equal(bits(out["w"][sample]), bits(w_ref))
     y_ref, _, _, _ = port.moe_layer(li, x=xs)
     mx, mr = errors(out["y_f32"][sample], y_ref)
+    y16 = (out["y_bf16"][sample].astype(np.uint32) << 16).view(np.float32)
+    mx16, mr16 = errors(y16, y_ref)
+    print(f"config {config}: sample of {len(sample)} tokens, fp32 output max abs {mx:.3e} mean rel {mr:.3e}; "
+          f"bf16 output max abs {mx16:.3e} mean rel {mr16:.3e}")
     assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+    assert mx16 <= MAX_ABS and mr16 <= MEAN_REL, (mx16, mr16)
