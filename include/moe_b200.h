@@ -113,10 +113,16 @@ MOE_B200_API int moe_b200_upload_router(moe_b200_engine_t* engine, int32_t layer
 /* One expert's gate [I x H], up [I x H] and down [H x I] projections in the
  * reference's GGUF MXFP4 bytes (per-expert records of codec_table.cpp.inc:
  * 1586-1646).  expert = -1 uploads the layer's shared expert.  The bytes are
- * repacked once into the device tile layout; the caller keeps ownership.
- * Replaces the residency upload of device_copy_tensor_from_host
- * (device_tensor_copy_ops.cpp.inc:73) for expert triplets.  The router of
- * the layer must be uploaded first. */
+ * repacked once into the block-scaled layout the GEMMs read, the only copy
+ * the engine keeps (0.53 bytes per weight, like GGUF); the caller keeps
+ * ownership of its buffers.  Replaces the residency upload of
+ * device_copy_tensor_from_host (device_tensor_copy_ops.cpp.inc:73) for
+ * expert triplets.  `src_on_device` = 1 takes the bytes from device memory
+ * (e.g. the engine's own resident copy) with no host round trip.  The work
+ * runs on the engine's upload stream, which is ordered after work queued on
+ * the legacy default stream (device sources written on another stream must
+ * be complete before the call); the call returns once its repack is done and
+ * stalls no other stream.  The router of the layer must be uploaded first. */
 MOE_B200_API int moe_b200_upload_expert(moe_b200_engine_t* engine, int32_t layer, int32_t expert, const uint8_t* gate,
                            uint64_t gate_bytes, const uint8_t* up, uint64_t up_bytes, const uint8_t* down,
                            uint64_t down_bytes, uint32_t hidden, uint32_t intermediate, int32_t src_on_device,

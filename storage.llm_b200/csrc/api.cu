@@ -140,6 +140,43 @@ LayerWeights* get_layer(moe_b200_engine* eng, int32_t layer, char* err) {
     return &eng->layers[layer];
 }
 
+int ensure_tile_form(moe_b200_engine* eng, LayerWeights* L, uint32_t slot, char* err) {
+    if (slot >= L->present.size() || !L->present[slot]) {
+        set_err(err, "expert slot %u not uploaded", slot);
+        return 0;
+    }
+    if (L->tile_ready[slot]) return 1;
+    const uint32_t H = L->H, I = L->I;
+    if (!L->gu.ptr) {
+        L->gu_stride = (uint64_t)ceil_div(I, kTileRows) * ceil_div(H, kTileK) * 2 * kTileBytes;
+        L->dn_stride = (uint64_t)ceil_div(H, kTileRows) * ceil_div(I, kTileK) * kTileBytes;
+        CK(L->gu.reserve(L->gu_stride * (L->E + 1)));
+        CK(L->dn.reserve(L->dn_stride * (L->E + 1)));
+    }
+    const uint64_t gu_need = (uint64_t)I * ceil_div(H, 32) * 17;
+    const uint64_t dn_need = (uint64_t)H * ceil_div(I, 32) * 17;
+    cudaStream_t st = eng->ustream;
+    CK(eng->staging.reserve(2 * gu_need + dn_need));
+    uint8_t* stg = eng->staging.as<uint8_t>();
+    const uint64_t mti = L->rp_i / 128, kth = L->kq / 128, mth = L->rp_h / 128, kti = L->iq / 128;
+    for (int pj = 0; pj < 2; ++pj) {
+        CK(launch_bs_to_gguf(L->bs_gu_codes.as<uint8_t>() + ((uint64_t)slot * 2 + pj) * L->rp_i * (L->kq / 2),
+                             L->bs_gu_sfa.as<uint8_t>() + (uint64_t)slot * mti * kth * 1024 + pj * 512, 1024, I, H,
+                             L->kq, stg + pj * gu_need, st));
+    }
+    CK(launch_bs_to_gguf(L->bs_dn_codes.as<uint8_t>() + (uint64_t)slot * L->rp_h * (L->iq / 2),
+                         L->bs_dn_sfa.as<uint8_t>() + (uint64_t)slot * mth * kti * 512, 512, H, I, L->iq,
+                         stg + 2 * gu_need, st));
+    uint8_t* gu_dst = L->gu.as<uint8_t>() + L->gu_stride * slot;
+    uint8_t* dn_dst = L->dn.as<uint8_t>() + L->dn_stride * slot;
+    CK(launch_repack_mxfp4(stg, I, H, gu_dst, 2 * kTileBytes, st));
+    CK(launch_repack_mxfp4(stg + gu_need, I, H, gu_dst + kTileBytes, 2 * kTileBytes, st));
+    CK(launch_repack_mxfp4(stg + 2 * gu_need, H, I, dn_dst, kTileBytes, st));
+    CK(cudaStreamSynchronize(st));
+    L->tile_ready[slot] = 1;
+    return 1;
+}
+
 int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cudaStream_t st, cudaEvent_t* ev,
                     uint32_t* launches, char* err) {
     auto mark = [&](int i) {
@@ -332,9 +369,11 @@ moe_b200_engine_t* moe_b200_create(const moe_b200_init_t* init, char* err) {
     if (eng->err_word.reserve(sizeof(uint32_t)) != cudaSuccess ||
         cudaMemset(eng->err_word.ptr, 0, sizeof(uint32_t)) != cudaSuccess ||
         cudaStreamCreateWithFlags(&eng->hstream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreate(&eng->ustream) != cudaSuccess ||
         cudaMallocHost(&eng->h_err, sizeof(uint32_t)) != cudaSuccess) {
         set_err(err, "device allocation failed");
         if (eng->hstream) cudaStreamDestroy(eng->hstream);
+        if (eng->ustream) cudaStreamDestroy(eng->ustream);
         eng->err_word.release();
         delete eng;
         return nullptr;
@@ -358,6 +397,7 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
     ep_release(eng->ep);
     if (eng->hstream) cudaStreamDestroy(eng->hstream);
+    if (eng->ustream) cudaStreamDestroy(eng->ustream);
     if (eng->h_err) cudaFreeHost(eng->h_err);
     delete eng;
 }
@@ -415,15 +455,13 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
         return 0;
     }
     CK(cudaSetDevice(eng->device));
-    if (L->I != intermediate || !L->gu.ptr) {
+    if (L->I != intermediate || !L->bs_gu_codes.ptr) {
         L->I = intermediate;
-        L->gu_stride = (uint64_t)ceil_div(intermediate, kTileRows) * ceil_div(hidden, kTileK) * 2 * kTileBytes;
-        L->dn_stride = (uint64_t)ceil_div(hidden, kTileRows) * ceil_div(intermediate, kTileK) * kTileBytes;
+        // a new shape drops the layer's tile form; it is derived again on demand
         L->gu.release();
         L->dn.release();
-        CK(L->gu.reserve(L->gu_stride * (L->E + 1)));
-        CK(L->dn.reserve(L->dn_stride * (L->E + 1)));
-        // block-scaled form
+        L->gu_stride = 0;
+        L->dn_stride = 0;
         L->rp_i = round_up(intermediate, 128);
         L->rp_h = round_up(hidden, 128);
         L->kq = round_up(hidden, 128);
@@ -446,26 +484,23 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
             return 0;
         }
         L->present.assign(L->E + 1, 0);
+        L->tile_ready.assign(L->E + 1, 0);
     }
     const uint32_t slot = expert < 0 ? L->E : (uint32_t)expert;
     const uint8_t* src[3] = {gate, up, down};
     const uint64_t need[3] = {gu_need, gu_need, dn_need};
     const uint8_t* dsrc[3] = {gate, up, down};
+    cudaStream_t st = eng->ustream;
     if (!src_on_device) {
         CK(eng->staging.reserve(2 * gu_need + dn_need));
-        uint8_t* st = eng->staging.as<uint8_t>();
+        uint8_t* stg = eng->staging.as<uint8_t>();
         uint64_t off = 0;
         for (int i = 0; i < 3; ++i) {
-            CK(cudaMemcpy(st + off, src[i], need[i], cudaMemcpyHostToDevice));
-            dsrc[i] = st + off;
+            CK(cudaMemcpyAsync(stg + off, src[i], need[i], cudaMemcpyHostToDevice, st));
+            dsrc[i] = stg + off;
             off += need[i];
         }
     }
-    uint8_t* gu_dst = L->gu.as<uint8_t>() + L->gu_stride * slot;
-    uint8_t* dn_dst = L->dn.as<uint8_t>() + L->dn_stride * slot;
-    CK(launch_repack_mxfp4(dsrc[0], intermediate, hidden, gu_dst, 2 * kTileBytes, 0));
-    CK(launch_repack_mxfp4(dsrc[1], intermediate, hidden, gu_dst + kTileBytes, 2 * kTileBytes, 0));
-    CK(launch_repack_mxfp4(dsrc[2], hidden, intermediate, dn_dst, kTileBytes, 0));
     {
         const uint64_t mti = L->rp_i / 128, kth = L->kq / 128, mth = L->rp_h / 128, kti = L->iq / 128;
         for (int pj = 0; pj < 2; ++pj) {
@@ -474,14 +509,17 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
             CK(launch_repack_bs(dsrc[pj], intermediate, hidden, L->rp_i, L->kq,
                                 L->bs_gu_codes.as<uint8_t>() + m * L->rp_i * (L->kq / 2),
                                 L->bs_gu_sfa.as<uint8_t>() + (uint64_t)slot * mti * kth * 1024 + pj * 512, 1024,
-                                0));
+                                st));
         }
         CK(launch_repack_bs(dsrc[2], hidden, intermediate, L->rp_h, L->iq,
                             L->bs_dn_codes.as<uint8_t>() + (uint64_t)slot * L->rp_h * (L->iq / 2),
-                            L->bs_dn_sfa.as<uint8_t>() + (uint64_t)slot * mth * kti * 512, 512, 0));
+                            L->bs_dn_sfa.as<uint8_t>() + (uint64_t)slot * mth * kti * 512, 512, st));
     }
-    CK(cudaDeviceSynchronize());
+    // the caller may reuse its buffers (and the next upload the staging
+    // buffer) once this returns: wait for this upload only, not the device
+    CK(cudaStreamSynchronize(st));
     L->present[slot] = 1;
+    L->tile_ready[slot] = 0;
     return 1;
 }
 
@@ -543,6 +581,11 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     const bool bs = cfg->gemm_path == MOE_B200_GEMM_BLOCKSCALED;
     CK(eng->yperm.reserve((size_t)P * H * 4));
     if (!bs) {
+        // the cross-check GEMMs read the tile form
+        for (uint32_t e = 0; e < E; ++e) {
+            if (!ensure_tile_form(eng, L, e, err)) return 0;
+        }
+        if (shared && !ensure_tile_form(eng, L, E, err)) return 0;
         CK(eng->xperm.reserve((size_t)rows_cap * Kp * 2));
         CK(eng->hperm.reserve((size_t)rows_cap * Ip * 2));
         // tensor maps over the permuted activations and the intermediate
@@ -743,6 +786,7 @@ int moe_b200_run_expert_triplet_f32(moe_b200_engine_t* eng, int layer, int exper
     const uint32_t slot = expert < 0 ? L->E : (uint32_t)expert;
     if (!L->present[slot]) return 0;
     CK(cudaSetDevice(eng->device));
+    if (!ensure_tile_form(eng, L, slot, err)) return 0;
     const uint32_t H = L->H, I = L->I;
     CK(eng->tri.reserve((size_t)(H + 2 * I + H) * 4));
     float* dx = eng->tri.as<float>();
@@ -778,6 +822,7 @@ int moe_b200_debug_dequant(moe_b200_engine_t* eng, int32_t layer, int32_t expert
         return 0;
     }
     CK(cudaSetDevice(eng->device));
+    if (!ensure_tile_form(eng, L, slot, err)) return 0;
     const uint8_t* tiles = proj == MOE_B200_PROJ_DOWN ? L->dn.as<uint8_t>() + L->dn_stride * slot
                                                       : L->gu.as<uint8_t>() + L->gu_stride * slot +
                                                             (proj == MOE_B200_PROJ_UP ? kTileBytes : 0);

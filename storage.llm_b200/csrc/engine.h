@@ -67,12 +67,17 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 struct LayerWeights {
     uint32_t E = 0, H = 0, I = 0;
     DevBuf router;          // bf16 [E x H]
+    // the one resident form of the experts, block-scaled: packed E2M1 codes
+    // + E8M0 scale blocks (what the product GEMMs read)
+    DevBuf bs_gu_codes, bs_gu_sfa, bs_dn_codes, bs_dn_sfa;
+    std::vector<uint8_t> present;  // [E+1]; slot E = shared expert
+    // tile form of the cross-check GEMMs, the fp32 triplet and the dequant
+    // hook ("wtile", common.cuh): allocated and derived from the
+    // block-scaled form only when one of those is first called
     DevBuf gu;              // [E+1] groups of interleaved gate/up tiles
     DevBuf dn;              // [E+1] groups of down tiles
     uint64_t gu_stride = 0, dn_stride = 0;
-    std::vector<uint8_t> present;  // [E+1]; slot E = shared expert
-    // block-scaled form: packed E2M1 codes + E8M0 scale blocks
-    DevBuf bs_gu_codes, bs_gu_sfa, bs_dn_codes, bs_dn_sfa;
+    std::vector<uint8_t> tile_ready;  // [E+1]: slot's tile form is current
     uint32_t rp_i = 0, rp_h = 0, kq = 0, iq = 0;  // rows padded to 128, K padded to 128
     CUtensorMap tmap_gu_codes{}, tmap_dn_codes{};
     void release_all() {
@@ -101,6 +106,11 @@ struct moe_b200_engine {
     int num_sms = 148;
     std::vector<LayerWeights> layers;
     DevBuf staging;  // GGUF bytes copied from the host before the repack
+    // uploads and tile-form derivations run here and wait only for
+    // themselves; a blocking stream, so it is ordered after work the caller
+    // queued on the legacy default stream (e.g. the copy that produced a
+    // device-resident source)
+    cudaStream_t ustream = nullptr;
     // workspace
     DevBuf logits, scores, ids, wts, tile_counts, rank, pos_of, row_token, row_assign, row_info;
     DevBuf g_count, g_offset, g_gu_off, g_dn_off;
@@ -139,6 +149,9 @@ namespace moe_b200 {
 
 int check_dims(const moe_b200_layer_cfg_t* c, char* err);
 LayerWeights* get_layer(moe_b200_engine* eng, int32_t layer, char* err);
+// Makes the tile form of `slot` current (allocating the layer's tile buffers
+// on first use) from its block-scaled form; synchronises the upload stream.
+int ensure_tile_form(moe_b200_engine* eng, LayerWeights* L, uint32_t slot, char* err);
 bool router_tmaps(moe_b200_engine* eng, const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H,
                   CUtensorMap* tx, CUtensorMap* tw);
 

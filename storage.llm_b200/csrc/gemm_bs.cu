@@ -304,6 +304,51 @@ cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, 
     return cudaGetLastError();
 }
 
+// The inverse of repack_bs_kernel: GGUF MXFP4 rows (per 32 elements one E8M0
+// byte, then 16 bytes holding element i in the low nibble of byte i and
+// element i + 16 in its high nibble) of one projection, rebuilt from its
+// block-scaled form.  Only the cross-check paths need the GGUF bytes again
+// (they repack them into their own tile form), so the upload keeps a single
+// copy of every expert.  One thread per output byte.
+__global__ void bs_to_gguf_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ sfa,
+                                  uint32_t sf_stride, uint32_t rows, uint32_t cols, uint32_t Kp,
+                                  uint8_t* __restrict__ gguf) {
+    const uint32_t nblk = ceil_div(cols, 32);
+    const uint32_t row_bytes = nblk * 17;
+    const uint32_t kt_n = Kp / 128;
+    const uint64_t total = (uint64_t)rows * row_bytes;
+    for (uint64_t idx = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; idx < total;
+         idx += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t r = (uint32_t)(idx / row_bytes);
+        const uint32_t rem = (uint32_t)(idx % row_bytes);
+        const uint32_t b = rem / 17, j = rem % 17;
+        const uint32_t mt = r / 128, rr = r % 128;
+        uint8_t v;
+        if (j == 0) {
+            const uint32_t kt = b / 4, q = b % 4;
+            v = sfa[((uint64_t)mt * kt_n + kt) * sf_stride + (rr % 32) * 16 + (rr / 32) * 4 + q];
+        } else {
+            auto code = [&](uint32_t k) -> uint32_t {
+                const uint64_t blk = (uint64_t)mt * kt_n + k / 128;
+                const uint8_t byte = codes[blk * 8192 + rr * 64 + (k % 128) / 2];
+                return (k & 1u) ? (byte >> 4) : (byte & 0x0Fu);
+            };
+            const uint32_t k_lo = b * 32 + (j - 1);
+            v = (uint8_t)(code(k_lo) | (code(k_lo + 16) << 4));  // past `cols` the block-scaled codes are 0
+        }
+        gguf[idx] = v;
+    }
+}
+
+cudaError_t launch_bs_to_gguf(const uint8_t* codes, const uint8_t* sfa, uint32_t sf_stride, uint32_t rows,
+                              uint32_t cols, uint32_t Kp, uint8_t* gguf, cudaStream_t st) {
+    const uint64_t work = (uint64_t)rows * ceil_div(cols, 32) * 17;
+    const uint64_t blocks = (work + 255) / 256;
+    bs_to_gguf_kernel<<<(unsigned)(blocks < 148 * 16 ? (blocks ? blocks : 1) : 148 * 16), 256, 0, st>>>(
+        codes, sfa, sf_stride, rows, cols, Kp, gguf);
+    return cudaGetLastError();
+}
+
 // The same planes and scale words as gather_quant_bs_kernel, computed once
 // per token instead of once per permuted row: a warp takes (token t, chunk
 // of kGqChunk K stages), reads and splits the token's row once, and stores

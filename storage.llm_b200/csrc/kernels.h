@@ -156,6 +156,10 @@ cudaError_t launch_gemm_tc(int mode, const CUtensorMap& tmap_b, const GemmParams
 // before reading what the predecessor wrote.
 cudaError_t launch_repack_bs(const uint8_t* gguf, uint32_t rows, uint32_t cols, uint32_t rows_pad, uint32_t Kp,
                              uint8_t* codes, uint8_t* sfa, uint32_t sf_stride, cudaStream_t st);
+// GGUF MXFP4 rows [rows x ceil(cols/32)*17] of one projection, rebuilt from
+// its block-scaled codes and scale blocks (the inverse of launch_repack_bs).
+cudaError_t launch_bs_to_gguf(const uint8_t* codes, const uint8_t* sfa, uint32_t sf_stride, uint32_t rows,
+                              uint32_t cols, uint32_t Kp, uint8_t* gguf, cudaStream_t st);
 // xb [2][rows_cap][Kp]: permuted rows of x as exact hi/lo E4M3 terms; their
 // scale words go to sf_atoms, one block per (token tile, 128-K stage), at the
 // tile and index the permutation recorded in row_info.

@@ -126,6 +126,43 @@ def test_expert_triplet_matches_oracle(engine, synth, port):
         engine.expert_triplet(0, 2, x[:100], 160)
 
 
+def test_device_resident_upload_matches_host_upload(L, synth):
+    """The residency hook's recommended binding: the expert bytes are already
+    in device memory (the engine's resident copy) and are uploaded with
+    src_on_device = 1.  The repacked experts must decode bit-exactly like the
+    GGUF bytes, and the layer must give bit-identical outputs from a host
+    upload and a device upload of the same bytes."""
+    import torch
+    shape = synth.small_shape(name="dev_upload", hidden=192, intermediate=160, experts=6, top_k=2, tokens=40,
+                              shared=True)
+    li = synth.make_layer(shape, seed=21)
+    rng = np.random.default_rng(21)
+    li.gate = synth.jitter_scales(li.gate, rng, 6, 3)  # varied per-block scales
+    li.down = synth.jitter_scales(li.down, rng, 6, 3)
+    eng = L.Engine(0, max_layers=2)
+    try:
+        eng.upload_layer(li, layer=0)
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        eng.upload_router(1, dev(li.router.view(np.int16)), shape.experts, shape.hidden, on_device=True)
+        for e in range(shape.experts):
+            eng.upload_expert(1, e, dev(li.gate[e]), dev(li.up[e]), dev(li.down[e]), shape.hidden,
+                              shape.intermediate, on_device=True)
+        eng.upload_expert(1, -1, dev(li.shared_gate), dev(li.shared_up), dev(li.shared_down), shape.hidden,
+                          shape.intermediate, on_device=True)
+        torch.cuda.synchronize()
+        for e in (0, shape.experts - 1, -1):
+            src = (li.gate[e], li.up[e], li.down[e]) if e >= 0 else (li.shared_gate, li.shared_up, li.shared_down)
+            for proj, rows, cols in ((0, 160, 192), (1, 160, 192), (2, 192, 160)):
+                got = bf16_to_f32(eng.dequant(1, e, proj, rows, cols))
+                assert np.array_equal(bits(got), bits(decode_gguf(src[proj], rows, cols))), (e, proj)
+        a = eng.forward_host(L.Engine.cfg(shape, layer=0), li.x)
+        b = eng.forward_host(L.Engine.cfg(shape, layer=1), li.x)
+        for k in ("y_f32", "ids", "w", "perm"):
+            assert np.array_equal(np.asarray(a[k]).view(np.uint8), np.asarray(b[k]).view(np.uint8)), k
+    finally:
+        eng.close()
+
+
 def test_group_tokens_matches_reference_fixture(L):
     g = golden("grouping.npz")
     ok, out, batches, cnt = L.group_tokens_by_expert(g["token"], g["expert"], g["score"], g["layer"])
