@@ -1,39 +1,51 @@
 """Benchmark of the B200 MoE expert-FFN layer: MoE-layer tokens/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config 1] [--tokens 256]
+                    [--config 4] [--tokens T] [--no-cpu-baseline] [--no-sweep]
 
 Prints ONE JSON line on rank 0.
 
-Workload (N=1 headline): configuration 1 of the benchmark -- H=2880, 32
-experts, top-4, I=2880, SwiGLU, MXFP4 weights, Zipf(1.1)-skewed routing --
-at its largest decode batch, 256 tokens per step.  Synthetic, seeded inputs
-(there is no dataset for this path).  A step is one layer forward over one
-batch: router top-k, permutation, gather, gate/up grouped GEMM + SwiGLU, down
-grouped GEMM, weighted combine.
+Workload (N=1 headline): configuration 4 of the benchmark, the largest
+configuration that fits one B200 -- H=7168, 256 routed experts, top-8, one
+always-on shared expert, I=2048, SwiGLU, MXFP4 weights (6.0 GB), 16,384
+tokens per step.  Synthetic, seeded inputs (there is no dataset for this
+path).  A step is one layer forward over one batch: router top-k,
+permutation, quantise-once of the token rows, gate/up grouped GEMM + SwiGLU,
+down grouped GEMM, weighted combine.
 
-* value     tokens/s over the timed steps with inputs resident in HBM, timed
-            with CUDA events on the launching stream (max over ranks);
+* value     tokens/s with inputs resident in HBM, timed with CUDA events on
+            the launching stream (max over ranks).  The K timed steps are
+            one window; the window is repeated until the timed work spans
+            about three seconds (so the clock sampler sees the load), and
+            the median window is reported;
 * e2e       the same metric through the host-buffer C-ABI call
             (moe_b200_layer_forward_host): pinned-host x in, y/ids/weights out,
             copies inside the timed region;
-* roofline  the dominant kernel (gate/up grouped GEMM): algorithmic bytes per
-            launch (MXFP4 bytes of the distinct experts routed to + activation
-            rows in + intermediate out) / its CUDA-event duration, against the
-            measured HBM copy bandwidth;
+* roofline  the dominant kernel, the gate/up grouped GEMM.  At prefill sizes
+            (configs 2 to 4) it is tensor-bound: its algorithmic FLOPs per
+            launch (4 H I per permuted row, the bf16-equivalent product the
+            layer defines) over its CUDA-event duration, against the dense
+            MXFP4 peak the metric names (9 PFLOP/s, spec); `issued` gives
+            the same kernel against the rate of the MMA kind it issues
+            (kind::mxf8f6f4, 4.5 PFLOP/s spec, two terms per product).
+            MEASURED_PEAKS.json has no FP4 or FP8 figure, so both peaks are
+            the spec's.  At decode sizes (config 0, 1) it is HBM-bound:
+            algorithmic bytes against the measured HBM copy bandwidth;
+* decode_sweep  the config 1 decode batches (1, 8, 32, 128, 256 tokens per
+            step) on the same GPU, each with its whole-layer HBM fraction;
 * cpu_baseline  the reference's own CPU path (oracle/_ref/libmoe_ref.so, the
             reference sources compiled by oracle/Makefile) timed on this host's
-            cores over one 256-token batch (kind "reference"), or the C
+            cores over a prefix of the batch (kind "reference"), or the C
             restatement when that library is absent (kind "port").
 
 L2: no flush between steps; instead the weights a step reads are never
-still cached when they are read again.  At the headline workload one layer's
-routed experts are 423 MB against the 126 MB L2.  Where one layer's touched
-weights are smaller (config 0, small token counts, a rank's expert block at 4
-or 8 GPUs), the layer is uploaded into several layer slots -- as a model's
-consecutive MoE layers would be -- and the steps cycle through them, so that
-at least twice the L2 is read between two uses of one copy
-("weight_copies_cycled" in `config`).
+still cached when they are read again.  At the headline workload one step
+reads all 6.0 GB of the layer's weights against the 126 MB L2.  Where one
+step's touched weights are smaller (config 0, small token counts, a rank's
+expert block at 4 or 8 GPUs), the layer is uploaded into several layer
+slots -- as a model's consecutive MoE layers would be -- and the steps cycle
+through them, so that at least twice the L2 is read between two uses of one
+copy (reported under "l2_reuse").
 
 Multi-GPU (torchrun, N ranks): expert parallelism.  Experts are placed over
 the ranks from a separate calibration batch (hot experts replicated), each
@@ -62,6 +74,8 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 PKG = ROOT / "storage.llm_b200"
+DEFAULT_CONFIG = 4
+METRIC = "MoE-layer tokens/sec"
 
 
 def load_pkg():
@@ -83,8 +97,14 @@ def measured_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+# Dense tensor peaks from the B200 spec (TFLOP/s).  MEASURED_PEAKS.json has
+# only bf16 (cuBLAS) and HBM figures.
+MXFP4_TFLOPS = 9000.0     # kind::mxf4 (E2M1 x E2M1), the metric's roofline
+MXF8F6F4_TFLOPS = 4500.0  # kind::mxf8f6f4 (the FP8 rate), the kind the GEMMs issue
 L2_BYTES = 126e6    # B200 L2
 MAX_COPIES = 16     # layer slots the engines are created with
+WINDOW_SECONDS = 3.0
+MAX_WINDOWS = 25
 
 
 def expert_bytes(shape) -> float:
@@ -96,6 +116,17 @@ def weight_copies(touched_bytes: float) -> int:
     """Layer copies the timed steps cycle through so that at least twice the
     L2 is read between two uses of one copy's weights."""
     return int(max(1, min(MAX_COPIES, math.ceil(2 * L2_BYTES / max(touched_bytes, 1.0)))))
+
+
+def default_tokens(synth, config: int) -> int:
+    shape = synth.CONFIGS[config]
+    return 256 if config == 1 else (shape.tokens or sum(synth.prefill_lengths()))
+
+
+def is_prefill(config: int) -> bool:
+    """Configurations whose GEMMs are tensor-bound (the metric's MXFP4
+    roofline); decode-sized ones are HBM-bound."""
+    return config >= 2
 
 
 class ClockSampler:
@@ -132,7 +163,7 @@ class ClockSampler:
             self.lines = [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
+        sm, mx, reasons, power = [], 0.0, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for l in getattr(self, "lines", []):
             f = [x.strip() for x in l.split(",")]
@@ -141,6 +172,7 @@ class ClockSampler:
             try:
                 sm.append(float(f[1]))
                 mx = max(mx, float(f[2]))
+                power.append(float(f[3]))
             except ValueError:
                 continue
             for n, v in zip(names, f[5:9]):
@@ -148,41 +180,62 @@ class ClockSampler:
                     reasons.add(n)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        load = sorted(sm)[len(sm) // 2:]  # upper half ~ under load
-        return {"sm_mhz": float(np.median(load)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        # samples under load: power at least half the peak seen (the sampler
+        # starts just before the timed windows and stops just after them)
+        pmax = max(power) if power else 0.0
+        load = [s for s, p in zip(sm, power) if p >= 0.5 * pmax] or sm
+        return {"sm_mhz": float(np.median(load)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "samples_under_load": len(load), "power_w_max": pmax}
 
 
-CPU_SAMPLE_TOKENS = 256  # tokens per CPU-timed batch (the headline's whole batch)
+# tokens of a batch the CPU arms time, per configuration: the reference runs
+# the layer token by token, so the rate over a prefix is the batch's rate;
+# the prefix keeps one CPU step near half a second on a 16-core host
+CPU_SAMPLE_TOKENS = {0: 64, 1: 256, 2: 256, 3: 256, 4: 64}
 
 
-def cpu_sample(li):
-    """The first CPU_SAMPLE_TOKENS tokens of a batch, and the batch size.
-    Each token goes through the reference layer on its own, so the rate over
-    a prefix is the rate over the batch; larger batches (configs 2 to 4)
-    are timed on their prefix so the CPU arms end within minutes."""
+def cpu_sample(li, config: int):
+    """The prefix of a batch the CPU arms run, and the batch size."""
     T_all = li.x.shape[0]
-    if T_all > CPU_SAMPLE_TOKENS:
-        li.x = np.ascontiguousarray(li.x[:CPU_SAMPLE_TOKENS])
+    n = CPU_SAMPLE_TOKENS.get(config, 256)
+    if T_all > n:
+        li.x = np.ascontiguousarray(li.x[:n])
     return li, T_all
 
 
-def cpu_baseline(li, seconds: float = 12.0):
-    """The reference's CPU layer (or the C restatement) on this host's cores."""
+def cpu_runner(li, shape):
+    """(run, kind, cores): the reference's CPU layer, or the C restatement."""
     sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle  # test infrastructure: the timed CPU baseline only
-    li, T_all = cpu_sample(li)
-    s = li.shape
+    import oracle  # test infrastructure: the timed CPU baseline and reference arm only
     if oracle.REF_SO.exists():
-        ref = oracle.Ref(oracle.metadata_json(s.top_k, norm_topk=s.norm_topk))
-        run = lambda: ref.moe_layer(li)
-        kind, cores = "reference", int(ref.lib.ref_row_threads())
-    else:
-        if not oracle.PORT_SO.exists():
-            oracle.build(ref=False)
-        port = oracle.Port()
-        cores = os.cpu_count() or 1
-        run = lambda: port.moe_layer(li, threads=cores)
-        kind = "port"
+        ref = oracle.Ref(oracle.metadata_json(shape.top_k, norm_topk=shape.norm_topk))
+        return (lambda: ref.moe_layer(li)), "reference", int(ref.lib.ref_row_threads())
+    if not oracle.PORT_SO.exists():
+        oracle.build(ref=False)
+    port = oracle.Port()
+    cores = os.cpu_count() or 1
+    return (lambda: port.moe_layer(li, threads=cores)), "port", cores
+
+
+def host_cpu() -> str:
+    try:
+        return subprocess.run(["bash", "-c", "lscpu | grep 'Model name' | head -1 | cut -d: -f2"],
+                              capture_output=True, text=True).stdout.strip()
+    except OSError:
+        return ""
+
+
+def sample_text(reps, T, T_all, el=None):
+    s = f"{reps} x {T}-token batches of the same workload" + (f" ({el:.1f} s)" if el is not None else "")
+    if T < T_all:
+        s += f", the first {T} of the step's {T_all} tokens (rate extrapolated)"
+    return s + f", per-token reference layer order, -march=x86-64-v3, host CPU {host_cpu()}"
+
+
+def cpu_baseline(li, shape, config: int, seconds: float = 12.0):
+    """The reference's CPU layer (or the C restatement) on this host's cores."""
+    li, T_all = cpu_sample(li, config)
+    run, kind, cores = cpu_runner(li, shape)
     run()  # warm
     t0 = time.perf_counter()
     reps = 0
@@ -193,35 +246,29 @@ def cpu_baseline(li, seconds: float = 12.0):
         if el >= seconds or reps >= 40:
             break
     T = li.x.shape[0]
-    try:
-        cpu = subprocess.run(["bash", "-c", "lscpu | grep 'Model name' | head -1 | cut -d: -f2"],
-                             capture_output=True, text=True).stdout.strip()
-    except OSError:
-        cpu = ""
     return {"value": T * reps / el, "unit": "tokens/s", "cores": cores, "kind": kind,
-            "sample": f"{reps} x {T}-token batches of the same workload ({el:.1f} s)"
-                      + (f", the first {T} of the step's {T_all} tokens (rate extrapolated)" if T < T_all else "")
-                      + f", per-token reference layer order, -march=x86-64-v3, host CPU {cpu}"}
+            "sample": sample_text(reps, T, T_all, el)}
+
+
+def config_dict(shape, args):
+    """The workload; identical in both arms (the GPU arm's L2 details are
+    reported beside it, under l2_reuse)."""
+    return {"workload": f"config{args.config}: H{shape.hidden} E{shape.experts} top{shape.top_k} "
+                        f"I{shape.intermediate} SwiGLU MXFP4"
+                        + (" + shared expert" if shape.shared else "")
+                        + f", {args.tokens} tokens/step" + (f", skew {shape.skew}" if shape.skew else ""),
+            "hidden": shape.hidden, "experts": shape.experts, "top_k": shape.top_k,
+            "intermediate": shape.intermediate, "tokens_per_step": args.tokens, "shared_expert": shape.shared,
+            "parallelism": f"ep{args.gpus}" if args.gpus > 1 else "single",
+            "l2": "inputs_exceed_l2"}
 
 
 def run_reference(args, shape, metric):
     """--impl reference: the reference's CPU path on the host cores."""
     import moe_b200.synth as synth
-    li, T_all = cpu_sample(synth.make_layer(shape, seed=0, tokens=args.tokens))
+    li, T_all = cpu_sample(synth.make_layer(shape, seed=0, tokens=args.tokens), args.config)
     T = li.x.shape[0]
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle
-    if oracle.REF_SO.exists():
-        ref = oracle.Ref(oracle.metadata_json(shape.top_k, norm_topk=shape.norm_topk))
-        step = lambda: ref.moe_layer(li)
-        kind, cores = "reference", int(ref.lib.ref_row_threads())
-    else:
-        if not oracle.PORT_SO.exists():
-            oracle.build(ref=False)
-        port = oracle.Port()
-        cores = os.cpu_count() or 1
-        step = lambda: port.moe_layer(li, threads=cores)
-        kind = "port"
+    step, kind, cores = cpu_runner(li, shape)
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
@@ -234,37 +281,22 @@ def run_reference(args, shape, metric):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded)", "config": config_dict(shape, args),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
-                             "sample": f"{args.steps} x {T}-token batches"
-                                       + (f", the first {T} of the step's {T_all} tokens (rate extrapolated)"
-                                          if T < T_all else "")},
+                             "sample": sample_text(args.steps, T, T_all)},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def config_dict(shape, args, copies: int = 1, touched_bytes: float | None = None):
-    d = {"workload": f"config{args.config}: H{shape.hidden} E{shape.experts} top{shape.top_k} "
-                     f"I{shape.intermediate} SwiGLU MXFP4, {args.tokens} tokens/step"
-                     + (f", skew {shape.skew}" if shape.skew else ""),
-         "hidden": shape.hidden, "experts": shape.experts, "top_k": shape.top_k,
-         "intermediate": shape.intermediate, "tokens_per_step": args.tokens, "shared_expert": shape.shared,
-         "parallelism": f"ep{args.gpus}" if args.gpus > 1 else "single",
-         "l2": "inputs_exceed_l2"}
-    if touched_bytes is not None:  # the GPU arms: weights read between two uses of one copy
-        d["weight_copies_cycled"] = copies
-        d["weight_bytes_between_reuses"] = touched_bytes * copies
-    return d
-
-
-def profiled_traffic(args):
+def profiled_traffic(config: int, tokens: int):
     """DRAM bytes (read + write) per launch of the gate/up GEMM, from the ncu
-    capture summarised under profiles/ for this workload (None without one)."""
-    if args.config != 1 or args.tokens != 256:
-        return None
-    f = ROOT / "profiles" / "gemm_bs_gate_up_c1_t256.md"
-    if not f.exists():
-        return None
-    for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            return float(line.split(":", 1)[1].strip())
+    capture summarised under profiles/ for this workload (None without one).
+    The summary names the workload it applies to on a `workload:` line."""
+    for f in sorted((ROOT / "profiles").glob("gemm_bs_gate_up_c*.md")):
+        txt = f.read_text().splitlines()
+        wl = next((l.split(":", 1)[1].strip() for l in txt if l.startswith("workload:")), None)
+        if wl != f"config{config} T={tokens}":
+            continue
+        for line in txt:
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
     return None
 
 
@@ -285,6 +317,58 @@ class StdoutToStderr:
         os.close(self.saved)
 
 
+def windows_for(step_s: float, steps: int) -> int:
+    """Repetitions of the K-step window so the timed work spans about
+    WINDOW_SECONDS."""
+    return int(max(1, min(MAX_WINDOWS, math.ceil(WINDOW_SECONDS / max(step_s * steps, 1e-6)))))
+
+
+def timed_windows(step, steps, windows, stream, dist=None):
+    """`windows` windows of exactly `steps` steps, each bracketed by a barrier
+    (multi-GPU) and device synchronisation on both sides and timed with CUDA
+    events on the launching stream; returns the per-window milliseconds
+    (max over ranks)."""
+    import torch
+    out = []
+    for _ in range(windows):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end)
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        out.append(ms)
+    return out
+
+
+def warmup_step_seconds(step, warmup, dist=None):
+    """Runs the warm-up steps; returns the seconds per step of the last half
+    (agreed over ranks, so every rank times the same number of windows)."""
+    import torch
+    half = max(1, warmup // 2)
+    for _ in range(warmup - half):
+        step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(half):
+        step()
+    torch.cuda.synchronize()
+    s = (time.perf_counter() - t0) / half
+    if dist:
+        t = torch.tensor([s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        s = float(t.item())
+    return s
+
+
 def calibrate_placement(shape, li, rank, world, dist, tokens):
     """Expert placement with replication from a calibration batch (not the
     timed tokens): per-expert routing counts summed over the ranks, experts
@@ -293,7 +377,7 @@ def calibrate_placement(shape, li, rank, world, dist, tokens):
     Every rank computes the same placement from the same counts."""
     import torch
     import moe_b200.synth as synth
-    xc = synth.gen_tokens(shape, tokens, seed=900 + rank, mu=li.mu)
+    xc = synth.gen_tokens(shape, min(tokens, 4096), seed=900 + rank, mu=li.mu)
     xf = (xc.astype(np.uint32) << 16).view(np.float32)
     wf = (np.ascontiguousarray(li.router).astype(np.uint32) << 16).view(np.float32)
     logits = xf @ wf.T  # routing decisions only; the layer itself routes exactly
@@ -323,6 +407,44 @@ def place_replicas(counts, world):
     return placement, (load.max() / max(load.mean(), 1e-9))
 
 
+def layer_flops(shape, T):
+    """Algorithmic FLOPs of one layer call (bf16-equivalent products):
+    T k 6 H I (+ T 6 H I shared) + 2 T H E (router)."""
+    H, I, E, K = shape.hidden, shape.intermediate, shape.experts, shape.top_k
+    return T * (K + (1 if shape.shared else 0)) * 6 * H * I + 2 * T * H * E
+
+
+def layer_bytes(shape, T, distinct):
+    """Algorithmic HBM bytes of one layer call: the MXFP4 weights of the
+    distinct experts routed to (+ the shared expert), the router rows, the
+    token rows in and out, and the permuted rows written and read once."""
+    H, E, K = shape.hidden, shape.experts, shape.top_k
+    wts = (distinct + (1 if shape.shared else 0)) * expert_bytes(shape)
+    return wts + E * H * 2 + 2 * T * H * 2 + 2 * T * K * H * 2
+
+
+def tensor_roofline(shape, T, gu_ms, dn_ms, traffic):
+    """The gate/up GEMM against the metric's MXFP4 roofline, and against the
+    rate of the MMA kind it issues (two E4M3 terms per bf16 activation)."""
+    H, I = shape.hidden, shape.intermediate
+    P = T * (shape.top_k + (1 if shape.shared else 0))
+    gu_flops = P * 4.0 * H * I
+    dn_flops = P * 2.0 * H * I
+    ach = gu_flops / (gu_ms / 1e3) / 1e12
+    dn_ach = dn_flops / (dn_ms / 1e3) / 1e12
+    _, bf16, bf16_kind = measured_peaks()
+    return {"kernel": "gemm_bs_kernel<gate_up> (grouped MXFP4 gate/up GEMM + SwiGLU)", "bound": "tensor",
+            "achieved": ach, "peak": MXFP4_TFLOPS, "unit": "TFLOP/s", "frac": ach / MXFP4_TFLOPS,
+            "peak_source": "spec: dense MXFP4 9 PFLOP/s (MEASURED_PEAKS.json has no FP4 or FP8 figure)",
+            "traffic": traffic, "algorithmic_flops_per_launch": gu_flops, "launch_ms": gu_ms,
+            "issued": {"mma": "tcgen05.mma kind::mxf8f6f4 block_scale: E2M1 weights x E4M3 hi + lo activation terms",
+                       "flops_issued_per_launch": 2 * gu_flops, "achieved": 2 * ach, "peak": MXF8F6F4_TFLOPS,
+                       "frac": 2 * ach / MXF8F6F4_TFLOPS, "peak_source": "spec: dense FP8-rate 4.5 PFLOP/s"},
+            "vs_measured_bf16_cublas": {"peak": bf16, "frac": ach / bf16, "peak_source": bf16_kind},
+            "down_gemm": {"achieved": dn_ach, "unit": "TFLOP/s", "launch_ms": dn_ms, "frac": dn_ach / MXFP4_TFLOPS,
+                          "issued_frac": 2 * dn_ach / MXF8F6F4_TFLOPS}}
+
+
 def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     """--gpus N > 1: moe_b200_ep_layer_forward on every rank (see the module docstring)."""
     import ctypes as C
@@ -345,6 +467,7 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     copies = weight_copies(touched)
     for layer in range(copies):
         eng.upload_layer_ep(li, layer=layer)
+    li.gate = li.up = li.down = None  # the host copies of the weights are no longer needed
     cfgs = [L.Engine.cfg(shape, layer=layer, gemm_path=L.GEMM_BLOCKSCALED) for layer in range(copies)]
     calls = [0]
 
@@ -362,23 +485,15 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     def step():
         eng.ep_forward(next_cfg(), x, T, y_bf16=y, ids=ids, w=w, stream=sp)
 
-    for _ in range(args.warmup):
-        step()
+    step_s = warmup_step_seconds(step, args.warmup, dist)
     eng.sync(sp)
     launches_per_step = eng.launches()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    windows = windows_for(step_s, args.steps)
     dist.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        start.record(stream)
-        for _ in range(args.steps):
-            step()
-        end.record(stream)
-        torch.cuda.synchronize()
-    ms = start.elapsed_time(end)
-    t = torch.tensor([ms], device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+        win_ms = timed_windows(step, args.steps, windows, stream, dist)
+    eng.sync(sp)
+    ms = float(np.median(win_ms))
     dist.barrier()
     value = T * args.steps * world / (ms / 1000.0)
     # per-phase breakdown: the same steps again with events between phases
@@ -410,11 +525,13 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
         if not ok:
             raise L.MoEError(eng.err.value.decode())
 
-    for _ in range(10):
+    for _ in range(3):
         step_host()
     dist.barrier()
     torch.cuda.synchronize()
-    e2e_steps = max(200, args.steps)  # host wall clock: a longer window for a steadier figure
+    n_e2e = torch.tensor([max(args.steps, int(math.ceil(2.0 / max(step_s, 1e-6))))], device="cuda")
+    dist.all_reduce(n_e2e, op=dist.ReduceOp.MAX)
+    e2e_steps = int(n_e2e.item())
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         step_host()
@@ -424,23 +541,36 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = T * e2e_steps * world / float(t.item())
 
-    # whole-layer HBM roofline of one rank: its expert block's MXFP4 bytes
-    # (every local expert is routed to at these batch sizes) + its token rows
-    hbm, _, peak_kind = measured_peaks()
     e_loc = len(eng.ep_local_expert_list(shape.experts))
-    layer_bytes = e_loc * 3 * shape.intermediate * H * 17 / 32 + T * H * 2 * 2 + 2 * T * K * H * 2
-    achieved = layer_bytes / (ms / args.steps / 1000.0) / 1e9
+    step_ms = ms / args.steps
+    if is_prefill(args.config):
+        # one rank's expert GEMMs: every row it received plus its own shared rows
+        P = float(recv.sum()) + (T if shape.shared else 0)
+        flops = P * 6.0 * H * shape.intermediate
+        ach = flops / (step_ms / 1e3) / 1e12
+        roofline = {"kernel": "whole layer on one expert-parallel rank (its grouped GEMMs' FLOPs over the step)",
+                    "bound": "tensor", "achieved": ach, "peak": MXFP4_TFLOPS, "unit": "TFLOP/s",
+                    "frac": ach / MXFP4_TFLOPS,
+                    "peak_source": "spec: dense MXFP4 9 PFLOP/s (MEASURED_PEAKS.json has no FP4 or FP8 figure)",
+                    "traffic": None, "algorithmic_flops_per_launch": flops, "launch_ms": step_ms,
+                    "issued": {"achieved": 2 * ach, "peak": MXF8F6F4_TFLOPS, "frac": 2 * ach / MXF8F6F4_TFLOPS}}
+    else:
+        hbm, _, peak_kind = measured_peaks()
+        lb = e_loc * expert_bytes(shape) + T * H * 2 * 2 + 2 * T * K * H * 2
+        achieved = lb / (step_ms / 1000.0) / 1e9
+        roofline = {"kernel": "whole layer on one expert-parallel rank", "bound": "hbm", "achieved": achieved,
+                    "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_kind,
+                    "traffic": None, "algorithmic_bytes_per_launch": lb, "launch_ms": step_ms}
     result = {
         "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-        "config": config_dict(shape, args, copies, touched),
+        "config": config_dict(shape, args),
+        "l2_reuse": {"weight_copies_cycled": copies, "weight_bytes_between_reuses": touched * copies},
+        "timing": {"windows": windows, "window_ms": win_ms, "reported": "median window"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2 * world,
-                "d2h_bytes_per_step": (T * H * 2 + T * K * 8) * world},
-        "roofline": {"kernel": "whole layer on one expert-parallel rank", "bound": "hbm", "achieved": achieved,
-                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_kind,
-                     "traffic": None, "algorithmic_bytes_per_launch": layer_bytes,
-                     "launch_ms": ms / args.steps},
+                "d2h_bytes_per_step": (T * H * 2 + T * K * 8) * world, "steps": e2e_steps},
+        "roofline": roofline,
         "expert_parallel": {"experts_per_gpu": e_loc, "rows_received_per_rank": rows_all,
                             "placement": "replicated, calibrated on a separate batch",
                             "replicas_per_expert": [len(r) for r in placement],
@@ -456,15 +586,139 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     dist.destroy_process_group()
 
 
+def single_gpu_layer(args, shape, li, local, eng, L, uploaded, sample_clocks=True):
+    """One configuration on one GPU: value, stages and e2e.  `uploaded` is
+    the set of layer slots of `eng` that already hold this layer (slot 0 at
+    least); more copies are uploaded when a step touches little."""
+    import ctypes as C
+    import torch
+
+    T, H, K = li.x.shape[0], shape.hidden, shape.top_k
+    cfg = L.Engine.cfg(shape)
+    x = torch.from_numpy(li.x.view(np.int16)).cuda()
+    y = torch.empty((T, H), dtype=torch.int16, device="cuda")
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    # one call tells which experts the batch routes to, hence the weight
+    # bytes a step reads and how many copies of the layer to cycle through
+    eng.forward(cfg, x, T, y_bf16=y, ids=ids, w=w, stream=sp)
+    eng.sync(sp)
+    routed = int((eng.read(L.BUF_GROUP_COUNT, (shape.experts,), np.uint32) > 0).sum())
+    touched = (routed + (1 if shape.shared else 0)) * expert_bytes(shape)
+    copies = weight_copies(touched)
+    for layer in range(1, copies):
+        if layer not in uploaded:
+            eng.upload_layer(li, layer=layer)
+            uploaded.add(layer)
+    cfgs = [cfg] + [L.Engine.cfg(shape, layer=layer) for layer in range(1, copies)]
+    calls = [0]
+
+    def next_cfg():
+        calls[0] += 1
+        return cfgs[(calls[0] - 1) % copies]
+
+    def step():
+        eng.forward(next_cfg(), x, T, y_bf16=y, ids=ids, w=w, stream=sp)
+
+    step_s = warmup_step_seconds(step, args.warmup)
+    eng.sync(sp)
+    launches_per_step = eng.launches()
+    windows = windows_for(step_s, args.steps)
+    clk = None
+    if sample_clocks:
+        with ClockSampler(local) as clk:
+            win_ms = timed_windows(step, args.steps, windows, stream)
+    else:
+        win_ms = timed_windows(step, args.steps, windows, stream)
+    eng.sync(sp)
+    ms = float(np.median(win_ms))
+    value = T * args.steps / (ms / 1000.0)
+
+    # per-stage breakdown: the same steps again with events between the
+    # stages (kept out of the headline region above)
+    eng.profile_enable(args.steps)
+    for _ in range(args.steps):
+        step()
+    eng.sync(sp)
+    stage_ms, prof_calls = eng.profile_read()
+    eng.profile_enable(0)
+    stages = {k: v / max(prof_calls, 1) for k, v in stage_ms.items()}
+
+    # end to end through the host-buffer C-ABI call
+    xh = torch.from_numpy(li.x.view(np.int16)).pin_memory()
+    yh = torch.empty((T, H), dtype=torch.int16).pin_memory()
+    idsh = torch.empty((T, K), dtype=torch.int32).pin_memory()
+    wh = torch.empty((T, K), dtype=torch.float32).pin_memory()
+    lib = L.load()
+
+    def step_host():
+        ok = lib.moe_b200_layer_forward_host(eng.h, C.byref(next_cfg()), xh.data_ptr(), T, yh.data_ptr(), None,
+                                             idsh.data_ptr(), wh.data_ptr(), None, eng.err)
+        if not ok:
+            raise L.MoEError(eng.err.value.decode())
+
+    for _ in range(3):
+        step_host()
+    torch.cuda.synchronize()
+    e2e_steps = max(args.steps, int(math.ceil(2.0 / max(step_s, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        step_host()
+    torch.cuda.synchronize()
+    e2e_value = T * e2e_steps / (time.perf_counter() - t0)
+
+    counts = eng.read(L.BUF_GROUP_COUNT, (shape.experts,), np.uint32)
+    distinct = int((counts > 0).sum())
+    return dict(value=value, ms=ms, win_ms=win_ms, windows=windows, stages=stages, e2e=e2e_value,
+                e2e_steps=e2e_steps, distinct=distinct, copies=copies, touched=touched,
+                launches=launches_per_step, clk=clk)
+
+
+def decode_sweep(args, local, L, synth):
+    """Config 1 at each decode batch size of its sweep, with the whole-layer
+    HBM fraction (algorithmic bytes / step time against the measured copy
+    bandwidth)."""
+    import torch
+    shape = synth.CONFIGS[1]
+    hbm, _, peak_kind = measured_peaks()
+    eng = L.Engine(local, max_layers=MAX_COPIES)
+    points = []
+    try:
+        li0 = synth.make_layer(shape, seed=0, tokens=256)
+        eng.upload_layer(li0)
+        uploaded = {0}
+        for T in synth.DECODE_SWEEP:
+            li = synth.LayerInputs(shape, li0.router, li0.gate, li0.up, li0.down,
+                                   synth.gen_tokens(shape, T, 0, li0.mu), mu=li0.mu)
+            r = single_gpu_layer(args, shape, li, local, eng, L, uploaded, sample_clocks=False)
+            step_ms = r["ms"] / args.steps
+            lb = layer_bytes(shape, T, r["distinct"])
+            ach = lb / (step_ms / 1e3) / 1e9
+            points.append({"tokens": T, "tokens_per_s": r["value"], "ms_per_step": step_ms,
+                           "e2e_tokens_per_s": r["e2e"], "distinct_experts": r["distinct"],
+                           "algorithmic_bytes": lb, "achieved_gbs": ach, "hbm_frac": ach / hbm,
+                           "weight_copies_cycled": r["copies"], "stages_ms_per_step": r["stages"]})
+        torch.cuda.synchronize()
+    finally:
+        eng.close()
+    return {"workload": f"config1: H{shape.hidden} E{shape.experts} top{shape.top_k} I{shape.intermediate} "
+                        f"SwiGLU MXFP4, skew {shape.skew}", "peak_gbs": hbm, "peak_source": peak_kind,
+            "points": points}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--config", type=int, default=DEFAULT_CONFIG)
     ap.add_argument("--tokens", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config 1 decode sweep of the default line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     load_pkg()
@@ -472,8 +726,8 @@ def main():
 
     shape = synth.CONFIGS[args.config]
     if args.tokens <= 0:
-        args.tokens = 256 if args.config == 1 else (shape.tokens or sum(synth.prefill_lengths()))
-    metric = "MoE-layer tokens/sec"
+        args.tokens = default_tokens(synth, args.config)
+    metric = METRIC
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -492,7 +746,7 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
 
     li = synth.make_layer(shape, seed=0, tokens=args.tokens)
     if world > 1:  # each rank its own token batch (weak scaling)
@@ -501,141 +755,50 @@ def main():
         return
     eng = L.Engine(local, max_layers=MAX_COPIES)
     eng.upload_layer(li)
-    cfg = L.Engine.cfg(shape)
+    r = single_gpu_layer(args, shape, li, local, eng, L, {0})
     T, H, K = args.tokens, shape.hidden, shape.top_k
-    x = torch.from_numpy(li.x.view(np.int16)).cuda()
-    y = torch.empty((T, H), dtype=torch.int16, device="cuda")
-    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
-    w = torch.empty((T, K), dtype=torch.float32, device="cuda")
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-
-    # one call tells which experts the batch routes to, hence the weight
-    # bytes a step reads and how many copies of the layer to cycle through
-    eng.forward(cfg, x, T, y_bf16=y, ids=ids, w=w, stream=sp)
-    eng.sync(sp)
-    routed = int((eng.read(L.BUF_GROUP_COUNT, (shape.experts,), np.uint32) > 0).sum())
-    touched = (routed + (1 if shape.shared else 0)) * expert_bytes(shape)
-    copies = weight_copies(touched)
-    for layer in range(1, copies):
-        eng.upload_layer(li, layer=layer)
-    cfgs = [cfg] + [L.Engine.cfg(shape, layer=layer) for layer in range(1, copies)]
-    calls = [0]
-
-    def next_cfg():
-        calls[0] += 1
-        return cfgs[(calls[0] - 1) % copies]
-
-    def step():
-        eng.forward(next_cfg(), x, T, y_bf16=y, ids=ids, w=w, stream=sp)
-
-    for _ in range(args.warmup):
-        step()
-    eng.sync(sp)
-    launches_per_step = eng.launches()
-
-    # ---- device-timed region: inputs resident in HBM ----
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        start.record(stream)
-        for _ in range(args.steps):
-            step()
-        end.record(stream)
-        torch.cuda.synchronize()
-    eng.sync(sp)
-    ms = start.elapsed_time(end)
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
-    value = T * args.steps * world / (ms / 1000.0)
-
-    # ---- per-stage breakdown: the same steps again with events between the
-    # stages (kept out of the headline region above) ----
-    eng.profile_enable(args.steps)
-    for _ in range(args.steps):
-        step()
-    eng.sync(sp)
-    stage_ms, prof_calls = eng.profile_read()
-    eng.profile_enable(0)
-
-    # ---- end to end through the host-buffer C-ABI call ----
-    xh = torch.from_numpy(li.x.view(np.int16)).pin_memory()
-    yh = torch.empty((T, H), dtype=torch.int16).pin_memory()
-    idsh = torch.empty((T, K), dtype=torch.int32).pin_memory()
-    wh = torch.empty((T, K), dtype=torch.float32).pin_memory()
-    lib = L.load()
-    import ctypes as C
-
-    def step_host():
-        ok = lib.moe_b200_layer_forward_host(eng.h, C.byref(next_cfg()), xh.data_ptr(), T, yh.data_ptr(), None,
-                                             idsh.data_ptr(), wh.data_ptr(), None, eng.err)
-        if not ok:
-            raise L.MoEError(eng.err.value.decode())
-
-    for _ in range(10):
-        step_host()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e2e_steps = max(200, args.steps)  # host wall clock: a longer window for a steadier figure
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        step_host()
-    torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e_value = T * e2e_steps * world / e2e_s
-
-    # ---- roofline of the dominant kernel (gate/up grouped GEMM) ----
-    counts = eng.read(L.BUF_GROUP_COUNT, (shape.experts,), np.uint32)
-    distinct = int((counts > 0).sum())
-    P = T * K
-    # algorithmic bytes: MXFP4 weights of the experts routed to (17 bytes per
-    # 32 elements) + the permuted activation rows in + the intermediate rows
-    # out, both at 2 bytes per element (bf16, or the E4M3 hi/lo pair)
-    Kp = H
-    Ip = shape.intermediate
-    gu_weight_bytes = distinct * 2 * shape.intermediate * H * 17 / 32
-    gu_bytes = gu_weight_bytes + P * Kp * 2 + P * Ip * 2
-    gu_ms = stage_ms["gate_up"] / max(prof_calls, 1)
-    hbm, bf16, peak_kind = measured_peaks()
-    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
-    dn_ms = stage_ms["down"] / max(prof_calls, 1)
-    dn_bytes = distinct * shape.intermediate * H * 17 / 32 + P * Ip * 2 + P * H * 4
-
+    stages = r["stages"]
+    gu_ms, dn_ms = stages["gate_up"], stages["down"]
+    hbm, _, peak_kind = measured_peaks()
+    P = T * K + (T if shape.shared else 0)
+    if is_prefill(args.config):
+        roofline = tensor_roofline(shape, T, gu_ms, dn_ms, profiled_traffic(args.config, T))
+    else:
+        # gate/up: the routed experts' gate and up weights + the permuted
+        # rows in + the intermediate out, at 2 bytes per element
+        gu_bytes = (r["distinct"] + (1 if shape.shared else 0)) * 2 * shape.intermediate * H * 17 / 32 \
+            + P * H * 2 + P * shape.intermediate * 2
+        achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
+        roofline = {"kernel": "gemm_bs_kernel<gate_up>", "bound": "hbm", "achieved": achieved, "peak": hbm,
+                    "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_kind,
+                    "traffic": profiled_traffic(args.config, T), "algorithmic_bytes_per_launch": gu_bytes,
+                    "launch_ms": gu_ms, "distinct_experts": r["distinct"]}
+    step_ms = r["ms"] / args.steps
+    lf = layer_flops(shape, T)
     result = {
-        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "metric": metric, "value": r["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-        "config": config_dict(shape, args, copies, touched),
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
-                "d2h_bytes_per_step": T * H * 2 + T * K * 8},
-        "roofline": {"kernel": "gemm_bs_kernel<gate_up>", "bound": "hbm", "achieved": achieved, "peak": hbm,
-                     "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_kind,
-                     "traffic": profiled_traffic(args), "algorithmic_bytes_per_launch": gu_bytes,
-                     "launch_ms": gu_ms, "distinct_experts": distinct},
-        "stages_ms_per_step": {k: v / max(prof_calls, 1) for k, v in stage_ms.items()},
-        "down_gemm": {"achieved_gbs": dn_bytes / (dn_ms / 1000.0) / 1e9, "launch_ms": dn_ms},
-        "gpu_launches": launches_per_step * args.steps,
-        "clocks": clk.summary(),
+        "config": config_dict(shape, args),
+        "l2_reuse": {"weight_copies_cycled": r["copies"], "weight_bytes_between_reuses": r["touched"] * r["copies"]},
+        "timing": {"windows": r["windows"], "window_ms": r["win_ms"], "reported": "median window"},
+        "e2e": {"value": r["e2e"], "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2 + T * K * 8, "steps": r["e2e_steps"]},
+        "roofline": roofline,
+        "layer": {"algorithmic_flops": lf, "tflops": lf / (step_ms / 1e3) / 1e12,
+                  "frac_of_mxfp4_peak": lf / (step_ms / 1e3) / 1e12 / MXFP4_TFLOPS,
+                  "algorithmic_bytes": layer_bytes(shape, T, r["distinct"]),
+                  "distinct_experts": r["distinct"]},
+        "stages_ms_per_step": stages,
+        "gpu_launches": r["launches"] * args.steps,
+        "clocks": r["clk"].summary() if r["clk"] else None,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        li_cpu = synth.make_layer(shape, seed=0, tokens=args.tokens)
-        result["cpu_baseline"] = cpu_baseline(li_cpu)
-    if rank == 0:
-        print(json.dumps(result), flush=True)
     eng.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+    if args.config == DEFAULT_CONFIG and not args.no_sweep:
+        result["decode_sweep"] = decode_sweep(args, local, L, synth)
+    if not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(li, shape, args.config)
+    print(json.dumps(result), flush=True)
 
 
 if __name__ == "__main__":
