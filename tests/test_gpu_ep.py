@@ -1,11 +1,14 @@
-"""Expert-parallel forward on two GPUs (moe_b200_ep_layer_forward over NCCL).
+"""Expert-parallel forward on two GPUs (moe_b200_ep_layer_forward: rows
+exchanged by this library's kernels over NVLink peer memory).
 
 Each rank owns half of the experts and feeds its own tokens; its output must
 match the CPU oracle's layer on those tokens under the same bars as the
 single-device tests (routing bit-exact, output within tolerance).  Cases
 cover a decode-sized batch, an idle rank (no tokens, still serving its
-experts) with the shared expert, and a batch past the single-block
-permutation limit.  Skipped with fewer than two GPUs.
+experts) with the shared expert, a batch past the single-block permutation
+limit, a replicated placement, and the dimensions of the largest benchmark
+configuration (H=7168, 256 experts, top-8, shared expert; 128 experts per
+rank).  Skipped with fewer than two GPUs.
 """
 import os
 import sys
@@ -41,7 +44,7 @@ def _rank_main(rank, uid, case, q):
 
     H, I, E, K, tokens, shared = case[:6]
     placement = case[6] if len(case) > 6 else None
-    shape = synth.small_shape(hidden=H, intermediate=I, experts=E, top_k=K, tokens=8, shared=shared)
+    shape = synth.small_shape(name="ep", hidden=H, intermediate=I, experts=E, top_k=K, tokens=8, shared=shared)
     li = synth.make_layer(shape, seed=23)
     T = tokens[rank]
     x = synth.gen_tokens(shape, T, seed=500 + rank, mu=None) if T else np.zeros((0, H), np.uint16)
@@ -76,12 +79,13 @@ CASES = [
     (256, 320, 8, 3, (64, 0), True),
     (128, 128, 8, 4, (2100, 700), False),
     (256, 320, 8, 3, (96, 80), True, REPLICATED),
+    (7168, 2048, 256, 8, (48, 40), True),
 ]
 
 
 @pytest.mark.skipif(_gpus() < WORLD, reason="needs two GPUs")
 @pytest.mark.parametrize("case", CASES, ids=["decode", "idle_rank_shared", "past_single_block_sort",
-                                            "replicated_placement"])
+                                            "replicated_placement", "config4_dims"])
 def test_expert_parallel_forward_matches_oracle(case):
     import multiprocessing as mp
     from conftest import load_pkg

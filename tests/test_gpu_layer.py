@@ -5,7 +5,15 @@ Bars:
   * permutation order: exact (moe_pc_group_tokens_by_expert order);
   * weight decode: bit-exact;
   * layer output: max abs err <= 2e-2 and mean rel err <= 1e-2, where
-    mean rel err = mean(|y - y_ref|) / mean(|y_ref|) over all elements.
+    mean rel err = mean(|y - y_ref|) / mean(|y_ref|) over all elements;
+  * the bf16 output is the round-to-nearest-even of the fp32 output, bit for
+    bit, and lies within the bar plus its own half unit in the last place:
+    at H = 7168 outputs reach |y| >= 8, where bf16's half-ulp alone is 0.031,
+    so no bf16 output could meet an absolute 2e-2 there.
+The cross-check GEMM paths (CUDA-core and TMEM-decode, test only) round the
+SwiGLU intermediate to bf16; at H = 7168 that rounding alone brings the
+output error to ~2e-2, so they are held to CROSSCHECK_MAX_ABS there.  The
+product path (block-scaled) meets the 2e-2 bar at every shape.
 """
 import numpy as np
 import pytest
@@ -16,6 +24,7 @@ pytestmark = pytest.mark.gpu
 
 MAX_ABS = 2e-2
 MEAN_REL = 1e-2
+CROSSCHECK_MAX_ABS = 3e-2  # cross-check paths (bf16 intermediate) at H >= 4096
 LAYER_FIXTURES = sorted(p.name for p in GOLDEN.glob("layer_*.npz"))
 
 
@@ -30,6 +39,23 @@ def bf16_to_f32(b):
 def errors(y, ref):
     d = np.abs(y.astype(np.float64) - ref.astype(np.float64))
     return float(d.max()), float(d.mean() / max(np.abs(ref).mean(), 1e-30))
+
+
+def f32_to_bf16_rne(y):
+    b = np.ascontiguousarray(y, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def check_bf16_output(y16, y32, ref, max_abs=MAX_ABS):
+    """The bf16 output: exactly the rounding of the fp32 output, and within
+    the bar plus its own half-ulp of the reference value."""
+    assert np.array_equal(y16, f32_to_bf16_rne(y32)), "bf16 output is not the rounding of the fp32 output"
+    _, e = np.frexp(np.abs(ref.astype(np.float64)))
+    half_ulp = np.ldexp(1.0, e - 9)
+    d = np.abs(bf16_to_f32(y16).astype(np.float64) - ref.astype(np.float64))
+    assert np.all(d <= max_abs + half_ulp), float((d - half_ulp).max())
+    _, mr = errors(bf16_to_f32(y16), ref)
+    assert mr <= MEAN_REL, mr
 
 
 @pytest.fixture(scope="module")
@@ -95,10 +121,10 @@ def check_layer_fixture(name, path, engine, synth, L):
     counts = engine.read(L.BUF_GROUP_COUNT, (E + int(li.shape.shared),), np.uint32)
     assert np.array_equal(counts[:E], np.bincount(out["ids"].ravel(), minlength=E))
     # layer output within tolerance, fp32 and bf16 outputs
+    bar = CROSSCHECK_MAX_ABS if path != L.GEMM_BLOCKSCALED and li.shape.hidden >= 4096 else MAX_ABS
     mx, mr = errors(out["y_f32"], g["y"])
-    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
-    mx2, mr2 = errors(bf16_to_f32(out["y_bf16"]), g["y"])
-    assert mx2 <= MAX_ABS and mr2 <= MEAN_REL, (mx2, mr2)
+    assert mx <= bar and mr <= MEAN_REL, (mx, mr)
+    check_bf16_output(out["y_bf16"], out["y_f32"], g["y"], bar)
     engine.sync()
 
 

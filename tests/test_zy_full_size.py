@@ -12,11 +12,14 @@ the ones whose cost does not grow with the batch, plus a seeded sample:
     output does not depend on the other tokens of the batch).
 Inputs are the bench's own (synth.make_layer(shape, seed=0, tokens=T)).
 Config 4 (16,384 tokens of H = 7168, 256 experts, top-8, one shared expert)
-is the largest: its bf16 output rounding alone is close to the 2e-2 bar, so
-the test prints the sample's measured error for the fp32 and bf16 outputs.
+is the largest; the test prints the sample's measured error for the fp32 and
+bf16 outputs.  The bf16 output is checked as the rounding of the fp32 output
+(bf16's own half-ulp at |y| >= 8 exceeds the absolute bar).
 """
 import numpy as np
 import pytest
+
+from test_gpu_layer import check_bf16_output
 
 pytestmark = pytest.mark.gpu
 
@@ -88,4 +91,4 @@ def test_full_size_configuration(engine, synth, L, port, config):
     print(f"config {config}: sample of {len(sample)} tokens, fp32 output max abs {mx:.3e} mean rel {mr:.3e}; "
           f"bf16 output max abs {mx16:.3e} mean rel {mr16:.3e}")
     assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
-    assert mx16 <= MAX_ABS and mr16 <= MEAN_REL, (mx16, mr16)
+    check_bf16_output(out["y_bf16"][sample], out["y_f32"][sample], y_ref)
