@@ -50,7 +50,14 @@ enum {
 enum {
     MOE_B200_GEMM_BLOCKSCALED = 0, /* tcgen05 kind::mxf8f6f4 block-scaled MMA on the E2M1 codes (default) */
     MOE_B200_GEMM_SIMT = 1,        /* CUDA-core grouped GEMMs, a cross-check for tests */
-    MOE_B200_GEMM_TMEM_DECODE = 2  /* tcgen05 kind::f16 with weights decoded to bf16 in TMEM */
+    MOE_B200_GEMM_TMEM_DECODE = 2, /* tcgen05 kind::f16 with weights decoded to bf16 in TMEM */
+    /* Opt-in fast mode, NOT within the layer tolerance: the activations and
+     * the SwiGLU intermediate are quantised to E2M1 with one E8M0 scale per
+     * 32 elements (like the weights) and both grouped GEMMs run tcgen05
+     * kind::mxf4 (FP4 x FP4).  Routing (ids, weights, permutation) is the
+     * exact path's; the output error is a few percent (measured figures are
+     * in the tests and the bench).  Single-device forward only. */
+    MOE_B200_GEMM_MXF4_FAST = 3
 };
 
 /* Explicit form of the routing metadata the reference reads from GGUF JSON

@@ -39,6 +39,10 @@ int check_dims(const moe_b200_layer_cfg_t* c, char* err) {
         set_err(err, "experts=%u outside 1..1024", c->experts);
         return 0;
     }
+    if (c->gemm_path < MOE_B200_GEMM_BLOCKSCALED || c->gemm_path > MOE_B200_GEMM_MXF4_FAST) {
+        set_err(err, "unknown gemm_path %d", c->gemm_path);
+        return 0;
+    }
     if (c->top_k == 0 || c->top_k > 32 || c->top_k > c->experts) {
         set_err(err, "top_k=%u outside 1..min(32, experts)", c->top_k);
         return 0;
@@ -67,15 +71,15 @@ int get_encoder(moe_b200_engine* eng, char* err) {
 // 2-D tiled tensor map with 128-byte swizzle.  `cols` counts elements of
 // `dtype`; `row_bytes` is the global row stride.
 int make_tmap2d(moe_b200_engine* eng, CUtensorMap* map, CUtensorMapDataType dtype, void* base, uint64_t cols,
-                uint64_t rows, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, char* err) {
+                uint64_t rows, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, char* err,
+                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     if (!get_encoder(eng, err)) return 0;
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {row_bytes};
     const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = eng->encode(map, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = eng->encode(map, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_err(err, "cuTensorMapEncodeTiled failed (%d)", (int)r);
         return 0;
@@ -226,6 +230,25 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
         DevBuf* buf;
         uint32_t cols;
     } specs[2] = {{eng->tmap_xb, &eng->xb, Kq}, {eng->tmap_hb, &eng->hb, Iq}};
+    for (int i = 0; i < 2 && job.fp4; ++i) {
+        // fast mode: [rows][cols / 2] packed E2M1 bytes at the start of the
+        // same buffer, 64-byte boxes of 32, 64 or 128 rows
+        CUtensorMap* maps = i == 0 ? eng->tmap_xq : eng->tmap_hq;
+        const uint64_t rows = specs[i].buf->bytes / (2ull * specs[i].cols);
+        const uint64_t rb = specs[i].cols / 2;
+        if (eng->fp4_map_key[i] != specs[i].buf->ptr || eng->fp4_map_dims[i][0] != specs[i].cols ||
+            eng->fp4_map_dims[i][1] != rows) {
+            for (int b = 0; b < 3; ++b) {
+                if (!make_tmap2d(eng, &maps[b], CU_TENSOR_MAP_DATA_TYPE_UINT8, specs[i].buf->ptr, rb, rows, rb, 64,
+                                 32u << b, err, CU_TENSOR_MAP_SWIZZLE_64B)) {
+                    return 0;
+                }
+            }
+            eng->fp4_map_key[i] = specs[i].buf->ptr;
+            eng->fp4_map_dims[i][0] = specs[i].cols;
+            eng->fp4_map_dims[i][1] = rows;
+        }
+    }
     for (int i = 0; i < 2; ++i) {
         const uint64_t rows = specs[i].buf->bytes / (2ull * specs[i].cols);
         if (eng->bs_map_key[i] != specs[i].buf->ptr || eng->bs_map_dims[i][0] != specs[i].cols ||
@@ -271,7 +294,16 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     mark(2);
     // permuted source rows as exact hi/lo E4M3 terms + their scale blocks
     const uint64_t xb_rows = eng->xb.bytes / (2ull * Kq), hb_rows = eng->hb.bytes / (2ull * Iq);
-    if (job.K > 1 && job.K <= 32 && (job.shared_rows == 0 || (job.shared_base == 0 && job.shared_rows == job.T))) {
+    const bool per_token = job.K <= 32 && (job.shared_rows == 0 || (job.shared_base == 0 && job.shared_rows == job.T));
+    if (job.fp4) {
+        if (!per_token) {
+            set_err(err, "the fast mode runs the single-device layer only");
+            return 0;
+        }
+        CK(launch_scatter_quant_fp4(job.src, H, Kq, job.T, job.K, eng->pos_of.as<uint32_t>(),
+                                    job.shared_rows ? gi.offset + job.E : nullptr, eng->row_info.as<uint32_t>(), P,
+                                    eng->xb.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(), st, true));
+    } else if (job.K > 1 && per_token) {
         // each token row feeds K (+1 shared) permuted rows: split it once
         CK(launch_scatter_quant_bs(job.src, H, Kq, job.T, job.K, eng->pos_of.as<uint32_t>(),
                                    job.shared_rows ? gi.offset + job.E : nullptr, eng->row_info.as<uint32_t>(), P,
@@ -301,11 +333,12 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     bp.sfb_atoms = eng->sfx_atoms.as<uint8_t>();
     bp.h_out = eng->hb.as<uint8_t>();
     bp.h_plane = hb_rows * Iq;
-    bp.h_stride = Iq;
+    bp.h_stride = job.fp4 ? Iq / 2 : Iq;
     bp.sfh_atoms = eng->sfh_atoms.as<uint8_t>();
     bp.m_valid = Iq;
     const int bi = block_n == 32 ? 0 : (block_n == 64 ? 1 : 2);
-    CK(launch_gemm_bs(kGateUp, (int)block_n, L->tmap_gu_codes, eng->tmap_xb[bi], bp, eng->num_sms, st, true));
+    CK(launch_gemm_bs(kGateUp, (int)block_n, job.fp4 ? L->tmap_gu_fp4 : L->tmap_gu_codes,
+                      job.fp4 ? eng->tmap_xq[bi] : eng->tmap_xb[bi], bp, eng->num_sms, st, true, job.fp4));
     *launches += 1;
     mark(4);
     // down: K = I (padded Iq), M = H rows (padded rp_h), output fp32 rows
@@ -326,7 +359,8 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     bp.ret_base = job.ret_base;
     bp.ret_rows = job.ret_rows;
     bp.ret_world = job.ret_world;
-    CK(launch_gemm_bs(kDown, (int)block_n, L->tmap_dn_codes, eng->tmap_hb[bi], bp, eng->num_sms, st, true));
+    CK(launch_gemm_bs(kDown, (int)block_n, job.fp4 ? L->tmap_dn_fp4 : L->tmap_dn_codes,
+                      job.fp4 ? eng->tmap_hq[bi] : eng->tmap_hb[bi], bp, eng->num_sms, st, true, job.fp4));
     *launches += 1;
     mark(5);
     return 1;
@@ -480,7 +514,11 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
         if (!make_tmap2d(eng, &L->tmap_gu_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_gu_codes.ptr, 128,
                          slots * 2 * L->rp_i * (L->kq / 128), 64, 128, 128, err) ||
             !make_tmap2d(eng, &L->tmap_dn_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_dn_codes.ptr, 128,
-                         slots * L->rp_h * (L->iq / 128), 64, 128, 128, err)) {
+                         slots * L->rp_h * (L->iq / 128), 64, 128, 128, err) ||
+            !make_tmap2d(eng, &L->tmap_gu_fp4, CU_TENSOR_MAP_DATA_TYPE_UINT8, L->bs_gu_codes.ptr, 64,
+                         slots * 2 * L->rp_i * (L->kq / 128), 64, 64, 128, err, CU_TENSOR_MAP_SWIZZLE_64B) ||
+            !make_tmap2d(eng, &L->tmap_dn_fp4, CU_TENSOR_MAP_DATA_TYPE_UINT8, L->bs_dn_codes.ptr, 64,
+                         slots * L->rp_h * (L->iq / 128), 64, 64, 128, err, CU_TENSOR_MAP_SWIZZLE_64B)) {
             return 0;
         }
         L->present.assign(L->E + 1, 0);
@@ -578,7 +616,8 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     CK(eng->g_offset.reserve((size_t)(G + 1) * 4));
     CK(eng->g_gu_off.reserve((size_t)(G + 1) * 4));
     CK(eng->g_dn_off.reserve((size_t)(G + 1) * 4));
-    const bool bs = cfg->gemm_path == MOE_B200_GEMM_BLOCKSCALED;
+    const bool fp4 = cfg->gemm_path == MOE_B200_GEMM_MXF4_FAST;
+    const bool bs = cfg->gemm_path == MOE_B200_GEMM_BLOCKSCALED || fp4;
     CK(eng->yperm.reserve((size_t)P * H * 4));
     if (!bs) {
         // the cross-check GEMMs read the tile form
@@ -640,6 +679,7 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         job.group_slot = nullptr;
         job.y = eng->yperm.as<float>();
         job.y_by_source = false;
+        job.fp4 = fp4;
         if (!run_blockscaled(eng, L, job, st, ev, &launches, err)) return 0;
     } else {
     GroupInfo gi;

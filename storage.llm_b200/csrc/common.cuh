@@ -309,6 +309,61 @@ __device__ __forceinline__ uint32_t idesc_bs_m128(uint32_t n, uint32_t sf_id) {
            | (sf_id << 29);      // A scale-factor id
 }
 
+// ---------------------------------------------------------------------------
+// Block-scaled MMA on packed FP4 operands (kind::mxf4, the fast mode): A and
+// B both E2M1, two codes per byte in shared memory, K = 64 per instruction,
+// one E8M0 scale per 32 K (scale_vec::2X: the two scale bytes of an MMA are
+// bytes sf_id and sf_id + 1 of each row's scale word, sf_id = 0 or 2).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_fp4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+}
+
+// Instruction descriptor for kind::mxf4: A and B E2M1, E8M0 scales, both
+// K-major, M = 128, N = n, K = 64; `sf_id` (0 or 2) picks the scale bytes.
+__device__ __forceinline__ uint32_t idesc_fp4_m128(uint32_t n, uint32_t sf_id) {
+    return (sf_id << 4)          // B scale-factor id
+           | (1u << 7)           // A format E2M1
+           | (1u << 10)          // B format E2M1
+           | ((n >> 3) << 17)    // N / 8
+           | (1u << 23)          // scale format E8M0
+           | ((128u >> 4) << 24) // M / 16
+           | (sf_id << 29);      // A scale-factor id
+}
+
+// Shared-memory descriptor, K-major with 64-byte swizzle: 64-byte rows (128
+// packed FP4 codes), 8-row groups 512 bytes apart (what a TMA SWIZZLE_64B box
+// of 64 bytes per row writes).  `addr` lies in a 512-byte aligned tile;
+// advancing K by 64 codes adds 32 bytes.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFF) >> 4);   // start address
+    d |= (uint64_t)1 << 16;                   // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(512 >> 4) << 32;          // stride byte offset: 8 rows x 64 B
+    d |= (uint64_t)1 << 46;                   // descriptor version (sm_100)
+    d |= (uint64_t)4 << 61;                   // SWIZZLE_64B
+    return d;
+}
+
+// Two fp32 values to E2M1 codes by the hardware conversion (round to nearest
+// even, saturating at +-6): the first argument in the low nibble.
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
+    uint32_t d;
+    asm("{\n\t.reg .b8 t;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\t"
+        "cvt.u32.u8 %0, t;\n\t}"
+        : "=r"(d)
+        : "f"(hi), "f"(lo));
+    return d;
+}
+
 // Shared-memory descriptor of a 32 x 128-bit scale-factor block (no swizzle,
 // 16-byte rows, 8-row core matrices 128 bytes apart), the source of
 // tcgen05.cp.32x128b.

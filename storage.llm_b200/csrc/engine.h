@@ -80,6 +80,9 @@ struct LayerWeights {
     std::vector<uint8_t> tile_ready;  // [E+1]: slot's tile form is current
     uint32_t rp_i = 0, rp_h = 0, kq = 0, iq = 0;  // rows padded to 128, K padded to 128
     CUtensorMap tmap_gu_codes{}, tmap_dn_codes{};
+    // the same codes as packed bytes (64-byte rows, 64-byte swizzle) for the
+    // fast mode's kind::mxf4 GEMMs
+    CUtensorMap tmap_gu_fp4{}, tmap_dn_fp4{};
     void release_all() {
         router.release();
         gu.release();
@@ -123,6 +126,10 @@ struct moe_b200_engine {
     CUtensorMap tmap_xb[3]{}, tmap_hb[3]{};
     const void* bs_map_key[2] = {nullptr, nullptr};
     uint64_t bs_map_dims[2][2] = {};
+    // fast mode: 2-D byte maps over the same buffers holding packed E2M1 rows
+    CUtensorMap tmap_xq[3]{}, tmap_hq[3]{};
+    const void* fp4_map_key[2] = {nullptr, nullptr};
+    uint64_t fp4_map_dims[2][2] = {};
     // host-call staging
     DevBuf hx, hy, hyf, hids, hw, hperm_out, tri;
     // host-buffer entry points: their own non-blocking stream, and a pinned
@@ -176,6 +183,7 @@ struct BsJob {
     const uint32_t* ret_base = nullptr;
     uint32_t ret_rows = 0;
     uint32_t ret_world = 0;
+    bool fp4 = false;            // fast mode: E2M1 activations, kind::mxf4 GEMMs
 };
 
 // Enqueues the pipeline on `st`; fills the engine's permutation buffers

@@ -46,18 +46,21 @@
 
 namespace moe_b200 {
 
-template <int MODE, int BN>
+// FP4: the fast mode (kind::mxf4): A and B packed E2M1 in shared memory, one
+// B term, 64-byte swizzled rows (one 128-K stage per row).
+template <int MODE, int BN, bool FP4 = false>
 struct BsCfg {
     static_assert(BN == 32 || BN == 64 || BN == 128, "tile width");
-    static constexpr bool kStackN = BN <= 64;
+    static constexpr bool kStackN = !FP4 && BN <= 64;
     static constexpr int kNA = MODE == kGateUp ? 2 : 1;       // A operands per stage
-    static constexpr int kABytes = 128 * 128;                 // smem bytes per A box
+    static constexpr int kABytes = FP4 ? 128 * 64 : 128 * 128;  // smem bytes per A box
     static constexpr int kATx = 128 * 128 / 2;                // packed bytes the A box moves
-    static constexpr int kBBytes = BN * 128;                  // smem bytes per B term (hi or lo)
+    static constexpr int kBTerms = FP4 ? 1 : 2;               // B terms per stage (hi, lo)
+    static constexpr int kBBytes = FP4 ? BN * 64 : BN * 128;  // smem bytes per B term
     static constexpr int kSFA = kNA * 512;                    // weight scale bytes per stage
-    static constexpr int kSFB = kStackN ? 512 : 1024;         // activation scale bytes per stage
+    static constexpr int kSFB = (FP4 || kStackN) ? 512 : 1024;  // activation scale bytes per stage
     static constexpr int kSFStage = kSFA + kSFB;
-    static constexpr int kStageBytes = kNA * kABytes + 2 * kBBytes + kSFStage;
+    static constexpr int kStageBytes = kNA * kABytes + kBTerms * kBBytes + kSFStage;
     static constexpr int kStages = (210 * 1024) / kStageBytes;
     static constexpr int kAccCols = kNA * (kStackN ? 2 * BN : BN);
     static constexpr int kAccs = 256 / kAccCols >= 2 ? 2 : 1;
@@ -171,6 +174,15 @@ __device__ __forceinline__ void split_e4m3_x4(const float v[4], uint32_t& hi4, u
     lo4 = cvt_e4m3x2(r[0] * inv2, r[1] * inv2) | (cvt_e4m3x2(r[2] * inv2, r[3] * inv2) << 16);
     s_hi = (uint8_t)(e1 + 127);
     s_lo = (uint8_t)(e2 + 127);
+}
+
+// Scale exponent of a 32-value block for E2M1 codes (fast mode): the
+// smallest e with amax <= 6 * 2^e, so the block maximum is never clipped.
+__device__ __forceinline__ int fp4_block_exp(float amax) {
+    if (!(amax > 0.f)) return -127;
+    int e = max(-127, (int)((__float_as_uint(amax) >> 23) & 0xFF) - 127 - 2);  // amax / 2^e in [4, 8)
+    if (amax > 6.0f * pow2f(e)) ++e;
+    return min(127, e);
 }
 
 // ---------------------------------------------------------------------------
@@ -457,6 +469,98 @@ cudaError_t launch_scatter_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, 
                          shared_off, row_info, rows, rows_cap, xb, sf_atoms);
 }
 
+// Fast mode: each token row split once into E2M1 codes with one E8M0 scale
+// per 32 elements (the smallest scale that keeps the block maximum at or
+// below 6; codes rounded to nearest even by the hardware conversion), stored
+// at each of the token's permuted rows like scatter_quant_bs_kernel:
+// xq [rows_cap][Kp/2] bytes, element 2j in the low nibble of byte j; the
+// four scale bytes of a 128-K stage as one word in the stage's 512-byte
+// scale block of the row's token tile, at sf_row_pos(index in tile).
+__global__ void __launch_bounds__(256) scatter_quant_fp4_kernel(const uint16_t* __restrict__ x, uint32_t H,
+                                                                uint32_t Kp, uint32_t T, uint32_t K,
+                                                                const uint32_t* __restrict__ pos_of,
+                                                                const uint32_t* __restrict__ shared_off,
+                                                                const uint32_t* __restrict__ row_info, uint32_t rows,
+                                                                uint8_t* __restrict__ xq,
+                                                                uint8_t* __restrict__ sf_atoms) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t nkt = Kp / 128;
+    const uint32_t chunks = (nkt + kGqChunk - 1) / kGqChunk;
+    const uint64_t tasks = (uint64_t)T * chunks;
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    pdl_wait();  // the permutation (positions, row info) first
+    pdl_trigger();
+    for (uint64_t task = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; task < tasks; task += warps) {
+        const uint32_t t = (uint32_t)(task / chunks);
+        const uint32_t kt0 = (uint32_t)(task % chunks) * kGqChunk;
+        uint32_t my_pos = 0xFFFFFFFFu, my_info = 0;
+        if (lane < K) {
+            const uint32_t q = __ldg(pos_of + (uint64_t)t * K + lane);
+            if (q < rows) {
+                my_pos = q;
+                my_info = __ldg(row_info + q);
+            }
+        }
+        uint32_t sh_pos = 0xFFFFFFFFu, sh_info = 0;
+        if (shared_off) {
+            const uint32_t q = __ldg(shared_off) + t;
+            if (q < rows) {
+                sh_pos = q;
+                sh_info = __ldg(row_info + q);
+            }
+        }
+        const uint16_t* xr = x + (uint64_t)t * H;
+        uint2 raw[kGqChunk];
+#pragma unroll
+        for (uint32_t c = 0; c < kGqChunk; ++c) {
+            const uint32_t k = (kt0 + c) * 128 + lane * 4;  // H % 8 == 0: four elements all in or all out
+            raw[c] = (kt0 + c < nkt && k < H) ? __ldg(reinterpret_cast<const uint2*>(xr + k)) : make_uint2(0, 0);
+        }
+#pragma unroll
+        for (uint32_t c = 0; c < kGqChunk; ++c) {
+            const uint32_t kt = kt0 + c;
+            if (kt >= nkt) break;  // uniform across the warp
+            const float v[4] = {__uint_as_float(raw[c].x << 16), __uint_as_float(raw[c].x & 0xffff0000u),
+                                __uint_as_float(raw[c].y << 16), __uint_as_float(raw[c].y & 0xffff0000u)};
+            uint32_t m = __float_as_uint(fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+            m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
+            const int e = fp4_block_exp(__uint_as_float(m));
+            const float inv = pow2f(-e);
+            const uint32_t codes = cvt_e2m1x2(v[0] * inv, v[1] * inv) | (cvt_e2m1x2(v[2] * inv, v[3] * inv) << 8);
+            uint32_t sw = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sw |= (uint32_t)(__shfl_sync(0xffffffffu, (uint32_t)(e + 127), 8 * j) & 0xFFu)
+                                              << (8 * j);
+            auto put = [&](uint32_t pos, uint32_t info) {
+                *reinterpret_cast<uint16_t*>(xq + (uint64_t)pos * (Kp / 2) + kt * 64 + lane * 2) = (uint16_t)codes;
+                if (lane == 0) {
+                    uint8_t* atom = sf_atoms + ((uint64_t)(info >> 8) * nkt + kt) * 512;
+                    *reinterpret_cast<uint32_t*>(atom + sf_row_pos(info & 0xFFu)) = sw;
+                }
+            };
+            for (uint32_t j = 0; j < K; ++j) {
+                const uint32_t pos = __shfl_sync(0xffffffffu, my_pos, j);
+                const uint32_t info = __shfl_sync(0xffffffffu, my_info, j);
+                if (pos != 0xFFFFFFFFu) put(pos, info);  // uniform across the warp
+            }
+            if (sh_pos != 0xFFFFFFFFu) put(sh_pos, sh_info);
+        }
+    }
+}
+
+cudaError_t launch_scatter_quant_fp4(const uint16_t* x, uint32_t H, uint32_t Kp, uint32_t T, uint32_t K,
+                                     const uint32_t* pos_of, const uint32_t* shared_off, const uint32_t* row_info,
+                                     uint32_t rows, uint8_t* xq, uint8_t* sf_atoms, cudaStream_t st, bool pdl) {
+    if (T == 0) return cudaSuccess;
+    if (K > 32) return cudaErrorInvalidValue;
+    const uint64_t tasks = (uint64_t)T * ((Kp / 128 + kGqChunk - 1) / kGqChunk);
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((tasks + 7) / 8, 148ull * 8ull);
+    return launch_kernel(scatter_quant_fp4_kernel, dim3(blocks), dim3(256), 0, st, pdl, x, H, Kp, T, K, pos_of,
+                         shared_off, row_info, rows, xq, sf_atoms);
+}
+
 cudaError_t launch_gather_quant_bs(const uint16_t* x, uint32_t H, uint32_t Kp, const uint32_t* row_token,
                                    const uint32_t* row_info, uint32_t rows, uint32_t rows_cap, uint32_t block_n,
                                    uint8_t* xb, uint8_t* sf_atoms, cudaStream_t st, bool pdl) {
@@ -585,14 +689,51 @@ __device__ __forceinline__ void h_store8(const float* hv, uint32_t c0, uint32_t 
     }
 }
 
+// Fast mode: the same 8 columns of SiLU(gate) * up as E2M1 codes for the
+// down GEMM -- per column one 32-element K block (the warp's 32 rows) with
+// one E8M0 scale; lanes 2i and 2i+1 form byte i of the row's packed codes
+// ([rows][h_stride] bytes, element 2i in the low nibble), stored by the even
+// lane; lane j stores column j's scale byte.
 template <int BN>
+__device__ __forceinline__ void h_store8_fp4(const float* hv, uint32_t c0, uint32_t nn, uint64_t row0, uint32_t m,
+                                             uint32_t lane, uint32_t quarter, const BsParams& p, uint8_t* h_atom) {
+    float mx[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mx[j] = warp_max_abs(hv[j]);
+    uint32_t byte[8];
+    uint8_t sc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int e = fp4_block_exp(mx[j]);
+        const uint32_t code = cvt_e2m1x2(hv[j] * pow2f(-e), 0.0f) & 0xFu;
+        byte[j] = code | (__shfl_down_sync(0xffffffffu, code, 1) << 4);
+        sc[j] = (uint8_t)(e + 127);
+    }
+    uint8_t* hp = p.h_out + (row0 + c0) * p.h_stride + (m >> 1);
+    if ((lane & 1u) == 0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (c0 + j < nn) hp[(uint64_t)j * p.h_stride] = (uint8_t)byte[j];
+        }
+    }
+    uint8_t s = sc[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) s = lane == (uint32_t)j ? sc[j] : s;
+    if (lane < 8 && c0 + lane < nn) h_atom[sfb_pos_hi<BN>(c0 + lane) + quarter] = s;
+}
+
+template <int BN, bool FP4 = false>
 __device__ __forceinline__ void gu_store8(const float* g, const float* u, uint32_t c0, uint32_t nn, uint64_t row0,
                                           uint32_t m, uint32_t lane, uint32_t quarter, const BsParams& p,
                                           uint8_t* h_atom) {
     float hv[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) hv[j] = silu_fast(g[j]) * u[j];
-    h_store8<BN>(hv, c0, nn, row0, m, lane, quarter, p, h_atom);
+    if constexpr (FP4) {
+        h_store8_fp4<BN>(hv, c0, nn, row0, m, lane, quarter, p, h_atom);
+    } else {
+        h_store8<BN>(hv, c0, nn, row0, m, lane, quarter, p, h_atom);
+    }
 }
 
 // One warp group's share [cb, cb + W) of a gate/up tile's token columns (the
@@ -600,11 +741,11 @@ __device__ __forceinline__ void gu_store8(const float* g, const float* u, uint32
 // share of the accumulator, then SiLU * up, the hi/lo split and the stores.
 // Stacked tiles drain into registers first, so the release comes before the
 // math and the next tile's MMAs overlap it.
-template <int BN, int W>
+template <int BN, int W, bool FP4 = false>
 __device__ __forceinline__ void gu_tile_part(const BsParams& p, const BsTileX& tc, uint32_t dbase, uint32_t cb,
                                              uint32_t m, uint32_t lane, uint32_t quarter, uint8_t* h_atom,
                                              uint64_t* acc_empty_bar) {
-    constexpr bool kStackN = BN <= 64;
+    constexpr bool kStackN = !FP4 && BN <= 64;
     constexpr uint32_t kLoOff = kStackN ? BN : 0;  // stacked: lo half follows hi
     constexpr uint32_t kProjOff = kStackN ? 2 * BN : BN;
     if constexpr (kStackN) {
@@ -646,19 +787,21 @@ __device__ __forceinline__ void gu_tile_part(const BsParams& p, const BsTileX& t
                 v0[i] = __uint_as_float(a[i]);
                 v1[i] = __uint_as_float(c[i]);
             }
-            gu_store8<BN>(v0, v1, c0, tc.nn, tc.row0, m, lane, quarter, p, h_atom);
-            if (c0 + 8 < tc.nn) gu_store8<BN>(v0 + 8, v1 + 8, c0 + 8, tc.nn, tc.row0, m, lane, quarter, p, h_atom);
+            gu_store8<BN, FP4>(v0, v1, c0, tc.nn, tc.row0, m, lane, quarter, p, h_atom);
+            if (c0 + 8 < tc.nn) {
+                gu_store8<BN, FP4>(v0 + 8, v1 + 8, c0 + 8, tc.nn, tc.row0, m, lane, quarter, p, h_atom);
+            }
         }
         tc_fence_before();
         mbar_arrive(acc_empty_bar);
     }
 }
 
-template <int MODE, int BN>
+template <int MODE, int BN, bool FP4>
 __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                          const __grid_constant__ CUtensorMap tmap_b,
                                                          const BsParams p) {
-    using C = BsCfg<MODE, BN>;
+    using C = BsCfg<MODE, BN, FP4>;
     // gate/up with one accumulator: the scale-factor warps drain and store the
     // upper half of each tile's columns (the MMAs wait for the whole
     // accumulator anyway), halving the epilogue's time per tile
@@ -670,8 +813,8 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
     uint8_t* sf_base = smem;                                                  // [stages][kSFStage]
     uint8_t* a_base = smem + C::kStages * C::kSFStage;                        // [stages][kNA][16 KB]
     a_base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(a_base) + 1023) & ~uintptr_t(1023));
-    uint8_t* b_base = a_base + C::kStages * C::kNA * C::kABytes;              // [stages][hi, lo][kBBytes]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + C::kStages * 2 * C::kBBytes);
+    uint8_t* b_base = a_base + C::kStages * C::kNA * C::kABytes;              // [stages][terms][kBBytes]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + C::kStages * C::kBTerms * C::kBBytes);
     uint64_t* load_full = bars;
     uint64_t* load_empty = load_full + C::kStages;
     uint64_t* sf_full = load_empty + C::kStages;   // scale factors stored in TMEM
@@ -728,7 +871,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 pre = min((uint32_t)C::kStages, p.k_tiles);
                 for (uint32_t kt = 0; kt < pre; ++kt) {
                     uint8_t* sf = sf_base + kt * C::kSFStage;
-                    mbar_arrive_expect_tx(&load_full[kt], C::kNA * C::kATx + C::kSFStage + 2 * C::kBBytes);
+                    mbar_arrive_expect_tx(&load_full[kt], C::kNA * C::kATx + C::kSFStage + C::kBTerms * C::kBBytes);
                     bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, &load_full[kt]);
 #pragma unroll
                     for (int pj = 0; pj < C::kNA; ++pj) {
@@ -749,7 +892,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                     uint8_t* sf = sf_base + stage * C::kSFStage;
                     const bool prefetched = tile == blockIdx.x && kt < pre;
                     if (!prefetched) {
-                        mbar_arrive_expect_tx(&load_full[stage], C::kNA * C::kATx + C::kSFStage + 2 * C::kBBytes);
+                        mbar_arrive_expect_tx(&load_full[stage], C::kNA * C::kATx + C::kSFStage + C::kBTerms * C::kBBytes);
                         bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, &load_full[stage]);
                     }
                     bulk_g2s(sf + C::kSFA, p.sfb_atoms + ((uint64_t)tc.ntile * p.k_tiles + kt) * C::kSFB, C::kSFB,
@@ -761,9 +904,15 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                         tma_load_2d(a_base + (stage * C::kNA + pj) * C::kABytes, &tmap_a, 0, (int32_t)(b * 128),
                                     &load_full[stage]);
                     }
-                    // hi and lo planes of the tile's token rows in one 3-D box
-                    tma_load_3d(b_base + stage * 2 * C::kBBytes, &tmap_b, (int32_t)(kt * 128), (int32_t)tc.row0, 0,
-                                &load_full[stage]);
+                    if constexpr (FP4) {
+                        // the tile's token rows: 64 bytes (128 codes) of each
+                        tma_load_2d(b_base + stage * C::kBBytes, &tmap_b, (int32_t)(kt * 64), (int32_t)tc.row0,
+                                    &load_full[stage]);
+                    } else {
+                        // hi and lo planes of the tile's token rows in one 3-D box
+                        tma_load_3d(b_base + stage * 2 * C::kBBytes, &tmap_b, (int32_t)(kt * 128), (int32_t)tc.row0,
+                                    0, &load_full[stage]);
+                    }
                     if (++stage == C::kStages) {
                         stage = 0;
                         phase ^= 1;
@@ -792,7 +941,20 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                     const uint32_t sfc = tmem + kSfCol0 + stage * C::kSFCols;
                     const uint32_t sfb = sfc + C::kNA * 4;
                     const uint32_t a_addr = smem_u32(a_base + stage * C::kNA * C::kABytes);
-                    const uint32_t b_addr = smem_u32(b_base + stage * 2 * C::kBBytes);
+                    const uint32_t b_addr = smem_u32(b_base + stage * C::kBTerms * C::kBBytes);
+                    if constexpr (FP4) {
+                        // two K = 64 MMAs per 128-K stage, scale bytes {0, 1} then {2, 3}
+#pragma unroll
+                        for (int kk = 0; kk < 2; ++kk) {
+                            const uint32_t idesc = idesc_fp4_m128(n_mma, 2 * kk);
+                            const uint64_t bdesc = smem_desc_sw64(b_addr + kk * 32);
+#pragma unroll
+                            for (int pj = 0; pj < C::kNA; ++pj) {
+                                const uint64_t adesc = smem_desc_sw64(a_addr + pj * C::kABytes + kk * 32);
+                                mma_fp4(d0 + pj * BN, adesc, bdesc, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
+                            }
+                        }
+                    } else {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t idesc = idesc_bs_m128(n_mma, kk);
@@ -809,6 +971,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                                 mma_bs(d, adesc, blo, idesc, sfc + pj * 4, sfb + 4, 1);
                             }
                         }
+                    }
                     }
                     mma_commit(&load_empty[stage]);
                     if (++stage == C::kStages) {
@@ -870,7 +1033,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 tc_fence_after();
                 const uint32_t quarter = warp & 3;
                 uint8_t* h_atom = p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * C::kSFB;
-                gu_tile_part<BN, kGuW>(p, tc, tmem + lane_addr, BN / 2, tc.mt * 128 + quarter * 32 + lane, lane,
+                gu_tile_part<BN, kGuW, FP4>(p, tc, tmem + lane_addr, BN / 2, tc.mt * 128 + quarter * 32 + lane, lane,
                                        quarter, h_atom, &acc_empty[0]);
                 eaccphase ^= 1;
             }
@@ -899,7 +1062,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
             constexpr uint32_t kLoOff = C::kStackN ? BN : 0;        // stacked: lo half follows hi
             constexpr uint32_t kProjOff = C::kStackN ? 2 * BN : BN;
             if constexpr (MODE == kGateUp) {
-                gu_tile_part<BN, kGuW>(p, tc, dbase, 0, m, lane, quarter, h_atom, &acc_empty[acc]);
+                gu_tile_part<BN, kGuW, FP4>(p, tc, dbase, 0, m, lane, quarter, h_atom, &acc_empty[acc]);
                 if (++acc == C::kAccs) {
                     acc = 0;
                     accphase ^= 1;
@@ -979,32 +1142,39 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
     if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-template <int MODE, int BN>
+template <int MODE, int BN, bool FP4>
 static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p, int num_sms,
                                   cudaStream_t st, bool pdl) {
-    using C = BsCfg<MODE, BN>;
+    using C = BsCfg<MODE, BN, FP4>;
     static uint64_t attr_set = 0;  // one bit per device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 64 && !((attr_set >> dev) & 1u)) {
-        e = cudaFuncSetAttribute(gemm_bs_kernel<MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        e = cudaFuncSetAttribute(gemm_bs_kernel<MODE, BN, FP4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::kSmem);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
     }
-    return launch_kernel(gemm_bs_kernel<MODE, BN>, dim3(num_sms), dim3(320), C::kSmem, st, pdl, ta, tb, p);
+    return launch_kernel(gemm_bs_kernel<MODE, BN, FP4>, dim3(num_sms), dim3(320), C::kSmem, st, pdl, ta, tb, p);
+}
+
+template <int MODE, bool FP4>
+static cudaError_t launch_bs_width(int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
+                                   int num_sms, cudaStream_t st, bool pdl) {
+    if (block_n == 32) return launch_bs_mode<MODE, 32, FP4>(ta, tb, p, num_sms, st, pdl);
+    if (block_n == 64) return launch_bs_mode<MODE, 64, FP4>(ta, tb, p, num_sms, st, pdl);
+    return launch_bs_mode<MODE, 128, FP4>(ta, tb, p, num_sms, st, pdl);
 }
 
 cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
-                           int num_sms, cudaStream_t st, bool pdl) {
+                           int num_sms, cudaStream_t st, bool pdl, bool fp4) {
     if (mode == kGateUp) {
-        if (block_n == 32) return launch_bs_mode<kGateUp, 32>(ta, tb, p, num_sms, st, pdl);
-        if (block_n == 64) return launch_bs_mode<kGateUp, 64>(ta, tb, p, num_sms, st, pdl);
-        return launch_bs_mode<kGateUp, 128>(ta, tb, p, num_sms, st, pdl);
+        return fp4 ? launch_bs_width<kGateUp, true>(block_n, ta, tb, p, num_sms, st, pdl)
+                   : launch_bs_width<kGateUp, false>(block_n, ta, tb, p, num_sms, st, pdl);
     }
-    if (block_n == 32) return launch_bs_mode<kDown, 32>(ta, tb, p, num_sms, st, pdl);
-    if (block_n == 64) return launch_bs_mode<kDown, 64>(ta, tb, p, num_sms, st, pdl);
-    return launch_bs_mode<kDown, 128>(ta, tb, p, num_sms, st, pdl);
+    return fp4 ? launch_bs_width<kDown, true>(block_n, ta, tb, p, num_sms, st, pdl)
+               : launch_bs_width<kDown, false>(block_n, ta, tb, p, num_sms, st, pdl);
 }
 
 }  // namespace moe_b200

@@ -176,8 +176,18 @@ cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, co
                                uint32_t groups, uint32_t m_tiles, uint32_t block_n, uint32_t max_tiles,
                                TileEntry* tiles, cudaStream_t st);
 // `tb` is a 3-D map over [2][rows][K] E4M3 bytes with a {128, block_n, 2} box.
+// fp4 (fast mode, kind::mxf4): `ta` is a byte map over the weight codes with
+// a {64, 128} box and `tb` a byte map over [rows][K/2] packed E2M1 codes with
+// a {64, block_n} box, both 64-byte swizzled; h_out is then [rows][I/2]
+// packed codes and the scale blocks are 512 bytes for every tile width.
 cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
-                           int num_sms, cudaStream_t st, bool pdl);
+                           int num_sms, cudaStream_t st, bool pdl, bool fp4 = false);
+// Fast mode: token rows of x as packed E2M1 codes [rows][Kp/2] with E8M0
+// scale words in 512-byte blocks per (token tile, 128-K stage), stored at
+// each of the token's permuted rows (as launch_scatter_quant_bs).
+cudaError_t launch_scatter_quant_fp4(const uint16_t* x, uint32_t H, uint32_t Kp, uint32_t T, uint32_t K,
+                                     const uint32_t* pos_of, const uint32_t* shared_off, const uint32_t* row_info,
+                                     uint32_t rows, uint8_t* xq, uint8_t* sf_atoms, cudaStream_t st, bool pdl);
 
 // CUDA-core grouped GEMMs used only to cross-check the tcgen05 kernels.
 cudaError_t launch_gemm_simt(int mode, const uint16_t* b, uint32_t b_stride, uint32_t rows, const GemmParams& p,

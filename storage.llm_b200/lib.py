@@ -20,7 +20,7 @@ ERR_LEN = 160
 EP_UID_BYTES = 128
 
 SCORE_SOFTMAX, SCORE_SIGMOID = 0, 1
-GEMM_BLOCKSCALED, GEMM_SIMT, GEMM_TMEM_DECODE = 0, 1, 2
+GEMM_BLOCKSCALED, GEMM_SIMT, GEMM_TMEM_DECODE, GEMM_MXF4_FAST = 0, 1, 2, 3
 GEMM_TCGEN05 = GEMM_BLOCKSCALED
 PROJ_GATE, PROJ_UP, PROJ_DOWN = 0, 1, 2
 BUF_LOGITS, BUF_SCORES, BUF_GROUP_COUNT, BUF_GROUP_OFFSET, BUF_ROW_TOKEN, BUF_XPERM, BUF_HPERM, BUF_YPERM = range(8)

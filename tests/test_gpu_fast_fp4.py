@@ -1,0 +1,121 @@
+"""The opt-in fast mode (gemm_path MOE_B200_GEMM_MXF4_FAST) through the C ABI.
+
+The fast mode quantises the token rows and the SwiGLU intermediate to E2M1
+codes with one E8M0 scale per 32 elements (the smallest power of two that
+keeps each block's maximum at or below 6, codes rounded to nearest even) and
+runs both grouped GEMMs as tcgen05 kind::mxf4.  It is not held to the layer
+tolerance; the tests check
+  * that routing is the exact path's: ids, weights and the permutation are
+    bit-identical to the default path's;
+  * the kernels against an emulation of the same arithmetic in numpy
+    (float64 products of the decoded E2M1 values): the quantisation, the
+    scale placement and the MMA operand layouts all show up here;
+  * the measured error against the oracle (the reference's fp32 layer),
+    within FAST_MAX_REL_ABS / FAST_MEAN_REL, and print it.
+"""
+import numpy as np
+import pytest
+
+from test_gpu_layer import bf16_to_f32, decode_gguf, engine, L  # noqa: F401
+
+pytestmark = pytest.mark.gpu
+
+E2M1 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+# the fast mode's documented error against the reference (measured on B200):
+# max |dy| / max |y_ref| and mean |dy| / mean |y_ref|
+FAST_MAX_REL_ABS = 0.25
+FAST_MEAN_REL = 0.15
+
+
+def e2m1_round(y):
+    """Round-to-nearest-even onto the E2M1 values (ties to the even code)."""
+    a = np.minimum(np.abs(y), 6.0)
+    idx = np.searchsorted(E2M1, a)  # E2M1[idx-1] < a <= E2M1[idx]
+    idx = np.clip(idx, 1, 7)
+    lo, hi = E2M1[idx - 1], E2M1[idx]
+    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & (idx % 2 == 0))
+    return np.sign(y) * np.where(pick_hi, hi, lo)
+
+
+def fp4_quant(v):
+    """Per 32-element block along the last axis: the fast mode's scale and codes."""
+    sh = v.shape
+    b = v.reshape(sh[:-1] + (sh[-1] // 32, 32)).astype(np.float64)
+    amax = np.abs(b).max(axis=-1, keepdims=True)
+    _, ex = np.frexp(amax)
+    e = np.maximum(ex - 1 - 2, -127)
+    e = np.where(amax > 6.0 * np.ldexp(1.0, e), e + 1, e)
+    e = np.where(amax > 0, np.minimum(e, 127), -127)
+    q = e2m1_round(b * np.ldexp(1.0, -e)) * np.ldexp(1.0, e)
+    return q.reshape(sh)
+
+
+def pad32(v):
+    n = v.shape[-1]
+    m = (n + 31) // 32 * 32
+    return np.pad(v, [(0, 0)] * (v.ndim - 1) + [(0, m - n)]) if m != n else v
+
+
+def emulate(li, ids, w):
+    """The fast mode's layer in float64 from the same routing."""
+    s = li.shape
+    H, I = s.hidden, s.intermediate
+    xf = pad32(bf16_to_f32(li.x).astype(np.float64))
+    xq = fp4_quant(xf)[:, :H]
+    dec = lambda a, r, c: decode_gguf(a, r, c).astype(np.float64)
+
+    def triplet(g, u, d, x):
+        gg, uu = dec(g, I, H) @ x, dec(u, I, H) @ x
+        h = gg / (1.0 + np.exp(-gg)) * uu
+        hq = fp4_quant(pad32(h[None, :]))[0, :I]
+        return dec(d, H, I) @ hq
+
+    y = np.zeros((li.x.shape[0], H))
+    for t in range(li.x.shape[0]):
+        if li.shared_gate is not None:
+            y[t] += triplet(li.shared_gate, li.shared_up, li.shared_down, xq[t])
+        for j, e in enumerate(ids[t]):
+            y[t] += w[t, j] * triplet(li.gate[e], li.up[e], li.down[e], xq[t])
+    return y
+
+
+@pytest.mark.parametrize("tokens,top_k,experts,shared", [(64, 2, 8, False), (300, 3, 8, True), (24, 4, 16, False)],
+                         ids=["t64_k2", "t300_k3_shared", "t24_k4"])
+def test_fast_mode_matches_its_emulation(engine, synth, L, tokens, top_k, experts, shared):
+    shape = synth.small_shape(name="fast", hidden=256, intermediate=320, experts=experts, top_k=top_k,
+                              tokens=tokens, shared=shared)
+    li = synth.make_layer(shape, seed=41)
+    rng = np.random.default_rng(41)
+    li.gate = synth.jitter_scales(li.gate, rng, 4, 2)
+    li.down = synth.jitter_scales(li.down, rng, 4, 2)
+    engine.upload_layer(li)
+    exact = engine.forward_host(L.Engine.cfg(shape), li.x)
+    fast = engine.forward_host(L.Engine.cfg(shape, gemm_path=L.GEMM_MXF4_FAST), li.x)
+    for k in ("ids", "w", "perm"):
+        assert np.array_equal(np.asarray(fast[k]).view(np.uint8), np.asarray(exact[k]).view(np.uint8)), k
+    y_emu = emulate(li, fast["ids"], fast["w"])
+    d = np.abs(fast["y_f32"].astype(np.float64) - y_emu)
+    scale = np.abs(y_emu).max()
+    # same quantised products; fp32 accumulation and the fast SiLU can flip
+    # an occasional rounding of the intermediate by one E2M1 step
+    assert d.max() <= 2e-2 * scale, (d.max(), scale)
+    assert d.mean() <= 1e-3 * np.abs(y_emu).mean(), (d.mean(), np.abs(y_emu).mean())
+    engine.sync()
+
+
+@pytest.mark.parametrize("config,tokens", [(1, 256), (3, 512), (4, 256)], ids=["c1_t256", "c3_t512", "c4_t256"])
+def test_fast_mode_error_against_oracle(engine, synth, L, port, config, tokens):
+    shape = synth.CONFIGS[config]
+    li = synth.make_layer(shape, seed=0, tokens=tokens)
+    engine.upload_layer(li)
+    fast = engine.forward_host(L.Engine.cfg(shape, gemm_path=L.GEMM_MXF4_FAST), li.x)
+    sample = np.sort(np.random.default_rng(7).choice(tokens, size=16, replace=False))
+    y_ref, ids_ref, w_ref, _ = port.moe_layer(li, x=li.x[sample])
+    assert np.array_equal(fast["ids"][sample], ids_ref)
+    d = np.abs(fast["y_f32"][sample].astype(np.float64) - y_ref)
+    rel_max = d.max() / np.abs(y_ref).max()
+    mean_rel = d.mean() / np.abs(y_ref).mean()
+    print(f"fast mode config {config}: max |dy| / max |y| = {rel_max:.3e}, max abs {d.max():.3e}, "
+          f"mean rel {mean_rel:.3e}")
+    assert rel_max <= FAST_MAX_REL_ABS and mean_rel <= FAST_MEAN_REL, (rel_max, mean_rel)
+    engine.sync()
