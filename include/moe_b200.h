@@ -62,13 +62,13 @@ enum {
 
 /* Explicit form of the routing metadata the reference reads from GGUF JSON
  * keys (num_experts_per_tok, scoring_func, norm_topk_prob,
- * routed_scaling_factor: generation_router.cpp.inc:361-482).
- * The layer is SiLU-gated with no tensors around the experts besides the
- * optional shared expert.  GELU activations, post-FFW norms, the MoE
- * pre-norm, expert down scales, a shared-expert gate and a router input
- * scale (generation_mlp.cpp.inc:94-104, 234-250, 380-570;
- * generation_router.cpp.inc:316-359) have no fields here: layers that have
- * them are not run by this library. */
+ * routed_scaling_factor: generation_router.cpp.inc:361-482), and of the
+ * block style it reads from the model's metadata (hidden_activation, and
+ * the Gemma unit offset of its RMSNorms: raw_forward_utils.cpp.inc:322-350).
+ * The tensors of a Gemma-style block around the experts (norms, down
+ * scales, shared-expert gate, router input scale) are uploaded per layer
+ * with moe_b200_upload_block.  A zero-initialised config is the plain
+ * SiLU-gated layer. */
 typedef struct {
     uint32_t hidden;       /* H, multiple of 8 */
     uint32_t intermediate; /* I */
@@ -88,7 +88,47 @@ typedef struct {
      * library); n_group <= 256. */
     uint32_t n_group;
     uint32_t topk_group;
+    /* Gated activation of the gate projection (moe_generation_gated_activation_cached,
+     * generation_mlp.cpp.inc:94-104): MOE_B200_ACT_*.  Block-scaled paths only. */
+    int32_t activation;
+    /* RMSNorms of the layer's block parts multiply by (1 + w) (Gemma models) */
+    int32_t norm_unit_offset;
+    float norm_eps;        /* RMSNorm epsilon of the block parts; <= 0 -> 1e-6 */
 } moe_b200_layer_cfg_t;
+
+enum {
+    MOE_B200_ACT_SILU = 0,      /* generation_silu.cpp.inc:20-26 */
+    MOE_B200_ACT_GELU_ERF = 1,  /* generation_silu.cpp.inc:28-30 */
+    MOE_B200_ACT_GELU_TANH = 2  /* generation_mlp.cpp.inc:94-97 */
+};
+
+/* Optional tensors of a Gemma-style MoE block around the experts, in the
+ * order the reference applies them per token (moe_layer_moe_mlp_f32,
+ * generation_mlp.cpp.inc:776-1442).  NULL = the part is absent.  fp32 [H]
+ * vectors unless stated:
+ *   pre_norm2        the routed experts and the router read
+ *                    RMSNorm(hidden) * pre_norm2 (:234-250, :820-831);
+ *   post_norm1       RMSNorm of the shared expert's output (:853-856);
+ *   post_norm2       RMSNorm of each routed expert's output (:414-429);
+ *   post_norm        RMSNorm of the block output (:572-594);
+ *   down_scale       scales of the routed outputs: 1 value (all experts), E
+ *                    (per expert) or E*H (per element); other counts leave
+ *                    them unscaled, as the reference does (:514-570);
+ *   shared_gate_inp  bf16 [H] row: the shared expert is scaled by
+ *                    sigmoid(row . x) (:478-512);
+ *   router_scale     1 or H values: the router reads hidden * rms(hidden)^-1
+ *                    * scale / sqrt(H) (generation_router.cpp.inc:316-359). */
+typedef struct {
+    const float* pre_norm2;
+    const float* post_norm1;
+    const float* post_norm2;
+    const float* post_norm;
+    const float* down_scale;
+    uint64_t down_scale_count;
+    const uint16_t* shared_gate_inp;
+    const float* router_scale;
+    uint64_t router_scale_count;
+} moe_b200_block_tensors_t;
 
 /* Same layout as moe_token_expert_assignment_t / moe_expert_batch_t
  * (include/parts/moe_tensor_types.h.inc:62-74). */
@@ -135,6 +175,15 @@ MOE_B200_API int moe_b200_upload_expert(moe_b200_engine_t* engine, int32_t layer
                            uint64_t down_bytes, uint32_t hidden, uint32_t intermediate, int32_t src_on_device,
                            char* err);
 
+/* The block tensors of a layer (copied into the engine; NULL clears them).
+ * The router of the layer must be uploaded first.  The layer's forward then
+ * applies them (moe_b200_block_forward when pre_norm2 or router_scale is
+ * set, since those read the residual stream).  Block parts need H <= 25600
+ * and run on the single-device, block-scaled forward (gemm_path 0 or 3).
+ * Replaces the CPU application of those tensors in moe_layer_moe_mlp_f32. */
+MOE_B200_API int moe_b200_upload_block(moe_b200_engine_t* engine, int32_t layer, const moe_b200_block_tensors_t* t,
+                                       int32_t src_on_device, char* err);
+
 /* The MoE FFN for `tokens` tokens, all pointers device memory, enqueued on
  * `stream` (a cudaStream_t; NULL = legacy default stream).  Replaces the
  * per-token moe_layer_moe_mlp_f32 expert phase (generation_mlp.cpp.inc:
@@ -158,6 +207,24 @@ MOE_B200_API int moe_b200_layer_forward(moe_b200_engine_t* engine, const moe_b20
 MOE_B200_API int moe_b200_layer_forward_host(moe_b200_engine_t* engine, const moe_b200_layer_cfg_t* cfg,
                                 const uint16_t* x_bf16, uint32_t tokens, uint16_t* y_bf16, float* y_f32,
                                 int32_t* topk_ids, float* topk_w, uint32_t* perm, char* err);
+
+/* The layer with its block parts (moe_b200_upload_block), device pointers:
+ * x_bf16 is the expert input (the shared expert's, and the routed experts'
+ * and the router's without pre_norm2), hidden_f32 [tokens x H] the residual
+ * stream the pre-norm and the router input scale read (may be NULL when the
+ * layer has neither).  y = what the block adds to hidden.  The routing is
+ * bit-exact with the reference also when the router reads RMSNorm(hidden) or
+ * the scaled residual stream; the pre-normed routed input is rounded to
+ * bf16 before the experts (tolerance parity). */
+MOE_B200_API int moe_b200_block_forward(moe_b200_engine_t* engine, const moe_b200_layer_cfg_t* cfg,
+                                        const uint16_t* x_bf16, const float* hidden_f32, uint32_t tokens,
+                                        uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w,
+                                        void* stream, char* err);
+/* Host-buffer variant (copies in, runs, copies out, synchronises). */
+MOE_B200_API int moe_b200_block_forward_host(moe_b200_engine_t* engine, const moe_b200_layer_cfg_t* cfg,
+                                             const uint16_t* x_bf16, const float* hidden_f32, uint32_t tokens,
+                                             uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w,
+                                             char* err);
 
 /* Waits for the engine's work and reports any error a kernel recorded
  * (bounded waits that timed out, out-of-range expert ids). */

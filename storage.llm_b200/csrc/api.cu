@@ -295,7 +295,30 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     // permuted source rows as exact hi/lo E4M3 terms + their scale blocks
     const uint64_t xb_rows = eng->xb.bytes / (2ull * Kq), hb_rows = eng->hb.bytes / (2ull * Iq);
     const bool per_token = job.K <= 32 && (job.shared_rows == 0 || (job.shared_base == 0 && job.shared_rows == job.T));
-    if (job.fp4) {
+    if (job.src_shared && !per_token) {
+        set_err(err, "separate shared-expert rows need the single-device layer");
+        return 0;
+    }
+    if (job.src_shared) {
+        // the routed rows from src, then the shared rows from src_shared
+        const uint32_t* soff = job.shared_rows ? gi.offset + job.E : nullptr;
+        if (job.fp4) {
+            CK(launch_scatter_quant_fp4(job.src, H, Kq, job.T, job.K, eng->pos_of.as<uint32_t>(), nullptr,
+                                        eng->row_info.as<uint32_t>(), P, eng->xb.as<uint8_t>(),
+                                        eng->sfx_atoms.as<uint8_t>(), st, true));
+            CK(launch_scatter_quant_fp4(job.src_shared, H, Kq, job.T, 0, eng->pos_of.as<uint32_t>(), soff,
+                                        eng->row_info.as<uint32_t>(), P, eng->xb.as<uint8_t>(),
+                                        eng->sfx_atoms.as<uint8_t>(), st, true));
+        } else {
+            CK(launch_scatter_quant_bs(job.src, H, Kq, job.T, job.K, eng->pos_of.as<uint32_t>(), nullptr,
+                                       eng->row_info.as<uint32_t>(), P, (uint32_t)xb_rows, block_n,
+                                       eng->xb.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(), st, true));
+            CK(launch_scatter_quant_bs(job.src_shared, H, Kq, job.T, 0, eng->pos_of.as<uint32_t>(), soff,
+                                       eng->row_info.as<uint32_t>(), P, (uint32_t)xb_rows, block_n,
+                                       eng->xb.as<uint8_t>(), eng->sfx_atoms.as<uint8_t>(), st, true));
+        }
+        *launches += 1;
+    } else if (job.fp4) {
         if (!per_token) {
             set_err(err, "the fast mode runs the single-device layer only");
             return 0;
@@ -321,6 +344,7 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     bp.count = gi.count;
     bp.offset = gi.offset;
     bp.err = errw;
+    bp.act = job.act;
     bp.group_slot = job.group_slot;
     // gate/up: K = H (padded Kq), M = I rows (padded rp_i), output h hi/lo
     bp.tile_off = gi.gu_tile_off;
@@ -561,9 +585,15 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
     return 1;
 }
 
-int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const uint16_t* x,
-                           uint32_t T, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w,
-                           uint32_t* perm, void* stream, char* err) {
+}  // extern "C"
+
+namespace {
+
+// The single-device layer (moe_b200_layer_forward and moe_b200_block_forward):
+// `hidden` is the residual stream the block parts may read (may be null).
+int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const uint16_t* x, const float* hidden,
+                 uint32_t T, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w, uint32_t* perm,
+                 void* stream, char* err) {
     if (!check_dims(cfg, err)) return 0;
     LayerWeights* L = get_layer(eng, cfg->layer, err);
     if (!L) return 0;
@@ -584,9 +614,29 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         set_err(err, "layer %d has no shared expert uploaded", cfg->layer);
         return 0;
     }
+    const bool fp4 = cfg->gemm_path == MOE_B200_GEMM_MXF4_FAST;
+    const bool bs = cfg->gemm_path == MOE_B200_GEMM_BLOCKSCALED || fp4;
+    const bool block = L->has_block() || cfg->activation != MOE_B200_ACT_SILU;
+    if (cfg->activation < MOE_B200_ACT_SILU || cfg->activation > MOE_B200_ACT_GELU_TANH) {
+        set_err(err, "unknown activation %d", cfg->activation);
+        return 0;
+    }
+    if (block && !bs) {
+        set_err(err, "block parts and GELU activations run on the block-scaled GEMM paths (gemm_path 0 or 3)");
+        return 0;
+    }
+    if (L->has_block() && H > 25600) {
+        set_err(err, "block parts support H <= 25600 (H=%u)", H);
+        return 0;
+    }
     if (T == 0) return 1;
     if (!x) {
         set_err(err, "null input");
+        return 0;
+    }
+    if (L->needs_hidden() && !hidden) {
+        set_err(err, "layer %d has a pre-norm or router input scale: give the residual stream "
+                     "(moe_b200_block_forward)", cfg->layer);
         return 0;
     }
     if ((uint64_t)T * K > 0x7fffffffull) {
@@ -616,8 +666,6 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     CK(eng->g_offset.reserve((size_t)(G + 1) * 4));
     CK(eng->g_gu_off.reserve((size_t)(G + 1) * 4));
     CK(eng->g_dn_off.reserve((size_t)(G + 1) * 4));
-    const bool fp4 = cfg->gemm_path == MOE_B200_GEMM_MXF4_FAST;
-    const bool bs = cfg->gemm_path == MOE_B200_GEMM_BLOCKSCALED || fp4;
     CK(eng->yperm.reserve((size_t)P * H * 4));
     if (!bs) {
         // the cross-check GEMMs read the tile form
@@ -659,12 +707,50 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
 
     const int sigmoid = cfg->score_func == MOE_B200_SCORE_SIGMOID;
     const float rscale = cfg->routed_scale > 0.f ? cfg->routed_scale : 1.0f;
-    CUtensorMap rtx, rtw;
-    const bool rt_tma = router_tmaps(eng, x, L->router.as<uint16_t>(), T, E, H, &rtx, &rtw);
-    CK(launch_router(x, L->router.as<uint16_t>(), T, E, H, K,
-                     RouteCfg{sigmoid, cfg->norm_topk, rscale, cfg->n_group, cfg->topk_group},
-                     eng->logits.as<float>(), ids, w, eng->scores.as<float>(), errw, st, &launches,
-                     rt_tma ? &rtx : nullptr, rt_tma ? &rtw : nullptr));
+    const RouteCfg rcfg{sigmoid, cfg->norm_topk, rscale, cfg->n_group, cfg->topk_group};
+    // block parts: the routed input RMSNorm(hidden) * pre_norm2, exactly as
+    // the reference computes it (fp32 for the router, bf16 for the experts)
+    const uint16_t* x_routed = x;
+    if (L->blk_pre_norm2.ptr) {
+        CK(eng->xr_f32.reserve((size_t)T * H * 4));
+        CK(eng->xr_bf16.reserve((size_t)T * H * 2));
+        CK(launch_row_norm_exact(hidden, T, H, L->blk_pre_norm2.as<float>(), H, 0, cfg->norm_eps,
+                                 cfg->norm_unit_offset, eng->xr_f32.as<float>(), eng->xr_bf16.as<uint16_t>(), st));
+        x_routed = eng->xr_bf16.as<uint16_t>();
+        launches += 1;
+    }
+    if (L->blk_router_scale.ptr || L->blk_pre_norm2.ptr) {
+        // the router reads an fp32 row: the scaled residual stream, or the
+        // pre-normed routed input
+        const float* rin = eng->xr_f32.as<float>();
+        if (L->blk_router_scale.ptr) {
+            CK(eng->rin_f32.reserve((size_t)T * H * 4));
+            CK(launch_row_norm_exact(hidden, T, H, L->blk_router_scale.as<float>(), L->blk_router_scale_count, 1, 0.f,
+                                     0, eng->rin_f32.as<float>(), nullptr, st));
+            rin = eng->rin_f32.as<float>();
+            launches += 1;
+        }
+        CK(launch_router_f32(rin, L->router.as<uint16_t>(), T, E, H, K, rcfg, eng->logits.as<float>(), ids, w,
+                             eng->scores.as<float>(), st, &launches));
+    } else {
+        CUtensorMap rtx, rtw;
+        const bool rt_tma = router_tmaps(eng, x, L->router.as<uint16_t>(), T, E, H, &rtx, &rtw);
+        CK(launch_router(x, L->router.as<uint16_t>(), T, E, H, K, rcfg, eng->logits.as<float>(), ids, w,
+                         eng->scores.as<float>(), errw, st, &launches, rt_tma ? &rtx : nullptr,
+                         rt_tma ? &rtw : nullptr));
+    }
+    // the shared-expert gate sigmoid(gate_inp . x): the router's exact dot and
+    // sigmoid with one expert
+    const bool gated = shared && L->blk_gate_inp.ptr;
+    if (gated) {
+        CK(eng->gate_logits.reserve((size_t)T * 4));
+        CK(eng->gate_ids.reserve((size_t)T * 4));
+        CK(eng->gate_w.reserve((size_t)T * 4));
+        CK(eng->gate_scores.reserve((size_t)T * 4));
+        CK(launch_router(x, L->blk_gate_inp.as<uint16_t>(), T, 1, H, 1, RouteCfg{1, 0, 1.0f, 0, 0},
+                         eng->gate_logits.as<float>(), eng->gate_ids.as<int32_t>(), eng->gate_w.as<float>(),
+                         eng->gate_scores.as<float>(), errw, st, &launches, nullptr, nullptr));
+    }
     mark(1);
 
     if (bs) {
@@ -675,7 +761,9 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
         job.E = E;
         job.shared_rows = shared_rows;
         job.shared_base = 0;
-        job.src = x;
+        job.src = x_routed;
+        job.src_shared = (x_routed != x && shared_rows) ? x : nullptr;
+        job.act = cfg->activation;
         job.group_slot = nullptr;
         job.y = eng->yperm.as<float>();
         job.y_by_source = false;
@@ -736,8 +824,16 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     mark(5);
     }
 
-    CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), w, T, K,
-                      shared ? eng->yperm.as<float>() + (size_t)n * H : nullptr, y_bf16, y_f32, st, bs));
+    if (L->has_block_combine()) {
+        BlockParts parts{L->blk_post_norm1.as<float>(), L->blk_post_norm2.as<float>(), L->blk_post_norm.as<float>(),
+                         L->blk_down_scale.as<float>(), L->blk_down_scale_count, cfg->norm_eps, cfg->norm_unit_offset};
+        CK(launch_block_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), ids, w, T, K, E,
+                                shared ? eng->yperm.as<float>() + (size_t)n * H : nullptr,
+                                gated ? eng->gate_w.as<float>() : nullptr, parts, y_bf16, y_f32, st, bs));
+    } else {
+        CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), w, T, K,
+                          shared ? eng->yperm.as<float>() + (size_t)n * H : nullptr, y_bf16, y_f32, st, bs));
+    }
     launches += 1;
     mark(6);
     if (perm) {
@@ -751,6 +847,97 @@ int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* c
     eng->last_Ip = Ip;
     eng->last_H = H;
     eng->last_launches = launches;
+    return 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_b200_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const uint16_t* x,
+                           uint32_t T, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w,
+                           uint32_t* perm, void* stream, char* err) {
+    return forward_impl(eng, cfg, x, nullptr, T, y_bf16, y_f32, topk_ids, topk_w, perm, stream, err);
+}
+
+int moe_b200_block_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const uint16_t* x,
+                           const float* hidden, uint32_t T, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids,
+                           float* topk_w, void* stream, char* err) {
+    return forward_impl(eng, cfg, x, hidden, T, y_bf16, y_f32, topk_ids, topk_w, nullptr, stream, err);
+}
+
+int moe_b200_block_forward_host(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const uint16_t* x,
+                                const float* hidden, uint32_t T, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids,
+                                float* topk_w, char* err) {
+    if (!check_dims(cfg, err)) return 0;
+    if (!eng) {
+        set_err(err, "null engine");
+        return 0;
+    }
+    if (T == 0) return 1;
+    if (!x) {
+        set_err(err, "null input");
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    const uint32_t H = cfg->hidden, K = cfg->top_k;
+    CK(eng->hx.reserve((size_t)T * H * 2));
+    CK(eng->hy.reserve((size_t)T * H * 2));
+    CK(eng->hyf.reserve((size_t)T * H * 4));
+    CK(eng->hids.reserve((size_t)T * K * 4));
+    CK(eng->hw.reserve((size_t)T * K * 4));
+    if (hidden) CK(eng->hhid.reserve((size_t)T * H * 4));
+    cudaStream_t st = eng->hstream;
+    CK(cudaMemcpyAsync(eng->hx.ptr, x, (size_t)T * H * 2, cudaMemcpyHostToDevice, st));
+    if (hidden) CK(cudaMemcpyAsync(eng->hhid.ptr, hidden, (size_t)T * H * 4, cudaMemcpyHostToDevice, st));
+    if (!forward_impl(eng, cfg, eng->hx.as<uint16_t>(), hidden ? eng->hhid.as<float>() : nullptr, T,
+                      y_bf16 ? eng->hy.as<uint16_t>() : nullptr, y_f32 ? eng->hyf.as<float>() : nullptr,
+                      eng->hids.as<int32_t>(), eng->hw.as<float>(), nullptr, st, err)) {
+        return 0;
+    }
+    if (y_bf16) CK(cudaMemcpyAsync(y_bf16, eng->hy.ptr, (size_t)T * H * 2, cudaMemcpyDeviceToHost, st));
+    if (y_f32) CK(cudaMemcpyAsync(y_f32, eng->hyf.ptr, (size_t)T * H * 4, cudaMemcpyDeviceToHost, st));
+    if (topk_ids) CK(cudaMemcpyAsync(topk_ids, eng->hids.ptr, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st));
+    if (topk_w) CK(cudaMemcpyAsync(topk_w, eng->hw.ptr, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st));
+    return moe_b200_sync(eng, st, err);
+}
+
+int moe_b200_upload_block(moe_b200_engine_t* eng, int32_t layer, const moe_b200_block_tensors_t* t,
+                          int32_t src_on_device, char* err) {
+    LayerWeights* L = get_layer(eng, layer, err);
+    if (!L) return 0;
+    if (!L->E) {
+        set_err(err, "upload the router of layer %d before its block tensors", layer);
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    CK(cudaStreamSynchronize(eng->ustream));
+    L->release_block();
+    if (!t) return 1;
+    const uint64_t H = L->H, E = L->E;
+    if ((t->down_scale && t->down_scale_count == 0) || (t->router_scale && t->router_scale_count == 0)) {
+        set_err(err, "a block scale tensor with zero values");
+        return 0;
+    }
+    const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    auto put = [&](DevBuf& dst, const void* src, uint64_t bytes) -> int {
+        if (!src) return 1;
+        CK(dst.reserve(bytes));
+        CK(cudaMemcpyAsync(dst.ptr, src, bytes, kind, eng->ustream));
+        return 1;
+    };
+    (void)E;
+    if (!put(L->blk_pre_norm2, t->pre_norm2, H * 4) || !put(L->blk_post_norm1, t->post_norm1, H * 4) ||
+        !put(L->blk_post_norm2, t->post_norm2, H * 4) || !put(L->blk_post_norm, t->post_norm, H * 4) ||
+        !put(L->blk_down_scale, t->down_scale, t->down_scale_count * 4) ||
+        !put(L->blk_gate_inp, t->shared_gate_inp, H * 2) ||
+        !put(L->blk_router_scale, t->router_scale, t->router_scale_count * 4)) {
+        L->release_block();
+        return 0;
+    }
+    L->blk_down_scale_count = t->down_scale ? t->down_scale_count : 0;
+    L->blk_router_scale_count = t->router_scale ? t->router_scale_count : 0;
+    CK(cudaStreamSynchronize(eng->ustream));
     return 1;
 }
 

@@ -78,12 +78,28 @@ struct LayerWeights {
     DevBuf dn;              // [E+1] groups of down tiles
     uint64_t gu_stride = 0, dn_stride = 0;
     std::vector<uint8_t> tile_ready;  // [E+1]: slot's tile form is current
+    // Gemma-style block parts (moe_b200_upload_block); empty = absent
+    DevBuf blk_pre_norm2, blk_post_norm1, blk_post_norm2, blk_post_norm, blk_down_scale, blk_gate_inp,
+        blk_router_scale;
+    uint64_t blk_down_scale_count = 0, blk_router_scale_count = 0;
+    bool has_block_combine() const {
+        return blk_post_norm1.ptr || blk_post_norm2.ptr || blk_post_norm.ptr || blk_down_scale.ptr || blk_gate_inp.ptr;
+    }
+    bool needs_hidden() const { return blk_pre_norm2.ptr || blk_router_scale.ptr; }
+    bool has_block() const { return has_block_combine() || needs_hidden(); }
+    void release_block() {
+        DevBuf* b[] = {&blk_pre_norm2, &blk_post_norm1, &blk_post_norm2, &blk_post_norm, &blk_down_scale,
+                       &blk_gate_inp, &blk_router_scale};
+        for (DevBuf* x : b) x->release();
+        blk_down_scale_count = blk_router_scale_count = 0;
+    }
     uint32_t rp_i = 0, rp_h = 0, kq = 0, iq = 0;  // rows padded to 128, K padded to 128
     CUtensorMap tmap_gu_codes{}, tmap_dn_codes{};
     // the same codes as packed bytes (64-byte rows, 64-byte swizzle) for the
     // fast mode's kind::mxf4 GEMMs
     CUtensorMap tmap_gu_fp4{}, tmap_dn_fp4{};
     void release_all() {
+        release_block();
         router.release();
         gu.release();
         dn.release();
@@ -122,6 +138,9 @@ struct moe_b200_engine {
     // block-scaled path: quantised activations and intermediate
     // (xb, hb hold a hi plane followed by a lo plane)
     DevBuf xb, sfx_atoms, hb, sfh_atoms, gu_tiles, dn_tiles;
+    // block parts: pre-normed routed input (fp32 for the router, bf16 for the
+    // experts), the router's fp32 input, the shared-expert gate's routing
+    DevBuf xr_f32, xr_bf16, rin_f32, gate_logits, gate_ids, gate_w, gate_scores;
     // 3-D maps over xb / hb: [0] 32-token box, [1] 64-token box, [2] 128-token box
     CUtensorMap tmap_xb[3]{}, tmap_hb[3]{};
     const void* bs_map_key[2] = {nullptr, nullptr};
@@ -131,7 +150,7 @@ struct moe_b200_engine {
     const void* fp4_map_key[2] = {nullptr, nullptr};
     uint64_t fp4_map_dims[2][2] = {};
     // host-call staging
-    DevBuf hx, hy, hyf, hids, hw, hperm_out, tri;
+    DevBuf hx, hy, hyf, hids, hw, hperm_out, tri, hhid;
     // host-buffer entry points: their own non-blocking stream, and a pinned
     // word the error code is copied into before the one synchronisation
     cudaStream_t hstream = nullptr;
@@ -172,6 +191,8 @@ struct BsJob {
     uint32_t shared_rows;        // rows of the shared-expert group (0: none) ...
     uint32_t shared_base;        // ... reading source rows shared_base + t
     const uint16_t* src;         // source rows, bf16 [*, H], device
+    const uint16_t* src_shared = nullptr;  // the shared group's source rows when they differ from src
+    int32_t act = 0;             // gated activation (MOE_B200_ACT_*)
     const uint32_t* group_slot;  // weight slot of each group (device); null: routed group g -> slot g,
                                  // shared group -> slot E of the layer
     float* y;                    // expert outputs, fp32 rows [*, H]

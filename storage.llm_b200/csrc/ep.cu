@@ -623,6 +623,11 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
         set_err(err, "the expert-parallel forward runs the block-scaled GEMM path only");
         return 0;
     }
+    if (cfg->activation != MOE_B200_ACT_SILU ||
+        (cfg->layer >= 0 && (size_t)cfg->layer < eng->layers.size() && eng->layers[cfg->layer].has_block())) {
+        set_err(err, "block parts and GELU activations run on the single-device forward");
+        return 0;
+    }
     EpState* ep = eng->ep;
     LayerWeights* L = get_layer(eng, cfg->layer, err);
     if (!L) return 0;

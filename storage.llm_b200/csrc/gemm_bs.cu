@@ -628,6 +628,16 @@ cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, co
 
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
+// The gated activation of the gate projection (moe_generation_gated_activation_cached,
+// generation_mlp.cpp.inc:94-104): SiLU, GELU in its erf form, or GELU in its
+// tanh form with x + 0.044715 x^3 as one multiply-add (CUDA's erff / tanhf;
+// tolerance parity like the rest of the expert math).
+__device__ __forceinline__ float gated_act(int act, float g) {
+    if (act == 1) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752440f));
+    if (act == 2) return 0.5f * g * (1.0f + tanhf(0.7978845608028654f * fmaf(0.044715f * g * g, g, g)));
+    return silu_fast(g);
+}
+
 // Gate/up epilogue for 8 token columns of one row m: h = SiLU(gate) * up,
 // split into hi/lo E4M3 with the down GEMM's block scales, stored.  The 8 chains
 // are independent and the code is branch-free (columns at or past nn are
@@ -728,7 +738,7 @@ __device__ __forceinline__ void gu_store8(const float* g, const float* u, uint32
                                           uint8_t* h_atom) {
     float hv[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) hv[j] = silu_fast(g[j]) * u[j];
+    for (int j = 0; j < 8; ++j) hv[j] = gated_act(p.act, g[j]) * u[j];
     if constexpr (FP4) {
         h_store8_fp4<BN>(hv, c0, nn, row0, m, lane, quarter, p, h_atom);
     } else {

@@ -77,8 +77,31 @@ struct BsParams {
     const uint32_t* ret_base;
     uint32_t ret_rows;
     uint32_t ret_world;
+    int32_t act;              // gate/up: 0 SiLU, 1 GELU (erf form), 2 GELU (tanh form)
     uint32_t* err;
 };
+
+// Block parts the combine applies (block.cu); null pointers are absent parts.
+struct BlockParts {
+    const float* post_norm1;   // [H] RMSNorm weight of the shared expert's output
+    const float* post_norm2;   // [H] RMSNorm weight of each routed expert's output
+    const float* post_norm;    // [H] RMSNorm weight of the block output
+    const float* down_scale;   // 1, E or E*H scales of the routed outputs
+    uint64_t down_scale_count;
+    float eps;                 // RMSNorm epsilon (<= 0: 1e-6)
+    int unit_offset;           // RMSNorm by (1 + w)
+};
+// Exact-order row RMSNorm (block.cu): mode 0 the MoE pre-norm with weight w,
+// mode 1 the router input scale (w = the scale, w_count values).
+cudaError_t launch_row_norm_exact(const float* in, uint32_t rows, uint32_t H, const float* w, uint64_t w_count,
+                                  int mode, float eps, int unit_offset, float* out_f32, uint16_t* out_bf16,
+                                  cudaStream_t st);
+// y[t] = post_norm(post_norm1(ys[t]) * gate[t] + sum_j w[t,j] * down_scale(post_norm2(yp[pos_of[t*K+j]])));
+// ys, gate may be null.  H <= 25600.
+cudaError_t launch_block_combine(const float* yp, uint32_t H, const uint32_t* pos_of, const int32_t* ids,
+                                 const float* w, uint32_t T, uint32_t K, uint32_t E, const float* ys,
+                                 const float* gate, const BlockParts& bp, uint16_t* y_bf16, float* y_f32,
+                                 cudaStream_t st, bool pdl);
 
 cudaError_t launch_repack_mxfp4(const uint8_t* gguf, uint32_t rows, uint32_t cols, uint8_t* out,
                                 uint32_t tile_stride, cudaStream_t stream);
@@ -100,6 +123,11 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
                           const RouteCfg& rc, float* logits, int32_t* ids, float* wout, float* scores, uint32_t* err,
                           cudaStream_t st, uint32_t* launches, const CUtensorMap* tmap_x = nullptr,
                           const CUtensorMap* tmap_w = nullptr);
+// The same routing from fp32 token rows x [T x H] (the logits in the
+// reference's FMA order, then the same top-k).
+cudaError_t launch_router_f32(const float* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
+                              const RouteCfg& rc, float* logits, int32_t* ids, float* wout, float* scores,
+                              cudaStream_t st, uint32_t* launches);
 // Box of the router's tensor maps: 128 bf16 columns x box_rows rows, no
 // swizzle (router_box_rows(true) for x, (false) for w).
 uint32_t router_box_rows(bool tokens);

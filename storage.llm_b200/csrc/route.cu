@@ -1165,6 +1165,64 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Router logits from fp32 token rows (a Gemma-style block whose router reads
+// RMSNorm(hidden) or the scaled residual stream), in the reference's order:
+// a half-warp per (token, expert) dot, lane l running chain l over elements
+// l, l + 16, ... of the 16-aligned part, then b_c = s_c + s_{c+8} and
+// ((b0 + b1) + b2) + ... + b7, then the 4-way and scalar tails on lane 0 --
+// the same arithmetic as RtLane::finish, so bf16-valued rows give the bf16
+// kernels' logits bit for bit.  One block per token, its 16 half-warps take
+// the experts in turn.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) router_logits_f32in_kernel(const float* __restrict__ x,
+                                                                  const uint16_t* __restrict__ w, uint32_t T,
+                                                                  uint32_t E, uint32_t H, float* __restrict__ logits) {
+    const uint32_t t = blockIdx.x;
+    const uint32_t hw = threadIdx.x >> 4, l = threadIdx.x & 15;
+    const uint32_t main_end = H & ~15u;
+    const float* xr = x + (uint64_t)t * H;
+    const unsigned mask = 0xFFFFu << (threadIdx.x & 16);
+    for (uint32_t e = hw; e < E; e += 16) {
+        const uint16_t* wr = w + (uint64_t)e * H;
+        float s = 0.0f;
+        for (uint32_t i = l; i < main_end; i += 16) s = __fmaf_rn(__ldg(xr + i), bf16_bits_to_f32(__ldg(wr + i)), s);
+        const float b = __fadd_rn(s, __shfl_down_sync(mask, s, 8, 16));  // lanes 0..7: b_l
+        float sum = __shfl_sync(mask, b, 0, 16);
+        for (int c = 1; c < 8; ++c) sum = __fadd_rn(sum, __shfl_sync(mask, b, c, 16));
+        if (l == 0) {
+            float out = 0.0f + sum;
+            if (main_end < H) {
+                uint32_t i = main_end;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                for (; i + 3 < H; i += 4) {
+                    a0 = __fmaf_rn(bf16_bits_to_f32(wr[i]), xr[i], a0);
+                    a1 = __fmaf_rn(bf16_bits_to_f32(wr[i + 1]), xr[i + 1], a1);
+                    a2 = __fmaf_rn(bf16_bits_to_f32(wr[i + 2]), xr[i + 2], a2);
+                    a3 = __fmaf_rn(bf16_bits_to_f32(wr[i + 3]), xr[i + 3], a3);
+                }
+                out = __fadd_rn(out, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
+                for (; i < H; ++i) out = __fmaf_rn(bf16_bits_to_f32(wr[i]), xr[i], out);
+            }
+            logits[(uint64_t)t * E + e] = out;
+        }
+    }
+}
+
+cudaError_t launch_router_f32(const float* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
+                              const RouteCfg& rc_in, float* logits, int32_t* ids, float* wout, float* scores,
+                              cudaStream_t st, uint32_t* launches) {
+    if (T == 0) return cudaSuccess;
+    RouteCfg rc = rc_in;
+    if (!(rc.sigmoid && rc.n_group > 1 && rc.topk_group > 0 && rc.topk_group < rc.n_group && E % rc.n_group == 0))
+        rc.n_group = rc.topk_group = 0;
+    if (rc.n_group > 256) return cudaErrorInvalidValue;
+    router_logits_f32in_kernel<<<T, 256, 0, st>>>(x, w, T, E, H, logits);
+    router_topk_kernel<<<ceil_div(T, 8), 256, 0, st>>>(logits, T, E, K, rc, ids, wout, scores);
+    if (launches) *launches += 2;
+    return cudaGetLastError();
+}
+
 uint32_t sort_tiles(uint32_t n) { return ceil_div(n, kSortTile); }
 
 cudaError_t launch_sort_count(const int32_t* keys, uint32_t n, uint32_t nb, uint32_t* tile_counts, uint32_t* rank,

@@ -20,6 +20,7 @@ ERR_LEN = 160
 EP_UID_BYTES = 128
 
 SCORE_SOFTMAX, SCORE_SIGMOID = 0, 1
+ACT_SILU, ACT_GELU_ERF, ACT_GELU_TANH = 0, 1, 2
 GEMM_BLOCKSCALED, GEMM_SIMT, GEMM_TMEM_DECODE, GEMM_MXF4_FAST = 0, 1, 2, 3
 GEMM_TCGEN05 = GEMM_BLOCKSCALED
 PROJ_GATE, PROJ_UP, PROJ_DOWN = 0, 1, 2
@@ -34,7 +35,14 @@ class LayerCfg(C.Structure):
     _fields_ = [("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("experts", C.c_uint32),
                 ("top_k", C.c_uint32), ("layer", C.c_int32), ("score_func", C.c_int32),
                 ("norm_topk", C.c_int32), ("routed_scale", C.c_float), ("use_shared", C.c_int32),
-                ("gemm_path", C.c_int32), ("n_group", C.c_uint32), ("topk_group", C.c_uint32)]
+                ("gemm_path", C.c_int32), ("n_group", C.c_uint32), ("topk_group", C.c_uint32),
+                ("activation", C.c_int32), ("norm_unit_offset", C.c_int32), ("norm_eps", C.c_float)]
+
+
+class BlockTensors(C.Structure):
+    _fields_ = [("pre_norm2", C.c_void_p), ("post_norm1", C.c_void_p), ("post_norm2", C.c_void_p),
+                ("post_norm", C.c_void_p), ("down_scale", C.c_void_p), ("down_scale_count", C.c_uint64),
+                ("shared_gate_inp", C.c_void_p), ("router_scale", C.c_void_p), ("router_scale_count", C.c_uint64)]
 
 
 class Assignment(C.Structure):
@@ -75,6 +83,12 @@ def load(path: Path = LIB_PATH) -> C.CDLL:
     lib.moe_b200_layer_forward.argtypes = [vp, C.POINTER(LayerCfg), vp, C.c_uint32, vp, vp, vp, vp, vp, vp, cp]
     lib.moe_b200_layer_forward_host.restype = C.c_int
     lib.moe_b200_layer_forward_host.argtypes = [vp, C.POINTER(LayerCfg), vp, C.c_uint32, vp, vp, vp, vp, vp, cp]
+    lib.moe_b200_upload_block.restype = C.c_int
+    lib.moe_b200_upload_block.argtypes = [vp, C.c_int32, C.POINTER(BlockTensors), C.c_int32, cp]
+    lib.moe_b200_block_forward.restype = C.c_int
+    lib.moe_b200_block_forward.argtypes = [vp, C.POINTER(LayerCfg), vp, vp, C.c_uint32, vp, vp, vp, vp, vp, cp]
+    lib.moe_b200_block_forward_host.restype = C.c_int
+    lib.moe_b200_block_forward_host.argtypes = [vp, C.POINTER(LayerCfg), vp, vp, C.c_uint32, vp, vp, vp, vp, cp]
     lib.moe_b200_sync.restype = C.c_int
     lib.moe_b200_sync.argtypes = [vp, vp, cp]
     lib.moe_b200_run_expert_triplet_f32.restype = C.c_int
@@ -182,11 +196,47 @@ class Engine:
     @staticmethod
     def cfg(shape, layer: int = 0, gemm_path: int = GEMM_TCGEN05, score_func: int = SCORE_SOFTMAX,
             norm_topk: Optional[bool] = None, routed_scale: float = 1.0, use_shared: Optional[bool] = None,
-            n_group: int = 0, topk_group: int = 0):
+            n_group: int = 0, topk_group: int = 0, activation: int = ACT_SILU, norm_unit_offset: bool = False,
+            norm_eps: float = 0.0):
         nt = shape.norm_topk if norm_topk is None else norm_topk
         us = shape.shared if use_shared is None else use_shared
         return LayerCfg(shape.hidden, shape.intermediate, shape.experts, shape.top_k, layer, score_func, int(nt),
-                        routed_scale, int(us), gemm_path, n_group, topk_group)
+                        routed_scale, int(us), gemm_path, n_group, topk_group, activation, int(norm_unit_offset),
+                        norm_eps)
+
+    def upload_block(self, layer: int, pre_norm2=None, post_norm1=None, post_norm2=None, post_norm=None,
+                     down_scale=None, shared_gate_inp=None, router_scale=None):
+        """The block tensors of a layer from host numpy arrays (None = absent)."""
+        keep = {}
+
+        def arr(name, a, dtype):
+            if a is None:
+                return None
+            keep[name] = np.ascontiguousarray(a, dtype=dtype)
+            return keep[name].ctypes.data
+
+        t = BlockTensors(arr("pn2", pre_norm2, np.float32), arr("n1", post_norm1, np.float32),
+                         arr("n2", post_norm2, np.float32), arr("n", post_norm, np.float32),
+                         arr("ds", down_scale, np.float32), 0 if down_scale is None else int(np.size(down_scale)),
+                         arr("sg", shared_gate_inp, np.uint16), arr("rs", router_scale, np.float32),
+                         0 if router_scale is None else int(np.size(router_scale)))
+        self._check(self.lib.moe_b200_upload_block(self.h, layer, C.byref(t), 0, self.err))
+
+    def clear_block(self, layer: int):
+        self._check(self.lib.moe_b200_upload_block(self.h, layer, None, 0, self.err))
+
+    def block_forward_host(self, cfg: LayerCfg, x: np.ndarray, hidden: Optional[np.ndarray] = None):
+        T = x.shape[0]
+        H, K = cfg.hidden, cfg.top_k
+        y = np.zeros((T, H), np.uint16)
+        yf = np.zeros((T, H), np.float32)
+        ids = np.zeros((T, K), np.int32)
+        w = np.zeros((T, K), np.float32)
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        hid = None if hidden is None else np.ascontiguousarray(hidden, dtype=np.float32)
+        self._check(self.lib.moe_b200_block_forward_host(self.h, C.byref(cfg), _ptr(x), _ptr(hid), T, _ptr(y),
+                                                         _ptr(yf), _ptr(ids), _ptr(w), self.err))
+        return dict(y_bf16=y, y_f32=yf, ids=ids, w=w)
 
     # -- forward ----------------------------------------------------------
     def forward(self, cfg: LayerCfg, x, tokens: int, y_bf16=None, y_f32=None, ids=None, w=None, perm=None,

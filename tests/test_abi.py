@@ -43,7 +43,8 @@ def test_struct_layouts(pkg, tmp_path):
     inc = Path(__file__).resolve().parents[1] / "include"
     lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "moe_b200.h"', "int main(void) {"]
     checks = [("moe_b200_layer_cfg_t", L.LayerCfg), ("moe_b200_assignment_t", L.Assignment),
-              ("moe_b200_batch_t", L.Batch), ("moe_b200_init_t", L.InitT)]
+              ("moe_b200_batch_t", L.Batch), ("moe_b200_init_t", L.InitT),
+              ("moe_b200_block_tensors_t", L.BlockTensors)]
     for cname, py in checks:
         lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
         for fname, _ in py._fields_:
