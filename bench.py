@@ -423,9 +423,10 @@ def layer_bytes(shape, T, distinct):
     return wts + E * H * 2 + 2 * T * H * 2 + 2 * T * K * H * 2
 
 
-def tensor_roofline(shape, T, gu_ms, dn_ms, traffic):
+def tensor_roofline(shape, T, gu_ms, dn_ms, traffic, fp4=False):
     """The gate/up GEMM against the metric's MXFP4 roofline, and against the
-    rate of the MMA kind it issues (two E4M3 terms per bf16 activation)."""
+    rate of the MMA kind it issues: two E4M3 terms per bf16 activation at the
+    FP8 rate, or (fast mode) one E2M1 term at the MXFP4 rate."""
     H, I = shape.hidden, shape.intermediate
     P = T * (shape.top_k + (1 if shape.shared else 0))
     gu_flops = P * 4.0 * H * I
@@ -437,12 +438,15 @@ def tensor_roofline(shape, T, gu_ms, dn_ms, traffic):
             "achieved": ach, "peak": MXFP4_TFLOPS, "unit": "TFLOP/s", "frac": ach / MXFP4_TFLOPS,
             "peak_source": "spec: dense MXFP4 9 PFLOP/s (MEASURED_PEAKS.json has no FP4 or FP8 figure)",
             "traffic": traffic, "algorithmic_flops_per_launch": gu_flops, "launch_ms": gu_ms,
-            "issued": {"mma": "tcgen05.mma kind::mxf8f6f4 block_scale: E2M1 weights x E4M3 hi + lo activation terms",
-                       "flops_issued_per_launch": 2 * gu_flops, "achieved": 2 * ach, "peak": MXF8F6F4_TFLOPS,
-                       "frac": 2 * ach / MXF8F6F4_TFLOPS, "peak_source": "spec: dense FP8-rate 4.5 PFLOP/s"},
+            "issued": ({"mma": "tcgen05.mma kind::mxf4 block_scale: E2M1 weights x E2M1 activations",
+                        "flops_issued_per_launch": gu_flops, "achieved": ach, "peak": MXFP4_TFLOPS,
+                        "frac": ach / MXFP4_TFLOPS, "peak_source": "spec: dense MXFP4 9 PFLOP/s"} if fp4 else
+                       {"mma": "tcgen05.mma kind::mxf8f6f4 block_scale: E2M1 weights x E4M3 hi + lo activation terms",
+                        "flops_issued_per_launch": 2 * gu_flops, "achieved": 2 * ach, "peak": MXF8F6F4_TFLOPS,
+                        "frac": 2 * ach / MXF8F6F4_TFLOPS, "peak_source": "spec: dense FP8-rate 4.5 PFLOP/s"}),
             "vs_measured_bf16_cublas": {"peak": bf16, "frac": ach / bf16, "peak_source": bf16_kind},
             "down_gemm": {"achieved": dn_ach, "unit": "TFLOP/s", "launch_ms": dn_ms, "frac": dn_ach / MXFP4_TFLOPS,
-                          "issued_frac": 2 * dn_ach / MXF8F6F4_TFLOPS}}
+                          "issued_frac": dn_ach / MXFP4_TFLOPS if fp4 else 2 * dn_ach / MXF8F6F4_TFLOPS}}
 
 
 def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
@@ -586,7 +590,7 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     dist.destroy_process_group()
 
 
-def single_gpu_layer(args, shape, li, local, eng, L, uploaded, sample_clocks=True):
+def single_gpu_layer(args, shape, li, local, eng, L, uploaded, sample_clocks=True, gemm_path=0):
     """One configuration on one GPU: value, stages and e2e.  `uploaded` is
     the set of layer slots of `eng` that already hold this layer (slot 0 at
     least); more copies are uploaded when a step touches little."""
@@ -594,7 +598,7 @@ def single_gpu_layer(args, shape, li, local, eng, L, uploaded, sample_clocks=Tru
     import torch
 
     T, H, K = li.x.shape[0], shape.hidden, shape.top_k
-    cfg = L.Engine.cfg(shape)
+    cfg = L.Engine.cfg(shape, gemm_path=gemm_path)
     x = torch.from_numpy(li.x.view(np.int16)).cuda()
     y = torch.empty((T, H), dtype=torch.int16, device="cuda")
     ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
@@ -613,7 +617,7 @@ def single_gpu_layer(args, shape, li, local, eng, L, uploaded, sample_clocks=Tru
         if layer not in uploaded:
             eng.upload_layer(li, layer=layer)
             uploaded.add(layer)
-    cfgs = [cfg] + [L.Engine.cfg(shape, layer=layer) for layer in range(1, copies)]
+    cfgs = [cfg] + [L.Engine.cfg(shape, layer=layer, gemm_path=gemm_path) for layer in range(1, copies)]
     calls = [0]
 
     def next_cfg():
@@ -677,6 +681,29 @@ def single_gpu_layer(args, shape, li, local, eng, L, uploaded, sample_clocks=Tru
                 launches=launches_per_step, clk=clk)
 
 
+def fast_mode(args, shape, li, local, eng, L):
+    """The opt-in fast mode (MOE_B200_GEMM_MXF4_FAST: E2M1 activations and
+    intermediate, kind::mxf4 GEMMs) on the same workload: its throughput, its
+    GEMMs against the MXFP4 roofline, and how far its output is from the
+    tolerance-matched path's on a sample of the batch (it is not held to the
+    layer tolerance)."""
+    T = li.x.shape[0]
+    r = single_gpu_layer(args, shape, li, local, eng, L, {0}, sample_clocks=False, gemm_path=L.GEMM_MXF4_FAST)
+    sample = np.sort(np.random.default_rng(11).choice(T, size=min(64, T), replace=False))
+    xs = np.ascontiguousarray(li.x[sample])
+    exact = eng.forward_host(L.Engine.cfg(shape), xs)["y_f32"].astype(np.float64)
+    fast = eng.forward_host(L.Engine.cfg(shape, gemm_path=L.GEMM_MXF4_FAST), xs)["y_f32"].astype(np.float64)
+    d = np.abs(fast - exact)
+    st = r["stages"]
+    return {"gemm_path": "MOE_B200_GEMM_MXF4_FAST", "tolerance_matched": False,
+            "value": r["value"], "unit": "tokens/s", "ms_per_step": r["ms"] / args.steps, "e2e": r["e2e"],
+            "stages_ms_per_step": st,
+            "roofline": tensor_roofline(shape, T, st["gate_up"], st["down"], None, fp4=True),
+            "deviation_from_exact_path": {"tokens": int(len(sample)),
+                                          "max_abs_over_max_abs_y": float(d.max() / np.abs(exact).max()),
+                                          "mean_rel": float(d.mean() / np.abs(exact).mean())}}
+
+
 def decode_sweep(args, local, L, synth):
     """Config 1 at each decode batch size of its sweep, with the whole-layer
     HBM fraction (algorithmic bytes / step time against the measured copy
@@ -719,6 +746,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config 1 decode sweep of the default line")
+    ap.add_argument("--no-fast", action="store_true", help="skip the fast-mode (kind::mxf4) figures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     load_pkg()
@@ -793,6 +821,8 @@ def main():
         "gpu_launches": r["launches"] * args.steps,
         "clocks": r["clk"].summary() if r["clk"] else None,
     }
+    if is_prefill(args.config) and not args.no_fast:
+        result["fast_mode"] = fast_mode(args, shape, li, local, eng, L)
     eng.close()
     if args.config == DEFAULT_CONFIG and not args.no_sweep:
         result["decode_sweep"] = decode_sweep(args, local, L, synth)
