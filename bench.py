@@ -492,7 +492,7 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
     step_s = warmup_step_seconds(step, args.warmup, dist)
     eng.sync(sp)
     launches_per_step = eng.launches()
-    windows = windows_for(step_s, args.steps)
+    windows = args.windows or windows_for(step_s, args.steps)
     dist.barrier()
     with ClockSampler(local) as clk:
         win_ms = timed_windows(step, args.steps, windows, stream, dist)
@@ -533,7 +533,8 @@ def run_expert_parallel(args, shape, li, metric, rank, world, local, dist):
         step_host()
     dist.barrier()
     torch.cuda.synchronize()
-    n_e2e = torch.tensor([max(args.steps, int(math.ceil(2.0 / max(step_s, 1e-6))))], device="cuda")
+    n_e2e = torch.tensor([args.e2e_steps or max(args.steps, int(math.ceil(2.0 / max(step_s, 1e-6))))],
+                         device="cuda")
     dist.all_reduce(n_e2e, op=dist.ReduceOp.MAX)
     e2e_steps = int(n_e2e.item())
     t0 = time.perf_counter()
@@ -630,7 +631,7 @@ def single_gpu_layer(args, shape, li, local, eng, L, uploaded, sample_clocks=Tru
     step_s = warmup_step_seconds(step, args.warmup)
     eng.sync(sp)
     launches_per_step = eng.launches()
-    windows = windows_for(step_s, args.steps)
+    windows = args.windows or windows_for(step_s, args.steps)
     clk = None
     if sample_clocks:
         with ClockSampler(local) as clk:
@@ -667,7 +668,7 @@ def single_gpu_layer(args, shape, li, local, eng, L, uploaded, sample_clocks=Tru
     for _ in range(3):
         step_host()
     torch.cuda.synchronize()
-    e2e_steps = max(args.steps, int(math.ceil(2.0 / max(step_s, 1e-6))))
+    e2e_steps = args.e2e_steps or max(args.steps, int(math.ceil(2.0 / max(step_s, 1e-6))))
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         step_host()
@@ -747,12 +748,20 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config 1 decode sweep of the default line")
     ap.add_argument("--no-fast", action="store_true", help="skip the fast-mode (kind::mxf4) figures")
+    # for profiling runs (a short, fixed launch sequence under ncu)
+    ap.add_argument("--windows", type=int, default=0, help="timed windows (0: enough for ~3 s)")
+    ap.add_argument("--e2e-steps", type=int, default=0, help="host-buffer steps (0: enough for ~2 s)")
+    ap.add_argument("--experts", type=int, default=0,
+                    help="profiling only: the configuration's shapes with this many routed experts")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     load_pkg()
     import moe_b200.synth as synth
 
     shape = synth.CONFIGS[args.config]
+    if args.experts:
+        import dataclasses
+        shape = dataclasses.replace(shape, name=f"{shape.name}_e{args.experts}", experts=args.experts)
     if args.tokens <= 0:
         args.tokens = default_tokens(synth, args.config)
     metric = METRIC
