@@ -632,10 +632,12 @@ __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f 
 // generation_mlp.cpp.inc:94-104): SiLU, GELU in its erf form, or GELU in its
 // tanh form with x + 0.044715 x^3 as one multiply-add (CUDA's erff / tanhf;
 // tolerance parity like the rest of the expert math).
-__device__ __forceinline__ float gated_act(int act, float g) {
+// The GELU forms are kept out of line and chosen once per 8 values, so the
+// SiLU path of the epilogue is the same code as without them (an inline
+// select per value would be if-converted into evaluating every form).
+__device__ __noinline__ float gelu_act(int act, float g) {
     if (act == 1) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752440f));
-    if (act == 2) return 0.5f * g * (1.0f + tanhf(0.7978845608028654f * fmaf(0.044715f * g * g, g, g)));
-    return silu_fast(g);
+    return 0.5f * g * (1.0f + tanhf(0.7978845608028654f * fmaf(0.044715f * g * g, g, g)));
 }
 
 // Gate/up epilogue for 8 token columns of one row m: h = SiLU(gate) * up,
@@ -738,7 +740,11 @@ __device__ __forceinline__ void gu_store8(const float* g, const float* u, uint32
                                           uint8_t* h_atom) {
     float hv[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) hv[j] = gated_act(p.act, g[j]) * u[j];
+    for (int j = 0; j < 8; ++j) hv[j] = silu_fast(g[j]) * u[j];
+    if (p.act != 0) {  // uniform across the grid
+#pragma unroll
+        for (int j = 0; j < 8; ++j) hv[j] = gelu_act(p.act, g[j]) * u[j];
+    }
     if constexpr (FP4) {
         h_store8_fp4<BN>(hv, c0, nn, row0, m, lane, quarter, p, h_atom);
     } else {
