@@ -94,6 +94,12 @@ typedef struct {
     /* RMSNorms of the layer's block parts multiply by (1 + w) (Gemma models) */
     int32_t norm_unit_offset;
     float norm_eps;        /* RMSNorm epsilon of the block parts; <= 0 -> 1e-6 */
+    /* Partial-failure policy.  0: an expert (or the shared expert, with
+     * use_shared) that was never uploaded makes the call fail.  1: the
+     * reference's policy (generation_mlp.cpp.inc:1418, 833-860): such an
+     * expert contributes nothing -- its term is left out of the sum and the
+     * remaining weights are not renormalised; routing is unchanged. */
+    int32_t skip_missing;
 } moe_b200_layer_cfg_t;
 
 enum {

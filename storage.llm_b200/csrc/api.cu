@@ -533,6 +533,12 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
         CK(L->bs_gu_sfa.reserve(slots * 2 * (L->rp_i / 128) * (L->kq / 128) * 512));
         CK(L->bs_dn_codes.reserve(slots * L->rp_h * (L->iq / 2)));
         CK(L->bs_dn_sfa.reserve(slots * (L->rp_h / 128) * (L->iq / 128) * 512));
+        // slots never uploaded hold zero codes: such an expert computes an
+        // exact zero row, which is what skipping it adds (skip_missing)
+        CK(cudaMemsetAsync(L->bs_gu_codes.ptr, 0, L->bs_gu_codes.bytes, eng->ustream));
+        CK(cudaMemsetAsync(L->bs_gu_sfa.ptr, 0, L->bs_gu_sfa.bytes, eng->ustream));
+        CK(cudaMemsetAsync(L->bs_dn_codes.ptr, 0, L->bs_dn_codes.bytes, eng->ustream));
+        CK(cudaMemsetAsync(L->bs_dn_sfa.ptr, 0, L->bs_dn_sfa.bytes, eng->ustream));
         // codes are 8 KB blocks of 128 rows x 128 K: a "tall" tensor of 128-element
         // rows, one 128 x 128 box per block
         if (!make_tmap2d(eng, &L->tmap_gu_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_gu_codes.ptr, 128,
@@ -603,14 +609,19 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
                 H, I);
         return 0;
     }
-    for (uint32_t e = 0; e < E; ++e) {
+    if (L->present.size() != (size_t)E + 1) {
+        set_err(err, "layer %d has no experts uploaded", cfg->layer);
+        return 0;
+    }
+    const bool skip_missing = cfg->skip_missing != 0;
+    for (uint32_t e = 0; e < E && !skip_missing; ++e) {
         if (!L->present[e]) {
             set_err(err, "expert %u of layer %d was never uploaded", e, cfg->layer);
             return 0;
         }
     }
     const bool shared = cfg->use_shared != 0;
-    if (shared && !L->present[E]) {
+    if (shared && !L->present[E] && !skip_missing) {
         set_err(err, "layer %d has no shared expert uploaded", cfg->layer);
         return 0;
     }
@@ -623,6 +634,10 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
     }
     if (block && !bs) {
         set_err(err, "block parts and GELU activations run on the block-scaled GEMM paths (gemm_path 0 or 3)");
+        return 0;
+    }
+    if (skip_missing && !bs) {
+        set_err(err, "skip_missing runs on the block-scaled GEMM paths (gemm_path 0 or 3)");
         return 0;
     }
     if (L->has_block() && H > 25600) {

@@ -640,14 +640,18 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     }
     if (ep->place_E != E && !ep_default_placement(ep, E, err)) return 0;
     const uint32_t e_loc = (uint32_t)ep->local_list.size();
+    if (L->present.size() != (size_t)E + 1) {
+        set_err(err, "layer %d has no experts uploaded", cfg->layer);
+        return 0;
+    }
     for (uint32_t e : ep->local_list) {
-        if (!L->present[e]) {
+        if (!L->present[e] && !cfg->skip_missing) {
             set_err(err, "local expert %u of layer %d was never uploaded", e, cfg->layer);
             return 0;
         }
     }
     const bool shared = cfg->use_shared != 0;
-    if (shared && !L->present[E]) {
+    if (shared && !L->present[E] && !cfg->skip_missing) {
         set_err(err, "layer %d has no shared expert uploaded", cfg->layer);
         return 0;
     }

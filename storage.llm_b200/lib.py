@@ -36,7 +36,8 @@ class LayerCfg(C.Structure):
                 ("top_k", C.c_uint32), ("layer", C.c_int32), ("score_func", C.c_int32),
                 ("norm_topk", C.c_int32), ("routed_scale", C.c_float), ("use_shared", C.c_int32),
                 ("gemm_path", C.c_int32), ("n_group", C.c_uint32), ("topk_group", C.c_uint32),
-                ("activation", C.c_int32), ("norm_unit_offset", C.c_int32), ("norm_eps", C.c_float)]
+                ("activation", C.c_int32), ("norm_unit_offset", C.c_int32), ("norm_eps", C.c_float),
+                ("skip_missing", C.c_int32)]
 
 
 class BlockTensors(C.Structure):
@@ -197,12 +198,12 @@ class Engine:
     def cfg(shape, layer: int = 0, gemm_path: int = GEMM_TCGEN05, score_func: int = SCORE_SOFTMAX,
             norm_topk: Optional[bool] = None, routed_scale: float = 1.0, use_shared: Optional[bool] = None,
             n_group: int = 0, topk_group: int = 0, activation: int = ACT_SILU, norm_unit_offset: bool = False,
-            norm_eps: float = 0.0):
+            norm_eps: float = 0.0, skip_missing: bool = False):
         nt = shape.norm_topk if norm_topk is None else norm_topk
         us = shape.shared if use_shared is None else use_shared
         return LayerCfg(shape.hidden, shape.intermediate, shape.experts, shape.top_k, layer, score_func, int(nt),
                         routed_scale, int(us), gemm_path, n_group, topk_group, activation, int(norm_unit_offset),
-                        norm_eps)
+                        norm_eps, int(skip_missing))
 
     def upload_block(self, layer: int, pre_norm2=None, post_norm1=None, post_norm2=None, post_norm=None,
                      down_scale=None, shared_gate_inp=None, router_scale=None):
