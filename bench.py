@@ -751,6 +751,8 @@ def main():
     # for profiling runs (a short, fixed launch sequence under ncu)
     ap.add_argument("--windows", type=int, default=0, help="timed windows (0: enough for ~3 s)")
     ap.add_argument("--e2e-steps", type=int, default=0, help="host-buffer steps (0: enough for ~2 s)")
+    ap.add_argument("--gemm-path", default="exact", choices=["exact", "fast"],
+                    help="profiling only: run the main line through the fast mode")
     ap.add_argument("--experts", type=int, default=0,
                     help="profiling only: the configuration's shapes with this many routed experts")
     args = ap.parse_args()
@@ -792,14 +794,16 @@ def main():
         return
     eng = L.Engine(local, max_layers=MAX_COPIES)
     eng.upload_layer(li)
-    r = single_gpu_layer(args, shape, li, local, eng, L, {0})
+    main_path = L.GEMM_MXF4_FAST if args.gemm_path == "fast" else L.GEMM_BLOCKSCALED
+    r = single_gpu_layer(args, shape, li, local, eng, L, {0}, gemm_path=main_path)
     T, H, K = args.tokens, shape.hidden, shape.top_k
     stages = r["stages"]
     gu_ms, dn_ms = stages["gate_up"], stages["down"]
     hbm, _, peak_kind = measured_peaks()
     P = T * K + (T if shape.shared else 0)
     if is_prefill(args.config):
-        roofline = tensor_roofline(shape, T, gu_ms, dn_ms, profiled_traffic(args.config, T))
+        roofline = tensor_roofline(shape, T, gu_ms, dn_ms, profiled_traffic(args.config, T),
+                                   fp4=main_path == L.GEMM_MXF4_FAST)
     else:
         # gate/up: the routed experts' gate and up weights + the permuted
         # rows in + the intermediate out, at 2 bytes per element
@@ -817,6 +821,8 @@ def main():
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
         "config": config_dict(shape, args),
+        "gemm_path": ("fast mode (kind::mxf4, not tolerance-matched)" if main_path == L.GEMM_MXF4_FAST
+                      else "block-scaled, tolerance-matched"),
         "l2_reuse": {"weight_copies_cycled": r["copies"], "weight_bytes_between_reuses": r["touched"] * r["copies"]},
         "timing": {"windows": r["windows"], "window_ms": r["win_ms"], "reported": "median window"},
         "e2e": {"value": r["e2e"], "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
