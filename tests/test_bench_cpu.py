@@ -78,3 +78,32 @@ def test_replica_placement_invariants():
         biggest = max(counts[e] / len(r) for e, r in enumerate(placement))
         assert load.max() <= load.mean() + biggest + 1e-9
         assert abs(imbalance - load.max() / max(load.mean(), 1e-9)) < 1e-9
+
+
+def test_tensor_roofline_arithmetic():
+    """The headline roofline: gate/up algorithmic FLOPs (4 H I per permuted
+    row, P = T (k + shared)) over the launch time, against the 9 PF MXFP4
+    peak; the issued view doubles the FLOPs (hi + lo terms) against the
+    4.5 PF FP8 rate, or keeps them against 9 PF in the fast mode; the
+    reference arm's config dict equals the GPU arm's."""
+    import importlib.util
+    import argparse
+    root = Path(__file__).resolve().parents[1]
+    spec = importlib.util.spec_from_file_location("bench_mod3", root / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    bench.load_pkg()
+    import moe_b200.synth as synth
+    c4 = synth.CONFIGS[4]
+    T = 16384
+    r = bench.tensor_roofline(c4, T, 8.0, 4.0, None)
+    flops = T * 9 * 4.0 * 7168 * 2048
+    assert abs(r["algorithmic_flops_per_launch"] - flops) < 1
+    assert abs(r["achieved"] - flops / 8e-3 / 1e12) < 1e-6
+    assert r["peak"] == 9000.0 and abs(r["frac"] - r["achieved"] / 9000.0) < 1e-12
+    assert abs(r["issued"]["frac"] - 2 * r["achieved"] / 4500.0) < 1e-12 and r["bound"] == "tensor"
+    f = bench.tensor_roofline(c4, T, 8.0, 4.0, None, fp4=True)
+    assert abs(f["issued"]["frac"] - f["achieved"] / 9000.0) < 1e-12
+    args = argparse.Namespace(config=4, tokens=T, gpus=1)
+    assert bench.config_dict(c4, args) == bench.config_dict(c4, args)
+    assert "weight_copies_cycled" not in bench.config_dict(c4, args)
