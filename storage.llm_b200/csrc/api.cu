@@ -202,8 +202,7 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     // config 1, 32 rows per group, are 5 % faster with 64; config 3, 256 rows
     // per group, 3 % faster with 128)
     const uint64_t avg_x = G ? (uint64_t)P / G : 0;
-    // (the fast mode's wide tiles are 96 tokens: two accumulators fit in TMEM)
-    const uint32_t block_n = avg_x <= 16 ? 32u : (avg_x <= 160 ? 64u : (job.fp4 ? 96u : kBlockN));
+    const uint32_t block_n = avg_x <= 16 ? 32u : (avg_x <= 160 ? 64u : kBlockN);
     const uint32_t ntiles = sort_tiles(n);
     const uint32_t token_tiles = P / block_n + G;  // upper bound of sum_g ceil(count_g / block_n)
     uint32_t* errw = eng->err_word.as<uint32_t>();
@@ -233,7 +232,7 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     } specs[2] = {{eng->tmap_xb, &eng->xb, Kq}, {eng->tmap_hb, &eng->hb, Iq}};
     for (int i = 0; i < 2 && job.fp4; ++i) {
         // fast mode: [rows][cols / 2] packed E2M1 bytes at the start of the
-        // same buffer, 64-byte boxes of 32, 64 or 96 rows
+        // same buffer, 64-byte boxes of 32, 64 or 128 rows
         CUtensorMap* maps = i == 0 ? eng->tmap_xq : eng->tmap_hq;
         const uint64_t rows = specs[i].buf->bytes / (2ull * specs[i].cols);
         const uint64_t rb = specs[i].cols / 2;
@@ -241,7 +240,7 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
             eng->fp4_map_dims[i][1] != rows) {
             for (int b = 0; b < 3; ++b) {
                 if (!make_tmap2d(eng, &maps[b], CU_TENSOR_MAP_DATA_TYPE_UINT8, specs[i].buf->ptr, rb, rows, rb, 64,
-                                 b == 2 ? 96u : 32u << b, err, CU_TENSOR_MAP_SWIZZLE_64B)) {
+                                 32u << b, err, CU_TENSOR_MAP_SWIZZLE_64B)) {
                     return 0;
                 }
             }

@@ -50,10 +50,7 @@ namespace moe_b200 {
 // B term, 64-byte swizzled rows (one 128-K stage per row).
 template <int MODE, int BN, bool FP4 = false>
 struct BsCfg {
-    // 96-token tiles are the fast mode's prefill width: two accumulators of
-    // gate + up (2 x 192 TMEM columns) and the scale-factor ring fit in TMEM,
-    // so a tile's epilogue overlaps the next tile's MMAs
-    static_assert(BN == 32 || BN == 64 || BN == 128 || (FP4 && BN == 96), "tile width");
+    static_assert(BN == 32 || BN == 64 || BN == 128, "tile width");
     static constexpr bool kStackN = !FP4 && BN <= 64;
     static constexpr int kNA = MODE == kGateUp ? 2 : 1;       // A operands per stage
     static constexpr int kABytes = FP4 ? 128 * 64 : 128 * 128;  // smem bytes per A box
@@ -66,14 +63,11 @@ struct BsCfg {
     static constexpr int kStageBytes = kNA * kABytes + kBTerms * kBBytes + kSFStage;
     static constexpr int kStages = (210 * 1024) / kStageBytes;
     static constexpr int kAccCols = kNA * (kStackN ? 2 * BN : BN);
+    static constexpr int kAccs = 256 / kAccCols >= 2 ? 2 : 1;
     static constexpr int kSFCols = kSFStage / 128;            // TMEM columns of scale factors per stage
-    // two accumulators whenever they fit beside the scale-factor ring
-    static constexpr int kAccs = 2 * kAccCols + kStages * kSFCols <= 512 ? 2 : 1;
-    // first TMEM column of the scale-factor ring
-    static constexpr int kSfCol0 = kAccs * kAccCols > 256 ? kAccs * kAccCols : 256;
     static constexpr int kSmem = kStages * kStageBytes + 2048 /*two 1024 alignments*/ + 512 /*barriers*/;
     static_assert(kStages >= 3, "pipeline too shallow");
-    static_assert(kAccs * kAccCols <= kSfCol0 && kSfCol0 + kStages * kSFCols <= 512, "TMEM budget");
+    static_assert(256 + kStages * kSFCols <= 512, "TMEM budget");
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
@@ -875,7 +869,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
     // after pdl_wait() in the producer.
     pdl_trigger();
     const uint32_t total = p.tile_off[p.groups];
-    constexpr uint32_t kSfCol0 = C::kSfCol0;
+    constexpr uint32_t kSfCol0 = 256;
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -1184,9 +1178,6 @@ static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, 
 template <int MODE, bool FP4>
 static cudaError_t launch_bs_width(int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
                                    int num_sms, cudaStream_t st, bool pdl) {
-    if constexpr (FP4) {
-        if (block_n == 96) return launch_bs_mode<MODE, 96, FP4>(ta, tb, p, num_sms, st, pdl);
-    }
     if (block_n == 32) return launch_bs_mode<MODE, 32, FP4>(ta, tb, p, num_sms, st, pdl);
     if (block_n == 64) return launch_bs_mode<MODE, 64, FP4>(ta, tb, p, num_sms, st, pdl);
     return launch_bs_mode<MODE, 128, FP4>(ta, tb, p, num_sms, st, pdl);
