@@ -82,8 +82,9 @@ def emulate(li, ids, w):
     return y
 
 
-@pytest.mark.parametrize("tokens,top_k,experts,shared", [(64, 2, 8, False), (300, 3, 8, True), (24, 4, 16, False)],
-                         ids=["t64_k2", "t300_k3_shared", "t24_k4"])
+@pytest.mark.parametrize("tokens,top_k,experts,shared",
+                         [(64, 2, 8, False), (300, 3, 8, True), (24, 4, 16, False), (1100, 2, 8, True)],
+                         ids=["t64_k2_tile32", "t300_k3_shared_tile64", "t24_k4", "t1100_shared_tile128"])
 def test_fast_mode_matches_its_emulation(engine, synth, L, tokens, top_k, experts, shared):
     shape = synth.small_shape(name="fast", hidden=256, intermediate=320, experts=experts, top_k=top_k,
                               tokens=tokens, shared=shared)
