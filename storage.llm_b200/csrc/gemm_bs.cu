@@ -952,21 +952,9 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                     // operands landed (observed here too, so this thread's MMAs
                     // are ordered after the copies) and the scale factors are in TMEM
                     if (!(ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull))) break;
-                    if constexpr (!FP4) {
-                        if (!(ok = mbar_wait(&sf_full[stage], phase, p.err, kErrTimeoutAFull))) break;
-                    }
+                    if (!(ok = mbar_wait(&sf_full[stage], phase, p.err, kErrTimeoutAFull))) break;
                     tc_fence_after();
                     const uint32_t sfc = tmem + kSfCol0 + stage * C::kSFCols;
-                    if constexpr (FP4) {
-                        // fast mode: a stage is only ~270 cycles of tensor work, too
-                        // short to hide the scale-factor warps' store / wait / signal
-                        // round trip, so this thread copies the stage's scale blocks
-                        // into TMEM itself, in order with its MMAs
-#pragma unroll
-                        for (int q = 0; q < C::kSFStage / 512; ++q) {
-                            tmem_cp_sf(sfc + q * 4, smem_desc_sf(smem_u32(sf_base + stage * C::kSFStage + q * 512)));
-                        }
-                    }
                     const uint32_t sfb = sfc + C::kNA * 4;
                     const uint32_t a_addr = smem_u32(a_base + stage * C::kNA * C::kABytes);
                     const uint32_t b_addr = smem_u32(b_base + stage * C::kBTerms * C::kBBytes);
@@ -1027,8 +1015,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         uint32_t stage = 0, phase = 0, eaccphase = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-            // (the fast mode's MMA thread copies the scale factors itself)
-            for (uint32_t kt = 0; !FP4 && kt < p.k_tiles; ++kt) {
+            for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
                 ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
