@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -264,14 +265,19 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
         }
     }
 
+    // CTA pairs take the 128-token tiles of the exact path when the weight
+    // row tiles pair up; the tile table then counts pairs of row tiles
+    const bool pair_ok = eng->cta_pairs && !job.fp4 && block_n == kBlockN;
+    const bool pair_gu = pair_ok && (L->rp_i / 128) % 2 == 0;
+    const bool pair_dn = pair_ok && (L->rp_h / 128) % 2 == 0;
     GroupInfo gi;
     gi.count = eng->g_count.as<uint32_t>();
     gi.offset = eng->g_offset.as<uint32_t>();
     gi.gu_tile_off = eng->g_gu_off.as<uint32_t>();
     gi.dn_tile_off = eng->g_dn_off.as<uint32_t>();
     gi.block_n = block_n;
-    gi.gu_row_tiles = L->rp_i / 128;
-    gi.dn_row_tiles = L->rp_h / 128;
+    gi.gu_row_tiles = L->rp_i / (pair_gu ? 256 : 128);
+    gi.dn_row_tiles = L->rp_h / (pair_dn ? 256 : 128);
     if (route_small_fits(n, job.E)) {
         // decode-sized batch: sort, offsets and both tile tables in one block
         CK(launch_route_small(job.ids, job.T, job.K, job.E, job.shared_rows, job.shared_base, gi,
@@ -285,9 +291,9 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
                           eng->tile_counts.as<uint32_t>(), eng->rank.as<uint32_t>(), gi, eng->pos_of.as<uint32_t>(),
                           eng->row_token.as<uint32_t>(), eng->row_assign.as<uint32_t>(),
                           eng->row_info.as<uint32_t>(), errw, st));
-        CK(launch_build_tiles(gi.count, gi.offset, gi.gu_tile_off, G, L->rp_i / 128, block_n,
+        CK(launch_build_tiles(gi.count, gi.offset, gi.gu_tile_off, G, gi.gu_row_tiles, block_n,
                               token_tiles * (L->rp_i / 128), eng->gu_tiles.as<TileEntry>(), st));
-        CK(launch_build_tiles(gi.count, gi.offset, gi.dn_tile_off, G, L->rp_h / 128, block_n,
+        CK(launch_build_tiles(gi.count, gi.offset, gi.dn_tile_off, G, gi.dn_row_tiles, block_n,
                               token_tiles * (L->rp_h / 128), eng->dn_tiles.as<TileEntry>(), st));
         *launches += 5;
     }
@@ -361,8 +367,10 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     bp.sfh_atoms = eng->sfh_atoms.as<uint8_t>();
     bp.m_valid = Iq;
     const int bi = block_n == 32 ? 0 : (block_n == 64 ? 1 : 2);
+    // a pair's CTAs each load half of the tile's token rows (the 64-row box)
     CK(launch_gemm_bs(kGateUp, (int)block_n, job.fp4 ? L->tmap_gu_fp4 : L->tmap_gu_codes,
-                      job.fp4 ? eng->tmap_xq[bi] : eng->tmap_xb[bi], bp, eng->num_sms, st, true, job.fp4));
+                      job.fp4 ? eng->tmap_xq[bi] : eng->tmap_xb[pair_gu ? 1 : bi], bp, eng->num_sms, st, true,
+                      job.fp4, pair_gu));
     *launches += 1;
     mark(4);
     // down: K = I (padded Iq), M = H rows (padded rp_h), output fp32 rows
@@ -384,7 +392,8 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     bp.ret_rows = job.ret_rows;
     bp.ret_world = job.ret_world;
     CK(launch_gemm_bs(kDown, (int)block_n, job.fp4 ? L->tmap_dn_fp4 : L->tmap_dn_codes,
-                      job.fp4 ? eng->tmap_hq[bi] : eng->tmap_hb[bi], bp, eng->num_sms, st, true, job.fp4));
+                      job.fp4 ? eng->tmap_hq[bi] : eng->tmap_hb[pair_dn ? 1 : bi], bp, eng->num_sms, st, true,
+                      job.fp4, pair_dn));
     *launches += 1;
     mark(5);
     return 1;
@@ -423,6 +432,10 @@ moe_b200_engine_t* moe_b200_create(const moe_b200_init_t* init, char* err) {
     }
     eng->device = device;
     eng->num_sms = prop.multiProcessorCount;
+    {
+        const char* v = std::getenv("MOE_B200_CTA_PAIRS");
+        eng->cta_pairs = !(v && v[0] == '0');
+    }
     eng->layers.resize(layers);
     if (eng->err_word.reserve(sizeof(uint32_t)) != cudaSuccess ||
         cudaMemset(eng->err_word.ptr, 0, sizeof(uint32_t)) != cudaSuccess ||

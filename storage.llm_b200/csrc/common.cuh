@@ -149,6 +149,27 @@ inline cudaError_t launch_kernel(void (*kernel)(Exp...), dim3 grid, dim3 block, 
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
 }
 
+// launch_kernel for clusters of two CTAs (grid.x even).
+template <typename... Exp, typename... Act>
+inline cudaError_t launch_kernel_cluster2(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem,
+                                          cudaStream_t st, bool pdl, Act&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
+}
+
 // ---------------------------------------------------------------------------
 // Bulk and tensor copies; each one fills only the issuing CTA's shared memory.
 // ---------------------------------------------------------------------------
@@ -245,6 +266,90 @@ __device__ __forceinline__ uint32_t idesc_bf16_m128(uint32_t n) {
            | ((128u >> 4) << 24);  // M / 16
 }
 
+// ---------------------------------------------------------------------------
+// CTA pairs (a cluster of two CTAs on the two SMs of a TPC running one
+// cta_group::2 MMA of M = 256): each CTA holds its 128 rows of A and half of
+// the B rows in its own shared memory; the even CTA (rank 0) issues the MMAs
+// and owns the barriers the MMA waits on.  Addresses of the rank-0 CTA's
+// barriers are shared::cluster addresses from mapa.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the variable at `p` in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_cluster(const void* p, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+    return a;
+}
+
+// Arrivals on another CTA's barrier.  Default (release, CTA-scope)
+// semantics as for local arrivals: what the barriers order here is tensor-
+// core and copy work (tcgen05 fences, complete_tx), not generic memory, and a
+// cluster-scope release would first drain this thread's global stores.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cl) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cl) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t bar_cl, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cl), "r"(bytes)
+                 : "memory");
+}
+
+// Every thread of both CTAs: arrive (release) and wait (acquire).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Tensor loads into this CTA's shared memory whose completion is counted on
+// the rank-0 CTA's barrier (bar_cl, a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                                 uint32_t bar_cl) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cl)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                                 int32_t c2, uint32_t bar_cl) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar_cl)
+        : "memory");
+}
+
+// TMEM of a CTA pair: one warp with the same warp index in each CTA executes
+// these; both CTAs get the same columns.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Arrives on the barrier at this offset in each CTA of `mask` once the
+// pair MMAs this thread issued so far have completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(mask)
+        : "memory");
+}
+
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (the layout a TMA SWIZZLE_128B box of 64 bf16 per row
 // writes).  `addr` must lie in a 1024-byte aligned tile; advancing K by 16
@@ -284,6 +389,20 @@ __device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_
         : "memory");
 }
 
+// The same MMA over a CTA pair (M = 256: rows 0-127 from the rank-0 CTA's
+// A, 128-255 from the rank-1 CTA's at the same shared-memory offset; B rows
+// [0, N/2) from the rank-0 CTA, [N/2, N) from the rank-1 CTA; each CTA's
+// TMEM holds its rows' accumulator, its rows' A scales and all N B scales).
+__device__ __forceinline__ void mma_bs_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+}
+
 // Same MMA with A read from tensor memory ([a_tmem]: lane 0, first column of
 // the 128-row A slice; one 32-bit column per 4 bytes of each row).
 __device__ __forceinline__ void mma_bs_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -297,17 +416,19 @@ __device__ __forceinline__ void mma_bs_ts(uint32_t d_tmem, uint32_t a_tmem, uint
 }
 
 // Instruction descriptor for kind::mxf8f6f4 block_scale: A E2M1, B E4M3,
-// E8M0 scales, both operands K-major, M = 128, N = n; `sf_id` selects the
-// byte of each 32-bit scale word (the 32-element K block inside a 128-K stage).
-__device__ __forceinline__ uint32_t idesc_bs_m128(uint32_t n, uint32_t sf_id) {
+// E8M0 scales, both operands K-major, M = m (128; 256 for a CTA pair),
+// N = n; `sf_id` selects the byte of each 32-bit scale word (the 32-element
+// K block inside a 128-K stage).
+__device__ __forceinline__ uint32_t idesc_bs(uint32_t m, uint32_t n, uint32_t sf_id) {
     return (sf_id << 4)          // B scale-factor id
            | (5u << 7)           // A format E2M1
            | (0u << 10)          // B format E4M3
            | ((n >> 3) << 17)    // N / 8
            | (1u << 23)          // scale format E8M0
-           | ((128u >> 4) << 24) // M / 16
+           | ((m >> 4) << 24)    // M / 16
            | (sf_id << 29);      // A scale-factor id
 }
+__device__ __forceinline__ uint32_t idesc_bs_m128(uint32_t n, uint32_t sf_id) { return idesc_bs(128, n, sf_id); }
 
 // ---------------------------------------------------------------------------
 // Block-scaled MMA on packed FP4 operands (kind::mxf4, the fast mode): A and

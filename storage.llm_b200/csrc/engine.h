@@ -123,6 +123,10 @@ struct moe_b200_engine {
     using EncodeTiledFn = moe_b200::EncodeTiledFn;
     int device = 0;
     int num_sms = 148;
+    // 128-token tiles of the exact path run on CTA pairs (cta_group::2);
+    // MOE_B200_CTA_PAIRS=0 in the environment at engine creation selects the
+    // one-CTA kernels instead
+    bool cta_pairs = true;
     std::vector<LayerWeights> layers;
     DevBuf staging;  // GGUF bytes copied from the host before the repack
     // uploads and tile-form derivations run here and wait only for

@@ -19,13 +19,14 @@
 //      memory opened with CUDA IPC); the host meanwhile reads the matrix
 //      (polling the mapped flag, no stream synchronisation), and in the rare
 //      call where a buffer must grow, all ranks grow and dispatch again;
-//   5. device barrier, then the block-scaled
-//      pipeline on the received rows, grouped by (local expert, source rank,
-//      source order); the shared expert's rows (the rank's own tokens) ride
-//      along as the extra group.  The down GEMM's epilogue stores every
-//      expert row straight into its source rank's return buffer, at the
-//      position the row was sent from: compute and the return exchange are
-//      one kernel, tile by tile;
+//   5. the block-scaled pipeline on the received rows, grouped by (local
+//      expert, source rank, source order).  The down GEMM's epilogue stores
+//      every expert row straight into its source rank's return buffer, at
+//      the position the row was sent from: compute and the return exchange
+//      are one kernel, tile by tile.  The shared expert on the rank's own
+//      tokens needs nothing from the exchange: its pipeline is enqueued on a
+//      side stream right after the router and runs while steps 2-4 move the
+//      counts and rows over NVLink;
 //   6. device barrier, then the single-device combine: shared row + the K
 //      expert rows in router order, one fused multiply-add each.
 // The device barriers store an epoch into every rank's control words
@@ -265,6 +266,12 @@ struct EpState {
     std::vector<uint32_t> rep_off, rep_ranks, local_list;
     DevBuf d_rep_off, d_rep_ranks, d_local_idx, meta;
     bool slots_dirty = true;
+    // the shared expert's rows (this rank's own tokens) run on a side stream
+    // while the token rows cross NVLink: its group map, its all-zero group
+    // ids, its output rows, and the fork / join events
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    DevBuf shared_slot, zero_ids, yshared;
 };
 
 void close_peers(EpState* ep, SymBuf& b) {
@@ -287,6 +294,12 @@ void ep_release(EpState* ep) {
                       &ep->recv_meta.local, &ep->ret.local, &ep->d_rep_off, &ep->d_rep_ranks,
                       &ep->d_local_idx, &ep->meta, &ep->ctrl.local, &ep->ctrl_ptrs, &ep->cap_rows};
     for (DevBuf* b : bufs) b->release();
+    ep->shared_slot.release();
+    ep->zero_ids.release();
+    ep->yshared.release();
+    if (ep->side) cudaStreamDestroy(ep->side);
+    if (ep->ev_fork) cudaEventDestroy(ep->ev_fork);
+    if (ep->ev_join) cudaEventDestroy(ep->ev_join);
     if (ep->h_ctrl) cudaFreeHost(ep->h_ctrl);
     delete ep;
 }
@@ -521,7 +534,10 @@ int moe_b200_ep_init(moe_b200_engine_t* eng, int rank, int world, const uint8_t*
         cudaHostGetDevicePointer(&ep->d_h_ctrl, ep->h_ctrl, 0) != cudaSuccess ||
         ep->barrier_word.reserve(4) != cudaSuccess || cudaMemset(ep->barrier_word.ptr, 0, 4) != cudaSuccess ||
         ep->ctrl.local.reserve(ctrl_bytes) != cudaSuccess ||
-        cudaMemset(ep->ctrl.local.ptr, 0, ctrl_bytes) != cudaSuccess) {
+        cudaMemset(ep->ctrl.local.ptr, 0, ctrl_bytes) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ep->side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ep->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ep->ev_join, cudaEventDisableTiming) != cudaSuccess) {
         set_err(err, "allocation failed");
         ep_release(ep);
         return 0;
@@ -700,6 +716,45 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     }
 
     mark(1);
+    // the shared expert's pass may start once the previous call's local
+    // experts are done with the workspace, i.e. from here on
+    CK(cudaEventRecord(ep->ev_fork, st));
+    if (ep->slots_dirty) {
+        std::vector<uint32_t> slots(ep->local_list);
+        CK(ep->slots.reserve(std::max<size_t>(slots.size(), 1) * 4));
+        if (!slots.empty()) {
+            CK(cudaMemcpy(ep->slots.ptr, slots.data(), slots.size() * 4, cudaMemcpyHostToDevice));
+        }
+        const uint32_t ss = E;  // the shared expert's slot
+        CK(ep->shared_slot.reserve(4));
+        CK(cudaMemcpy(ep->shared_slot.ptr, &ss, 4, cudaMemcpyHostToDevice));
+        ep->slots_dirty = false;
+    }
+    // The shared expert on this rank's own tokens needs nothing from the
+    // exchange: its pipeline (one group, all token ids 0, the shared slot)
+    // runs on the side stream while the counts and rows cross NVLink.  A
+    // workspace that the received rows' pass grows later is reallocated by
+    // cudaFree / cudaMalloc, which wait for this pass first.
+    const uint32_t shared_rows = shared ? T : 0;
+    if (shared_rows) {
+        if (ep->zero_ids.bytes < (size_t)T * 4) {
+            CK(ep->zero_ids.reserve((size_t)T * 4));
+            CK(cudaMemset(ep->zero_ids.ptr, 0, ep->zero_ids.bytes));
+        }
+        CK(ep->yshared.reserve((size_t)T * H * 4));
+        BsJob sj{};
+        sj.ids = ep->zero_ids.as<int32_t>();
+        sj.T = T;
+        sj.K = 1;
+        sj.E = 1;
+        sj.src = x;
+        sj.group_slot = ep->shared_slot.as<uint32_t>();
+        sj.y = ep->yshared.as<float>();
+        sj.y_by_source = true;
+        CK(cudaStreamWaitEvent(ep->side, ep->ev_fork, 0));
+        if (!run_blockscaled(eng, L, sj, ep->side, nullptr, &launches, err)) return 0;
+        CK(cudaEventRecord(ep->ev_join, ep->side));
+    }
     // 2. stable sort of the assignments by owner rank
     CK(ep->dest.reserve((size_t)std::max(n, 1u) * 4));
     CK(ep->pos.reserve((size_t)std::max(n, 1u) * 4));
@@ -800,13 +855,10 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
         return 0;
     }
     const uint32_t n_recv = (uint32_t)recv_of[me];
-    const uint32_t shared_rows = shared ? T : 0;
-    const uint32_t rows = n_recv + shared_rows;  // rows the local experts run on
     {
         std::vector<uint64_t> need_x(W), need_meta(W), need_ret(W);
         for (uint32_t q = 0; q < W; ++q) {
-            const uint64_t tq = n_of[q] / K;  // rank q's tokens
-            need_x[q] = (recv_of[q] + (shared ? tq : 0)) * H * 2 + 16;
+            need_x[q] = recv_of[q] * H * 2 + 16;
             need_meta[q] = recv_of[q] * 4 + 16;
             need_ret[q] = n_of[q] * H * 4 + 16;
         }
@@ -823,40 +875,30 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     }
     uint16_t* recv_x = ep->recv_x.local.as<uint16_t>();
     void** d_ptrs = ep->ptrs.as<void*>();
-    if (shared_rows) {
-        CK(cudaMemcpyAsync(recv_x + (size_t)n_recv * H, x, (size_t)T * H * 2, cudaMemcpyDeviceToDevice, st));
-    }
     mark(3);
     mark(4);
 
-    // 5. local experts (+ the shared expert on the local tokens); the down
-    //    GEMM stores other ranks' rows into their return buffers
-    if (ep->slots_dirty) {
-        std::vector<uint32_t> slots(ep->local_list);
-        slots.push_back(E);  // the shared expert's slot
-        CK(ep->slots.reserve(slots.size() * 4));
-        CK(cudaMemcpy(ep->slots.ptr, slots.data(), slots.size() * 4, cudaMemcpyHostToDevice));
-        ep->slots_dirty = false;
-    }
-    CK(ep->yloc.reserve((size_t)std::max(rows, 1u) * H * 4));
-    if (rows > 0) {
-        BsJob job{};
-        job.ids = ep->recv_meta.local.as<int32_t>();
-        job.T = n_recv;
-        job.K = 1;
-        job.E = e_loc;
-        job.shared_rows = shared_rows;
-        job.shared_base = n_recv;
-        job.src = recv_x;
-        job.group_slot = ep->slots.as<uint32_t>();
-        job.y = ep->yloc.as<float>();
-        job.y_by_source = true;
-        job.ret_ptrs = reinterpret_cast<float* const*>(d_ptrs + 2 * W);
-        job.ret_roff = d_roff;
-        job.ret_base = d_sbase;
-        job.ret_rows = n_recv;
-        job.ret_world = W;
-        if (!run_blockscaled(eng, L, job, st, nullptr, &launches, err)) return 0;
+    // 5. local experts on the received rows (after the shared expert's pass,
+    //    which used the same workspace); the down GEMM stores other ranks'
+    //    rows into their return buffers
+    if (shared_rows) CK(cudaStreamWaitEvent(st, ep->ev_join, 0));
+    CK(ep->yloc.reserve((size_t)std::max(n_recv, 1u) * H * 4));
+    BsJob mj{};
+    mj.ids = ep->recv_meta.local.as<int32_t>();
+    mj.T = n_recv;
+    mj.K = 1;
+    mj.E = e_loc;
+    mj.src = recv_x;
+    mj.group_slot = ep->slots.as<uint32_t>();
+    mj.y = ep->yloc.as<float>();
+    mj.y_by_source = true;
+    mj.ret_ptrs = reinterpret_cast<float* const*>(d_ptrs + 2 * W);
+    mj.ret_roff = d_roff;
+    mj.ret_base = d_sbase;
+    mj.ret_rows = n_recv;
+    mj.ret_world = W;
+    if (n_recv > 0) {
+        if (!run_blockscaled(eng, L, mj, st, nullptr, &launches, err)) return 0;
     }
     mark(5);
 
@@ -865,7 +907,7 @@ int moe_b200_ep_layer_forward(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t
     launches += 1;
     if (T > 0) {
         CK(launch_combine(ep->ret.local.as<float>(), H, ep->pos.as<uint32_t>(), w, T, K,
-                          shared ? ep->yloc.as<float>() + (size_t)n_recv * H : nullptr, y_bf16, y_f32, st, false));
+                          shared ? ep->yshared.as<float>() : nullptr, y_bf16, y_f32, st, false));
         launches += 1;
     }
     mark(6);

@@ -48,15 +48,17 @@ namespace moe_b200 {
 
 // FP4: the fast mode (kind::mxf4): A and B packed E2M1 in shared memory, one
 // B term, 64-byte swizzled rows (one 128-K stage per row).
-template <int MODE, int BN, bool FP4 = false>
+template <int MODE, int BN, bool FP4 = false, bool PAIR = false>
 struct BsCfg {
     static_assert(BN == 32 || BN == 64 || BN == 128, "tile width");
+    static_assert(!PAIR || (BN == 128 && !FP4), "CTA pairs run the exact path's 128-token tiles");
     static constexpr bool kStackN = !FP4 && BN <= 64;
     static constexpr int kNA = MODE == kGateUp ? 2 : 1;       // A operands per stage
     static constexpr int kABytes = FP4 ? 128 * 64 : 128 * 128;  // smem bytes per A box
     static constexpr int kATx = 128 * 128 / 2;                // packed bytes the A box moves
     static constexpr int kBTerms = FP4 ? 1 : 2;               // B terms per stage (hi, lo)
-    static constexpr int kBBytes = FP4 ? BN * 64 : BN * 128;  // smem bytes per B term
+    static constexpr int kBRows = PAIR ? BN / 2 : BN;         // B rows in this CTA's shared memory
+    static constexpr int kBBytes = FP4 ? kBRows * 64 : kBRows * 128;  // smem bytes per B term
     static constexpr int kSFA = kNA * 512;                    // weight scale bytes per stage
     static constexpr int kSFB = (FP4 || kStackN) ? 512 : 1024;  // activation scale bytes per stage
     static constexpr int kSFStage = kSFA + kSFB;
@@ -69,6 +71,7 @@ struct BsCfg {
     static_assert(kStages >= 3, "pipeline too shallow");
     static_assert(256 + kStages * kSFCols <= 512, "TMEM budget");
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
+    static_assert(((PAIR ? 4 : 3) * kStages + 2 * kAccs) * 8 + 4 <= 512, "barrier space");
 };
 
 // Byte offsets of a token row's hi and lo scale words inside a stage's
@@ -757,10 +760,24 @@ __device__ __forceinline__ void gu_store8(const float* g, const float* u, uint32
 // share of the accumulator, then SiLU * up, the hi/lo split and the stores.
 // Stacked tiles drain into registers first, so the release comes before the
 // math and the next tile's MMAs overlap it.
-template <int BN, int W, bool FP4 = false>
+// Hands an accumulator back to the MMA issuer after this thread's last TMEM
+// read (tc_fence_before already done): one arrival per thread on the local
+// barrier, or, in a CTA pair, one per warp on the rank-0 CTA's barrier
+// (acc_empty_cl, a shared::cluster address).
+template <bool PAIR>
+__device__ __forceinline__ void acc_release(uint64_t* acc_empty_bar, uint32_t acc_empty_cl) {
+    if constexpr (PAIR) {
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(acc_empty_cl);
+    } else {
+        mbar_arrive(acc_empty_bar);
+    }
+}
+
+template <int BN, int W, bool FP4 = false, bool PAIR = false>
 __device__ __forceinline__ void gu_tile_part(const BsParams& p, const BsTileX& tc, uint32_t dbase, uint32_t cb,
                                              uint32_t m, uint32_t lane, uint32_t quarter, uint8_t* h_atom,
-                                             uint64_t* acc_empty_bar) {
+                                             uint64_t* acc_empty_bar, uint32_t acc_empty_cl) {
     constexpr bool kStackN = !FP4 && BN <= 64;
     constexpr uint32_t kLoOff = kStackN ? BN : 0;  // stacked: lo half follows hi
     constexpr uint32_t kProjOff = kStackN ? 2 * BN : BN;
@@ -784,7 +801,7 @@ __device__ __forceinline__ void gu_tile_part(const BsParams& p, const BsTileX& t
             }
         }
         tc_fence_before();
-        mbar_arrive(acc_empty_bar);
+        acc_release<PAIR>(acc_empty_bar, acc_empty_cl);
 #pragma unroll
         for (uint32_t j0 = 0; j0 < (uint32_t)W; j0 += 8) {
             const uint32_t c0 = cb + j0;
@@ -809,15 +826,15 @@ __device__ __forceinline__ void gu_tile_part(const BsParams& p, const BsTileX& t
             }
         }
         tc_fence_before();
-        mbar_arrive(acc_empty_bar);
+        acc_release<PAIR>(acc_empty_bar, acc_empty_cl);
     }
 }
 
-template <int MODE, int BN, bool FP4>
+template <int MODE, int BN, bool FP4, bool PAIR>
 __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                          const __grid_constant__ CUtensorMap tmap_b,
                                                          const BsParams p) {
-    using C = BsCfg<MODE, BN, FP4>;
+    using C = BsCfg<MODE, BN, FP4, PAIR>;
     // gate/up with one accumulator: the scale-factor warps drain and store the
     // upper half of each tile's columns (the MMAs wait for the whole
     // accumulator anyway), halving the epilogue's time per tile
@@ -836,18 +853,37 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
     uint64_t* sf_full = load_empty + C::kStages;   // scale factors stored in TMEM
     uint64_t* acc_full = sf_full + C::kStages;
     uint64_t* acc_empty = acc_full + C::kAccs;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + C::kAccs);
+    uint64_t* sf_load = acc_empty + C::kAccs;      // CTA pairs: this CTA's scale blocks landed
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sf_load + (PAIR ? C::kStages : 0));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // CTA pairs walk the tile table per pair (a tile entry's row tile is a
+    // pair of 128-row tiles; rank 1 takes the second) and the rank-0 CTA
+    // issues the M = 256 MMAs.  The MMA waits on the rank-0 CTA's load_full
+    // (both CTAs' operand copies complete there), sf_full (both CTAs' scale-
+    // factor warps) and acc_empty (both CTAs' epilogues); its commits arrive
+    // on load_empty and acc_full in both CTAs.  Each CTA's scale blocks land
+    // on its own sf_load.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0;
+    const uint32_t first = PAIR ? blockIdx.x >> 1 : blockIdx.x;
+    const uint32_t step = PAIR ? gridDim.x >> 1 : gridDim.x;
+    auto tile_at = [&](uint32_t t) {
+        BsTileX tc = load_tile(p, t);
+        if constexpr (PAIR) tc.mt = tc.mt * 2 + rank;
+        return tc;
+    };
+    // token columns of a tile's MMAs (stacked: hi rows [0, BN), lo rows [BN, 2 BN))
+    auto tile_n = [](uint32_t nn) { return C::kStackN ? 2u * BN : max(16u, (nn + 15u) & ~15u); };
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::kStages; ++i) {
-            mbar_init(&load_full[i], 1);
+            mbar_init(&load_full[i], PAIR ? 2 : 1);
             mbar_init(&load_empty[i], 1);
-            mbar_init(&sf_full[i], 4);
+            mbar_init(&sf_full[i], PAIR ? 8 : 4);
+            if (PAIR) mbar_init(&sf_load[i], 1);
         }
         for (int i = 0; i < C::kAccs; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], kGuSplit ? 256 : 128);
+            mbar_init(&acc_empty[i], PAIR ? 2 * (kGuSplit ? 8 : 4) : (kGuSplit ? 256 : 128));
         }
         fence_mbar_init();
     }
@@ -856,11 +892,20 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         prefetch_tmap(&tmap_b);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_holder, 512);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_holder, 512);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_holder, 512);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) {
+        cluster_sync();  // both CTAs' barriers initialised before any remote arrival
+    } else {
+        __syncthreads();
+    }
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     // The tile table and weights were ready before this grid launched (the
@@ -876,54 +921,70 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         if (lane == 0) {
             uint32_t stage = 0, phase = 0;
             bool ok = true;
+            constexpr uint32_t kOpBytes = C::kNA * C::kATx + C::kBTerms * C::kBBytes;
+            // arms stage s for this CTA's copies of one use
+            auto arm = [&](uint32_t s) {
+                if constexpr (PAIR) {
+                    mbar_arrive_expect_tx(&sf_load[s], C::kSFStage);
+                    mbar_arrive_expect_tx_cluster(mapa_cluster(&load_full[s], 0), kOpBytes);
+                } else {
+                    mbar_arrive_expect_tx(&load_full[s], kOpBytes + C::kSFStage);
+                }
+            };
+            auto sf_bar = [&](uint32_t s) { return PAIR ? &sf_load[s] : &load_full[s]; };
+            auto load_a = [&](uint32_t s, uint64_t ablk0, uint32_t kt) {
+#pragma unroll
+                for (int pj = 0; pj < C::kNA; ++pj) {
+                    const uint64_t b = ablk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt;  // weight block
+                    uint8_t* dst = a_base + (s * C::kNA + pj) * C::kABytes;
+                    if constexpr (PAIR) {
+                        tma_load_2d_pair(dst, &tmap_a, 0, (int32_t)(b * 128), mapa_cluster(&load_full[s], 0));
+                    } else {
+                        tma_load_2d(dst, &tmap_a, 0, (int32_t)(b * 128), &load_full[s]);
+                    }
+                }
+            };
             // weights of the first tile's first stages before waiting for the
             // previous kernel: they do not depend on it
             uint32_t pre = 0;
-            if (blockIdx.x < total) {
-                const BsTileX tc = load_tile(p, blockIdx.x);
+            if (first < total) {
+                const BsTileX tc = tile_at(first);
                 const uint32_t slot = p.group_slot ? __ldg(p.group_slot + tc.g) : tc.g;
                 const uint64_t ablk0 = ((uint64_t)slot * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
                 const uint64_t sblk0 = ((uint64_t)slot * p.m_tiles + tc.mt) * p.k_tiles;
                 pre = min((uint32_t)C::kStages, p.k_tiles);
                 for (uint32_t kt = 0; kt < pre; ++kt) {
-                    uint8_t* sf = sf_base + kt * C::kSFStage;
-                    mbar_arrive_expect_tx(&load_full[kt], C::kNA * C::kATx + C::kSFStage + C::kBTerms * C::kBBytes);
-                    bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, &load_full[kt]);
-#pragma unroll
-                    for (int pj = 0; pj < C::kNA; ++pj) {
-                        const uint64_t b = ablk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt;
-                        tma_load_2d(a_base + (kt * C::kNA + pj) * C::kABytes, &tmap_a, 0, (int32_t)(b * 128),
-                                    &load_full[kt]);
-                    }
+                    arm(kt);
+                    bulk_g2s(sf_base + kt * C::kSFStage, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, sf_bar(kt));
+                    load_a(kt, ablk0, kt);
                 }
             }
             pdl_wait();
-            for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-                const BsTileX tc = load_tile(p, tile);
+            for (uint32_t tile = first; ok && tile < total; tile += step) {
+                const BsTileX tc = tile_at(tile);
                 const uint32_t slot = p.group_slot ? __ldg(p.group_slot + tc.g) : tc.g;  // weights of the group
                 const uint64_t ablk0 = ((uint64_t)slot * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
                 const uint64_t sblk0 = ((uint64_t)slot * p.m_tiles + tc.mt) * p.k_tiles;
+                // a pair's rank 1 holds B rows [N/2, N) of the tile
+                const int32_t b_row = (int32_t)(tc.row0 + (PAIR ? rank * (tile_n(tc.nn) / 2) : 0));
                 for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
                     if (!(ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty))) break;
                     uint8_t* sf = sf_base + stage * C::kSFStage;
-                    const bool prefetched = tile == blockIdx.x && kt < pre;
+                    const bool prefetched = tile == first && kt < pre;
                     if (!prefetched) {
-                        mbar_arrive_expect_tx(&load_full[stage], C::kNA * C::kATx + C::kSFStage + C::kBTerms * C::kBBytes);
-                        bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, &load_full[stage]);
+                        arm(stage);
+                        bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, sf_bar(stage));
+                        load_a(stage, ablk0, kt);
                     }
                     bulk_g2s(sf + C::kSFA, p.sfb_atoms + ((uint64_t)tc.ntile * p.k_tiles + kt) * C::kSFB, C::kSFB,
-                             &load_full[stage]);
-#pragma unroll
-                    for (int pj = 0; pj < C::kNA; ++pj) {
-                        if (prefetched) break;
-                        const uint64_t b = ablk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt;  // weight block
-                        tma_load_2d(a_base + (stage * C::kNA + pj) * C::kABytes, &tmap_a, 0, (int32_t)(b * 128),
-                                    &load_full[stage]);
-                    }
+                             sf_bar(stage));
                     if constexpr (FP4) {
                         // the tile's token rows: 64 bytes (128 codes) of each
                         tma_load_2d(b_base + stage * C::kBBytes, &tmap_b, (int32_t)(kt * 64), (int32_t)tc.row0,
                                     &load_full[stage]);
+                    } else if constexpr (PAIR) {
+                        tma_load_3d_pair(b_base + stage * 2 * C::kBBytes, &tmap_b, (int32_t)(kt * 128), b_row, 0,
+                                         mapa_cluster(&load_full[stage], 0));
                     } else {
                         // hi and lo planes of the tile's token rows in one 3-D box
                         tma_load_3d(b_base + stage * 2 * C::kBBytes, &tmap_b, (int32_t)(kt * 128), (int32_t)tc.row0,
@@ -938,13 +999,12 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        if (lane == 0 && rank == 0) {
             uint32_t stage = 0, phase = 0, acc = 0, accphase = 0;
             bool ok = true;
-            for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+            for (uint32_t tile = first; ok && tile < total; tile += step) {
                 const BsTileX tc = load_tile(p, tile);
-                // stacked: hi rows [0, BN) then lo rows [BN, 2 BN); else one term per MMA
-                const uint32_t n_mma = C::kStackN ? 2 * BN : max(16u, (tc.nn + 15u) & ~15u);
+                const uint32_t n_mma = tile_n(tc.nn);
                 if (!(ok = mbar_wait(&acc_empty[acc], accphase ^ 1, p.err, kErrTimeoutAccEmpty))) break;
                 tc_fence_after();
                 const uint32_t d0 = tmem + acc * C::kAccCols;
@@ -973,7 +1033,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                     } else {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint32_t idesc = idesc_bs_m128(n_mma, kk);
+                        const uint32_t idesc = idesc_bs(PAIR ? 256 : 128, n_mma, kk);
                         const uint64_t bhi = smem_desc_sw128(b_addr + kk * 32);
 #pragma unroll
                         for (int pj = 0; pj < C::kNA; ++pj) {
@@ -983,20 +1043,33 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                             } else {
                                 const uint64_t blo = smem_desc_sw128(b_addr + C::kBBytes + kk * 32);
                                 const uint32_t d = d0 + pj * BN;
-                                mma_bs(d, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
-                                mma_bs(d, adesc, blo, idesc, sfc + pj * 4, sfb + 4, 1);
+                                if constexpr (PAIR) {
+                                    mma_bs_pair(d, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
+                                    mma_bs_pair(d, adesc, blo, idesc, sfc + pj * 4, sfb + 4, 1);
+                                } else {
+                                    mma_bs(d, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
+                                    mma_bs(d, adesc, blo, idesc, sfc + pj * 4, sfb + 4, 1);
+                                }
                             }
                         }
                     }
                     }
-                    mma_commit(&load_empty[stage]);
+                    if constexpr (PAIR) {
+                        mma_commit_pair(&load_empty[stage], 0x3);
+                    } else {
+                        mma_commit(&load_empty[stage]);
+                    }
                     if (++stage == C::kStages) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (!ok) break;
-                mma_commit(&acc_full[acc]);
+                if constexpr (PAIR) {
+                    mma_commit_pair(&acc_full[acc], 0x3);
+                } else {
+                    mma_commit(&acc_full[acc]);
+                }
                 if (++acc == C::kAccs) {
                     acc = 0;
                     accphase ^= 1;
@@ -1009,14 +1082,16 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         // of the stage's scale columns: lane l of every quarter holds bytes
         // [16 l, 16 l + 16) of each 512-byte block (the layout the MMA reads).
         // Doing this with tcgen05.st here keeps it off the tensor pipe.  The
-        // slot of stage u is free once stage u's operands have landed: the
-        // producer reloaded it only after the MMAs of stage u - kStages were done.
+        // slot of stage u is free once stage u's scale blocks have landed: the
+        // producer reloaded them only after the MMAs of stage u - kStages were
+        // done.  In a pair each CTA stores its own rows' A scales and all the
+        // tile's B scales.
         const uint32_t lane_addr = ((warp & 3) * 32) << 16;
         uint32_t stage = 0, phase = 0, eaccphase = 0;
         bool ok = true;
-        for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+        for (uint32_t tile = first; ok && tile < total; tile += step) {
             for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
-                ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull);
+                ok = mbar_wait(PAIR ? &sf_load[stage] : &load_full[stage], phase, p.err, kErrTimeoutLoadFull);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
                     break;
@@ -1032,7 +1107,13 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sf_full[stage]);
+                if (lane == 0) {
+                    if constexpr (PAIR) {
+                        mbar_arrive_cluster(mapa_cluster(&sf_full[stage], 0));
+                    } else {
+                        mbar_arrive(&sf_full[stage]);
+                    }
+                }
                 if (++stage == C::kStages) {
                     stage = 0;
                     phase ^= 1;
@@ -1040,7 +1121,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
             }
             if constexpr (kGuSplit) {
                 if (!ok) break;
-                const BsTileX tc = load_tile(p, tile);
+                const BsTileX tc = tile_at(tile);
                 ok = mbar_wait(&acc_full[0], eaccphase, p.err, kErrTimeoutAccFull, true);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
@@ -1049,8 +1130,9 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 tc_fence_after();
                 const uint32_t quarter = warp & 3;
                 uint8_t* h_atom = p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * C::kSFB;
-                gu_tile_part<BN, kGuW, FP4>(p, tc, tmem + lane_addr, BN / 2, tc.mt * 128 + quarter * 32 + lane, lane,
-                                       quarter, h_atom, &acc_empty[0]);
+                gu_tile_part<BN, kGuW, FP4, PAIR>(p, tc, tmem + lane_addr, BN / 2, tc.mt * 128 + quarter * 32 + lane,
+                                                  lane, quarter, h_atom, &acc_empty[0],
+                                                  PAIR ? mapa_cluster(&acc_empty[0], 0) : 0u);
                 eaccphase ^= 1;
             }
         }
@@ -1061,8 +1143,8 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         const uint32_t lane_addr = (quarter * 32) << 16;
         uint32_t acc = 0, accphase = 0;
         bool ok = true;
-        for (uint32_t tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-            const BsTileX tc = load_tile(p, tile);
+        for (uint32_t tile = first; ok && tile < total; tile += step) {
+            const BsTileX tc = tile_at(tile);
             ok = mbar_wait(&acc_full[acc], accphase, p.err, kErrTimeoutAccFull, true);
             if (!__all_sync(0xffffffffu, ok)) {
                 ok = false;
@@ -1072,13 +1154,14 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
             const uint32_t m = tc.mt * 128 + r;
             const uint64_t row0 = tc.row0;
             const uint32_t dbase = tmem + lane_addr + acc * C::kAccCols;
+            const uint32_t acc_empty_cl = PAIR ? mapa_cluster(&acc_empty[acc], 0) : 0u;
             // the down GEMM's scale block for this token tile and 128-K stage (= mt)
             uint8_t* h_atom =
                 MODE == kGateUp ? p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * C::kSFB : nullptr;
             constexpr uint32_t kLoOff = C::kStackN ? BN : 0;        // stacked: lo half follows hi
-            constexpr uint32_t kProjOff = C::kStackN ? 2 * BN : BN;
             if constexpr (MODE == kGateUp) {
-                gu_tile_part<BN, kGuW, FP4>(p, tc, dbase, 0, m, lane, quarter, h_atom, &acc_empty[acc]);
+                gu_tile_part<BN, kGuW, FP4, PAIR>(p, tc, dbase, 0, m, lane, quarter, h_atom, &acc_empty[acc],
+                                                  acc_empty_cl);
                 if (++acc == C::kAccs) {
                     acc = 0;
                     accphase ^= 1;
@@ -1143,7 +1226,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 }
             }
             tc_fence_before();
-            mbar_arrive(&acc_empty[acc]);
+            acc_release<PAIR>(&acc_empty[acc], acc_empty_cl);
             if (++acc == C::kAccs) {
                 acc = 0;
                 accphase ^= 1;
@@ -1153,44 +1236,92 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
     }
 
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) {
+        cluster_sync();  // no MMA, remote arrival or TMEM access of either CTA is left
+    } else {
+        __syncthreads();
+    }
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, 512);
+    if (warp == 1) {
+        if constexpr (PAIR) {
+            tmem_dealloc_pair(tmem, 512);
+        } else {
+            tmem_dealloc(tmem, 512);
+        }
+    }
 }
 
-template <int MODE, int BN, bool FP4>
+// CTA-pair grids: two CTAs per cluster, as many clusters as can be resident
+// at once (the SMs of a GPC pair up by TPC), found once per device and mode.
+template <typename K>
+static int pair_grid(K kernel, int smem, int num_sms, int* cache) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return 0;
+    if (cache[dev] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(num_sms & ~1));
+        cfg.blockDim = dim3(320);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) clusters = 0;
+        cache[dev] = clusters > 0 ? std::min(2 * clusters, num_sms & ~1) : -1;
+    }
+    return cache[dev];
+}
+
+template <int MODE, int BN, bool FP4, bool PAIR>
 static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p, int num_sms,
                                   cudaStream_t st, bool pdl) {
-    using C = BsCfg<MODE, BN, FP4>;
+    using C = BsCfg<MODE, BN, FP4, PAIR>;
     static uint64_t attr_set = 0;  // one bit per device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 64 && !((attr_set >> dev) & 1u)) {
-        e = cudaFuncSetAttribute(gemm_bs_kernel<MODE, BN, FP4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemm_bs_kernel<MODE, BN, FP4, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  C::kSmem);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
     }
-    return launch_kernel(gemm_bs_kernel<MODE, BN, FP4>, dim3(num_sms), dim3(320), C::kSmem, st, pdl, ta, tb, p);
+    if constexpr (PAIR) {
+        static int grid_cache[64] = {};
+        const int grid = pair_grid(gemm_bs_kernel<MODE, BN, FP4, PAIR>, C::kSmem, num_sms, grid_cache);
+        if (grid <= 0) return cudaErrorNotSupported;
+        return launch_kernel_cluster2(gemm_bs_kernel<MODE, BN, FP4, PAIR>, dim3(grid), dim3(320), C::kSmem, st, pdl,
+                                      ta, tb, p);
+    } else {
+        return launch_kernel(gemm_bs_kernel<MODE, BN, FP4, PAIR>, dim3(num_sms), dim3(320), C::kSmem, st, pdl, ta,
+                             tb, p);
+    }
 }
 
 template <int MODE, bool FP4>
-static cudaError_t launch_bs_width(int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
-                                   int num_sms, cudaStream_t st, bool pdl) {
-    if (block_n == 32) return launch_bs_mode<MODE, 32, FP4>(ta, tb, p, num_sms, st, pdl);
-    if (block_n == 64) return launch_bs_mode<MODE, 64, FP4>(ta, tb, p, num_sms, st, pdl);
-    return launch_bs_mode<MODE, 128, FP4>(ta, tb, p, num_sms, st, pdl);
+static cudaError_t launch_bs_width(int block_n, bool pair, const CUtensorMap& ta, const CUtensorMap& tb,
+                                   const BsParams& p, int num_sms, cudaStream_t st, bool pdl) {
+    if (block_n == 32) return launch_bs_mode<MODE, 32, FP4, false>(ta, tb, p, num_sms, st, pdl);
+    if (block_n == 64) return launch_bs_mode<MODE, 64, FP4, false>(ta, tb, p, num_sms, st, pdl);
+    if constexpr (!FP4) {
+        if (pair) return launch_bs_mode<MODE, 128, false, true>(ta, tb, p, num_sms, st, pdl);
+    }
+    return launch_bs_mode<MODE, 128, FP4, false>(ta, tb, p, num_sms, st, pdl);
 }
 
 cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
-                           int num_sms, cudaStream_t st, bool pdl, bool fp4) {
+                           int num_sms, cudaStream_t st, bool pdl, bool fp4, bool pair) {
+    if (pair && (fp4 || block_n != 128)) return cudaErrorInvalidValue;
     if (mode == kGateUp) {
-        return fp4 ? launch_bs_width<kGateUp, true>(block_n, ta, tb, p, num_sms, st, pdl)
-                   : launch_bs_width<kGateUp, false>(block_n, ta, tb, p, num_sms, st, pdl);
+        return fp4 ? launch_bs_width<kGateUp, true>(block_n, false, ta, tb, p, num_sms, st, pdl)
+                   : launch_bs_width<kGateUp, false>(block_n, pair, ta, tb, p, num_sms, st, pdl);
     }
-    return fp4 ? launch_bs_width<kDown, true>(block_n, ta, tb, p, num_sms, st, pdl)
-               : launch_bs_width<kDown, false>(block_n, ta, tb, p, num_sms, st, pdl);
+    return fp4 ? launch_bs_width<kDown, true>(block_n, false, ta, tb, p, num_sms, st, pdl)
+               : launch_bs_width<kDown, false>(block_n, pair, ta, tb, p, num_sms, st, pdl);
 }
 
 }  // namespace moe_b200

@@ -208,8 +208,11 @@ cudaError_t launch_build_tiles(const uint32_t* count, const uint32_t* offset, co
 // a {64, 128} box and `tb` a byte map over [rows][K/2] packed E2M1 codes with
 // a {64, block_n} box, both 64-byte swizzled; h_out is then [rows][I/2]
 // packed codes and the scale blocks are 512 bytes for every tile width.
+// pair (exact path, 128-token tiles): CTA pairs run cta_group::2 MMAs of 256
+// weight rows; the tile table's row tiles are then pairs of 128-row tiles
+// (m_tiles even) and `tb`'s box is {128, 64, 2}, half a tile's token rows.
 cudaError_t launch_gemm_bs(int mode, int block_n, const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p,
-                           int num_sms, cudaStream_t st, bool pdl, bool fp4 = false);
+                           int num_sms, cudaStream_t st, bool pdl, bool fp4 = false, bool pair = false);
 // Fast mode: token rows of x as packed E2M1 codes [rows][Kp/2] with E8M0
 // scale words in 512-byte blocks per (token tile, 128-K stage), stored at
 // each of the token's permuted rows (as launch_scatter_quant_bs).
