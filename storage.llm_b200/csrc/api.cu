@@ -469,6 +469,9 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
     ep_release(eng->ep);
     if (eng->hstream) cudaStreamDestroy(eng->hstream);
     if (eng->ustream) cudaStreamDestroy(eng->ustream);
+    if (eng->pipe_in) cudaStreamDestroy(eng->pipe_in);
+    if (eng->pipe_out) cudaStreamDestroy(eng->pipe_out);
+    for (cudaEvent_t e : eng->pipe_ev) cudaEventDestroy(e);
     if (eng->h_err) cudaFreeHost(eng->h_err);
     delete eng;
 }
@@ -608,11 +611,36 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
 
 namespace {
 
+// Host-buffer calls on large batches overlap the copies with the per-token
+// stages: x arrives in token chunks (pipe_in), the router runs on each chunk
+// as it lands, and the combine runs chunk by chunk with each chunk's rows,
+// ids and weights copied back (pipe_out) while the next is combined.  Every
+// token's result is computed exactly as without the chunks.
+constexpr uint32_t kPipeChunks = 8;
+constexpr uint32_t kPipeMinTokens = 4096;
+
+struct HostPipe {
+    const uint16_t* x;  // host rows of the batch
+    uint16_t* y_bf16;   // host outputs (null: not wanted)
+    float* y_f32;
+    int32_t* ids;
+    float* w;
+};
+
+// Token range of chunk c.
+inline void pipe_range(uint32_t T, uint32_t c, uint32_t* t0, uint32_t* t1) {
+    const uint32_t tc = ceil_div(T, kPipeChunks);
+    *t0 = std::min(T, c * tc);
+    *t1 = std::min(T, *t0 + tc);
+}
+
 // The single-device layer (moe_b200_layer_forward and moe_b200_block_forward):
 // `hidden` is the residual stream the block parts may read (may be null).
+// `pipe`: the call's host buffers (moe_b200_layer_forward_host), x then being
+// the device buffer the chunks are copied into.
 int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const uint16_t* x, const float* hidden,
                  uint32_t T, uint16_t* y_bf16, float* y_f32, int32_t* topk_ids, float* topk_w, uint32_t* perm,
-                 void* stream, char* err) {
+                 void* stream, char* err, const HostPipe* pipe = nullptr) {
     if (!check_dims(cfg, err)) return 0;
     LayerWeights* L = get_layer(eng, cfg->layer, err);
     if (!L) return 0;
@@ -760,6 +788,23 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
         }
         CK(launch_router_f32(rin, L->router.as<uint16_t>(), T, E, H, K, rcfg, eng->logits.as<float>(), ids, w,
                              eng->scores.as<float>(), st, &launches));
+    } else if (pipe) {
+        for (uint32_t c = 0; c < kPipeChunks; ++c) {
+            uint32_t t0, t1;
+            pipe_range(T, c, &t0, &t1);
+            if (t0 == t1) continue;
+            uint16_t* xc = const_cast<uint16_t*>(x) + (size_t)t0 * H;
+            CK(cudaMemcpyAsync(xc, pipe->x + (size_t)t0 * H, (size_t)(t1 - t0) * H * 2, cudaMemcpyHostToDevice,
+                               eng->pipe_in));
+            CK(cudaEventRecord(eng->pipe_ev[c], eng->pipe_in));
+            CK(cudaStreamWaitEvent(st, eng->pipe_ev[c], 0));
+            CUtensorMap rtx, rtw;
+            const bool rt_tma = router_tmaps(eng, xc, L->router.as<uint16_t>(), t1 - t0, E, H, &rtx, &rtw);
+            CK(launch_router(xc, L->router.as<uint16_t>(), t1 - t0, E, H, K, rcfg,
+                             eng->logits.as<float>() + (size_t)t0 * E, ids + (size_t)t0 * K, w + (size_t)t0 * K,
+                             eng->scores.as<float>() + (size_t)t0 * E, errw, st, &launches, rt_tma ? &rtx : nullptr,
+                             rt_tma ? &rtw : nullptr));
+        }
     } else {
         CUtensorMap rtx, rtw;
         const bool rt_tma = router_tmaps(eng, x, L->router.as<uint16_t>(), T, E, H, &rtx, &rtw);
@@ -852,17 +897,55 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
     mark(5);
     }
 
-    if (L->has_block_combine()) {
-        BlockParts parts{L->blk_post_norm1.as<float>(), L->blk_post_norm2.as<float>(), L->blk_post_norm.as<float>(),
-                         L->blk_down_scale.as<float>(), L->blk_down_scale_count, cfg->norm_eps, cfg->norm_unit_offset};
-        CK(launch_block_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), ids, w, T, K, E,
-                                shared ? eng->yperm.as<float>() + (size_t)n * H : nullptr,
-                                gated ? eng->gate_w.as<float>() : nullptr, parts, y_bf16, y_f32, st, bs));
-    } else {
-        CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>(), w, T, K,
-                          shared ? eng->yperm.as<float>() + (size_t)n * H : nullptr, y_bf16, y_f32, st, bs));
+    // tokens [t0, t1): the combine, then (host-buffer calls) their copy back
+    auto combine = [&](uint32_t t0, uint32_t t1) -> int {
+        const float* ys = shared ? eng->yperm.as<float>() + (size_t)(n + t0) * H : nullptr;
+        uint16_t* yb = y_bf16 ? y_bf16 + (size_t)t0 * H : nullptr;
+        float* yf = y_f32 ? y_f32 + (size_t)t0 * H : nullptr;
+        if (L->has_block_combine()) {
+            BlockParts parts{L->blk_post_norm1.as<float>(), L->blk_post_norm2.as<float>(),
+                             L->blk_post_norm.as<float>(), L->blk_down_scale.as<float>(), L->blk_down_scale_count,
+                             cfg->norm_eps, cfg->norm_unit_offset};
+            CK(launch_block_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>() + (size_t)t0 * K,
+                                    ids + (size_t)t0 * K, w + (size_t)t0 * K, t1 - t0, K, E, ys,
+                                    gated ? eng->gate_w.as<float>() + t0 : nullptr, parts, yb, yf, st, bs));
+        } else {
+            CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>() + (size_t)t0 * K,
+                              w + (size_t)t0 * K, t1 - t0, K, ys, yb, yf, st, bs));
+        }
+        launches += 1;
+        return 1;
+    };
+    if (pipe) {
+        for (uint32_t c = 0; c < kPipeChunks; ++c) {
+            uint32_t t0, t1;
+            pipe_range(T, c, &t0, &t1);
+            if (t0 == t1) continue;
+            if (!combine(t0, t1)) return 0;
+            cudaEvent_t e = eng->pipe_ev[kPipeChunks + c];
+            CK(cudaEventRecord(e, st));
+            CK(cudaStreamWaitEvent(eng->pipe_out, e, 0));
+            const size_t rows = t1 - t0;
+            if (pipe->y_bf16) {
+                CK(cudaMemcpyAsync(pipe->y_bf16 + (size_t)t0 * H, y_bf16 + (size_t)t0 * H, rows * H * 2,
+                                   cudaMemcpyDeviceToHost, eng->pipe_out));
+            }
+            if (pipe->y_f32) {
+                CK(cudaMemcpyAsync(pipe->y_f32 + (size_t)t0 * H, y_f32 + (size_t)t0 * H, rows * H * 4,
+                                   cudaMemcpyDeviceToHost, eng->pipe_out));
+            }
+            if (pipe->ids) {
+                CK(cudaMemcpyAsync(pipe->ids + (size_t)t0 * K, ids + (size_t)t0 * K, rows * K * 4,
+                                   cudaMemcpyDeviceToHost, eng->pipe_out));
+            }
+            if (pipe->w) {
+                CK(cudaMemcpyAsync(pipe->w + (size_t)t0 * K, w + (size_t)t0 * K, rows * K * 4,
+                                   cudaMemcpyDeviceToHost, eng->pipe_out));
+            }
+        }
+    } else if (!combine(0, T)) {
+        return 0;
     }
-    launches += 1;
     mark(6);
     if (perm) {
         CK(cudaMemcpyAsync(perm, eng->row_assign.ptr, (size_t)n * 4, cudaMemcpyDeviceToDevice, st));
@@ -1015,6 +1098,32 @@ int moe_b200_layer_forward_host(moe_b200_engine_t* eng, const moe_b200_layer_cfg
     CK(eng->hw.reserve((size_t)T * K * 4));
     CK(eng->hperm_out.reserve((size_t)T * K * 4));
     cudaStream_t st = eng->hstream;
+    // large batches without the permutation output: chunked copies (the
+    // plain router path only; the f32 router of the block parts reads the
+    // residual stream, which this call does not take)
+    const LayerWeights* Lp = (cfg->layer >= 0 && (size_t)cfg->layer < eng->layers.size()) ? &eng->layers[cfg->layer]
+                                                                                            : nullptr;
+    const bool chunked = T >= kPipeMinTokens && !perm && Lp && !Lp->blk_pre_norm2.ptr && !Lp->blk_router_scale.ptr;
+    if (chunked) {
+        if (!eng->pipe_in) {
+            CK(cudaStreamCreateWithFlags(&eng->pipe_in, cudaStreamNonBlocking));
+            CK(cudaStreamCreateWithFlags(&eng->pipe_out, cudaStreamNonBlocking));
+        }
+        while (eng->pipe_ev.size() < 2 * kPipeChunks) {
+            cudaEvent_t e;
+            CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            eng->pipe_ev.push_back(e);
+        }
+        const HostPipe pipe{x, y_bf16, y_f32, topk_ids, topk_w};
+        if (!forward_impl(eng, cfg, eng->hx.as<uint16_t>(), nullptr, T, y_bf16 ? eng->hy.as<uint16_t>() : nullptr,
+                          y_f32 ? eng->hyf.as<float>() : nullptr, eng->hids.as<int32_t>(), eng->hw.as<float>(),
+                          nullptr, st, err, &pipe)) {
+            return 0;
+        }
+        if (!moe_b200_sync(eng, st, err)) return 0;
+        CK(cudaStreamSynchronize(eng->pipe_out));
+        return 1;
+    }
     CK(cudaMemcpyAsync(eng->hx.ptr, x, (size_t)T * H * 2, cudaMemcpyHostToDevice, st));
     if (!moe_b200_layer_forward(eng, cfg, eng->hx.as<uint16_t>(), T, y_bf16 ? eng->hy.as<uint16_t>() : nullptr,
                                 y_f32 ? eng->hyf.as<float>() : nullptr, eng->hids.as<int32_t>(),

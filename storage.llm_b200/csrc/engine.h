@@ -158,6 +158,11 @@ struct moe_b200_engine {
     // host-buffer entry points: their own non-blocking stream, and a pinned
     // word the error code is copied into before the one synchronisation
     cudaStream_t hstream = nullptr;
+    // host-buffer calls on large batches: token chunks of x are copied in on
+    // pipe_in and routed as they land; the combined rows go back on pipe_out
+    // chunk by chunk (events: kPipeChunks copy-ins, then kPipeChunks combines)
+    cudaStream_t pipe_in = nullptr, pipe_out = nullptr;
+    std::vector<cudaEvent_t> pipe_ev;
     uint32_t* h_err = nullptr;
     CUtensorMap tmap_x{}, tmap_h{};
     void* tmap_x_base = nullptr;

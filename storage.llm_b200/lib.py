@@ -247,14 +247,16 @@ class Engine:
                                                     _ptr(y_f32), _ptr(ids), _ptr(w), _ptr(perm), stream,
                                                     self.err))
 
-    def forward_host(self, cfg: LayerCfg, x: np.ndarray, want_f32: bool = True):
+    def forward_host(self, cfg: LayerCfg, x: np.ndarray, want_f32: bool = True, want_perm: bool = True):
+        """want_perm=False leaves the permutation out, which lets large
+        batches overlap their copies with the router and the combine."""
         T = x.shape[0]
         H, K = cfg.hidden, cfg.top_k
         y = np.zeros((T, H), np.uint16)
         yf = np.zeros((T, H), np.float32) if want_f32 else None
         ids = np.zeros((T, K), np.int32)
         w = np.zeros((T, K), np.float32)
-        perm = np.zeros(T * K, np.uint32)
+        perm = np.zeros(T * K, np.uint32) if want_perm else None
         x = np.ascontiguousarray(x, dtype=np.uint16)
         self._check(self.lib.moe_b200_layer_forward_host(self.h, C.byref(cfg), _ptr(x), T, _ptr(y), _ptr(yf),
                                                          _ptr(ids), _ptr(w), _ptr(perm), self.err))
