@@ -1008,11 +1008,25 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 if (!(ok = mbar_wait(&acc_empty[acc], accphase ^ 1, p.err, kErrTimeoutAccEmpty))) break;
                 tc_fence_after();
                 const uint32_t d0 = tmem + acc * C::kAccCols;
+                // The next stage's barriers are tested (without blocking) while
+                // this stage's MMAs still fill the tensor pipe's queue; when both
+                // have completed, the stage boundary needs no wait.
+                bool next_ready = false;
                 for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
                     // operands landed (observed here too, so this thread's MMAs
                     // are ordered after the copies) and the scale factors are in TMEM
-                    if (!(ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull))) break;
-                    if (!(ok = mbar_wait(&sf_full[stage], phase, p.err, kErrTimeoutAFull))) break;
+                    if (!next_ready) {
+                        if (!(ok = mbar_wait(&load_full[stage], phase, p.err, kErrTimeoutLoadFull))) break;
+                        if (!(ok = mbar_wait(&sf_full[stage], phase, p.err, kErrTimeoutAFull))) break;
+                    }
+                    next_ready = false;
+                    const bool look = kt + 1 < p.k_tiles;
+                    const uint32_t nstage = stage + 1 == (uint32_t)C::kStages ? 0u : stage + 1;
+                    const uint32_t nphase = stage + 1 == (uint32_t)C::kStages ? phase ^ 1 : phase;
+                    auto look_ahead = [&]() {
+                        next_ready = look && mbar_test_wait(&load_full[nstage], nphase) &&
+                                     mbar_test_wait(&sf_full[nstage], nphase);
+                    };
                     tc_fence_after();
                     const uint32_t sfc = tmem + kSfCol0 + stage * C::kSFCols;
                     const uint32_t sfb = sfc + C::kNA * 4;
@@ -1029,6 +1043,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                                 const uint64_t adesc = smem_desc_sw64(a_addr + pj * C::kABytes + kk * 32);
                                 mma_fp4(d0 + pj * BN, adesc, bdesc, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
                             }
+                            if (kk == 0) look_ahead();
                         }
                     } else {
 #pragma unroll
@@ -1052,6 +1067,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                                 }
                             }
                         }
+                        if (kk == 2) look_ahead();
                     }
                     }
                     if constexpr (PAIR) {
