@@ -48,10 +48,13 @@ namespace moe_b200 {
 
 // FP4: the fast mode (kind::mxf4): A and B packed E2M1 in shared memory, one
 // B term, 64-byte swizzled rows (one 128-K stage per row).
-template <int MODE, int BN, bool FP4 = false, bool PAIR = false>
+// KB: 128-K blocks per pipeline stage (2 on CTA pairs, whose smaller B
+// halves leave room for stages twice as deep in K: half the stage hand-offs).
+template <int MODE, int BN, bool FP4 = false, bool PAIR = false, int KB = 1>
 struct BsCfg {
     static_assert(BN == 32 || BN == 64 || BN == 128, "tile width");
     static_assert(!PAIR || (BN == 128 && !FP4), "CTA pairs run the exact path's 128-token tiles");
+    static_assert(KB == 1 || (KB == 2 && PAIR), "two K blocks per stage on CTA pairs");
     static constexpr bool kStackN = !FP4 && BN <= 64;
     static constexpr int kNA = MODE == kGateUp ? 2 : 1;       // A operands per stage
     static constexpr int kABytes = FP4 ? 128 * 64 : 128 * 128;  // smem bytes per A box
@@ -59,16 +62,18 @@ struct BsCfg {
     static constexpr int kBTerms = FP4 ? 1 : 2;               // B terms per stage (hi, lo)
     static constexpr int kBRows = PAIR ? BN / 2 : BN;         // B rows in this CTA's shared memory
     static constexpr int kBBytes = FP4 ? kBRows * 64 : kBRows * 128;  // smem bytes per B term
-    static constexpr int kSFA = kNA * 512;                    // weight scale bytes per stage
-    static constexpr int kSFB = (FP4 || kStackN) ? 512 : 1024;  // activation scale bytes per stage
-    static constexpr int kSFStage = kSFA + kSFB;
-    static constexpr int kStageBytes = kNA * kABytes + kBTerms * kBBytes + kSFStage;
+    static constexpr int kSFA = kNA * 512;                    // weight scale bytes per K block
+    static constexpr int kSFB = (FP4 || kStackN) ? 512 : 1024;  // activation scale bytes per K block
+    static constexpr int kSFBlock = kSFA + kSFB;
+    static constexpr int kSFStage = KB * kSFBlock;
+    static constexpr int kStageBytes = KB * (kNA * kABytes + kBTerms * kBBytes) + kSFStage;
     static constexpr int kStages = (210 * 1024) / kStageBytes;
     static constexpr int kAccCols = kNA * (kStackN ? 2 * BN : BN);
     static constexpr int kAccs = 256 / kAccCols >= 2 ? 2 : 1;
     static constexpr int kSFCols = kSFStage / 128;            // TMEM columns of scale factors per stage
+    static constexpr int kSFBlockCols = kSFBlock / 128;       // ... per K block
     static constexpr int kSmem = kStages * kStageBytes + 2048 /*two 1024 alignments*/ + 512 /*barriers*/;
-    static_assert(kStages >= 3, "pipeline too shallow");
+    static_assert(kStages >= (KB == 2 ? 2 : 3), "pipeline too shallow");
     static_assert(256 + kStages * kSFCols <= 512, "TMEM budget");
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
     static_assert(((PAIR ? 4 : 3) * kStages + 2 * kAccs) * 8 + 4 <= 512, "barrier space");
@@ -830,11 +835,11 @@ __device__ __forceinline__ void gu_tile_part(const BsParams& p, const BsTileX& t
     }
 }
 
-template <int MODE, int BN, bool FP4, bool PAIR>
+template <int MODE, int BN, bool FP4, bool PAIR, int KB>
 __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                          const __grid_constant__ CUtensorMap tmap_b,
                                                          const BsParams p) {
-    using C = BsCfg<MODE, BN, FP4, PAIR>;
+    using C = BsCfg<MODE, BN, FP4, PAIR, KB>;
     // gate/up with one accumulator: the scale-factor warps drain and store the
     // upper half of each tile's columns (the MMAs wait for the whole
     // accumulator anyway), halving the epilogue's time per tile
@@ -843,11 +848,11 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     // scale blocks first (small), then the 1024-aligned operand tiles
-    uint8_t* sf_base = smem;                                                  // [stages][kSFStage]
-    uint8_t* a_base = smem + C::kStages * C::kSFStage;                        // [stages][kNA][16 KB]
+    uint8_t* sf_base = smem;                                         // [stages][KB][kSFBlock]
+    uint8_t* a_base = smem + C::kStages * C::kSFStage;               // [stages][KB][kNA][16 KB]
     a_base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(a_base) + 1023) & ~uintptr_t(1023));
-    uint8_t* b_base = a_base + C::kStages * C::kNA * C::kABytes;              // [stages][terms][kBBytes]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + C::kStages * C::kBTerms * C::kBBytes);
+    uint8_t* b_base = a_base + C::kStages * KB * C::kNA * C::kABytes;  // [stages][KB][terms][kBBytes]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + C::kStages * KB * C::kBTerms * C::kBBytes);
     uint64_t* load_full = bars;
     uint64_t* load_empty = load_full + C::kStages;
     uint64_t* sf_full = load_empty + C::kStages;   // scale factors stored in TMEM
@@ -921,7 +926,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         if (lane == 0) {
             uint32_t stage = 0, phase = 0;
             bool ok = true;
-            constexpr uint32_t kOpBytes = C::kNA * C::kATx + C::kBTerms * C::kBBytes;
+            constexpr uint32_t kOpBytes = KB * (C::kNA * C::kATx + C::kBTerms * C::kBBytes);
             // arms stage s for this CTA's copies of one use
             auto arm = [&](uint32_t s) {
                 if constexpr (PAIR) {
@@ -932,15 +937,21 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 }
             };
             auto sf_bar = [&](uint32_t s) { return PAIR ? &sf_load[s] : &load_full[s]; };
-            auto load_a = [&](uint32_t s, uint64_t ablk0, uint32_t kt) {
+            // the weight blocks and weight scales of the stage's K blocks kt..
+            auto load_a = [&](uint32_t s, uint64_t ablk0, uint64_t sblk0, uint32_t kt) {
 #pragma unroll
-                for (int pj = 0; pj < C::kNA; ++pj) {
-                    const uint64_t b = ablk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt;  // weight block
-                    uint8_t* dst = a_base + (s * C::kNA + pj) * C::kABytes;
-                    if constexpr (PAIR) {
-                        tma_load_2d_pair(dst, &tmap_a, 0, (int32_t)(b * 128), mapa_cluster(&load_full[s], 0));
-                    } else {
-                        tma_load_2d(dst, &tmap_a, 0, (int32_t)(b * 128), &load_full[s]);
+                for (int kb = 0; kb < KB; ++kb) {
+                    bulk_g2s(sf_base + s * C::kSFStage + kb * C::kSFBlock, p.sfa + (sblk0 + kt + kb) * C::kSFA,
+                             C::kSFA, sf_bar(s));
+#pragma unroll
+                    for (int pj = 0; pj < C::kNA; ++pj) {
+                        const uint64_t b = ablk0 + (uint64_t)pj * p.m_tiles * p.k_tiles + kt + kb;  // weight block
+                        uint8_t* dst = a_base + ((s * KB + kb) * C::kNA + pj) * C::kABytes;
+                        if constexpr (PAIR) {
+                            tma_load_2d_pair(dst, &tmap_a, 0, (int32_t)(b * 128), mapa_cluster(&load_full[s], 0));
+                        } else {
+                            tma_load_2d(dst, &tmap_a, 0, (int32_t)(b * 128), &load_full[s]);
+                        }
                     }
                 }
             };
@@ -952,11 +963,10 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 const uint32_t slot = p.group_slot ? __ldg(p.group_slot + tc.g) : tc.g;
                 const uint64_t ablk0 = ((uint64_t)slot * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
                 const uint64_t sblk0 = ((uint64_t)slot * p.m_tiles + tc.mt) * p.k_tiles;
-                pre = min((uint32_t)C::kStages, p.k_tiles);
-                for (uint32_t kt = 0; kt < pre; ++kt) {
-                    arm(kt);
-                    bulk_g2s(sf_base + kt * C::kSFStage, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, sf_bar(kt));
-                    load_a(kt, ablk0, kt);
+                pre = min((uint32_t)C::kStages, p.k_tiles / KB);
+                for (uint32_t s = 0; s < pre; ++s) {
+                    arm(s);
+                    load_a(s, ablk0, sblk0, s * KB);
                 }
             }
             pdl_wait();
@@ -967,28 +977,31 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 const uint64_t sblk0 = ((uint64_t)slot * p.m_tiles + tc.mt) * p.k_tiles;
                 // a pair's rank 1 holds B rows [N/2, N) of the tile
                 const int32_t b_row = (int32_t)(tc.row0 + (PAIR ? rank * (tile_n(tc.nn) / 2) : 0));
-                for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
+                for (uint32_t kt = 0; kt < p.k_tiles; kt += KB) {
                     if (!(ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty))) break;
                     uint8_t* sf = sf_base + stage * C::kSFStage;
-                    const bool prefetched = tile == first && kt < pre;
+                    const bool prefetched = tile == first && kt / KB < pre;
                     if (!prefetched) {
                         arm(stage);
-                        bulk_g2s(sf, p.sfa + (sblk0 + kt) * C::kSFA, C::kSFA, sf_bar(stage));
-                        load_a(stage, ablk0, kt);
+                        load_a(stage, ablk0, sblk0, kt);
                     }
-                    bulk_g2s(sf + C::kSFA, p.sfb_atoms + ((uint64_t)tc.ntile * p.k_tiles + kt) * C::kSFB, C::kSFB,
-                             sf_bar(stage));
-                    if constexpr (FP4) {
-                        // the tile's token rows: 64 bytes (128 codes) of each
-                        tma_load_2d(b_base + stage * C::kBBytes, &tmap_b, (int32_t)(kt * 64), (int32_t)tc.row0,
-                                    &load_full[stage]);
-                    } else if constexpr (PAIR) {
-                        tma_load_3d_pair(b_base + stage * 2 * C::kBBytes, &tmap_b, (int32_t)(kt * 128), b_row, 0,
-                                         mapa_cluster(&load_full[stage], 0));
-                    } else {
-                        // hi and lo planes of the tile's token rows in one 3-D box
-                        tma_load_3d(b_base + stage * 2 * C::kBBytes, &tmap_b, (int32_t)(kt * 128), (int32_t)tc.row0,
-                                    0, &load_full[stage]);
+#pragma unroll
+                    for (int kb = 0; kb < KB; ++kb) {
+                        bulk_g2s(sf + kb * C::kSFBlock + C::kSFA,
+                                 p.sfb_atoms + ((uint64_t)tc.ntile * p.k_tiles + kt + kb) * C::kSFB, C::kSFB,
+                                 sf_bar(stage));
+                        uint8_t* bdst = b_base + (stage * KB + kb) * C::kBTerms * C::kBBytes;
+                        if constexpr (FP4) {
+                            // the tile's token rows: 64 bytes (128 codes) of each
+                            tma_load_2d(bdst, &tmap_b, (int32_t)((kt + kb) * 64), (int32_t)tc.row0, &load_full[stage]);
+                        } else if constexpr (PAIR) {
+                            tma_load_3d_pair(bdst, &tmap_b, (int32_t)((kt + kb) * 128), b_row, 0,
+                                             mapa_cluster(&load_full[stage], 0));
+                        } else {
+                            // hi and lo planes of the tile's token rows in one 3-D box
+                            tma_load_3d(bdst, &tmap_b, (int32_t)((kt + kb) * 128), (int32_t)tc.row0, 0,
+                                        &load_full[stage]);
+                        }
                     }
                     if (++stage == C::kStages) {
                         stage = 0;
@@ -1012,7 +1025,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 // this stage's MMAs still fill the tensor pipe's queue; when both
                 // have completed, the stage boundary needs no wait.
                 bool next_ready = false;
-                for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
+                for (uint32_t kt = 0; kt < p.k_tiles; kt += KB) {
                     // operands landed (observed here too, so this thread's MMAs
                     // are ordered after the copies) and the scale factors are in TMEM
                     if (!next_ready) {
@@ -1020,7 +1033,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                         if (!(ok = mbar_wait(&sf_full[stage], phase, p.err, kErrTimeoutAFull))) break;
                     }
                     next_ready = false;
-                    const bool look = kt + 1 < p.k_tiles;
+                    const bool look = kt + KB < p.k_tiles;
                     const uint32_t nstage = stage + 1 == (uint32_t)C::kStages ? 0u : stage + 1;
                     const uint32_t nphase = stage + 1 == (uint32_t)C::kStages ? phase ^ 1 : phase;
                     auto look_ahead = [&]() {
@@ -1028,10 +1041,13 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                                      mbar_test_wait(&sf_full[nstage], nphase);
                     };
                     tc_fence_after();
-                    const uint32_t sfc = tmem + kSfCol0 + stage * C::kSFCols;
+#pragma unroll
+                    for (int kb = 0; kb < KB; ++kb) {
+                    const uint32_t sfc = tmem + kSfCol0 + stage * C::kSFCols + kb * C::kSFBlockCols;
                     const uint32_t sfb = sfc + C::kNA * 4;
-                    const uint32_t a_addr = smem_u32(a_base + stage * C::kNA * C::kABytes);
-                    const uint32_t b_addr = smem_u32(b_base + stage * C::kBTerms * C::kBBytes);
+                    const uint32_t a_addr = smem_u32(a_base + (stage * KB + kb) * C::kNA * C::kABytes);
+                    const uint32_t b_addr = smem_u32(b_base + (stage * KB + kb) * C::kBTerms * C::kBBytes);
+                    const uint32_t kacc = kt + kb;  // 0 only for the tile's first K block
                     if constexpr (FP4) {
                         // two K = 64 MMAs per 128-K stage, scale bytes {0, 1} then {2, 3}
 #pragma unroll
@@ -1041,9 +1057,9 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
 #pragma unroll
                             for (int pj = 0; pj < C::kNA; ++pj) {
                                 const uint64_t adesc = smem_desc_sw64(a_addr + pj * C::kABytes + kk * 32);
-                                mma_fp4(d0 + pj * BN, adesc, bdesc, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
+                                mma_fp4(d0 + pj * BN, adesc, bdesc, idesc, sfc + pj * 4, sfb, (kacc | kk) != 0);
                             }
-                            if (kk == 0) look_ahead();
+                            if (kb == KB - 1 && kk == 0) look_ahead();
                         }
                     } else {
 #pragma unroll
@@ -1054,20 +1070,21 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                         for (int pj = 0; pj < C::kNA; ++pj) {
                             const uint64_t adesc = smem_desc_sw128(a_addr + pj * C::kABytes + kk * 32);
                             if (C::kStackN) {
-                                mma_bs(d0 + pj * 2 * BN, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
+                                mma_bs(d0 + pj * 2 * BN, adesc, bhi, idesc, sfc + pj * 4, sfb, (kacc | kk) != 0);
                             } else {
                                 const uint64_t blo = smem_desc_sw128(b_addr + C::kBBytes + kk * 32);
                                 const uint32_t d = d0 + pj * BN;
                                 if constexpr (PAIR) {
-                                    mma_bs_pair(d, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
+                                    mma_bs_pair(d, adesc, bhi, idesc, sfc + pj * 4, sfb, (kacc | kk) != 0);
                                     mma_bs_pair(d, adesc, blo, idesc, sfc + pj * 4, sfb + 4, 1);
                                 } else {
-                                    mma_bs(d, adesc, bhi, idesc, sfc + pj * 4, sfb, (kt | kk) != 0);
+                                    mma_bs(d, adesc, bhi, idesc, sfc + pj * 4, sfb, (kacc | kk) != 0);
                                     mma_bs(d, adesc, blo, idesc, sfc + pj * 4, sfb + 4, 1);
                                 }
                             }
                         }
-                        if (kk == 2) look_ahead();
+                        if (kb == KB - 1 && kk == 2) look_ahead();
+                    }
                     }
                     }
                     if constexpr (PAIR) {
@@ -1106,7 +1123,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         uint32_t stage = 0, phase = 0, eaccphase = 0;
         bool ok = true;
         for (uint32_t tile = first; ok && tile < total; tile += step) {
-            for (uint32_t kt = 0; kt < p.k_tiles; ++kt) {
+            for (uint32_t kt = 0; kt < p.k_tiles; kt += KB) {
                 ok = mbar_wait(PAIR ? &sf_load[stage] : &load_full[stage], phase, p.err, kErrTimeoutLoadFull);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
@@ -1292,28 +1309,28 @@ static int pair_grid(K kernel, int smem, int num_sms, int* cache) {
     return cache[dev];
 }
 
-template <int MODE, int BN, bool FP4, bool PAIR>
+template <int MODE, int BN, bool FP4, bool PAIR, int KB = 1>
 static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, const BsParams& p, int num_sms,
                                   cudaStream_t st, bool pdl) {
-    using C = BsCfg<MODE, BN, FP4, PAIR>;
+    using C = BsCfg<MODE, BN, FP4, PAIR, KB>;
     static uint64_t attr_set = 0;  // one bit per device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 64 && !((attr_set >> dev) & 1u)) {
-        e = cudaFuncSetAttribute(gemm_bs_kernel<MODE, BN, FP4, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  C::kSmem);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
     }
     if constexpr (PAIR) {
         static int grid_cache[64] = {};
-        const int grid = pair_grid(gemm_bs_kernel<MODE, BN, FP4, PAIR>, C::kSmem, num_sms, grid_cache);
+        const int grid = pair_grid(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, C::kSmem, num_sms, grid_cache);
         if (grid <= 0) return cudaErrorNotSupported;
-        return launch_kernel_cluster2(gemm_bs_kernel<MODE, BN, FP4, PAIR>, dim3(grid), dim3(320), C::kSmem, st, pdl,
+        return launch_kernel_cluster2(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(grid), dim3(320), C::kSmem, st, pdl,
                                       ta, tb, p);
     } else {
-        return launch_kernel(gemm_bs_kernel<MODE, BN, FP4, PAIR>, dim3(num_sms), dim3(320), C::kSmem, st, pdl, ta,
+        return launch_kernel(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(num_sms), dim3(320), C::kSmem, st, pdl, ta,
                              tb, p);
     }
 }
@@ -1324,7 +1341,11 @@ static cudaError_t launch_bs_width(int block_n, bool pair, const CUtensorMap& ta
     if (block_n == 32) return launch_bs_mode<MODE, 32, FP4, false>(ta, tb, p, num_sms, st, pdl);
     if (block_n == 64) return launch_bs_mode<MODE, 64, FP4, false>(ta, tb, p, num_sms, st, pdl);
     if constexpr (!FP4) {
-        if (pair) return launch_bs_mode<MODE, 128, false, true>(ta, tb, p, num_sms, st, pdl);
+        if (pair) {
+            // two 128-K blocks per stage when the K blocks pair up
+            return p.k_tiles % 2 == 0 ? launch_bs_mode<MODE, 128, false, true, 2>(ta, tb, p, num_sms, st, pdl)
+                                      : launch_bs_mode<MODE, 128, false, true, 1>(ta, tb, p, num_sms, st, pdl);
+        }
     }
     return launch_bs_mode<MODE, 128, FP4, false>(ta, tb, p, num_sms, st, pdl);
 }
