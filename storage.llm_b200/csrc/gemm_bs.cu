@@ -49,12 +49,15 @@ namespace moe_b200 {
 // FP4: the fast mode (kind::mxf4): A and B packed E2M1 in shared memory, one
 // B term, 64-byte swizzled rows (one 128-K stage per row).
 // KB: 128-K blocks per pipeline stage (2 on CTA pairs, whose smaller B
-// halves leave room for stages twice as deep in K: half the stage hand-offs).
+// halves leave room for stages twice as deep in K, and in the fast mode,
+// whose packed operands make a 128-K stage only four MMAs: fewer stage
+// hand-offs per MMA).
 template <int MODE, int BN, bool FP4 = false, bool PAIR = false, int KB = 1>
 struct BsCfg {
     static_assert(BN == 32 || BN == 64 || BN == 128, "tile width");
     static_assert(!PAIR || (BN == 128 && !FP4), "CTA pairs run the exact path's 128-token tiles");
-    static_assert(KB == 1 || (KB == 2 && PAIR), "two K blocks per stage on CTA pairs");
+    static_assert(KB == 1 || (KB == 2 && PAIR) || ((KB == 2 || KB == 4) && FP4),
+                  "several K blocks per stage: CTA pairs and the fast mode's small stages");
     static constexpr bool kStackN = !FP4 && BN <= 64;
     static constexpr int kNA = MODE == kGateUp ? 2 : 1;       // A operands per stage
     static constexpr int kABytes = FP4 ? 128 * 64 : 128 * 128;  // smem bytes per A box
@@ -73,7 +76,7 @@ struct BsCfg {
     static constexpr int kSFCols = kSFStage / 128;            // TMEM columns of scale factors per stage
     static constexpr int kSFBlockCols = kSFBlock / 128;       // ... per K block
     static constexpr int kSmem = kStages * kStageBytes + 2048 /*two 1024 alignments*/ + 512 /*barriers*/;
-    static_assert(kStages >= (KB == 2 ? 2 : 3), "pipeline too shallow");
+    static_assert(kStages >= (KB >= 2 ? 2 : 3), "pipeline too shallow");
     static_assert(256 + kStages * kSFCols <= 512, "TMEM budget");
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
     static_assert(((PAIR ? 4 : 3) * kStages + 2 * kAccs) * 8 + 4 <= 512, "barrier space");
@@ -1340,6 +1343,14 @@ static cudaError_t launch_bs_width(int block_n, bool pair, const CUtensorMap& ta
                                    const BsParams& p, int num_sms, cudaStream_t st, bool pdl) {
     if (block_n == 32) return launch_bs_mode<MODE, 32, FP4, false>(ta, tb, p, num_sms, st, pdl);
     if (block_n == 64) return launch_bs_mode<MODE, 64, FP4, false>(ta, tb, p, num_sms, st, pdl);
+    if constexpr (FP4) {
+        // the fast mode's 128-token tiles: 2 K blocks per stage for gate/up,
+        // 4 for down (measured at config 4: gate/up 3.56 / 3.02 / 3.21 ms and
+        // down 2.50 / 2.08 / 1.86 ms with 1 / 2 / 4 blocks per stage)
+        constexpr int kFkb = MODE == kGateUp ? 2 : 4;
+        if (p.k_tiles % kFkb == 0) return launch_bs_mode<MODE, 128, true, false, kFkb>(ta, tb, p, num_sms, st, pdl);
+        if (p.k_tiles % 2 == 0) return launch_bs_mode<MODE, 128, true, false, 2>(ta, tb, p, num_sms, st, pdl);
+    }
     if constexpr (!FP4) {
         if (pair) {
             // two 128-K blocks per stage when the K blocks pair up
