@@ -76,6 +76,12 @@ struct BsCfg {
     static constexpr int kSFCols = kSFStage / 128;            // TMEM columns of scale factors per stage
     static constexpr int kSFBlockCols = kSFBlock / 128;       // ... per K block
     static constexpr int kSmem = kStages * kStageBytes + 2048 /*two 1024 alignments*/ + 512 /*barriers*/;
+    // gate/up with one accumulator: its epilogue holds up the next tile's
+    // MMAs, so more warps share it -- for 128-token tiles four groups of four
+    // warps (the scale-factor warps are one of them, 576 threads), else two
+    static constexpr bool kGuSplit = MODE == kGateUp && kAccs == 1;
+    static constexpr int kEpiGroups = kGuSplit ? (BN == 128 ? 4 : 2) : 1;
+    static constexpr int kThreads = kEpiGroups == 4 ? 576 : 320;
     static_assert(kStages >= (KB >= 2 ? 2 : 3), "pipeline too shallow");
     static_assert(256 + kStages * kSFCols <= 512, "TMEM budget");
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
@@ -839,15 +845,17 @@ __device__ __forceinline__ void gu_tile_part(const BsParams& p, const BsTileX& t
 }
 
 template <int MODE, int BN, bool FP4, bool PAIR, int KB>
-__global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
+__global__ void __launch_bounds__(BsCfg<MODE, BN, FP4, PAIR, KB>::kThreads, 1)
+    gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                          const __grid_constant__ CUtensorMap tmap_b,
                                                          const BsParams p) {
     using C = BsCfg<MODE, BN, FP4, PAIR, KB>;
-    // gate/up with one accumulator: the scale-factor warps drain and store the
-    // upper half of each tile's columns (the MMAs wait for the whole
-    // accumulator anyway), halving the epilogue's time per tile
-    constexpr bool kGuSplit = MODE == kGateUp && C::kAccs == 1;
-    constexpr int kGuW = kGuSplit ? BN / 2 : BN;
+    // gate/up with one accumulator: the epilogue warps, the scale-factor
+    // warps and (128-token tiles) warps 10-17 drain and store one group of
+    // each tile's columns each (the MMAs wait for the whole accumulator
+    // anyway), dividing the epilogue's time per tile
+    constexpr bool kGuSplit = C::kGuSplit;
+    constexpr int kGuW = BN / C::kEpiGroups;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     // scale blocks first (small), then the 1024-aligned operand tiles
@@ -891,7 +899,7 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
         }
         for (int i = 0; i < C::kAccs; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], PAIR ? 2 * (kGuSplit ? 8 : 4) : (kGuSplit ? 256 : 128));
+            mbar_init(&acc_empty[i], PAIR ? 2 * 4 * C::kEpiGroups : 128 * C::kEpiGroups);
         }
         fence_mbar_init();
     }
@@ -1112,8 +1120,8 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 }
             }
         }
-    } else if (warp >= 6) {
-        // ------------------------------------------------------------ scale factors
+    } else if (warp >= 6 && warp < 10) {
+        // ------------------------------------------------------------ scale factors (warps 6-9)
         // Each warp stores the stage's scale blocks into its TMEM lane quarter
         // of the stage's scale columns: lane l of every quarter holds bytes
         // [16 l, 16 l + 16) of each 512-byte block (the layout the MMA reads).
@@ -1166,9 +1174,34 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
                 tc_fence_after();
                 const uint32_t quarter = warp & 3;
                 uint8_t* h_atom = p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * C::kSFB;
-                gu_tile_part<BN, kGuW, FP4, PAIR>(p, tc, tmem + lane_addr, BN / 2, tc.mt * 128 + quarter * 32 + lane,
+                gu_tile_part<BN, kGuW, FP4, PAIR>(p, tc, tmem + lane_addr, kGuW, tc.mt * 128 + quarter * 32 + lane,
                                                   lane, quarter, h_atom, &acc_empty[0],
                                                   PAIR ? mapa_cluster(&acc_empty[0], 0) : 0u);
+                eaccphase ^= 1;
+            }
+        }
+    } else if (warp >= 10) {
+        // ------------------------------------------------------------ epilogue groups 2 and 3
+        // (gate/up 128-token tiles with one accumulator: columns
+        // [group * kGuW, (group + 1) * kGuW) of each tile)
+        if constexpr (C::kEpiGroups == 4) {
+            const uint32_t quarter = warp & 3;
+            const uint32_t lane_addr = (quarter * 32) << 16;
+            const uint32_t group = (warp - 2) >> 2;
+            uint32_t eaccphase = 0;
+            bool ok = true;
+            for (uint32_t tile = first; ok && tile < total; tile += step) {
+                const BsTileX tc = tile_at(tile);
+                ok = mbar_wait(&acc_full[0], eaccphase, p.err, kErrTimeoutAccFull, true);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint8_t* h_atom = p.sfh_atoms + ((uint64_t)tc.ntile * p.m_tiles + tc.mt) * C::kSFB;
+                gu_tile_part<BN, kGuW, FP4, PAIR>(p, tc, tmem + lane_addr, group * kGuW,
+                                                  tc.mt * 128 + quarter * 32 + lane, lane, quarter, h_atom,
+                                                  &acc_empty[0], PAIR ? mapa_cluster(&acc_empty[0], 0) : 0u);
                 eaccphase ^= 1;
             }
         }
@@ -1290,13 +1323,13 @@ __global__ void __launch_bounds__(320, 1) gemm_bs_kernel(const __grid_constant__
 // CTA-pair grids: two CTAs per cluster, as many clusters as can be resident
 // at once (the SMs of a GPC pair up by TPC), found once per device and mode.
 template <typename K>
-static int pair_grid(K kernel, int smem, int num_sms, int* cache) {
+static int pair_grid(K kernel, int smem, int threads, int num_sms, int* cache) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return 0;
     if (cache[dev] == 0) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)(num_sms & ~1));
-        cfg.blockDim = dim3(320);
+        cfg.blockDim = dim3((unsigned)threads);
         cfg.dynamicSmemBytes = (size_t)smem;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1328,12 +1361,13 @@ static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, 
     }
     if constexpr (PAIR) {
         static int grid_cache[64] = {};
-        const int grid = pair_grid(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, C::kSmem, num_sms, grid_cache);
+        const int grid = pair_grid(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, C::kSmem, C::kThreads, num_sms,
+                                   grid_cache);
         if (grid <= 0) return cudaErrorNotSupported;
-        return launch_kernel_cluster2(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(grid), dim3(320), C::kSmem, st, pdl,
+        return launch_kernel_cluster2(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(grid), dim3(C::kThreads), C::kSmem, st, pdl,
                                       ta, tb, p);
     } else {
-        return launch_kernel(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(num_sms), dim3(320), C::kSmem, st, pdl, ta,
+        return launch_kernel(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(num_sms), dim3(C::kThreads), C::kSmem, st, pdl, ta,
                              tb, p);
     }
 }
