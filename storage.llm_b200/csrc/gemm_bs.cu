@@ -49,16 +49,17 @@ namespace moe_b200 {
 // FP4: the fast mode (kind::mxf4): A and B packed E2M1 in shared memory, one
 // B term, 64-byte swizzled rows (one 128-K stage per row).
 // KB: 128-K blocks per pipeline stage (2 on CTA pairs, whose smaller B
-// halves leave room for stages twice as deep in K, and in the fast mode,
-// whose packed operands make a 128-K stage only four MMAs: fewer stage
-// hand-offs per MMA).
+// halves leave room for stages twice as deep in K; 2 on the stacked 32- and
+// 64-token down tiles and 2 or 4 in the fast mode, whose 128-K blocks are
+// only 8 or 4 MMAs): fewer stage hand-offs per MMA.  A tile's last stage holds the
+// K blocks that are left (K blocks need not divide by KB).
 template <int MODE, int BN, bool FP4 = false, bool PAIR = false, int KB = 1>
 struct BsCfg {
     static_assert(BN == 32 || BN == 64 || BN == 128, "tile width");
     static_assert(!PAIR || (BN == 128 && !FP4), "CTA pairs run the exact path's 128-token tiles");
-    static_assert(KB == 1 || (KB == 2 && PAIR) || ((KB == 2 || KB == 4) && FP4),
-                  "several K blocks per stage: CTA pairs and the fast mode's small stages");
     static constexpr bool kStackN = !FP4 && BN <= 64;
+    static_assert(KB == 1 || (KB == 2 && (PAIR || kStackN)) || ((KB == 2 || KB == 4) && FP4),
+                  "several K blocks per stage: CTA pairs, stacked tiles and the fast mode's small stages");
     static constexpr int kNA = MODE == kGateUp ? 2 : 1;       // A operands per stage
     static constexpr int kABytes = FP4 ? 128 * 64 : 128 * 128;  // smem bytes per A box
     static constexpr int kATx = 128 * 128 / 2;                // packed bytes the A box moves
@@ -937,21 +938,22 @@ __global__ void __launch_bounds__(BsCfg<MODE, BN, FP4, PAIR, KB>::kThreads, 1)
         if (lane == 0) {
             uint32_t stage = 0, phase = 0;
             bool ok = true;
-            constexpr uint32_t kOpBytes = KB * (C::kNA * C::kATx + C::kBTerms * C::kBBytes);
-            // arms stage s for this CTA's copies of one use
-            auto arm = [&](uint32_t s) {
+            constexpr uint32_t kOpBytes = C::kNA * C::kATx + C::kBTerms * C::kBBytes;  // per K block
+            // arms stage s for this CTA's copies of one use (nk K blocks)
+            auto arm = [&](uint32_t s, uint32_t nk) {
                 if constexpr (PAIR) {
-                    mbar_arrive_expect_tx(&sf_load[s], C::kSFStage);
-                    mbar_arrive_expect_tx_cluster(mapa_cluster(&load_full[s], 0), kOpBytes);
+                    mbar_arrive_expect_tx(&sf_load[s], nk * C::kSFBlock);
+                    mbar_arrive_expect_tx_cluster(mapa_cluster(&load_full[s], 0), nk * kOpBytes);
                 } else {
-                    mbar_arrive_expect_tx(&load_full[s], kOpBytes + C::kSFStage);
+                    mbar_arrive_expect_tx(&load_full[s], nk * (kOpBytes + C::kSFBlock));
                 }
             };
             auto sf_bar = [&](uint32_t s) { return PAIR ? &sf_load[s] : &load_full[s]; };
             // the weight blocks and weight scales of the stage's K blocks kt..
-            auto load_a = [&](uint32_t s, uint64_t ablk0, uint64_t sblk0, uint32_t kt) {
+            auto load_a = [&](uint32_t s, uint64_t ablk0, uint64_t sblk0, uint32_t kt, uint32_t nk) {
 #pragma unroll
                 for (int kb = 0; kb < KB; ++kb) {
+                    if ((uint32_t)kb >= nk) break;
                     bulk_g2s(sf_base + s * C::kSFStage + kb * C::kSFBlock, p.sfa + (sblk0 + kt + kb) * C::kSFA,
                              C::kSFA, sf_bar(s));
 #pragma unroll
@@ -974,10 +976,11 @@ __global__ void __launch_bounds__(BsCfg<MODE, BN, FP4, PAIR, KB>::kThreads, 1)
                 const uint32_t slot = p.group_slot ? __ldg(p.group_slot + tc.g) : tc.g;
                 const uint64_t ablk0 = ((uint64_t)slot * C::kNA * p.m_tiles + tc.mt) * p.k_tiles;
                 const uint64_t sblk0 = ((uint64_t)slot * p.m_tiles + tc.mt) * p.k_tiles;
-                pre = min((uint32_t)C::kStages, p.k_tiles / KB);
+                pre = min((uint32_t)C::kStages, ceil_div(p.k_tiles, KB));
                 for (uint32_t s = 0; s < pre; ++s) {
-                    arm(s);
-                    load_a(s, ablk0, sblk0, s * KB);
+                    const uint32_t nk = (KB == 1 ? 1u : min((uint32_t)KB, p.k_tiles - s * KB));
+                    arm(s, nk);
+                    load_a(s, ablk0, sblk0, s * KB, nk);
                 }
             }
             pdl_wait();
@@ -991,13 +994,15 @@ __global__ void __launch_bounds__(BsCfg<MODE, BN, FP4, PAIR, KB>::kThreads, 1)
                 for (uint32_t kt = 0; kt < p.k_tiles; kt += KB) {
                     if (!(ok = mbar_wait(&load_empty[stage], phase ^ 1, p.err, kErrTimeoutLoadEmpty))) break;
                     uint8_t* sf = sf_base + stage * C::kSFStage;
+                    const uint32_t nk = (KB == 1 ? 1u : min((uint32_t)KB, p.k_tiles - kt));
                     const bool prefetched = tile == first && kt / KB < pre;
                     if (!prefetched) {
-                        arm(stage);
-                        load_a(stage, ablk0, sblk0, kt);
+                        arm(stage, nk);
+                        load_a(stage, ablk0, sblk0, kt, nk);
                     }
 #pragma unroll
                     for (int kb = 0; kb < KB; ++kb) {
+                        if ((uint32_t)kb >= nk) break;
                         bulk_g2s(sf + kb * C::kSFBlock + C::kSFA,
                                  p.sfb_atoms + ((uint64_t)tc.ntile * p.k_tiles + kt + kb) * C::kSFB, C::kSFB,
                                  sf_bar(stage));
@@ -1052,8 +1057,10 @@ __global__ void __launch_bounds__(BsCfg<MODE, BN, FP4, PAIR, KB>::kThreads, 1)
                                      mbar_test_wait(&sf_full[nstage], nphase);
                     };
                     tc_fence_after();
+                    const uint32_t nk = (KB == 1 ? 1u : min((uint32_t)KB, p.k_tiles - kt));
 #pragma unroll
                     for (int kb = 0; kb < KB; ++kb) {
+                    if ((uint32_t)kb >= nk) break;
                     const uint32_t sfc = tmem + kSfCol0 + stage * C::kSFCols + kb * C::kSFBlockCols;
                     const uint32_t sfb = sfc + C::kNA * 4;
                     const uint32_t a_addr = smem_u32(a_base + (stage * KB + kb) * C::kNA * C::kABytes);
@@ -1070,7 +1077,7 @@ __global__ void __launch_bounds__(BsCfg<MODE, BN, FP4, PAIR, KB>::kThreads, 1)
                                 const uint64_t adesc = smem_desc_sw64(a_addr + pj * C::kABytes + kk * 32);
                                 mma_fp4(d0 + pj * BN, adesc, bdesc, idesc, sfc + pj * 4, sfb, (kacc | kk) != 0);
                             }
-                            if (kb == KB - 1 && kk == 0) look_ahead();
+                            if ((uint32_t)kb + 1 == nk && kk == 0) look_ahead();
                         }
                     } else {
 #pragma unroll
@@ -1094,7 +1101,7 @@ __global__ void __launch_bounds__(BsCfg<MODE, BN, FP4, PAIR, KB>::kThreads, 1)
                                 }
                             }
                         }
-                        if (kb == KB - 1 && kk == 2) look_ahead();
+                        if ((uint32_t)kb + 1 == nk && kk == 2) look_ahead();
                     }
                     }
                     }
@@ -1142,8 +1149,10 @@ __global__ void __launch_bounds__(BsCfg<MODE, BN, FP4, PAIR, KB>::kThreads, 1)
                 }
                 const uint8_t* sf = sf_base + stage * C::kSFStage + lane * 16;
                 const uint32_t col = tmem + lane_addr + kSfCol0 + stage * C::kSFCols;
+                const int nq = (int)(KB == 1 ? 1u : min((uint32_t)KB, p.k_tiles - kt)) * (C::kSFBlock / 512);
 #pragma unroll
                 for (int q = 0; q < C::kSFStage / 512; ++q) {
+                    if (q >= nq) break;
                     const uint4 v = *reinterpret_cast<const uint4*>(sf + q * 512);
                     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
                     MOE_TMEM_ST4(col + q * 4, w);
@@ -1375,6 +1384,14 @@ static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, 
 template <int MODE, bool FP4>
 static cudaError_t launch_bs_width(int block_n, bool pair, const CUtensorMap& ta, const CUtensorMap& tb,
                                    const BsParams& p, int num_sms, cudaStream_t st, bool pdl) {
+    if constexpr (!FP4 && MODE == kDown) {
+        // stacked down tiles: two K blocks per stage (3 stages of 66 KB at 64
+        // tokens; measured at config 1, 256 tokens: 68 -> 65 us).  The gate/up
+        // ones keep one: two 99 KB stages are too shallow for their weight
+        // stream (105 -> 116 us).
+        if (block_n == 32) return launch_bs_mode<MODE, 32, false, false, 2>(ta, tb, p, num_sms, st, pdl);
+        if (block_n == 64) return launch_bs_mode<MODE, 64, false, false, 2>(ta, tb, p, num_sms, st, pdl);
+    }
     if (block_n == 32) return launch_bs_mode<MODE, 32, FP4, false>(ta, tb, p, num_sms, st, pdl);
     if (block_n == 64) return launch_bs_mode<MODE, 64, FP4, false>(ta, tb, p, num_sms, st, pdl);
     if constexpr (FP4) {
@@ -1382,14 +1399,12 @@ static cudaError_t launch_bs_width(int block_n, bool pair, const CUtensorMap& ta
         // 4 for down (measured at config 4: gate/up 3.56 / 3.02 / 3.21 ms and
         // down 2.50 / 2.08 / 1.86 ms with 1 / 2 / 4 blocks per stage)
         constexpr int kFkb = MODE == kGateUp ? 2 : 4;
-        if (p.k_tiles % kFkb == 0) return launch_bs_mode<MODE, 128, true, false, kFkb>(ta, tb, p, num_sms, st, pdl);
-        if (p.k_tiles % 2 == 0) return launch_bs_mode<MODE, 128, true, false, 2>(ta, tb, p, num_sms, st, pdl);
+        return launch_bs_mode<MODE, 128, true, false, kFkb>(ta, tb, p, num_sms, st, pdl);
     }
     if constexpr (!FP4) {
         if (pair) {
-            // two 128-K blocks per stage when the K blocks pair up
-            return p.k_tiles % 2 == 0 ? launch_bs_mode<MODE, 128, false, true, 2>(ta, tb, p, num_sms, st, pdl)
-                                      : launch_bs_mode<MODE, 128, false, true, 1>(ta, tb, p, num_sms, st, pdl);
+            // two 128-K blocks per stage
+            return launch_bs_mode<MODE, 128, false, true, 2>(ta, tb, p, num_sms, st, pdl);
         }
     }
     return launch_bs_mode<MODE, 128, FP4, false>(ta, tb, p, num_sms, st, pdl);
