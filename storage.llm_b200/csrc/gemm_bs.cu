@@ -431,39 +431,61 @@ __global__ void __launch_bounds__(256) scatter_quant_bs_kernel(const uint16_t* _
             const uint32_t k = (kt0 + c) * 128 + lane * 4;  // H % 8 == 0: four elements all in or all out
             raw[c] = (kt0 + c < nkt && k < H) ? __ldg(reinterpret_cast<const uint2*>(xr + k)) : make_uint2(0, 0);
         }
+        // the chunk's K blocks split first, then each destination row
+        // resolved once and written for all of them
+        const uint32_t nc = min(kGqChunk, nkt - kt0);
+        uint32_t hi4[kGqChunk], lo4[kGqChunk], shw[kGqChunk], slw[kGqChunk];
 #pragma unroll
         for (uint32_t c = 0; c < kGqChunk; ++c) {
-            const uint32_t kt = kt0 + c;
-            if (kt >= nkt) break;  // uniform across the warp
             const float v[4] = {__uint_as_float(raw[c].x << 16), __uint_as_float(raw[c].x & 0xffff0000u),
                                 __uint_as_float(raw[c].y << 16), __uint_as_float(raw[c].y & 0xffff0000u)};
-            uint32_t hi4, lo4;
             uint8_t sh, sl;
-            split_e4m3_x4(v, hi4, lo4, sh, sl);
+            split_e4m3_x4(v, hi4[c], lo4[c], sh, sl);
             // block j's scale bytes sit in lane 8j; gather them into one word
-            uint32_t shw = 0, slw = 0;
+            shw[c] = 0;
+            slw[c] = 0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                shw |= (uint32_t)(uint8_t)__shfl_sync(0xffffffffu, (uint32_t)sh, 8 * j) << (8 * j);
-                slw |= (uint32_t)(uint8_t)__shfl_sync(0xffffffffu, (uint32_t)sl, 8 * j) << (8 * j);
+                shw[c] |= (uint32_t)(uint8_t)__shfl_sync(0xffffffffu, (uint32_t)sh, 8 * j) << (8 * j);
+                slw[c] |= (uint32_t)(uint8_t)__shfl_sync(0xffffffffu, (uint32_t)sl, 8 * j) << (8 * j);
             }
-            auto put = [&](uint32_t pos, uint32_t info) {
-                uint32_t* dh = reinterpret_cast<uint32_t*>(xb + (uint64_t)pos * Kp) + lane;
-                dh[kt * 32] = hi4;
-                reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(dh) + xplane)[kt * 32] = lo4;
-                if (lane == 0) {
-                    uint8_t* atom = sf_atoms + ((uint64_t)(info >> 8) * nkt + kt) * kAtom;
-                    *reinterpret_cast<uint32_t*>(atom + sfb_pos_hi<BN>(info & 0xFFu)) = shw;
-                    *reinterpret_cast<uint32_t*>(atom + sfb_pos_lo<BN>(info & 0xFFu)) = slw;
-                }
-            };
-            for (uint32_t j = 0; j < K; ++j) {
-                const uint32_t pos = __shfl_sync(0xffffffffu, my_pos, j);
-                const uint32_t info = __shfl_sync(0xffffffffu, my_info, j);
-                if (pos != 0xFFFFFFFFu) put(pos, info);  // uniform across the warp
-            }
-            if (sh_pos != 0xFFFFFFFFu) put(sh_pos, sh_info);
         }
+        auto put = [&](uint32_t pos, uint32_t info) {
+            uint32_t* dh = reinterpret_cast<uint32_t*>(xb + (uint64_t)pos * Kp) + lane + kt0 * 32;
+            uint32_t* dl = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(dh) + xplane);
+            if (nc == kGqChunk) {
+#pragma unroll
+                for (uint32_t c = 0; c < kGqChunk; ++c) {
+                    dh[c * 32] = hi4[c];
+                    dl[c * 32] = lo4[c];
+                }
+            } else {
+#pragma unroll
+                for (uint32_t c = 0; c < kGqChunk; ++c) {
+                    if (c < nc) {
+                        dh[c * 32] = hi4[c];
+                        dl[c * 32] = lo4[c];
+                    }
+                }
+            }
+            if (lane < nc) {  // lane c stores K block kt0 + c's scale words
+                uint32_t h = shw[0], l = slw[0];
+#pragma unroll
+                for (uint32_t c = 1; c < kGqChunk; ++c) {
+                    h = lane == c ? shw[c] : h;
+                    l = lane == c ? slw[c] : l;
+                }
+                uint8_t* atom = sf_atoms + ((uint64_t)(info >> 8) * nkt + kt0 + lane) * kAtom;
+                *reinterpret_cast<uint32_t*>(atom + sfb_pos_hi<BN>(info & 0xFFu)) = h;
+                *reinterpret_cast<uint32_t*>(atom + sfb_pos_lo<BN>(info & 0xFFu)) = l;
+            }
+        };
+        for (uint32_t j = 0; j < K; ++j) {
+            const uint32_t pos = __shfl_sync(0xffffffffu, my_pos, j);
+            const uint32_t info = __shfl_sync(0xffffffffu, my_info, j);
+            if (pos != 0xFFFFFFFFu) put(pos, info);  // uniform across the warp
+        }
+        if (sh_pos != 0xFFFFFFFFu) put(sh_pos, sh_info);
     }
 }
 
