@@ -122,30 +122,27 @@ __device__ __forceinline__ int block_exp(float amax) {
     return amax > 0.f ? max(-127, min(127, e)) : -127;
 }
 
-// The value of round-to-nearest-even of y (|y| < 448) to E4M3 (the code
-// itself comes from the hardware conversion, cvt_e4m3x2, which rounds the
-// same way).  Normal range (|y| >= 2^-6): keep 3 mantissa bits of the fp32
-// pattern (RNE on the 20 dropped bits; a carry into the exponent is the
-// correct next binade).  Subnormal range: multiples of 2^-9, rounded by adding
-// and subtracting 1.5 * 2^14 (whose fp32 ulp is 2^-9).  Both ranges are
-// computed and one is selected, so the code has no per-lane branch.
-__device__ __forceinline__ float e4m3_rne_value(float y) {
-    const uint32_t sign = __float_as_uint(y) & 0x80000000u;
-    const float ay = fabsf(y);
-    uint32_t b = __float_as_uint(ay);
-    b = (b + 0x7FFFFu + ((b >> 20) & 1u)) & 0xFFF00000u;
-    const float q_s = __fsub_rn(__fadd_rn(ay, 24576.0f), 24576.0f);
-    return __uint_as_float((ay >= 0.015625f ? b : __float_as_uint(q_s)) | sign);
-}
-
 // Two fp32 values to E4M3 codes by the hardware conversion (round to nearest
 // even, saturating finite; no saturation happens for |y| < 448): the first
-// argument in the low byte.  One conversion per two values; the rounded value
-// a residual needs comes from e4m3_rne_value.
+// argument in the low byte.  One conversion per two values.
 __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
     uint16_t d;
     asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(hi), "f"(lo));
     return d;
+}
+
+// The values of the two E4M3 codes in the low 16 bits of `code2` (low byte
+// first), exactly: every E4M3 value is an f16 value, so the hardware
+// conversion to f16x2 and then to fp32 loses nothing.  The residual of the
+// hi/lo split needs the rounded hi value; this is it, two at a time.
+__device__ __forceinline__ void e4m3x2_values(uint32_t code2, float& lo, float& hi) {
+    asm("{\n\t.reg .b32 h2;\n\t.reg .b16 l, h;\n\t"
+        "cvt.rn.f16x2.e4m3x2 h2, %2;\n\t"
+        "mov.b32 {l, h}, h2;\n\t"
+        "cvt.f32.f16 %0, l;\n\t"
+        "cvt.f32.f16 %1, h;\n\t}"
+        : "=f"(lo), "=f"(hi)
+        : "h"((uint16_t)code2));
 }
 
 // Splits the 32 values held by a warp (one per lane, one 32-element K block)
@@ -153,8 +150,11 @@ __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
 __device__ __forceinline__ void split_e4m3_warp(float v, uint8_t& hi, uint8_t& lo, uint8_t& s_hi, uint8_t& s_lo) {
     const int e1 = block_exp(warp_max_abs(v));
     const float y = v * pow2f(-e1);
-    hi = (uint8_t)cvt_e4m3x2(y, 0.0f);
-    const float r = v - e4m3_rne_value(y) * pow2f(e1);
+    const uint32_t c = cvt_e4m3x2(y, 0.0f);
+    hi = (uint8_t)c;
+    float q, q_unused;
+    e4m3x2_values(c, q, q_unused);
+    const float r = v - q * pow2f(e1);
     const int e2 = block_exp(warp_max_abs(r));
     lo = (uint8_t)cvt_e4m3x2(r * pow2f(-e2), 0.0f);
     s_hi = (uint8_t)(e1 + 127);
@@ -179,13 +179,15 @@ __device__ __forceinline__ void split_e4m3_x4(const float v[4], uint32_t& hi4, u
     const int e1 = block_exp(group_max(m));
     float r[4];
     const float inv1 = pow2f(-e1), sc1 = pow2f(e1);
-    float y[4];
+    float y[4], q[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        y[i] = v[i] * inv1;
-        r[i] = v[i] - e4m3_rne_value(y[i]) * sc1;
-    }
-    hi4 = cvt_e4m3x2(y[0], y[1]) | (cvt_e4m3x2(y[2], y[3]) << 16);
+    for (int i = 0; i < 4; ++i) y[i] = v[i] * inv1;
+    const uint32_t c01 = cvt_e4m3x2(y[0], y[1]), c23 = cvt_e4m3x2(y[2], y[3]);
+    hi4 = c01 | (c23 << 16);
+    e4m3x2_values(c01, q[0], q[1]);
+    e4m3x2_values(c23, q[2], q[3]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = v[i] - q[i] * sc1;
     m = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
     const int e2 = block_exp(group_max(m));
     const float inv2 = pow2f(-e2);
@@ -692,25 +694,41 @@ __device__ __forceinline__ void h_store8(const float* hv, uint32_t c0, uint32_t 
     // split_e4m3_warp for the 8 values, written phase by phase (all block
     // maxima of a phase back to back) so the independent chains overlap
     // around the warp reductions
+    // (codes two columns per conversion, the rounded hi values from the
+    // reverse conversion)
     uint8_t hi[8], lo[8], sh[8], sl[8];
-    float mx[8], r[8];
+    float mx[8], r[8], y[8];
+    int e[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) mx[j] = warp_max_abs(hv[j]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const int e1 = block_exp(mx[j]);
-        const float y = hv[j] * pow2f(-e1);
-        hi[j] = (uint8_t)cvt_e4m3x2(y, 0.0f);
-        r[j] = hv[j] - e4m3_rne_value(y) * pow2f(e1);
-        sh[j] = (uint8_t)(e1 + 127);
+        e[j] = block_exp(mx[j]);
+        y[j] = hv[j] * pow2f(-e[j]);
+        sh[j] = (uint8_t)(e[j] + 127);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        const uint32_t c = cvt_e4m3x2(y[j], y[j + 1]);
+        hi[j] = (uint8_t)c;
+        hi[j + 1] = (uint8_t)(c >> 8);
+        float q0, q1;
+        e4m3x2_values(c, q0, q1);
+        r[j] = hv[j] - q0 * pow2f(e[j]);
+        r[j + 1] = hv[j + 1] - q1 * pow2f(e[j + 1]);
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) mx[j] = warp_max_abs(r[j]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const int e2 = block_exp(mx[j]);
-        lo[j] = (uint8_t)cvt_e4m3x2(r[j] * pow2f(-e2), 0.0f);
-        sl[j] = (uint8_t)(e2 + 127);
+        e[j] = block_exp(mx[j]);
+        sl[j] = (uint8_t)(e[j] + 127);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        const uint32_t c = cvt_e4m3x2(r[j] * pow2f(-e[j]), r[j + 1] * pow2f(-e[j + 1]));
+        lo[j] = (uint8_t)c;
+        lo[j + 1] = (uint8_t)(c >> 8);
     }
     uint8_t* hp = p.h_out + (row0 + c0) * p.h_stride + m;
     uint8_t* lp = hp + p.h_plane;
