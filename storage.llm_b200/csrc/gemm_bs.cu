@@ -31,13 +31,16 @@
 //          block of the down GEMM), so the down GEMM reads it directly.
 // kDown:   the epilogue writes fp32 expert outputs for the combine.
 //
-// Warp roles (320 threads, one CTA per SM, persistent over a precomputed tile
-// table):
-//   warp 0     producer: per stage one bulk copy of the weight scales, one of
-//              the activation scales, the A boxes, and one B box
-//   warp 1     TMEM owner and MMA issue
-//   warps 2-5  epilogue, one TMEM lane quarter each
-//   warps 6-9  scale factors into TMEM, one lane quarter each
+// Warp roles (320 threads, one CTA per SM -- or per SM of a CTA pair --,
+// persistent over a precomputed tile table):
+//   warp 0      producer: per 128-K block one bulk copy of the weight scales,
+//               one of the activation scales, the A boxes and one B box
+//   warp 1      TMEM owner and MMA issue (in a CTA pair, the rank-0 CTA's)
+//   warps 2-5   epilogue, one TMEM lane quarter each
+//   warps 6-9   scale factors into TMEM, one lane quarter each; for gate/up
+//               tiles with one accumulator also a share of the epilogue
+//   warps 10-17 (576 threads: 128-token gate/up tiles with one accumulator)
+//               two more epilogue groups
 // All waits are bounded and report through p.err.
 #include <algorithm>
 
