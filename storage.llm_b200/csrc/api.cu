@@ -463,7 +463,8 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
                       &eng->g_offset, &eng->g_gu_off, &eng->g_dn_off, &eng->xperm, &eng->hperm,
                       &eng->yperm, &eng->err_word, &eng->hx, &eng->hy, &eng->hyf, &eng->hids,
                       &eng->hw, &eng->hperm_out, &eng->tri, &eng->xb,
-                      &eng->sfx_atoms, &eng->hb, &eng->sfh_atoms, &eng->gu_tiles, &eng->dn_tiles};
+                      &eng->sfx_atoms, &eng->hb, &eng->sfh_atoms, &eng->gu_tiles, &eng->dn_tiles,
+                      &eng->pipe_ys, &eng->pipe_zero_ids, &eng->pipe_slot};
     for (DevBuf* b : bufs) b->release();
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
     ep_release(eng->ep);
@@ -764,6 +765,19 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
     const int sigmoid = cfg->score_func == MOE_B200_SCORE_SIGMOID;
     const float rscale = cfg->routed_scale > 0.f ? cfg->routed_scale : 1.0f;
     const RouteCfg rcfg{sigmoid, cfg->norm_topk, rscale, cfg->n_group, cfg->topk_group};
+    // host-buffer calls: the shared expert needs no routing, so its pipeline
+    // runs on each token chunk right after the chunk lands, under the copies
+    // of the chunks after it; the routed pass then leaves it out
+    const bool pipe_shared = pipe && shared && bs;
+    if (pipe_shared) {
+        CK(eng->pipe_ys.reserve((size_t)T * H * 4));
+        if (eng->pipe_zero_ids.bytes < (size_t)T * 4) {
+            CK(eng->pipe_zero_ids.reserve((size_t)T * 4));
+            CK(cudaMemsetAsync(eng->pipe_zero_ids.ptr, 0, eng->pipe_zero_ids.bytes, st));
+        }
+        CK(eng->pipe_slot.reserve(4));
+        CK(cudaMemcpyAsync(eng->pipe_slot.ptr, &L->E, 4, cudaMemcpyHostToDevice, st));
+    }
     // block parts: the routed input RMSNorm(hidden) * pre_norm2, exactly as
     // the reference computes it (fp32 for the router, bf16 for the experts)
     const uint16_t* x_routed = x;
@@ -804,6 +818,23 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
                              eng->logits.as<float>() + (size_t)t0 * E, ids + (size_t)t0 * K, w + (size_t)t0 * K,
                              eng->scores.as<float>() + (size_t)t0 * E, errw, st, &launches, rt_tma ? &rtx : nullptr,
                              rt_tma ? &rtw : nullptr));
+            if (pipe_shared) {
+                // the shared expert on this chunk: one group, its own output rows
+                BsJob sj{};
+                sj.ids = eng->pipe_zero_ids.as<int32_t>();
+                sj.T = t1 - t0;
+                sj.K = 1;
+                sj.E = 1;
+                sj.shared_rows = 0;
+                sj.shared_base = 0;
+                sj.src = xc;
+                sj.act = cfg->activation;
+                sj.group_slot = eng->pipe_slot.as<uint32_t>();
+                sj.y = eng->pipe_ys.as<float>() + (size_t)t0 * H;
+                sj.y_by_source = true;
+                sj.fp4 = fp4;
+                if (!run_blockscaled(eng, L, sj, st, nullptr, &launches, err)) return 0;
+            }
         }
     } else {
         CUtensorMap rtx, rtw;
@@ -832,7 +863,7 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
         job.T = T;
         job.K = K;
         job.E = E;
-        job.shared_rows = shared_rows;
+        job.shared_rows = pipe_shared ? 0 : shared_rows;
         job.shared_base = 0;
         job.src = x_routed;
         job.src_shared = (x_routed != x && shared_rows) ? x : nullptr;
@@ -899,7 +930,9 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
 
     // tokens [t0, t1): the combine, then (host-buffer calls) their copy back
     auto combine = [&](uint32_t t0, uint32_t t1) -> int {
-        const float* ys = shared ? eng->yperm.as<float>() + (size_t)(n + t0) * H : nullptr;
+        const float* ys = !shared      ? nullptr
+                          : pipe_shared ? eng->pipe_ys.as<float>() + (size_t)t0 * H
+                                        : eng->yperm.as<float>() + (size_t)(n + t0) * H;
         uint16_t* yb = y_bf16 ? y_bf16 + (size_t)t0 * H : nullptr;
         float* yf = y_f32 ? y_f32 + (size_t)t0 * H : nullptr;
         if (L->has_block_combine()) {

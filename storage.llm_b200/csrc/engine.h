@@ -163,6 +163,9 @@ struct moe_b200_engine {
     // chunk by chunk (events: kPipeChunks copy-ins, then kPipeChunks combines)
     cudaStream_t pipe_in = nullptr, pipe_out = nullptr;
     std::vector<cudaEvent_t> pipe_ev;
+    // ... and the shared expert runs on each chunk as it lands: its output
+    // rows by token, its all-zero group ids, its one-entry group -> slot map
+    DevBuf pipe_ys, pipe_zero_ids, pipe_slot;
     uint32_t* h_err = nullptr;
     CUtensorMap tmap_x{}, tmap_h{};
     void* tmap_x_base = nullptr;
