@@ -1416,11 +1416,11 @@ static cudaError_t launch_bs_mode(const CUtensorMap& ta, const CUtensorMap& tb, 
         const int grid = pair_grid(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, C::kSmem, C::kThreads, num_sms,
                                    grid_cache);
         if (grid <= 0) return cudaErrorNotSupported;
-        return launch_kernel_cluster2(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(grid), dim3(C::kThreads), C::kSmem, st, pdl,
-                                      ta, tb, p);
+        return launch_kernel_cluster2(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(grid), dim3(C::kThreads),
+                                      C::kSmem, st, pdl, ta, tb, p);
     } else {
-        return launch_kernel(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(num_sms), dim3(C::kThreads), C::kSmem, st, pdl, ta,
-                             tb, p);
+        return launch_kernel(gemm_bs_kernel<MODE, BN, FP4, PAIR, KB>, dim3(num_sms), dim3(C::kThreads), C::kSmem,
+                             st, pdl, ta, tb, p);
     }
 }
 
