@@ -181,6 +181,28 @@ MOE_B200_API int moe_b200_upload_expert(moe_b200_engine_t* engine, int32_t layer
                            uint64_t down_bytes, uint32_t hidden, uint32_t intermediate, int32_t src_on_device,
                            char* err);
 
+/* Repacked-expert records: the second half of the residency upload hook
+ * (device_tensor_copy_ops.cpp.inc:73), so that a persisted cache beside the
+ * model's JUJU sections makes re-residency a plain copy with no repack.
+ * A record is one expert's block-scaled form exactly as the engine stores
+ * it, four byte ranges back to back (Ip = I and Hp = H rounded up to 128):
+ *   gate/up codes  [2][Ip][Hp/2]   E2M1 pairs, 8 KB blocks of 128 rows x 128 K
+ *   gate/up scales [Ip/128][Hp/128][gate, up][512]  E8M0, the MMA's layout
+ *   down codes     [Hp][Ip/2]
+ *   down scales    [Hp/128][Ip/128][512]
+ * Its size depends only on H and I (0 for a shape the engine rejects).
+ * Export copies a resident expert's record (expert -1: the shared expert)
+ * to host or device memory; import installs a record as upload_expert would
+ * have left it, without the repack.  Both run on the upload stream and return
+ * when their copies are done.  A record carries no shape or checksum of its
+ * own: the file that keeps it does (storage.llm_b200/expert_cache.py). */
+MOE_B200_API uint64_t moe_b200_expert_record_bytes(uint32_t hidden, uint32_t intermediate);
+MOE_B200_API int moe_b200_export_expert(moe_b200_engine_t* engine, int32_t layer, int32_t expert, uint8_t* dst,
+                           uint64_t dst_bytes, int32_t dst_on_device, char* err);
+MOE_B200_API int moe_b200_import_expert(moe_b200_engine_t* engine, int32_t layer, int32_t expert, const uint8_t* src,
+                           uint64_t src_bytes, uint32_t hidden, uint32_t intermediate, int32_t src_on_device,
+                           char* err);
+
 /* The block tensors of a layer (copied into the engine; NULL clears them).
  * The router of the layer must be uploaded first.  The layer's forward then
  * applies them (moe_b200_block_forward when pre_norm2 or router_scale is

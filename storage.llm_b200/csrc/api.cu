@@ -145,6 +145,73 @@ LayerWeights* get_layer(moe_b200_engine* eng, int32_t layer, char* err) {
     return &eng->layers[layer];
 }
 
+// The layer's block-scaled expert store for experts of I = intermediate
+// rows (H = the router's): allocated, zeroed and mapped on the first expert
+// of a shape; a new intermediate size drops the layer's experts.
+int ensure_bs_layout(moe_b200_engine* eng, LayerWeights* L, uint32_t intermediate, char* err) {
+    if (L->I == intermediate && L->bs_gu_codes.ptr) return 1;
+    const uint32_t hidden = L->H;
+    L->I = 0;  // set once the store is complete, so a failure here starts over next time
+    // a new shape drops the layer's tile form; it is derived again on demand
+    L->gu.release();
+    L->dn.release();
+    L->gu_stride = 0;
+    L->dn_stride = 0;
+    L->rp_i = round_up(intermediate, 128);
+    L->rp_h = round_up(hidden, 128);
+    L->kq = round_up(hidden, 128);
+    L->iq = round_up(intermediate, 128);
+    const uint64_t slots = L->E + 1;
+    L->bs_gu_codes.release();
+    L->bs_gu_sfa.release();
+    L->bs_dn_codes.release();
+    L->bs_dn_sfa.release();
+    L->present.assign(L->E + 1, 0);
+    L->tile_ready.assign(L->E + 1, 0);
+    CK(L->bs_gu_codes.reserve(slots * 2 * L->rp_i * (L->kq / 2)));
+    CK(L->bs_gu_sfa.reserve(slots * 2 * (L->rp_i / 128) * (L->kq / 128) * 512));
+    CK(L->bs_dn_codes.reserve(slots * L->rp_h * (L->iq / 2)));
+    CK(L->bs_dn_sfa.reserve(slots * (L->rp_h / 128) * (L->iq / 128) * 512));
+    // slots never uploaded hold zero codes: such an expert computes an
+    // exact zero row, which is what skipping it adds (skip_missing)
+    CK(cudaMemsetAsync(L->bs_gu_codes.ptr, 0, L->bs_gu_codes.bytes, eng->ustream));
+    CK(cudaMemsetAsync(L->bs_gu_sfa.ptr, 0, L->bs_gu_sfa.bytes, eng->ustream));
+    CK(cudaMemsetAsync(L->bs_dn_codes.ptr, 0, L->bs_dn_codes.bytes, eng->ustream));
+    CK(cudaMemsetAsync(L->bs_dn_sfa.ptr, 0, L->bs_dn_sfa.bytes, eng->ustream));
+    // codes are 8 KB blocks of 128 rows x 128 K: a "tall" tensor of 128-element
+    // rows, one 128 x 128 box per block
+    if (!make_tmap2d(eng, &L->tmap_gu_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_gu_codes.ptr, 128,
+                     slots * 2 * L->rp_i * (L->kq / 128), 64, 128, 128, err) ||
+        !make_tmap2d(eng, &L->tmap_dn_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_dn_codes.ptr, 128,
+                     slots * L->rp_h * (L->iq / 128), 64, 128, 128, err) ||
+        !make_tmap2d(eng, &L->tmap_gu_fp4, CU_TENSOR_MAP_DATA_TYPE_UINT8, L->bs_gu_codes.ptr, 64,
+                     slots * 2 * L->rp_i * (L->kq / 128), 64, 64, 128, err, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_tmap2d(eng, &L->tmap_dn_fp4, CU_TENSOR_MAP_DATA_TYPE_UINT8, L->bs_dn_codes.ptr, 64,
+                     slots * L->rp_h * (L->iq / 128), 64, 64, 128, err, CU_TENSOR_MAP_SWIZZLE_64B)) {
+        return 0;
+    }
+    L->I = intermediate;
+    return 1;
+}
+
+// One expert slot's block-scaled form as the four byte ranges of an expert
+// record, in record order: gate and up codes, their scale blocks, down codes,
+// down scale blocks.
+struct RecordPart {
+    uint8_t* dev;
+    uint64_t bytes;
+};
+void record_parts(const LayerWeights* L, uint32_t slot, RecordPart out[4]) {
+    const uint64_t gu_codes = 2ull * L->rp_i * (L->kq / 2);
+    const uint64_t gu_sfa = 2ull * (L->rp_i / 128) * (L->kq / 128) * 512;
+    const uint64_t dn_codes = (uint64_t)L->rp_h * (L->iq / 2);
+    const uint64_t dn_sfa = (uint64_t)(L->rp_h / 128) * (L->iq / 128) * 512;
+    out[0] = {L->bs_gu_codes.as<uint8_t>() + slot * gu_codes, gu_codes};
+    out[1] = {L->bs_gu_sfa.as<uint8_t>() + slot * gu_sfa, gu_sfa};
+    out[2] = {L->bs_dn_codes.as<uint8_t>() + slot * dn_codes, dn_codes};
+    out[3] = {L->bs_dn_sfa.as<uint8_t>() + slot * dn_sfa, dn_sfa};
+}
+
 int ensure_tile_form(moe_b200_engine* eng, LayerWeights* L, uint32_t slot, char* err) {
     if (slot >= L->present.size() || !L->present[slot]) {
         set_err(err, "expert slot %u not uploaded", slot);
@@ -530,47 +597,7 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
         return 0;
     }
     CK(cudaSetDevice(eng->device));
-    if (L->I != intermediate || !L->bs_gu_codes.ptr) {
-        L->I = intermediate;
-        // a new shape drops the layer's tile form; it is derived again on demand
-        L->gu.release();
-        L->dn.release();
-        L->gu_stride = 0;
-        L->dn_stride = 0;
-        L->rp_i = round_up(intermediate, 128);
-        L->rp_h = round_up(hidden, 128);
-        L->kq = round_up(hidden, 128);
-        L->iq = round_up(intermediate, 128);
-        const uint64_t slots = L->E + 1;
-        L->bs_gu_codes.release();
-        L->bs_gu_sfa.release();
-        L->bs_dn_codes.release();
-        L->bs_dn_sfa.release();
-        CK(L->bs_gu_codes.reserve(slots * 2 * L->rp_i * (L->kq / 2)));
-        CK(L->bs_gu_sfa.reserve(slots * 2 * (L->rp_i / 128) * (L->kq / 128) * 512));
-        CK(L->bs_dn_codes.reserve(slots * L->rp_h * (L->iq / 2)));
-        CK(L->bs_dn_sfa.reserve(slots * (L->rp_h / 128) * (L->iq / 128) * 512));
-        // slots never uploaded hold zero codes: such an expert computes an
-        // exact zero row, which is what skipping it adds (skip_missing)
-        CK(cudaMemsetAsync(L->bs_gu_codes.ptr, 0, L->bs_gu_codes.bytes, eng->ustream));
-        CK(cudaMemsetAsync(L->bs_gu_sfa.ptr, 0, L->bs_gu_sfa.bytes, eng->ustream));
-        CK(cudaMemsetAsync(L->bs_dn_codes.ptr, 0, L->bs_dn_codes.bytes, eng->ustream));
-        CK(cudaMemsetAsync(L->bs_dn_sfa.ptr, 0, L->bs_dn_sfa.bytes, eng->ustream));
-        // codes are 8 KB blocks of 128 rows x 128 K: a "tall" tensor of 128-element
-        // rows, one 128 x 128 box per block
-        if (!make_tmap2d(eng, &L->tmap_gu_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_gu_codes.ptr, 128,
-                         slots * 2 * L->rp_i * (L->kq / 128), 64, 128, 128, err) ||
-            !make_tmap2d(eng, &L->tmap_dn_codes, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->bs_dn_codes.ptr, 128,
-                         slots * L->rp_h * (L->iq / 128), 64, 128, 128, err) ||
-            !make_tmap2d(eng, &L->tmap_gu_fp4, CU_TENSOR_MAP_DATA_TYPE_UINT8, L->bs_gu_codes.ptr, 64,
-                         slots * 2 * L->rp_i * (L->kq / 128), 64, 64, 128, err, CU_TENSOR_MAP_SWIZZLE_64B) ||
-            !make_tmap2d(eng, &L->tmap_dn_fp4, CU_TENSOR_MAP_DATA_TYPE_UINT8, L->bs_dn_codes.ptr, 64,
-                         slots * L->rp_h * (L->iq / 128), 64, 64, 128, err, CU_TENSOR_MAP_SWIZZLE_64B)) {
-            return 0;
-        }
-        L->present.assign(L->E + 1, 0);
-        L->tile_ready.assign(L->E + 1, 0);
-    }
+    if (!ensure_bs_layout(eng, L, intermediate, err)) return 0;
     const uint32_t slot = expert < 0 ? L->E : (uint32_t)expert;
     const uint8_t* src[3] = {gate, up, down};
     const uint64_t need[3] = {gu_need, gu_need, dn_need};
@@ -603,6 +630,86 @@ int moe_b200_upload_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert
     // the caller may reuse its buffers (and the next upload the staging
     // buffer) once this returns: wait for this upload only, not the device
     CK(cudaStreamSynchronize(st));
+    L->present[slot] = 1;
+    L->tile_ready[slot] = 0;
+    return 1;
+}
+
+uint64_t moe_b200_expert_record_bytes(uint32_t hidden, uint32_t intermediate) {
+    if (hidden == 0 || intermediate == 0 || intermediate > 100000 || hidden > 100000) return 0;
+    const uint64_t rp_i = round_up(intermediate, 128), rp_h = round_up(hidden, 128);
+    const uint64_t kq = rp_h, iq = rp_i;
+    return 2 * rp_i * (kq / 2) + 2 * (rp_i / 128) * (kq / 128) * 512 + rp_h * (iq / 2) + (rp_h / 128) * (iq / 128) * 512;
+}
+
+int moe_b200_export_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert, uint8_t* dst, uint64_t dst_bytes,
+                           int32_t dst_on_device, char* err) {
+    LayerWeights* L = get_layer(eng, layer, err);
+    if (!L) return 0;
+    if (!L->E || !L->I || expert < -1 || expert >= (int32_t)L->E) {
+        set_err(err, "layer %d has no expert %d", layer, expert);
+        return 0;
+    }
+    const uint32_t slot = expert < 0 ? L->E : (uint32_t)expert;
+    if (slot >= L->present.size() || !L->present[slot]) {
+        set_err(err, "expert %d of layer %d is not resident", expert, layer);
+        return 0;
+    }
+    const uint64_t need = moe_b200_expert_record_bytes(L->H, L->I);
+    if (!dst || dst_bytes < need) {
+        set_err(err, "expert record needs %llu bytes, got %llu", (unsigned long long)need,
+                (unsigned long long)dst_bytes);
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    RecordPart parts[4];
+    record_parts(L, slot, parts);
+    uint64_t off = 0;
+    for (const RecordPart& r : parts) {
+        CK(cudaMemcpyAsync(dst + off, r.dev, r.bytes, dst_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                           eng->ustream));
+        off += r.bytes;
+    }
+    CK(cudaStreamSynchronize(eng->ustream));
+    return 1;
+}
+
+int moe_b200_import_expert(moe_b200_engine_t* eng, int32_t layer, int32_t expert, const uint8_t* src,
+                           uint64_t src_bytes, uint32_t hidden, uint32_t intermediate, int32_t src_on_device,
+                           char* err) {
+    LayerWeights* L = get_layer(eng, layer, err);
+    if (!L) return 0;
+    if (!L->E) {
+        set_err(err, "upload the router of layer %d before its experts", layer);
+        return 0;
+    }
+    if (hidden != L->H || intermediate == 0 || intermediate > 100000) {
+        set_err(err, "expert shape H=%u I=%u does not match layer H=%u", hidden, intermediate, L->H);
+        return 0;
+    }
+    if (expert < -1 || expert >= (int32_t)L->E) {
+        set_err(err, "expert %d outside -1..%u", expert, L->E - 1);
+        return 0;
+    }
+    const uint64_t need = moe_b200_expert_record_bytes(hidden, intermediate);
+    if (!src || src_bytes != need) {
+        set_err(err, "expert record of H=%u I=%u is %llu bytes, got %llu", hidden, intermediate,
+                (unsigned long long)need, (unsigned long long)src_bytes);
+        return 0;
+    }
+    CK(cudaSetDevice(eng->device));
+    if (!ensure_bs_layout(eng, L, intermediate, err)) return 0;
+    const uint32_t slot = expert < 0 ? L->E : (uint32_t)expert;
+    RecordPart parts[4];
+    record_parts(L, slot, parts);
+    uint64_t off = 0;
+    for (const RecordPart& r : parts) {
+        CK(cudaMemcpyAsync(r.dev, src + off, r.bytes, src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                           eng->ustream));
+        off += r.bytes;
+    }
+    // the caller may reuse its buffer once this returns
+    CK(cudaStreamSynchronize(eng->ustream));
     L->present[slot] = 1;
     L->tile_ready[slot] = 0;
     return 1;

@@ -80,6 +80,13 @@ def load(path: Path = LIB_PATH) -> C.CDLL:
     lib.moe_b200_upload_expert.restype = C.c_int
     lib.moe_b200_upload_expert.argtypes = [vp, C.c_int32, C.c_int32, vp, C.c_uint64, vp, C.c_uint64, vp,
                                            C.c_uint64, C.c_uint32, C.c_uint32, C.c_int32, cp]
+    lib.moe_b200_expert_record_bytes.restype = C.c_uint64
+    lib.moe_b200_expert_record_bytes.argtypes = [C.c_uint32, C.c_uint32]
+    lib.moe_b200_export_expert.restype = C.c_int
+    lib.moe_b200_export_expert.argtypes = [vp, C.c_int32, C.c_int32, vp, C.c_uint64, C.c_int32, cp]
+    lib.moe_b200_import_expert.restype = C.c_int
+    lib.moe_b200_import_expert.argtypes = [vp, C.c_int32, C.c_int32, vp, C.c_uint64, C.c_uint32, C.c_uint32,
+                                           C.c_int32, cp]
     lib.moe_b200_layer_forward.restype = C.c_int
     lib.moe_b200_layer_forward.argtypes = [vp, C.POINTER(LayerCfg), vp, C.c_uint32, vp, vp, vp, vp, vp, vp, cp]
     lib.moe_b200_layer_forward_host.restype = C.c_int
@@ -182,6 +189,24 @@ class Engine:
         self._check(self.lib.moe_b200_upload_expert(self.h, layer, expert, _ptr(gate), nb(gate), _ptr(up), nb(up),
                                                     _ptr(down), nb(down), hidden, intermediate, int(on_device),
                                                     self.err))
+
+    def record_bytes(self, hidden: int, intermediate: int) -> int:
+        """Bytes of one repacked-expert record for experts of this shape."""
+        return int(self.lib.moe_b200_expert_record_bytes(hidden, intermediate))
+
+    def export_expert(self, layer: int, expert: int, hidden: int, intermediate: int) -> np.ndarray:
+        """A resident expert's repacked record (expert -1: the shared expert) as host bytes."""
+        out = np.empty(self.record_bytes(hidden, intermediate), np.uint8)
+        self._check(self.lib.moe_b200_export_expert(self.h, layer, expert, _ptr(out), out.nbytes, 0, self.err))
+        return out
+
+    def import_expert(self, layer: int, expert: int, record, hidden: int, intermediate: int,
+                      on_device: bool = False):
+        """Installs a repacked record (host numpy bytes, or a device tensor with
+        on_device) as upload_expert would have left the expert, without the repack."""
+        nb = record.nbytes if isinstance(record, np.ndarray) else record.numel() * record.element_size()
+        self._check(self.lib.moe_b200_import_expert(self.h, layer, expert, _ptr(record), nb, hidden, intermediate,
+                                                    int(on_device), self.err))
 
     def upload_layer(self, li, layer: int = 0):
         """Uploads a synth.LayerInputs (host numpy GGUF bytes)."""

@@ -1,0 +1,155 @@
+"""Persisted repacked-expert cache (storage.llm_b200/expert_cache.py) on the
+CPU: the file format round trip, its checks, and the residency choice
+between a cached record and the repacking upload (against a fake engine)."""
+import os
+
+import numpy as np
+import pytest
+
+
+@pytest.fixture(scope="module")
+def ec(pkg):
+    import moe_b200.expert_cache as m
+    return m
+
+
+def _records(ec, rng, hidden, inter, n):
+    rb = ec.record_bytes(hidden, inter)
+    return [(li, e, int(rng.integers(0, 2**63)), rng.integers(0, 256, rb, dtype=np.uint8))
+            for li, e in n]
+
+
+def test_record_bytes_matches_the_library(ec, pkg):
+    import moe_b200.lib as L
+    lib = L.load()
+    for h, i in ((64, 96), (1024, 512), (2880, 2880), (7168, 2048), (896, 384), (100, 30)):
+        assert ec.record_bytes(h, i) == lib.moe_b200_expert_record_bytes(h, i) > 0
+    assert ec.record_bytes(0, 64) == lib.moe_b200_expert_record_bytes(0, 64) == 0
+
+
+def test_round_trip(ec, tmp_path):
+    rng = np.random.default_rng(0)
+    recs = _records(ec, rng, 256, 384, [(0, 0), (0, 3), (0, -1), (2, 1)])
+    path = str(tmp_path / "m.b200cache")
+    assert ec.write_cache(path, 256, 384, recs) == 4
+    f = ec.CacheFile(path)
+    assert (f.hidden, f.intermediate, f.record_bytes) == (256, 384, ec.record_bytes(256, 384))
+    for layer, expert, key, rec in recs:
+        assert f.entries[(layer, expert)].offset % ec.ALIGN == 0
+        got = f.get(layer, expert, key)
+        assert got is not None and np.array_equal(got, rec)
+        assert np.array_equal(f.get(layer, expert), rec)      # no key: any record
+        assert f.get(layer, expert, key ^ 1) is None          # other source bytes
+    assert f.get(0, 1) is None and f.get(1, 0) is None
+    f.close()
+    assert os.path.getsize(path) % ec.ALIGN == 0
+
+
+def test_empty_cache(ec, tmp_path):
+    path = str(tmp_path / "e.b200cache")
+    assert ec.write_cache(path, 128, 128, []) == 0
+    f = ec.CacheFile(path)
+    assert f.entries == {} and f.get(0, 0) is None
+
+
+def test_write_checks(ec, tmp_path):
+    rng = np.random.default_rng(1)
+    rb = ec.record_bytes(128, 256)
+    path = str(tmp_path / "w.b200cache")
+    with pytest.raises(ec.CacheError):
+        ec.write_cache(path, 128, 256, [(0, 0, 1, np.zeros(rb - 1, np.uint8))])
+    with pytest.raises(ec.CacheError):
+        rec = rng.integers(0, 256, rb, dtype=np.uint8)
+        ec.write_cache(path, 128, 256, [(0, 0, 1, rec), (0, 0, 2, rec)])
+    with pytest.raises(ec.CacheError):
+        ec.write_cache(path, 0, 256, [])
+    assert not os.path.exists(path)
+
+
+def _corrupt(path, offset, n=1):
+    with open(path, "r+b") as fh:
+        fh.seek(offset)
+        b = bytearray(fh.read(n))
+        fh.seek(offset)
+        fh.write(bytes(x ^ 0xFF for x in b))
+
+
+def test_read_checks(ec, tmp_path):
+    rng = np.random.default_rng(2)
+    recs = _records(ec, rng, 128, 128, [(0, 0), (0, 1)])
+    path = str(tmp_path / "r.b200cache")
+    ec.write_cache(path, 128, 128, recs)
+    # a flipped record byte fails that record's checksum, not the other's
+    off = ec.CacheFile(path).entries[(0, 1)].offset
+    _corrupt(path, off + 17)
+    f = ec.CacheFile(path)
+    assert np.array_equal(f.get(0, 0, recs[0][2]), recs[0][3])
+    with pytest.raises(ec.CacheError, match="checksum"):
+        f.get(0, 1, recs[1][2])
+    # a damaged entry table, a wrong magic and a truncated file are refused
+    ec.write_cache(path, 128, 128, recs)
+    _corrupt(path, ec.HEADER_BYTES + 3)
+    with pytest.raises(ec.CacheError, match="entry table"):
+        ec.CacheFile(path)
+    ec.write_cache(path, 128, 128, recs)
+    _corrupt(path, 0)
+    with pytest.raises(ec.CacheError, match="not a repacked-expert cache"):
+        ec.CacheFile(path)
+    ec.write_cache(path, 128, 128, recs)
+    size = os.path.getsize(path)
+    with open(path, "r+b") as fh:
+        fh.truncate(size - ec.ALIGN)
+    with pytest.raises(ec.CacheError, match="outside the file"):
+        ec.CacheFile(path)
+    with open(path, "r+b") as fh:
+        fh.truncate(100)
+    with pytest.raises(ec.CacheError, match="shorter than the header"):
+        ec.CacheFile(path)
+
+
+def test_source_key(ec):
+    rng = np.random.default_rng(3)
+    g, u, d = (rng.integers(0, 256, 170, dtype=np.uint8) for _ in range(3))
+    k = ec.source_key(g, u, d)
+    assert k == ec.source_key(g.copy(), u.copy(), d.copy())
+    g2 = g.copy()
+    g2[5] ^= 1
+    assert ec.source_key(g2, u, d) != k
+    assert ec.source_key(u, g, d) != k
+    # the same concatenated bytes split differently are another expert
+    assert ec.source_key(g[:-1], np.concatenate([g[-1:], u]), d) != k
+
+
+class FakeEngine:
+    def __init__(self):
+        self.calls = []
+
+    def import_expert(self, layer, expert, rec, hidden, intermediate, on_device=False):
+        self.calls.append(("import", layer, expert, bytes(rec[:4])))
+
+    def upload_expert(self, layer, expert, gate, up, down, hidden, intermediate, on_device=False):
+        self.calls.append(("upload", layer, expert))
+
+    def export_expert(self, layer, expert, hidden, intermediate):
+        rb = self.rb
+        return np.full(rb, (layer * 16 + expert) & 0xFF, np.uint8)
+
+
+def test_make_resident_prefers_a_matching_record(ec, tmp_path):
+    rng = np.random.default_rng(4)
+    H, I = 128, 256
+    src = {e: tuple(rng.integers(0, 256, 64, dtype=np.uint8) for _ in range(3)) for e in (0, 1, -1)}
+    eng = FakeEngine()
+    eng.rb = ec.record_bytes(H, I)
+    path = str(tmp_path / "res.b200cache")
+    keys = {(0, 0): ec.source_key(*src[0]), (0, -1): ec.source_key(*src[-1])}
+    assert ec.save_resident(eng, path, H, I, keys) == 2
+    cache = ec.CacheFile(path)
+    assert ec.make_resident(eng, cache, 0, 0, *src[0], H, I) is True          # cached, same source bytes
+    assert ec.make_resident(eng, cache, 0, -1, *src[-1], H, I) is True        # the shared expert
+    assert ec.make_resident(eng, cache, 0, 1, *src[1], H, I) is False         # not in the cache
+    assert ec.make_resident(eng, cache, 0, 0, *src[1], H, I) is False         # other source bytes
+    assert ec.make_resident(eng, cache, 0, 0, *src[0], H, I + 128) is False   # other shape
+    assert ec.make_resident(eng, None, 0, 0, *src[0], H, I) is False
+    assert eng.calls == [("import", 0, 0, bytes([0] * 4)), ("import", 0, -1, bytes([0xFF] * 4)),
+                         ("upload", 0, 1), ("upload", 0, 0), ("upload", 0, 0), ("upload", 0, 0)]
