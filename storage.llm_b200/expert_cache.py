@@ -155,16 +155,23 @@ class CacheFile:
             self.entries[(layer, expert)] = Entry(layer, expert, key, off, crc)
         self._map = np.memmap(path, np.uint8, mode="r") if count else None
 
-    def get(self, layer: int, expert: int, key: Optional[int] = None) -> Optional[np.ndarray]:
-        """The record of (layer, expert), checked against its CRC; None when
-        the file has none or its source key differs from `key`."""
+    def get(self, layer: int, expert: int, key: Optional[int] = None, verify: bool = True) -> Optional[np.ndarray]:
+        """The record of (layer, expert), checked against its CRC unless
+        verify is False (after verify_all); None when the file has none or its
+        source key differs from `key`."""
         e = self.entries.get((layer, expert))
         if e is None or (key is not None and e.key != (int(key) & (2**64 - 1))):
             return None
         rec = np.asarray(self._map[e.offset:e.offset + self.record_bytes])
-        if zlib.crc32(rec) != e.crc:
+        if verify and zlib.crc32(rec) != e.crc:
             raise CacheError(f"{self.path}: record of layer {layer} expert {expert} fails its checksum")
         return rec
+
+    def verify_all(self):
+        """Checks every record's CRC once (e.g. when the cache is opened), so
+        that residency events can read records with verify=False."""
+        for (layer, expert) in self.entries:
+            self.get(layer, expert)
 
     def close(self):
         self._map = None
@@ -179,12 +186,14 @@ def save_resident(engine, path: str, hidden: int, intermediate: int, keys: Dict[
 
 
 def make_resident(engine, cache: Optional[CacheFile], layer: int, expert: int, gate, up, down, hidden: int,
-                  intermediate: int) -> bool:
+                  intermediate: int, key: Optional[int] = None, verify: bool = True) -> bool:
     """Makes one expert resident: from its cached record when the cache holds
     one made from these source bytes (no repack; returns True), else by the
-    repacking upload (returns False)."""
+    repacking upload (returns False).  `key`: the source key if the caller
+    keeps it (a residency index computes it once per model), else it is
+    computed from the bytes here; `verify`: CacheFile.get's record check."""
     if cache is not None and cache.hidden == hidden and cache.intermediate == intermediate:
-        rec = cache.get(layer, expert, source_key(gate, up, down))
+        rec = cache.get(layer, expert, source_key(gate, up, down) if key is None else key, verify=verify)
         if rec is not None:
             engine.import_expert(layer, expert, rec, hidden, intermediate)
             return True

@@ -86,6 +86,9 @@ def test_read_checks(ec, tmp_path):
     assert np.array_equal(f.get(0, 0, recs[0][2]), recs[0][3])
     with pytest.raises(ec.CacheError, match="checksum"):
         f.get(0, 1, recs[1][2])
+    with pytest.raises(ec.CacheError, match="checksum"):
+        f.verify_all()
+    assert f.get(0, 1, recs[1][2], verify=False) is not None   # unchecked reads are the caller's choice
     # a damaged entry table, a wrong magic and a truncated file are refused
     ec.write_cache(path, 128, 128, recs)
     _corrupt(path, ec.HEADER_BYTES + 3)
@@ -151,5 +154,9 @@ def test_make_resident_prefers_a_matching_record(ec, tmp_path):
     assert ec.make_resident(eng, cache, 0, 0, *src[1], H, I) is False         # other source bytes
     assert ec.make_resident(eng, cache, 0, 0, *src[0], H, I + 128) is False   # other shape
     assert ec.make_resident(eng, None, 0, 0, *src[0], H, I) is False
+    cache.verify_all()
+    assert ec.make_resident(eng, cache, 0, 0, *src[0], H, I, key=keys[(0, 0)], verify=False) is True
+    assert ec.make_resident(eng, cache, 0, 0, *src[0], H, I, key=keys[(0, 0)] ^ 1, verify=False) is False
     assert eng.calls == [("import", 0, 0, bytes([0] * 4)), ("import", 0, -1, bytes([0xFF] * 4)),
-                         ("upload", 0, 1), ("upload", 0, 0), ("upload", 0, 0), ("upload", 0, 0)]
+                         ("upload", 0, 1), ("upload", 0, 0), ("upload", 0, 0), ("upload", 0, 0),
+                         ("import", 0, 0, bytes([0] * 4)), ("upload", 0, 0)]
