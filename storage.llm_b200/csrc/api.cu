@@ -345,27 +345,7 @@ int run_blockscaled(moe_b200_engine* eng, LayerWeights* L, const BsJob& job, cud
     gi.block_n = block_n;
     gi.gu_row_tiles = L->rp_i / (pair_gu ? 256 : 128);
     gi.dn_row_tiles = L->rp_h / (pair_dn ? 256 : 128);
-    if (job.router_x) {
-        // decode-sized batch, router not run yet: logits, top-k, then (in the
-        // router's last block) sort, offsets and both tile tables, one launch
-        RouteSmallArgs ra{};
-        ra.shared_rows = job.shared_rows;
-        ra.shared_base = job.shared_base;
-        ra.gi = gi;
-        ra.gu_tiles = eng->gu_tiles.as<TileEntry>();
-        ra.gu_max = token_tiles * (L->rp_i / 128);
-        ra.dn_tiles = eng->dn_tiles.as<TileEntry>();
-        ra.dn_max = token_tiles * (L->rp_h / 128);
-        ra.pos_of = eng->pos_of.as<uint32_t>();
-        ra.row_token = eng->row_token.as<uint32_t>();
-        ra.row_assign = eng->row_assign.as<uint32_t>();
-        ra.row_info = eng->row_info.as<uint32_t>();
-        ra.counter = eng->route_counter.as<uint32_t>();
-        CK(launch_router_route(job.router_x, job.router_rows, job.T, job.E, H, job.K, job.router_cfg,
-                               job.router_logits, const_cast<int32_t*>(job.ids), job.router_w, job.router_scores,
-                               errw, ra, st));
-        *launches += 1;
-    } else if (route_small_fits(n, job.E)) {
+    if (route_small_fits(n, job.E)) {
         // decode-sized batch: sort, offsets and both tile tables in one block
         CK(launch_route_small(job.ids, job.T, job.K, job.E, job.shared_rows, job.shared_base, gi,
                               eng->gu_tiles.as<TileEntry>(), token_tiles * (L->rp_i / 128),
@@ -522,14 +502,10 @@ moe_b200_engine_t* moe_b200_create(const moe_b200_init_t* init, char* err) {
     {
         const char* v = std::getenv("MOE_B200_CTA_PAIRS");
         eng->cta_pairs = !(v && v[0] == '0');
-        const char* f = std::getenv("MOE_B200_FUSED_ROUTE");
-        eng->fused_route = !(f && f[0] == '0');
     }
     eng->layers.resize(layers);
     if (eng->err_word.reserve(sizeof(uint32_t)) != cudaSuccess ||
         cudaMemset(eng->err_word.ptr, 0, sizeof(uint32_t)) != cudaSuccess ||
-        eng->route_counter.reserve(sizeof(uint32_t)) != cudaSuccess ||
-        cudaMemset(eng->route_counter.ptr, 0, sizeof(uint32_t)) != cudaSuccess ||
         cudaStreamCreateWithFlags(&eng->hstream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreate(&eng->ustream) != cudaSuccess ||
         cudaMallocHost(&eng->h_err, sizeof(uint32_t)) != cudaSuccess) {
@@ -537,7 +513,6 @@ moe_b200_engine_t* moe_b200_create(const moe_b200_init_t* init, char* err) {
         if (eng->hstream) cudaStreamDestroy(eng->hstream);
         if (eng->ustream) cudaStreamDestroy(eng->ustream);
         eng->err_word.release();
-        eng->route_counter.release();
         delete eng;
         return nullptr;
     }
@@ -556,7 +531,7 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
                       &eng->yperm, &eng->err_word, &eng->hx, &eng->hy, &eng->hyf, &eng->hids,
                       &eng->hw, &eng->hperm_out, &eng->tri, &eng->xb,
                       &eng->sfx_atoms, &eng->hb, &eng->sfh_atoms, &eng->gu_tiles, &eng->dn_tiles,
-                      &eng->pipe_ys, &eng->pipe_zero_ids, &eng->pipe_slot, &eng->route_counter};
+                      &eng->pipe_ys, &eng->pipe_zero_ids, &eng->pipe_slot};
     for (DevBuf* b : bufs) b->release();
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
     ep_release(eng->ep);
@@ -903,7 +878,6 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
     // runs on each token chunk right after the chunk lands, under the copies
     // of the chunks after it; the routed pass then leaves it out
     const bool pipe_shared = pipe && shared && bs;
-    bool defer_router = false;
     if (pipe_shared) {
         CK(eng->pipe_ys.reserve((size_t)T * H * 4));
         if (eng->pipe_zero_ids.bytes < (size_t)T * 4) {
@@ -971,8 +945,6 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
                 if (!run_blockscaled(eng, L, sj, st, nullptr, &launches, err)) return 0;
             }
         }
-    } else if (bs && eng->fused_route && router_route_fits(x, L->router.as<uint16_t>(), T, E, H, K)) {
-        defer_router = true;  // launched together with the permutation (run_blockscaled)
     } else {
         CUtensorMap rtx, rtw;
         const bool rt_tma = router_tmaps(eng, x, L->router.as<uint16_t>(), T, E, H, &rtx, &rtw);
@@ -1009,14 +981,6 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
         job.y = eng->yperm.as<float>();
         job.y_by_source = false;
         job.fp4 = fp4;
-        if (defer_router) {
-            job.router_x = x;
-            job.router_rows = L->router.as<uint16_t>();
-            job.router_cfg = rcfg;
-            job.router_logits = eng->logits.as<float>();
-            job.router_w = w;
-            job.router_scores = eng->scores.as<float>();
-        }
         if (!run_blockscaled(eng, L, job, st, ev, &launches, err)) return 0;
     } else {
     GroupInfo gi;

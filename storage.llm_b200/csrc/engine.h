@@ -127,9 +127,6 @@ struct moe_b200_engine {
     // MOE_B200_CTA_PAIRS=0 in the environment at engine creation selects the
     // one-CTA kernels instead
     bool cta_pairs = true;
-    // decode-sized batches run the router and the single-block permutation
-    // as one launch; MOE_B200_FUSED_ROUTE=0 at engine creation keeps two
-    bool fused_route = true;
     std::vector<LayerWeights> layers;
     DevBuf staging;  // GGUF bytes copied from the host before the repack
     // uploads and tile-form derivations run here and wait only for
@@ -142,7 +139,6 @@ struct moe_b200_engine {
     DevBuf g_count, g_offset, g_gu_off, g_dn_off;
     DevBuf xperm, hperm, yperm;
     DevBuf err_word;
-    DevBuf route_counter;  // launch_router_route's block counter (0 between calls)
     // block-scaled path: quantised activations and intermediate
     // (xb, hb hold a hi plane followed by a lo plane)
     DevBuf xb, sfx_atoms, hb, sfh_atoms, gu_tiles, dn_tiles;
@@ -221,15 +217,6 @@ struct BsJob {
     uint32_t ret_rows = 0;
     uint32_t ret_world = 0;
     bool fp4 = false;            // fast mode: E2M1 activations, kind::mxf4 GEMMs
-    // decode-sized single-device calls: the router was not launched yet; it
-    // runs together with the permutation (launch_router_route) on these
-    // arguments, writing `ids` and `router_w`
-    const uint16_t* router_x = nullptr;
-    const uint16_t* router_rows = nullptr;
-    RouteCfg router_cfg{};
-    float* router_logits = nullptr;
-    float* router_w = nullptr;
-    float* router_scores = nullptr;
 };
 
 // Enqueues the pipeline on `st`; fills the engine's permutation buffers

@@ -153,26 +153,6 @@ cudaError_t launch_route_small(const int32_t* ids, uint32_t T, uint32_t K, uint3
                                uint32_t shared_base, GroupInfo gi, TileEntry* gu_tiles, uint32_t gu_max,
                                TileEntry* dn_tiles, uint32_t dn_max, uint32_t* pos_of, uint32_t* row_token,
                                uint32_t* row_assign, uint32_t* row_info, uint32_t* err, cudaStream_t st, bool pdl);
-// The permutation's outputs and layout (launch_route_small's arguments after
-// the ids), for the router that runs it in its own last block.
-struct RouteSmallArgs {
-    uint32_t shared_rows, shared_base;
-    GroupInfo gi;
-    TileEntry* gu_tiles;
-    uint32_t gu_max;
-    TileEntry* dn_tiles;
-    uint32_t dn_max;
-    uint32_t *pos_of, *row_token, *row_assign, *row_info;
-    uint32_t* counter;  // a device word that is 0 between calls (the launch leaves it 0)
-};
-// Decode-sized batches: the small-batch router (logits + top-k) and the
-// single-block permutation in one launch -- the router block that finishes
-// last runs the permutation.  Applies when router_route_fits(); same outputs
-// as launch_router followed by launch_route_small.
-bool router_route_fits(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K);
-cudaError_t launch_router_route(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
-                                const RouteCfg& rc, float* logits, int32_t* ids, float* wout, float* scores,
-                                uint32_t* err, const RouteSmallArgs& ra, cudaStream_t st);
 // Generic pieces of the stable counting sort, used by the grouping utility.
 struct AssignRec {
     uint32_t token_index, layer, expert;

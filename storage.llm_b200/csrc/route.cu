@@ -622,12 +622,14 @@ constexpr int kRfMaxDots = 64;          // tb * E per block (8 threads each, 512
 constexpr int kRfMaxE = 64;
 constexpr uint32_t kRfSmemMax = 200 * 1024;
 
-__device__ __forceinline__ void router_fused_body(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
-                                                  uint32_t T, uint32_t E, uint32_t H, uint32_t K, uint32_t tb,
-                                                  const RouteCfg& rc, float* __restrict__ logits,
-                                                  int32_t* __restrict__ ids, float* __restrict__ wout,
-                                                  float* __restrict__ scores, uint32_t* __restrict__ err,
-                                                  uint8_t* rf_smem, uint64_t& bar) {
+__global__ void __launch_bounds__(512) router_fused_kernel(const uint16_t* __restrict__ x,
+                                                           const uint16_t* __restrict__ w, uint32_t T, uint32_t E,
+                                                           uint32_t H, uint32_t K, uint32_t tb, RouteCfg rc,
+                                                           float* __restrict__ logits, int32_t* __restrict__ ids,
+                                                           float* __restrict__ wout, float* __restrict__ scores,
+                                                           uint32_t* __restrict__ err) {
+    extern __shared__ __align__(16) uint8_t rf_smem[];
+    __shared__ uint64_t bar;
     const uint32_t pitch = H * 2 + 32;  // bytes per staged row
     uint8_t* xs = rf_smem;                               // [tb] rows
     uint8_t* ws = rf_smem + (size_t)tb * pitch;          // [E] rows
@@ -709,17 +711,6 @@ __device__ __forceinline__ void router_fused_body(const uint16_t* __restrict__ x
             topk_token(lg + (size_t)tt * E, t0 + tt, E, K, rc, ids, wout, scores);
         }
     }
-}
-
-__global__ void __launch_bounds__(512) router_fused_kernel(const uint16_t* __restrict__ x,
-                                                           const uint16_t* __restrict__ w, uint32_t T, uint32_t E,
-                                                           uint32_t H, uint32_t K, uint32_t tb, RouteCfg rc,
-                                                           float* __restrict__ logits, int32_t* __restrict__ ids,
-                                                           float* __restrict__ wout, float* __restrict__ scores,
-                                                           uint32_t* __restrict__ err) {
-    extern __shared__ __align__(16) uint8_t rf_smem[];
-    __shared__ uint64_t bar;
-    router_fused_body(x, w, T, E, H, K, tb, rc, logits, ids, wout, scores, err, rf_smem, bar);
 }
 
 // ---------------------------------------------------------------------------
@@ -854,7 +845,7 @@ __global__ void __launch_bounds__(1024) sort_scan_kernel(uint32_t* __restrict__ 
 // entries).  1024 threads; warp w sorts the contiguous segment
 // [w * seg, (w + 1) * seg) of the assignments, seg a multiple of 32.
 // ---------------------------------------------------------------------------
-constexpr uint32_t kSmallN = 8192;  // assignments (8 per lane in a block of 32 warps)
+constexpr uint32_t kSmallN = 8192;  // assignments (8 per lane)
 constexpr uint32_t kSmallE = 256;   // experts
 
 __device__ __forceinline__ void fill_tiles(const uint32_t* cnt, const uint32_t* off, const uint32_t* toff,
@@ -887,49 +878,35 @@ __device__ __forceinline__ uint32_t row_tile_info(uint32_t tile_off, uint32_t n,
     return ((tile_off / gi.gu_row_tiles + n / gi.block_n) << 8) | (n % gi.block_n);
 }
 
-// Shared-memory arrays of route_small_body for NW warps.
-template <int NW>
-struct RouteSmallSmem {
-    uint32_t cnt[NW][kSmallE];  // per-warp counts, then each warp's base within the expert
-    uint32_t gcnt[kSmallE + 2], goff[kSmallE + 2], gut[kSmallE + 2], dnt[kSmallE + 2];
-};
-
-// The single-block permutation for a block of NW warps (NW * 32 threads):
-// a stable counting sort of the n assignments by expert (warp w takes the
-// w-th segment of the assignments, so the order inside an expert is the
-// assignment order whatever NW is), the group offsets, both tile tables,
-// each permuted row's token, assignment and tile position.  The ids are read
-// through L2 (ld.global.cg), so a router block of the same grid that stored
-// them before the grid-wide counter handed this block the work is seen.
-template <int NW>
-__device__ __forceinline__ void route_small_body(const int32_t* ids, uint32_t n, uint32_t K, uint32_t E,
-                                                 uint32_t shared_rows, uint32_t shared_base, const GroupInfo& gi,
-                                                 TileEntry* __restrict__ gu_tiles, uint32_t gu_max,
-                                                 TileEntry* __restrict__ dn_tiles, uint32_t dn_max,
-                                                 uint32_t* __restrict__ pos_of, uint32_t* __restrict__ row_token,
-                                                 uint32_t* __restrict__ row_assign, uint32_t* __restrict__ row_info,
-                                                 uint32_t* __restrict__ err, RouteSmallSmem<NW>& sm) {
-    constexpr uint32_t kPer = kSmallN / (NW * 32);  // assignments per lane at most
-    auto& cnt = sm.cnt;
-    uint32_t* gcnt = sm.gcnt;
-    uint32_t* goff = sm.goff;
-    uint32_t* gut = sm.gut;
-    uint32_t* dnt = sm.dnt;
+__global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t K,
+                                                           uint32_t E, uint32_t shared_rows, uint32_t shared_base,
+                                                           GroupInfo gi,
+                                                           TileEntry* __restrict__ gu_tiles, uint32_t gu_max,
+                                                           TileEntry* __restrict__ dn_tiles, uint32_t dn_max,
+                                                           uint32_t* __restrict__ pos_of,
+                                                           uint32_t* __restrict__ row_token,
+                                                           uint32_t* __restrict__ row_assign,
+                                                           uint32_t* __restrict__ row_info,
+                                                           uint32_t* __restrict__ err) {
+    __shared__ uint32_t cnt[32][kSmallE];  // per-warp counts, then each warp's base within the expert
+    __shared__ uint32_t gcnt[kSmallE + 2], goff[kSmallE + 2], gut[kSmallE + 2], dnt[kSmallE + 2];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t G = E + (shared_rows ? 1 : 0);
-    for (uint32_t i = threadIdx.x; i < NW * kSmallE; i += blockDim.x) (&cnt[0][0])[i] = 0;
+    pdl_wait();  // the router's ids
+    pdl_trigger();
+    for (uint32_t i = threadIdx.x; i < 32 * kSmallE; i += blockDim.x) (&cnt[0][0])[i] = 0;
     __syncthreads();
-    const uint32_t seg = ceil_div(ceil_div(n, (uint32_t)NW), 32u) * 32u;
+    const uint32_t seg = ceil_div(ceil_div(n, 32u), 32u) * 32u;
     const uint32_t s0 = warp * seg;
     const unsigned lt = (1u << lane) - 1u;
-    uint32_t rk[kPer];
-    int32_t bk[kPer];
+    uint32_t rk[kSmallN / 1024];
+    int32_t bk[kSmallN / 1024];
 #pragma unroll
-    for (uint32_t s = 0; s < kPer; ++s) {
+    for (uint32_t s = 0; s < kSmallN / 1024; ++s) {
         const uint32_t i = s0 + s * 32 + lane;
         int32_t b = -1;
         if (s * 32 < seg && i < n) {
-            b = __ldcg(ids + i);
+            b = ids[i];
             if (b < 0 || (uint32_t)b >= E) {
                 record_error(err, kErrBadExpert);
                 b = -1;
@@ -948,7 +925,7 @@ __device__ __forceinline__ void route_small_body(const int32_t* ids, uint32_t n,
     // assignments precede warp w + 1's), and the expert's total
     for (uint32_t b = threadIdx.x; b < E; b += blockDim.x) {
         uint32_t run = 0;
-        for (uint32_t w = 0; w < (uint32_t)NW; ++w) {
+        for (uint32_t w = 0; w < 32; ++w) {
             const uint32_t c = cnt[w][b];
             cnt[w][b] = run;
             run += c;
@@ -1009,7 +986,7 @@ __device__ __forceinline__ void route_small_body(const int32_t* ids, uint32_t n,
     }
     // destinations
 #pragma unroll
-    for (uint32_t s = 0; s < kPer; ++s) {
+    for (uint32_t s = 0; s < kSmallN / 1024; ++s) {
         const uint32_t i = s0 + s * 32 + lane;
         const int32_t b = bk[s];
         if (b >= 0) {
@@ -1029,52 +1006,6 @@ __device__ __forceinline__ void route_small_body(const int32_t* ids, uint32_t n,
     }
     if (gu_tiles) fill_tiles(gcnt, goff, gut, G, gi.gu_row_tiles, gi.block_n, gu_tiles, gu_max);
     if (dn_tiles) fill_tiles(gcnt, goff, dnt, G, gi.dn_row_tiles, gi.block_n, dn_tiles, dn_max);
-}
-
-__global__ void __launch_bounds__(1024) route_small_kernel(const int32_t* __restrict__ ids, uint32_t n, uint32_t K,
-                                                           uint32_t E, uint32_t shared_rows, uint32_t shared_base,
-                                                           GroupInfo gi,
-                                                           TileEntry* __restrict__ gu_tiles, uint32_t gu_max,
-                                                           TileEntry* __restrict__ dn_tiles, uint32_t dn_max,
-                                                           uint32_t* __restrict__ pos_of,
-                                                           uint32_t* __restrict__ row_token,
-                                                           uint32_t* __restrict__ row_assign,
-                                                           uint32_t* __restrict__ row_info,
-                                                           uint32_t* __restrict__ err) {
-    __shared__ RouteSmallSmem<32> sm;
-    pdl_wait();  // the router's ids
-    pdl_trigger();
-    route_small_body<32>(ids, n, K, E, shared_rows, shared_base, gi, gu_tiles, gu_max, dn_tiles, dn_max, pos_of,
-                         row_token, row_assign, row_info, err, sm);
-}
-
-// router_fused_kernel, then the permutation in the grid's last block: every
-// block stores its tokens' ids and weights, fences them and counts itself on
-// ra.counter; the block that brings the count to gridDim.x runs
-// route_small_body over all the ids (in the shared memory the router no
-// longer needs) and puts the counter back to 0 for the next launch.  A block
-// whose row copies timed out still counts itself, so the permutation always
-// runs (and reports ids out of range); the timeout is in the error word.
-__global__ void __launch_bounds__(512, 1) router_route_kernel(const uint16_t* __restrict__ x,
-                                                           const uint16_t* __restrict__ w, uint32_t T, uint32_t E,
-                                                           uint32_t H, uint32_t K, uint32_t tb, RouteCfg rc,
-                                                           float* __restrict__ logits, int32_t* __restrict__ ids,
-                                                           float* __restrict__ wout, float* __restrict__ scores,
-                                                           uint32_t* __restrict__ err, RouteSmallArgs ra) {
-    extern __shared__ __align__(16) uint8_t rf_smem[];
-    __shared__ uint64_t bar;
-    __shared__ uint32_t last;
-    router_fused_body(x, w, T, E, H, K, tb, rc, logits, ids, wout, scores, err, rf_smem, bar);
-    __threadfence();  // this thread's ids and weights, before the count
-    __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(ra.counter, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    route_small_body<16>(ids, T * K, K, E, ra.shared_rows, ra.shared_base, ra.gi, ra.gu_tiles, ra.gu_max,
-                         ra.dn_tiles, ra.dn_max, ra.pos_of, ra.row_token, ra.row_assign, ra.row_info, err,
-                         *reinterpret_cast<RouteSmallSmem<16>*>(rf_smem));
-    if (threadIdx.x == 0) *ra.counter = 0;
 }
 
 // Destination of every assignment a = t*K + j, and for every permuted row:
@@ -1181,37 +1112,6 @@ bool router_wants_tma(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t
     if (T == 0 || router_fused_tb(x, w, T, E, H)) return false;
     return H % 8 == 0 && !(reinterpret_cast<uintptr_t>(x) & 15) && !(reinterpret_cast<uintptr_t>(w) & 15) &&
            (H & ~15u) > 0;
-}
-
-bool router_route_fits(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K) {
-    return T > 0 && router_fused_tb(x, w, T, E, H) != 0 && route_small_fits(T * K, E);
-}
-
-cudaError_t launch_router_route(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
-                                const RouteCfg& rc_in, float* logits, int32_t* ids, float* wout, float* scores,
-                                uint32_t* err, const RouteSmallArgs& ra, cudaStream_t st) {
-    if (!router_route_fits(x, w, T, E, H, K) || !ra.counter) return cudaErrorInvalidValue;
-    RouteCfg rc = rc_in;
-    // the group limit applies under the reference's conditions only (as launch_router)
-    if (!(rc.sigmoid && rc.n_group > 1 && rc.topk_group > 0 && rc.topk_group < rc.n_group && E % rc.n_group == 0))
-        rc.n_group = rc.topk_group = 0;
-    if (rc.n_group > 256) return cudaErrorInvalidValue;
-    const uint32_t tb = router_fused_tb(x, w, T, E, H);
-    static uint64_t attr_set = 0;  // one bit per device
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 64 && !((attr_set >> dev) & 1u)) {
-        e = cudaFuncSetAttribute(router_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRfSmemMax);
-        if (e != cudaSuccess) return e;
-        attr_set |= 1ull << dev;
-    }
-    const size_t smem = std::max((size_t)(tb + E) * (H * 2 + 32) + (size_t)tb * E * 4, sizeof(RouteSmallSmem<16>));
-    // a plain launch: it starts after the previous kernel on the stream has
-    // finished, so two launches never share the counter
-    router_route_kernel<<<ceil_div(T, tb), 512, smem, st>>>(x, w, T, E, H, K, tb, rc, logits, ids, wout, scores, err,
-                                                           ra);
-    return cudaGetLastError();
 }
 
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, uint32_t T, uint32_t E, uint32_t H, uint32_t K,
