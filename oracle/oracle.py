@@ -273,6 +273,9 @@ class Ref:
                                       C.c_uint32, _i32p, _f32p, _f32p]
         L.ref_moe_layer.restype = C.c_int
         L.ref_moe_layer.argtypes = [C.c_void_p, C.POINTER(RefLayer), _u16p, C.c_uint32, _f32p, _i32p, _f32p]
+        L.ref_moe_layer_engine.restype = C.c_int
+        L.ref_moe_layer_engine.argtypes = [C.c_void_p, C.POINTER(RefLayer), _u16p, C.c_uint32, _f32p, _i32p, _f32p,
+                                           C.c_char_p]
         L.ref_moe_block.restype = C.c_int
         L.ref_moe_block.argtypes = [C.c_void_p, C.POINTER(RefBlock), _u16p, _f32p, C.c_uint32, _f32p, _i32p,
                                     _f32p]
@@ -307,6 +310,26 @@ class Ref:
         if not self.lib.ref_moe_layer(self.engine, C.byref(d), _p(x, _u16p), T, _p(y, _f32p), _p(ids, _i32p),
                                       _p(w, _f32p)):
             raise RuntimeError("reference layer failed")
+        return y, ids, w
+
+    def moe_layer_engine(self, li, shard_path: str, x=None):
+        """The layer through the reference's moe_layer_moe_mlp_f32 itself, the
+        experts as tensor records over a shard file written to shard_path
+        (ref_harness.cpp ref_moe_layer_engine); returns y, ids, w."""
+        s = li.shape
+        x = _c(li.x if x is None else x, np.uint16)
+        T = x.shape[0]
+        keep = [_c(li.router, np.uint16), _c(li.gate, np.uint8), _c(li.up, np.uint8), _c(li.down, np.uint8),
+                _c(li.shared_gate, np.uint8), _c(li.shared_up, np.uint8), _c(li.shared_down, np.uint8)]
+        d = RefLayer(s.hidden, s.intermediate, s.experts, s.top_k, _p(keep[0], _u16p), _p(keep[1], _u8p),
+                     _p(keep[2], _u8p), _p(keep[3], _u8p), _p(keep[4], _u8p), _p(keep[5], _u8p),
+                     _p(keep[6], _u8p))
+        y = np.zeros((T, s.hidden), np.float32)
+        ids = np.zeros((T, s.top_k), np.int32)
+        w = np.zeros((T, s.top_k), np.float32)
+        if not self.lib.ref_moe_layer_engine(self.engine, C.byref(d), _p(x, _u16p), T, _p(y, _f32p),
+                                             _p(ids, _i32p), _p(w, _f32p), str(shard_path).encode()):
+            raise RuntimeError("reference layer function failed")
         return y, ids, w
 
     def moe_block(self, li, blk: Block, hidden=None, x=None):

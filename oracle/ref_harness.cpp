@@ -22,6 +22,9 @@
 // ref_moe_block adds the optional parts of Gemma-style blocks around the
 // experts through the reference's own functions for them (the MoE pre-norm,
 // post-FFW norms 1/2/final, expert down scales, shared-expert gate).
+// ref_moe_layer_engine runs moe_layer_moe_mlp_f32 itself, its experts filed
+// as tensor records over a shard file, which pins the leaf composition above
+// to the layer function the engine calls.
 // Weights are passed in the reference's GGUF MXFP4 byte layout (17-byte
 // blocks per 32 K-elements, tensor_layout.cpp.inc:174-176).
 #include "moe_engine/src/moe_pc_engine.cpp"
@@ -472,6 +475,157 @@ int ref_group_tokens_by_expert(const moe_token_expert_assignment_t* a, uint32_t 
                                moe_expert_batch_t* batches, uint32_t max_batches,
                                uint32_t* batch_count) {
     return moe_pc_group_tokens_by_expert(a, n, sorted, batches, max_batches, batch_count);
+}
+
+// The layer through moe_layer_moe_mlp_f32 itself (generation_mlp.cpp.inc:
+// 776-1442), one call per token as the engine makes it
+// (generation_forward.cpp.inc:212-215).  The experts become tensor records
+// the way the codec table makes them: their GGUF MXFP4 bytes are written to
+// `shard_path` (gate, up, down of expert 0, then expert 1, ...), each
+// projection gets a moe_tensor_record over its byte range finished by the
+// reference's finalize_tensor_layout with the MXFP4 encoding, and
+// tensor_slots_set files it under (layer 0, expert, projection); the layer
+// function then finds, maps and decodes them through find_tensor_record,
+// get_or_map_tensor_shard and moe_dot_tensor_record_row.  The shared expert
+// is the layer's dense MLP (ffn_gate/ffn_up/ffn_down.weight as MXFP4 tensors,
+// which moe_layer_common_dense_mlp_f32 finds first, :596-727, 833-860), the
+// router as in ref_moe_layer.  The engine's residency bookkeeping (expert
+// states, which the prefetch and heat updates consult) is emptied, so the
+// call computes without tier moves; the phase is prefill (no speculative
+// prefetch).  Input: s->norm = the token's row; hidden = 0, so the residual
+// add leaves hidden = mlp; y_f32 receives s->mlp, ids and w the router's
+// selection.  Any block parts a ref_moe_block call left in the engine are
+// removed first: this entry point is the plain layer.
+int ref_moe_layer_engine(void* eng, const ref_layer_desc* d, const uint16_t* x_bf16, uint32_t tokens,
+                         float* y_f32, int32_t* out_ids, float* out_w, const char* shard_path) {
+    mxcsr_guard guard;
+    moe_pc_engine* engine = static_cast<moe_pc_engine*>(eng);
+    if (!engine || !d || !x_bf16 || !y_f32 || !shard_path) return 0;
+    const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, K = d->top_k;
+    const int32_t layer = 0;
+    const uint64_t row_h = (uint64_t)((H + 31u) / 32u) * 17u;
+    const uint64_t row_i = (uint64_t)((I + 31u) / 32u) * 17u;
+    const uint64_t gu_bytes = (uint64_t)I * row_h, dn_bytes = (uint64_t)H * row_i;
+
+    // the shard file: [expert][gate, up, down]
+    {
+        FILE* f = std::fopen(shard_path, "wb");
+        if (!f) return 0;
+        bool ok = true;
+        for (uint32_t e = 0; e < E && ok; ++e) {
+            ok = std::fwrite(d->gate + (uint64_t)e * gu_bytes, 1, gu_bytes, f) == gu_bytes &&
+                 std::fwrite(d->up + (uint64_t)e * gu_bytes, 1, gu_bytes, f) == gu_bytes &&
+                 std::fwrite(d->down + (uint64_t)e * dn_bytes, 1, dn_bytes, f) == dn_bytes;
+        }
+        ok = std::fclose(f) == 0 && ok;
+        if (!ok) return 0;
+    }
+    // a shard number of its own per call (past the fast-slot cache), so a
+    // mapping of an earlier call's file is never reused
+    static std::atomic<uint32_t> next_shard{moe_SOURCE_MMAP_FAST_SLOTS + 1u};
+    const uint32_t shard = next_shard.fetch_add(1u);
+    engine->tensor_paths.push_back(shard_path);
+    const uint16_t path_index = (uint16_t)(engine->tensor_paths.size() - 1u);
+    tensor_slots_reset(engine);
+    const moe_projection_t projs[3] = {moe_PROJ_GATE, moe_PROJ_UP, moe_PROJ_DOWN};
+    uint64_t offset = 0;
+    for (uint32_t e = 0; e < E; ++e) {
+        for (int p = 0; p < 3; ++p) {
+            const bool down = projs[p] == moe_PROJ_DOWN;
+            moe_tensor_record rec{};
+            rec.info.weight_byte_offset = offset;
+            rec.info.weight_byte_length = down ? dn_bytes : gu_bytes;
+            rec.info.part = 0;
+            rec.info.shard = shard;
+            rec.info.layer = (uint32_t)layer;
+            rec.info.expert = e;
+            rec.info.proj = projs[p];
+            rec.info.rows = down ? H : I;
+            rec.info.cols = down ? I : H;
+            rec.info.groups = (rec.info.cols + 31u) / 32u;
+            rec.info.group_size = 32u;
+            rec.resolved_path_index = path_index;
+            finalize_tensor_layout(&rec, moe_WEIGHT_ENCODING_MXFP4);
+            engine->tensors.push_back(rec);
+            tensor_slots_set(engine, layer, (int)e, projs[p], engine->tensors.size() - 1u);
+            offset += rec.info.weight_byte_length;
+        }
+    }
+
+    // router, and the shared expert as the layer's dense MLP
+    clear_router_scale(engine, layer);
+    {
+        moe_raw_tensor_cache_entry r{};
+        r.base = reinterpret_cast<const uint8_t*>(d->router_bf16);
+        r.bytes = (uint64_t)E * H * 2ull;
+        r.rows = E;
+        r.cols = H;
+        r.scalar_encoding = moe_RAW_SCALAR_BF16;
+        r.weight_format = moe_WEIGHT_ENCODING_RAW_BF16;
+        std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
+        engine->raw_tensor_cache[router_cache_key(layer)] = r;
+    }
+    const char* block_parts[] = {"pre_ffw_norm_2.weight", "post_ffw_norm_1.weight", "post_ffw_norm_2.weight",
+                                 "post_ffw_norm.weight", "ffn_down_exps.scale", "shared_expert_gate.weight"};
+    for (const char* sfx : block_parts) put_common(engine, layer, sfx, nullptr, 0, 0, 0, 0, 0);
+    const bool shared = d->shared_gate && d->shared_up && d->shared_down;
+    struct {
+        const char* suffix;
+        const uint8_t* data;
+        uint32_t rows, cols;
+    } dense[3] = {{"ffn_gate.weight", d->shared_gate, I, H},
+                  {"ffn_up.weight", d->shared_up, I, H},
+                  {"ffn_down.weight", d->shared_down, H, I}};
+    for (const auto& t : dense) {
+        std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
+        const uint64_t key = common_key(layer, t.suffix);
+        if (!shared) {
+            engine->raw_tensor_cache.erase(key);
+            continue;
+        }
+        moe_raw_tensor_cache_entry e{};
+        e.base = t.data;
+        e.weight_row_bytes = (uint64_t)((t.cols + 31u) / 32u) * 17u;
+        e.bytes = (uint64_t)t.rows * e.weight_row_bytes;
+        e.rows = t.rows;
+        e.cols = t.cols;
+        e.scalar_encoding = moe_RAW_SCALAR_UNKNOWN;
+        e.weight_format = moe_WEIGHT_ENCODING_MXFP4;
+        engine->raw_tensor_cache[key] = e;
+    }
+
+    {
+        std::lock_guard<std::mutex> lock(engine->map_mutex);
+        engine->expert_states.clear();
+    }
+    engine->generation_phase.store(moe_GEN_PHASE_PREFILL, std::memory_order_release);
+    moe_storage_constants_t c = moe_engine_storage_constants_or_static(engine);
+    c.hidden_size = H;
+    c.expert_intermediate_size = I;
+    c.experts_per_moe_layer = E;
+    c.first_moe_layer = 0;
+    c.last_moe_layer = 0;
+
+    moe_decode_scratch s;
+    s.mlp.resize(H);
+    s.shared.resize(H);
+    s.expert.resize(H);
+    s.norm.resize(H);
+    s.residual.resize(H);
+    s.gate.resize(I);
+    s.up.resize(I);
+    s.expert_work.resize(K);
+    std::vector<float> hidden(H);
+    for (uint32_t t = 0; t < tokens; ++t) {
+        for (uint32_t h = 0; h < H; ++h) s.norm[h] = bf16_to_f32(x_bf16[(uint64_t)t * H + h]);
+        std::fill(hidden.begin(), hidden.end(), 0.0f);
+        if (!moe_layer_moe_mlp_f32(engine, layer, &s, hidden.data(), &c)) return 0;
+        if (s.selected_experts.size() != K || s.selected_weights.size() != K) return 0;
+        std::memcpy(y_f32 + (uint64_t)t * H, s.mlp.data(), (size_t)H * sizeof(float));
+        if (out_ids) for (uint32_t j = 0; j < K; ++j) out_ids[(uint64_t)t * K + j] = s.selected_experts[j];
+        if (out_w) for (uint32_t j = 0; j < K; ++j) out_w[(uint64_t)t * K + j] = s.selected_weights[j];
+    }
+    return 1;
 }
 
 }  // extern "C"

@@ -275,3 +275,37 @@ def test_oracle_struct_layout(oracle_mod, tmp_path):
     assert int(got["size"]) == ctypes.sizeof(L)
     for fname, _ in L._fields_:
         assert int(got[fname]) == getattr(L, fname).offset, fname
+
+
+LAYER_FUNCTION_SHAPES = {
+    "e12_k3": dict(tokens=12, experts=12, top_k=3),
+    "shared": dict(name="s2", hidden=96, intermediate=64, tokens=9, shared=True),
+    "norm_topk": dict(name="nt", hidden=64, intermediate=48, experts=8, top_k=4, tokens=6, norm_topk=True),
+    # config 4's hidden and intermediate sizes with the shared expert, 12 experts, top-8
+    "c4_dims": dict(name="c4d", hidden=7168, intermediate=2048, experts=12, top_k=8, tokens=2, shared=True),
+    **EXTREME_SHAPES,
+}
+
+
+@pytest.mark.parametrize("name", sorted(LAYER_FUNCTION_SHAPES))
+def test_reference_layer_function_matches_composed_layer(name, ref_lib, port, synth, tmp_path):
+    """The reference's moe_layer_moe_mlp_f32 itself -- its experts found as
+    tensor records over a shard file, mapped and decoded by the engine's own
+    record path -- against the leaf composition (ref_moe_layer) and the
+    oracle restatement, bit for bit."""
+    shape = synth.small_shape(name=name, **{k: v for k, v in LAYER_FUNCTION_SHAPES[name].items() if k != "name"})
+    li = synth.make_layer(shape, seed=61)
+    ref = ref_lib.Ref(ref_lib.metadata_json(shape.top_k, norm_topk=shape.norm_topk))
+    try:
+        y_fn, i_fn, w_fn = ref.moe_layer_engine(li, tmp_path / "shard.bin")
+        y_c, i_c, w_c = ref.moe_layer(li)
+    finally:
+        ref.close()
+    assert np.array_equal(i_fn, i_c)
+    assert np.array_equal(bits(w_fn), bits(w_c))
+    assert np.array_equal(bits(y_fn), bits(y_c))
+    y_p, i_p, w_p, ties = port.moe_layer(li)
+    assert ties == 0
+    assert np.array_equal(i_fn, i_p)
+    assert np.array_equal(bits(w_fn), bits(w_p))
+    assert np.array_equal(bits(y_fn), bits(y_p))
