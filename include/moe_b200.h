@@ -203,6 +203,33 @@ MOE_B200_API int moe_b200_import_expert(moe_b200_engine_t* engine, int32_t layer
                            uint64_t src_bytes, uint32_t hidden, uint32_t intermediate, int32_t src_on_device,
                            char* err);
 
+/* The cache file of such records, read from C (host code, no device needed).
+ * The file is the one storage.llm_b200/expert_cache.py writes:
+ *   - a 4096-byte header: magic "MOEB200R", version, H, I, record size,
+ *     entry count, the entry table's offset and CRC-32;
+ *   - 64-byte entries: layer, expert, source key, record offset, CRC-32;
+ *   - records at 4096-aligned offsets.
+ * Each record is keyed by the source bytes it was made from:
+ * moe_b200_source_key is BLAKE2b-64 (RFC 7693) over the gate, up and down
+ * GGUF bytes, each preceded by its byte count as 8 little-endian bytes.
+ * open maps the file read-only and checks the header and the entry table;
+ * it returns NULL with `err` set otherwise.  record returns the record of
+ * (layer, expert) (expert -1: the shared expert) inside the mapping, valid
+ * until close.  It returns NULL with err[0] == 0 when the file holds no
+ * record of that slot made from `source_key`.  With verify != 0 it also
+ * checks the record's CRC-32, and returns NULL with `err` set on a mismatch.
+ * A record found goes to moe_b200_import_expert with
+ * moe_b200_expert_record_bytes(H, I) bytes. */
+typedef struct moe_b200_expert_cache moe_b200_expert_cache_t;
+MOE_B200_API uint64_t moe_b200_source_key(const uint8_t* gate, uint64_t gate_bytes, const uint8_t* up,
+                           uint64_t up_bytes, const uint8_t* down, uint64_t down_bytes);
+MOE_B200_API moe_b200_expert_cache_t* moe_b200_expert_cache_open(const char* path, char* err);
+MOE_B200_API void moe_b200_expert_cache_close(moe_b200_expert_cache_t* cache);
+MOE_B200_API int moe_b200_expert_cache_info(const moe_b200_expert_cache_t* cache, uint32_t* hidden,
+                           uint32_t* intermediate, uint64_t* record_bytes, uint32_t* entries);
+MOE_B200_API const uint8_t* moe_b200_expert_cache_record(const moe_b200_expert_cache_t* cache, int32_t layer,
+                           int32_t expert, uint64_t source_key, int32_t verify, char* err);
+
 /* The block tensors of a layer (copied into the engine; NULL clears them).
  * The router of the layer must be uploaded first.  The layer's forward then
  * applies them (moe_b200_block_forward when pre_norm2 or router_scale is

@@ -19,7 +19,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OBJ = HERE / "_build"
 LIB = HERE / "libmoe_b200.so"
-SOURCES = ["api.cu", "route.cu", "repack.cu", "gemm_tc.cu", "gemm_simt.cu", "group.cu", "group_noalloc.cu", "gemm_bs.cu", "block.cu",
+SOURCES = ["api.cu", "route.cu", "repack.cu", "gemm_tc.cu", "gemm_simt.cu", "group.cu", "group_noalloc.cu", "gemm_bs.cu", "block.cu", "cache.cu",
            "ep.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -87,6 +87,16 @@ def load(path: Path = LIB_PATH) -> C.CDLL:
     lib.moe_b200_import_expert.restype = C.c_int
     lib.moe_b200_import_expert.argtypes = [vp, C.c_int32, C.c_int32, vp, C.c_uint64, C.c_uint32, C.c_uint32,
                                            C.c_int32, cp]
+    lib.moe_b200_source_key.restype = C.c_uint64
+    lib.moe_b200_source_key.argtypes = [vp, C.c_uint64, vp, C.c_uint64, vp, C.c_uint64]
+    lib.moe_b200_expert_cache_open.restype = vp
+    lib.moe_b200_expert_cache_open.argtypes = [C.c_char_p, cp]
+    lib.moe_b200_expert_cache_close.argtypes = [vp]
+    lib.moe_b200_expert_cache_info.restype = C.c_int
+    lib.moe_b200_expert_cache_info.argtypes = [vp, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                               C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)]
+    lib.moe_b200_expert_cache_record.restype = vp
+    lib.moe_b200_expert_cache_record.argtypes = [vp, C.c_int32, C.c_int32, C.c_uint64, C.c_int32, cp]
     lib.moe_b200_layer_forward.restype = C.c_int
     lib.moe_b200_layer_forward.argtypes = [vp, C.POINTER(LayerCfg), vp, C.c_uint32, vp, vp, vp, vp, vp, vp, cp]
     lib.moe_b200_layer_forward_host.restype = C.c_int

@@ -160,3 +160,76 @@ def test_make_resident_prefers_a_matching_record(ec, tmp_path):
     assert eng.calls == [("import", 0, 0, bytes([0] * 4)), ("import", 0, -1, bytes([0xFF] * 4)),
                          ("upload", 0, 1), ("upload", 0, 0), ("upload", 0, 0), ("upload", 0, 0),
                          ("import", 0, 0, bytes([0] * 4)), ("upload", 0, 0)]
+
+
+# -- the C reader of the same files (moe_b200_expert_cache_*, no device) -----
+
+@pytest.fixture(scope="module")
+def clib(pkg):
+    import moe_b200.lib as L
+    return L.load()
+
+
+def _c_key(clib, g, u, d):
+    import ctypes as C
+    arrs = [np.ascontiguousarray(a, np.uint8) for a in (g, u, d)]
+    ptr = lambda a: a.ctypes.data_as(C.c_void_p) if a.size else None
+    return int(clib.moe_b200_source_key(ptr(arrs[0]), arrs[0].nbytes, ptr(arrs[1]), arrs[1].nbytes,
+                                        ptr(arrs[2]), arrs[2].nbytes))
+
+
+def test_c_source_key_matches_python(ec, clib):
+    rng = np.random.default_rng(7)
+    # lengths around the 128-byte BLAKE2b block, an empty part, a multi-block part
+    for sizes in ((0, 0, 0), (1, 2, 3), (104, 0, 0), (120, 8, 0), (128, 128, 128), (127, 129, 256), (5000, 17, 1),
+                  (170, 170, 340)):
+        g, u, d = (rng.integers(0, 256, n, dtype=np.uint8) for n in sizes)
+        assert _c_key(clib, g, u, d) == ec.source_key(g, u, d), sizes
+
+
+def test_c_reader_matches_python_writer(ec, clib, tmp_path):
+    import ctypes as C
+    rng = np.random.default_rng(8)
+    H, I = 256, 384
+    recs = _records(ec, rng, H, I, [(0, 0), (0, 5), (0, -1), (3, 2)])
+    path = str(tmp_path / "c.b200cache")
+    ec.write_cache(path, H, I, recs)
+    err = C.create_string_buffer(160)
+    cache = clib.moe_b200_expert_cache_open(path.encode(), err)
+    assert cache, err.value
+    try:
+        h, i, rb, n = C.c_uint32(), C.c_uint32(), C.c_uint64(), C.c_uint32()
+        assert clib.moe_b200_expert_cache_info(cache, C.byref(h), C.byref(i), C.byref(rb), C.byref(n)) == 1
+        assert (h.value, i.value, rb.value, n.value) == (H, I, ec.record_bytes(H, I), 4)
+        for layer, expert, key, rec in recs:
+            p = clib.moe_b200_expert_cache_record(cache, layer, expert, key, 1, err)
+            assert p, err.value
+            got = np.ctypeslib.as_array((C.c_uint8 * rb.value).from_address(p))
+            assert np.array_equal(got, rec)
+            # another source key or slot: no record, no error
+            assert not clib.moe_b200_expert_cache_record(cache, layer, expert, key ^ 1, 1, err)
+            assert err.value == b""
+        assert not clib.moe_b200_expert_cache_record(cache, 1, 0, recs[0][2], 1, err)
+    finally:
+        clib.moe_b200_expert_cache_close(cache)
+    # a flipped record byte: refused when checked, returned when not
+    _corrupt(path, ec.CacheFile(path).entries[(0, 5)].offset + 99)
+    cache = clib.moe_b200_expert_cache_open(path.encode(), err)
+    assert cache, err.value
+    try:
+        assert not clib.moe_b200_expert_cache_record(cache, 0, 5, recs[1][2], 1, err)
+        assert b"checksum" in err.value
+        assert clib.moe_b200_expert_cache_record(cache, 0, 5, recs[1][2], 0, err)
+        assert clib.moe_b200_expert_cache_record(cache, 0, 0, recs[0][2], 1, err)
+    finally:
+        clib.moe_b200_expert_cache_close(cache)
+    # files the reader refuses: damaged table, wrong magic, truncated, absent
+    for damage, msg in ((lambda: _corrupt(path, ec.HEADER_BYTES + 9), b"entry table checksum"),
+                        (lambda: _corrupt(path, 1), b"not a repacked-expert cache"),
+                        (lambda: open(path, "r+b").truncate(os.path.getsize(path) - ec.ALIGN), b"outside the file"),
+                        (lambda: open(path, "r+b").truncate(64), b"shorter than the header")):
+        ec.write_cache(path, H, I, recs)
+        damage()
+        assert not clib.moe_b200_expert_cache_open(path.encode(), err)
+        assert msg in err.value, (msg, err.value)
+    assert not clib.moe_b200_expert_cache_open(str(tmp_path / "absent").encode(), err)
