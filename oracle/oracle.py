@@ -276,6 +276,9 @@ class Ref:
         L.ref_moe_layer_engine.restype = C.c_int
         L.ref_moe_layer_engine.argtypes = [C.c_void_p, C.POINTER(RefLayer), _u16p, C.c_uint32, _f32p, _i32p, _f32p,
                                            C.c_char_p]
+        L.ref_moe_block_engine.restype = C.c_int
+        L.ref_moe_block_engine.argtypes = [C.c_void_p, C.POINTER(RefBlock), _u16p, _f32p, C.c_uint32, _f32p, _i32p,
+                                           _f32p, C.c_char_p]
         L.ref_moe_block.restype = C.c_int
         L.ref_moe_block.argtypes = [C.c_void_p, C.POINTER(RefBlock), _u16p, _f32p, C.c_uint32, _f32p, _i32p,
                                     _f32p]
@@ -332,10 +335,12 @@ class Ref:
             raise RuntimeError("reference layer function failed")
         return y, ids, w
 
-    def moe_block(self, li, blk: Block, hidden=None, x=None):
+    def moe_block(self, li, blk: Block, hidden=None, x=None, shard_path=None):
         """The block with its optional parts (the engine's metadata must
         carry blk.metadata()); returns y (what the block adds to hidden),
-        ids, w."""
+        ids, w.  With shard_path, through the reference's
+        moe_layer_moe_mlp_f32 itself (ref_moe_block_engine), else the leaf
+        composition (ref_moe_block)."""
         s = li.shape
         x = _c(li.x if x is None else x, np.uint16)
         T = x.shape[0]
@@ -353,8 +358,13 @@ class Ref:
         y = np.zeros((T, s.hidden), np.float32)
         ids = np.zeros((T, s.top_k), np.int32)
         w = np.zeros((T, s.top_k), np.float32)
-        if not self.lib.ref_moe_block(self.engine, C.byref(d), _p(x, _u16p), _p(keep[13], _f32p), T,
-                                      _p(y, _f32p), _p(ids, _i32p), _p(w, _f32p)):
+        if shard_path is not None:
+            ok = self.lib.ref_moe_block_engine(self.engine, C.byref(d), _p(x, _u16p), _p(keep[13], _f32p), T,
+                                               _p(y, _f32p), _p(ids, _i32p), _p(w, _f32p), str(shard_path).encode())
+        else:
+            ok = self.lib.ref_moe_block(self.engine, C.byref(d), _p(x, _u16p), _p(keep[13], _f32p), T,
+                                        _p(y, _f32p), _p(ids, _i32p), _p(w, _f32p))
+        if not ok:
             raise RuntimeError("reference block failed")
         return y, ids, w
 

@@ -310,6 +310,41 @@ void put_common(moe_pc_engine* engine, int32_t layer, const char* suffix, const 
 
 }  // namespace
 
+namespace {
+
+// The optional block parts of `bd` in this engine's tensor cache, each under
+// the first suffix the reference looks it up by (absent ones removed).
+void install_block_parts(moe_pc_engine* engine, int32_t layer, const ref_block_desc* bd) {
+    const uint32_t H = bd->base.hidden;
+    const uint8_t F32 = moe_RAW_SCALAR_F32, BF16 = moe_RAW_SCALAR_BF16;
+    const uint8_t RAW_F32 = moe_WEIGHT_ENCODING_RAW_FP32, RAW_BF16 = moe_WEIGHT_ENCODING_RAW_BF16;
+    put_common(engine, layer, "pre_ffw_norm_2.weight", bd->pre_norm2, H, H, 0, F32, RAW_F32);
+    put_common(engine, layer, "post_ffw_norm_1.weight", bd->post_norm1, H, H, 0, F32, RAW_F32);
+    put_common(engine, layer, "post_ffw_norm_2.weight", bd->post_norm2, H, H, 0, F32, RAW_F32);
+    put_common(engine, layer, "post_ffw_norm.weight", bd->post_norm, H, H, 0, F32, RAW_F32);
+    put_common(engine, layer, "ffn_down_exps.scale", bd->down_scale, bd->down_scale_count,
+               (uint32_t)bd->down_scale_count, 0, F32, RAW_F32);
+    put_common(engine, layer, "shared_expert_gate.weight", bd->shared_gate_inp, H, 1, H, BF16, RAW_BF16);
+    // the router's own lookup of its input scale (moe_map_router_scale_tensor,
+    // generation_router.cpp.inc:272-314) keys it with the router's hash
+    const uint64_t key = router_scale_key(layer);
+    std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
+    if (bd->router_scale && bd->router_scale_count) {
+        moe_raw_tensor_cache_entry e{};
+        e.base = reinterpret_cast<const uint8_t*>(bd->router_scale);
+        e.bytes = bd->router_scale_count * 4ull;
+        e.rows = (uint32_t)bd->router_scale_count;
+        e.cols = 0;
+        e.scalar_encoding = F32;
+        e.weight_format = RAW_F32;
+        engine->raw_tensor_cache[key] = e;
+    } else {
+        engine->raw_tensor_cache.erase(key);
+    }
+}
+
+}  // namespace
+
 // The MoE block for T tokens, one token at a time, composed from the
 // reference's own functions in moe_layer_moe_mlp_f32's order
 // (generation_mlp.cpp.inc:776-1442): the routed input is
@@ -347,31 +382,7 @@ int ref_moe_block(void* eng, const ref_block_desc* bd, const uint16_t* x_bf16, c
         std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
         engine->raw_tensor_cache[router_cache_key(layer)] = r;
     }
-    put_common(engine, layer, "pre_ffw_norm_2.weight", bd->pre_norm2, H, H, 0, F32, RAW_F32);
-    put_common(engine, layer, "post_ffw_norm_1.weight", bd->post_norm1, H, H, 0, F32, RAW_F32);
-    put_common(engine, layer, "post_ffw_norm_2.weight", bd->post_norm2, H, H, 0, F32, RAW_F32);
-    put_common(engine, layer, "post_ffw_norm.weight", bd->post_norm, H, H, 0, F32, RAW_F32);
-    put_common(engine, layer, "ffn_down_exps.scale", bd->down_scale, bd->down_scale_count,
-               (uint32_t)bd->down_scale_count, 0, F32, RAW_F32);
-    put_common(engine, layer, "shared_expert_gate.weight", bd->shared_gate_inp, H, 1, H, BF16, RAW_BF16);
-    {
-        // the router's own lookup of its input scale (moe_map_router_scale_tensor,
-        // generation_router.cpp.inc:272-314) keys it with the router's hash
-        const uint64_t key = router_scale_key(layer);
-        std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
-        if (bd->router_scale && bd->router_scale_count) {
-            moe_raw_tensor_cache_entry e{};
-            e.base = reinterpret_cast<const uint8_t*>(bd->router_scale);
-            e.bytes = bd->router_scale_count * 4ull;
-            e.rows = (uint32_t)bd->router_scale_count;
-            e.cols = 0;
-            e.scalar_encoding = F32;
-            e.weight_format = RAW_F32;
-            engine->raw_tensor_cache[key] = e;
-        } else {
-            engine->raw_tensor_cache.erase(key);
-        }
-    }
+    install_block_parts(engine, layer, bd);
     const int activation_mode = moe_engine_gelu_activation_mode(engine);
     const float eps = bd->eps;
 
@@ -494,13 +505,14 @@ int ref_group_tokens_by_expert(const moe_token_expert_assignment_t* a, uint32_t 
 // call computes without tier moves; the phase is prefill (no speculative
 // prefetch).  Input: s->norm = the token's row; hidden = 0, so the residual
 // add leaves hidden = mlp; y_f32 receives s->mlp, ids and w the router's
-// selection.  Any block parts a ref_moe_block call left in the engine are
-// removed first: this entry point is the plain layer.
-int ref_moe_layer_engine(void* eng, const ref_layer_desc* d, const uint16_t* x_bf16, uint32_t tokens,
-                         float* y_f32, int32_t* out_ids, float* out_w, const char* shard_path) {
-    mxcsr_guard guard;
-    moe_pc_engine* engine = static_cast<moe_pc_engine*>(eng);
+// selection.  Without `bd` (the plain layer) any block parts a
+// ref_moe_block call left in the engine are removed first; with it, they are
+// installed and `hidden_in` is the residual stream (ref_moe_block_engine).
+static int run_layer_function(moe_pc_engine* engine, const ref_layer_desc* d, const ref_block_desc* bd,
+                              const uint16_t* x_bf16, const float* hidden_in, uint32_t tokens, float* y_f32,
+                              int32_t* out_ids, float* out_w, const char* shard_path) {
     if (!engine || !d || !x_bf16 || !y_f32 || !shard_path) return 0;
+    if (bd && (bd->pre_norm2 || bd->router_scale) && !hidden_in) return 0;
     const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, K = d->top_k;
     const int32_t layer = 0;
     const uint64_t row_h = (uint64_t)((H + 31u) / 32u) * 17u;
@@ -553,7 +565,7 @@ int ref_moe_layer_engine(void* eng, const ref_layer_desc* d, const uint16_t* x_b
     }
 
     // router, and the shared expert as the layer's dense MLP
-    clear_router_scale(engine, layer);
+    if (!bd) clear_router_scale(engine, layer);
     {
         moe_raw_tensor_cache_entry r{};
         r.base = reinterpret_cast<const uint8_t*>(d->router_bf16);
@@ -565,9 +577,33 @@ int ref_moe_layer_engine(void* eng, const ref_layer_desc* d, const uint16_t* x_b
         std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
         engine->raw_tensor_cache[router_cache_key(layer)] = r;
     }
-    const char* block_parts[] = {"pre_ffw_norm_2.weight", "post_ffw_norm_1.weight", "post_ffw_norm_2.weight",
-                                 "post_ffw_norm.weight", "ffn_down_exps.scale", "shared_expert_gate.weight"};
-    for (const char* sfx : block_parts) put_common(engine, layer, sfx, nullptr, 0, 0, 0, 0, 0);
+    {
+        // whether the router reads the residual stream is decided from the
+        // model's tensor names (moe_engine_has_common_tensor_suffix, which
+        // also remembers its answers): name the scale tensor exactly when the
+        // block has one.  Its slot is out of range, so a lookup of the tensor
+        // itself still finds the cached copy installed below.
+        const std::string scale_name = "blk." + std::to_string(layer) + ".ffn_gate_inp.scale";
+        if (bd && bd->router_scale && bd->router_scale_count) {
+            engine->gguf_common_tensor_slots[scale_name] = SIZE_MAX;
+        } else {
+            engine->gguf_common_tensor_slots.erase(scale_name);
+        }
+        std::unique_lock<std::shared_mutex> lock(engine->common_tensor_suffix_cache_mutex);
+        engine->common_tensor_suffix_cache.clear();
+    }
+    if (bd) {
+        install_block_parts(engine, layer, bd);
+        // the layer function takes its RMSNorm epsilon from the model's config
+        moe_attn_config_t acfg = moe_generation_attn_config(engine);
+        acfg.rms_norm_eps = bd->eps;
+        engine->attn_config = acfg;
+        engine->attn_config_valid.store(true, std::memory_order_release);
+    } else {
+        const char* block_parts[] = {"pre_ffw_norm_2.weight", "post_ffw_norm_1.weight", "post_ffw_norm_2.weight",
+                                     "post_ffw_norm.weight", "ffn_down_exps.scale", "shared_expert_gate.weight"};
+        for (const char* sfx : block_parts) put_common(engine, layer, sfx, nullptr, 0, 0, 0, 0, 0);
+    }
     const bool shared = d->shared_gate && d->shared_up && d->shared_down;
     struct {
         const char* suffix;
@@ -616,16 +652,43 @@ int ref_moe_layer_engine(void* eng, const ref_layer_desc* d, const uint16_t* x_b
     s.up.resize(I);
     s.expert_work.resize(K);
     std::vector<float> hidden(H);
+    // what the layer adds to hidden: the final post-FFW norm's output when
+    // the block has one (moe_add_mlp_residual_f32 leaves it in s.shared), else mlp
+    const std::vector<float>& added = (bd && bd->post_norm) ? s.shared : s.mlp;
     for (uint32_t t = 0; t < tokens; ++t) {
         for (uint32_t h = 0; h < H; ++h) s.norm[h] = bf16_to_f32(x_bf16[(uint64_t)t * H + h]);
-        std::fill(hidden.begin(), hidden.end(), 0.0f);
+        if (hidden_in) {
+            std::memcpy(hidden.data(), hidden_in + (uint64_t)t * H, (size_t)H * sizeof(float));
+        } else {
+            std::fill(hidden.begin(), hidden.end(), 0.0f);
+        }
         if (!moe_layer_moe_mlp_f32(engine, layer, &s, hidden.data(), &c)) return 0;
         if (s.selected_experts.size() != K || s.selected_weights.size() != K) return 0;
-        std::memcpy(y_f32 + (uint64_t)t * H, s.mlp.data(), (size_t)H * sizeof(float));
+        std::memcpy(y_f32 + (uint64_t)t * H, added.data(), (size_t)H * sizeof(float));
         if (out_ids) for (uint32_t j = 0; j < K; ++j) out_ids[(uint64_t)t * K + j] = s.selected_experts[j];
         if (out_w) for (uint32_t j = 0; j < K; ++j) out_w[(uint64_t)t * K + j] = s.selected_weights[j];
     }
     return 1;
+}
+
+int ref_moe_layer_engine(void* eng, const ref_layer_desc* d, const uint16_t* x_bf16, uint32_t tokens,
+                         float* y_f32, int32_t* out_ids, float* out_w, const char* shard_path) {
+    mxcsr_guard guard;
+    return run_layer_function(static_cast<moe_pc_engine*>(eng), d, nullptr, x_bf16, nullptr, tokens, y_f32, out_ids,
+                              out_w, shard_path);
+}
+
+// The same with the Gemma-style block parts of `bd` (ref_moe_block's inputs:
+// x the normalised row the shared expert reads, hidden the fp32 residual
+// stream the pre-norm and a scaled router read); y receives what the block
+// adds to hidden.  The engine's metadata must carry the block's activation
+// and unit offset, as for ref_moe_block; its RMSNorm epsilon is set here.
+int ref_moe_block_engine(void* eng, const ref_block_desc* bd, const uint16_t* x_bf16, const float* hidden,
+                         uint32_t tokens, float* y_f32, int32_t* out_ids, float* out_w, const char* shard_path) {
+    mxcsr_guard guard;
+    if (!bd) return 0;
+    return run_layer_function(static_cast<moe_pc_engine*>(eng), &bd->base, bd, x_bf16, hidden, tokens, y_f32,
+                              out_ids, out_w, shard_path);
 }
 
 }  // extern "C"

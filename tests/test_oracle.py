@@ -309,3 +309,41 @@ def test_reference_layer_function_matches_composed_layer(name, ref_lib, port, sy
     assert np.array_equal(i_fn, i_p)
     assert np.array_equal(bits(w_fn), bits(w_p))
     assert np.array_equal(bits(y_fn), bits(y_p))
+
+
+BLOCK_FUNCTION_OPTIONS = {
+    "all_on": dict(activation=1, unit_offset=True, pre_norm2=True, post_norm1=True, post_norm2=True, post_norm=True,
+                   down_scale="element", shared_gate_inp=True, router_scale="element"),
+    "tanh_scalar": dict(activation=2, unit_offset=False, pre_norm2=True, post_norm1=False, post_norm2=True,
+                        post_norm=True, down_scale="expert", shared_gate_inp=False, router_scale="scalar"),
+    "silu_post_only": dict(activation=0, unit_offset=False, pre_norm2=False, post_norm1=True, post_norm2=False,
+                           post_norm=False, down_scale="scalar", shared_gate_inp=True, router_scale=None),
+}
+
+
+@pytest.mark.parametrize("opt", sorted(BLOCK_FUNCTION_OPTIONS))
+def test_reference_layer_function_matches_composed_block(opt, ref_lib, port, synth, tmp_path):
+    """moe_layer_moe_mlp_f32 itself with Gemma-style block parts (pre-norm,
+    post-FFW norms, down scales, shared-expert gate, router input scale)
+    against the leaf composition (ref_moe_block) and the restatement."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("make_golden", GOLDEN / "make_golden.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    opts = BLOCK_FUNCTION_OPTIONS[opt]
+    for shape in (synth.small_shape(name="bf1", shared=True, tokens=6, experts=8, top_k=2),
+                  synth.small_shape(name="bf2", hidden=80, intermediate=100, tokens=5, experts=8, top_k=3)):
+        li = synth.make_layer(shape, seed=71)
+        blk, hidden = mg.block_inputs(shape, 71, opts)
+        ref = ref_lib.Ref(ref_lib.metadata_json(shape.top_k, norm_topk=shape.norm_topk, block=blk))
+        try:
+            y_fn, i_fn, w_fn = ref.moe_block(li, blk, hidden=hidden, shard_path=tmp_path / "shard.bin")
+            y_c, i_c, w_c = ref.moe_block(li, blk, hidden=hidden)
+        finally:
+            ref.close()
+        assert np.array_equal(i_fn, i_c), shape.name
+        assert np.array_equal(bits(w_fn), bits(w_c)), shape.name
+        assert np.array_equal(bits(y_fn), bits(y_c)), shape.name
+        y_p, i_p, w_p, ties = port.moe_block(li, blk, hidden=hidden)
+        assert ties == 0
+        assert np.array_equal(bits(y_fn), bits(y_p)), shape.name
