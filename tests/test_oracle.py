@@ -347,3 +347,42 @@ def test_reference_layer_function_matches_composed_block(opt, ref_lib, port, syn
         y_p, i_p, w_p, ties = port.moe_block(li, blk, hidden=hidden)
         assert ties == 0
         assert np.array_equal(bits(y_fn), bits(y_p)), shape.name
+
+
+ROUTER_FUNCTION_CASES = {
+    # sigmoid scores with a routed scale, renormalised
+    "sigmoid_scaled": dict(shape=dict(hidden=96, intermediate=64, experts=16, top_k=4, tokens=7, norm_topk=True),
+                           route=dict(sigmoid=True, routed_scale=2.5)),
+    # sigmoid with the group limit: 8 groups of 4 experts, 3 kept
+    "group_limit": dict(shape=dict(hidden=64, intermediate=48, experts=32, top_k=6, tokens=6, shared=True),
+                        route=dict(sigmoid=True, routed_scale=1.0, n_group=8, topk_group=3)),
+    # sigmoid, not renormalised, one expert per group, 5 groups kept
+    "group_of_one": dict(shape=dict(hidden=80, intermediate=40, experts=16, top_k=4, tokens=5),
+                         route=dict(sigmoid=True, routed_scale=1.5, n_group=16, topk_group=5)),
+}
+
+
+@pytest.mark.parametrize("case", sorted(ROUTER_FUNCTION_CASES))
+def test_reference_layer_function_matches_sigmoid_group_routing(case, ref_lib, port, synth, tmp_path):
+    """DeepSeek-style routing (sigmoid scores, routed scale, group limit)
+    through moe_layer_moe_mlp_f32 itself, against the composition and the
+    restatement, bit for bit."""
+    c = ROUTER_FUNCTION_CASES[case]
+    shape = synth.small_shape(name=case, **c["shape"])
+    r = c["route"]
+    li = synth.make_layer(shape, seed=81)
+    ref = ref_lib.Ref(ref_lib.metadata_json(shape.top_k, norm_topk=shape.norm_topk, **r))
+    try:
+        y_fn, i_fn, w_fn = ref.moe_layer_engine(li, tmp_path / "shard.bin")
+        y_c, i_c, w_c = ref.moe_layer(li)
+    finally:
+        ref.close()
+    assert np.array_equal(i_fn, i_c)
+    assert np.array_equal(bits(w_fn), bits(w_c))
+    assert np.array_equal(bits(y_fn), bits(y_c))
+    y_p, i_p, w_p, ties = port.moe_layer(li, score_sigmoid=int(r["sigmoid"]), routed_scale=r["routed_scale"],
+                                         n_group=r.get("n_group", 0), topk_group=r.get("topk_group", 0))
+    assert ties == 0
+    assert np.array_equal(i_fn, i_p)
+    assert np.array_equal(bits(w_fn), bits(w_p))
+    assert np.array_equal(bits(y_fn), bits(y_p))
