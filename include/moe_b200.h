@@ -96,9 +96,13 @@ typedef struct {
     float norm_eps;        /* RMSNorm epsilon of the block parts; <= 0 -> 1e-6 */
     /* Partial-failure policy.  0: an expert (or the shared expert, with
      * use_shared) that was never uploaded makes the call fail.  1: the
-     * reference's policy (generation_mlp.cpp.inc:1418, 833-860): such an
-     * expert contributes nothing -- its term is left out of the sum and the
-     * remaining weights are not renormalised; routing is unchanged. */
+     * reference's policy (generation_mlp.cpp.inc:1219-1282, 833-860): such an
+     * expert contributes nothing; when norm_topk is set the combine divides
+     * the weights of the token's other experts by their sum; a token whose
+     * selected experts are all missing fails the call, as the reference's
+     * layer fails.  The routing and the returned weights are unchanged.
+     * (The expert-parallel forward leaves missing terms out without the
+     * renormalisation.) */
     int32_t skip_missing;
 } moe_b200_layer_cfg_t;
 

@@ -446,7 +446,8 @@ static void* mo_layer_worker(void* arg) {
     float* su = (float*)malloc(sizeof(float) * I);
     int32_t* ids = (int32_t*)malloc(sizeof(int32_t) * K);
     float* w = (float*)malloc(sizeof(float) * K);
-    j->ok = x && xe && mlp && out && tmp && sg && su && ids && w &&
+    float* cw = (float*)malloc(sizeof(float) * K);  /* the combine's weights */
+    j->ok = x && xe && mlp && out && tmp && sg && su && ids && w && cw &&
             (!(L->pre_norm2 || L->router_scale) || j->hidden);
     for (uint32_t t = j->t0; j->ok && t < j->t1; ++t) {
         for (uint32_t h = 0; h < H; ++h) x[h] = mo_bf16(j->x_bf16[(uint64_t)t * H + h]);
@@ -456,7 +457,7 @@ static void* mo_layer_worker(void* arg) {
             xr = xe;
         }
         memset(mlp, 0, sizeof(float) * H);
-        if (L->shared_gate && L->shared_up && L->shared_down) {
+        if (L->shared_gate && L->shared_up && L->shared_down && (!L->present || L->present[L->experts])) {
             mo_triplet_act(act, L->shared_gate, L->shared_up, L->shared_down, x, H, I, sg, su, out);
             float g = 1.0f;
             if (L->shared_gate_inp) g = 1.0f / (1.0f + expf(-mo_bf16_dot_row(L->shared_gate_inp, x, H)));
@@ -471,8 +472,31 @@ static void* mo_layer_worker(void* arg) {
          * (generation_mlp.cpp.inc:866-871) */
         const float* rin = L->router_scale ? j->hidden + (uint64_t)t * H : xr;
         if (!mo_router_topk(L, rin, ids, w, &j->ties)) { j->ok = 0; break; }
+        /* partial failure (generation_mlp.cpp.inc:1219-1282): missing experts
+         * drop out; with a renormalising router the others' weights are
+         * multiplied by 1 / (their sum, in router order) */
+        memcpy(cw, w, sizeof(float) * K);
+        if (L->present) {
+            uint32_t mapped = 0;
+            float wsum = 0.0f;
+            for (uint32_t e = 0; e < K; ++e) {
+                if (L->present[ids[e]]) {
+                    ++mapped;
+                    wsum += w[e];
+                }
+            }
+            if (mapped == 0) { j->ok = 0; break; }
+            if (mapped < K) {
+                const float scale = 1.0f / wsum;
+                const int renorm = L->norm_topk && wsum > 1e-9f;
+                for (uint32_t e = 0; e < K; ++e) {
+                    cw[e] = !L->present[ids[e]] ? 0.0f : (renorm ? w[e] * scale : w[e]);
+                }
+            }
+        }
         for (uint32_t e = 0; e < K; ++e) {
             const uint64_t ex = (uint64_t)ids[e];
+            if (L->present && !L->present[ex]) continue;
             mo_triplet_act(act, L->gate + ex * gu_bytes, L->up + ex * gu_bytes, L->down + ex * d_bytes,
                            xr, H, I, sg, su, out);
             if (L->post_norm2) {
@@ -480,7 +504,7 @@ static void* mo_layer_worker(void* arg) {
                 memcpy(out, tmp, sizeof(float) * H);
             }
             mo_down_scale(L, (uint32_t)ex, out);
-            mo_axpy(mlp, out, w[e], H);
+            mo_axpy(mlp, out, cw[e], H);
         }
         float* yt = j->y + (uint64_t)t * H;
         if (L->post_norm) {
@@ -491,7 +515,7 @@ static void* mo_layer_worker(void* arg) {
         if (j->ids) memcpy(j->ids + (uint64_t)t * K, ids, sizeof(int32_t) * K);
         if (j->w) memcpy(j->w + (uint64_t)t * K, w, sizeof(float) * K);
     }
-    free(x); free(xe); free(mlp); free(out); free(tmp); free(sg); free(su); free(ids); free(w);
+    free(x); free(xe); free(mlp); free(out); free(tmp); free(sg); free(su); free(ids); free(w); free(cw);
     return NULL;
 }
 

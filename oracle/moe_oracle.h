@@ -55,6 +55,13 @@ typedef struct {
      * hidden * rms^-1 * scale / sqrt(H) of the residual stream (needs hidden). */
     const float* router_scale;     /* 1 (one for all elements) or H values */
     uint64_t router_scale_count;
+    /* Experts the layer cannot use (generation_mlp.cpp.inc:1219-1282): E + 1
+     * bytes, 0 = missing, the last one the shared expert; NULL = all present.
+     * A missing routed expert is left out and, when the router renormalises
+     * its top-k, the others' combine weights are divided by their sum; a
+     * token whose experts are all missing fails, as the reference's layer
+     * does.  The router's ids and weights themselves are unchanged. */
+    const uint8_t* present;
 } mo_layer_t;
 
 float mo_e8m0_to_f32(uint8_t v);

@@ -59,7 +59,7 @@ class MoLayer(C.Structure):
                 ("activation", C.c_int32), ("norm_unit_offset", C.c_int32), ("norm_eps", C.c_float),
                 ("pre_norm2", _f32p), ("post_norm1", _f32p), ("post_norm2", _f32p), ("post_norm", _f32p),
                 ("down_scale", _f32p), ("down_scale_count", C.c_uint64), ("shared_gate_inp", _u16p),
-                ("router_scale", _f32p), ("router_scale_count", C.c_uint64)]
+                ("router_scale", _f32p), ("router_scale_count", C.c_uint64), ("present", _u8p)]
 
 
 class RefLayer(C.Structure):
@@ -154,16 +154,20 @@ class Port:
         L.mo_rmsnorm.restype = C.c_int
         L.mo_rmsnorm.argtypes = [_f32p, _f32p, C.c_uint32, C.c_float, C.c_int32, _f32p]
 
-    def _layer(self, li, score_sigmoid=0, norm_topk=None, routed_scale=1.0, n_group=0, topk_group=0):
+    def _layer(self, li, score_sigmoid=0, norm_topk=None, routed_scale=1.0, n_group=0, topk_group=0,
+               present=None):
+        """present: E + 1 flags (the last the shared expert), 0 = missing; None = all."""
         s = li.shape
         keep = dict(router=_c(li.router, np.uint16), gate=_c(li.gate, np.uint8), up=_c(li.up, np.uint8),
                     down=_c(li.down, np.uint8), sg=_c(li.shared_gate, np.uint8),
-                    su=_c(li.shared_up, np.uint8), sd=_c(li.shared_down, np.uint8))
+                    su=_c(li.shared_up, np.uint8), sd=_c(li.shared_down, np.uint8),
+                    present=_c(present, np.uint8))
         nt = s.norm_topk if norm_topk is None else norm_topk
         L = MoLayer(s.hidden, s.intermediate, s.experts, s.top_k, int(score_sigmoid), int(nt),
                     float(routed_scale), _p(keep["router"], _u16p), _p(keep["gate"], _u8p),
                     _p(keep["up"], _u8p), _p(keep["down"], _u8p), _p(keep["sg"], _u8p),
                     _p(keep["su"], _u8p), _p(keep["sd"], _u8p), int(n_group), int(topk_group))
+        L.present = _p(keep["present"], _u8p)
         return L, keep
 
     def moe_layer(self, li, x=None, threads: int = 0, **kw):
@@ -276,6 +280,9 @@ class Ref:
         L.ref_moe_layer_engine.restype = C.c_int
         L.ref_moe_layer_engine.argtypes = [C.c_void_p, C.POINTER(RefLayer), _u16p, C.c_uint32, _f32p, _i32p, _f32p,
                                            C.c_char_p]
+        L.ref_moe_layer_engine_present.restype = C.c_int
+        L.ref_moe_layer_engine_present.argtypes = [C.c_void_p, C.POINTER(RefLayer), _u16p, C.c_uint32, _f32p, _i32p,
+                                                   _f32p, C.c_char_p, _u8p]
         L.ref_moe_block_engine.restype = C.c_int
         L.ref_moe_block_engine.argtypes = [C.c_void_p, C.POINTER(RefBlock), _u16p, _f32p, C.c_uint32, _f32p, _i32p,
                                            _f32p, C.c_char_p]
@@ -315,10 +322,11 @@ class Ref:
             raise RuntimeError("reference layer failed")
         return y, ids, w
 
-    def moe_layer_engine(self, li, shard_path: str, x=None):
+    def moe_layer_engine(self, li, shard_path: str, x=None, present=None):
         """The layer through the reference's moe_layer_moe_mlp_f32 itself, the
         experts as tensor records over a shard file written to shard_path
-        (ref_harness.cpp ref_moe_layer_engine); returns y, ids, w."""
+        (ref_harness.cpp ref_moe_layer_engine); returns y, ids, w.  present:
+        E + 1 flags (the last the shared expert), 0 = the expert is missing."""
         s = li.shape
         x = _c(li.x if x is None else x, np.uint16)
         T = x.shape[0]
@@ -330,8 +338,15 @@ class Ref:
         y = np.zeros((T, s.hidden), np.float32)
         ids = np.zeros((T, s.top_k), np.int32)
         w = np.zeros((T, s.top_k), np.float32)
-        if not self.lib.ref_moe_layer_engine(self.engine, C.byref(d), _p(x, _u16p), T, _p(y, _f32p),
-                                             _p(ids, _i32p), _p(w, _f32p), str(shard_path).encode()):
+        if present is None:
+            ok = self.lib.ref_moe_layer_engine(self.engine, C.byref(d), _p(x, _u16p), T, _p(y, _f32p),
+                                               _p(ids, _i32p), _p(w, _f32p), str(shard_path).encode())
+        else:
+            pr = _c(present, np.uint8)
+            ok = self.lib.ref_moe_layer_engine_present(self.engine, C.byref(d), _p(x, _u16p), T, _p(y, _f32p),
+                                                       _p(ids, _i32p), _p(w, _f32p), str(shard_path).encode(),
+                                                       _p(pr, _u8p))
+        if not ok:
             raise RuntimeError("reference layer function failed")
         return y, ids, w
 

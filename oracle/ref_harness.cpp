@@ -510,7 +510,8 @@ int ref_group_tokens_by_expert(const moe_token_expert_assignment_t* a, uint32_t 
 // installed and `hidden_in` is the residual stream (ref_moe_block_engine).
 static int run_layer_function(moe_pc_engine* engine, const ref_layer_desc* d, const ref_block_desc* bd,
                               const uint16_t* x_bf16, const float* hidden_in, uint32_t tokens, float* y_f32,
-                              int32_t* out_ids, float* out_w, const char* shard_path) {
+                              int32_t* out_ids, float* out_w, const char* shard_path,
+                              const uint8_t* present = nullptr) {
     if (!engine || !d || !x_bf16 || !y_f32 || !shard_path) return 0;
     if (bd && (bd->pre_norm2 || bd->router_scale) && !hidden_in) return 0;
     const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, K = d->top_k;
@@ -559,7 +560,8 @@ static int run_layer_function(moe_pc_engine* engine, const ref_layer_desc* d, co
             rec.resolved_path_index = path_index;
             finalize_tensor_layout(&rec, moe_WEIGHT_ENCODING_MXFP4);
             engine->tensors.push_back(rec);
-            tensor_slots_set(engine, layer, (int)e, projs[p], engine->tensors.size() - 1u);
+            // a missing expert has no record: the layer's partial-failure path
+            if (!present || present[e]) tensor_slots_set(engine, layer, (int)e, projs[p], engine->tensors.size() - 1u);
             offset += rec.info.weight_byte_length;
         }
     }
@@ -604,7 +606,7 @@ static int run_layer_function(moe_pc_engine* engine, const ref_layer_desc* d, co
                                      "post_ffw_norm.weight", "ffn_down_exps.scale", "shared_expert_gate.weight"};
         for (const char* sfx : block_parts) put_common(engine, layer, sfx, nullptr, 0, 0, 0, 0, 0);
     }
-    const bool shared = d->shared_gate && d->shared_up && d->shared_down;
+    const bool shared = d->shared_gate && d->shared_up && d->shared_down && (!present || present[E]);
     struct {
         const char* suffix;
         const uint8_t* data;
@@ -676,6 +678,18 @@ int ref_moe_layer_engine(void* eng, const ref_layer_desc* d, const uint16_t* x_b
     mxcsr_guard guard;
     return run_layer_function(static_cast<moe_pc_engine*>(eng), d, nullptr, x_bf16, nullptr, tokens, y_f32, out_ids,
                               out_w, shard_path);
+}
+
+// The same with some experts missing: present[e] == 0 (e < E) files no
+// records for routed expert e, present[E] == 0 leaves the shared expert out,
+// so the layer function takes its partial-failure path
+// (generation_mlp.cpp.inc:1219-1282, 833-860).
+int ref_moe_layer_engine_present(void* eng, const ref_layer_desc* d, const uint16_t* x_bf16, uint32_t tokens,
+                                 float* y_f32, int32_t* out_ids, float* out_w, const char* shard_path,
+                                 const uint8_t* present) {
+    mxcsr_guard guard;
+    return run_layer_function(static_cast<moe_pc_engine*>(eng), d, nullptr, x_bf16, nullptr, tokens, y_f32, out_ids,
+                              out_w, shard_path, present);
 }
 
 // The same with the Gemma-style block parts of `bd` (ref_moe_block's inputs:

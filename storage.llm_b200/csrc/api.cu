@@ -531,7 +531,7 @@ void moe_b200_destroy(moe_b200_engine_t* eng) {
                       &eng->yperm, &eng->err_word, &eng->hx, &eng->hy, &eng->hyf, &eng->hids,
                       &eng->hw, &eng->hperm_out, &eng->tri, &eng->xb,
                       &eng->sfx_atoms, &eng->hb, &eng->sfh_atoms, &eng->gu_tiles, &eng->dn_tiles,
-                      &eng->pipe_ys, &eng->pipe_zero_ids, &eng->pipe_slot};
+                      &eng->pipe_ys, &eng->pipe_zero_ids, &eng->pipe_slot, &eng->present_dev, &eng->comb_w};
     for (DevBuf* b : bufs) b->release();
     for (cudaEvent_t e : eng->prof_events) cudaEventDestroy(e);
     ep_release(eng->ep);
@@ -1037,6 +1037,21 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
     mark(5);
     }
 
+    // missing experts (skip_missing): the combine weights of the reference's
+    // partial-failure policy -- 0 for a missing expert (whose zero codes add
+    // nothing anyway), the others renormalised when the router renormalises
+    // its top-k -- and an error for a token whose experts are all missing
+    const float* cw = w;
+    if (skip_missing &&
+        std::find(L->present.begin(), L->present.begin() + E, (uint8_t)0) != L->present.begin() + E) {
+        CK(eng->present_dev.reserve(E));
+        CK(cudaMemcpyAsync(eng->present_dev.ptr, L->present.data(), E, cudaMemcpyHostToDevice, st));
+        CK(eng->comb_w.reserve((size_t)T * K * 4));
+        CK(launch_combine_weights(ids, w, eng->present_dev.as<uint8_t>(), T, K, E, cfg->norm_topk != 0,
+                                  eng->comb_w.as<float>(), errw, st));
+        launches += 1;
+        cw = eng->comb_w.as<float>();
+    }
     // tokens [t0, t1): the combine, then (host-buffer calls) their copy back
     auto combine = [&](uint32_t t0, uint32_t t1) -> int {
         const float* ys = !shared      ? nullptr
@@ -1049,11 +1064,11 @@ int forward_impl(moe_b200_engine_t* eng, const moe_b200_layer_cfg_t* cfg, const 
                              L->blk_post_norm.as<float>(), L->blk_down_scale.as<float>(), L->blk_down_scale_count,
                              cfg->norm_eps, cfg->norm_unit_offset};
             CK(launch_block_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>() + (size_t)t0 * K,
-                                    ids + (size_t)t0 * K, w + (size_t)t0 * K, t1 - t0, K, E, ys,
+                                    ids + (size_t)t0 * K, cw + (size_t)t0 * K, t1 - t0, K, E, ys,
                                     gated ? eng->gate_w.as<float>() + t0 : nullptr, parts, yb, yf, st, bs));
         } else {
             CK(launch_combine(eng->yperm.as<float>(), H, eng->pos_of.as<uint32_t>() + (size_t)t0 * K,
-                              w + (size_t)t0 * K, t1 - t0, K, ys, yb, yf, st, bs));
+                              cw + (size_t)t0 * K, t1 - t0, K, ys, yb, yf, st, bs));
         }
         launches += 1;
         return 1;
@@ -1209,6 +1224,7 @@ int moe_b200_sync(moe_b200_engine_t* eng, void* stream, char* err) {
         CK(cudaMemsetAsync(eng->err_word.ptr, 0, 4, st));
         CK(cudaStreamSynchronize(st));
         const char* what = code == kErrBadExpert            ? "expert id out of range"
+                           : code == kErrAllExpertsMissing  ? "every expert of a token is missing (skip_missing)"
                            : code == kErrTimeoutRouterLoad  ? "bounded wait timed out in the router"
                            : code == kErrTimeoutPeer        ? "bounded wait for another rank timed out"
                                                             : "bounded wait timed out in a GEMM pipeline";

@@ -60,6 +60,7 @@ enum : uint32_t {
     kErrTimeoutRouterLoad = 7,
     kErrTimeoutPeer = 8,
     kErrBadExpert = 16,
+    kErrAllExpertsMissing = 17,
 };
 
 __device__ __forceinline__ void record_error(uint32_t* err, uint32_t code) {

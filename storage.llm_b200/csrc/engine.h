@@ -139,6 +139,9 @@ struct moe_b200_engine {
     DevBuf g_count, g_offset, g_gu_off, g_dn_off;
     DevBuf xperm, hperm, yperm;
     DevBuf err_word;
+    // skip_missing with a renormalising router: the layer's expert presence
+    // and the combine weights computed from it
+    DevBuf present_dev, comb_w;
     // block-scaled path: quantised activations and intermediate
     // (xb, hb hold a hi plane followed by a lo plane)
     DevBuf xb, sfx_atoms, hb, sfh_atoms, gu_tiles, dn_tiles;

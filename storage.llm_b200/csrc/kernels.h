@@ -172,6 +172,13 @@ cudaError_t launch_gather(const uint16_t* x, uint32_t H, uint32_t Kp, const uint
 // y[t] = ys[t] (shared expert rows, may be null) + sum_j w[t,j] * yp[pos_of[t*K+j]].
 cudaError_t launch_combine(const float* yp, uint32_t H, const uint32_t* pos_of, const float* w, uint32_t T,
                            uint32_t K, const float* ys, uint16_t* y_bf16, float* y_f32, cudaStream_t st, bool pdl);
+// cw [T x K]: the combine weights when some experts are missing (present
+// [E] bytes, 0 = missing): 0 for missing experts; for the others w, times
+// 1 / (the sum of the present experts' w, router order) when norm (a
+// renormalising router); kErrAllExpertsMissing when a token has none (the
+// reference's partial-failure policy, generation_mlp.cpp.inc:1219-1282).
+cudaError_t launch_combine_weights(const int32_t* ids, const float* w, const uint8_t* present, uint32_t T,
+                                   uint32_t K, uint32_t E, bool norm, float* cw, uint32_t* err, cudaStream_t st);
 
 // tcgen05 grouped GEMMs (gemm_tc.cu).  `tmap_b` covers the permuted
 // activation rows [rows x Kp] bf16 with a 64 x block_n box, 128-byte swizzle.

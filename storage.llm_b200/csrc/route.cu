@@ -1283,4 +1283,40 @@ cudaError_t launch_combine(const float* yp, uint32_t H, const uint32_t* pos_of, 
                          y_f32);
 }
 
+// Combine weights of a layer with missing experts (generation_mlp.cpp.inc:
+// 1219-1282): per token the missing experts' weights are 0 and, when the
+// router renormalises its top-k (norm), the others' are multiplied by
+// 1 / (their sum, added in router order); a token whose experts are all
+// missing records kErrAllExpertsMissing (the reference fails the layer
+// there).  One thread per token.
+__global__ void combine_weights_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w,
+                                       const uint8_t* __restrict__ present, uint32_t T, uint32_t K, uint32_t E,
+                                       int norm, float* __restrict__ cw, uint32_t* __restrict__ err) {
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    const int32_t* id = ids + (uint64_t)t * K;
+    const float* wt = w + (uint64_t)t * K;
+    float* out = cw + (uint64_t)t * K;
+    auto here = [&](uint32_t j) { return (uint32_t)id[j] < E && present[id[j]] != 0; };
+    uint32_t mapped = 0;
+    float wsum = 0.0f;
+    for (uint32_t j = 0; j < K; ++j) {
+        if (here(j)) {
+            ++mapped;
+            wsum = __fadd_rn(wsum, wt[j]);
+        }
+    }
+    if (mapped == 0) record_error(err, kErrAllExpertsMissing);
+    const bool renorm = norm && mapped < K && wsum > 1e-9f;
+    const float scale = renorm ? __fdiv_rn(1.0f, wsum) : 1.0f;
+    for (uint32_t j = 0; j < K; ++j) out[j] = !here(j) ? 0.0f : (renorm ? __fmul_rn(wt[j], scale) : wt[j]);
+}
+
+cudaError_t launch_combine_weights(const int32_t* ids, const float* w, const uint8_t* present, uint32_t T,
+                                   uint32_t K, uint32_t E, bool norm, float* cw, uint32_t* err, cudaStream_t st) {
+    if (T == 0) return cudaSuccess;
+    combine_weights_kernel<<<ceil_div(T, 256u), 256, 0, st>>>(ids, w, present, T, K, E, norm ? 1 : 0, cw, err);
+    return cudaGetLastError();
+}
+
 }  // namespace moe_b200

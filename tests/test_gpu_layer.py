@@ -189,16 +189,19 @@ def test_device_resident_upload_matches_host_upload(L, synth):
         eng.close()
 
 
-def test_missing_expert_policy(L, synth, port):
-    """The reference's partial-failure policy (generation_mlp.cpp.inc:1418,
-    and the shared expert's at :833-860): an expert that is not available is
-    left out of the sum, the other weights are not renormalised and the
-    routing is unchanged.  With skip_missing the library does the same for
-    experts never uploaded; without it the call fails.  Checked against the
-    oracle on a layer whose missing experts have all-zero down weights (their
-    term is then exactly zero)."""
-    shape = synth.small_shape(name="missing", hidden=192, intermediate=160, experts=6, top_k=2, tokens=40,
-                              shared=True)
+@pytest.mark.parametrize("norm_topk", [False, True], ids=["plain_router", "renormalising_router"])
+def test_missing_expert_policy(L, synth, port, norm_topk):
+    """The reference's partial-failure policy (generation_mlp.cpp.inc:
+    1219-1282, and the shared expert's at :833-860): an expert that is not
+    available is left out of the sum, and a router that renormalises its
+    top-k has the others' combine weights divided by their sum; the routing
+    and the returned weights are unchanged.  With skip_missing the library
+    does the same for experts never uploaded; without it the call fails.
+    Checked against the oracle given the same missing experts (its rule is
+    pinned to the reference's layer function in tests/test_oracle.py)."""
+    # top-3 of 6 with 2 missing: every token keeps at least one expert
+    shape = synth.small_shape(name="missing", hidden=192, intermediate=160, experts=6, top_k=3, tokens=40,
+                              shared=True, norm_topk=norm_topk)
     li = synth.make_layer(shape, seed=71)
     missing = (1, 4)
     eng = L.Engine(0)
@@ -213,15 +216,38 @@ def test_missing_expert_policy(L, synth, port):
         out = eng.forward_host(L.Engine.cfg(shape, skip_missing=True), li.x)
     finally:
         eng.close()
-    ref_li = synth.LayerInputs(shape, li.router, li.gate, li.up, li.down.copy(), li.x, li.shared_gate, li.shared_up,
-                               np.zeros_like(li.shared_down))  # the shared expert is missing too
-    for e in missing:
-        ref_li.down[e] = 0
-    y_ref, ids_ref, w_ref, _ = port.moe_layer(ref_li)
+    present = np.ones(shape.experts + 1, np.uint8)
+    present[list(missing)] = 0
+    present[shape.experts] = 0  # the shared expert is missing too
+    y_ref, ids_ref, w_ref, _ = port.moe_layer(li, present=present)
     assert np.array_equal(out["ids"], ids_ref) and np.array_equal(bits(out["w"]), bits(w_ref))
     assert np.isin(ids_ref, missing).any()  # the case exercises a skipped expert
     mx, mr = errors(out["y_f32"], y_ref)
     assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+
+
+def test_missing_all_experts_of_a_token_fails(L, synth, port):
+    """A token whose selected experts are all missing fails the layer, as in
+    the reference (generation_mlp.cpp.inc:1219-1239), skip_missing or not."""
+    shape = synth.small_shape(name="all_missing", hidden=128, intermediate=96, experts=6, top_k=2, tokens=40)
+    li = synth.make_layer(shape, seed=71)
+    present = np.ones(shape.experts + 1, np.uint8)
+    ids, _, _, _ = port.router_topk(li)
+    missing = tuple(int(e) for e in ids[0])  # token 0's two experts
+    present[list(missing)] = 0
+    with pytest.raises(RuntimeError):
+        port.moe_layer(li, present=present)
+    eng = L.Engine(0)
+    try:
+        eng.upload_router(0, np.ascontiguousarray(li.router), shape.experts, shape.hidden)
+        for e in range(shape.experts):
+            if e not in missing:
+                eng.upload_expert(0, e, np.ascontiguousarray(li.gate[e]), np.ascontiguousarray(li.up[e]),
+                                  np.ascontiguousarray(li.down[e]), shape.hidden, shape.intermediate)
+        with pytest.raises(L.MoEError, match="every expert of a token is missing"):
+            eng.forward_host(L.Engine.cfg(shape, skip_missing=True), li.x)
+    finally:
+        eng.close()
 
 
 def test_group_tokens_matches_reference_fixture(L):

@@ -386,3 +386,57 @@ def test_reference_layer_function_matches_sigmoid_group_routing(case, ref_lib, p
     assert np.array_equal(i_fn, i_p)
     assert np.array_equal(bits(w_fn), bits(w_p))
     assert np.array_equal(bits(y_fn), bits(y_p))
+
+
+@pytest.mark.parametrize("norm_topk", [False, True], ids=["no_renorm", "renorm"])
+@pytest.mark.parametrize("shared_missing", [False, True], ids=["shared_present", "shared_missing"])
+def test_reference_partial_failure_matches_port(norm_topk, shared_missing, ref_lib, port, synth, tmp_path):
+    """The reference's partial-failure policy through its own layer function
+    (generation_mlp.cpp.inc:1219-1282): experts without records drop out of
+    the sum, a renormalising router divides the others' combine weights by
+    their sum, and the router's ids and weights stay as routed.  Held bit for
+    bit to the restatement given the same missing experts."""
+    shape = synth.small_shape(name="pf", hidden=96, intermediate=64, experts=8, top_k=3, tokens=24, shared=True,
+                              norm_topk=norm_topk)
+    li = synth.make_layer(shape, seed=91)
+    present = np.ones(shape.experts + 1, np.uint8)
+    present[[2, 5]] = 0
+    if shared_missing:
+        present[shape.experts] = 0
+    ref = ref_lib.Ref(ref_lib.metadata_json(shape.top_k, norm_topk=norm_topk))
+    try:
+        y_fn, i_fn, w_fn = ref.moe_layer_engine(li, tmp_path / "shard.bin", present=present)
+    finally:
+        ref.close()
+    y_p, i_p, w_p, ties = port.moe_layer(li, present=present)
+    assert ties == 0
+    assert np.isin(i_p, [2, 5]).any()     # some token routes to a missing expert
+    assert np.array_equal(i_fn, i_p)
+    assert np.array_equal(bits(w_fn), bits(w_p))
+    assert np.array_equal(bits(y_fn), bits(y_p))
+    # Leaving the missing experts' terms at zero with the routed weights (their
+    # down weights zeroed) is the policy without renormalisation only.
+    zeroed = synth.LayerInputs(shape, li.router, li.gate, li.up, li.down.copy(), li.x, li.shared_gate, li.shared_up,
+                               np.zeros_like(li.shared_down) if shared_missing else li.shared_down)
+    zeroed.down[[2, 5]] = 0
+    y_z, _, _, _ = port.moe_layer(zeroed)
+    assert np.array_equal(y_z, y_p) != norm_topk
+
+
+def test_reference_fails_a_token_whose_experts_are_all_missing(ref_lib, port, synth, tmp_path):
+    """The reference's layer function fails when none of a token's selected
+    experts has records (generation_mlp.cpp.inc:1219-1239); so does the
+    restatement."""
+    shape = synth.small_shape(name="am", hidden=64, intermediate=48, experts=6, top_k=2, tokens=4)
+    li = synth.make_layer(shape, seed=93)
+    ids, _, _, _ = port.router_topk(li)
+    present = np.ones(shape.experts + 1, np.uint8)
+    present[list(ids[0])] = 0
+    ref = ref_lib.Ref(ref_lib.metadata_json(shape.top_k))
+    try:
+        with pytest.raises(RuntimeError):
+            ref.moe_layer_engine(li, tmp_path / "shard.bin", present=present)
+    finally:
+        ref.close()
+    with pytest.raises(RuntimeError):
+        port.moe_layer(li, present=present)
