@@ -233,3 +233,39 @@ def test_c_reader_matches_python_writer(ec, clib, tmp_path):
         assert not clib.moe_b200_expert_cache_open(path.encode(), err)
         assert msg in err.value, (msg, err.value)
     assert not clib.moe_b200_expert_cache_open(str(tmp_path / "absent").encode(), err)
+
+
+def test_c_reader_survives_damaged_files(ec, clib, tmp_path):
+    """Random byte flips anywhere in a cache file either leave it readable
+    (the records still CRC-checked) or make open refuse it with a message;
+    nothing is read outside the file."""
+    import ctypes as C
+    rng = np.random.default_rng(9)
+    H, I = 128, 128
+    recs = _records(ec, rng, H, I, [(0, 0), (0, 1), (1, 3)])
+    clean = str(tmp_path / "clean.b200cache")
+    ec.write_cache(clean, H, I, recs)
+    data = bytearray(open(clean, "rb").read())
+    err = C.create_string_buffer(160)
+    path = str(tmp_path / "fuzz.b200cache")
+    # header and entry table, where a flip changes what open believes
+    spots = list(rng.integers(0, 64, 40)) + list(rng.integers(ec.HEADER_BYTES, ec.HEADER_BYTES + 3 * 64, 40))
+    for off in spots:
+        d = bytearray(data)
+        d[int(off)] ^= int(rng.integers(1, 256))
+        with open(path, "wb") as f:
+            f.write(d)
+        cache = clib.moe_b200_expert_cache_open(path.encode(), err)
+        if not cache:
+            assert err.value, off
+            continue
+        try:
+            rb = C.c_uint64()
+            assert clib.moe_b200_expert_cache_info(cache, None, None, C.byref(rb), None) == 1
+            for layer, expert, key, rec in recs:
+                p = clib.moe_b200_expert_cache_record(cache, layer, expert, key, 1, err)
+                if p:  # a record that is returned is the one written
+                    got = np.ctypeslib.as_array((C.c_uint8 * rb.value).from_address(p))
+                    assert np.array_equal(got, rec)
+        finally:
+            clib.moe_b200_expert_cache_close(cache)
