@@ -369,16 +369,14 @@ int ref_moe_block(void* eng, const ref_block_desc* bd, const uint16_t* x_bf16, c
     const uint64_t row_i = (uint64_t)((I + 31u) / 32u) * 17u;
     const uint64_t expert_gu_bytes = (uint64_t)I * row_h;
     const uint64_t expert_d_bytes = (uint64_t)H * row_i;
-    const uint8_t F32 = moe_RAW_SCALAR_F32, BF16 = moe_RAW_SCALAR_BF16;
-    const uint8_t RAW_F32 = moe_WEIGHT_ENCODING_RAW_FP32, RAW_BF16 = moe_WEIGHT_ENCODING_RAW_BF16;
     {
         moe_raw_tensor_cache_entry r{};
         r.base = reinterpret_cast<const uint8_t*>(d->router_bf16);
         r.bytes = (uint64_t)E * H * 2ull;
         r.rows = E;
         r.cols = H;
-        r.scalar_encoding = BF16;
-        r.weight_format = RAW_BF16;
+        r.scalar_encoding = moe_RAW_SCALAR_BF16;
+        r.weight_format = moe_WEIGHT_ENCODING_RAW_BF16;
         std::unique_lock<std::shared_mutex> lock(engine->raw_tensor_cache_mutex);
         engine->raw_tensor_cache[router_cache_key(layer)] = r;
     }
